@@ -1,0 +1,369 @@
+#!/usr/bin/env python3
+"""Tree-attention fwd+bwd benchmark (BASELINE config 2 by default).
+
+One step = tree attention forward + backward over one DFS-packed tree:
+16,384 tokens (root prompt 2048, 2-4 children, node lengths U[64,512], depth
+<= 6), 32 q heads / 8 kv heads, head_dim 128, bf16.  With N GPUs each rank
+processes its own seeded tree (weak scaling, no collective on the data path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Useful FLOPs = 14 * D * Hq * V (fwd 4*D*V + bwd 10*D*V per head, V = visible
+(query, key) pairs).  ``value`` times inputs already in HBM (L2 flushed
+between steps); ``e2e`` times the public API from pinned host buffers: host
+packer + metadata copy + q/k/v/dO upload + fwd + bwd + dQ/dK/dV download.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "Tree-attn fwd+bwd useful TFLOP/s & tokens/s at 1/2/4/8 B200"
+HQ, HKV, D = 32, 8, 128
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=1000)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def workload(rank: int, seed: int):
+    from tree_training_b200.synthetic import config2_tree
+    import tree_training_b200 as tt
+    roots = config2_tree(seed + rank)
+    info = tt.build_dfs_tree_info(roots)
+    meta = info.attn_meta()
+    V = meta.visible_pairs
+    return roots, info, meta, V
+
+
+def useful_flops(V: int, hq: int = HQ, d: int = D):
+    return 4.0 * d * V * hq, 10.0 * d * V * hq
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while running."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.dev = device
+        self.proc = None
+        self.lines = []
+
+    def _gpu_id(self):
+        try:
+            u = torch.cuda.get_device_properties(self.dev).uuid
+            return "GPU-" + str(u)
+        except Exception:
+            return str(self.dev.index or 0)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", self._gpu_id()],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world, local, backend="nccl"):
+    if world > 1:
+        import torch.distributed as dist
+        kw = dict(backend=backend, timeout=datetime.timedelta(seconds=600))
+        if backend == "nccl":
+            kw["device_id"] = torch.device("cuda", local)
+        dist.init_process_group(**kw)
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_baseline_sample(meta, V, hq=4, hkv=1):
+    """Reference CPU path (HF sdpa_attention_forward + dense additive mask,
+    fwd + autograd bwd) on one GQA group (4 q heads, 1 kv head) of the tree."""
+    from oracle.ref_cpu import time_sample
+    secs = time_sample(meta, hq, hkv, D, torch.bfloat16)
+    fl = 14.0 * D * V * hq
+    return {"value": fl / secs / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port", "seconds": secs,
+            "tokens_per_s": meta.n_q * (hq / HQ) / secs,
+            "sample": f"fwd+bwd of {hq} q heads / {hkv} kv head (of {HQ}/{HKV}) over the full "
+                      f"{meta.n_q}-token tree, bf16, transformers sdpa_attention_forward with "
+                      f"the dense additive mask on {torch.get_num_threads()} threads"}
+
+
+def run_reference(args):
+    world, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    _, info, meta, V = workload(0, args.seed)
+    from oracle.ref_cpu import time_sample
+    for _ in range(args.warmup):
+        time_sample(meta, 4, 1, D, torch.bfloat16)
+    ts = [time_sample(meta, 4, 1, D, torch.bfloat16) for _ in range(args.steps)]
+    t = statistics.mean(ts)
+    fl = 14.0 * D * V * 4
+    val = fl / t / 1e12
+    sample = (f"each step: fwd+bwd of 4 q heads / 1 kv head (of {HQ}/{HKV}) over the full "
+              f"{meta.n_q}-token config-2 tree, bf16, transformers sdpa_attention_forward with "
+              f"the reference's dense additive mask, {torch.get_num_threads()} threads")
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "tokens_per_s": meta.n_q * (4 / HQ) / t,
+            "config": {"workload": "config2: one 16k-token DFS tree, 32/8 heads, D=128, "
+                                   "tree attention fwd+bwd", "tokens": meta.n_q,
+                       "visible_pairs": V, "sample_heads": "4 of 32"},
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import tree_training_b200 as tt
+    from tree_training_b200 import _lib
+    world, rank, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    init_dist(world, local)
+    roots, info, meta, V = workload(rank, args.seed)
+    f_fwd, f_bwd = useful_flops(V)
+    N = meta.n_q
+    g = torch.Generator(device=dev).manual_seed(rank)
+    mk = lambda *s: (torch.randn(*s, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    q0, k0, v0, do = mk(N, HQ, D), mk(N, HKV, D), mk(N, HKV, D), mk(N, HQ, D)
+    q, k, v = (x.clone().requires_grad_(True) for x in (q0, k0, v0))
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        q.grad = k.grad = v.grad = None
+        out = tt.tree_attention(q, k, v, meta)
+        out.backward(do)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    tt.check_device_status(dev)
+    barrier(world)
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    clocks = ClockSampler(dev)
+    clocks.start()
+    launches0 = _lib.lib().tt_kernel_launches()
+    torch.cuda.synchronize()
+    barrier(world)
+    for i in range(args.steps):
+        flush.zero_()                       # L2 flush between timed steps
+        q.grad = k.grad = v.grad = None
+        ev[i][0].record()
+        out = tt.tree_attention(q, k, v, meta)
+        ev[i][1].record()
+        out.backward(do)
+        ev[i][2].record()
+    torch.cuda.synchronize()
+    barrier(world)
+    launches = _lib.lib().tt_kernel_launches() - launches0
+    clk = clocks.stop()
+    tt.check_device_status(dev)
+    t_fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in ev) / 1e3
+    t_bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in ev) / 1e3
+    t_step = t_fwd + t_bwd
+    t_max = max_over_ranks(t_step, world, dev)
+    flops_all = sum_over_ranks(f_fwd + f_bwd, world, dev)
+    tokens_all = sum_over_ranks(float(N), world, dev)
+    value = flops_all / t_max / 1e12
+
+    # ---- end to end through the public API from pinned host buffers ----
+    pin = lambda t: t.detach().cpu().pin_memory()
+    qh, kh, vh, doh = pin(q0), pin(k0), pin(v0), pin(do)
+    dqh = torch.empty_like(qh).pin_memory()
+    dkh = torch.empty_like(kh).pin_memory()
+    dvh = torch.empty_like(vh).pin_memory()
+    h2d = d2h = 0
+
+    def e2e_step():
+        nonlocal h2d, d2h
+        inf = tt.build_dfs_tree_info(roots)          # host packer
+        m = inf.attn_meta()
+        qd = qh.to(dev, non_blocking=True).requires_grad_(True)
+        kd = kh.to(dev, non_blocking=True).requires_grad_(True)
+        vd = vh.to(dev, non_blocking=True).requires_grad_(True)
+        dod = doh.to(dev, non_blocking=True)
+        o = tt.tree_attention(qd, kd, vd, m)
+        o.backward(dod)
+        dqh.copy_(qd.grad, non_blocking=True)
+        dkh.copy_(kd.grad, non_blocking=True)
+        dvh.copy_(vd.grad, non_blocking=True)
+        h2d = (sum(x.numel() * x.element_size() for x in (qh, kh, vh, doh)) + m.h2d_bytes())
+        d2h = sum(x.numel() * x.element_size() for x in (dqh, dkh, dvh))
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e_ts = []
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        e2e_step()
+        b.record()
+        b.synchronize()
+        e_ts.append(a.elapsed_time(b) / 1e3)
+    t_e2e = max_over_ranks(statistics.mean(e_ts), world, dev)
+    e2e_value = flops_all / t_e2e / 1e12
+
+    pk, pk_src = peaks()
+    dominant = "bwd" if t_bwd >= t_fwd else "fwd"
+    achieved = (f_bwd / t_bwd if dominant == "bwd" else f_fwd / t_fwd) / 1e12
+    peak = float(pk["bf16_tflops"])
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as fh:
+            traffic = json.load(fh).get(dominant)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": t_max * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "tokens_per_s": tokens_all / t_max,
+            "config": {"workload": "config2: one DFS-packed 16k-token tree per GPU "
+                                   "(root 2048, 2-4 children, node len U[64,512], depth<=6), "
+                                   "32 q / 8 kv heads, head_dim 128, tree attention fwd+bwd",
+                       "tokens_per_gpu": N, "visible_pairs_rank0": V,
+                       "density_vs_causal": V / (N * (N + 1) / 2), "l2": "flushed (256 MiB write) "
+                       "between timed steps", "parallelism": f"dp{world} (independent trees)"},
+            "fwd_ms": t_fwd * 1e3, "bwd_ms": t_bwd * 1e3,
+            "fwd_tflops": f_fwd / t_fwd / 1e12, "bwd_tflops": f_bwd / t_bwd / 1e12,
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": t_e2e * 1e3,
+                    "tokens_per_s": tokens_all / t_e2e},
+            "roofline": {"bound": "tensor", "kernel": f"tree attention {dominant}",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{pk_src} bf16 dense (burst)"},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_sample(meta, V)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,164 @@
+/*
+ * tree_training_b200 — C ABI of the B200 (sm_100a) tree-training hot path.
+ *
+ * Plain pointers and sizes only: no torch types cross this boundary.  Device
+ * pointers are caller-owned (the library never allocates or frees caller
+ * memory); `stream` is a cudaStream_t passed as void*.  Every function
+ * returns a TT_* status; kernels never trap or assert: a bounded device wait
+ * that gives up writes a nonzero code into `*status` (a device int32 the
+ * caller may poll), and the host-side launcher returns TT_ERR_CUDA when a
+ * launch fails.
+ *
+ * Index conventions (one packed sequence, batch 1, as in the reference):
+ *   query rows    i in [0, n_q)   — the tokens of one partition in DFS order
+ *   key columns   j in [0, n_kv)  — gateway tokens first, then the partition
+ *   key j is visible to query rows [kv_lo[j], kv_hi[j]).
+ * Tensors are [tokens, heads, head_dim] with the last dim contiguous; token
+ * and head strides are given in elements.
+ *
+ * Reference citations are file:line inside Jinghui-Wang/tree-training
+ * (TF/ = transformers 5.5 site-packages, which the reference calls into).
+ */
+#ifndef TREE_TRAINING_B200_H
+#define TREE_TRAINING_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum tt_status {
+  TT_OK = 0,
+  TT_ERR_INVALID_ARG = 1,    /* bad size, pointer, or a forest that is not in pre-order */
+  TT_ERR_UNSUPPORTED = 2,    /* dtype / head_dim / stride combination not implemented */
+  TT_ERR_CUDA = 3,           /* a CUDA runtime call or launch failed */
+  TT_ERR_DEVICE_TIMEOUT = 4, /* a bounded device wait gave up (written to *status) */
+  TT_ERR_NOT_INTERVAL = 5,   /* a mask column is not one contiguous run of rows */
+  TT_ERR_WORKSPACE = 6,      /* workspace smaller than the *_workspace_size answer */
+  TT_ERR_CAPACITY = 7        /* an output list is shorter than needed */
+};
+
+enum tt_dtype { TT_F32 = 0, TT_BF16 = 1, TT_F16 = 2, TT_U8 = 3 };
+
+/* Human-readable text of a status code (static storage). */
+const char* tt_status_string(int status);
+
+/* ABI version; bumped on any signature change. */
+int tt_abi_version(void);
+
+/* Kernel path for the attention entry points: 0 = automatic (tcgen05 for
+ * bf16/f16 head_dim 128, exact CUDA-core kernels otherwise), 1 = always the
+ * exact CUDA-core kernels (used to cross-check the tensor-core path).  The
+ * environment variable TT_KERNEL_PATH=1 sets the initial value.  Returns the
+ * previous setting.  Tile shapes (tt_attn_tile_shape) follow this setting. */
+int tt_set_kernel_path(int path);
+
+/* Number of CUDA kernels this library has launched since it was loaded
+ * (all entry points, all devices).  Lets a benchmark report how many of its
+ * own kernels ran inside a timed region. */
+int64_t tt_kernel_launches(void);
+
+/* ------------------------------------------------------------------------
+ * Host packer.  Replaces the position/boundary/parent/leaf part of
+ * build_dfs_tree_info (dfs_tree_forward.py:91-139) and, instead of the dense
+ * [N,N] mask it builds (dfs_tree_forward.py:141-172), writes the per-key
+ * visible-row intervals.  The forest comes in pre-order: node i has
+ * node_len[i] tokens and parent node_parent[i] (< i, or -1 for a root).
+ * pos_ids[t] = pos_offset + (tokens in t's ancestor nodes) + offset in node
+ * (dfs_tree_forward.py:125-126; pos_offset is tree_grad_hybrid.py:308-310).
+ * Outputs: pos_ids[N], chunk_bounds[2*n_nodes] (start,end pairs),
+ * subtree_end[n_nodes] (token one past the node's subtree), leaf_ids (nodes
+ * without children, DFS order; *n_leaves set), token_node[N], kv_lo[N],
+ * kv_hi[N] (row intervals of the partition's own keys).  Any output pointer
+ * may be NULL.  Host memory.  Returns TT_ERR_INVALID_ARG if the order is
+ * not a pre-order.
+ */
+int tt_pack_forest(int32_t n_nodes, const int32_t* node_len, const int32_t* node_parent,
+                   int32_t pos_offset, int32_t* pos_ids, int32_t* chunk_bounds,
+                   int32_t* subtree_end, int32_t* leaf_ids, int32_t* n_leaves,
+                   int32_t* token_node, int32_t* kv_lo, int32_t* kv_hi);
+
+/* Gateway key intervals from the reference's additive bias vector
+ * (tree_grad_hybrid.py:206-209, consumed at :313-315): bias 0 -> visible to
+ * every row [0, n_q), -inf -> no row.  Host memory.  Any other value ->
+ * TT_ERR_NOT_INTERVAL. */
+int tt_gateway_intervals_from_bias(int32_t past_len, const float* bias, int32_t n_q,
+                                   int32_t* kv_lo, int32_t* kv_hi);
+
+/* ------------------------------------------------------------------------
+ * Tile work lists (host).  For q-tiles of tile_q rows and kv-tiles of
+ * tile_kv columns: fwd_ptr[n_qt+1]/fwd_list = per q-tile the visible
+ * kv-tiles (ascending), bwd_ptr[n_kt+1]/bwd_list = per kv-tile the visible
+ * q-tiles (ascending).  Entry = tile_index*2 + partial, where partial=0 means
+ * every (row, key) of the pair is visible (the kernel skips the mask test).
+ * Lists need capacity n_qt*n_kt entries (list_cap); *visible_pairs = number
+ * of visible (row, key) pairs.  Any of the four list pointers may be NULL.
+ */
+int tt_build_tiles(int32_t n_q, int32_t n_kv, const int32_t* kv_lo, const int32_t* kv_hi,
+                   int32_t tile_q, int32_t tile_kv, int32_t* fwd_ptr, int32_t* fwd_list,
+                   int32_t* bwd_ptr, int32_t* bwd_list, int64_t list_cap,
+                   int64_t* visible_pairs);
+
+/* Tile shape that tt_tree_attn_fwd / _bwd expect for a dtype and head dim
+ * (lists must be built with it).  kind: 0 = forward, 1 = backward. */
+int tt_attn_tile_shape(int dtype, int32_t head_dim, int kind, int32_t* tile_q,
+                       int32_t* tile_kv);
+
+/* ------------------------------------------------------------------------
+ * Dense mask -> key intervals (device).  Lets the reference's own drivers
+ * pass their dense mask unchanged (dfs_tree_forward.py:548-550,
+ * tree_grad_hybrid.py:312-317): visible = (value == 0) for float masks, or
+ * nonzero for TT_U8 (bool) masks; masked = -inf / a value below -1e30.
+ * A column whose visible rows are not one run, or any other value, sets
+ * *status = TT_ERR_NOT_INTERVAL.  mask[i*stride_q + j*stride_kv].
+ */
+int tt_mask_to_intervals(int mask_dtype, int32_t n_q, int32_t n_kv, const void* mask,
+                         int64_t stride_q, int64_t stride_kv, int32_t* kv_lo, int32_t* kv_hi,
+                         int32_t* status, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Tree attention forward.  Replaces the attention call that the reference
+ * reaches through HF (TF/integrations/sdpa_attention.py:92-101 with the mask
+ * of dfs_tree_forward.py:548-550 / tree_grad_hybrid.py:313-317): for every
+ * q head h, O = softmax(Q K^T * scale + M) V with M from the key intervals,
+ * GQA by h / (hq / hkv).  out [n_q, hq, head_dim] contiguous, in `dtype`;
+ * lse [hq, n_q] fp32 natural-log row log-sum-exp (+inf for a row that sees no
+ * key).  dtype TT_BF16 / TT_F16 run the tcgen05 path for head_dim 128 (and
+ * the exact SIMT path otherwise); TT_F32 runs the SIMT path (fp32 FMA).
+ */
+int tt_tree_attn_fwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv,
+                     int32_t head_dim, const void* q, int64_t q_st, int64_t q_sh,
+                     const void* k, int64_t k_st, int64_t k_sh, const void* v, int64_t v_st,
+                     int64_t v_sh, const int32_t* kv_lo, const int32_t* kv_hi,
+                     const int32_t* fwd_ptr, const int32_t* fwd_list, float scale, void* out,
+                     float* lse, int32_t* status, void* stream);
+
+/* Workspace bytes tt_tree_attn_bwd needs (fp32 row terms; dQ accumulator
+ * for the tcgen05 path). */
+int64_t tt_tree_attn_bwd_workspace_size(int dtype, int32_t n_q, int32_t n_kv, int32_t hq,
+                                        int32_t hkv, int32_t head_dim);
+
+/* Tree attention backward: the autograd of the call above (what torch
+ * autograd computes through SDPA in the reference's loss.backward(),
+ * tree_grad_hybrid.py:533-535, tree_grad_ckpt.py:103-107).  out/dout are
+ * [n_q, hq, head_dim] (token/head strides given for dout); dq, dk, dv are
+ * written with the given strides (dk/dv include the gateway keys, so the
+ * gateway leaf tensors get gradients as with SDPA).  Deterministic for
+ * dk/dv.  fwd lists drive the dQ pass, bwd lists the dK/dV pass. */
+int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv,
+                     int32_t head_dim, const void* q, int64_t q_st, int64_t q_sh,
+                     const void* k, int64_t k_st, int64_t k_sh, const void* v, int64_t v_st,
+                     int64_t v_sh, const void* out, const void* dout, int64_t do_st,
+                     int64_t do_sh, const float* lse, const int32_t* kv_lo,
+                     const int32_t* kv_hi, const int32_t* fwd_ptr, const int32_t* fwd_list,
+                     const int32_t* bwd_ptr, const int32_t* bwd_list, float scale, void* dq,
+                     int64_t dq_st, int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh,
+                     void* dv, int64_t dv_st, int64_t dv_sh, void* workspace,
+                     int64_t workspace_bytes, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TREE_TRAINING_B200_H */

@@ -1,0 +1,404 @@
+// Tree attention forward on the 5th-generation tensor cores (sm_100a).
+//
+// Replaces the SDPA call the reference reaches through HF
+// (TF/integrations/sdpa_attention.py:92-101) with its dense additive mask
+// (dfs_tree_forward.py:548-550, tree_grad_hybrid.py:313-317): for one q head
+// and one 128-row query tile, O = softmax(Q K^T * scale + M) V over the kv
+// tiles that the host work list marks visible, M evaluated in registers from
+// the per-key row intervals [kv_lo, kv_hi).
+//
+// CTA = 6 warps, one (q head, q tile) each:
+//   warp 0    TMA producer: Q once, then K/V tiles into a 2-stage ring
+//   warp 1    MMA issuer:   S_j = Q K_j^T into TMEM (double buffered),
+//                           O += P_{j-1} V_{j-1} with P read from TMEM
+//   warps 2-5 softmax:      one thread per query row (= TMEM lane); masks
+//                           partial tiles, keeps the running max/sum, writes
+//                           P (bf16/fp16) over S in TMEM, rescales O only when
+//                           the max grows by more than 2^8, final epilogue.
+// TMEM columns: [0,128) S/P buffer 0, [128,256) S/P buffer 1, [256,384) O.
+#include <type_traits>
+
+#include "tt_sm100.cuh"
+
+namespace tt {
+namespace sm100 {
+namespace {
+
+constexpr int kBM = 128;                  // query rows per tile
+constexpr int kBN = 128;                  // keys per tile
+constexpr int kD = 128;                   // head dim
+constexpr int kStages = 2;                // K/V ring depth
+constexpr int kTileBytes = kBM * kD * 2;  // one 128 x 128 16-bit tile
+constexpr int kHalfBytes = kTileBytes / 2;  // one 64-column swizzle block
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 256;
+constexpr float kRescaleThreshold = 8.0f;   // log2 units
+
+struct FwdBarriers {
+  uint64_t q_full;
+  uint64_t k_full[kStages];
+  uint64_t v_full[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int32_t abort;
+};
+
+constexpr size_t kSmemBytes = 1024 + kTileBytes * (1 + 2 * kStages) + sizeof(FwdBarriers);
+
+__device__ __forceinline__ void raise_abort(FwdBarriers* sh, int32_t* status) {
+  set_status(status, TT_ERR_DEVICE_TIMEOUT);
+  *reinterpret_cast<volatile int32_t*>(&sh->abort) = 1;
+}
+
+template <bool kBf16>
+__global__ void __launch_bounds__(kThreads, 1)
+attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+            const __grid_constant__ CUtensorMap tm_v, int n_q, int n_kv, int rep,
+            const int32_t* __restrict__ kv_lo, const int32_t* __restrict__ kv_hi,
+            const int32_t* __restrict__ fwd_ptr, const int32_t* __restrict__ fwd_list,
+            float scale_log2, void* __restrict__ out_, float* __restrict__ lse,
+            int32_t* status) {
+  using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = base;
+  uint8_t* sK = sQ + kTileBytes;
+  uint8_t* sV = sK + kStages * kTileBytes;
+  FwdBarriers* sh = reinterpret_cast<FwdBarriers*>(sV + kStages * kTileBytes);
+  const volatile int32_t* abort_flag = &sh->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hq = gridDim.x;
+  const int h = blockIdx.x;
+  const int qt = gridDim.y - 1 - blockIdx.y;  // heavier (later) tiles first
+  const int hk = h / rep;
+  const int e0 = fwd_ptr[qt];
+  const int n_it = fwd_ptr[qt + 1] - e0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sh->q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sh->k_full[s], 1);
+      mbar_init(&sh->v_full[s], 1);
+      mbar_init(&sh->kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh->s_full[b], 1);
+      mbar_init(&sh->p_full[b], 128);
+    }
+    mbar_init(&sh->o_done, 1);
+    mbar_init(&sh->drain, 1);
+    sh->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sh->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && n_it > 0) {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+      mbar_arrive_expect_tx(&sh->q_full, kTileBytes);
+      tma_load_3d(sQ, &tm_q, &sh->q_full, 0, qt * kBM, h);
+      tma_load_3d(sQ + kHalfBytes, &tm_q, &sh->q_full, 64, qt * kBM, h);
+      int issued[kStages] = {0};
+      bool ok = true;
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int s = it % kStages;
+        if (it >= kStages) ok = mbar_wait(&sh->kv_empty[s], ((it / kStages) - 1) & 1, abort_flag);
+        if (!ok) break;
+        const int kt = fwd_list[e0 + it] >> 1;
+        uint8_t* k_dst = sK + s * kTileBytes;
+        uint8_t* v_dst = sV + s * kTileBytes;
+        mbar_arrive_expect_tx(&sh->k_full[s], kTileBytes);
+        tma_load_3d(k_dst, &tm_k, &sh->k_full[s], 0, kt * kBN, hk);
+        tma_load_3d(k_dst + kHalfBytes, &tm_k, &sh->k_full[s], 64, kt * kBN, hk);
+        mbar_arrive_expect_tx(&sh->v_full[s], kTileBytes);
+        tma_load_3d(v_dst, &tm_v, &sh->v_full[s], 0, kt * kBN, hk);
+        tma_load_3d(v_dst + kHalfBytes, &tm_v, &sh->v_full[s], 64, kt * kBN, hk);
+        issued[s] += 1;
+      }
+      if (!ok) {
+        raise_abort(sh, status);
+        // let the copies already in flight land before the CTA exits
+        mbar_wait(&sh->q_full, 0, nullptr);
+        for (int s = 0; s < kStages; ++s)
+          if (issued[s] > 0) {
+            mbar_wait(&sh->k_full[s], (issued[s] - 1) & 1, nullptr);
+            mbar_wait(&sh->v_full[s], (issued[s] - 1) & 1, nullptr);
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_it > 0) {
+      constexpr uint32_t id_s = idesc_f16(kBf16, kBM, kBN, false);
+      constexpr uint32_t id_o = idesc_f16(kBf16, kBM, kD, true);
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      bool ok = mbar_wait(&sh->q_full, 0, abort_flag);
+      tc_fence_after();
+      for (int it = 0; it <= n_it && ok; ++it) {
+        if (it < n_it) {
+          const int s = it % kStages, b = it & 1;
+          ok = mbar_wait(&sh->k_full[s], (it / kStages) & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+            const uint64_t da = desc_sw128(q_addr + off, 16, 1024);
+            const uint64_t db = desc_sw128(k_addr + s * kTileBytes + off, 16, 1024);
+            mma_ss(tmem + b * 128, da, db, id_s, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&sh->s_full[b]);
+        }
+        if (it > 0) {
+          const int j = it - 1, s = j % kStages, b = j & 1;
+          ok = mbar_wait(&sh->p_full[b], (j >> 1) & 1, abort_flag);
+          if (ok) ok = mbar_wait(&sh->v_full[s], (j / kStages) & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            // B = V tile, MN-major: 16 keys per step = 16 rows of 128 bytes
+            const uint64_t db = desc_sw128(v_addr + s * kTileBytes + kk * 2048, kHalfBytes, 1024);
+            mma_ts(tmem + kColO, tmem + b * 128 + kk * 8, db, id_o,
+                   (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&sh->kv_empty[s]);
+          tc_commit(&sh->o_done);
+        }
+      }
+      if (!ok) {
+        raise_abort(sh, status);
+        tc_commit(&sh->drain);
+        mbar_wait(&sh->drain, 0, nullptr);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int quad = warp & 3;              // TMEM lane quadrant of this warp
+    const int r = quad * 32 + lane;         // row within the tile
+    const int row = qt * kBM + r;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int ent = fwd_list[e0 + it];
+      const int kt = ent >> 1;
+      const bool partial = ent & 1;
+      const int b = it & 1;
+      ok = mbar_wait(&sh->s_full[b], (it >> 1) & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      float s[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        float t[32];
+        tmem_ld32(lane_addr + b * 128 + c * 32, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
+      }
+      if (partial) {
+        const int j0 = kt * kBN;
+        if (j0 + kBN <= n_kv) {
+          const int4* lo4 = reinterpret_cast<const int4*>(kv_lo + j0);
+          const int4* hi4 = reinterpret_cast<const int4*>(kv_hi + j0);
+#pragma unroll
+          for (int c = 0; c < kBN / 4; ++c) {
+            const int4 a = __ldg(lo4 + c), z = __ldg(hi4 + c);
+            if (!visible(a.x, z.x, row)) s[4 * c + 0] = -INFINITY;
+            if (!visible(a.y, z.y, row)) s[4 * c + 1] = -INFINITY;
+            if (!visible(a.z, z.z, row)) s[4 * c + 2] = -INFINITY;
+            if (!visible(a.w, z.w, row)) s[4 * c + 3] = -INFINITY;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c) {
+            const int j = j0 + c;
+            const bool vis = j < n_kv && visible(__ldg(kv_lo + j), __ldg(kv_hi + j), row);
+            if (!vis) s[c] = -INFINITY;
+          }
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, s[c]);
+      const float m_new = fmaxf(m_run, mx * scale_log2);
+      // PV_{it-1} must be complete before O may be rescaled; waiting every
+      // iteration keeps the o_done phases observed in order.
+      if (it > 0) {
+        ok = mbar_wait(&sh->o_done, (it - 1) & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+      }
+      float alpha = 1.f;
+      bool need = false;
+      if (m_run == -INFINITY) {
+        m_run = m_new;  // every earlier P of this row was 0: nothing to rescale
+      } else if (m_new > m_run + kRescaleThreshold) {
+        alpha = exp2f(m_run - m_new);
+        m_run = m_new;
+        need = true;
+      }
+      if (__any_sync(0xffffffffu, need)) {
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < kD / 32; ++c) {
+          float o[32];
+          uint32_t w[32];
+          tmem_ld32(lane_addr + kColO + c * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * alpha);
+          tmem_st32(lane_addr + kColO + c * 32, w);
+        }
+        tmem_st_wait();
+      }
+      l_run *= alpha;
+      const float mb = (m_run == -INFINITY) ? 0.f : m_run;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = exp2f(fmaf(s[half * 64 + 2 * i], scale_log2, -mb));
+          const float p1 = exp2f(fmaf(s[half * 64 + 2 * i + 1], scale_log2, -mb));
+          l_run += p0 + p1;
+          pk[i] = pack2<kBf16>(p0, p1);
+        }
+        tmem_st32(lane_addr + b * 128 + half * 32, pk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&sh->p_full[b]);
+    }
+    if (ok && n_it > 0) {
+      ok = mbar_wait(&sh->o_done, (n_it - 1) & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      T* out = reinterpret_cast<T*>(out_) + static_cast<int64_t>(row) * hq * kD + h * kD;
+#pragma unroll 1
+      for (int c = 0; c < kD / 32; ++c) {
+        float o[32];
+        if (n_it > 0) {
+          tmem_ld32(lane_addr + kColO + c * 32, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (row < n_q) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) w[i] = pack2<kBf16>(o[2 * i] * inv, o[2 * i + 1] * inv);
+          uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+      if (row < n_q)
+        lse[static_cast<int64_t>(h) * n_q + row] =
+            l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : INFINITY;
+    } else {
+      raise_abort(sh, status);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---- host side ---------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// [tokens, heads, 128] 16-bit tensor -> 3-D map {dim, token, head}, box
+// {64, 128, 1}, 128-byte swizzle, zero fill outside the tensor.
+int make_map(CUtensorMap* map, bool bf16, const void* ptr, int64_t n_tok, int64_t n_head,
+             int64_t st_tok, int64_t st_head) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return TT_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (st_tok * 2) % 16 || (st_head * 2) % 16)
+    return TT_ERR_UNSUPPORTED;
+  cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)n_tok, (cuuint64_t)n_head};
+  cuuint64_t strides[2] = {(cuuint64_t)(st_tok * 2), (cuuint64_t)(st_head * 2)};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                  3, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TT_OK : TT_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+}  // namespace sm100
+}  // namespace tt
+
+int tt_launch_attn_fwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv,
+                             int32_t D, const void* q, int64_t q_st, int64_t q_sh,
+                             const void* k, int64_t k_st, int64_t k_sh, const void* v,
+                             int64_t v_st, int64_t v_sh, const int32_t* kv_lo,
+                             const int32_t* kv_hi, const int32_t* fwd_ptr,
+                             const int32_t* fwd_list, float scale, void* out, float* lse,
+                             int32_t* status, cudaStream_t st) {
+  using namespace tt::sm100;
+  if (D != kD || (dtype != TT_BF16 && dtype != TT_F16)) return TT_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(kv_lo) & 15) || (reinterpret_cast<uintptr_t>(kv_hi) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15))
+    return TT_ERR_UNSUPPORTED;
+  if (n_q == 0) return TT_OK;
+  const bool bf16 = dtype == TT_BF16;
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = make_map(&mq, bf16, q, n_q, hq, q_st, q_sh)) != TT_OK) return rc;
+  if ((rc = make_map(&mk, bf16, k, n_kv, hkv, k_st, k_sh)) != TT_OK) return rc;
+  if ((rc = make_map(&mv, bf16, v, n_kv, hkv, v_st, v_sh)) != TT_OK) return rc;
+  const int n_qt = (n_q + kBM - 1) / kBM;
+  dim3 grid(hq, n_qt);
+  const float scale_log2 = scale * 1.4426950408889634f;
+  auto kern = bf16 ? attn_fwd_tc<true> : attn_fwd_tc<false>;
+  TT_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kSmemBytes));
+  kern<<<grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, n_q, n_kv, hq / hkv, kv_lo, kv_hi,
+                                           fwd_ptr, fwd_list, scale_log2, out, lse, status);
+  tt_count_launches(1);
+  return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
+}
