@@ -123,8 +123,9 @@ int tt_mask_to_intervals(int mask_dtype, int32_t n_q, int32_t n_kv, const void* 
  * of dfs_tree_forward.py:548-550 / tree_grad_hybrid.py:313-317): for every
  * q head h, O = softmax(Q K^T * scale + M) V with M from the key intervals,
  * GQA by h / (hq / hkv).  out [n_q, hq, head_dim] contiguous, in `dtype`;
- * lse [hq, n_q] fp32 natural-log row log-sum-exp (+inf for a row that sees no
- * key).  dtype TT_BF16 / TT_F16 run the tcgen05 path for head_dim 128 (and
+ * lse [hq, ld] fp32 natural-log row log-sum-exp with ld = n_q rounded up to a
+ * multiple of 128 (+inf for a row that sees no key and for the ld - n_q
+ * padding rows).  dtype TT_BF16 / TT_F16 run the tcgen05 path for head_dim 128 (and
  * the exact SIMT path otherwise); TT_F32 runs the SIMT path (fp32 FMA).
  */
 int tt_tree_attn_fwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv,

@@ -160,6 +160,23 @@ def test_tensor_core_forward_matches_exact_path():
     assert float((a - b).abs().max() / b.abs().max()) < 1e-2
 
 
+@pytest.mark.parametrize("seed,n,hq,hkv,past", [(11, 2500, 8, 2, 50), (12, 4000, 10, 2, 0),
+                                                (13, 129, 4, 1, 1)])
+def test_tensor_core_backward_matches_exact_path(seed, n, hq, hkv, past):
+    """Full fwd+bwd through both kernel paths on the same bf16 inputs."""
+    meta, q, k, v, do = make_case(seed, n, hq, hkv, 128, 32, 400, past)
+    res = []
+    for path in (0, 1):
+        prev = _lib.lib().tt_set_kernel_path(path)
+        try:
+            m = tt.TreeAttnMeta(meta.n_q, meta.kv_lo, meta.kv_hi)
+            res.append(run(q, k, v, m, do, torch.bfloat16))
+        finally:
+            _lib.lib().tt_set_kernel_path(prev)
+    for name, a, b in zip(("out", "dq", "dk", "dv"), res[0], res[1]):
+        assert rel(a, b) < 1.5e-2, name
+
+
 def test_dense_mask_conversion_matches_packer():
     meta, *_ = make_case(10, 900, 1, 1, 32, 8, 100, past=21)
     m = torch.full((1, 1, meta.n_q, meta.n_kv), float("-inf"), device=DEV)

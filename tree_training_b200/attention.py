@@ -43,6 +43,11 @@ def check_device_status(device: Optional[torch.device] = None) -> None:
             raise _lib.TTError("device kernel", code)
 
 
+def lse_ld(n_q: int) -> int:
+    """Row stride of the LSE / delta buffers: n_q rounded up to 128."""
+    return (n_q + 127) // 128 * 128
+
+
 def tile_shape(dtype: torch.dtype, head_dim: int, kind: int) -> Tuple[int, int]:
     tq = np.zeros(1, np.int32)
     tk = np.zeros(1, np.int32)
@@ -72,7 +77,7 @@ def attn_fwd_raw(q, k, v, meta_dev, scale: float):
     n_q, hq, D = q.shape
     n_kv, hkv, _ = k.shape
     out = torch.empty((n_q, hq, D), dtype=q.dtype, device=q.device)
-    lse = torch.empty((hq, n_q), dtype=torch.float32, device=q.device)
+    lse = torch.empty((hq, lse_ld(n_q)), dtype=torch.float32, device=q.device)
     _lib.call("tt_tree_attn_fwd", _DTYPES[q.dtype], n_q, n_kv, hq, hkv, D,
               q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1),
               v.data_ptr(), v.stride(0), v.stride(1), meta_dev["kv_lo"].data_ptr(),
@@ -127,7 +132,7 @@ def _tree_attn_fwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_lo: 
 def _(q, k, v, kv_lo, kv_hi, fwd_ptr, fwd_list, b_fwd_ptr, b_fwd_list, b_bwd_ptr, b_bwd_list,
       scale):
     n_q, hq, D = q.shape
-    return q.new_empty((n_q, hq, D)), q.new_empty((hq, n_q), dtype=torch.float32)
+    return q.new_empty((n_q, hq, D)), q.new_empty((hq, lse_ld(n_q)), dtype=torch.float32)
 
 
 @torch.library.custom_op("tt_b200::tree_attn_bwd", mutates_args=())

@@ -44,7 +44,7 @@ extern "C" int tt_set_kernel_path(int path) {
 extern "C" int tt_attn_tile_shape(int dtype, int32_t D, int kind, int32_t* tile_q,
                                   int32_t* tile_kv) {
   if (!tile_q || !tile_kv || (kind != 0 && kind != 1)) return TT_ERR_INVALID_ARG;
-  if (tc_path(dtype, D) && kind == 0) {
+  if (tc_path(dtype, D)) {
     *tile_q = 128;
     *tile_kv = 128;
   } else {
@@ -90,8 +90,8 @@ extern "C" int64_t tt_tree_attn_bwd_workspace_size(int dtype, int32_t n_q, int32
   (void)n_kv;
   (void)hkv;
   (void)D;
-  // fp32 delta = rowsum(dO * O) per (head, row)
-  int64_t bytes = (int64_t)hq * n_q * 4;
+  // fp32 delta = rowsum(dO * O) per (head, row), rows padded like the LSE
+  int64_t bytes = (int64_t)hq * tt::lse_ld(n_q) * 4;
   return (bytes + 255) / 256 * 256;
 }
 
@@ -107,13 +107,18 @@ extern "C" int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq
                                 int64_t dk_sh, void* dv, int64_t dv_st, int64_t dv_sh,
                                 void* workspace, int64_t workspace_bytes, int32_t* status,
                                 void* stream) {
-  (void)status;
   if (!valid_dims(n_q, n_kv, hq, hkv, D)) return TT_ERR_INVALID_ARG;
   if (workspace_bytes < tt_tree_attn_bwd_workspace_size(dtype, n_q, n_kv, hq, hkv, D))
     return TT_ERR_WORKSPACE;
   if ((n_q > 0 && (!q || !out || !dout || !lse || !dq || !fwd_ptr)) ||
       (n_kv > 0 && (!k || !v || !dk || !dv || !kv_lo || !kv_hi || !bwd_ptr)))
     return TT_ERR_INVALID_ARG;
+  if (tc_path(dtype, D))
+    return tt_launch_attn_bwd_sm100(dtype, n_q, n_kv, hq, hkv, D, q, q_st, q_sh, k, k_st, k_sh, v,
+                                    v_st, v_sh, out, dout, do_st, do_sh, lse, kv_lo, kv_hi,
+                                    fwd_ptr, fwd_list, bwd_ptr, bwd_list, scale, dq, dq_st, dq_sh,
+                                    dk, dk_st, dk_sh, dv, dv_st, dv_sh, (float*)workspace, status,
+                                    (cudaStream_t)stream);
   return tt_launch_attn_bwd_simt(dtype, n_q, n_kv, hq, hkv, D, q, q_st, q_sh, k, k_st, k_sh, v,
                                  v_st, v_sh, out, dout, do_st, do_sh, lse, kv_lo, kv_hi, fwd_ptr,
                                  fwd_list, bwd_ptr, bwd_list, scale, dq, dq_st, dq_sh, dk, dk_st,

@@ -313,9 +313,10 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
           for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
       }
-      if (row < n_q)
-        lse[static_cast<int64_t>(h) * n_q + row] =
-            l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : INFINITY;
+      // rows past n_q are the padding of the [hq, lse_ld(n_q)] layout: +inf
+      lse[static_cast<int64_t>(h) * lse_ld(n_q) + row] =
+          (row < n_q && l_run > 0.f) ? (m_run + __log2f(l_run)) * 0.69314718055994531f
+                                     : INFINITY;
     } else {
       raise_abort(sh, status);
     }

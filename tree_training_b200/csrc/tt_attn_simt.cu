@@ -101,7 +101,7 @@ attn_fwd_simt(int n_q, int n_kv, int rep, const T* __restrict__ q, int64_t q_st,
 #pragma unroll
     for (int i = 0; i < DPT; ++i)
       out[(int64_t)row * hq * D + h * D + sl + kTPR * i] = from_f32<T>(o[i] * inv);
-    if (sl == 0) lse[(int64_t)h * n_q + row] = l > 0.f ? m + logf(l) : INFINITY;
+    if (sl == 0) lse[(int64_t)h * lse_ld(n_q) + row] = l > 0.f ? m + logf(l) : INFINITY;
   }
 }
 
@@ -111,15 +111,17 @@ __global__ void attn_bwd_delta(int n_q, int hq, int D, const T* __restrict__ out
                                const T* __restrict__ dout, int64_t do_st, int64_t do_sh,
                                float* __restrict__ delta) {
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (w >= n_q * hq) return;
+  const int ld = lse_ld(n_q);
+  if (w >= ld * hq) return;
   const int i = w / hq, h = w % hq;
   float acc = 0.f;
-  for (int d = lane; d < D; d += 32)
+  if (i < n_q)
+    for (int d = lane; d < D; d += 32)
     acc = fmaf(to_f32(out[(int64_t)i * hq * D + h * D + d]), to_f32(dout[i * do_st + h * do_sh + d]),
                acc);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) delta[(int64_t)h * n_q + i] = acc;
+  if (lane == 0) delta[(int64_t)h * ld + i] = acc;
 }
 
 template <typename T, int D>
@@ -166,8 +168,8 @@ attn_bwd_dkdv_simt(int n_q, int n_kv, int hq, int rep, const T* __restrict__ q, 
       }
       for (int rr = tid; rr < kBQ; rr += kThreads) {
         const int row = qt * kBQ + rr;
-        sLse[rr] = row < n_q ? lse[(int64_t)h * n_q + row] : INFINITY;
-        sDel[rr] = row < n_q ? delta[(int64_t)h * n_q + row] : 0.f;
+        sLse[rr] = row < n_q ? lse[(int64_t)h * lse_ld(n_q) + row] : INFINITY;
+        sDel[rr] = row < n_q ? delta[(int64_t)h * lse_ld(n_q) + row] : 0.f;
       }
       __syncthreads();
 #pragma unroll 2
@@ -228,8 +230,8 @@ attn_bwd_dq_simt(int n_q, int n_kv, int rep, const T* __restrict__ q, int64_t q_
     dor[i] = rv ? to_f32(dout[row * do_st + h * do_sh + sl + kTPR * i]) : 0.f;
     g[i] = 0.f;
   }
-  const float lrow = rv ? lse[(int64_t)h * n_q + row] : INFINITY;
-  const float drow = rv ? delta[(int64_t)h * n_q + row] : 0.f;
+  const float lrow = rv ? lse[(int64_t)h * lse_ld(n_q) + row] : INFINITY;
+  const float drow = rv ? delta[(int64_t)h * lse_ld(n_q) + row] : 0.f;
   const int e0 = fwd_ptr[qt], e1 = fwd_ptr[qt + 1];
   for (int e = e0; e < e1; ++e) {
     const int kt = fwd_list[e] >> 1;
@@ -351,6 +353,12 @@ int launch_mask(int n_q, int n_kv, const void* mask, int64_t sq, int64_t skv, in
   return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
 }
 
+__global__ void lse_fill_pad(int n_q, int hq, float* lse) {
+  const int ld = lse_ld(n_q), pad = ld - n_q;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx < pad * hq) lse[(int64_t)(idx / pad) * ld + n_q + idx % pad] = INFINITY;
+}
+
 template <typename T, int D>
 int launch_fwd(int n_q, int n_kv, int hq, int hkv, const void* q, int64_t q_st, int64_t q_sh,
                const void* k, int64_t k_st, int64_t k_sh, const void* v, int64_t v_st,
@@ -363,7 +371,9 @@ int launch_fwd(int n_q, int n_kv, int hq, int hkv, const void* q, int64_t q_st, 
   kern<<<grid, kThreads, smem, st>>>(n_q, n_kv, hq / hkv, (const T*)q, q_st, q_sh, (const T*)k,
                                      k_st, k_sh, (const T*)v, v_st, v_sh, lo, hi, fp, fl, scale,
                                      (T*)out, lse);
-  tt_count_launches(1);
+  const int pad = lse_ld(n_q) - n_q;
+  if (pad > 0) lse_fill_pad<<<(pad * hq + 255) / 256, 256, 0, st>>>(n_q, hq, lse);
+  tt_count_launches(pad > 0 ? 2 : 1);
   return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
 }
 
@@ -376,7 +386,7 @@ int launch_bwd(int n_q, int n_kv, int hq, int hkv, const void* q, int64_t q_st, 
                int64_t dq_st, int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
                int64_t dv_st, int64_t dv_sh, float* delta, cudaStream_t st) {
   const int rep = hq / hkv;
-  const int warps = n_q * hq;
+  const int warps = lse_ld(n_q) * hq;
   if (warps > 0)
     attn_bwd_delta<T><<<(warps + 7) / 8, 256, 0, st>>>(n_q, hq, D, (const T*)out, (const T*)dout,
                                                         do_st, do_sh, delta);

@@ -40,6 +40,11 @@ __device__ __forceinline__ bool visible(int32_t lo, int32_t hi, int32_t row) {
   return (row >= lo) & (row < hi);
 }
 
+// Row stride of the per-(head, row) fp32 terms (LSE, delta): rows padded to a
+// multiple of 128 so tensor-core kernels read whole tiles with vector loads.
+// Padding rows hold LSE = +inf (no probability mass) and delta = 0.
+__host__ __device__ __forceinline__ int lse_ld(int n_q) { return (n_q + 127) & ~127; }
+
 // Record the first error code a kernel hits (never traps).
 __device__ __forceinline__ void set_status(int32_t* status, int32_t code) {
   if (status) atomicCAS(status, 0, code);
@@ -79,3 +84,14 @@ int tt_launch_attn_fwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
                              const int32_t* kv_hi, const int32_t* fwd_ptr,
                              const int32_t* fwd_list, float scale, void* out, float* lse,
                              int32_t* status, cudaStream_t stream);
+int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv,
+                             int32_t D, const void* q, int64_t q_st, int64_t q_sh,
+                             const void* k, int64_t k_st, int64_t k_sh, const void* v,
+                             int64_t v_st, int64_t v_sh, const void* out, const void* dout,
+                             int64_t do_st, int64_t do_sh, const float* lse,
+                             const int32_t* kv_lo, const int32_t* kv_hi, const int32_t* fwd_ptr,
+                             const int32_t* fwd_list, const int32_t* bwd_ptr,
+                             const int32_t* bwd_list, float scale, void* dq, int64_t dq_st,
+                             int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
+                             int64_t dv_st, int64_t dv_sh, float* delta, int32_t* status,
+                             cudaStream_t stream);
