@@ -43,6 +43,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=1000)
+    ap.add_argument("--tokens", type=int, default=16384,
+                    help="tree token budget (16384 = config 2; smaller for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -56,10 +58,10 @@ def peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
-def workload(rank: int, seed: int):
-    from tree_training_b200.synthetic import config2_tree
+def workload(rank: int, seed: int, tokens: int = 16384):
+    from tree_training_b200.synthetic import bfs_tree
     import tree_training_b200 as tt
-    roots = config2_tree(seed + rank)
+    roots = bfs_tree(seed + rank, tokens, 64, 512, min(2048, tokens // 8))
     info = tt.build_dfs_tree_info(roots)
     meta = info.attn_meta()
     V = meta.visible_pairs
@@ -131,6 +133,32 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+class PhaseTimer:
+    """Records CUDA events between the backward's kernels (installed with
+    tree_training_b200.attention.set_phase_timer during the timed steps)."""
+
+    def __init__(self):
+        self.steps = []
+
+    def new_step(self):
+        self.steps.append({})
+
+    def mark(self, stream, name):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        self.steps[-1][name] = e
+
+    def durations(self):
+        out = {"attn_bwd_delta_tc": [], "attn_bwd_dkdv_tc": [], "attn_bwd_dq_tc": []}
+        for st in self.steps:
+            if "bwd_start" not in st:
+                continue
+            out["attn_bwd_delta_tc"].append(st["bwd_start"].elapsed_time(st["prep_done"]))
+            out["attn_bwd_dkdv_tc"].append(st["prep_done"].elapsed_time(st["dkdv_done"]))
+            out["attn_bwd_dq_tc"].append(st["prep_done"].elapsed_time(st["dq_done"]))
+        return {k: statistics.mean(v) / 1e3 for k, v in out.items() if v}
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -190,7 +218,7 @@ def run_reference(args):
     if rank != 0:
         return 0
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    _, info, meta, V = workload(0, args.seed)
+    _, info, meta, V = workload(0, args.seed, args.tokens)
     from oracle.ref_cpu import time_sample
     for _ in range(args.warmup):
         time_sample(meta, 4, 1, D, torch.bfloat16)
@@ -219,12 +247,13 @@ def run_reference(args):
 
 def run_ours(args):
     import tree_training_b200 as tt
+    from tree_training_b200.attention import set_phase_timer
     from tree_training_b200 import _lib
     world, rank, local = dist_env()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     init_dist(world, local)
-    roots, info, meta, V = workload(rank, args.seed)
+    roots, info, meta, V = workload(rank, args.seed, args.tokens)
     f_fwd, f_bwd = useful_flops(V)
     N = meta.n_q
     g = torch.Generator(device=dev).manual_seed(rank)
@@ -245,19 +274,23 @@ def run_ours(args):
     barrier(world)
 
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    timer = PhaseTimer()
     clocks = ClockSampler(dev)
     clocks.start()
     launches0 = _lib.lib().tt_kernel_launches()
     torch.cuda.synchronize()
     barrier(world)
+    set_phase_timer(timer)
     for i in range(args.steps):
         flush.zero_()                       # L2 flush between timed steps
         q.grad = k.grad = v.grad = None
+        timer.new_step()
         ev[i][0].record()
         out = tt.tree_attention(q, k, v, meta)
         ev[i][1].record()
         out.backward(do)
         ev[i][2].record()
+    set_phase_timer(None)
     torch.cuda.synchronize()
     barrier(world)
     launches = _lib.lib().tt_kernel_launches() - launches0
@@ -265,6 +298,7 @@ def run_ours(args):
     tt.check_device_status(dev)
     t_fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in ev) / 1e3
     t_bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in ev) / 1e3
+    kern = timer.durations()        # per-kernel seconds, live, on their own streams
     t_step = t_fwd + t_bwd
     t_max = max_over_ranks(t_step, world, dev)
     flops_all = sum_over_ranks(f_fwd + f_bwd, world, dev)
@@ -314,14 +348,22 @@ def run_ours(args):
     e2e_value = flops_all / t_e2e / 1e12
 
     pk, pk_src = peaks()
-    dominant = "bwd" if t_bwd >= t_fwd else "fwd"
-    achieved = (f_bwd / t_bwd if dominant == "bwd" else f_fwd / t_fwd) / 1e12
+    # algorithmic FLOPs of each kernel as designed (2*D per visible pair and GEMM):
+    # forward 2 GEMMs, dK/dV 4 (S^T, dP^T, dV, dK), dQ 3 (S, dP, dQ)
+    kflops = {"attn_fwd_tc": 4.0 * D * V * HQ, "attn_bwd_dkdv_tc": 8.0 * D * V * HQ,
+              "attn_bwd_dq_tc": 6.0 * D * V * HQ}
+    kern["attn_fwd_tc"] = t_fwd
+    dominant = max(kflops, key=lambda n: kern.get(n, 0.0))
+    achieved = kflops[dominant] / kern[dominant] / 1e12
     peak = float(pk["bf16_tflops"])
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "ncu_traffic.json")
-    if os.path.exists(tp):
+    tp = os.path.join(ROOT, "profiles", "tree_attn_config2_dram_traffic.txt")
+    if os.path.exists(tp) and args.tokens == 16384:
         with open(tp) as fh:
-            traffic = json.load(fh).get(dominant)
+            for ln in fh:
+                f = ln.split()
+                if len(f) == 2 and not ln.startswith("#") and f[0] == dominant:
+                    traffic = float(f[1])
 
     if rank == 0:
         line = {
@@ -341,7 +383,8 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": t_e2e * 1e3,
                     "tokens_per_s": tokens_all / t_e2e},
-            "roofline": {"bound": "tensor", "kernel": f"tree attention {dominant}",
+            "kernel_ms": {n: t * 1e3 for n, t in kern.items()},
+            "roofline": {"bound": "tensor", "kernel": dominant,
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": f"{pk_src} bf16 dense (burst)"},

@@ -156,7 +156,13 @@ int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t h
                      const int32_t* bwd_ptr, const int32_t* bwd_list, float scale, void* dq,
                      int64_t dq_st, int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh,
                      void* dv, int64_t dv_st, int64_t dv_sh, void* workspace,
-                     int64_t workspace_bytes, int32_t* status, void* stream);
+                     int64_t workspace_bytes, int phases, int32_t* status, void* stream);
+
+/* `phases` of tt_tree_attn_bwd (bitmask; TT_BWD_ALL runs the whole backward).
+ * PREP computes the fp32 row terms delta = rowsum(dO * O) into the workspace;
+ * DKDV and DQ read them and are independent of each other, so a caller may
+ * run them on two streams after PREP. */
+enum tt_bwd_phase { TT_BWD_PREP = 1, TT_BWD_DKDV = 2, TT_BWD_DQ = 4, TT_BWD_ALL = 7 };
 
 #ifdef __cplusplus
 }

@@ -23,6 +23,7 @@ TT_ERR_WORKSPACE = 6
 TT_ERR_CAPACITY = 7
 
 TT_F32, TT_BF16, TT_F16, TT_U8 = 0, 1, 2, 3
+TT_BWD_PREP, TT_BWD_DKDV, TT_BWD_DQ, TT_BWD_ALL = 1, 2, 4, 7
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -49,7 +50,7 @@ SIGNATURES = {
                                 _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
                                 _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _F32,
                                 _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
-                                _P, _I64, _P, _P]),
+                                _P, _I64, _INT, _P, _P]),
 }
 
 _lib = None

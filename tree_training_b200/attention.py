@@ -99,17 +99,57 @@ def attn_bwd_raw(dout, q, k, v, out, lse, meta_dev, scale: float):
     ws_bytes = int(_lib.lib().tt_tree_attn_bwd_workspace_size(dt, n_q, n_kv, hq, hkv, D))
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)
     out = out.contiguous()
-    _lib.call("tt_tree_attn_bwd", dt, n_q, n_kv, hq, hkv, D,
-              q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1),
-              v.data_ptr(), v.stride(0), v.stride(1), out.data_ptr(), dout.data_ptr(),
-              dout.stride(0), dout.stride(1), lse.data_ptr(), meta_dev["kv_lo"].data_ptr(),
-              meta_dev["kv_hi"].data_ptr(), meta_dev["fwd_ptr"].data_ptr(),
-              meta_dev["fwd_list"].data_ptr(), meta_dev["bwd_ptr"].data_ptr(),
-              meta_dev["bwd_list"].data_ptr(), float(scale),
-              dq.data_ptr(), dq.stride(0), dq.stride(1), dk.data_ptr(), dk.stride(0),
-              dk.stride(1), dv.data_ptr(), dv.stride(0), dv.stride(1), ws.data_ptr(), ws_bytes,
-              _status_word(q.device).data_ptr(), _stream_ptr(q.device))
+    args = [dt, n_q, n_kv, hq, hkv, D,
+            q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1),
+            v.data_ptr(), v.stride(0), v.stride(1), out.data_ptr(), dout.data_ptr(),
+            dout.stride(0), dout.stride(1), lse.data_ptr(), meta_dev["kv_lo"].data_ptr(),
+            meta_dev["kv_hi"].data_ptr(), meta_dev["fwd_ptr"].data_ptr(),
+            meta_dev["fwd_list"].data_ptr(), meta_dev["bwd_ptr"].data_ptr(),
+            meta_dev["bwd_list"].data_ptr(), float(scale),
+            dq.data_ptr(), dq.stride(0), dq.stride(1), dk.data_ptr(), dk.stride(0),
+            dk.stride(1), dv.data_ptr(), dv.stride(0), dv.stride(1), ws.data_ptr(), ws_bytes]
+    status = _status_word(q.device).data_ptr()
+    main = torch.cuda.current_stream(q.device)
+    timer = _PHASE_TIMER
+    if timer is not None:
+        timer.mark(main, "bwd_start")
+    _lib.call("tt_tree_attn_bwd", *args, _lib.TT_BWD_PREP, status, main.cuda_stream)
+    if timer is not None:
+        timer.mark(main, "prep_done")
+    # dK/dV and dQ only share read-only inputs: run them side by side
+    side = _side_stream(q.device)
+    side.wait_stream(main)
+    _lib.call("tt_tree_attn_bwd", *args, _lib.TT_BWD_DKDV, status, main.cuda_stream)
+    if timer is not None:
+        timer.mark(main, "dkdv_done")
+    with torch.cuda.stream(side):
+        _lib.call("tt_tree_attn_bwd", *args, _lib.TT_BWD_DQ, status, side.cuda_stream)
+        if timer is not None:
+            timer.mark(side, "dq_done")
+    main.wait_stream(side)
+    for t in (ws, dq, q, k, v, out, dout, lse):
+        t.record_stream(side)
     return dq, dk, dv
+
+
+_side_streams: dict = {}
+_PHASE_TIMER = None
+
+
+def _side_stream(device) -> torch.cuda.Stream:
+    s = _side_streams.get(device)
+    if s is None:
+        s = torch.cuda.Stream(device=device)
+        _side_streams[device] = s
+    return s
+
+
+def set_phase_timer(timer) -> None:
+    """Install an object with ``mark(stream, name)`` that records CUDA events
+    between the backward's kernels (used by bench.py to time each kernel
+    live); ``None`` removes it."""
+    global _PHASE_TIMER
+    _PHASE_TIMER = timer
 
 
 # -----------------------------------------------------------------------------

@@ -105,8 +105,8 @@ extern "C" int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq
                                 const int32_t* bwd_ptr, const int32_t* bwd_list, float scale,
                                 void* dq, int64_t dq_st, int64_t dq_sh, void* dk, int64_t dk_st,
                                 int64_t dk_sh, void* dv, int64_t dv_st, int64_t dv_sh,
-                                void* workspace, int64_t workspace_bytes, int32_t* status,
-                                void* stream) {
+                                void* workspace, int64_t workspace_bytes, int phases,
+                                int32_t* status, void* stream) {
   if (!valid_dims(n_q, n_kv, hq, hkv, D)) return TT_ERR_INVALID_ARG;
   if (workspace_bytes < tt_tree_attn_bwd_workspace_size(dtype, n_q, n_kv, hq, hkv, D))
     return TT_ERR_WORKSPACE;
@@ -117,10 +117,11 @@ extern "C" int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq
     return tt_launch_attn_bwd_sm100(dtype, n_q, n_kv, hq, hkv, D, q, q_st, q_sh, k, k_st, k_sh, v,
                                     v_st, v_sh, out, dout, do_st, do_sh, lse, kv_lo, kv_hi,
                                     fwd_ptr, fwd_list, bwd_ptr, bwd_list, scale, dq, dq_st, dq_sh,
-                                    dk, dk_st, dk_sh, dv, dv_st, dv_sh, (float*)workspace, status,
+                                    dk, dk_st, dk_sh, dv, dv_st, dv_sh, (float*)workspace, phases, status,
                                     (cudaStream_t)stream);
   return tt_launch_attn_bwd_simt(dtype, n_q, n_kv, hq, hkv, D, q, q_st, q_sh, k, k_st, k_sh, v,
                                  v_st, v_sh, out, dout, do_st, do_sh, lse, kv_lo, kv_hi, fwd_ptr,
                                  fwd_list, bwd_ptr, bwd_list, scale, dq, dq_st, dq_sh, dk, dk_st,
-                                 dk_sh, dv, dv_st, dv_sh, (float*)workspace, (cudaStream_t)stream);
+                                 dk_sh, dv, dv_st, dv_sh, (float*)workspace, phases,
+                                 (cudaStream_t)stream);
 }

@@ -573,8 +573,8 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
                              const int32_t* fwd_list, const int32_t* bwd_ptr,
                              const int32_t* bwd_list, float scale, void* dq, int64_t dq_st,
                              int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
-                             int64_t dv_st, int64_t dv_sh, float* delta, int32_t* status,
-                             cudaStream_t st) {
+                             int64_t dv_st, int64_t dv_sh, float* delta, int phases,
+                             int32_t* status, cudaStream_t st) {
   using namespace tt::sm100;
   if (D != kD || (dtype != TT_BF16 && dtype != TT_F16)) return TT_ERR_UNSUPPORTED;
   if (!aligned16(kv_lo) || !aligned16(kv_hi) || !aligned16(lse) || !aligned16(delta) ||
@@ -585,8 +585,10 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
   const bool bf16 = dtype == TT_BF16;
   if (n_q == 0 || n_kv == 0) {
     // one side empty: every gradient on the other side is zero
-    int n = zero_grad(dk, n_kv, hkv, dk_st, dk_sh, st) + zero_grad(dv, n_kv, hkv, dv_st, dv_sh, st) +
-            zero_grad(dq, n_q, hq, dq_st, dq_sh, st);
+    int n = 0;
+    if (phases & TT_BWD_DKDV)
+      n += zero_grad(dk, n_kv, hkv, dk_st, dk_sh, st) + zero_grad(dv, n_kv, hkv, dv_st, dv_sh, st);
+    if (phases & TT_BWD_DQ) n += zero_grad(dq, n_q, hq, dq_st, dq_sh, st);
     tt_count_launches(n);
     return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
   }
@@ -599,7 +601,7 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
   const int ld = tt::lse_ld(n_q);
   const int warps = ld * hq;
   int launches = 0;
-  if (warps > 0) {
+  if (warps > 0 && (phases & TT_BWD_PREP)) {
     if (bf16)
       attn_bwd_delta_tc<__nv_bfloat16><<<(warps + 7) / 8, 256, 0, st>>>(
           n_q, hq, (const __nv_bfloat16*)out, (const __nv_bfloat16*)dout, do_st, do_sh, delta);
@@ -610,7 +612,7 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
   }
   const float scale_log2 = scale * 1.4426950408889634f;
   const int rep = hq / hkv;
-  {
+  if (phases & TT_BWD_DKDV) {
     auto kdkdv = bf16 ? attn_bwd_dkdv_tc<true> : attn_bwd_dkdv_tc<false>;
     TT_CUDA_OK(cudaFuncSetAttribute(kdkdv, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemBytes));
@@ -620,7 +622,7 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
                                            dk_st, dk_sh, dv, dv_st, dv_sh, status);
     ++launches;
   }
-  {
+  if (phases & TT_BWD_DQ) {
     auto kdq = bf16 ? attn_bwd_dq_tc<true> : attn_bwd_dq_tc<false>;
     TT_CUDA_OK(cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemBytes));

@@ -384,30 +384,37 @@ int launch_bwd(int n_q, int n_kv, int hq, int hkv, const void* q, int64_t q_st, 
                const float* lse, const int32_t* lo, const int32_t* hi, const int32_t* fp,
                const int32_t* fl, const int32_t* bp, const int32_t* bl, float scale, void* dq,
                int64_t dq_st, int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
-               int64_t dv_st, int64_t dv_sh, float* delta, cudaStream_t st) {
+               int64_t dv_st, int64_t dv_sh, float* delta, int phases, cudaStream_t st) {
   const int rep = hq / hkv;
   const int warps = lse_ld(n_q) * hq;
-  if (warps > 0)
+  int launches = 0;
+  if (warps > 0 && (phases & TT_BWD_PREP)) {
+    ++launches;
     attn_bwd_delta<T><<<(warps + 7) / 8, 256, 0, st>>>(n_q, hq, D, (const T*)out, (const T*)dout,
                                                         do_st, do_sh, delta);
+  }
   const size_t smem_kv = 2 * kBQ * D * sizeof(float) + 2 * kBQ * sizeof(float);
   auto kkv = attn_bwd_dkdv_simt<T, D>;
   TT_CUDA_OK(cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_kv));
   dim3 gkv((n_kv + kBK - 1) / kBK, hkv);
-  if (n_kv > 0)
+  if (n_kv > 0 && (phases & TT_BWD_DKDV)) {
+    ++launches;
     kkv<<<gkv, kThreads, smem_kv, st>>>(n_q, n_kv, hq, rep, (const T*)q, q_st, q_sh, (const T*)k,
                                         k_st, k_sh, (const T*)v, v_st, v_sh, (const T*)dout, do_st,
                                         do_sh, lse, delta, lo, hi, bp, bl, scale, (T*)dk, dk_st,
                                         dk_sh, (T*)dv, dv_st, dv_sh);
+  }
   const size_t smem_q = 2 * kBK * D * sizeof(float) + 2 * kBK * sizeof(int32_t);
   auto kq = attn_bwd_dq_simt<T, D>;
   TT_CUDA_OK(cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_q));
   dim3 gq((n_q + kBQ - 1) / kBQ, hq);
-  if (n_q > 0)
+  if (n_q > 0 && (phases & TT_BWD_DQ)) {
+    ++launches;
     kq<<<gq, kThreads, smem_q, st>>>(n_q, n_kv, rep, (const T*)q, q_st, q_sh, (const T*)k, k_st,
                                      k_sh, (const T*)v, v_st, v_sh, (const T*)dout, do_st, do_sh,
                                      lse, delta, lo, hi, fp, fl, scale, (T*)dq, dq_st, dq_sh);
-  tt_count_launches((warps > 0) + (n_kv > 0) + (n_q > 0));
+  }
+  tt_count_launches(launches);
   return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
 }
 
@@ -468,11 +475,11 @@ int tt_launch_attn_bwd_simt(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, in
                             const int32_t* bwd_ptr, const int32_t* bwd_list, float scale,
                             void* dq, int64_t dq_st, int64_t dq_sh, void* dk, int64_t dk_st,
                             int64_t dk_sh, void* dv, int64_t dv_st, int64_t dv_sh, float* delta,
-                            cudaStream_t st) {
+                            int phases, cudaStream_t st) {
 #define TT_BWD_ARGS                                                                          \
   n_q, n_kv, hq, hkv, q, q_st, q_sh, k, k_st, k_sh, v, v_st, v_sh, out, dout, do_st, do_sh, lse, \
       kv_lo, kv_hi, fwd_ptr, fwd_list, bwd_ptr, bwd_list, scale, dq, dq_st, dq_sh, dk, dk_st,    \
-      dk_sh, dv, dv_st, dv_sh, delta, st
+      dk_sh, dv, dv_st, dv_sh, delta, phases, st
   switch (D) {
     case 32: return tt::dispatch_bwd_dtype<32>(dtype, TT_BWD_ARGS);
     case 64: return tt::dispatch_bwd_dtype<64>(dtype, TT_BWD_ARGS);

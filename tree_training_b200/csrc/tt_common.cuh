@@ -71,7 +71,7 @@ int tt_launch_attn_bwd_simt(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, in
                             const int32_t* bwd_ptr, const int32_t* bwd_list, float scale,
                             void* dq, int64_t dq_st, int64_t dq_sh, void* dk, int64_t dk_st,
                             int64_t dk_sh, void* dv, int64_t dv_st, int64_t dv_sh, float* delta,
-                            cudaStream_t stream);
+                            int phases, cudaStream_t stream);
 int tt_launch_mask_to_intervals(int mask_dtype, int32_t n_q, int32_t n_kv, const void* mask,
                                 int64_t stride_q, int64_t stride_kv, int32_t* kv_lo,
                                 int32_t* kv_hi, int32_t* status, cudaStream_t stream);
@@ -93,5 +93,5 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
                              const int32_t* fwd_list, const int32_t* bwd_ptr,
                              const int32_t* bwd_list, float scale, void* dq, int64_t dq_st,
                              int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
-                             int64_t dv_st, int64_t dv_sh, float* delta, int32_t* status,
-                             cudaStream_t stream);
+                             int64_t dv_st, int64_t dv_sh, float* delta, int phases,
+                             int32_t* status, cudaStream_t stream);
