@@ -164,6 +164,32 @@ int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t h
  * run them on two streams after PREP. */
 enum tt_bwd_phase { TT_BWD_PREP = 1, TT_BWD_DKDV = 2, TT_BWD_DQ = 4, TT_BWD_ALL = 7 };
 
+/* Allocation-free variant of tt_tree_attn_bwd (same arguments without the
+ * workspace and phases; no counterpart in the reference).  For callers that
+ * cannot pass a scratch buffer and must not have the library call cudaMalloc
+ * (a binding that mirrors the reference's inputs-and-outputs call, or a
+ * runtime whose device memory belongs to its own pooling allocator).  Scratch
+ * lives in a fixed 8 MiB array inside the library's device image, held by
+ * every GPU that loads the library until exit: problems with
+ * hq * round_up(n_q, 128) > tt_tree_attn_bwd_noalloc_max_row_terms() are
+ * rejected with TT_ERR_WORKSPACE before anything runs.  The first call on a
+ * device looks the array up (make it before any stream capture; the device of
+ * the pointers must be current); every call shares the array, so calls whose
+ * kernels overlap on the GPU race.  Calls no allocating routine. */
+int tt_tree_attn_bwd_noalloc(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv,
+                             int32_t head_dim, const void* q, int64_t q_st, int64_t q_sh,
+                             const void* k, int64_t k_st, int64_t k_sh, const void* v,
+                             int64_t v_st, int64_t v_sh, const void* out, const void* dout,
+                             int64_t do_st, int64_t do_sh, const float* lse,
+                             const int32_t* kv_lo, const int32_t* kv_hi, const int32_t* fwd_ptr,
+                             const int32_t* fwd_list, const int32_t* bwd_ptr,
+                             const int32_t* bwd_list, float scale, void* dq, int64_t dq_st,
+                             int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
+                             int64_t dv_st, int64_t dv_sh, int32_t* status, void* stream);
+
+/* Largest hq * round_up(n_q, 128) that tt_tree_attn_bwd_noalloc accepts. */
+int64_t tt_tree_attn_bwd_noalloc_max_row_terms(void);
+
 #ifdef __cplusplus
 }
 #endif
