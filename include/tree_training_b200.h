@@ -146,7 +146,10 @@ int64_t tt_tree_attn_bwd_workspace_size(int dtype, int32_t n_q, int32_t n_kv, in
  * [n_q, hq, head_dim] (token/head strides given for dout); dq, dk, dv are
  * written with the given strides (dk/dv include the gateway keys, so the
  * gateway leaf tensors get gradients as with SDPA).  Deterministic for
- * dk/dv.  fwd lists drive the dQ pass, bwd lists the dK/dV pass. */
+ * dk/dv.  fwd lists drive the dQ pass, bwd lists the dK/dV pass.  On the
+ * tcgen05 path kv_lo/kv_hi must be readable up to round_up(n_kv, 128) entries
+ * with zeros past n_kv (whole 128-key tiles are bulk-copied), and lse, the
+ * workspace and all outputs must be 16-byte aligned. */
 int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv,
                      int32_t head_dim, const void* q, int64_t q_st, int64_t q_sh,
                      const void* k, int64_t k_st, int64_t k_sh, const void* v, int64_t v_st,

@@ -7,18 +7,25 @@
 //
 //   dK/dV kernel  one CTA per (kv head, 128-key tile); loops over the q heads
 //                 of its GQA group and the q tiles the work list marks
-//                 visible.  S^T = K Q^T and dP^T = V dO^T (A, B from shared
-//                 memory); the softmax warps turn them into P^T and
-//                 dS^T = P^T (dP^T - delta) and store both back into TMEM as
-//                 16-bit; then dV += P^T dO and dK += dS^T Q read A from TMEM.
-//   dQ kernel     one CTA per (q head, 128-row tile), the forward's loop:
+//                 visible, in 64-row sub-tiles.  S^T = K Q^T and
+//                 dP^T = V dO^T (A, B from shared memory); the elementwise
+//                 warps turn them into P^T and dS^T = P^T (dP^T - delta) and
+//                 write both back into TMEM as 16-bit; then dV += P^T dO and
+//                 dK += dS^T Q read A from TMEM.
+//   dQ kernel     one CTA per (q head, 128-row tile), in 64-key sub-tiles:
 //                 S = Q K^T, dP = dO V^T, dS = P (dP - delta) into TMEM,
 //                 dQ += dS K.
 //
-// TMEM (512 columns): dK/dV kernel S^T|P^T [0,128), dP^T|dS^T [128,256),
-// dV [256,384), dK [384,512); dQ kernel S|dS [0,128), dP [128,256),
-// dQ [256,384).  Warp roles as in the forward: warp 0 TMA, warp 1 MMA,
-// warps 2-5 elementwise (one thread per TMEM lane).
+// Sub-tile accumulators are double buffered in TMEM so the MMAs of sub-tile
+// u+1 run while the elementwise warps process sub-tile u.  TMEM (512 cols):
+//   buffer b in {0,1}: S [64b, 64b+64), dP [128+64b, 128+64b+64)
+//   dK/dV kernel: dV [256,384), dK [384,512);  dQ kernel: dQ [256,384).
+// Warps: 0 TMA producer, 1 MMA issuer, 2..9 elementwise (two warps per TMEM
+// lane quadrant; warp half h owns columns [32h, 32h+32) of each sub-tile and
+// writes its 16-bit P / dS into the first 16 of those columns, i.e. only into
+// columns it has already read, so the two warps never race).  LSE/delta (dK/dV)
+// and the key intervals (dQ) of each streamed tile are bulk-copied into shared
+// memory on the same mbarrier as the tile.
 #include <type_traits>
 
 #include "tt_sm100.cuh"
@@ -27,28 +34,33 @@ namespace tt {
 namespace sm100 {
 namespace {
 
-constexpr int kT = 128;                   // rows per tile (keys or queries)
-constexpr int kD = 128;                   // head dim
+constexpr int kT = 128;                    // rows per tile (keys or queries)
+constexpr int kD = 128;                    // head dim
+constexpr int kSub = 64;                   // sub-tile width along the streamed dim
 constexpr int kTileBytes = kT * kD * 2;
-constexpr int kHalfBytes = kTileBytes / 2;
-constexpr int kThreads = 192;
+constexpr int kHalfBytes = kTileBytes / 2; // one 64-dim swizzle block of 128 rows
+constexpr int kSubOff = kSub * 128;        // byte offset of sub-tile 1 inside a block
+constexpr int kThreads = 320;
+constexpr int kEw = 256;                   // elementwise threads
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdBarriers {
   uint64_t fixed_full;      // the tiles loaded once (K,V or Q,dO)
-  uint64_t a_full[2];       // streamed tile A (Q or K)
+  uint64_t a_full[2];       // streamed tile A (Q or K) + its row/key terms
   uint64_t b_full[2];       // streamed tile B (dO or V)
   uint64_t ab_empty[2];
-  uint64_t sdp_full;        // S and dP accumulators ready
-  uint64_t ew_full;         // P / dS written back to TMEM (128 arrivals)
+  uint64_t sdp_full[2];     // S and dP of a sub-tile ready (per TMEM buffer)
+  uint64_t ew_full[2];      // P / dS of a sub-tile written back (256 arrivals)
   uint64_t acc_done;        // every MMA of the CTA finished
   uint64_t drain;
   uint32_t tmem_base;
   int32_t abort;
 };
 
-constexpr size_t kSmemBytes = 1024 + 6 * kTileBytes + sizeof(BwdBarriers);
+// per stage: two 128-entry 4-byte arrays (LSE + delta, or kv_lo + kv_hi)
+constexpr int kAuxBytes = 2 * kT * 4;
+constexpr size_t kSmemBytes = 1024 + 6 * kTileBytes + 2 * kAuxBytes + sizeof(BwdBarriers);
 
 __device__ __forceinline__ void raise_abort(BwdBarriers* sh, int32_t* status) {
   set_status(status, TT_ERR_DEVICE_TIMEOUT);
@@ -61,18 +73,19 @@ __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
     mbar_init(&sh->a_full[s], 1);
     mbar_init(&sh->b_full[s], 1);
     mbar_init(&sh->ab_empty[s], 1);
+    mbar_init(&sh->sdp_full[s], 1);
+    mbar_init(&sh->ew_full[s], kEw);
   }
-  mbar_init(&sh->sdp_full, 1);
-  mbar_init(&sh->ew_full, 128);
   mbar_init(&sh->acc_done, 1);
   mbar_init(&sh->drain, 1);
   sh->abort = 0;
   fence_mbar_init();
 }
 
-// 128x128 (K = 128) product of two K-major 128-byte-swizzled smem tiles.
-__device__ __forceinline__ void mma_tile_ss(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr,
-                                            uint32_t idesc) {
+// D[128 x 64] = A[128 rows] * B[64 rows]^T over K = 128 dims; both operands are
+// K-major 128-byte-swizzled smem tiles, b_addr = first row of the 64-row block.
+__device__ __forceinline__ void mma_ss_n64(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr,
+                                           uint32_t idesc) {
 #pragma unroll
   for (int kk = 0; kk < kD / 16; ++kk) {
     const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
@@ -81,14 +94,17 @@ __device__ __forceinline__ void mma_tile_ss(uint32_t d_tmem, uint32_t a_addr, ui
   }
 }
 
-// D[128 x 128] (+)= A[128 x 128 from TMEM, 16-bit] * B, B an MN-major smem
-// tile [K rows][128] (K = 128 rows of 128 dims).
-__device__ __forceinline__ void mma_tile_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr,
-                                            uint32_t idesc, bool accumulate) {
+// D[128 x 128] (+)= A[128 x 64, 16-bit in TMEM] * B[64 rows x 128 dims], B an
+// MN-major smem block starting at row b_addr.  A's 64 columns of K sit as two
+// 16-column groups at a_tmem and a_tmem + 32 (one per elementwise warp half).
+__device__ __forceinline__ void mma_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr,
+                                           uint32_t idesc, bool accumulate) {
 #pragma unroll
-  for (int kk = 0; kk < kT / 16; ++kk)
-    mma_ts(d_tmem, a_tmem + kk * 8, desc_sw128(b_addr + kk * 2048, kHalfBytes, 1024), idesc,
+  for (int kk = 0; kk < kSub / 16; ++kk) {
+    const uint32_t a = a_tmem + (kk < 2 ? kk * 8 : 32 + (kk - 2) * 8);
+    mma_ts(d_tmem, a, desc_sw128(b_addr + kk * 2048, kHalfBytes, 1024), idesc,
            (accumulate || kk > 0) ? 1u : 0u);
+  }
 }
 
 template <bool kBf16>
@@ -99,6 +115,93 @@ __device__ __forceinline__ void store_row32(void* base, const float (&v)[32], fl
   uint4* dst = reinterpret_cast<uint4*>(base);
 #pragma unroll
   for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) &
+                                    ~static_cast<uintptr_t>(1023));
+}
+
+// Streams `n_it` (A, B) tile pairs through the 2-stage ring; `coord(it, &row,
+// &head, &aux_a, &aux_b)` gives the tile row / head and the two 512-byte
+// arrays to bulk-copy with tile A.
+template <typename Coord>
+__device__ __forceinline__ void produce(BwdBarriers* sh, const volatile int32_t* abort_flag,
+                                        int32_t* status, int n_it, uint8_t* sA, uint8_t* sB,
+                                        uint8_t* aux, const CUtensorMap* ta,
+                                        const CUtensorMap* tb, Coord coord) {
+  int issued[2] = {0, 0};
+  bool ok = true;
+  for (int it = 0; it < n_it; ++it) {
+    const int s = it & 1;
+    if (it >= 2) ok = mbar_wait(&sh->ab_empty[s], ((it >> 1) - 1) & 1, abort_flag);
+    if (!ok) break;
+    int row, head;
+    const void *xa, *xb;
+    coord(it, &row, &head, &xa, &xb);
+    uint8_t* a_dst = sA + s * kTileBytes;
+    uint8_t* b_dst = sB + s * kTileBytes;
+    uint8_t* x_dst = aux + s * kAuxBytes;
+    mbar_arrive_expect_tx(&sh->a_full[s], kTileBytes + kAuxBytes);
+    tma_load_3d(a_dst, ta, &sh->a_full[s], 0, row, head);
+    tma_load_3d(a_dst + kHalfBytes, ta, &sh->a_full[s], 64, row, head);
+    bulk_load(x_dst, xa, kAuxBytes / 2, &sh->a_full[s]);
+    bulk_load(x_dst + kAuxBytes / 2, xb, kAuxBytes / 2, &sh->a_full[s]);
+    mbar_arrive_expect_tx(&sh->b_full[s], kTileBytes);
+    tma_load_3d(b_dst, tb, &sh->b_full[s], 0, row, head);
+    tma_load_3d(b_dst + kHalfBytes, tb, &sh->b_full[s], 64, row, head);
+    issued[s] += 1;
+  }
+  if (!ok) {
+    raise_abort(sh, status);
+    mbar_wait(&sh->fixed_full, 0, nullptr);
+    for (int s = 0; s < 2; ++s)
+      if (issued[s] > 0) {
+        mbar_wait(&sh->a_full[s], (issued[s] - 1) & 1, nullptr);
+        mbar_wait(&sh->b_full[s], (issued[s] - 1) & 1, nullptr);
+      }
+  }
+}
+
+// MMA issue loop shared by both kernels.  For sub-tile u (tile it = u/2,
+// half sb = u%2, stage s = it%2, TMEM buffer b = sb):
+//   sdp(u):  S_b = X * A[sb]^T, dP_b = Y * B[sb]^T   (X, Y fixed tiles)
+//   acc(u):  per-kernel TS products reading P_b / dS_b
+template <typename Acc>
+__device__ __forceinline__ void mma_loop(BwdBarriers* sh, const volatile int32_t* abort_flag,
+                                         int32_t* status, uint32_t tmem, int n_it,
+                                         uint32_t x_addr, uint32_t y_addr, uint32_t a_addr,
+                                         uint32_t b_addr, uint32_t id_s, Acc acc) {
+  const int n_u = 2 * n_it;
+  bool ok = mbar_wait(&sh->fixed_full, 0, abort_flag);
+  auto sdp = [&](int u) -> bool {
+    const int it = u >> 1, sb = u & 1, s = it & 1;
+    if (sb == 0) {
+      if (!mbar_wait(&sh->a_full[s], (it >> 1) & 1, abort_flag)) return false;
+      if (!mbar_wait(&sh->b_full[s], (it >> 1) & 1, abort_flag)) return false;
+      tc_fence_after();
+    }
+    const uint32_t off = s * kTileBytes + sb * kSubOff;
+    mma_ss_n64(tmem + 64 * sb, x_addr, a_addr + off, id_s);
+    mma_ss_n64(tmem + 128 + 64 * sb, y_addr, b_addr + off, id_s);
+    tc_commit(&sh->sdp_full[sb]);
+    return true;
+  };
+  if (ok && n_u > 0) ok = sdp(0);
+  for (int u = 0; u < n_u && ok; ++u) {
+    if (u + 1 < n_u && !(ok = sdp(u + 1))) break;
+    const int sb = u & 1, s = (u >> 1) & 1;
+    if (!(ok = mbar_wait(&sh->ew_full[sb], (u >> 1) & 1, abort_flag))) break;
+    tc_fence_after();
+    acc(u, s, sb, u > 0);
+    if (sb == 1) tc_commit(&sh->ab_empty[s]);
+  }
+  tc_commit(&sh->acc_done);
+  if (!ok) {
+    raise_abort(sh, status);
+    tc_commit(&sh->drain);
+    mbar_wait(&sh->drain, 0, nullptr);
+  }
 }
 
 // ===================================================================== dK/dV
@@ -114,13 +217,13 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                  int64_t dv_st, int64_t dv_sh, int32_t* status) {
   using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* base = align1024(smem_raw);
   uint8_t* sK = base;
   uint8_t* sV = sK + kTileBytes;
   uint8_t* sQ = sV + kTileBytes;           // 2 stages
   uint8_t* sDO = sQ + 2 * kTileBytes;      // 2 stages
-  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(sDO + 2 * kTileBytes);
+  uint8_t* aux = sDO + 2 * kTileBytes;     // 2 stages x (LSE[128], delta[128])
+  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + 2 * kAuxBytes);
   const volatile int32_t* abort_flag = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -140,7 +243,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
-  constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384;
+  constexpr uint32_t kColDV = 256, kColDK = 384;
 
   if (warp == 0) {
     if (lane == 0 && n_it > 0) {
@@ -151,116 +254,79 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tma_load_3d(sK + kHalfBytes, &tm_k, &sh->fixed_full, 64, kt * kT, hk);
       tma_load_3d(sV, &tm_v, &sh->fixed_full, 0, kt * kT, hk);
       tma_load_3d(sV + kHalfBytes, &tm_v, &sh->fixed_full, 64, kt * kT, hk);
-      int issued[2] = {0, 0};
-      bool ok = true;
-      for (int it = 0; it < n_it; ++it) {
-        const int s = it & 1;
-        if (it >= 2) ok = mbar_wait(&sh->ab_empty[s], ((it >> 1) - 1) & 1, abort_flag);
-        if (!ok) break;
-        const int h = hk * rep + it / n_list;
-        const int qt = bwd_list[e0 + it % n_list] >> 1;
-        uint8_t* q_dst = sQ + s * kTileBytes;
-        uint8_t* o_dst = sDO + s * kTileBytes;
-        mbar_arrive_expect_tx(&sh->a_full[s], kTileBytes);
-        tma_load_3d(q_dst, &tm_q, &sh->a_full[s], 0, qt * kT, h);
-        tma_load_3d(q_dst + kHalfBytes, &tm_q, &sh->a_full[s], 64, qt * kT, h);
-        mbar_arrive_expect_tx(&sh->b_full[s], kTileBytes);
-        tma_load_3d(o_dst, &tm_do, &sh->b_full[s], 0, qt * kT, h);
-        tma_load_3d(o_dst + kHalfBytes, &tm_do, &sh->b_full[s], 64, qt * kT, h);
-        issued[s] += 1;
-      }
-      if (!ok) {
-        raise_abort(sh, status);
-        mbar_wait(&sh->fixed_full, 0, nullptr);
-        for (int s = 0; s < 2; ++s)
-          if (issued[s] > 0) {
-            mbar_wait(&sh->a_full[s], (issued[s] - 1) & 1, nullptr);
-            mbar_wait(&sh->b_full[s], (issued[s] - 1) & 1, nullptr);
-          }
-      }
+      produce(sh, abort_flag, status, n_it, sQ, sDO, aux, &tm_q, &tm_do,
+              [&](int it, int* row, int* head, const void** xa, const void** xb) {
+                const int h = hk * rep + it / n_list;
+                const int q0 = (bwd_list[e0 + it % n_list] >> 1) * kT;
+                *row = q0;
+                *head = h;
+                *xa = lse + static_cast<int64_t>(h) * ld + q0;
+                *xb = delta + static_cast<int64_t>(h) * ld + q0;
+              });
     }
   } else if (warp == 1) {
     if (lane == 0 && n_it > 0) {
-      constexpr uint32_t id_ss = idesc_f16(kBf16, kT, kT, false);
-      constexpr uint32_t id_ts = idesc_f16(kBf16, kT, kD, true);
-      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
+      constexpr uint32_t id_o = idesc_f16(kBf16, kT, kD, true);
       const uint32_t q_addr = smem_u32(sQ), o_addr = smem_u32(sDO);
-      bool ok = mbar_wait(&sh->fixed_full, 0, abort_flag);
-      for (int it = 0; it < n_it && ok; ++it) {
-        const int s = it & 1;
-        ok = mbar_wait(&sh->a_full[s], (it >> 1) & 1, abort_flag);
-        if (ok) ok = mbar_wait(&sh->b_full[s], (it >> 1) & 1, abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-        mma_tile_ss(tmem + kColS, k_addr, q_addr + s * kTileBytes, id_ss);    // S^T = K Q^T
-        mma_tile_ss(tmem + kColDP, v_addr, o_addr + s * kTileBytes, id_ss);   // dP^T = V dO^T
-        tc_commit(&sh->sdp_full);
-        ok = mbar_wait(&sh->ew_full, it & 1, abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-        mma_tile_ts(tmem + kColDV, tmem + kColS, o_addr + s * kTileBytes, id_ts, it > 0);
-        mma_tile_ts(tmem + kColDK, tmem + kColDP, q_addr + s * kTileBytes, id_ts, it > 0);
-        tc_commit(&sh->ab_empty[s]);
-      }
-      tc_commit(&sh->acc_done);
-      if (!ok) {
-        raise_abort(sh, status);
-        tc_commit(&sh->drain);
-        mbar_wait(&sh->drain, 0, nullptr);
-      }
+      mma_loop(sh, abort_flag, status, tmem, n_it, smem_u32(sK), smem_u32(sV), q_addr, o_addr,
+               id_s, [&](int u, int s, int sb, bool accumulate) {
+                 const uint32_t off = s * kTileBytes + sb * kSubOff;
+                 mma_ts_k64(tmem + kColDV, tmem + 64 * sb, o_addr + off, id_o, accumulate);
+                 mma_ts_k64(tmem + kColDK, tmem + 128 + 64 * sb, q_addr + off, id_o, accumulate);
+               });
     }
   } else {
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;          // key within the tile = TMEM lane
     const int j = kt * kT + r;
     const int lo = j < n_kv ? kv_lo[j] : 0;
     const int hi = j < n_kv ? kv_hi[j] : 0;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     bool ok = true;
-    for (int it = 0; it < n_it; ++it) {
-      const int h = hk * rep + it / n_list;
+    const int n_u = 2 * n_it;
+    for (int u = 0; u < n_u; ++u) {
+      const int it = u >> 1, sb = u & 1, s = it & 1;
       const int ent = bwd_list[e0 + it % n_list];
-      const int q0 = (ent >> 1) * kT;
+      const int c0 = sb * kSub + half * 32;   // first q column (within the tile) of this warp
+      const int q0 = (ent >> 1) * kT + c0;
       const bool partial = ent & 1;
-      const float4* lse4 = reinterpret_cast<const float4*>(lse + static_cast<int64_t>(h) * ld + q0);
-      const float4* del4 = reinterpret_cast<const float4*>(delta + static_cast<int64_t>(h) * ld + q0);
-      ok = mbar_wait(&sh->sdp_full, it & 1, abort_flag);
+      ok = mbar_wait(&sh->sdp_full[sb], (u >> 1) & 1, abort_flag);
+      if (ok && sb == 0) ok = mbar_wait(&sh->a_full[s], (it >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < kT / 32; ++c) {
-        float sv[32], dp[32];
-        tmem_ld32(lane_addr + kColS + c * 32, sv);
-        tmem_ld32(lane_addr + kColDP + c * 32, dp);
-        uint32_t pw[16], dw[16];
+      const uint32_t cs = 64 * sb + 32 * half, cp = 128 + 64 * sb + 32 * half;
+      float sv[32], dp[32];
+      tmem_ld32(lane_addr + cs, sv);
+      tmem_ld32(lane_addr + cp, dp);
+      const float4* L4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes) + c0 / 4;
+      const float4* D4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes + kAuxBytes / 2) + c0 / 4;
+      uint32_t pw[16], dw[16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 l4 = __ldg(lse4 + c * 8 + i);
-          const float4 d4 = __ldg(del4 + c * 8 + i);
-          const float la[4] = {l4.x, l4.y, l4.z, l4.w};
-          const float da[4] = {d4.x, d4.y, d4.z, d4.w};
-          float p[4], ds[4];
+      for (int i = 0; i < 8; ++i) {
+        const float4 l4 = L4[i], d4 = D4[i];
+        const float la[4] = {l4.x, l4.y, l4.z, l4.w};
+        const float da[4] = {d4.x, d4.y, d4.z, d4.w};
+        float p[4], ds[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int col = c * 32 + i * 4 + u;
-            float pv = exp2f(fmaf(sv[i * 4 + u], scale_log2, -la[u] * kLog2e));
-            if (partial && !visible(lo, hi, q0 + col)) pv = 0.f;
-            p[u] = pv;
-            ds[u] = pv * (dp[i * 4 + u] - da[u]);
-          }
-          pw[2 * i] = pack2<kBf16>(p[0], p[1]);
-          pw[2 * i + 1] = pack2<kBf16>(p[2], p[3]);
-          dw[2 * i] = pack2<kBf16>(ds[0], ds[1]);
-          dw[2 * i + 1] = pack2<kBf16>(ds[2], ds[3]);
+        for (int w = 0; w < 4; ++w) {
+          float pv = exp2f(fmaf(sv[4 * i + w], scale_log2, -la[w] * kLog2e));
+          if (partial && !visible(lo, hi, q0 + 4 * i + w)) pv = 0.f;
+          p[w] = pv;
+          ds[w] = pv * (dp[4 * i + w] - da[w]);
         }
-        // 16 packed columns; chunk c overwrites columns already read
-        tmem_st16(lane_addr + kColS + c * 16, pw);
-        tmem_st16(lane_addr + kColDP + c * 16, dw);
+        pw[2 * i] = pack2<kBf16>(p[0], p[1]);
+        pw[2 * i + 1] = pack2<kBf16>(p[2], p[3]);
+        dw[2 * i] = pack2<kBf16>(ds[0], ds[1]);
+        dw[2 * i + 1] = pack2<kBf16>(ds[2], ds[3]);
       }
+      tmem_st16(lane_addr + cs, pw);
+      tmem_st16(lane_addr + cp, dw);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&sh->ew_full);
+      mbar_arrive(&sh->ew_full[sb]);
     }
     if (ok && n_it > 0) {
       ok = mbar_wait(&sh->acc_done, 0, abort_flag);
@@ -272,7 +338,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       T* dv = reinterpret_cast<T*>(dv_) + static_cast<int64_t>(j) * dv_st + hk * dv_sh;
       T* dk = reinterpret_cast<T*>(dk_) + static_cast<int64_t>(j) * dk_st + hk * dk_sh;
 #pragma unroll 1
-      for (int c = 0; c < kD / 32; ++c) {
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {
         float a[32];
         if (n_it > 0) {
           tmem_ld32(lane_addr + kColDV + c * 32, a);
@@ -308,13 +374,13 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
                void* __restrict__ dq_, int64_t dq_st, int64_t dq_sh, int32_t* status) {
   using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* base = align1024(smem_raw);
   uint8_t* sQ = base;
   uint8_t* sDO = sQ + kTileBytes;
   uint8_t* sK = sDO + kTileBytes;          // 2 stages
   uint8_t* sV = sK + 2 * kTileBytes;       // 2 stages
-  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(sV + 2 * kTileBytes);
+  uint8_t* aux = sV + 2 * kTileBytes;      // 2 stages x (kv_lo[128], kv_hi[128])
+  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + 2 * kAuxBytes);
   const volatile int32_t* abort_flag = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -334,7 +400,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
-  constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256;
+  constexpr uint32_t kColDQ = 256;
 
   if (warp == 0) {
     if (lane == 0 && n_it > 0) {
@@ -345,116 +411,74 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tma_load_3d(sQ + kHalfBytes, &tm_q, &sh->fixed_full, 64, qt * kT, h);
       tma_load_3d(sDO, &tm_do, &sh->fixed_full, 0, qt * kT, h);
       tma_load_3d(sDO + kHalfBytes, &tm_do, &sh->fixed_full, 64, qt * kT, h);
-      int issued[2] = {0, 0};
-      bool ok = true;
-      for (int it = 0; it < n_it; ++it) {
-        const int s = it & 1;
-        if (it >= 2) ok = mbar_wait(&sh->ab_empty[s], ((it >> 1) - 1) & 1, abort_flag);
-        if (!ok) break;
-        const int kt = fwd_list[e0 + it] >> 1;
-        uint8_t* k_dst = sK + s * kTileBytes;
-        uint8_t* v_dst = sV + s * kTileBytes;
-        mbar_arrive_expect_tx(&sh->a_full[s], kTileBytes);
-        tma_load_3d(k_dst, &tm_k, &sh->a_full[s], 0, kt * kT, hk);
-        tma_load_3d(k_dst + kHalfBytes, &tm_k, &sh->a_full[s], 64, kt * kT, hk);
-        mbar_arrive_expect_tx(&sh->b_full[s], kTileBytes);
-        tma_load_3d(v_dst, &tm_v, &sh->b_full[s], 0, kt * kT, hk);
-        tma_load_3d(v_dst + kHalfBytes, &tm_v, &sh->b_full[s], 64, kt * kT, hk);
-        issued[s] += 1;
-      }
-      if (!ok) {
-        raise_abort(sh, status);
-        mbar_wait(&sh->fixed_full, 0, nullptr);
-        for (int s = 0; s < 2; ++s)
-          if (issued[s] > 0) {
-            mbar_wait(&sh->a_full[s], (issued[s] - 1) & 1, nullptr);
-            mbar_wait(&sh->b_full[s], (issued[s] - 1) & 1, nullptr);
-          }
-      }
+      produce(sh, abort_flag, status, n_it, sK, sV, aux, &tm_k, &tm_v,
+              [&](int it, int* row, int* head, const void** xa, const void** xb) {
+                const int j0 = (fwd_list[e0 + it] >> 1) * kT;
+                *row = j0;
+                *head = hk;
+                *xa = kv_lo + j0;
+                *xb = kv_hi + j0;
+              });
     }
   } else if (warp == 1) {
     if (lane == 0 && n_it > 0) {
-      constexpr uint32_t id_ss = idesc_f16(kBf16, kT, kT, false);
-      constexpr uint32_t id_ts = idesc_f16(kBf16, kT, kD, true);
-      const uint32_t q_addr = smem_u32(sQ), o_addr = smem_u32(sDO);
-      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      bool ok = mbar_wait(&sh->fixed_full, 0, abort_flag);
-      for (int it = 0; it < n_it && ok; ++it) {
-        const int s = it & 1;
-        ok = mbar_wait(&sh->a_full[s], (it >> 1) & 1, abort_flag);
-        if (ok) ok = mbar_wait(&sh->b_full[s], (it >> 1) & 1, abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-        mma_tile_ss(tmem + kColS, q_addr, k_addr + s * kTileBytes, id_ss);    // S = Q K^T
-        mma_tile_ss(tmem + kColDP, o_addr, v_addr + s * kTileBytes, id_ss);   // dP = dO V^T
-        tc_commit(&sh->sdp_full);
-        ok = mbar_wait(&sh->ew_full, it & 1, abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-        mma_tile_ts(tmem + kColDQ, tmem + kColS, k_addr + s * kTileBytes, id_ts, it > 0);
-        tc_commit(&sh->ab_empty[s]);
-      }
-      tc_commit(&sh->acc_done);
-      if (!ok) {
-        raise_abort(sh, status);
-        tc_commit(&sh->drain);
-        mbar_wait(&sh->drain, 0, nullptr);
-      }
+      constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
+      constexpr uint32_t id_o = idesc_f16(kBf16, kT, kD, true);
+      const uint32_t k_addr = smem_u32(sK);
+      mma_loop(sh, abort_flag, status, tmem, n_it, smem_u32(sQ), smem_u32(sDO), k_addr,
+               smem_u32(sV), id_s, [&](int u, int s, int sb, bool accumulate) {
+                 mma_ts_k64(tmem + kColDQ, tmem + 64 * sb, k_addr + s * kTileBytes + sb * kSubOff,
+                            id_o, accumulate);
+               });
     }
   } else {
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     const int row = qt * kT + r;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const float l2 = lse[static_cast<int64_t>(h) * ld + row] * kLog2e;   // padded rows: +inf
     const float dr = delta[static_cast<int64_t>(h) * ld + row];
     bool ok = true;
-    for (int it = 0; it < n_it; ++it) {
+    const int n_u = 2 * n_it;
+    for (int u = 0; u < n_u; ++u) {
+      const int it = u >> 1, sb = u & 1, s = it & 1;
       const int ent = fwd_list[e0 + it];
-      const int j0 = (ent >> 1) * kT;
       const bool partial = ent & 1;
-      const bool vec = j0 + kT <= n_kv;
-      ok = mbar_wait(&sh->sdp_full, it & 1, abort_flag);
+      const int c0 = sb * kSub + half * 32;  // first key column (within the tile) of this warp
+      ok = mbar_wait(&sh->sdp_full[sb], (u >> 1) & 1, abort_flag);
+      if (ok && sb == 0) ok = mbar_wait(&sh->a_full[s], (it >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < kT / 32; ++c) {
-        float sv[32], dp[32];
-        tmem_ld32(lane_addr + kColS + c * 32, sv);
-        tmem_ld32(lane_addr + kColDP + c * 32, dp);
-        float p[32];
+      const uint32_t cs = 64 * sb + 32 * half, cp = 128 + 64 * sb + 32 * half;
+      float sv[32], dp[32];
+      tmem_ld32(lane_addr + cs, sv);
+      tmem_ld32(lane_addr + cp, dp);
+      float p[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) p[i] = exp2f(fmaf(sv[i], scale_log2, -l2));
-        if (partial) {
-          if (vec) {
-            const int4* lo4 = reinterpret_cast<const int4*>(kv_lo + j0 + c * 32);
-            const int4* hi4 = reinterpret_cast<const int4*>(kv_hi + j0 + c * 32);
+      for (int i = 0; i < 32; ++i) p[i] = exp2f(fmaf(sv[i], scale_log2, -l2));
+      if (partial) {
+        // key intervals of this tile, zero-padded past n_kv (never visible)
+        const int4* LO = reinterpret_cast<const int4*>(aux + s * kAuxBytes) + c0 / 4;
+        const int4* HI = reinterpret_cast<const int4*>(aux + s * kAuxBytes + kAuxBytes / 2) + c0 / 4;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int4 a = __ldg(lo4 + i), z = __ldg(hi4 + i);
-              if (!visible(a.x, z.x, row)) p[4 * i + 0] = 0.f;
-              if (!visible(a.y, z.y, row)) p[4 * i + 1] = 0.f;
-              if (!visible(a.z, z.z, row)) p[4 * i + 2] = 0.f;
-              if (!visible(a.w, z.w, row)) p[4 * i + 3] = 0.f;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int jj = j0 + c * 32 + i;
-              if (!(jj < n_kv && visible(__ldg(kv_lo + jj), __ldg(kv_hi + jj), row))) p[i] = 0.f;
-            }
-          }
+        for (int i = 0; i < 8; ++i) {
+          const int4 a = LO[i], z = HI[i];
+          if (!visible(a.x, z.x, row)) p[4 * i + 0] = 0.f;
+          if (!visible(a.y, z.y, row)) p[4 * i + 1] = 0.f;
+          if (!visible(a.z, z.z, row)) p[4 * i + 2] = 0.f;
+          if (!visible(a.w, z.w, row)) p[4 * i + 3] = 0.f;
         }
-        uint32_t dw[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          dw[i] = pack2<kBf16>(p[2 * i] * (dp[2 * i] - dr), p[2 * i + 1] * (dp[2 * i + 1] - dr));
-        tmem_st16(lane_addr + kColS + c * 16, dw);
       }
+      uint32_t dw[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        dw[i] = pack2<kBf16>(p[2 * i] * (dp[2 * i] - dr), p[2 * i + 1] * (dp[2 * i + 1] - dr));
+      tmem_st16(lane_addr + cs, dw);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&sh->ew_full);
+      mbar_arrive(&sh->ew_full[sb]);
     }
     if (ok && n_it > 0) {
       ok = mbar_wait(&sh->acc_done, 0, abort_flag);
@@ -464,7 +488,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tc_fence_after();
       T* dq = reinterpret_cast<T*>(dq_) + static_cast<int64_t>(row) * dq_st + h * dq_sh;
 #pragma unroll 1
-      for (int c = 0; c < kD / 32; ++c) {
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {
         float a[32];
         if (n_it > 0) {
           tmem_ld32(lane_addr + kColDQ + c * 32, a);
