@@ -126,7 +126,9 @@ int tt_mask_to_intervals(int mask_dtype, int32_t n_q, int32_t n_kv, const void* 
  * lse [hq, ld] fp32 natural-log row log-sum-exp with ld = n_q rounded up to a
  * multiple of 128 (+inf for a row that sees no key and for the ld - n_q
  * padding rows).  dtype TT_BF16 / TT_F16 run the tcgen05 path for head_dim 128 (and
- * the exact SIMT path otherwise); TT_F32 runs the SIMT path (fp32 FMA).
+ * the exact SIMT path otherwise); TT_F32 runs the SIMT path (fp32 FMA).  On the
+ * tcgen05 path kv_lo/kv_hi must be 16-byte aligned and readable up to
+ * round_up(n_kv, 128) entries with zeros past n_kv.
  */
 int tt_tree_attn_fwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv,
                      int32_t head_dim, const void* q, int64_t q_st, int64_t q_sh,

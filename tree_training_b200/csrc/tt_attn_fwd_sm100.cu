@@ -2,20 +2,26 @@
 //
 // Replaces the SDPA call the reference reaches through HF
 // (TF/integrations/sdpa_attention.py:92-101) with its dense additive mask
-// (dfs_tree_forward.py:548-550, tree_grad_hybrid.py:313-317): for one q head
-// and one 128-row query tile, O = softmax(Q K^T * scale + M) V over the kv
-// tiles that the host work list marks visible, M evaluated in registers from
-// the per-key row intervals [kv_lo, kv_hi).
+// (dfs_tree_forward.py:548-550, tree_grad_hybrid.py:313-317): for a 128-row
+// query tile, O = softmax(Q K^T * scale + M) V over the kv tiles the host work
+// list marks visible, M evaluated in registers from the per-key row intervals
+// [kv_lo, kv_hi).
 //
-// CTA = 6 warps, one (q head, q tile) each:
-//   warp 0    TMA producer: Q once, then K/V tiles into a 2-stage ring
-//   warp 1    MMA issuer:   S_j = Q K_j^T into TMEM (double buffered),
-//                           O += P_{j-1} V_{j-1} with P read from TMEM
-//   warps 2-5 softmax:      one thread per query row (= TMEM lane); masks
-//                           partial tiles, keeps the running max/sum, writes
-//                           P (bf16/fp16) over S in TMEM, rescales O only when
-//                           the max grows by more than 2^8, final epilogue.
-// TMEM columns: [0,128) S/P buffer 0, [128,256) S/P buffer 1, [256,384) O.
+// One CTA handles the same query tile for two q heads of one GQA group: they
+// read the same K/V tiles and the same mask, so each K/V tile feeds two
+// 128x128 score tiles (half the K/V traffic per FLOP of one head per CTA) and
+// the two softmax warpgroups alternate with the tensor core (ping-pong):
+//
+//   warp 0    TMA producer: Q of both heads once, then K/V tiles (+ the key
+//             intervals of partial tiles) into a 2-stage ring
+//   warp 1    MMA issuer:   S0 = Q0 K^T, S1 = Q1 K^T, then per head
+//             O_g += P_g V with P_g read from TMEM, S_g of the next tile issued
+//             as soon as PV_g is
+//   warps 2-5 softmax of head 0, warps 6-9 softmax of head 1: one thread per
+//             query row (= TMEM lane), lazy O rescaling (max grows > 2^8),
+//             P written over S in TMEM, final normalisation and store.
+// TMEM columns: S0|P0 [0,128), S1|P1 [128,256), O0 [256,384), O1 [384,512).
+// With an odd group size the last CTA of a group has one valid head.
 #include <type_traits>
 
 #include "tt_sm100.cuh"
@@ -30,9 +36,9 @@ constexpr int kD = 128;                   // head dim
 constexpr int kStages = 2;                // K/V ring depth
 constexpr int kTileBytes = kBM * kD * 2;  // one 128 x 128 16-bit tile
 constexpr int kHalfBytes = kTileBytes / 2;  // one 64-column swizzle block
-constexpr int kThreads = 192;
+constexpr int kAuxBytes = 2 * kBN * 4;      // kv_lo[128] + kv_hi[128] of a stage
+constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
 struct FwdBarriers {
@@ -40,15 +46,16 @@ struct FwdBarriers {
   uint64_t k_full[kStages];
   uint64_t v_full[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t p_full[2];
-  uint64_t o_done;
+  uint64_t s_full[2];       // per head
+  uint64_t p_full[2];       // per head, 128 arrivals
+  uint64_t o_done[2];       // per head
   uint64_t drain;
   uint32_t tmem_base;
   int32_t abort;
 };
 
-constexpr size_t kSmemBytes = 1024 + kTileBytes * (1 + 2 * kStages) + sizeof(FwdBarriers);
+constexpr size_t kSmemBytes =
+    1024 + kTileBytes * (2 + 2 * kStages) + kStages * kAuxBytes + sizeof(FwdBarriers);
 
 __device__ __forceinline__ void raise_abort(FwdBarriers* sh, int32_t* status) {
   set_status(status, TT_ERR_DEVICE_TIMEOUT);
@@ -58,26 +65,27 @@ __device__ __forceinline__ void raise_abort(FwdBarriers* sh, int32_t* status) {
 template <bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-            const __grid_constant__ CUtensorMap tm_v, int n_q, int n_kv, int rep,
-            const int32_t* __restrict__ kv_lo, const int32_t* __restrict__ kv_hi,
-            const int32_t* __restrict__ fwd_ptr, const int32_t* __restrict__ fwd_list,
-            float scale_log2, void* __restrict__ out_, float* __restrict__ lse,
-            int32_t* status) {
+            const __grid_constant__ CUtensorMap tm_v, int n_q, int n_kv, int hq, int rep,
+            int pairs_per_group, const int32_t* __restrict__ kv_lo,
+            const int32_t* __restrict__ kv_hi, const int32_t* __restrict__ fwd_ptr,
+            const int32_t* __restrict__ fwd_list, float scale_log2, void* __restrict__ out_,
+            float* __restrict__ lse, int32_t* status) {
   using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sQ = base;
-  uint8_t* sK = sQ + kTileBytes;
-  uint8_t* sV = sK + kStages * kTileBytes;
-  FwdBarriers* sh = reinterpret_cast<FwdBarriers*>(sV + kStages * kTileBytes);
+  uint8_t* sQ = base;                                // 2 heads
+  uint8_t* sK = sQ + 2 * kTileBytes;                 // kStages
+  uint8_t* sV = sK + kStages * kTileBytes;           // kStages
+  uint8_t* aux = sV + kStages * kTileBytes;          // kStages x (kv_lo, kv_hi)
+  FwdBarriers* sh = reinterpret_cast<FwdBarriers*>(aux + kStages * kAuxBytes);
   const volatile int32_t* abort_flag = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hq = gridDim.x;
-  const int h = blockIdx.x;
+  const int hk = blockIdx.x / pairs_per_group;
+  const int h0 = hk * rep + 2 * (blockIdx.x % pairs_per_group);
+  const int n_heads = (h0 + 1 < (hk + 1) * rep) ? 2 : 1;
   const int qt = gridDim.y - 1 - blockIdx.y;  // heavier (later) tiles first
-  const int hk = h / rep;
   const int e0 = fwd_ptr[qt];
   const int n_it = fwd_ptr[qt + 1] - e0;
 
@@ -88,11 +96,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
       mbar_init(&sh->v_full[s], 1);
       mbar_init(&sh->kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sh->s_full[b], 1);
-      mbar_init(&sh->p_full[b], 128);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&sh->s_full[g], 1);
+      mbar_init(&sh->p_full[g], 128);
+      mbar_init(&sh->o_done[g], 1);
     }
-    mbar_init(&sh->o_done, 1);
     mbar_init(&sh->drain, 1);
     sh->abort = 0;
     fence_mbar_init();
@@ -112,21 +120,30 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
-      mbar_arrive_expect_tx(&sh->q_full, kTileBytes);
-      tma_load_3d(sQ, &tm_q, &sh->q_full, 0, qt * kBM, h);
-      tma_load_3d(sQ + kHalfBytes, &tm_q, &sh->q_full, 64, qt * kBM, h);
+      mbar_arrive_expect_tx(&sh->q_full, n_heads * kTileBytes);
+      for (int g = 0; g < n_heads; ++g) {
+        tma_load_3d(sQ + g * kTileBytes, &tm_q, &sh->q_full, 0, qt * kBM, h0 + g);
+        tma_load_3d(sQ + g * kTileBytes + kHalfBytes, &tm_q, &sh->q_full, 64, qt * kBM, h0 + g);
+      }
       int issued[kStages] = {0};
       bool ok = true;
       for (int it = 0; it < n_it && ok; ++it) {
         const int s = it % kStages;
         if (it >= kStages) ok = mbar_wait(&sh->kv_empty[s], ((it / kStages) - 1) & 1, abort_flag);
         if (!ok) break;
-        const int kt = fwd_list[e0 + it] >> 1;
+        const int ent = fwd_list[e0 + it];
+        const int kt = ent >> 1;
         uint8_t* k_dst = sK + s * kTileBytes;
         uint8_t* v_dst = sV + s * kTileBytes;
-        mbar_arrive_expect_tx(&sh->k_full[s], kTileBytes);
+        const bool partial = ent & 1;
+        mbar_arrive_expect_tx(&sh->k_full[s], kTileBytes + (partial ? kAuxBytes : 0));
         tma_load_3d(k_dst, &tm_k, &sh->k_full[s], 0, kt * kBN, hk);
         tma_load_3d(k_dst + kHalfBytes, &tm_k, &sh->k_full[s], 64, kt * kBN, hk);
+        if (partial) {
+          bulk_load(aux + s * kAuxBytes, kv_lo + kt * kBN, kAuxBytes / 2, &sh->k_full[s]);
+          bulk_load(aux + s * kAuxBytes + kAuxBytes / 2, kv_hi + kt * kBN, kAuxBytes / 2,
+                    &sh->k_full[s]);
+        }
         mbar_arrive_expect_tx(&sh->v_full[s], kTileBytes);
         tma_load_3d(v_dst, &tm_v, &sh->v_full[s], 0, kt * kBN, hk);
         tma_load_3d(v_dst + kHalfBytes, &tm_v, &sh->v_full[s], 64, kt * kBN, hk);
@@ -149,39 +166,54 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
       constexpr uint32_t id_s = idesc_f16(kBf16, kBM, kBN, false);
       constexpr uint32_t id_o = idesc_f16(kBf16, kBM, kD, true);
       const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      auto issue_s = [&](int g, int it) {
+        const int s = it % kStages;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_ss(tmem + g * 128, desc_sw128(q_addr + g * kTileBytes + off, 16, 1024),
+                 desc_sw128(k_addr + s * kTileBytes + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&sh->s_full[g]);
+      };
+      auto issue_pv = [&](int g, int it) {
+        const int s = it % kStages;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          mma_ts(tmem + 256 + g * 128, tmem + g * 128 + kk * 8,
+                 desc_sw128(v_addr + s * kTileBytes + kk * 2048, kHalfBytes, 1024), id_o,
+                 (it > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&sh->o_done[g]);
+      };
       bool ok = mbar_wait(&sh->q_full, 0, abort_flag);
-      tc_fence_after();
-      for (int it = 0; it <= n_it && ok; ++it) {
-        if (it < n_it) {
-          const int s = it % kStages, b = it & 1;
-          ok = mbar_wait(&sh->k_full[s], (it / kStages) & 1, abort_flag);
+      if (ok) ok = mbar_wait(&sh->k_full[0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        for (int g = 0; g < n_heads; ++g) issue_s(g, 0);
+      }
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        const bool more = it + 1 < n_it;
+        const int s1 = (it + 1) % kStages;
+        bool k_next = false;
+        for (int g = 0; g < n_heads && ok; ++g) {
+          ok = mbar_wait(&sh->p_full[g], it & 1, abort_flag);
+          if (ok && g == 0) ok = mbar_wait(&sh->v_full[s], ph, abort_flag);
           if (!ok) break;
           tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-            const uint64_t da = desc_sw128(q_addr + off, 16, 1024);
-            const uint64_t db = desc_sw128(k_addr + s * kTileBytes + off, 16, 1024);
-            mma_ss(tmem + b * 128, da, db, id_s, kk > 0 ? 1u : 0u);
+          issue_pv(g, it);
+          if (more) {
+            if (!k_next) {
+              ok = mbar_wait(&sh->k_full[s1], ((it + 1) / kStages) & 1, abort_flag);
+              if (!ok) break;
+              tc_fence_after();
+              k_next = true;
+            }
+            issue_s(g, it + 1);
           }
-          tc_commit(&sh->s_full[b]);
         }
-        if (it > 0) {
-          const int j = it - 1, s = j % kStages, b = j & 1;
-          ok = mbar_wait(&sh->p_full[b], (j >> 1) & 1, abort_flag);
-          if (ok) ok = mbar_wait(&sh->v_full[s], (j / kStages) & 1, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            // B = V tile, MN-major: 16 keys per step = 16 rows of 128 bytes
-            const uint64_t db = desc_sw128(v_addr + s * kTileBytes + kk * 2048, kHalfBytes, 1024);
-            mma_ts(tmem + kColO, tmem + b * 128 + kk * 8, db, id_o,
-                   (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(&sh->kv_empty[s]);
-          tc_commit(&sh->o_done);
-        }
+        if (ok) tc_commit(&sh->kv_empty[s]);
       }
       if (!ok) {
         raise_abort(sh, status);
@@ -191,134 +223,132 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
     }
   } else {
     // ------------------------------------------------------------ softmax
+    const int g = (warp - 2) >> 2;          // head of this warpgroup
     const int quad = warp & 3;              // TMEM lane quadrant of this warp
     const int r = quad * 32 + lane;         // row within the tile
     const int row = qt * kBM + r;
+    const int h = h0 + g;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t col_s = g * 128, col_o = 256 + g * 128;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int it = 0; it < n_it; ++it) {
-      const int ent = fwd_list[e0 + it];
-      const int kt = ent >> 1;
-      const bool partial = ent & 1;
-      const int b = it & 1;
-      ok = mbar_wait(&sh->s_full[b], (it >> 1) & 1, abort_flag);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      float s[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        float t[32];
-        tmem_ld32(lane_addr + b * 128 + c * 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
-      }
-      if (partial) {
-        const int j0 = kt * kBN;
-        if (j0 + kBN <= n_kv) {
-          const int4* lo4 = reinterpret_cast<const int4*>(kv_lo + j0);
-          const int4* hi4 = reinterpret_cast<const int4*>(kv_hi + j0);
-#pragma unroll
-          for (int c = 0; c < kBN / 4; ++c) {
-            const int4 a = __ldg(lo4 + c), z = __ldg(hi4 + c);
-            if (!visible(a.x, z.x, row)) s[4 * c + 0] = -INFINITY;
-            if (!visible(a.y, z.y, row)) s[4 * c + 1] = -INFINITY;
-            if (!visible(a.z, z.z, row)) s[4 * c + 2] = -INFINITY;
-            if (!visible(a.w, z.w, row)) s[4 * c + 3] = -INFINITY;
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < kBN; ++c) {
-            const int j = j0 + c;
-            const bool vis = j < n_kv && visible(__ldg(kv_lo + j), __ldg(kv_hi + j), row);
-            if (!vis) s[c] = -INFINITY;
-          }
-        }
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, s[c]);
-      const float m_new = fmaxf(m_run, mx * scale_log2);
-      // PV_{it-1} must be complete before O may be rescaled; waiting every
-      // iteration keeps the o_done phases observed in order.
-      if (it > 0) {
-        ok = mbar_wait(&sh->o_done, (it - 1) & 1, abort_flag);
+    if (g < n_heads) {
+      for (int it = 0; it < n_it; ++it) {
+        const int ent = fwd_list[e0 + it];
+        const bool partial = ent & 1;
+        const int s = it % kStages;
+        ok = mbar_wait(&sh->s_full[g], it & 1, abort_flag);
+        // the key intervals arrived with the K tile (k_full); S_g completing
+        // implies K landed, the explicit wait makes the shared data visible
+        if (ok && partial) ok = mbar_wait(&sh->k_full[s], (it / kStages) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
-      }
-      float alpha = 1.f;
-      bool need = false;
-      if (m_run == -INFINITY) {
-        m_run = m_new;  // every earlier P of this row was 0: nothing to rescale
-      } else if (m_new > m_run + kRescaleThreshold) {
-        alpha = exp2f(m_run - m_new);
-        m_run = m_new;
-        need = true;
-      }
-      if (__any_sync(0xffffffffu, need)) {
         tc_fence_after();
+        float sv[kBN];
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) {
+          float t[32];
+          tmem_ld32(lane_addr + col_s + c * 32, t);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = t[i];
+        }
+        if (partial) {
+          const int4* lo4 = reinterpret_cast<const int4*>(aux + s * kAuxBytes);
+          const int4* hi4 = reinterpret_cast<const int4*>(aux + s * kAuxBytes + kAuxBytes / 2);
+#pragma unroll
+          for (int c = 0; c < kBN / 4; ++c) {
+            const int4 a = lo4[c], z = hi4[c];
+            if (!visible(a.x, z.x, row)) sv[4 * c + 0] = -INFINITY;
+            if (!visible(a.y, z.y, row)) sv[4 * c + 1] = -INFINITY;
+            if (!visible(a.z, z.z, row)) sv[4 * c + 2] = -INFINITY;
+            if (!visible(a.w, z.w, row)) sv[4 * c + 3] = -INFINITY;
+          }
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, sv[c]);
+        const float m_new = fmaxf(m_run, mx * scale_log2);
+        // PV_g(it-1) must be complete before O_g may be rescaled; waiting
+        // every iteration keeps the o_done phases observed in order.
+        if (it > 0) {
+          ok = mbar_wait(&sh->o_done[g], (it - 1) & 1, abort_flag);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+        }
+        float alpha = 1.f;
+        bool need = false;
+        if (m_run == -INFINITY) {
+          m_run = m_new;  // every earlier P of this row was 0: nothing to rescale
+        } else if (m_new > m_run + kRescaleThreshold) {
+          alpha = exp2f(m_run - m_new);
+          m_run = m_new;
+          need = true;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < kD / 32; ++c) {
+            float o[32];
+            uint32_t w[32];
+            tmem_ld32(lane_addr + col_o + c * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * alpha);
+            tmem_st32(lane_addr + col_o + c * 32, w);
+          }
+          tmem_st_wait();
+        }
+        l_run *= alpha;
+        const float mb = (m_run == -INFINITY) ? 0.f : m_run;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float p0 = exp2f(fmaf(sv[hf * 64 + 2 * i], scale_log2, -mb));
+            const float p1 = exp2f(fmaf(sv[hf * 64 + 2 * i + 1], scale_log2, -mb));
+            l_run += p0 + p1;
+            pk[i] = pack2<kBf16>(p0, p1);
+          }
+          tmem_st32(lane_addr + col_s + hf * 32, pk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sh->p_full[g]);
+      }
+      if (ok && n_it > 0) {
+        ok = mbar_wait(&sh->o_done[g], (n_it - 1) & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (ok) {
+        tc_fence_after();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        T* out = reinterpret_cast<T*>(out_) + static_cast<int64_t>(row) * hq * kD + h * kD;
 #pragma unroll 1
         for (int c = 0; c < kD / 32; ++c) {
           float o[32];
-          uint32_t w[32];
-          tmem_ld32(lane_addr + kColO + c * 32, o);
+          if (n_it > 0) {
+            tmem_ld32(lane_addr + col_o + c * 32, o);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * alpha);
-          tmem_st32(lane_addr + kColO + c * 32, w);
+            for (int i = 0; i < 32; ++i) o[i] = 0.f;
+          }
+          if (row < n_q) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) w[i] = pack2<kBf16>(o[2 * i] * inv, o[2 * i + 1] * inv);
+            uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
         }
-        tmem_st_wait();
+        // rows past n_q are the padding of the [hq, lse_ld(n_q)] layout: +inf
+        lse[static_cast<int64_t>(h) * lse_ld(n_q) + row] =
+            (row < n_q && l_run > 0.f) ? (m_run + __log2f(l_run)) * 0.69314718055994531f
+                                       : INFINITY;
+      } else {
+        raise_abort(sh, status);
       }
-      l_run *= alpha;
-      const float mb = (m_run == -INFINITY) ? 0.f : m_run;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float p0 = exp2f(fmaf(s[half * 64 + 2 * i], scale_log2, -mb));
-          const float p1 = exp2f(fmaf(s[half * 64 + 2 * i + 1], scale_log2, -mb));
-          l_run += p0 + p1;
-          pk[i] = pack2<kBf16>(p0, p1);
-        }
-        tmem_st32(lane_addr + b * 128 + half * 32, pk);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&sh->p_full[b]);
-    }
-    if (ok && n_it > 0) {
-      ok = mbar_wait(&sh->o_done, (n_it - 1) & 1, abort_flag);
-      ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok) {
-      tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      T* out = reinterpret_cast<T*>(out_) + static_cast<int64_t>(row) * hq * kD + h * kD;
-#pragma unroll 1
-      for (int c = 0; c < kD / 32; ++c) {
-        float o[32];
-        if (n_it > 0) {
-          tmem_ld32(lane_addr + kColO + c * 32, o);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = 0.f;
-        }
-        if (row < n_q) {
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = pack2<kBf16>(o[2 * i] * inv, o[2 * i + 1] * inv);
-          uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-        }
-      }
-      // rows past n_q are the padding of the [hq, lse_ld(n_q)] layout: +inf
-      lse[static_cast<int64_t>(h) * lse_ld(n_q) + row] =
-          (row < n_q && l_run > 0.f) ? (m_run + __log2f(l_run)) * 0.69314718055994531f
-                                     : INFINITY;
-    } else {
-      raise_abort(sh, status);
     }
   }
   tc_fence_before();
@@ -393,12 +423,14 @@ int tt_launch_attn_fwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
   if ((rc = make_map(&mk, bf16, k, n_kv, hkv, k_st, k_sh)) != TT_OK) return rc;
   if ((rc = make_map(&mv, bf16, v, n_kv, hkv, v_st, v_sh)) != TT_OK) return rc;
   const int n_qt = (n_q + kBM - 1) / kBM;
-  dim3 grid(hq, n_qt);
+  const int rep = hq / hkv;
+  const int pairs = (rep + 1) / 2;            // CTAs per GQA group (two heads each)
+  dim3 grid(hkv * pairs, n_qt);
   const float scale_log2 = scale * 1.4426950408889634f;
   auto kern = bf16 ? attn_fwd_tc<true> : attn_fwd_tc<false>;
   TT_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)kSmemBytes));
-  kern<<<grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, n_q, n_kv, hq / hkv, kv_lo, kv_hi,
+  kern<<<grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, n_q, n_kv, hq, rep, pairs, kv_lo, kv_hi,
                                            fwd_ptr, fwd_list, scale_log2, out, lse, status);
   tt_count_launches(1);
   return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
