@@ -150,12 +150,12 @@ def test_tensor_core_forward_matches_exact_path():
     meta, q, k, v, do = make_case(9, 3000, 8, 2, 128, 64, 512, root_len=700)
     qt, kt, vt = (torch.tensor(x, dtype=torch.bfloat16, device=DEV) for x in (q, k, v))
     a = tt.tree_attention(qt, kt, vt, meta).float()
-    prev = _lib.lib().tt_set_kernel_path(1)
+    prev = _lib.set_kernel_path(1)
     try:
         meta2 = tt.TreeAttnMeta(meta.n_q, meta.kv_lo, meta.kv_hi)
         b = tt.tree_attention(qt, kt, vt, meta2).float()
     finally:
-        _lib.lib().tt_set_kernel_path(prev)
+        _lib.set_kernel_path(prev)
     torch.cuda.synchronize()
     assert float((a - b).abs().max() / b.abs().max()) < 1e-2
 
@@ -167,12 +167,12 @@ def test_tensor_core_backward_matches_exact_path(seed, n, hq, hkv, past):
     meta, q, k, v, do = make_case(seed, n, hq, hkv, 128, 32, 400, past)
     res = []
     for path in (0, 1):
-        prev = _lib.lib().tt_set_kernel_path(path)
+        prev = _lib.set_kernel_path(path)
         try:
             m = tt.TreeAttnMeta(meta.n_q, meta.kv_lo, meta.kv_hi)
             res.append(run(q, k, v, m, do, torch.bfloat16))
         finally:
-            _lib.lib().tt_set_kernel_path(prev)
+            _lib.set_kernel_path(prev)
     for name, a, b in zip(("out", "dq", "dk", "dv"), res[0], res[1]):
         assert rel(a, b) < 1.5e-2, name
 

@@ -57,7 +57,7 @@ def _rel(a, b):
 
 @pytest.mark.parametrize("dtype,D,tol", [(torch.bfloat16, 128, 1.5e-2), (torch.float32, 64, 1e-4)])
 def test_noalloc_backward_matches_workspace_backward(dtype, D, tol):
-    prev = _lib.lib().tt_set_kernel_path(0)
+    prev = _lib.set_kernel_path(0)
     try:
         meta, q, k, v, do = _case(31, 1500, 8, 2, D, dtype, past=37)
         scale = D ** -0.5
@@ -87,7 +87,7 @@ def test_noalloc_backward_matches_workspace_backward(dtype, D, tol):
                 assert torch.isfinite(a.float()).all()
                 assert _rel(a, b) < tol
     finally:
-        _lib.lib().tt_set_kernel_path(prev)
+        _lib.set_kernel_path(prev)
 
 
 def test_noalloc_rejects_problems_beyond_its_fixed_scratch():

@@ -102,3 +102,18 @@ def call(name: str, *args) -> int:
     rc = getattr(lib(), name)(*args)
     check(name, rc)
     return rc
+
+
+_path_generation = [0]
+
+
+def set_kernel_path(path: int) -> int:
+    """Select the attention kernel path (0 automatic, 1 exact CUDA-core) and
+    invalidate cached tile shapes.  Returns the previous setting."""
+    prev = lib().tt_set_kernel_path(int(path))
+    _path_generation[0] += 1
+    return prev
+
+
+def path_generation() -> int:
+    return _path_generation[0]

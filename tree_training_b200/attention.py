@@ -48,11 +48,21 @@ def lse_ld(n_q: int) -> int:
     return (n_q + 127) // 128 * 128
 
 
+_tile_cache: dict = {}
+
+
 def tile_shape(dtype: torch.dtype, head_dim: int, kind: int) -> Tuple[int, int]:
-    tq = np.zeros(1, np.int32)
-    tk = np.zeros(1, np.int32)
-    _lib.call("tt_attn_tile_shape", _DTYPES[dtype], head_dim, kind, tq.ctypes.data, tk.ctypes.data)
-    return int(tq[0]), int(tk[0])
+    """Tile shape the library's kernels expect (cached per kernel-path setting)."""
+    key = (_lib.path_generation(), dtype, head_dim, kind)
+    t = _tile_cache.get(key)
+    if t is None:
+        tq = np.zeros(1, np.int32)
+        tk = np.zeros(1, np.int32)
+        _lib.call("tt_attn_tile_shape", _DTYPES[dtype], head_dim, kind, tq.ctypes.data,
+                  tk.ctypes.data)
+        t = (int(tq[0]), int(tk[0]))
+        _tile_cache[key] = t
+    return t
 
 
 def _check_tensor(name, t, ndim=3):

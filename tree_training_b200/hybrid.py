@@ -1,0 +1,359 @@
+"""Tree-training drivers on the B200 attention path (pure-attention models).
+
+Drop-ins for the reference drivers that call the hot path:
+
+* ``partition_tree`` / ``SubtreePartition``   (tree_grad_hybrid.py:48-95)
+* ``GatewayCache``                            (tree_grad_ckpt_opath.py:66-133)
+* ``tree_grad_hybrid``                        (tree_grad_hybrid.py:434-539)
+* ``tree_grad_ckpt_sequential``               (tree_grad_ckpt.py:39-107)
+* ``make_tree_loss_fn``                       (tree_grad_hybrid.py:546-558)
+
+Differences from the reference, all on the plumbing side of the op:
+
+* no dense mask: each partition's keys carry row intervals (``TreeAttnMeta``)
+  that reach the ``tree_sm100`` attention through ``model(..., tree_meta=)``;
+* gateway keys inherit their parent partition's visibility
+  (``gateway_mask="tree"``, the default).  ``gateway_mask="reference"``
+  reproduces tree_grad_hybrid.py:207 exactly, where every key of the parent's
+  own gateway is made visible again — with two cut levels that lets a DFS
+  sibling of the parent partition leak into the child partition;
+* gateway gradients are accumulated in fp32 on the device (the reference
+  copies each one to host memory in fp32, tree_grad_hybrid.py:220-225).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Callable, Dict, List, Optional, Tuple
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from .attention import ATTN_IMPL_NAME, register_hf_attention, tree_mask_placeholder
+from .packer import TreeNode, build_dfs_tree_info  # noqa: F401  (TreeNode re-export)
+
+
+# ---------------------------------------------------------------------------
+# partitioning
+# ---------------------------------------------------------------------------
+
+@dataclass
+class SubtreePartition:
+    entry_nodes: list
+    dfs_nodes: list = field(default_factory=list)
+    cut_node_set: set = field(default_factory=set)
+    leaf_node_set: set = field(default_factory=set)
+    parent: Optional["SubtreePartition"] = None
+    parent_cut_node: object = None
+    pos_offset: int = 0
+    token_count: int = 0
+
+
+def partition_tree(roots, max_tokens: int) -> List[SubtreePartition]:
+    """Greedy DFS budget split with the reference's rules: a child that would
+    push a non-empty partition past ``max_tokens`` is deferred, its parent
+    becomes a cut node, every deferred child starts a new partition once the
+    current one is complete, and every forest root starts its own partition."""
+    parts: List[SubtreePartition] = []
+
+    def build(entry, parent, cut_node):
+        p = SubtreePartition(entry_nodes=list(entry), parent=parent, parent_cut_node=cut_node)
+        parts.append(p)
+        deferred = []
+
+        def visit(node, is_entry):
+            L = len(node.token_ids)
+            if not is_entry and p.token_count > 0 and p.token_count + L > max_tokens:
+                return False
+            p.dfs_nodes.append(node)
+            p.token_count += L
+            for ch in node.children:
+                if not visit(ch, False):
+                    p.cut_node_set.add(id(node))
+                    deferred.append((node, ch))
+            if not node.children and id(node) not in p.cut_node_set:
+                p.leaf_node_set.add(id(node))
+            return True
+
+        for r in entry:
+            visit(r, True)
+        for cn, ch in deferred:
+            build([ch], p, cn)
+
+    for r in roots:
+        build([r], None, None)
+    return parts
+
+
+# ---------------------------------------------------------------------------
+# gateway KV cache (HF Cache duck type)
+# ---------------------------------------------------------------------------
+
+class GatewayCache:
+    """Concatenates a partition's gateway K/V (leaf tensors) in front of its
+    own K/V in every attention layer and records the result for gradient
+    chaining (tree_grad_ckpt_opath.py:66-133)."""
+
+    def __init__(self, gate_kv: List[Tuple[torch.Tensor, torch.Tensor]]):
+        self._gate_kv = gate_kv
+        self._full_kv: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
+
+    def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
+        if layer_idx < len(self._gate_kv) and self._gate_kv[layer_idx][0] is not None:
+            gk, gv = self._gate_kv[layer_idx]
+            full_k = torch.cat([gk, key_states], dim=-2)
+            full_v = torch.cat([gv, value_states], dim=-2)
+        else:
+            full_k, full_v = key_states, value_states
+        self._full_kv[layer_idx] = (full_k, full_v)
+        return full_k, full_v
+
+    def get_seq_length(self, layer_idx: int = 0) -> int:
+        if layer_idx < len(self._gate_kv) and self._gate_kv[layer_idx][0] is not None:
+            return self._gate_kv[layer_idx][0].shape[-2]
+        return 0
+
+    def get_mask_sizes(self, cache_position, layer_idx: int = 0):
+        return self.get_seq_length(layer_idx) + cache_position.shape[0], 0
+
+
+@dataclass
+class SubtreeGateway:
+    key_gates: List[torch.Tensor]
+    val_gates: List[torch.Tensor]
+    raw_keys: List[torch.Tensor]
+    raw_vals: List[torch.Tensor]
+    acc_k: List[list]
+    acc_v: List[list]
+    past_len: int
+    gw_lo: np.ndarray           # key intervals of the gateway keys (rows of the child)
+    gw_visible: np.ndarray      # bool per gateway key
+    pos_offset: int
+
+
+def _fp32_accumulator_hook(acc: list):
+    """Sum the gradient reaching a gateway leaf in fp32 on its device and stop
+    the 16-bit .grad accumulation (the reference does the sum on the host)."""
+    def hook(g):
+        g32 = g.detach().float()
+        acc[0] = g32 if acc[0] is None else acc[0] + g32
+        return torch.zeros_like(g)
+    return hook
+
+
+# ---------------------------------------------------------------------------
+# one partition forward
+# ---------------------------------------------------------------------------
+
+def _partition_forest(p: SubtreePartition):
+    """The partition's members as a forest of light nodes (reference copy order,
+    tree_grad_hybrid.py:110-130) plus original-node bookkeeping."""
+    members = {id(n) for n in p.dfs_nodes}
+
+    class _N:
+        __slots__ = ("token_ids", "children", "orig")
+
+        def __init__(self, orig):
+            self.orig = orig
+            self.token_ids = orig.token_ids
+            self.children = [_N(c) for c in orig.children if id(c) in members]
+
+    return [_N(n) for n in p.entry_nodes if id(n) in members]
+
+
+def _subtree_forward(model, p: SubtreePartition, gw: Optional[SubtreeGateway], dev, gateway_mask):
+    forest = _partition_forest(p)
+    info = build_dfs_tree_info(forest, pos_offset=p.pos_offset)
+    N = info.N
+    past = gw.past_len if gw is not None else 0
+    if gw is not None:
+        vis = gw.gw_visible
+        meta = info.attn_meta(np.zeros(past, np.int32), np.where(vis, N, 0).astype(np.int32))
+    else:
+        meta = info.attn_meta()
+    ids = torch.as_tensor(info.dfs_token_ids_np, device=dev).unsqueeze(0)
+    pos = torch.as_tensor(info.dfs_pos_ids_np.astype(np.int64), device=dev).unsqueeze(0)
+    cache = GatewayCache(list(zip(gw.key_gates, gw.val_gates)) if gw is not None else [])
+    dtype = next(model.parameters()).dtype
+    mask = tree_mask_placeholder(meta, dtype=dtype, device=dev)
+    out = model(input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=cache,
+                use_cache=True, tree_meta=meta)
+    full_kv = [cache._full_kv[l] for l in sorted(cache._full_kv)]
+    return out.logits, info, full_kv
+
+
+def _make_child_gateways(full_kv, info, p: SubtreePartition, gw: Optional[SubtreeGateway],
+                         cut_nodes, gateway_mask: str) -> Dict[int, SubtreeGateway]:
+    """Gateway of each cut node (tree_grad_hybrid.py:174-250): the parent's
+    keys up to the end of the cut node, visible where they are the cut node's
+    ancestors (or, for the parent's own gateway keys, where the parent saw
+    them), and the depth-based position offset of the cut node's children."""
+    node_idx = {id(n.orig): i for i, n in enumerate(info.nodes)}
+    out = {}
+    for cn in cut_nodes:
+        total, vis, pos_off = gateway_visibility(
+            info, node_idx[id(cn)], p.pos_offset, gw.gw_visible if gw is not None else None,
+            gateway_mask)
+        kg, vg, rk, rv, ak, av = [], [], [], [], [], []
+        for fk, fv in full_kv:
+            k_raw = fk[:, :, :total, :]
+            v_raw = fv[:, :, :total, :]
+            gk = k_raw.detach().requires_grad_(True)
+            gv_ = v_raw.detach().requires_grad_(True)
+            acc_k, acc_v = [None], [None]
+            gk.register_hook(_fp32_accumulator_hook(acc_k))
+            gv_.register_hook(_fp32_accumulator_hook(acc_v))
+            kg.append(gk)
+            vg.append(gv_)
+            rk.append(k_raw)
+            rv.append(v_raw)
+            ak.append(acc_k)
+            av.append(acc_v)
+        out[id(cn)] = SubtreeGateway(kg, vg, rk, rv, ak, av, total, np.zeros(total, np.int32),
+                                     vis, pos_off)
+    return out
+
+
+def gateway_visibility(info, c: int, pos_offset: int, parent_visible: Optional[np.ndarray],
+                       gateway_mask: str = "tree"):
+    """Gateway of cut node ``c`` of a partition (tree_grad_hybrid.py:198-209).
+
+    Returns (total keys, bool visibility per key, pos_offset of the children).
+    Keys are the partition's own gateway keys followed by its tokens up to the
+    end of ``c``; a token key is visible iff it lies in an ancestor (or ``c``
+    itself).  The partition's own gateway keys keep the visibility they had in
+    the partition (``"tree"``) or are all made visible (``"reference"``, the
+    reference's ``bias[:parent_past_len] = 0``)."""
+    parent_past = 0 if parent_visible is None else len(parent_visible)
+    bounds = info.chunk_bounds_np
+    total = parent_past + int(bounds[c, 1])
+    vis = np.zeros(total, bool)
+    if parent_past:
+        vis[:parent_past] = True if gateway_mask == "reference" else parent_visible
+    a = c
+    while a >= 0:
+        s, e = bounds[a]
+        vis[parent_past + s: parent_past + e] = True
+        a = int(info.parents_np[a])
+    # depth-based offset of the cut node's children (tree_grad_hybrid.py:202-204)
+    pos_off = pos_offset + _depth_of(info, c) + int(bounds[c, 1] - bounds[c, 0])
+    return total, vis, pos_off
+
+
+def _depth_of(info, c) -> int:
+    """Token count of c's ancestors (its depth offset), also for a 0-token node."""
+    d = 0
+    a = int(info.parents_np[c])
+    while a >= 0:
+        d += int(info.chunk_bounds_np[a, 1] - info.chunk_bounds_np[a, 0])
+        a = int(info.parents_np[a])
+    return d
+
+
+def _chain_gateway_grads(gw: SubtreeGateway, retain_graph: bool) -> None:
+    raws, grads = [], []
+    for rk, rv, ak, av in zip(gw.raw_keys, gw.raw_vals, gw.acc_k, gw.acc_v):
+        if ak[0] is not None:
+            raws.append(rk)
+            grads.append(ak[0].to(rk.dtype))
+        if av[0] is not None:
+            raws.append(rv)
+            grads.append(av[0].to(rv.dtype))
+    if raws:
+        torch.autograd.backward(raws, grads, retain_graph=retain_graph)
+
+
+# ---------------------------------------------------------------------------
+# drivers
+# ---------------------------------------------------------------------------
+
+def _ensure_tree_attention(model):
+    register_hf_attention()
+    cfg = model.config
+    if getattr(cfg, "_attn_implementation", None) != ATTN_IMPL_NAME:
+        cfg._attn_implementation = ATTN_IMPL_NAME
+
+
+def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
+                     gateway_mask: str = "tree") -> None:
+    """Partitioned tree forward/backward (tree_grad_hybrid.py:434-539):
+    partitions run top-down, each with the gateway K/V of its cut node; then
+    bottom-up, each partition backpropagates its leaf losses and chains the
+    fp32 gateway gradients it received into its own graph, exactly once per
+    gateway.  Accumulates parameter gradients into ``.grad``."""
+    if gateway_mask not in ("tree", "reference"):
+        raise ValueError("gateway_mask must be 'tree' or 'reference'")
+    _ensure_tree_attention(model)
+    dev = next(model.parameters()).device
+    parts = partition_tree(roots, max_tokens)
+    children_of: Dict[int, List[Tuple[object, SubtreePartition]]] = {id(p): [] for p in parts}
+    for p in parts:
+        if p.parent is not None:
+            children_of[id(p.parent)].append((p.parent_cut_node, p))
+    gateways: Dict[int, SubtreeGateway] = {}
+    fwd: Dict[int, tuple] = {}
+    for p in parts:
+        gw = gateways.get(id(p))
+        p.pos_offset = gw.pos_offset if gw is not None else 0
+        logits, info, full_kv = _subtree_forward(model, p, gw, dev, gateway_mask)
+        fwd[id(p)] = (logits, info)
+        seen, cuts = set(), []
+        for cn, _ in children_of[id(p)]:
+            if id(cn) not in seen:
+                seen.add(id(cn))
+                cuts.append(cn)
+        if cuts:
+            child = _make_child_gateways(full_kv, info, p, gw, cuts, gateway_mask)
+            for cn, cp in children_of[id(p)]:
+                gateways[id(cp)] = child[id(cn)]
+    for p in reversed(parts):
+        logits, info = fwd[id(p)]
+        leaf_chunks = []
+        for c in info.leaf_chunk_ids_np.tolist():
+            orig = info.nodes[c].orig
+            if id(orig) in p.leaf_node_set:
+                s, e = info.chunk_bounds_np[c]
+                leaf_chunks.append((int(s), int(e), orig))
+        uniq, seen = [], set()
+        for cn, cp in children_of[id(p)]:
+            g = gateways.get(id(cp))
+            if g is not None and id(g) not in seen:
+                seen.add(id(g))
+                uniq.append(g)
+        remaining = len(leaf_chunks) + len(uniq)
+        for s, e, orig in leaf_chunks:
+            remaining -= 1
+            leaf_loss_fn(logits[:, s:e, :], orig).backward(retain_graph=remaining > 0)
+        for g in uniq:
+            remaining -= 1
+            _chain_gateway_grads(g, retain_graph=remaining > 0)
+
+
+def tree_grad_ckpt_sequential(model, roots, leaf_loss_fn: Callable) -> None:
+    """One packed forward over the whole forest, then per-leaf backward with
+    retain_graph on all but the last leaf (tree_grad_ckpt.py:39-107)."""
+    _ensure_tree_attention(model)
+    dev = next(model.parameters()).device
+    info = build_dfs_tree_info(roots)
+    meta = info.attn_meta()
+    ids = torch.as_tensor(info.dfs_token_ids_np, device=dev).unsqueeze(0)
+    pos = torch.as_tensor(info.dfs_pos_ids_np.astype(np.int64), device=dev).unsqueeze(0)
+    dtype = next(model.parameters()).dtype
+    mask = tree_mask_placeholder(meta, dtype=dtype, device=dev)
+    logits = model(input_ids=ids, attention_mask=mask, position_ids=pos, use_cache=False,
+                   tree_meta=meta).logits
+    leaves = info.leaf_chunk_ids_np.tolist()
+    for i, c in enumerate(leaves):
+        s, e = info.chunk_bounds_np[c]
+        leaf_loss_fn(logits[:, int(s):int(e), :], info.nodes[c]).backward(
+            retain_graph=i < len(leaves) - 1)
+
+
+def make_tree_loss_fn(leaf_labels, leaf_nodes, n_leaves: int, ignore_index: int = -100):
+    """Per-leaf CE / n_leaves (tree_grad_hybrid.py:546-558)."""
+    label_map = {id(n): lab for n, lab in zip(leaf_nodes, leaf_labels)}
+
+    def _fn(logits, node):
+        labels = label_map[id(getattr(node, "orig", node))].to(logits.device)
+        return F.cross_entropy(logits[0], labels, ignore_index=ignore_index) / n_leaves
+    return _fn

@@ -217,10 +217,10 @@ class TreeAttnMeta:
 
     def device(self, device: torch.device, tile_q: int, tile_kv: int) -> dict:
         """Device tensors for one tile shape (copied once, then cached)."""
-        key = (str(device), tile_q, tile_kv)
+        key = (device, tile_q, tile_kv)
         d = self._dev.get(key)
         if d is None:
-            ivk = (str(device), "iv")
+            ivk = (device, "iv")
             iv = self._dev.get(ivk)
             if iv is None:
                 # one buffer, padded so vectorised kernel reads stay inside it
