@@ -284,7 +284,7 @@ def run_ours(args):
     # Let the host enqueue the timed steps while the GPU idles in a short sleep,
     # so the events time the device work, not Python launch gaps (the e2e
     # number below includes all host work).
-    torch.cuda._sleep(int(12e6) * args.steps)
+    torch.cuda._sleep(int(8e6) * args.steps)
     host0 = time.perf_counter()
     for i in range(args.steps):
         flush.zero_()                       # L2 flush between timed steps

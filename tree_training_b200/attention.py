@@ -136,9 +136,10 @@ def attn_bwd_raw(dout, q, k, v, out, lse, meta_dev, scale: float):
         _lib.call("tt_tree_attn_bwd", *args, _lib.TT_BWD_DQ, status, side.cuda_stream)
         if timer is not None:
             timer.mark(side, "dq_done")
+    # Every tensor the side stream touched was allocated on `main`, and `main`
+    # waits for the side stream here, so any later reuse of their memory (which
+    # the caching allocator orders on `main`) is ordered after the dQ kernel.
     main.wait_stream(side)
-    for t in (ws, dq, q, k, v, out, dout, lse):
-        t.record_stream(side)
     return dq, dk, dv
 
 
