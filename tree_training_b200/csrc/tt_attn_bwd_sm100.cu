@@ -299,8 +299,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tc_fence_after();
       const uint32_t cs = 64 * sb + 32 * half, cp = 128 + 64 * sb + 32 * half;
       float sv[32], dp[32];
-      tmem_ld32(lane_addr + cs, sv);
-      tmem_ld32(lane_addr + cp, dp);
+      tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
       const float4* L4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes) + c0 / 4;
       const float4* D4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes + kAuxBytes / 2) + c0 / 4;
       uint32_t pw[16], dw[16];
@@ -453,8 +452,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tc_fence_after();
       const uint32_t cs = 64 * sb + 32 * half, cp = 128 + 64 * sb + 32 * half;
       float sv[32], dp[32];
-      tmem_ld32(lane_addr + cs, sv);
-      tmem_ld32(lane_addr + cp, dp);
+      tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
       float p[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) p[i] = exp2f(fmaf(sv[i], scale_log2, -l2));

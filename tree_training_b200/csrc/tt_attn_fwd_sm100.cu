@@ -246,11 +246,14 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
         tc_fence_after();
         float sv[kBN];
 #pragma unroll
-        for (int c = 0; c < kBN / 32; ++c) {
-          float t[32];
-          tmem_ld32(lane_addr + col_s + c * 32, t);
+        for (int c = 0; c < kBN / 64; ++c) {
+          float t0[32], t1[32];
+          tmem_ld32x2(lane_addr + col_s + c * 64, lane_addr + col_s + c * 64 + 32, t0, t1);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = t[i];
+          for (int i = 0; i < 32; ++i) {
+            sv[c * 64 + i] = t0[i];
+            sv[c * 64 + 32 + i] = t1[i];
+          }
         }
         if (partial) {
           const int4* lo4 = reinterpret_cast<const int4*>(aux + s * kAuxBytes);
