@@ -195,6 +195,71 @@ int tt_tree_attn_bwd_noalloc(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
 /* Largest hq * round_up(n_q, 128) that tt_tree_attn_bwd_noalloc accepts. */
 int64_t tt_tree_attn_bwd_noalloc_max_row_terms(void);
 
+/* ------------------------------------------------------------------------
+ * Tree gated delta rule (GDN).  Replaces torch_chunk_gated_delta_rule_tree_varlen
+ * (tree_dfs_ssm.py:38-156; same algorithm at dfs_tree_forward.py:253-353 and
+ * tree_grad_hybrid_ssm.py:48-135): one chunk per tree node, each node starting
+ * from the state after its PARENT node (tree_dfs_ssm.py:131-132), intra-node
+ * correction T = I + A + A^2 (the reference's row loop, :119-126), fp32
+ * internally.  Batch 1.  q, k: [S, Hk, Dk] with H % Hk == 0 (v-head h uses
+ * k-head h / (H/Hk)); v: [S, H, Dv]; all contiguous in `dtype`; g, beta: fp32
+ * [S, H].  bounds/parents: HOST int32 arrays (node i = tokens
+ * [bounds[2i], bounds[2i+1]), parent < i or -1, pre-order).  initial_state:
+ * fp32 [H, Dk, Dv] or NULL (zeros).  out: [S, H, Dv] in `dtype`; last_state:
+ * fp32 [H, Dk, Dv] = state after the LAST DFS node (tree_dfs_ssm.py:155), or
+ * NULL.  use_qk_l2norm: x * rsqrt(sum x^2 + 1e-6) on q and k first (:67-69).
+ * Dk, Dv <= 256.  Workspace: tt_gdn_tree_workspace_size(..., backward=0/1).
+ */
+int64_t tt_gdn_tree_workspace_size(int32_t S, int32_t H, int32_t Dk, int32_t Dv,
+                                   int32_t n_nodes, const int32_t* bounds, int backward);
+
+int tt_gdn_tree_fwd(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
+                    const void* q, const void* k, const void* v, const float* g,
+                    const float* beta, int32_t n_nodes, const int32_t* bounds,
+                    const int32_t* parents, const float* initial_state, int use_qk_l2norm,
+                    void* out, float* last_state, void* workspace, int64_t workspace_bytes,
+                    void* stream);
+
+/* Gradients of tt_gdn_tree_fwd (what torch autograd computes through the
+ * reference's Python loop): dout [S, H, Dv] (`dtype`), dlast fp32 [H, Dk, Dv]
+ * or NULL -> dq, dk (`dtype`, k-head layout, summed over each GQA group), dv
+ * (`dtype`), dg, dbeta (fp32 [S, H]), dinit fp32 [H, Dk, Dv] (or NULL).  The
+ * forward is recomputed inside (nothing is kept between the two calls). */
+int tt_gdn_tree_bwd(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
+                    const void* q, const void* k, const void* v, const float* g,
+                    const float* beta, int32_t n_nodes, const int32_t* bounds,
+                    const int32_t* parents, const float* initial_state, int use_qk_l2norm,
+                    const void* dout, const float* dlast, void* dq, void* dk, void* dv,
+                    float* dg, float* dbeta, float* dinit, void* workspace,
+                    int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Tree-correct depthwise causal conv + SiLU.  Replaces _tree_correct_conv_varlen
+ * (tree_dfs_ssm.py:285-348; dfs_tree_forward.py:191-246): each token's window
+ * is the K-1 tokens before it on its root-to-node path (the reference's saved
+ * parent context), zero padded at roots.  x, out: [C, S] (channels x tokens,
+ * token-contiguous, `dtype`); weight fp32 [C, K]; bias fp32 [C] or NULL.
+ * pred: device int32 [S, K-1], pred[t, m-1] = the token m steps before t on
+ * its path or -1 (tt_conv_predecessors builds it on the host).  K <= 8.
+ */
+int tt_conv_predecessors(int32_t n_nodes, const int32_t* bounds, const int32_t* parents,
+                         int32_t K, int32_t* pred);
+
+int tt_tree_conv_fwd(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
+                     const float* weight, const float* bias, const int32_t* pred, void* out,
+                     void* stream);
+
+/* dout [C, S] -> dx [C, S] (`dtype`), dweight fp32 [C, K], dbias fp32 [C] (or
+ * NULL).  Deterministic: dx gathers over each token's successors (succ CSR from
+ * tt_conv_successors), dweight/dbias reduce per channel without atomics. */
+int tt_conv_successors(int32_t S, int32_t K, const int32_t* pred, int32_t* succ_ptr,
+                       int32_t* succ_tok, int32_t* succ_lag, int64_t cap);
+
+int tt_tree_conv_bwd(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
+                     const float* weight, const float* bias, const int32_t* pred,
+                     const int32_t* succ_ptr, const int32_t* succ_tok, const int32_t* succ_lag,
+                     const void* dout, void* dx, float* dweight, float* dbias, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,176 @@
+"""Tree GDN and tree conv on a B200 vs the reference's outputs and the oracle.
+
+* golden fixtures produced by torch_chunk_gated_delta_rule_tree_varlen and
+  _tree_correct_conv_varlen themselves: fp32 path, max_rel < 2e-5 (the GDN bar)
+* random trees vs the float64 oracle: fp32 < 5e-5, bf16 < 2e-2
+* config-4 size (16,384-token tree, 16 k-heads / 32 v-heads, D=128, bf16):
+  one k-head and its two v-heads checked against the oracle
+"""
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import tree_oracle as O
+from tests.golden_util import load
+
+import tree_training_b200 as tt
+from tree_training_b200.gdn import _tree_correct_conv_varlen, torch_chunk_gated_delta_rule_tree_varlen
+from tree_training_b200.synthetic import random_branching_tree
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0)
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / (np.abs(b).max() + 1e-30))
+
+
+def run_gdn(q, k, v, g, beta, bounds, parents, init, l2, dout, dlast, dtype):
+    T = lambda x: torch.tensor(x, dtype=dtype, device=DEV, requires_grad=True)
+    F32 = lambda x: torch.tensor(x, dtype=torch.float32, device=DEV, requires_grad=True)
+    qt, kt, vt = T(q), T(k), T(v)
+    gt, bt = F32(g), F32(beta)
+    it = F32(init) if init is not None else None
+    out, last = torch_chunk_gated_delta_rule_tree_varlen(
+        qt, kt, vt, gt, bt, bounds, parents, initial_state=it,
+        output_final_state=dlast is not None, use_qk_l2norm_in_kernel=l2)
+    loss = (out.float() * torch.tensor(dout, dtype=torch.float32, device=DEV)).sum()
+    if dlast is not None:
+        loss = loss + (last * torch.tensor(dlast, dtype=torch.float32, device=DEV)).sum()
+    loss.backward()
+    torch.cuda.synchronize()
+    f = lambda t: None if t is None else t.detach().double().cpu().numpy()
+    return dict(out=f(out), last=f(last), dq=f(qt.grad), dk=f(kt.grad), dv=f(vt.grad),
+                dg=f(gt.grad), dbeta=f(bt.grad), dinit=f(it.grad) if it is not None else None)
+
+
+@pytest.mark.parametrize("name", ["gdn_tree_l2", "gdn_tree_init_final", "gdn_forest47"])
+def test_gdn_matches_reference_fixture(name):
+    d = load(name)
+    bounds = [tuple(b) for b in d["chunk_boundaries"].tolist()]
+    parents = d["chunk_parent_map"].tolist()
+    init = d["init"] if d["init"].size else None
+    dlast = d["dlast"] if d["dlast"].size else None
+    got = run_gdn(d["q"], d["k"], d["v"], d["g"], d["beta"], bounds, parents, init,
+                  bool(int(d["l2norm"])), d["dout"], dlast, torch.float32)
+    for key in ("out", "dq", "dk", "dv", "dg", "dbeta"):
+        assert rel(got[key], d[key]) < 2e-5, key
+    if dlast is not None:
+        assert rel(got["last"], d["last"]) < 2e-5
+    if init is not None:
+        assert rel(got["dinit"], d["dinit"]) < 2e-5
+
+
+def _case(seed, S, Hk, H, D, lo, hi, init=False):
+    roots = random_branching_tree(seed, S, lo, hi)
+    info = tt.build_dfs_tree_info(roots)
+    g_ = np.random.default_rng(seed)
+    q = g_.standard_normal((1, S, Hk, D))
+    k = g_.standard_normal((1, S, Hk, D))
+    v = g_.standard_normal((1, S, H, D)) * 0.5
+    gg = -np.log1p(np.exp(-g_.standard_normal((1, S, H))))         # logsigmoid(N(0,1))
+    bt = 1.0 / (1.0 + np.exp(-g_.standard_normal((1, S, H))))      # sigmoid(N(0,1))
+    s0 = g_.standard_normal((1, H, D, D)) * 0.05 if init else None
+    do = g_.standard_normal((1, S, H, D))
+    dl = g_.standard_normal((1, H, D, D)) if init else None
+    return info, q, k, v, gg, bt, s0, do, dl
+
+
+def _oracle(info, q, k, v, gg, bt, s0, do, dl):
+    out, states = O.gdn_tree_fwd(q, k, v, gg, bt, info.chunk_boundaries, info.chunk_parent_map,
+                                 s0, True)
+    grads = O.gdn_tree_bwd(q, k, v, gg, bt, info.chunk_boundaries, info.chunk_parent_map, do,
+                           s0, True, dl)
+    return dict(out=out, last=states[-1], dq=grads[0], dk=grads[1], dv=grads[2], dg=grads[3],
+                dbeta=grads[4], dinit=grads[5])
+
+
+@pytest.mark.parametrize("dtype,tol,init", [(torch.float32, 5e-5, True), (torch.bfloat16, 2e-2, False)])
+def test_gdn_random_tree_vs_oracle(dtype, tol, init):
+    info, q, k, v, gg, bt, s0, do, dl = _case(3, 1200, 2, 4, 64, 16, 300, init)
+    if dtype == torch.bfloat16:
+        rnd = lambda x: torch.tensor(x, dtype=torch.bfloat16).double().numpy()
+        q, k, v = rnd(q), rnd(k), rnd(v)
+    ref = _oracle(info, q, k, v, gg, bt, s0, do, dl)
+    got = run_gdn(q, k, v, gg, bt, info.chunk_boundaries, info.chunk_parent_map, s0, True, do,
+                  dl, dtype)
+    keys = ["out", "dq", "dk", "dv", "dg", "dbeta"] + (["last", "dinit"] if init else [])
+    for key in keys:
+        assert rel(got[key], ref[key]) < tol, key
+
+
+def test_gdn_config4_size_head_slice_vs_oracle():
+    """BASELINE config 4 shape; the oracle checks k-head 0 and its v-heads 0, 1."""
+    S, Hk, H, D = 16384, 16, 32, 128
+    info, q, k, v, gg, bt, _, do, _ = _case(4, S, Hk, H, D, 16, 300)
+    rnd = lambda x: torch.tensor(x, dtype=torch.bfloat16).double().numpy()
+    q, k, v = rnd(q), rnd(k), rnd(v)
+    got = run_gdn(q, k, v, gg, bt, info.chunk_boundaries, info.chunk_parent_map, None, True, do,
+                  None, torch.bfloat16)
+    for key in got:
+        if got[key] is not None:
+            assert np.isfinite(got[key]).all(), key
+    sl = slice(0, 2)
+    ref = _oracle(info, q[:, :, :1], k[:, :, :1], v[:, :, sl], gg[:, :, sl], bt[:, :, sl], None,
+                  do[:, :, sl], None)
+    assert rel(got["out"][:, :, sl], ref["out"]) < 2e-2
+    assert rel(got["dv"][:, :, sl], ref["dv"]) < 2e-2
+    assert rel(got["dq"][:, :, :1], ref["dq"]) < 2e-2
+    assert rel(got["dk"][:, :, :1], ref["dk"]) < 2e-2
+    assert rel(got["dg"][:, :, sl], ref["dg"]) < 2e-2
+    assert rel(got["dbeta"][:, :, sl], ref["dbeta"]) < 2e-2
+
+
+class _Conv:
+    """The attributes of a GatedDeltaNet layer that the conv drop-in reads."""
+
+    def __init__(self, w, b=None):
+        self.conv1d = torch.nn.Conv1d(w.shape[0], w.shape[0], w.shape[1], groups=w.shape[0],
+                                      padding=w.shape[1] - 1, bias=b is not None).to(DEV)
+        with torch.no_grad():
+            self.conv1d.weight.copy_(torch.tensor(w[:, None, :], dtype=torch.float32))
+            if b is not None:
+                self.conv1d.bias.copy_(torch.tensor(b, dtype=torch.float32))
+        self.conv_kernel_size = w.shape[1]
+        self.activation = "silu"
+        self.causal_conv1d_fn = None
+
+
+@pytest.mark.parametrize("name", ["conv_tree", "conv_short_nodes"])
+def test_tree_conv_matches_reference_fixture(name):
+    d = load(name)
+    ssm = _Conv(d["weight"])
+    x = torch.tensor(d["x"], dtype=torch.float32, device=DEV, requires_grad=True)
+    bounds = [tuple(b) for b in d["chunk_boundaries"].tolist()]
+    y = _tree_correct_conv_varlen(ssm, x, bounds, d["chunk_parent_map"].tolist())
+    y.backward(torch.tensor(d["dout"], dtype=torch.float32, device=DEV))
+    f = lambda t: t.detach().double().cpu().numpy()
+    assert rel(f(y), d["out"]) < 1e-5
+    assert rel(f(x.grad), d["dx"]) < 1e-5
+    assert rel(f(ssm.conv1d.weight.grad)[:, 0], d["dweight"]) < 1e-5
+
+
+def test_tree_conv_random_tree_with_bias_vs_oracle():
+    info = tt.build_dfs_tree_info(random_branching_tree(9, 3000, 1, 40))
+    g_ = np.random.default_rng(9)
+    C, K = 64, 4
+    x = g_.standard_normal((2, C, info.N))
+    w = g_.standard_normal((C, K)) * 0.5
+    b = g_.standard_normal(C) * 0.1
+    dy = g_.standard_normal((2, C, info.N))
+    ssm = _Conv(w, b)
+    xt = torch.tensor(x, dtype=torch.float32, device=DEV, requires_grad=True)
+    y = _tree_correct_conv_varlen(ssm, xt, info.chunk_boundaries, info.chunk_parent_map)
+    y.backward(torch.tensor(dy, dtype=torch.float32, device=DEV))
+    ref_y, _ = O.tree_conv_fwd(x, w, info.chunk_boundaries, info.chunk_parent_map, b)
+    dx, dw, db = O.tree_conv_bwd(x, w, info.chunk_boundaries, info.chunk_parent_map, dy, b)
+    f = lambda t: t.detach().double().cpu().numpy()
+    assert rel(f(y), ref_y) < 1e-5
+    assert rel(f(xt.grad), dx) < 1e-5
+    assert rel(f(ssm.conv1d.weight.grad)[:, 0], dw) < 1e-5
+    assert rel(f(ssm.conv1d.bias.grad), db) < 1e-5

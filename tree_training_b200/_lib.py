@@ -57,6 +57,17 @@ SIGNATURES = {
                                         _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
                                         _P, _P]),
     "tt_tree_attn_bwd_noalloc_max_row_terms": (_I64, []),
+    "tt_gdn_tree_workspace_size": (_I64, [_I32, _I32, _I32, _I32, _I32, _P, _INT]),
+    "tt_gdn_tree_fwd": (_INT, [_INT, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P,
+                               _I32, _P, _P, _P, _INT, _P, _P, _P, _I64, _P]),
+    "tt_gdn_tree_bwd": (_INT, [_INT, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P,
+                               _I32, _P, _P, _P, _INT, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                               _I64, _P]),
+    "tt_conv_predecessors": (_INT, [_I32, _P, _P, _I32, _P]),
+    "tt_conv_successors": (_INT, [_I32, _I32, _P, _P, _P, _P, _I64]),
+    "tt_tree_conv_fwd": (_INT, [_INT, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),
+    "tt_tree_conv_bwd": (_INT, [_INT, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                _P, _P, _P]),
 }
 
 _lib = None

@@ -1,0 +1,955 @@
+// Tree gated delta rule (GDN), forward and backward, fp32 internally.
+//
+// Restates torch_chunk_gated_delta_rule_tree_varlen (tree_dfs_ssm.py:38-156):
+// one chunk per tree node c (tokens [s, e), L = e - s), per v-head:
+//   gam = cumsum(g)                                   (:106)
+//   D[j,m] = exp(gam_j - gam_m) for j >= m            (:109)
+//   A = -(beta_j k_j . k_m) D   strictly lower        (:116)
+//   T = I + A + A^2   (the row loop at :119-126)      applied as x + Ax + A(Ax)
+//   U = T (v beta),  W = T (k beta e^gam)             (:127-128)
+//   S_in = state after the PARENT node                (:131-132)
+//   Vn = U - W S_in                                   (:134-135)
+//   O = (q e^gam) S_in + (q k^T * D, lower incl.) Vn  (:137-140)
+//   S_out = e^{gam_L} S_in + (k e^{gam_L - gam})^T Vn (:144-148)
+// and the exact gradient of that function (what torch autograd computes
+// through the reference's Python loop).
+//
+// Everything is expressed as per-node segmented GEMMs (one descriptor per
+// node, any strides per operand) plus elementwise kernels; node states only
+// depend on the parent, so the recurrence runs one launch set per tree depth
+// level (all nodes of a level in parallel) and the backward runs the levels in
+// reverse, summing each node's state gradient over its children without
+// atomics.  Internal layout: per-token vectors [H][S][D] fp32, per-node LxL
+// matrices packed per node ([H][sum L^2]), states [n_nodes+1][H][Dk][Dv].
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "tt_common.cuh"
+
+namespace tt {
+namespace gdn {
+namespace {
+
+struct SegDesc {
+  int M, N, K, pad;
+  long long a_off, a_rs, a_cs;
+  long long b_off, b_rs, b_cs;
+  long long c_off, c_rs, c_cs;
+};
+
+constexpr int kBM = 64, kBN = 64, kBK = 16;
+
+// C[i,j] = alpha * sum_k A[i,k] B[k,j] + beta * C[i,j] for each segment and
+// head (blockIdx.z); operand element (r, c) of segment s lives at
+// base + head * h_stride + off_s + r * rs_s + c * cs_s.
+__global__ void __launch_bounds__(256)
+seg_gemm(const SegDesc* __restrict__ segs, const float* __restrict__ A, long long a_hs,
+         const float* __restrict__ B, long long b_hs, float* __restrict__ C, long long c_hs,
+         float alpha, float beta) {
+  const SegDesc sd = segs[blockIdx.y];
+  const int n_tn = (sd.N + kBN - 1) / kBN;
+  const int tm = blockIdx.x / n_tn, tn = blockIdx.x % n_tn;
+  if (tm * kBM >= sd.M || sd.N <= 0) return;
+  const int h = blockIdx.z;
+  const float* a = A + h * a_hs + sd.a_off;
+  const float* b = B + h * b_hs + sd.b_off;
+  float* c = C + h * c_hs + sd.c_off;
+  __shared__ float sa[kBK][kBM + 4];
+  __shared__ float sb[kBK][kBN + 4];
+  const int tid = threadIdx.x;
+  const int ty = tid / 16, tx = tid % 16;
+  float acc[4][4] = {};
+  const int i0 = tm * kBM, j0 = tn * kBN;
+  for (int k0 = 0; k0 < sd.K; k0 += kBK) {
+    // A tile [kBM x kBK] (stored transposed in smem); make the fastest thread
+    // index walk the unit-stride dimension
+    for (int e = tid; e < kBM * kBK; e += 256) {
+      int r, kk;
+      if (sd.a_cs == 1) { r = e / kBK; kk = e % kBK; } else { r = e % kBM; kk = e / kBM; }
+      const int gi = i0 + r, gk = k0 + kk;
+      sa[kk][r] = (gi < sd.M && gk < sd.K) ? a[gi * sd.a_rs + gk * sd.a_cs] : 0.f;
+    }
+    for (int e = tid; e < kBK * kBN; e += 256) {
+      int kk, cc;
+      if (sd.b_cs == 1) { kk = e / kBN; cc = e % kBN; } else { kk = e % kBK; cc = e / kBK; }
+      const int gk = k0 + kk, gj = j0 + cc;
+      sb[kk][cc] = (gk < sd.K && gj < sd.N) ? b[gk * sd.b_rs + gj * sd.b_cs] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kBK; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        av[u] = sa[kk][ty + 16 * u];
+        bv[u] = sb[kk][tx + 16 * u];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int w = 0; w < 4; ++w) acc[u][w] = fmaf(av[u], bv[w], acc[u][w]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int gi = i0 + ty + 16 * u;
+    if (gi >= sd.M) continue;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int gj = j0 + tx + 16 * w;
+      if (gj >= sd.N) continue;
+      float* p = c + gi * sd.c_rs + gj * sd.c_cs;
+      *p = alpha * acc[u][w] + (beta != 0.f ? beta * *p : 0.f);
+    }
+  }
+}
+
+// ---- elementwise kernels ---------------------------------------------------------
+
+// Per (head, token): normalised/scaled q and k, v, beta, and the scaled copies
+// used as GEMM operands.  gam must already hold the per-node cumsum.
+template <typename T>
+__global__ void prep_tokens(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__ q,
+                            const T* __restrict__ k, const T* __restrict__ v,
+                            const float* __restrict__ beta, const float* __restrict__ gam,
+                            const float* __restrict__ gl_tok, int l2norm, float q_scale,
+                            float* Q, float* K, float* Vb, float* Kb, float* Kbg, float* Qg,
+                            float* Kd) {
+  const int t = blockIdx.x, h = blockIdx.y;
+  const int hk = h / (H / Hk);
+  const T* qr = q + ((long long)t * Hk + hk) * Dk;
+  const T* kr = k + ((long long)t * Hk + hk) * Dk;
+  __shared__ float red[2][32];
+  float sq = 0.f, sk = 0.f;
+  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+    const float a = to_f32(qr[d]), b = to_f32(kr[d]);
+    sq += a * a;
+    sk += b * b;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    sk += __shfl_xor_sync(0xffffffffu, sk, o);
+  }
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    red[0][wid] = sq;
+    red[1][wid] = sk;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f, b = 0.f;
+    for (int w = 0; w < nw; ++w) {
+      a += red[0][w];
+      b += red[1][w];
+    }
+    red[0][0] = a;
+    red[1][0] = b;
+  }
+  __syncthreads();
+  const float rq = l2norm ? rsqrtf(red[0][0] + 1e-6f) : 1.f;
+  const float rk = l2norm ? rsqrtf(red[1][0] + 1e-6f) : 1.f;
+  const long long ht = (long long)h * S + t;
+  const float bt = beta[(long long)t * H + h];
+  const float gm = gam[ht];
+  const float eg = expf(gm), ed = expf(gl_tok[ht] - gm);
+  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+    const float qs = to_f32(qr[d]) * rq * q_scale;
+    const float ks = to_f32(kr[d]) * rk;
+    Q[ht * Dk + d] = qs;
+    K[ht * Dk + d] = ks;
+    Kb[ht * Dk + d] = ks * bt;
+    Kbg[ht * Dk + d] = ks * bt * eg;
+    Qg[ht * Dk + d] = qs * eg;
+    Kd[ht * Dk + d] = ks * ed;
+  }
+  const T* vr = v + ((long long)t * H + h) * Dv;
+  for (int d = threadIdx.x; d < Dv; d += blockDim.x) Vb[ht * Dv + d] = to_f32(vr[d]) * bt;
+}
+
+// Per (node, head): gam = cumsum(g) over the node's tokens, gl_tok = gam at the
+// node's last token (written for every token of the node), gl[c] too.
+__global__ void node_cumsum(int S, int H, int n_nodes, const int* __restrict__ nstart,
+                            const int* __restrict__ nlen, const float* __restrict__ g,
+                            float* gam, float* gl_tok, float* gl) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int h = blockIdx.y;
+  if (c >= n_nodes) return;
+  const int s = nstart[c], L = nlen[c];
+  float acc = 0.f;
+  for (int j = 0; j < L; ++j) {
+    acc += g[(long long)(s + j) * H + h];
+    gam[(long long)h * S + s + j] = acc;
+  }
+  for (int j = 0; j < L; ++j) gl_tok[(long long)h * S + s + j] = acc;
+  gl[(long long)h * n_nodes + c] = acc;
+}
+
+// In place on the packed LxL matrices of every node: A = -KK * D (strict
+// lower), Aqk = QK * D (lower incl.).  Raw products are kept in KK/QK.
+__global__ void decay_masks(int S, const int* __restrict__ nstart, const int* __restrict__ nlen,
+                            const long long* __restrict__ loff, long long l_hs,
+                            const float* __restrict__ gam, const float* __restrict__ KK,
+                            const float* __restrict__ QK, float* Am, float* Aqk) {
+  const int c = blockIdx.y, h = blockIdx.z, j = blockIdx.x;
+  const int L = nlen[c];
+  if (j >= L) return;
+  const long long base = h * l_hs + loff[c] + (long long)j * L;
+  const float gj = gam[(long long)h * S + nstart[c] + j];
+  for (int m = threadIdx.x; m < L; m += blockDim.x) {
+    const float d = m <= j ? expf(gj - gam[(long long)h * S + nstart[c] + m]) : 0.f;
+    Am[base + m] = m < j ? -KK[base + m] * d : 0.f;
+    Aqk[base + m] = m <= j ? QK[base + m] * d : 0.f;
+  }
+}
+
+__global__ void add_arrays(long long n, const float* __restrict__ a, const float* __restrict__ b,
+                           float* out) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = a[i] + b[i];
+}
+
+__global__ void copy_array(long long n, const float* __restrict__ a, float* out) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = a[i];
+}
+
+// states[c+1][h] += exp(gl[h][c]) * states[parent+1][h]   for the level's nodes
+__global__ void state_decay_add(int H, int DkDv, int n_nodes, const int* __restrict__ nodes,
+                                const int* __restrict__ parent, const float* __restrict__ gl,
+                                float* states) {
+  const int c = nodes[blockIdx.y], h = blockIdx.z;
+  const long long hs = (long long)H * DkDv;
+  const float f = expf(gl[(long long)h * n_nodes + c]);
+  const float* src = states + (long long)(parent[c] + 1) * hs + (long long)h * DkDv;
+  float* dst = states + (long long)(c + 1) * hs + (long long)h * DkDv;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < DkDv; i += gridDim.x * blockDim.x)
+    dst[i] += f * src[i];
+}
+
+// Fill states[0] (initial state or zeros).
+__global__ void init_state(long long n, const float* __restrict__ init, float* s0) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) s0[i] = init ? init[i] : 0.f;
+}
+
+template <typename T>
+__global__ void store_out(int S, int H, int Dv, const float* __restrict__ O, T* out) {
+  const int t = blockIdx.x, h = blockIdx.y;
+  for (int d = threadIdx.x; d < Dv; d += blockDim.x)
+    out[((long long)t * H + h) * Dv + d] = from_f32<T>(O[((long long)h * S + t) * Dv + d]);
+}
+
+template <typename T>
+__global__ void load_dout(int S, int H, int Dv, const T* __restrict__ dout, float* dO) {
+  const int t = blockIdx.x, h = blockIdx.y;
+  for (int d = threadIdx.x; d < Dv; d += blockDim.x)
+    dO[((long long)h * S + t) * Dv + d] = to_f32(dout[((long long)t * H + h) * Dv + d]);
+}
+
+// dSo[c] = sum over children dSi[ch] (+ dlast for the last DFS node) for the
+// level's nodes; children in CSR (child_ptr, child_idx).
+__global__ void gather_dstate(int H, int DkDv, int n_nodes, const int* __restrict__ nodes,
+                              const int* __restrict__ child_ptr, const int* __restrict__ child_idx,
+                              const float* __restrict__ dSi, const float* __restrict__ dlast,
+                              float* dSo) {
+  const int c = nodes[blockIdx.y], h = blockIdx.z;
+  const long long hs = (long long)H * DkDv;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < DkDv; i += gridDim.x * blockDim.x) {
+    float a = (dlast && c == n_nodes - 1) ? dlast[(long long)h * DkDv + i] : 0.f;
+    for (int e = child_ptr[c]; e < child_ptr[c + 1]; ++e)
+      a += dSi[(long long)child_idx[e] * hs + (long long)h * DkDv + i];
+    dSo[(long long)c * hs + (long long)h * DkDv + i] = a;
+  }
+}
+
+// dSi[c] += exp(gl[c]) dSo[c]  and  dgl[h][c] = exp(gl[c]) <S_in, dSo>  (the
+// gradient of the state decay factor) for the level's nodes.
+__global__ void dstate_decay(int H, int DkDv, int n_nodes, const int* __restrict__ nodes,
+                             const int* __restrict__ parent, const float* __restrict__ gl,
+                             const float* __restrict__ states, const float* __restrict__ dSo,
+                             float* dSi, float* dgl) {
+  const int c = nodes[blockIdx.x], h = blockIdx.y;
+  const long long hs = (long long)H * DkDv;
+  const float f = expf(gl[(long long)h * n_nodes + c]);
+  const float* sin = states + (long long)(parent[c] + 1) * hs + (long long)h * DkDv;
+  const float* so = dSo + (long long)c * hs + (long long)h * DkDv;
+  float* si = dSi + (long long)c * hs + (long long)h * DkDv;
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < DkDv; i += blockDim.x) {
+    si[i] += f * so[i];
+    acc += sin[i] * so[i];
+  }
+  __shared__ float red[32];
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a += red[w];
+    dgl[(long long)h * n_nodes + c] = f * a;
+  }
+}
+
+// On every node's LxL matrices:
+//   dA  = (dT + dT A^T + A^T dT) on the strict lower part (inputs combined by
+//         the caller into dA = dT + X, X = dT A^T + A^T dT), masked here;
+//   G   = -dA * D (-> dKb += G K, dK += G^T Kb)
+//   F   = dAqk * D (lower incl.; -> dQ += F K, dK += F^T Q)
+//   dDD = (-dA * KK + dAqk * QK) * D, whose row/col sums give dgam.
+__global__ void grad_masks(int S, const int* __restrict__ nstart, const int* __restrict__ nlen,
+                           const long long* __restrict__ loff, long long l_hs,
+                           const float* __restrict__ gam, const float* __restrict__ KK,
+                           const float* __restrict__ QK, float* dA, float* dAqk, float* dDD) {
+  const int c = blockIdx.y, h = blockIdx.z, j = blockIdx.x;
+  const int L = nlen[c];
+  if (j >= L) return;
+  const long long base = h * l_hs + loff[c] + (long long)j * L;
+  const float gj = gam[(long long)h * S + nstart[c] + j];
+  for (int m = threadIdx.x; m < L; m += blockDim.x) {
+    const float d = m <= j ? expf(gj - gam[(long long)h * S + nstart[c] + m]) : 0.f;
+    const float da = m < j ? dA[base + m] : 0.f;
+    const float dq = m <= j ? dAqk[base + m] : 0.f;
+    dDD[base + m] = (-da * KK[base + m] + dq * QK[base + m]) * d;
+    dA[base + m] = -da * d;      // G
+    dAqk[base + m] = dq * d;     // F
+  }
+}
+
+// dgam_j += sum_m dDD[j, m] - sum_i dDD[i, j]  (per node, per head)
+__global__ void ddd_rowcol(int S, const int* __restrict__ nstart, const int* __restrict__ nlen,
+                           const long long* __restrict__ loff, long long l_hs,
+                           const float* __restrict__ dDD, float* dgam) {
+  const int c = blockIdx.y, h = blockIdx.z, j = blockIdx.x;
+  const int L = nlen[c];
+  if (j >= L) return;
+  const float* base = dDD + h * l_hs + loff[c];
+  float acc = 0.f;
+  for (int m = threadIdx.x; m < L; m += blockDim.x) acc += base[(long long)j * L + m] - base[(long long)m * L + j];
+  __shared__ float red[32];
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a += red[w];
+    dgam[(long long)h * S + nstart[c] + j] += a;
+  }
+}
+
+// Per (head, token): assemble the input gradients.  Inputs (fp32 [H][S][D]):
+// dQs (grad of the scaled q, incl. the e^gam part via dQg), dKt (grad of k
+// from all k-terms except the beta-scaled ones), dKb (grad of k*beta incl.
+// dKbg*e^gam), dVb; plus gam, gl, and the Qg/Kbg/Kd-dependent dgam parts.
+template <typename T>
+__global__ void assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__ q,
+                                     const T* __restrict__ k, const T* __restrict__ v,
+                                     const float* __restrict__ beta, const float* __restrict__ gam,
+                                     const float* __restrict__ gl_tok, int l2norm, float q_scale,
+                                     const float* __restrict__ dQ, const float* __restrict__ dQg,
+                                     const float* __restrict__ dK, const float* __restrict__ dKd,
+                                     const float* __restrict__ dKb, const float* __restrict__ dKbg,
+                                     const float* __restrict__ dVb, float* dgam, float* dq_h,
+                                     float* dk_h, float* dbeta_out, T* dv_out) {
+  const int t = blockIdx.x, h = blockIdx.y;
+  const int hk = h / (H / Hk);
+  const long long ht = (long long)h * S + t;
+  const T* qr = q + ((long long)t * Hk + hk) * Dk;
+  const T* kr = k + ((long long)t * Hk + hk) * Dk;
+  const float bt = beta[(long long)t * H + h];
+  const float gm = gam[ht];
+  const float eg = expf(gm), ed = expf(gl_tok[ht] - gm);
+  // norms again (cheap) for the normalised q/k and the l2norm backward
+  __shared__ float red[6][32];
+  float sq = 0.f, sk = 0.f;
+  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+    const float a = to_f32(qr[d]), b = to_f32(kr[d]);
+    sq += a * a;
+    sk += b * b;
+  }
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  auto block_sum = [&](float x, int slot) -> float {
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    __syncthreads();
+    if (lane == 0) red[slot][wid] = x;
+    __syncthreads();
+    float a = 0.f;
+    for (int w = 0; w < nw; ++w) a += red[slot][w];
+    return a;
+  };
+  sq = block_sum(sq, 0);
+  sk = block_sum(sk, 1);
+  const float rq = l2norm ? rsqrtf(sq + 1e-6f) : 1.f;
+  const float rk = l2norm ? rsqrtf(sk + 1e-6f) : 1.f;
+  // d(scaled q) = dQ + dQg e^gam ; d(k) = dK + dKd e^{gl-gam} + beta (dKb + dKbg e^gam)
+  float p_qg = 0.f, p_kbg = 0.f, p_kd = 0.f, p_kb = 0.f, xdq = 0.f, xdk = 0.f;
+  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+    const float qn = to_f32(qr[d]) * rq, kn = to_f32(kr[d]) * rk;
+    const float qs = qn * q_scale;
+    const float gqs = dQ[ht * Dk + d] + dQg[ht * Dk + d] * eg;
+    const float gkb = dKb[ht * Dk + d] + dKbg[ht * Dk + d] * eg;
+    const float gk = dK[ht * Dk + d] + dKd[ht * Dk + d] * ed + bt * gkb;
+    p_qg += qs * eg * dQg[ht * Dk + d];
+    p_kbg += kn * bt * eg * dKbg[ht * Dk + d];
+    p_kd += kn * ed * dKd[ht * Dk + d];
+    p_kb += kn * gkb;
+    const float gqn = gqs * q_scale;          // grad wrt normalised q
+    xdq += qn * gqn;
+    xdk += kn * gk;
+    dq_h[ht * Dk + d] = gqn;                  // finished below with the l2norm backward
+    dk_h[ht * Dk + d] = gk;
+  }
+  p_qg = block_sum(p_qg, 2);
+  p_kbg = block_sum(p_kbg, 3);
+  p_kd = block_sum(p_kd, 4);
+  p_kb = block_sum(p_kb, 5);
+  xdq = block_sum(xdq, 0);
+  xdk = block_sum(xdk, 1);
+  // y = x r (r = (|x|^2+eps)^-1/2): dx = r dy - r^3 (x.dy) x = r (dy - (y.dy) y)
+  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+    if (l2norm) {
+      const float qn = to_f32(qr[d]) * rq, kn = to_f32(kr[d]) * rk;
+      dq_h[ht * Dk + d] = rq * (dq_h[ht * Dk + d] - xdq * qn);
+      dk_h[ht * Dk + d] = rk * (dk_h[ht * Dk + d] - xdk * kn);
+    }
+  }
+  float p_vb = 0.f;
+  const T* vr = v + ((long long)t * H + h) * Dv;
+  for (int d = threadIdx.x; d < Dv; d += blockDim.x) {
+    const float g = dVb[ht * Dv + d];
+    p_vb += to_f32(vr[d]) * g;
+    dv_out[((long long)t * H + h) * Dv + d] = from_f32<T>(g * bt);
+  }
+  p_vb = block_sum(p_vb, 2);
+  if (threadIdx.x == 0) {
+    dbeta_out[(long long)t * H + h] = p_kb + p_vb;
+    // e^gam terms of Qg, Kbg and the -gam of Kd (the +gl part goes to the node's last token)
+    dgam[ht] += p_qg + p_kbg - p_kd;
+  }
+}
+
+// dgl per node from the Kd term: sum over the node's tokens of kn e^{gl-gam} . dKd,
+// added to dgam at the node's last token together with the state-decay part.
+// Then dg = reverse cumsum of dgam within the node.
+__global__ void node_dg(int S, int H, int n_nodes, const int* __restrict__ nstart,
+                        const int* __restrict__ nlen, const float* __restrict__ kd_dot,
+                        const float* __restrict__ dgl, float* dgam, float* dg) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x, h = blockIdx.y;
+  if (c >= n_nodes) return;
+  const int s = nstart[c], L = nlen[c];
+  if (L == 0) return;
+  float tail = dgl[(long long)h * n_nodes + c];
+  for (int j = 0; j < L; ++j) tail += kd_dot[(long long)h * S + s + j];
+  dgam[(long long)h * S + s + L - 1] += tail;
+  float acc = 0.f;
+  for (int j = L - 1; j >= 0; --j) {
+    acc += dgam[(long long)h * S + s + j];
+    dg[(long long)(s + j) * H + h] = acc;
+  }
+}
+
+// kd_dot[h][t] = kn_t e^{gl-gam_t} . dKd_t  (per token, reduced over Dk)
+__global__ void kd_dot_kernel(int S, int Dk, const float* __restrict__ Kd,
+                              const float* __restrict__ dKd, float* out) {
+  const long long ht = (long long)blockIdx.y * S + blockIdx.x;
+  float acc = 0.f;
+  for (int d = threadIdx.x; d < Dk; d += blockDim.x) acc += Kd[ht * Dk + d] * dKd[ht * Dk + d];
+  __shared__ float red[32];
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a += red[w];
+    out[ht] = a;
+  }
+}
+
+// dq/dk per k-head: sum the per-v-head gradients of each GQA group, cast.
+template <typename T>
+__global__ void reduce_gqa(int S, int Hk, int H, int Dk, const float* __restrict__ src, T* dst) {
+  const int t = blockIdx.x, hk = blockIdx.y, rep = H / Hk;
+  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+    float a = 0.f;
+    for (int r = 0; r < rep; ++r) a += src[(((long long)(hk * rep + r)) * S + t) * Dk + d];
+    dst[((long long)t * Hk + hk) * Dk + d] = from_f32<T>(a);
+  }
+}
+
+__global__ void dinit_kernel(int H, int DkDv, int n_roots, const int* __restrict__ roots,
+                             const float* __restrict__ dSi, float* dinit) {
+  const long long hs = (long long)H * DkDv;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= hs) return;
+  float a = 0.f;
+  for (int r = 0; r < n_roots; ++r) a += dSi[(long long)roots[r] * hs + i];
+  dinit[i] = a;
+}
+
+// =============================================================================
+// host orchestration
+// =============================================================================
+
+struct Plan {
+  int S, H, Hk, Dk, Dv, n;
+  std::vector<int> start, len, parent, depth;
+  std::vector<long long> loff;     // packed LxL offset per node
+  long long ll_total = 0;          // sum L^2
+  int max_len = 0, max_depth = 0;
+  std::vector<std::vector<int>> levels;
+  std::vector<int> child_ptr, child_idx, roots;
+};
+
+int make_plan(Plan& p, int S, int H, int Hk, int Dk, int Dv, int n, const int32_t* bounds,
+              const int32_t* parents) {
+  p.S = S; p.H = H; p.Hk = Hk; p.Dk = Dk; p.Dv = Dv; p.n = n;
+  p.start.resize(n); p.len.resize(n); p.parent.resize(n); p.depth.resize(n); p.loff.resize(n);
+  int expect = 0;
+  for (int c = 0; c < n; ++c) {
+    const int s = bounds[2 * c], e = bounds[2 * c + 1], par = parents[c];
+    if (s != expect || e < s || par < -1 || par >= c) return TT_ERR_INVALID_ARG;
+    expect = e;
+    p.start[c] = s; p.len[c] = e - s; p.parent[c] = par;
+    p.depth[c] = par < 0 ? 0 : p.depth[par] + 1;
+    p.loff[c] = p.ll_total;
+    p.ll_total += (long long)(e - s) * (e - s);
+    p.max_len = std::max(p.max_len, e - s);
+    p.max_depth = std::max(p.max_depth, p.depth[c]);
+  }
+  if (expect != S) return TT_ERR_INVALID_ARG;
+  p.levels.assign(p.max_depth + 1, {});
+  for (int c = 0; c < n; ++c) p.levels[p.depth[c]].push_back(c);
+  p.child_ptr.assign(n + 1, 0);
+  for (int c = 0; c < n; ++c) if (p.parent[c] >= 0) p.child_ptr[p.parent[c] + 1]++;
+  for (int c = 0; c < n; ++c) p.child_ptr[c + 1] += p.child_ptr[c];
+  p.child_idx.resize(p.child_ptr[n]);
+  std::vector<int> fill(p.child_ptr.begin(), p.child_ptr.end() - 1);
+  for (int c = 0; c < n; ++c) {
+    if (p.parent[c] >= 0) p.child_idx[fill[p.parent[c]]++] = c;
+    else p.roots.push_back(c);
+  }
+  return TT_OK;
+}
+
+// Bump allocator over the caller's workspace (256-byte aligned pieces).
+struct Arena {
+  char* base;
+  int64_t cap, used = 0;
+  bool sizing;
+  template <typename T>
+  T* get(long long n) {
+    const int64_t bytes = ((int64_t)std::max<long long>(n, 1) * (int64_t)sizeof(T) + 255) / 256 * 256;
+    T* r = sizing ? nullptr : reinterpret_cast<T*>(base + used);
+    used += bytes;
+    return r;
+  }
+};
+
+// All device buffers of one forward (+ backward) run.
+struct Bufs {
+  float *gam, *gl_tok, *gl, *Q, *K, *Vb, *Kb, *Kbg, *Qg, *Kd, *U, *W, *T1, *Vn, *O;
+  float *KK, *QK, *Am, *Aqk, *states;
+  // backward
+  float *dO, *dVn, *dQg, *dKd, *dW, *dT, *dA, *dAqk, *dDD, *X, *dVb, *dKbg, *dKb, *dQ, *dK;
+  float *dSo, *dSi, *dgl, *dgam, *kd_dot, *dq_h, *dk_h;
+  int *d_start, *d_len, *d_parent, *d_child_ptr, *d_child_idx, *d_roots, *d_level_nodes;
+  long long* d_loff;
+  SegDesc* d_desc;
+};
+
+// Descriptor sets: built on the host in one vector, copied once.
+struct DescSet { int first, count; };
+
+struct Builder {
+  const Plan& p;
+  std::vector<SegDesc> all;
+  explicit Builder(const Plan& pl) : p(pl) {}
+  DescSet add(const std::vector<SegDesc>& v) {
+    DescSet d{(int)all.size(), (int)v.size()};
+    all.insert(all.end(), v.begin(), v.end());
+    return d;
+  }
+};
+
+SegDesc desc(int M, int N, int K, long long ao, long long ars, long long acs, long long bo,
+             long long brs, long long bcs, long long co, long long crs, long long ccs) {
+  SegDesc d;
+  d.M = M; d.N = N; d.K = K; d.pad = 0;
+  d.a_off = ao; d.a_rs = ars; d.a_cs = acs;
+  d.b_off = bo; d.b_rs = brs; d.b_cs = bcs;
+  d.c_off = co; d.c_rs = crs; d.c_cs = ccs;
+  return d;
+}
+
+void launch_gemm(const SegDesc* d_desc, DescSet ds, int max_m, int max_n, int H, const float* A,
+                 long long a_hs, const float* B, long long b_hs, float* C, long long c_hs,
+                 float alpha, float beta, cudaStream_t st) {
+  if (ds.count == 0 || max_m <= 0 || max_n <= 0) return;
+  const int tiles = ((max_m + kBM - 1) / kBM) * ((max_n + kBN - 1) / kBN);
+  dim3 grid(tiles, ds.count, H);
+  seg_gemm<<<grid, 256, 0, st>>>(d_desc + ds.first, A, a_hs, B, b_hs, C, c_hs, alpha, beta);
+  tt_count_launches(1);
+}
+
+template <typename T>
+int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_, const void* v_,
+        const float* g, const float* beta, const float* init, int l2norm, void* out_,
+        float* last_state, const void* dout_, const float* dlast, void* dq_, void* dk_,
+        void* dv_, float* dg, float* dbeta, float* dinit, cudaStream_t st) {
+  const T* q = (const T*)q_;
+  const T* k = (const T*)k_;
+  const T* v = (const T*)v_;
+  const int S = p.S, H = p.H, Dk = p.Dk, Dv = p.Dv, n = p.n, Hk = p.Hk;
+  const long long vk = (long long)S * Dk, vv = (long long)S * Dv;   // head strides
+  const long long llh = p.ll_total;
+  const int DkDv = Dk * Dv;
+  const long long sh = (long long)H * DkDv;                           // one state set
+  Bufs b{};
+  b.gam = ar.get<float>((long long)H * S);
+  b.gl_tok = ar.get<float>((long long)H * S);
+  b.gl = ar.get<float>((long long)H * n);
+  b.Q = ar.get<float>(H * vk); b.K = ar.get<float>(H * vk); b.Vb = ar.get<float>(H * vv);
+  b.Kb = ar.get<float>(H * vk); b.Kbg = ar.get<float>(H * vk); b.Qg = ar.get<float>(H * vk);
+  b.Kd = ar.get<float>(H * vk); b.U = ar.get<float>(H * vv); b.W = ar.get<float>(H * vk);
+  b.T1 = ar.get<float>(H * std::max(vk, vv)); b.Vn = ar.get<float>(H * vv);
+  b.O = ar.get<float>(H * vv);
+  b.KK = ar.get<float>(H * llh); b.QK = ar.get<float>(H * llh);
+  b.Am = ar.get<float>(H * llh); b.Aqk = ar.get<float>(H * llh);
+  b.states = ar.get<float>((long long)(n + 1) * sh);
+  if (backward) {
+    b.dO = ar.get<float>(H * vv); b.dVn = ar.get<float>(H * vv); b.dQg = ar.get<float>(H * vk);
+    b.dKd = ar.get<float>(H * vk); b.dW = ar.get<float>(H * vk);
+    b.dT = ar.get<float>(H * llh); b.dA = ar.get<float>(H * llh); b.dAqk = ar.get<float>(H * llh);
+    b.dDD = ar.get<float>(H * llh); b.X = ar.get<float>(H * llh);
+    b.dVb = ar.get<float>(H * vv); b.dKbg = ar.get<float>(H * vk); b.dKb = ar.get<float>(H * vk);
+    b.dQ = ar.get<float>(H * vk); b.dK = ar.get<float>(H * vk);
+    b.dSo = ar.get<float>((long long)n * sh); b.dSi = ar.get<float>((long long)n * sh);
+    b.dgl = ar.get<float>((long long)H * n); b.dgam = ar.get<float>((long long)H * S);
+    b.kd_dot = ar.get<float>((long long)H * S);
+    b.dq_h = ar.get<float>(H * vk); b.dk_h = ar.get<float>(H * vk);
+  }
+  // metadata + descriptors
+  Builder bd(p);
+  std::vector<SegDesc> v_kk, v_qk, v_av, v_ak, v_ws, v_qs, v_aqv, v_kdv;
+  std::vector<std::vector<SegDesc>> lv_ws(p.levels.size()), lv_qs(p.levels.size()),
+      lv_aqv(p.levels.size()), lv_kdv(p.levels.size());
+  for (int c = 0; c < n; ++c) {
+    const int L = p.len[c];
+    const long long tk = (long long)p.start[c] * Dk, tv = (long long)p.start[c] * Dv;
+    const long long lo = p.loff[c];
+    // KK = Kb K^T, QK = Q K^T : [L x L], K = Dk
+    v_kk.push_back(desc(L, L, Dk, tk, Dk, 1, tk, 1, Dk, lo, L, 1));
+    // A * X for X = [L x Dv] (U) / [L x Dk] (W)
+    v_av.push_back(desc(L, Dv, L, lo, L, 1, tv, Dv, 1, tv, Dv, 1));
+    v_ak.push_back(desc(L, Dk, L, lo, L, 1, tk, Dk, 1, tk, Dk, 1));
+  }
+  const long long st_off = sh;   // states[c+1] offset base (per-head stride added by kernel)
+  for (size_t d = 0; d < p.levels.size(); ++d) {
+    for (int c : p.levels[d]) {
+      const int L = p.len[c];
+      const long long tk = (long long)p.start[c] * Dk, tv = (long long)p.start[c] * Dv;
+      const long long sin = (long long)(p.parent[c] + 1) * st_off;
+      const long long sout = (long long)(c + 1) * st_off;
+      // Vn -= W S_in : [L x Dv] = [L x Dk][Dk x Dv]
+      lv_ws[d].push_back(desc(L, Dv, Dk, tk, Dk, 1, sin, Dv, 1, tv, Dv, 1));
+      // O = Qg S_in
+      lv_qs[d].push_back(desc(L, Dv, Dk, tk, Dk, 1, sin, Dv, 1, tv, Dv, 1));
+      // O += Aqk Vn
+      lv_aqv[d].push_back(desc(L, Dv, L, p.loff[c], L, 1, tv, Dv, 1, tv, Dv, 1));
+      // S_out = Kd^T Vn : [Dk x Dv] = [Dk x L][L x Dv]
+      lv_kdv[d].push_back(desc(Dk, Dv, L, tk, 1, Dk, tv, Dv, 1, sout, Dv, 1));
+    }
+  }
+  DescSet ds_kk = bd.add(v_kk), ds_av = bd.add(v_av), ds_ak = bd.add(v_ak);
+  std::vector<DescSet> ds_ws, ds_qs, ds_aqv, ds_kdv;
+  for (size_t d = 0; d < p.levels.size(); ++d) {
+    ds_ws.push_back(bd.add(lv_ws[d]));
+    ds_qs.push_back(bd.add(lv_qs[d]));
+    ds_aqv.push_back(bd.add(lv_aqv[d]));
+    ds_kdv.push_back(bd.add(lv_kdv[d]));
+  }
+  // backward descriptors
+  std::vector<std::vector<SegDesc>> lb_dvn1(p.levels.size()), lb_dvn2(p.levels.size()),
+      lb_dsi1(p.levels.size()), lb_dsi2(p.levels.size());
+  std::vector<SegDesc> b_dqg, b_dkd, b_dw, b_daqk, b_dt1, b_dt2, b_x1, b_x2, b_tvt, b_tvt2,
+      b_tkt, b_tkt2, b_gk, b_gtk, b_fk, b_ftq;
+  if (backward) {
+    for (size_t d = 0; d < p.levels.size(); ++d) {
+      for (int c : p.levels[d]) {
+        const int L = p.len[c];
+        const long long tk = (long long)p.start[c] * Dk, tv = (long long)p.start[c] * Dv;
+        const long long lo = p.loff[c];
+        const long long so = (long long)c * st_off;
+        // dVn = Aqk^T dO : [L x Dv] = [L x L]^T [L x Dv]
+        lb_dvn1[d].push_back(desc(L, Dv, L, lo, 1, L, tv, Dv, 1, tv, Dv, 1));
+        // dVn += Kd dSo : [L x Dv] = [L x Dk][Dk x Dv]
+        lb_dvn2[d].push_back(desc(L, Dv, Dk, tk, Dk, 1, so, Dv, 1, tv, Dv, 1));
+        // dSi = Qg^T dO : [Dk x Dv] = [Dk x L][L x Dv]
+        lb_dsi1[d].push_back(desc(Dk, Dv, L, tk, 1, Dk, tv, Dv, 1, so, Dv, 1));
+        // dSi -= W^T dVn
+        lb_dsi2[d].push_back(desc(Dk, Dv, L, tk, 1, Dk, tv, Dv, 1, so, Dv, 1));
+      }
+    }
+    for (int c = 0; c < n; ++c) {
+      const int L = p.len[c];
+      const long long tk = (long long)p.start[c] * Dk, tv = (long long)p.start[c] * Dv;
+      const long long lo = p.loff[c];
+      const long long sin = (long long)(p.parent[c] + 1) * st_off;
+      const long long so = (long long)c * st_off;
+      // dQg = dO S_in^T : [L x Dk] = [L x Dv][Dv x Dk]
+      b_dqg.push_back(desc(L, Dk, Dv, tv, Dv, 1, sin, 1, Dv, tk, Dk, 1));
+      // dKd = Vn dSo^T
+      b_dkd.push_back(desc(L, Dk, Dv, tv, Dv, 1, so, 1, Dv, tk, Dk, 1));
+      // dW = -dVn S_in^T
+      b_dw.push_back(desc(L, Dk, Dv, tv, Dv, 1, sin, 1, Dv, tk, Dk, 1));
+      // dAqk = dO Vn^T : [L x L]
+      b_daqk.push_back(desc(L, L, Dv, tv, Dv, 1, tv, 1, Dv, lo, L, 1));
+      // dT = dVn Vb^T + dW Kbg^T
+      b_dt1.push_back(desc(L, L, Dv, tv, Dv, 1, tv, 1, Dv, lo, L, 1));
+      b_dt2.push_back(desc(L, L, Dk, tk, Dk, 1, tk, 1, Dk, lo, L, 1));
+      // X = dT A^T : [L x L] = [L x L][L x L]^T ; X += A^T dT
+      b_x1.push_back(desc(L, L, L, lo, L, 1, lo, 1, L, lo, L, 1));
+      b_x2.push_back(desc(L, L, L, lo, 1, L, lo, L, 1, lo, L, 1));
+      // T^T y = y + A^T y + A^T (A^T y)  for y = dVn [L x Dv] and dW [L x Dk]
+      b_tvt.push_back(desc(L, Dv, L, lo, 1, L, tv, Dv, 1, tv, Dv, 1));
+      b_tkt.push_back(desc(L, Dk, L, lo, 1, L, tk, Dk, 1, tk, Dk, 1));
+      // G K (dKb += G K), G^T Kb (dK += G^T Kb), F K (dQ += F K), F^T Q (dK += F^T Q)
+      b_gk.push_back(desc(L, Dk, L, lo, L, 1, tk, Dk, 1, tk, Dk, 1));
+      b_gtk.push_back(desc(L, Dk, L, lo, 1, L, tk, Dk, 1, tk, Dk, 1));
+    }
+  }
+  DescSet ds_dqg = bd.add(b_dqg), ds_dkd = bd.add(b_dkd), ds_dw = bd.add(b_dw),
+          ds_daqk = bd.add(b_daqk), ds_dt1 = bd.add(b_dt1), ds_dt2 = bd.add(b_dt2),
+          ds_x1 = bd.add(b_x1), ds_x2 = bd.add(b_x2), ds_tvt = bd.add(b_tvt),
+          ds_tkt = bd.add(b_tkt), ds_gk = bd.add(b_gk), ds_gtk = bd.add(b_gtk);
+  std::vector<DescSet> ds_dvn1, ds_dvn2, ds_dsi1, ds_dsi2;
+  for (size_t d = 0; d < p.levels.size(); ++d) {
+    ds_dvn1.push_back(bd.add(lb_dvn1[d]));
+    ds_dvn2.push_back(bd.add(lb_dvn2[d]));
+    ds_dsi1.push_back(bd.add(lb_dsi1[d]));
+    ds_dsi2.push_back(bd.add(lb_dsi2[d]));
+  }
+  // int metadata
+  std::vector<int> level_nodes, level_first;
+  for (auto& l : p.levels) {
+    level_first.push_back((int)level_nodes.size());
+    level_nodes.insert(level_nodes.end(), l.begin(), l.end());
+  }
+  b.d_start = ar.get<int>(n); b.d_len = ar.get<int>(n); b.d_parent = ar.get<int>(n);
+  b.d_child_ptr = ar.get<int>(n + 1); b.d_child_idx = ar.get<int>(std::max<size_t>(1, p.child_idx.size()));
+  b.d_roots = ar.get<int>(std::max<size_t>(1, p.roots.size()));
+  b.d_level_nodes = ar.get<int>(std::max<size_t>(1, level_nodes.size()));
+  b.d_loff = ar.get<long long>(n);
+  b.d_desc = ar.get<SegDesc>((long long)bd.all.size());
+  if (ar.sizing) return TT_OK;
+  if (ar.used > ar.cap) return TT_ERR_WORKSPACE;
+  auto h2d = [&](void* dst, const void* src, size_t bytes) -> int {
+    if (bytes == 0) return TT_OK;
+    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, st) == cudaSuccess ? TT_OK
+                                                                                        : TT_ERR_CUDA;
+  };
+  int rc = TT_OK;
+  rc |= h2d(b.d_start, p.start.data(), n * 4);
+  rc |= h2d(b.d_len, p.len.data(), n * 4);
+  rc |= h2d(b.d_parent, p.parent.data(), n * 4);
+  rc |= h2d(b.d_child_ptr, p.child_ptr.data(), (n + 1) * 4);
+  rc |= h2d(b.d_child_idx, p.child_idx.data(), p.child_idx.size() * 4);
+  rc |= h2d(b.d_roots, p.roots.data(), p.roots.size() * 4);
+  rc |= h2d(b.d_level_nodes, level_nodes.data(), level_nodes.size() * 4);
+  rc |= h2d(b.d_loff, p.loff.data(), n * 8);
+  rc |= h2d(b.d_desc, bd.all.data(), bd.all.size() * sizeof(SegDesc));
+  if (rc != TT_OK) return TT_ERR_CUDA;
+
+  const int max_l = p.max_len;
+  const float q_scale = 1.f / sqrtf((float)Dk);
+  auto blocks = [](long long nel) { return (unsigned)((nel + 255) / 256); };
+  int launches = 0;
+  // ---------------------------------------------------------------- forward
+  node_cumsum<<<dim3((n + 127) / 128, H), 128, 0, st>>>(S, H, n, b.d_start, b.d_len, g, b.gam,
+                                                        b.gl_tok, b.gl);
+  prep_tokens<T><<<dim3(S, H), 128, 0, st>>>(S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok,
+                                             l2norm, q_scale, b.Q, b.K, b.Vb, b.Kb, b.Kbg, b.Qg,
+                                             b.Kd);
+  launches += 2;
+  launch_gemm(b.d_desc, ds_kk, max_l, max_l, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, ds_kk, max_l, max_l, H, b.Q, vk, b.K, vk, b.QK, llh, 1.f, 0.f, st);
+  decay_masks<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.gam,
+                                                 b.KK, b.QK, b.Am, b.Aqk);
+  ++launches;
+  // U = Vb + A Vb + A (A Vb);  W = Kbg + A Kbg + A (A Kbg)
+  launch_gemm(b.d_desc, ds_av, max_l, Dv, H, b.Am, llh, b.Vb, vv, b.T1, vv, 1.f, 0.f, st);
+  add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.Vb, b.T1, b.U);
+  launch_gemm(b.d_desc, ds_av, max_l, Dv, H, b.Am, llh, b.T1, vv, b.U, vv, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, ds_ak, max_l, Dk, H, b.Am, llh, b.Kbg, vk, b.T1, vk, 1.f, 0.f, st);
+  add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.Kbg, b.T1, b.W);
+  launch_gemm(b.d_desc, ds_ak, max_l, Dk, H, b.Am, llh, b.T1, vk, b.W, vk, 1.f, 1.f, st);
+  copy_array<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.U, b.Vn);
+  init_state<<<blocks(sh), 256, 0, st>>>(sh, init, b.states);
+  launches += 4;
+  for (size_t d = 0; d < p.levels.size(); ++d) {
+    const int cnt = (int)p.levels[d].size();
+    // states are [n+1][H][Dk][Dv]: per-head stride DkDv, segment offsets cover (c+1)*H*DkDv
+    launch_gemm(b.d_desc, ds_ws[d], max_l, Dv, H, b.W, vk, b.states, DkDv, b.Vn, vv, -1.f, 1.f, st);
+    launch_gemm(b.d_desc, ds_qs[d], max_l, Dv, H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, ds_aqv[d], max_l, Dv, H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f, st);
+    launch_gemm(b.d_desc, ds_kdv[d], Dk, Dv, H, b.Kd, vk, b.Vn, vv, b.states, DkDv, 1.f, 0.f, st);
+    state_decay_add<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
+        H, DkDv, n, b.d_level_nodes + level_first[d], b.d_parent, b.gl, b.states);
+    ++launches;
+  }
+  if (!backward) {
+    store_out<T><<<dim3(S, H), 128, 0, st>>>(S, H, Dv, b.O, (T*)out_);
+    ++launches;
+    if (last_state) {
+      TT_CUDA_OK(cudaMemcpyAsync(last_state, b.states + (long long)n * sh, sh * 4,
+                                 cudaMemcpyDeviceToDevice, st));
+    }
+    tt_count_launches(launches);
+    return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
+  }
+  // ---------------------------------------------------------------- backward
+  load_dout<T><<<dim3(S, H), 128, 0, st>>>(S, H, Dv, (const T*)dout_, b.dO);
+  ++launches;
+  for (int d = (int)p.levels.size() - 1; d >= 0; --d) {
+    const int cnt = (int)p.levels[d].size();
+    gather_dstate<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
+        H, DkDv, n, b.d_level_nodes + level_first[d], b.d_child_ptr, b.d_child_idx, b.dSi, dlast,
+        b.dSo);
+    launch_gemm(b.d_desc, ds_dvn1[d], max_l, Dv, H, b.Aqk, llh, b.dO, vv, b.dVn, vv, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, ds_dvn2[d], max_l, Dv, H, b.Kd, vk, b.dSo, DkDv, b.dVn, vv, 1.f, 1.f, st);
+    launch_gemm(b.d_desc, ds_dsi1[d], Dk, Dv, H, b.Qg, vk, b.dO, vv, b.dSi, DkDv, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, ds_dsi2[d], Dk, Dv, H, b.W, vk, b.dVn, vv, b.dSi, DkDv, -1.f, 1.f, st);
+    dstate_decay<<<dim3(cnt, H), 256, 0, st>>>(H, DkDv, n, b.d_level_nodes + level_first[d],
+                                               b.d_parent, b.gl, b.states, b.dSo, b.dSi, b.dgl);
+    launches += 2;
+  }
+  // per-node gradients, no more dependencies between nodes
+  launch_gemm(b.d_desc, ds_dqg, max_l, Dk, H, b.dO, vv, b.states, DkDv, b.dQg, vk, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, ds_dkd, max_l, Dk, H, b.Vn, vv, b.dSo, DkDv, b.dKd, vk, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, ds_dw, max_l, Dk, H, b.dVn, vv, b.states, DkDv, b.dW, vk, -1.f, 0.f, st);
+  launch_gemm(b.d_desc, ds_daqk, max_l, max_l, H, b.dO, vv, b.Vn, vv, b.dAqk, llh, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, ds_dt1, max_l, max_l, H, b.dVn, vv, b.Vb, vv, b.dT, llh, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, ds_dt2, max_l, max_l, H, b.dW, vk, b.Kbg, vk, b.dT, llh, 1.f, 1.f, st);
+  // dA = dT + dT A^T + A^T dT  (masked in grad_masks)
+  copy_array<<<blocks(H * llh), 256, 0, st>>>(H * llh, b.dT, b.dA);
+  launch_gemm(b.d_desc, ds_x1, max_l, max_l, H, b.dT, llh, b.Am, llh, b.dA, llh, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, ds_x2, max_l, max_l, H, b.Am, llh, b.dT, llh, b.dA, llh, 1.f, 1.f, st);
+  // dVb = T^T dVn = dVn + A^T dVn + A^T (A^T dVn);  dKbg = T^T dW
+  launch_gemm(b.d_desc, ds_tvt, max_l, Dv, H, b.Am, llh, b.dVn, vv, b.T1, vv, 1.f, 0.f, st);
+  add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.dVn, b.T1, b.dVb);
+  launch_gemm(b.d_desc, ds_tvt, max_l, Dv, H, b.Am, llh, b.T1, vv, b.dVb, vv, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, ds_tkt, max_l, Dk, H, b.Am, llh, b.dW, vk, b.T1, vk, 1.f, 0.f, st);
+  add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.dW, b.T1, b.dKbg);
+  launch_gemm(b.d_desc, ds_tkt, max_l, Dk, H, b.Am, llh, b.T1, vk, b.dKbg, vk, 1.f, 1.f, st);
+  launches += 3;
+  // masks: dA -> G = -dA*D, dAqk -> F = dAqk*D, dDD
+  TT_CUDA_OK(cudaMemsetAsync(b.dgam, 0, (size_t)H * S * 4, st));
+  grad_masks<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.gam,
+                                                b.KK, b.QK, b.dA, b.dAqk, b.dDD);
+  ddd_rowcol<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.dDD,
+                                                b.dgam);
+  launches += 2;
+  // dKb = G K ; dK = G^T Kb + F^T Q ; dQ = F K
+  launch_gemm(b.d_desc, ds_gk, max_l, Dk, H, b.dA, llh, b.K, vk, b.dKb, vk, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, ds_gtk, max_l, Dk, H, b.dA, llh, b.Kb, vk, b.dK, vk, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, ds_gtk, max_l, Dk, H, b.dAqk, llh, b.Q, vk, b.dK, vk, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, ds_gk, max_l, Dk, H, b.dAqk, llh, b.K, vk, b.dQ, vk, 1.f, 0.f, st);
+  kd_dot_kernel<<<dim3(S, H), 128, 0, st>>>(S, Dk, b.Kd, b.dKd, b.kd_dot);
+  assemble_token_grads<T><<<dim3(S, H), 128, 0, st>>>(
+      S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok, l2norm, q_scale, b.dQ, b.dQg, b.dK,
+      b.dKd, b.dKb, b.dKbg, b.dVb, b.dgam, b.dq_h, b.dk_h, dbeta, (T*)dv_);
+  node_dg<<<dim3((n + 127) / 128, H), 128, 0, st>>>(S, H, n, b.d_start, b.d_len, b.kd_dot, b.dgl,
+                                                    b.dgam, dg);
+  reduce_gqa<T><<<dim3(S, Hk), 128, 0, st>>>(S, Hk, H, Dk, b.dq_h, (T*)dq_);
+  reduce_gqa<T><<<dim3(S, Hk), 128, 0, st>>>(S, Hk, H, Dk, b.dk_h, (T*)dk_);
+  launches += 5;
+  if (dinit) {
+    dinit_kernel<<<blocks(sh), 256, 0, st>>>(H, DkDv, (int)p.roots.size(), b.d_roots, b.dSi, dinit);
+    ++launches;
+  }
+  tt_count_launches(launches);
+  return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
+}
+
+template <typename Fn>
+int dispatch(int dtype, Fn fn) {
+  switch (dtype) {
+    case TT_F32: return fn(float());
+    case TT_BF16: return fn(__nv_bfloat16());
+    case TT_F16: return fn(__half());
+    default: return TT_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace
+}  // namespace gdn
+}  // namespace tt
+
+using tt::gdn::Arena;
+using tt::gdn::Plan;
+
+extern "C" int64_t tt_gdn_tree_workspace_size(int32_t S, int32_t H, int32_t Dk, int32_t Dv,
+                                              int32_t n_nodes, const int32_t* bounds,
+                                              int backward) {
+  if (S < 0 || H <= 0 || Dk <= 0 || Dv <= 0 || n_nodes < 0 || (n_nodes > 0 && !bounds)) return -1;
+  std::vector<int32_t> parents(n_nodes, -1);
+  Plan p;
+  if (tt::gdn::make_plan(p, S, H, 1, Dk, Dv, n_nodes, bounds, parents.data()) != TT_OK) return -1;
+  Arena ar{nullptr, 0, 0, true};
+  tt::gdn::run<float>(p, backward != 0, ar, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                      0, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                      nullptr, nullptr, nullptr);
+  // every level holds at least one node; descriptor count does not depend on
+  // the parents beyond the level split, so size it for the worst case (a chain)
+  return ar.used + (int64_t)(n_nodes + 1) * 4 * (int64_t)sizeof(tt::gdn::SegDesc) * 2 + 4096;
+}
+
+static int gdn_check(int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv, int32_t n_nodes,
+                     const int32_t* bounds, const int32_t* parents) {
+  if (S < 0 || Hk <= 0 || H <= 0 || H % Hk || Dk <= 0 || Dv <= 0 || Dk > 256 || Dv > 256 ||
+      n_nodes < 0 || (n_nodes > 0 && (!bounds || !parents)))
+    return TT_ERR_INVALID_ARG;
+  return TT_OK;
+}
+
+extern "C" int tt_gdn_tree_fwd(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
+                               const void* q, const void* k, const void* v, const float* g,
+                               const float* beta, int32_t n_nodes, const int32_t* bounds,
+                               const int32_t* parents, const float* initial_state,
+                               int use_qk_l2norm, void* out, float* last_state, void* workspace,
+                               int64_t workspace_bytes, void* stream) {
+  int rc = gdn_check(S, Hk, H, Dk, Dv, n_nodes, bounds, parents);
+  if (rc != TT_OK) return rc;
+  if (S == 0 || n_nodes == 0) return TT_OK;
+  Plan p;
+  if ((rc = tt::gdn::make_plan(p, S, H, Hk, Dk, Dv, n_nodes, bounds, parents)) != TT_OK) return rc;
+  Arena ar{(char*)workspace, workspace_bytes, 0, false};
+  return tt::gdn::dispatch(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    return tt::gdn::run<T>(p, false, ar, q, k, v, g, beta, initial_state, use_qk_l2norm, out,
+                           last_state, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                           nullptr, nullptr, (cudaStream_t)stream);
+  });
+}
+
+extern "C" int tt_gdn_tree_bwd(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
+                               const void* q, const void* k, const void* v, const float* g,
+                               const float* beta, int32_t n_nodes, const int32_t* bounds,
+                               const int32_t* parents, const float* initial_state,
+                               int use_qk_l2norm, const void* dout, const float* dlast, void* dq,
+                               void* dk, void* dv, float* dg, float* dbeta, float* dinit,
+                               void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = gdn_check(S, Hk, H, Dk, Dv, n_nodes, bounds, parents);
+  if (rc != TT_OK) return rc;
+  if (S == 0 || n_nodes == 0) return TT_OK;
+  Plan p;
+  if ((rc = tt::gdn::make_plan(p, S, H, Hk, Dk, Dv, n_nodes, bounds, parents)) != TT_OK) return rc;
+  Arena ar{(char*)workspace, workspace_bytes, 0, false};
+  return tt::gdn::dispatch(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    return tt::gdn::run<T>(p, true, ar, q, k, v, g, beta, initial_state, use_qk_l2norm, nullptr,
+                           nullptr, dout, dlast, dq, dk, dv, dg, dbeta, dinit,
+                           (cudaStream_t)stream);
+  });
+}

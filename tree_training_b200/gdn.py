@@ -1,0 +1,272 @@
+"""Tree gated delta rule and tree-correct conv as torch custom ops.
+
+Drop-ins (same signatures and return conventions as the reference):
+
+* ``torch_chunk_gated_delta_rule_tree_varlen`` (tree_dfs_ssm.py:38-156)
+* ``_tree_correct_conv_varlen`` (tree_dfs_ssm.py:285-348)
+
+Both run in the C-ABI library (``tt_gdn_tree_fwd/_bwd``, ``tt_tree_conv_fwd/
+_bwd``) with fp32 arithmetic inside; there is no PyTorch fallback.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from . import _lib
+from .attention import _DTYPES, _stream_ptr
+
+
+def _tree_arrays(chunk_boundaries, chunk_parent_map) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bounds [n, 2] / parents [n] as int32 CPU tensors (lists, arrays or tensors)."""
+    if isinstance(chunk_boundaries, torch.Tensor):
+        b = chunk_boundaries.detach().to("cpu", torch.int32).reshape(-1, 2).contiguous()
+    else:
+        b = torch.as_tensor(np.asarray(chunk_boundaries, dtype=np.int32).reshape(-1, 2))
+    if isinstance(chunk_parent_map, torch.Tensor):
+        p = chunk_parent_map.detach().to("cpu", torch.int32).reshape(-1).contiguous()
+    else:
+        p = torch.as_tensor(np.asarray(chunk_parent_map, dtype=np.int32).reshape(-1))
+    return b, p
+
+
+# -----------------------------------------------------------------------------
+# GDN
+# -----------------------------------------------------------------------------
+
+def _ws(S, H, Dk, Dv, bounds: torch.Tensor, backward: bool, device) -> Tuple[torch.Tensor, int]:
+    n = int(bounds.shape[0])
+    nbytes = int(_lib.lib().tt_gdn_tree_workspace_size(S, H, Dk, Dv, n, bounds.data_ptr(),
+                                                       int(backward)))
+    if nbytes < 0:
+        raise ValueError("tree GDN: invalid chunk boundaries")
+    return torch.empty(max(nbytes, 16), dtype=torch.uint8, device=device), nbytes
+
+
+@torch.library.custom_op("tt_b200::gdn_tree_fwd", mutates_args=())
+def _gdn_fwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
+                beta: torch.Tensor, bounds: torch.Tensor, parents: torch.Tensor,
+                init: torch.Tensor, has_init: bool, l2norm: bool,
+                want_last: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+    """q/k [S, Hk, Dk], v [S, H, Dv] (one dtype), g/beta fp32 [S, H],
+    bounds int32 [n, 2], parents int32 [n] (CPU) -> out [S, H, Dv], last fp32
+    [H, Dk, Dv] (zeros-shaped when not requested)."""
+    S, Hk, Dk = q.shape
+    H, Dv = v.shape[1], v.shape[2]
+    out = torch.empty((S, H, Dv), dtype=q.dtype, device=q.device)
+    last = torch.empty((H, Dk, Dv) if want_last else (0,), dtype=torch.float32, device=q.device)
+    ws, nbytes = _ws(S, H, Dk, Dv, bounds, False, q.device)
+    _lib.call("tt_gdn_tree_fwd", _DTYPES[q.dtype], S, Hk, H, Dk, Dv, q.data_ptr(), k.data_ptr(),
+              v.data_ptr(), g.data_ptr(), beta.data_ptr(), int(bounds.shape[0]),
+              bounds.data_ptr(), parents.data_ptr(), init.data_ptr() if has_init else None,
+              int(l2norm), out.data_ptr(), last.data_ptr() if want_last else None,
+              ws.data_ptr(), nbytes, _stream_ptr(q.device))
+    return out, last
+
+
+@_gdn_fwd_op.register_fake
+def _(q, k, v, g, beta, bounds, parents, init, has_init, l2norm, want_last):
+    S, Hk, Dk = q.shape
+    H, Dv = v.shape[1], v.shape[2]
+    return (q.new_empty((S, H, Dv)),
+            q.new_empty((H, Dk, Dv) if want_last else (0,), dtype=torch.float32))
+
+
+@torch.library.custom_op("tt_b200::gdn_tree_bwd", mutates_args=())
+def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: torch.Tensor,
+                k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                bounds: torch.Tensor, parents: torch.Tensor, init: torch.Tensor, has_init: bool,
+                l2norm: bool) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                       torch.Tensor, torch.Tensor]:
+    S, Hk, Dk = q.shape
+    H, Dv = v.shape[1], v.shape[2]
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dg = torch.empty((S, H), dtype=torch.float32, device=q.device)
+    db = torch.empty((S, H), dtype=torch.float32, device=q.device)
+    dinit = torch.zeros((H, Dk, Dv) if has_init else (0,), dtype=torch.float32, device=q.device)
+    ws, nbytes = _ws(S, H, Dk, Dv, bounds, True, q.device)
+    _lib.call("tt_gdn_tree_bwd", _DTYPES[q.dtype], S, Hk, H, Dk, Dv, q.data_ptr(), k.data_ptr(),
+              v.data_ptr(), g.data_ptr(), beta.data_ptr(), int(bounds.shape[0]),
+              bounds.data_ptr(), parents.data_ptr(), init.data_ptr() if has_init else None,
+              int(l2norm), dout.contiguous().data_ptr(),
+              dlast.contiguous().data_ptr() if has_dlast else None, dq.data_ptr(),
+              dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), db.data_ptr(),
+              dinit.data_ptr() if has_init else None, ws.data_ptr(), nbytes,
+              _stream_ptr(q.device))
+    return dq, dk, dv, dg, db, dinit
+
+
+@_gdn_bwd_op.register_fake
+def _(dout, dlast, has_dlast, q, k, v, g, beta, bounds, parents, init, has_init, l2norm):
+    S, Hk, Dk = q.shape
+    H, Dv = v.shape[1], v.shape[2]
+    f = lambda *s: q.new_empty(s, dtype=torch.float32)
+    return (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), f(S, H), f(S, H),
+            f(H, Dk, Dv) if has_init else f(0))
+
+
+def _gdn_setup(ctx, inputs, output):
+    q, k, v, g, beta, bounds, parents, init, has_init, l2norm, want_last = inputs
+    ctx.save_for_backward(q, k, v, g, beta, bounds, parents, init)
+    ctx.has_init, ctx.l2norm, ctx.want_last = has_init, l2norm, want_last
+
+
+def _gdn_backward(ctx, dout, dlast):
+    q, k, v, g, beta, bounds, parents, init = ctx.saved_tensors
+    has_dlast = ctx.want_last and dlast is not None and dlast.numel() > 0
+    if dout is None:
+        dout = torch.zeros((q.shape[0], v.shape[1], v.shape[2]), dtype=q.dtype, device=q.device)
+    dq, dk, dv, dg, db, dinit = _gdn_bwd_op(
+        dout, dlast if has_dlast else dout.new_empty(0, dtype=torch.float32), bool(has_dlast),
+        q, k, v, g, beta, bounds, parents, init, ctx.has_init, ctx.l2norm)
+    return (dq, dk, dv, dg, db, None, None, dinit if ctx.has_init else None, None, None, None)
+
+
+_gdn_fwd_op.register_autograd(_gdn_backward, setup_context=_gdn_setup)
+
+
+def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_boundaries,
+                                             chunk_parent_map, initial_state=None,
+                                             output_final_state=False,
+                                             use_qk_l2norm_in_kernel=False):
+    """Drop-in for tree_dfs_ssm.py:38-156.
+
+    query/key [B, S, Hk, Dk] (Hk == H, or a divisor of H: v-head h then uses
+    k-head h // (H // Hk)), value [B, S, H, Dv], g/beta [B, S, H];
+    chunk_boundaries / chunk_parent_map as lists or tensors.  Returns
+    (core_out [B, S, H, Dv] in query's dtype, last_state [B, H, Dk, Dv] fp32 or
+    None) with gradients for every tensor input."""
+    if query.dtype not in _DTYPES or key.dtype != query.dtype or value.dtype != query.dtype:
+        raise TypeError("tree GDN: query, key, value must share one of float32/bfloat16/float16")
+    if not query.is_cuda:
+        raise RuntimeError("tree GDN: CUDA tensors required (no CPU path)")
+    bounds, parents = _tree_arrays(chunk_boundaries, chunk_parent_map)
+    B = query.shape[0]
+    outs, lasts = [], []
+    for b in range(B):
+        q = query[b].contiguous()
+        k = key[b].contiguous()
+        v = value[b].contiguous()
+        gg = g[b].float().contiguous()
+        bt = beta[b].float().contiguous()
+        has_init = initial_state is not None
+        init = (initial_state[b].float().contiguous() if has_init
+                else q.new_empty(0, dtype=torch.float32))
+        o, last = _gdn_fwd_op(q, k, v, gg, bt, bounds, parents, init, has_init,
+                              bool(use_qk_l2norm_in_kernel), bool(output_final_state))
+        outs.append(o)
+        lasts.append(last)
+    core = torch.stack(outs, 0)
+    last_state = torch.stack(lasts, 0) if output_final_state else None
+    return core, last_state
+
+
+# -----------------------------------------------------------------------------
+# tree conv
+# -----------------------------------------------------------------------------
+
+class TreeConvPlan:
+    """Predecessor / successor tables of one tree for a width-K conv (device)."""
+
+    def __init__(self, bounds: torch.Tensor, parents: torch.Tensor, K: int, device):
+        n = int(bounds.shape[0])
+        S = int(bounds[-1, 1]) if n else 0
+        self.S, self.K = S, K
+        pred = np.zeros((max(S, 1), max(K - 1, 1)), np.int32)
+        _lib.call("tt_conv_predecessors", n, bounds.data_ptr(), parents.data_ptr(), K,
+                  pred.ctypes.data)
+        cap = max(S * max(K - 1, 1), 1)
+        sp = np.zeros(S + 1, np.int32)
+        stok = np.zeros(cap, np.int32)
+        slag = np.zeros(cap, np.int32)
+        _lib.call("tt_conv_successors", S, K, pred.ctypes.data, sp.ctypes.data, stok.ctypes.data,
+                  slag.ctypes.data, cap)
+        self.pred = torch.from_numpy(pred).to(device)
+        self.succ_ptr = torch.from_numpy(sp).to(device)
+        self.succ_tok = torch.from_numpy(stok).to(device)
+        self.succ_lag = torch.from_numpy(slag).to(device)
+
+
+@torch.library.custom_op("tt_b200::tree_conv_fwd", mutates_args=())
+def _conv_fwd_op(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, has_b: bool,
+                 pred: torch.Tensor, sp: torch.Tensor, stok: torch.Tensor,
+                 slag: torch.Tensor) -> torch.Tensor:
+    C, S = x.shape
+    K = w.shape[1]
+    out = torch.empty_like(x)
+    _lib.call("tt_tree_conv_fwd", _DTYPES[x.dtype], C, S, K, x.data_ptr(), w.data_ptr(),
+              b.data_ptr() if has_b else None, pred.data_ptr(), out.data_ptr(),
+              _stream_ptr(x.device))
+    return out
+
+
+@_conv_fwd_op.register_fake
+def _(x, w, b, has_b, pred, sp, stok, slag):
+    return torch.empty_like(x)
+
+
+@torch.library.custom_op("tt_b200::tree_conv_bwd", mutates_args=())
+def _conv_bwd_op(dy: torch.Tensor, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor,
+                 has_b: bool, pred: torch.Tensor, sp: torch.Tensor, stok: torch.Tensor,
+                 slag: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    C, S = x.shape
+    K = w.shape[1]
+    dx = torch.empty_like(x)
+    dw = torch.empty_like(w)
+    db = torch.empty((C,) if has_b else (0,), dtype=torch.float32, device=x.device)
+    _lib.call("tt_tree_conv_bwd", _DTYPES[x.dtype], C, S, K, x.data_ptr(), w.data_ptr(),
+              b.data_ptr() if has_b else None, pred.data_ptr(), sp.data_ptr(), stok.data_ptr(),
+              slag.data_ptr(), dy.contiguous().data_ptr(), dx.data_ptr(), dw.data_ptr(),
+              db.data_ptr() if has_b else None, _stream_ptr(x.device))
+    return dx, dw, db
+
+
+@_conv_bwd_op.register_fake
+def _(dy, x, w, b, has_b, pred, sp, stok, slag):
+    return (torch.empty_like(x), torch.empty_like(w),
+            x.new_empty((x.shape[0],) if has_b else (0,), dtype=torch.float32))
+
+
+def _conv_setup(ctx, inputs, output):
+    x, w, b, has_b, pred, sp, stok, slag = inputs
+    ctx.save_for_backward(x, w, b, pred, sp, stok, slag)
+    ctx.has_b = has_b
+
+
+def _conv_backward(ctx, dy):
+    x, w, b, pred, sp, stok, slag = ctx.saved_tensors
+    dx, dw, db = _conv_bwd_op(dy, x, w, b, ctx.has_b, pred, sp, stok, slag)
+    return dx, dw, (db if ctx.has_b else None), None, None, None, None, None
+
+
+_conv_fwd_op.register_autograd(_conv_backward, setup_context=_conv_setup)
+
+
+def tree_conv(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
+              chunk_boundaries, chunk_parent_map) -> torch.Tensor:
+    """silu(depthwise causal conv over each token's tree path).  x [B, C, S],
+    weight [C, K] (or [C, 1, K] as stored by nn.Conv1d), bias [C] or None."""
+    if not x.is_cuda:
+        raise RuntimeError("tree conv: CUDA tensors required (no CPU path)")
+    if x.dtype not in _DTYPES:
+        raise TypeError("tree conv: float32/bfloat16/float16 input required")
+    w = weight.reshape(weight.shape[0], -1).float().contiguous()
+    bounds, parents = _tree_arrays(chunk_boundaries, chunk_parent_map)
+    plan = TreeConvPlan(bounds, parents, int(w.shape[1]), x.device)
+    has_b = bias is not None
+    b = bias.float().contiguous() if has_b else w.new_empty(0)
+    outs = [_conv_fwd_op(x[i].contiguous(), w, b, has_b, plan.pred, plan.succ_ptr,
+                         plan.succ_tok, plan.succ_lag) for i in range(x.shape[0])]
+    return torch.stack(outs, 0)
+
+
+def _tree_correct_conv_varlen(ssm, mixed_qkv_raw, chunk_boundaries, chunk_parent_map):
+    """Drop-in for tree_dfs_ssm.py:285-348: uses ``ssm.conv1d`` (weight
+    [C, 1, K], optional bias) with SiLU, on [B, C, S]."""
+    act = getattr(ssm, "activation", "silu")
+    if act not in ("silu", "swish"):
+        raise ValueError(f"tree conv implements SiLU only, got activation={act!r}")
+    return tree_conv(mixed_qkv_raw, ssm.conv1d.weight, ssm.conv1d.bias, chunk_boundaries,
+                     chunk_parent_map)
