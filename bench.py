@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--tokens", type=int, default=16384,
                     help="tree token budget (16384 = config 2; smaller for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["attn", "gdn"], default="attn",
+                    help="attn = config 2 tree attention (the headline); gdn = config 4 tree "
+                         "conv + gated delta rule")
     return ap.parse_args()
 
 
@@ -408,10 +411,110 @@ def run_ours(args):
     return 0
 
 
+GDN_HK, GDN_H, GDN_D, GDN_K = 16, 32, 128, 4
+
+
+def gdn_workload(seed: int, tokens: int):
+    """Config 4: random 2-4 branching tree, node lengths U[16,300]."""
+    from tree_training_b200.synthetic import random_branching_tree
+    import tree_training_b200 as tt
+    return tt.build_dfs_tree_info(random_branching_tree(seed, tokens, 16, 300))
+
+
+def gdn_bytes_per_token():
+    """Algorithmic HBM bytes per token of one fwd+bwd step (bf16 in/out, fp32
+    g/beta): conv input read x2 + output write, q/k/v reads, g/beta, core out,
+    and the same again for the gradients."""
+    C = 2 * GDN_HK * GDN_D + GDN_H * GDN_D
+    fwd = C * 2 * 2 + (2 * GDN_HK * GDN_D + GDN_H * GDN_D) * 2 + 2 * GDN_H * 4 + GDN_H * GDN_D * 2
+    return 3 * fwd
+
+
+def run_gdn(args):
+    import tree_training_b200 as tt
+    from tree_training_b200 import _lib
+    from tree_training_b200.gdn import torch_chunk_gated_delta_rule_tree_varlen, tree_conv
+    world, rank, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    init_dist(world, local)
+    info = gdn_workload(args.seed + rank, args.tokens)
+    S = info.N
+    C = 2 * GDN_HK * GDN_D + GDN_H * GDN_D
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = (torch.randn(1, C, S, generator=g, device=dev)).to(torch.bfloat16).requires_grad_(True)
+    w = (torch.randn(C, GDN_K, generator=g, device=dev) * 0.5).requires_grad_(True)
+    a = torch.randn(1, S, GDN_H, generator=g, device=dev)
+    gg = torch.nn.functional.logsigmoid(a).requires_grad_(True)
+    bt = torch.sigmoid(torch.randn(1, S, GDN_H, generator=g, device=dev)).requires_grad_(True)
+    do = torch.randn(1, S, GDN_H, GDN_D, generator=g, device=dev).to(torch.bfloat16)
+    bounds, parents = info.chunk_boundaries, info.chunk_parent_map
+
+    def step():
+        for t in (x, w, gg, bt):
+            t.grad = None
+        y = tree_conv(x, w, None, bounds, parents)            # [1, C, S]
+        yt = y.transpose(1, 2)
+        q = yt[..., :GDN_HK * GDN_D].reshape(1, S, GDN_HK, GDN_D)
+        k = yt[..., GDN_HK * GDN_D:2 * GDN_HK * GDN_D].reshape(1, S, GDN_HK, GDN_D)
+        v = yt[..., 2 * GDN_HK * GDN_D:].reshape(1, S, GDN_H, GDN_D)
+        out, _ = torch_chunk_gated_delta_rule_tree_varlen(q, k, v, gg, bt, bounds, parents,
+                                                          use_qk_l2norm_in_kernel=True)
+        out.backward(do)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    clocks = ClockSampler(dev)
+    clocks.start()
+    launches0 = _lib.lib().tt_kernel_launches()
+    barrier(world)
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record()
+        step()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    launches = _lib.lib().tt_kernel_launches() - launches0
+    clk = clocks.stop()
+    t = statistics.mean(a.elapsed_time(b) for a, b in ev) / 1e3
+    t_max = max_over_ranks(t, world, dev)
+    tokens_all = sum_over_ranks(float(S), world, dev)
+    pk, pk_src = peaks()
+    achieved = S * gdn_bytes_per_token() / t / 1e9
+    if rank == 0:
+        line = {"metric": "Tree GDN (conv + gated delta rule) fwd+bwd tokens/s",
+                "value": tokens_all / t_max, "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": t_max * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16 in/out, fp32 state and arithmetic", "data": "synthetic",
+                "config": {"workload": "config4: one DFS tree per GPU, random 2-4 branching, "
+                                       "node len U[16,300], 16 qk / 32 v heads, D=128, conv K=4, "
+                                       "q/k l2norm", "tokens": S, "nodes": info.n_chunks,
+                           "l2": "flushed between steps"},
+                "roofline": {"bound": "hbm", "kernel": "whole step",
+                             "achieved": achieved, "peak": float(pk["hbm_gbs"]), "unit": "GB/s",
+                             "frac": achieved / float(pk["hbm_gbs"]), "traffic": None,
+                             "algorithmic_bytes_per_token": gdn_bytes_per_token(),
+                             "peak_source": pk_src},
+                "gpu_launches": int(launches), "clocks": clk}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "gdn":
+        return run_gdn(args)
     return run_ours(args)
 
 

@@ -311,7 +311,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         float p[4], ds[4];
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-          float pv = exp2f(fmaf(sv[4 * i + w], scale_log2, -la[w] * kLog2e));
+          float pv = fast_exp2(fmaf(sv[4 * i + w], scale_log2, -la[w] * kLog2e));
           if (partial && !visible(lo, hi, q0 + 4 * i + w)) pv = 0.f;
           p[w] = pv;
           ds[w] = pv * (dp[4 * i + w] - da[w]);
@@ -455,7 +455,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
       float p[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) p[i] = exp2f(fmaf(sv[i], scale_log2, -l2));
+      for (int i = 0; i < 32; ++i) p[i] = fast_exp2(fmaf(sv[i], scale_log2, -l2));
       if (partial) {
         // key intervals of this tile, zero-padded past n_kv (never visible)
         const int4* LO = reinterpret_cast<const int4*>(aux + s * kAuxBytes) + c0 / 4;

@@ -307,8 +307,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
           uint32_t pk[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const float p0 = exp2f(fmaf(sv[hf * 64 + 2 * i], scale_log2, -mb));
-            const float p1 = exp2f(fmaf(sv[hf * 64 + 2 * i + 1], scale_log2, -mb));
+            const float p0 = fast_exp2(fmaf(sv[hf * 64 + 2 * i], scale_log2, -mb));
+            const float p1 = fast_exp2(fmaf(sv[hf * 64 + 2 * i + 1], scale_log2, -mb));
             l_run += p0 + p1;
             pk[i] = pack2<kBf16>(p0, p1);
           }
