@@ -5,17 +5,21 @@
 // computed without atomics in two kernels that recompute P from the saved
 // row log-sum-exp:
 //
-//   dK/dV kernel  one CTA per (kv head, 128-key tile); loops over the q heads
-//                 of its GQA group and the q tiles the work list marks
-//                 visible, in 64-row sub-tiles.  S^T = K Q^T and
-//                 dP^T = V dO^T (A, B from shared memory); the elementwise
-//                 warps turn them into P^T and dS^T = P^T (dP^T - delta) and
-//                 write both back into TMEM as 16-bit; then dV += P^T dO and
-//                 dK += dS^T Q read A from TMEM.
-//   dQ kernel     one CTA per (q head, 128-row tile), in 64-key sub-tiles:
+//   dK/dV kernel  one CTA per (kv head, 128-key tile) holding K and V; streams
+//                 the q heads of its GQA group x the q tiles the work list
+//                 marks visible, as 64-row sub-tiles of Q and dO.
+//                 S^T = K Q^T and dP^T = V dO^T (A, B from shared memory); the
+//                 elementwise warps turn them into P^T and dS^T = P^T (dP^T -
+//                 delta), written back into TMEM as 16-bit; then dV += P^T dO
+//                 and dK += dS^T Q read A from TMEM.
+//   dQ kernel     one CTA per (q head, 128-row tile) holding Q and dO; streams
+//                 the visible kv tiles as 64-key sub-tiles of K and V:
 //                 S = Q K^T, dP = dO V^T, dS = P (dP - delta) into TMEM,
 //                 dQ += dS K.
 //
+// Streamed sub-tiles go through a 4-stage ring (each stage: two 64 x 128
+// 16-bit sub-tiles + their 64 row terms or key intervals, bulk-copied on the
+// same mbarrier), released per sub-tile, so loads run three sub-tiles ahead.
 // Sub-tile accumulators are double buffered in TMEM so the MMAs of sub-tile
 // u+1 run while the elementwise warps process sub-tile u.  TMEM (512 cols):
 //   buffer b in {0,1}: S [64b, 64b+64), dP [128+64b, 128+64b+64)
@@ -23,9 +27,7 @@
 // Warps: 0 TMA producer, 1 MMA issuer, 2..9 elementwise (two warps per TMEM
 // lane quadrant; warp half h owns columns [32h, 32h+32) of each sub-tile and
 // writes its 16-bit P / dS into the first 16 of those columns, i.e. only into
-// columns it has already read, so the two warps never race).  LSE/delta (dK/dV)
-// and the key intervals (dQ) of each streamed tile are bulk-copied into shared
-// memory on the same mbarrier as the tile.
+// columns it has already read, so the two warps never race).
 #include <type_traits>
 
 #include "tt_sm100.cuh"
@@ -34,33 +36,36 @@ namespace tt {
 namespace sm100 {
 namespace {
 
-constexpr int kT = 128;                    // rows per tile (keys or queries)
-constexpr int kD = 128;                    // head dim
-constexpr int kSub = 64;                   // sub-tile width along the streamed dim
-constexpr int kTileBytes = kT * kD * 2;
-constexpr int kHalfBytes = kTileBytes / 2; // one 64-dim swizzle block of 128 rows
-constexpr int kSubOff = kSub * 128;        // byte offset of sub-tile 1 inside a block
+constexpr int kT = 128;                     // rows of the fixed tiles and of a list tile
+constexpr int kD = 128;                     // head dim
+constexpr int kSub = 64;                    // rows of a streamed sub-tile
+constexpr int kStages = 4;                  // streamed ring depth
+constexpr int kTileBytes = kT * kD * 2;     // fixed tile (128 rows)
+constexpr int kTileHalf = kTileBytes / 2;   // one 64-dim swizzle block of a fixed tile
+constexpr int kSubBytes = kSub * kD * 2;    // streamed sub-tile (64 rows)
+constexpr int kSubHalf = kSubBytes / 2;     // one 64-dim swizzle block of a sub-tile
+constexpr int kAuxHalf = kSub * 4;          // 64 four-byte entries
+constexpr int kAuxBytes = 2 * kAuxHalf;     // per stage: two 64-entry arrays
 constexpr int kThreads = 320;
-constexpr int kEw = 256;                   // elementwise threads
+constexpr int kEw = 256;                    // elementwise threads
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdBarriers {
-  uint64_t fixed_full;      // the tiles loaded once (K,V or Q,dO)
-  uint64_t a_full[2];       // streamed tile A (Q or K) + its row/key terms
-  uint64_t b_full[2];       // streamed tile B (dO or V)
-  uint64_t ab_empty[2];
-  uint64_t sdp_full[2];     // S and dP of a sub-tile ready (per TMEM buffer)
-  uint64_t ew_full[2];      // P / dS of a sub-tile written back (256 arrivals)
-  uint64_t acc_done;        // every MMA of the CTA finished
+  uint64_t fixed_full;       // the two tiles loaded once (K,V or Q,dO)
+  uint64_t a_full[kStages];  // streamed sub-tile A (Q or K) + its aux arrays
+  uint64_t b_full[kStages];  // streamed sub-tile B (dO or V)
+  uint64_t ab_empty[kStages];
+  uint64_t sdp_full[2];      // S and dP of a sub-tile ready (per TMEM buffer)
+  uint64_t ew_full[2];       // P / dS of a sub-tile written back (256 arrivals)
+  uint64_t acc_done;         // every MMA of the CTA finished
   uint64_t drain;
   uint32_t tmem_base;
   int32_t abort;
 };
 
-// per stage: two 128-entry 4-byte arrays (LSE + delta, or kv_lo + kv_hi)
-constexpr int kAuxBytes = 2 * kT * 4;
-constexpr size_t kSmemBytes = 1024 + 6 * kTileBytes + 2 * kAuxBytes + sizeof(BwdBarriers);
+constexpr size_t kSmemBytes = 1024 + 2 * kTileBytes + 2 * kStages * kSubBytes +
+                              kStages * kAuxBytes + sizeof(BwdBarriers);
 
 __device__ __forceinline__ void raise_abort(BwdBarriers* sh, int32_t* status) {
   set_status(status, TT_ERR_DEVICE_TIMEOUT);
@@ -69,12 +74,14 @@ __device__ __forceinline__ void raise_abort(BwdBarriers* sh, int32_t* status) {
 
 __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
   mbar_init(&sh->fixed_full, 1);
-  for (int s = 0; s < 2; ++s) {
+  for (int s = 0; s < kStages; ++s) {
     mbar_init(&sh->a_full[s], 1);
     mbar_init(&sh->b_full[s], 1);
     mbar_init(&sh->ab_empty[s], 1);
-    mbar_init(&sh->sdp_full[s], 1);
-    mbar_init(&sh->ew_full[s], kEw);
+  }
+  for (int b = 0; b < 2; ++b) {
+    mbar_init(&sh->sdp_full[b], 1);
+    mbar_init(&sh->ew_full[b], kEw);
   }
   mbar_init(&sh->acc_done, 1);
   mbar_init(&sh->drain, 1);
@@ -82,27 +89,28 @@ __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
   fence_mbar_init();
 }
 
-// D[128 x 64] = A[128 rows] * B[64 rows]^T over K = 128 dims; both operands are
-// K-major 128-byte-swizzled smem tiles, b_addr = first row of the 64-row block.
-__device__ __forceinline__ void mma_ss_n64(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr,
+// D[128 x 64] = X[128 rows] * A[64 rows]^T over K = 128 dims; X is a fixed
+// 128-row tile, A a 64-row streamed sub-tile, both K-major 128-byte swizzled.
+__device__ __forceinline__ void mma_ss_n64(uint32_t d_tmem, uint32_t x_addr, uint32_t a_addr,
                                            uint32_t idesc) {
 #pragma unroll
   for (int kk = 0; kk < kD / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-    mma_ss(d_tmem, desc_sw128(a_addr + off, 16, 1024), desc_sw128(b_addr + off, 16, 1024), idesc,
+    const uint32_t ox = (kk >> 2) * kTileHalf + (kk & 3) * 32;
+    const uint32_t oa = (kk >> 2) * kSubHalf + (kk & 3) * 32;
+    mma_ss(d_tmem, desc_sw128(x_addr + ox, 16, 1024), desc_sw128(a_addr + oa, 16, 1024), idesc,
            kk > 0 ? 1u : 0u);
   }
 }
 
-// D[128 x 128] (+)= A[128 x 64, 16-bit in TMEM] * B[64 rows x 128 dims], B an
-// MN-major smem block starting at row b_addr.  A's 64 columns of K sit as two
-// 16-column groups at a_tmem and a_tmem + 32 (one per elementwise warp half).
+// D[128 x 128] (+)= A[128 x 64, 16-bit in TMEM] * B[64 rows x 128 dims], B a
+// streamed sub-tile read MN-major.  A's 64 columns of K sit as two 16-column
+// groups at a_tmem and a_tmem + 32 (one per elementwise warp half).
 __device__ __forceinline__ void mma_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr,
                                            uint32_t idesc, bool accumulate) {
 #pragma unroll
   for (int kk = 0; kk < kSub / 16; ++kk) {
     const uint32_t a = a_tmem + (kk < 2 ? kk * 8 : 32 + (kk - 2) * 8);
-    mma_ts(d_tmem, a, desc_sw128(b_addr + kk * 2048, kHalfBytes, 1024), idesc,
+    mma_ts(d_tmem, a, desc_sw128(b_addr + kk * 2048, kSubHalf, 1024), idesc,
            (accumulate || kk > 0) ? 1u : 0u);
   }
 }
@@ -122,40 +130,40 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
                                     ~static_cast<uintptr_t>(1023));
 }
 
-// Streams `n_it` (A, B) tile pairs through the 2-stage ring; `coord(it, &row,
-// &head, &aux_a, &aux_b)` gives the tile row / head and the two 512-byte
-// arrays to bulk-copy with tile A.
+// Streams `n_u` (A, B) sub-tile pairs through the ring; `coord(u, &row,
+// &head, &aux_a, &aux_b)` gives the sub-tile's first row / head and the two
+// 256-byte arrays to bulk-copy with sub-tile A.
 template <typename Coord>
 __device__ __forceinline__ void produce(BwdBarriers* sh, const volatile int32_t* abort_flag,
-                                        int32_t* status, int n_it, uint8_t* sA, uint8_t* sB,
+                                        int32_t* status, int n_u, uint8_t* ringA, uint8_t* ringB,
                                         uint8_t* aux, const CUtensorMap* ta,
                                         const CUtensorMap* tb, Coord coord) {
-  int issued[2] = {0, 0};
+  int issued[kStages] = {0, 0, 0, 0};
   bool ok = true;
-  for (int it = 0; it < n_it; ++it) {
-    const int s = it & 1;
-    if (it >= 2) ok = mbar_wait(&sh->ab_empty[s], ((it >> 1) - 1) & 1, abort_flag);
+  for (int u = 0; u < n_u; ++u) {
+    const int s = u % kStages;
+    if (u >= kStages) ok = mbar_wait(&sh->ab_empty[s], ((u / kStages) - 1) & 1, abort_flag);
     if (!ok) break;
     int row, head;
     const void *xa, *xb;
-    coord(it, &row, &head, &xa, &xb);
-    uint8_t* a_dst = sA + s * kTileBytes;
-    uint8_t* b_dst = sB + s * kTileBytes;
+    coord(u, &row, &head, &xa, &xb);
+    uint8_t* a_dst = ringA + s * kSubBytes;
+    uint8_t* b_dst = ringB + s * kSubBytes;
     uint8_t* x_dst = aux + s * kAuxBytes;
-    mbar_arrive_expect_tx(&sh->a_full[s], kTileBytes + kAuxBytes);
+    mbar_arrive_expect_tx(&sh->a_full[s], kSubBytes + kAuxBytes);
     tma_load_3d(a_dst, ta, &sh->a_full[s], 0, row, head);
-    tma_load_3d(a_dst + kHalfBytes, ta, &sh->a_full[s], 64, row, head);
-    bulk_load(x_dst, xa, kAuxBytes / 2, &sh->a_full[s]);
-    bulk_load(x_dst + kAuxBytes / 2, xb, kAuxBytes / 2, &sh->a_full[s]);
-    mbar_arrive_expect_tx(&sh->b_full[s], kTileBytes);
+    tma_load_3d(a_dst + kSubHalf, ta, &sh->a_full[s], 64, row, head);
+    bulk_load(x_dst, xa, kAuxHalf, &sh->a_full[s]);
+    bulk_load(x_dst + kAuxHalf, xb, kAuxHalf, &sh->a_full[s]);
+    mbar_arrive_expect_tx(&sh->b_full[s], kSubBytes);
     tma_load_3d(b_dst, tb, &sh->b_full[s], 0, row, head);
-    tma_load_3d(b_dst + kHalfBytes, tb, &sh->b_full[s], 64, row, head);
+    tma_load_3d(b_dst + kSubHalf, tb, &sh->b_full[s], 64, row, head);
     issued[s] += 1;
   }
   if (!ok) {
     raise_abort(sh, status);
     mbar_wait(&sh->fixed_full, 0, nullptr);
-    for (int s = 0; s < 2; ++s)
+    for (int s = 0; s < kStages; ++s)
       if (issued[s] > 0) {
         mbar_wait(&sh->a_full[s], (issued[s] - 1) & 1, nullptr);
         mbar_wait(&sh->b_full[s], (issued[s] - 1) & 1, nullptr);
@@ -163,38 +171,35 @@ __device__ __forceinline__ void produce(BwdBarriers* sh, const volatile int32_t*
   }
 }
 
-// MMA issue loop shared by both kernels.  For sub-tile u (tile it = u/2,
-// half sb = u%2, stage s = it%2, TMEM buffer b = sb):
-//   sdp(u):  S_b = X * A[sb]^T, dP_b = Y * B[sb]^T   (X, Y fixed tiles)
-//   acc(u):  per-kernel TS products reading P_b / dS_b
+// MMA issue loop shared by both kernels.  Sub-tile u uses ring stage
+// s = u % kStages and TMEM buffer b = u % 2:
+//   sdp(u):  S_b = X * A_s^T, dP_b = Y * B_s^T   (X, Y the fixed tiles)
+//   acc(u):  the kernel's TS products reading P_b / dS_b and the stage's tiles
 template <typename Acc>
 __device__ __forceinline__ void mma_loop(BwdBarriers* sh, const volatile int32_t* abort_flag,
-                                         int32_t* status, uint32_t tmem, int n_it,
-                                         uint32_t x_addr, uint32_t y_addr, uint32_t a_addr,
-                                         uint32_t b_addr, uint32_t id_s, Acc acc) {
-  const int n_u = 2 * n_it;
+                                         int32_t* status, uint32_t tmem, int n_u,
+                                         uint32_t x_addr, uint32_t y_addr, uint32_t ring_a,
+                                         uint32_t ring_b, uint32_t id_s, Acc acc) {
   bool ok = mbar_wait(&sh->fixed_full, 0, abort_flag);
   auto sdp = [&](int u) -> bool {
-    const int it = u >> 1, sb = u & 1, s = it & 1;
-    if (sb == 0) {
-      if (!mbar_wait(&sh->a_full[s], (it >> 1) & 1, abort_flag)) return false;
-      if (!mbar_wait(&sh->b_full[s], (it >> 1) & 1, abort_flag)) return false;
-      tc_fence_after();
-    }
-    const uint32_t off = s * kTileBytes + sb * kSubOff;
-    mma_ss_n64(tmem + 64 * sb, x_addr, a_addr + off, id_s);
-    mma_ss_n64(tmem + 128 + 64 * sb, y_addr, b_addr + off, id_s);
-    tc_commit(&sh->sdp_full[sb]);
+    const int s = u % kStages, b = u & 1;
+    const uint32_t ph = (u / kStages) & 1;
+    if (!mbar_wait(&sh->a_full[s], ph, abort_flag)) return false;
+    if (!mbar_wait(&sh->b_full[s], ph, abort_flag)) return false;
+    tc_fence_after();
+    mma_ss_n64(tmem + 64 * b, x_addr, ring_a + s * kSubBytes, id_s);
+    mma_ss_n64(tmem + 128 + 64 * b, y_addr, ring_b + s * kSubBytes, id_s);
+    tc_commit(&sh->sdp_full[b]);
     return true;
   };
   if (ok && n_u > 0) ok = sdp(0);
   for (int u = 0; u < n_u && ok; ++u) {
     if (u + 1 < n_u && !(ok = sdp(u + 1))) break;
-    const int sb = u & 1, s = (u >> 1) & 1;
-    if (!(ok = mbar_wait(&sh->ew_full[sb], (u >> 1) & 1, abort_flag))) break;
+    const int b = u & 1, s = u % kStages;
+    if (!(ok = mbar_wait(&sh->ew_full[b], (u >> 1) & 1, abort_flag))) break;
     tc_fence_after();
-    acc(u, s, sb, u > 0);
-    if (sb == 1) tc_commit(&sh->ab_empty[s]);
+    acc(s, b, u > 0);
+    tc_commit(&sh->ab_empty[s]);
   }
   tc_commit(&sh->acc_done);
   if (!ok) {
@@ -220,10 +225,10 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   uint8_t* base = align1024(smem_raw);
   uint8_t* sK = base;
   uint8_t* sV = sK + kTileBytes;
-  uint8_t* sQ = sV + kTileBytes;           // 2 stages
-  uint8_t* sDO = sQ + 2 * kTileBytes;      // 2 stages
-  uint8_t* aux = sDO + 2 * kTileBytes;     // 2 stages x (LSE[128], delta[128])
-  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + 2 * kAuxBytes);
+  uint8_t* rQ = sV + kTileBytes;                 // kStages x Q sub-tile
+  uint8_t* rDO = rQ + kStages * kSubBytes;       // kStages x dO sub-tile
+  uint8_t* aux = rDO + kStages * kSubBytes;      // kStages x (LSE[64], delta[64])
+  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + kStages * kAuxBytes);
   const volatile int32_t* abort_flag = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -231,7 +236,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   const int kt = blockIdx.y;                 // root-side tiles (longest lists) first
   const int e0 = bwd_ptr[kt];
   const int n_list = bwd_ptr[kt + 1] - e0;
-  const int n_it = rep * n_list;
+  const int n_u = 2 * rep * n_list;          // 64-row sub-tiles
   const int ld = lse_ld(n_q);
 
   if (threadIdx.x == 0) init_barriers(sh);
@@ -246,18 +251,19 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   constexpr uint32_t kColDV = 256, kColDK = 384;
 
   if (warp == 0) {
-    if (lane == 0 && n_it > 0) {
+    if (lane == 0 && n_u > 0) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_do);
       mbar_arrive_expect_tx(&sh->fixed_full, 2 * kTileBytes);
       tma_load_3d(sK, &tm_k, &sh->fixed_full, 0, kt * kT, hk);
-      tma_load_3d(sK + kHalfBytes, &tm_k, &sh->fixed_full, 64, kt * kT, hk);
+      tma_load_3d(sK + kTileHalf, &tm_k, &sh->fixed_full, 64, kt * kT, hk);
       tma_load_3d(sV, &tm_v, &sh->fixed_full, 0, kt * kT, hk);
-      tma_load_3d(sV + kHalfBytes, &tm_v, &sh->fixed_full, 64, kt * kT, hk);
-      produce(sh, abort_flag, status, n_it, sQ, sDO, aux, &tm_q, &tm_do,
-              [&](int it, int* row, int* head, const void** xa, const void** xb) {
+      tma_load_3d(sV + kTileHalf, &tm_v, &sh->fixed_full, 64, kt * kT, hk);
+      produce(sh, abort_flag, status, n_u, rQ, rDO, aux, &tm_q, &tm_do,
+              [&](int u, int* row, int* head, const void** xa, const void** xb) {
+                const int it = u >> 1;
                 const int h = hk * rep + it / n_list;
-                const int q0 = (bwd_list[e0 + it % n_list] >> 1) * kT;
+                const int q0 = (bwd_list[e0 + it % n_list] >> 1) * kT + (u & 1) * kSub;
                 *row = q0;
                 *head = h;
                 *xa = lse + static_cast<int64_t>(h) * ld + q0;
@@ -265,15 +271,15 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
               });
     }
   } else if (warp == 1) {
-    if (lane == 0 && n_it > 0) {
+    if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
       constexpr uint32_t id_o = idesc_f16(kBf16, kT, kD, true);
-      const uint32_t q_addr = smem_u32(sQ), o_addr = smem_u32(sDO);
-      mma_loop(sh, abort_flag, status, tmem, n_it, smem_u32(sK), smem_u32(sV), q_addr, o_addr,
-               id_s, [&](int u, int s, int sb, bool accumulate) {
-                 const uint32_t off = s * kTileBytes + sb * kSubOff;
-                 mma_ts_k64(tmem + kColDV, tmem + 64 * sb, o_addr + off, id_o, accumulate);
-                 mma_ts_k64(tmem + kColDK, tmem + 128 + 64 * sb, q_addr + off, id_o, accumulate);
+      const uint32_t q_addr = smem_u32(rQ), o_addr = smem_u32(rDO);
+      mma_loop(sh, abort_flag, status, tmem, n_u, smem_u32(sK), smem_u32(sV), q_addr, o_addr,
+               id_s, [&](int s, int b, bool accumulate) {
+                 mma_ts_k64(tmem + kColDV, tmem + 64 * b, o_addr + s * kSubBytes, id_o, accumulate);
+                 mma_ts_k64(tmem + kColDK, tmem + 128 + 64 * b, q_addr + s * kSubBytes, id_o,
+                            accumulate);
                });
     }
   } else {
@@ -285,23 +291,21 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const int hi = j < n_kv ? kv_hi[j] : 0;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     bool ok = true;
-    const int n_u = 2 * n_it;
     for (int u = 0; u < n_u; ++u) {
-      const int it = u >> 1, sb = u & 1, s = it & 1;
+      const int it = u >> 1, b = u & 1, s = u % kStages;
       const int ent = bwd_list[e0 + it % n_list];
-      const int c0 = sb * kSub + half * 32;   // first q column (within the tile) of this warp
-      const int q0 = (ent >> 1) * kT + c0;
+      const int q0 = (ent >> 1) * kT + b * kSub + half * 32;   // first q row of this warp
       const bool partial = ent & 1;
-      ok = mbar_wait(&sh->sdp_full[sb], (u >> 1) & 1, abort_flag);
-      if (ok && sb == 0) ok = mbar_wait(&sh->a_full[s], (it >> 1) & 1, abort_flag);
+      ok = mbar_wait(&sh->sdp_full[b], (u >> 1) & 1, abort_flag);
+      if (ok) ok = mbar_wait(&sh->a_full[s], (u / kStages) & 1, abort_flag);   // aux visible
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t cs = 64 * sb + 32 * half, cp = 128 + 64 * sb + 32 * half;
+      const uint32_t cs = 64 * b + 32 * half, cp = 128 + 64 * b + 32 * half;
       float sv[32], dp[32];
       tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
-      const float4* L4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes) + c0 / 4;
-      const float4* D4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes + kAuxBytes / 2) + c0 / 4;
+      const float4* L4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes) + half * 8;
+      const float4* D4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes + kAuxHalf) + half * 8;
       uint32_t pw[16], dw[16];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -325,9 +329,9 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tmem_st16(lane_addr + cp, dw);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&sh->ew_full[sb]);
+      mbar_arrive(&sh->ew_full[b]);
     }
-    if (ok && n_it > 0) {
+    if (ok && n_u > 0) {
       ok = mbar_wait(&sh->acc_done, 0, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
     }
@@ -339,14 +343,14 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 #pragma unroll 1
       for (int c = 2 * half; c < 2 * half + 2; ++c) {
         float a[32];
-        if (n_it > 0) {
+        if (n_u > 0) {
           tmem_ld32(lane_addr + kColDV + c * 32, a);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) a[i] = 0.f;
         }
         if (j < n_kv) store_row32<kBf16>(dv + c * 32, a, 1.f);
-        if (n_it > 0) tmem_ld32(lane_addr + kColDK + c * 32, a);
+        if (n_u > 0) tmem_ld32(lane_addr + kColDK + c * 32, a);
         if (j < n_kv) store_row32<kBf16>(dk + c * 32, a, scale);
       }
     } else {
@@ -376,10 +380,10 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   uint8_t* base = align1024(smem_raw);
   uint8_t* sQ = base;
   uint8_t* sDO = sQ + kTileBytes;
-  uint8_t* sK = sDO + kTileBytes;          // 2 stages
-  uint8_t* sV = sK + 2 * kTileBytes;       // 2 stages
-  uint8_t* aux = sV + 2 * kTileBytes;      // 2 stages x (kv_lo[128], kv_hi[128])
-  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + 2 * kAuxBytes);
+  uint8_t* rK = sDO + kTileBytes;                // kStages x K sub-tile
+  uint8_t* rV = rK + kStages * kSubBytes;        // kStages x V sub-tile
+  uint8_t* aux = rV + kStages * kSubBytes;       // kStages x (kv_lo[64], kv_hi[64])
+  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + kStages * kAuxBytes);
   const volatile int32_t* abort_flag = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -387,7 +391,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   const int qt = gridDim.y - 1 - blockIdx.y;
   const int hk = h / rep;
   const int e0 = fwd_ptr[qt];
-  const int n_it = fwd_ptr[qt + 1] - e0;
+  const int n_u = 2 * (fwd_ptr[qt + 1] - e0);
   const int ld = lse_ld(n_q);
 
   if (threadIdx.x == 0) init_barriers(sh);
@@ -402,17 +406,17 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   constexpr uint32_t kColDQ = 256;
 
   if (warp == 0) {
-    if (lane == 0 && n_it > 0) {
+    if (lane == 0 && n_u > 0) {
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
       mbar_arrive_expect_tx(&sh->fixed_full, 2 * kTileBytes);
       tma_load_3d(sQ, &tm_q, &sh->fixed_full, 0, qt * kT, h);
-      tma_load_3d(sQ + kHalfBytes, &tm_q, &sh->fixed_full, 64, qt * kT, h);
+      tma_load_3d(sQ + kTileHalf, &tm_q, &sh->fixed_full, 64, qt * kT, h);
       tma_load_3d(sDO, &tm_do, &sh->fixed_full, 0, qt * kT, h);
-      tma_load_3d(sDO + kHalfBytes, &tm_do, &sh->fixed_full, 64, qt * kT, h);
-      produce(sh, abort_flag, status, n_it, sK, sV, aux, &tm_k, &tm_v,
-              [&](int it, int* row, int* head, const void** xa, const void** xb) {
-                const int j0 = (fwd_list[e0 + it] >> 1) * kT;
+      tma_load_3d(sDO + kTileHalf, &tm_do, &sh->fixed_full, 64, qt * kT, h);
+      produce(sh, abort_flag, status, n_u, rK, rV, aux, &tm_k, &tm_v,
+              [&](int u, int* row, int* head, const void** xa, const void** xb) {
+                const int j0 = (fwd_list[e0 + (u >> 1)] >> 1) * kT + (u & 1) * kSub;
                 *row = j0;
                 *head = hk;
                 *xa = kv_lo + j0;
@@ -420,14 +424,14 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
               });
     }
   } else if (warp == 1) {
-    if (lane == 0 && n_it > 0) {
+    if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
       constexpr uint32_t id_o = idesc_f16(kBf16, kT, kD, true);
-      const uint32_t k_addr = smem_u32(sK);
-      mma_loop(sh, abort_flag, status, tmem, n_it, smem_u32(sQ), smem_u32(sDO), k_addr,
-               smem_u32(sV), id_s, [&](int u, int s, int sb, bool accumulate) {
-                 mma_ts_k64(tmem + kColDQ, tmem + 64 * sb, k_addr + s * kTileBytes + sb * kSubOff,
-                            id_o, accumulate);
+      const uint32_t k_addr = smem_u32(rK);
+      mma_loop(sh, abort_flag, status, tmem, n_u, smem_u32(sQ), smem_u32(sDO), k_addr,
+               smem_u32(rV), id_s, [&](int s, int b, bool accumulate) {
+                 mma_ts_k64(tmem + kColDQ, tmem + 64 * b, k_addr + s * kSubBytes, id_o,
+                            accumulate);
                });
     }
   } else {
@@ -439,27 +443,24 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     const float l2 = lse[static_cast<int64_t>(h) * ld + row] * kLog2e;   // padded rows: +inf
     const float dr = delta[static_cast<int64_t>(h) * ld + row];
     bool ok = true;
-    const int n_u = 2 * n_it;
     for (int u = 0; u < n_u; ++u) {
-      const int it = u >> 1, sb = u & 1, s = it & 1;
-      const int ent = fwd_list[e0 + it];
-      const bool partial = ent & 1;
-      const int c0 = sb * kSub + half * 32;  // first key column (within the tile) of this warp
-      ok = mbar_wait(&sh->sdp_full[sb], (u >> 1) & 1, abort_flag);
-      if (ok && sb == 0) ok = mbar_wait(&sh->a_full[s], (it >> 1) & 1, abort_flag);
+      const int b = u & 1, s = u % kStages;
+      const bool partial = fwd_list[e0 + (u >> 1)] & 1;
+      ok = mbar_wait(&sh->sdp_full[b], (u >> 1) & 1, abort_flag);
+      if (ok && partial) ok = mbar_wait(&sh->a_full[s], (u / kStages) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t cs = 64 * sb + 32 * half, cp = 128 + 64 * sb + 32 * half;
+      const uint32_t cs = 64 * b + 32 * half, cp = 128 + 64 * b + 32 * half;
       float sv[32], dp[32];
       tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
       float p[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) p[i] = fast_exp2(fmaf(sv[i], scale_log2, -l2));
       if (partial) {
-        // key intervals of this tile, zero-padded past n_kv (never visible)
-        const int4* LO = reinterpret_cast<const int4*>(aux + s * kAuxBytes) + c0 / 4;
-        const int4* HI = reinterpret_cast<const int4*>(aux + s * kAuxBytes + kAuxBytes / 2) + c0 / 4;
+        // key intervals of this sub-tile, zero-padded past n_kv (never visible)
+        const int4* LO = reinterpret_cast<const int4*>(aux + s * kAuxBytes) + half * 8;
+        const int4* HI = reinterpret_cast<const int4*>(aux + s * kAuxBytes + kAuxHalf) + half * 8;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int4 a = LO[i], z = HI[i];
@@ -476,9 +477,9 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tmem_st16(lane_addr + cs, dw);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&sh->ew_full[sb]);
+      mbar_arrive(&sh->ew_full[b]);
     }
-    if (ok && n_it > 0) {
+    if (ok && n_u > 0) {
       ok = mbar_wait(&sh->acc_done, 0, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
     }
@@ -488,7 +489,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
 #pragma unroll 1
       for (int c = 2 * half; c < 2 * half + 2; ++c) {
         float a[32];
-        if (n_it > 0) {
+        if (n_u > 0) {
           tmem_ld32(lane_addr + kColDQ + c * 32, a);
         } else {
 #pragma unroll
@@ -538,8 +539,10 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// [tokens, heads, 128] 16-bit tensor -> 3-D map {dim, token, head}, box
+// {64, box_rows, 1}, 128-byte swizzle, zero fill outside the tensor.
 int make_map(CUtensorMap* map, bool bf16, const void* ptr, int64_t n_tok, int64_t n_head,
-             int64_t st_tok, int64_t st_head) {
+             int64_t st_tok, int64_t st_head, int box_rows) {
   static EncodeTiledFn fn = nullptr;
   if (!fn) {
     void* p = nullptr;
@@ -554,7 +557,7 @@ int make_map(CUtensorMap* map, bool bf16, const void* ptr, int64_t n_tok, int64_
     return TT_ERR_UNSUPPORTED;
   cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)n_tok, (cuuint64_t)n_head};
   cuuint64_t strides[2] = {(cuuint64_t)(st_tok * 2), (cuuint64_t)(st_head * 2)};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                   3, const_cast<void*>(ptr), dims, strides, box, estr,
@@ -614,12 +617,6 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
     tt_count_launches(n);
     return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
   }
-  CUtensorMap mq, mk, mv, mdo;
-  int rc;
-  if ((rc = make_map(&mq, bf16, q, n_q, hq, q_st, q_sh)) != TT_OK) return rc;
-  if ((rc = make_map(&mk, bf16, k, n_kv, hkv, k_st, k_sh)) != TT_OK) return rc;
-  if ((rc = make_map(&mv, bf16, v, n_kv, hkv, v_st, v_sh)) != TT_OK) return rc;
-  if ((rc = make_map(&mdo, bf16, dout, n_q, hq, do_st, do_sh)) != TT_OK) return rc;
   const int ld = tt::lse_ld(n_q);
   const int warps = ld * hq;
   int launches = 0;
@@ -634,7 +631,14 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
   }
   const float scale_log2 = scale * 1.4426950408889634f;
   const int rep = hq / hkv;
+  int rc;
   if (phases & TT_BWD_DKDV) {
+    // fixed K/V tiles (128 rows), streamed Q/dO sub-tiles (64 rows)
+    CUtensorMap mq, mk, mv, mdo;
+    if ((rc = make_map(&mq, bf16, q, n_q, hq, q_st, q_sh, kSub)) != TT_OK) return rc;
+    if ((rc = make_map(&mk, bf16, k, n_kv, hkv, k_st, k_sh, kT)) != TT_OK) return rc;
+    if ((rc = make_map(&mv, bf16, v, n_kv, hkv, v_st, v_sh, kT)) != TT_OK) return rc;
+    if ((rc = make_map(&mdo, bf16, dout, n_q, hq, do_st, do_sh, kSub)) != TT_OK) return rc;
     auto kdkdv = bf16 ? attn_bwd_dkdv_tc<true> : attn_bwd_dkdv_tc<false>;
     TT_CUDA_OK(cudaFuncSetAttribute(kdkdv, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemBytes));
@@ -645,6 +649,12 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
     ++launches;
   }
   if (phases & TT_BWD_DQ) {
+    // fixed Q/dO tiles (128 rows), streamed K/V sub-tiles (64 rows)
+    CUtensorMap mq, mk, mv, mdo;
+    if ((rc = make_map(&mq, bf16, q, n_q, hq, q_st, q_sh, kT)) != TT_OK) return rc;
+    if ((rc = make_map(&mk, bf16, k, n_kv, hkv, k_st, k_sh, kSub)) != TT_OK) return rc;
+    if ((rc = make_map(&mv, bf16, v, n_kv, hkv, v_st, v_sh, kSub)) != TT_OK) return rc;
+    if ((rc = make_map(&mdo, bf16, dout, n_q, hq, do_st, do_sh, kT)) != TT_OK) return rc;
     auto kdq = bf16 ? attn_bwd_dq_tc<true> : attn_bwd_dq_tc<false>;
     TT_CUDA_OK(cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemBytes));
