@@ -267,9 +267,14 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
             if (!visible(a.w, z.w, row)) sv[4 * c + 3] = -INFINITY;
           }
         }
-        float mx = -INFINITY;
+        // row max as 8 independent chains (a single chain is 128 dependent ops)
+        float mx8[8];
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, sv[c]);
+        for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
+#pragma unroll
+        for (int c = 8; c < kBN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float m_new = fmaxf(m_run, mx * scale_log2);
         // PV_g(it-1) must be complete before O_g may be rescaled; waiting
         // every iteration keeps the o_done phases observed in order.
@@ -303,17 +308,20 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
         l_run *= alpha;
         const float mb = (m_run == -INFINITY) ? 0.f : m_run;
 #pragma unroll
+        float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};   // 8 independent partial sums
+#pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           uint32_t pk[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float p0 = fast_exp2(fmaf(sv[hf * 64 + 2 * i], scale_log2, -mb));
             const float p1 = fast_exp2(fmaf(sv[hf * 64 + 2 * i + 1], scale_log2, -mb));
-            l_run += p0 + p1;
+            ls[i & 7] += p0 + p1;
             pk[i] = pack2<kBf16>(p0, p1);
           }
           tmem_st32(lane_addr + col_s + hf * 32, pk);
         }
+        l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&sh->p_full[g]);
