@@ -33,19 +33,26 @@ namespace {
 constexpr int kBM = 128;                  // query rows per tile
 constexpr int kBN = 128;                  // keys per tile
 constexpr int kD = 128;                   // head dim
-constexpr int kStages = 2;                // K/V ring depth
+constexpr int kStages = 2;                // K ring and V ring depth
+constexpr int kAuxStages = 4;             // key-interval ring depth
 constexpr int kTileBytes = kBM * kD * 2;  // one 128 x 128 16-bit tile
 constexpr int kHalfBytes = kTileBytes / 2;  // one 64-column swizzle block
-constexpr int kAuxBytes = 2 * kBN * 4;      // kv_lo[128] + kv_hi[128] of a stage
+constexpr int kAuxBytes = 2 * kBN * 4;      // kv_lo[128] + kv_hi[128] of a tile
 constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
+#ifndef TT_FWD_EMU_PER8
+#define TT_FWD_EMU_PER8 2
+#endif
+constexpr int kEmuPer8 = TT_FWD_EMU_PER8;   // exp2 column pairs of 8 on the FMA pipe
 
 struct FwdBarriers {
   uint64_t q_full;
   uint64_t k_full[kStages];
   uint64_t v_full[kStages];
-  uint64_t kv_empty[kStages];
+  uint64_t k_empty[kStages];    // the last score MMA of the stage's tile completed
+  uint64_t v_empty[kStages];    // the last PV MMA of the stage's tile completed
+  uint64_t aux_full[kAuxStages];
   uint64_t s_full[2];       // per head
   uint64_t p_full[2];       // per head, 128 arrivals
   uint64_t o_done[2];       // per head
@@ -55,7 +62,7 @@ struct FwdBarriers {
 };
 
 constexpr size_t kSmemBytes =
-    1024 + kTileBytes * (2 + 2 * kStages) + kStages * kAuxBytes + sizeof(FwdBarriers);
+    1024 + kTileBytes * (2 + 2 * kStages) + kAuxStages * kAuxBytes + sizeof(FwdBarriers);
 
 __device__ __forceinline__ void raise_abort(FwdBarriers* sh, int32_t* status) {
   set_status(status, TT_ERR_DEVICE_TIMEOUT);
@@ -77,8 +84,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
   uint8_t* sQ = base;                                // 2 heads
   uint8_t* sK = sQ + 2 * kTileBytes;                 // kStages
   uint8_t* sV = sK + kStages * kTileBytes;           // kStages
-  uint8_t* aux = sV + kStages * kTileBytes;          // kStages x (kv_lo, kv_hi)
-  FwdBarriers* sh = reinterpret_cast<FwdBarriers*>(aux + kStages * kAuxBytes);
+  uint8_t* aux = sV + kStages * kTileBytes;          // kAuxStages x (kv_lo, kv_hi)
+  FwdBarriers* sh = reinterpret_cast<FwdBarriers*>(aux + kAuxStages * kAuxBytes);
   const volatile int32_t* abort_flag = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -94,8 +101,10 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sh->k_full[s], 1);
       mbar_init(&sh->v_full[s], 1);
-      mbar_init(&sh->kv_empty[s], 1);
+      mbar_init(&sh->k_empty[s], 1);
+      mbar_init(&sh->v_empty[s], 1);
     }
+    for (int a = 0; a < kAuxStages; ++a) mbar_init(&sh->aux_full[a], 1);
     for (int g = 0; g < 2; ++g) {
       mbar_init(&sh->s_full[g], 1);
       mbar_init(&sh->p_full[g], 128);
@@ -125,39 +134,49 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
         tma_load_3d(sQ + g * kTileBytes, &tm_q, &sh->q_full, 0, qt * kBM, h0 + g);
         tma_load_3d(sQ + g * kTileBytes + kHalfBytes, &tm_q, &sh->q_full, 64, qt * kBM, h0 + g);
       }
-      int issued[kStages] = {0};
+      int n_k[kStages] = {0}, n_v[kStages] = {0}, n_aux[kAuxStages] = {0};
       bool ok = true;
+      // K of tile it reuses the stage once the score MMAs of tile it-2 are
+      // done, V once its PV MMAs are; those releases come in the order
+      // K(it), V(it), K(it+1), ... so one thread issues them in that order.
       for (int it = 0; it < n_it && ok; ++it) {
         const int s = it % kStages;
-        if (it >= kStages) ok = mbar_wait(&sh->kv_empty[s], ((it / kStages) - 1) & 1, abort_flag);
-        if (!ok) break;
         const int ent = fwd_list[e0 + it];
         const int kt = ent >> 1;
+        if (it >= kStages) ok = mbar_wait(&sh->k_empty[s], ((it / kStages) - 1) & 1, abort_flag);
+        if (!ok) break;
         uint8_t* k_dst = sK + s * kTileBytes;
-        uint8_t* v_dst = sV + s * kTileBytes;
-        const bool partial = ent & 1;
-        mbar_arrive_expect_tx(&sh->k_full[s], kTileBytes + (partial ? kAuxBytes : 0));
+        mbar_arrive_expect_tx(&sh->k_full[s], kTileBytes);
         tma_load_3d(k_dst, &tm_k, &sh->k_full[s], 0, kt * kBN, hk);
         tma_load_3d(k_dst + kHalfBytes, &tm_k, &sh->k_full[s], 64, kt * kBN, hk);
-        if (partial) {
-          bulk_load(aux + s * kAuxBytes, kv_lo + kt * kBN, kAuxBytes / 2, &sh->k_full[s]);
-          bulk_load(aux + s * kAuxBytes + kAuxBytes / 2, kv_hi + kt * kBN, kAuxBytes / 2,
-                    &sh->k_full[s]);
+        n_k[s] += 1;
+        if (ent & 1) {
+          // the key intervals of a partial tile: read by the softmax warps,
+          // whose progress past tile it is implied by the release of K(it+2)
+          const int a = it % kAuxStages;
+          uint8_t* a_dst = aux + a * kAuxBytes;
+          mbar_arrive_expect_tx(&sh->aux_full[a], kAuxBytes);
+          bulk_load(a_dst, kv_lo + kt * kBN, kAuxBytes / 2, &sh->aux_full[a]);
+          bulk_load(a_dst + kAuxBytes / 2, kv_hi + kt * kBN, kAuxBytes / 2, &sh->aux_full[a]);
+          n_aux[a] += 1;
         }
+        if (it >= kStages) ok = mbar_wait(&sh->v_empty[s], ((it / kStages) - 1) & 1, abort_flag);
+        if (!ok) break;
         mbar_arrive_expect_tx(&sh->v_full[s], kTileBytes);
-        tma_load_3d(v_dst, &tm_v, &sh->v_full[s], 0, kt * kBN, hk);
-        tma_load_3d(v_dst + kHalfBytes, &tm_v, &sh->v_full[s], 64, kt * kBN, hk);
-        issued[s] += 1;
+        tma_load_3d(sV + s * kTileBytes, &tm_v, &sh->v_full[s], 0, kt * kBN, hk);
+        tma_load_3d(sV + s * kTileBytes + kHalfBytes, &tm_v, &sh->v_full[s], 64, kt * kBN, hk);
+        n_v[s] += 1;
       }
       if (!ok) {
         raise_abort(sh, status);
         // let the copies already in flight land before the CTA exits
         mbar_wait(&sh->q_full, 0, nullptr);
-        for (int s = 0; s < kStages; ++s)
-          if (issued[s] > 0) {
-            mbar_wait(&sh->k_full[s], (issued[s] - 1) & 1, nullptr);
-            mbar_wait(&sh->v_full[s], (issued[s] - 1) & 1, nullptr);
-          }
+        for (int s = 0; s < kStages; ++s) {
+          if (n_k[s] > 0) mbar_wait(&sh->k_full[s], (n_k[s] - 1) & 1, nullptr);
+          if (n_v[s] > 0) mbar_wait(&sh->v_full[s], (n_v[s] - 1) & 1, nullptr);
+        }
+        for (int a = 0; a < kAuxStages; ++a)
+          if (n_aux[a] > 0) mbar_wait(&sh->aux_full[a], (n_aux[a] - 1) & 1, nullptr);
       }
     }
   } else if (warp == 1) {
@@ -183,13 +202,14 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
           mma_ts(tmem + 256 + g * 128, tmem + g * 128 + kk * 8,
                  desc_sw128(v_addr + s * kTileBytes + kk * 2048, kHalfBytes, 1024), id_o,
                  (it > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&sh->o_done[g]);
+        if (it == n_it - 1) tc_commit(&sh->o_done[g]);   // the final O_g
       };
       bool ok = mbar_wait(&sh->q_full, 0, abort_flag);
       if (ok) ok = mbar_wait(&sh->k_full[0], 0, abort_flag);
       if (ok) {
         tc_fence_after();
         for (int g = 0; g < n_heads; ++g) issue_s(g, 0);
+        tc_commit(&sh->k_empty[0]);
       }
       for (int it = 0; it < n_it && ok; ++it) {
         const int s = it % kStages;
@@ -213,7 +233,10 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
             issue_s(g, it + 1);
           }
         }
-        if (ok) tc_commit(&sh->kv_empty[s]);
+        if (ok) {
+          tc_commit(&sh->v_empty[s]);
+          if (more) tc_commit(&sh->k_empty[s1]);
+        }
       }
       if (!ok) {
         raise_abort(sh, status);
@@ -232,32 +255,27 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
     const uint32_t col_s = g * 128, col_o = 256 + g * 128;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    uint32_t aux_phase = 0;   // bit a: parity of the next load of interval stage a
     if (g < n_heads) {
       for (int it = 0; it < n_it; ++it) {
         const int ent = fwd_list[e0 + it];
         const bool partial = ent & 1;
-        const int s = it % kStages;
         ok = mbar_wait(&sh->s_full[g], it & 1, abort_flag);
-        // the key intervals arrived with the K tile (k_full); S_g completing
-        // implies K landed, the explicit wait makes the shared data visible
-        if (ok && partial) ok = mbar_wait(&sh->k_full[s], (it / kStages) & 1, abort_flag);
+        // interval stages are loaded for partial tiles only, so their phase
+        // is counted here rather than derived from it
+        const int as = it % kAuxStages;
+        if (ok && partial) {
+          ok = mbar_wait(&sh->aux_full[as], (aux_phase >> as) & 1u, abort_flag);
+          aux_phase ^= 1u << as;
+        }
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
         float sv[kBN];
-#pragma unroll
-        for (int c = 0; c < kBN / 64; ++c) {
-          float t0[32], t1[32];
-          tmem_ld32x2(lane_addr + col_s + c * 64, lane_addr + col_s + c * 64 + 32, t0, t1);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            sv[c * 64 + i] = t0[i];
-            sv[c * 64 + 32 + i] = t1[i];
-          }
-        }
+        tmem_ld128(lane_addr + col_s, sv);
         if (partial) {
-          const int4* lo4 = reinterpret_cast<const int4*>(aux + s * kAuxBytes);
-          const int4* hi4 = reinterpret_cast<const int4*>(aux + s * kAuxBytes + kAuxBytes / 2);
+          const int4* lo4 = reinterpret_cast<const int4*>(aux + as * kAuxBytes);
+          const int4* hi4 = reinterpret_cast<const int4*>(aux + as * kAuxBytes + kAuxBytes / 2);
 #pragma unroll
           for (int c = 0; c < kBN / 4; ++c) {
             const int4 a = lo4[c], z = hi4[c];
@@ -267,22 +285,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
             if (!visible(a.w, z.w, row)) sv[4 * c + 3] = -INFINITY;
           }
         }
-        // row max as 8 independent chains (a single chain is 128 dependent ops)
-        float mx8[8];
+        // row max: 3-input max over 4 independent chains
+        float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
-#pragma unroll
-        for (int c = 8; c < kBN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        for (int c = 4; c < kBN; c += 2) mx4[(c >> 1) & 3] = fmax3(mx4[(c >> 1) & 3], sv[c], sv[c + 1]);
+        const float mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
         const float m_new = fmaxf(m_run, mx * scale_log2);
-        // PV_g(it-1) must be complete before O_g may be rescaled; waiting
-        // every iteration keeps the o_done phases observed in order.
-        if (it > 0) {
-          ok = mbar_wait(&sh->o_done[g], (it - 1) & 1, abort_flag);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-        }
         float alpha = 1.f;
         bool need = false;
         if (m_run == -INFINITY) {
@@ -293,7 +301,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
           need = true;
         }
         if (__any_sync(0xffffffffu, need)) {
-          tc_fence_after();
+          // PV_g(it-1) has completed: the commit that signalled S_g(it) was
+          // issued after it, and a commit tracks every earlier MMA.
 #pragma unroll 1
           for (int c = 0; c < kD / 32; ++c) {
             float o[32];
@@ -307,27 +316,37 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
         }
         l_run *= alpha;
         const float mb = (m_run == -INFINITY) ? 0.f : m_run;
-#pragma unroll
-        float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};   // 8 independent partial sums
+        const float2 sc2 = make_float2(scale_log2, scale_log2), nmb2 = make_float2(-mb, -mb);
+        // exponentials: kEmuPer8 of every 8 column pairs on the FMA pipe, the
+        // rest on the SFU; 4 independent paired partial sums
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           uint32_t pk[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const float p0 = fast_exp2(fmaf(sv[hf * 64 + 2 * i], scale_log2, -mb));
-            const float p1 = fast_exp2(fmaf(sv[hf * 64 + 2 * i + 1], scale_log2, -mb));
-            ls[i & 7] += p0 + p1;
-            pk[i] = pack2<kBf16>(p0, p1);
+            const float2 x = ffma2(make_float2(sv[hf * 64 + 2 * i], sv[hf * 64 + 2 * i + 1]), sc2, nmb2);
+            float2 pr;
+            if ((i & 7) < kEmuPer8) {
+              pr = exp2_poly2(x);
+            } else {
+              pr.x = fast_exp2(x.x);
+              pr.y = fast_exp2(x.y);
+            }
+            acc[i & 3] = fadd2(acc[i & 3], pr);
+            pk[i] = pack2<kBf16>(pr.x, pr.y);
           }
           tmem_st32(lane_addr + col_s + hf * 32, pk);
         }
-        l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+        const float2 a01 = fadd2(acc[0], acc[1]), a23 = fadd2(acc[2], acc[3]);
+        l_run += (a01.x + a23.x) + (a01.y + a23.y);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&sh->p_full[g]);
       }
       if (ok && n_it > 0) {
-        ok = mbar_wait(&sh->o_done[g], (n_it - 1) & 1, abort_flag);
+        ok = mbar_wait(&sh->o_done[g], 0, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
       }
       if (ok) {
