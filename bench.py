@@ -46,9 +46,16 @@ def parse():
     ap.add_argument("--tokens", type=int, default=16384,
                     help="tree token budget (16384 = config 2; smaller for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["attn", "gdn"], default="attn",
+    ap.add_argument("--workload", choices=["attn", "gdn", "attn3", "e2e5"], default="attn",
                     help="attn = config 2 tree attention (the headline); gdn = config 4 tree "
-                         "conv + gated delta rule")
+                         "conv + gated delta rule; attn3 = config 3 (8 trees of 65,536 tokens, "
+                         "40/8 heads, round robin over ranks); e2e5 = config 5 (random-init "
+                         "Qwen3-4B architecture, tree_grad_hybrid on one 32k-token tree per GPU, "
+                         "gradient averaging, AdamW)")
+    ap.add_argument("--trees", type=int, default=8, help="attn3: number of trees in the job")
+    ap.add_argument("--layers", type=int, default=36, help="e2e5: decoder layers (36 = Qwen3-4B)")
+    ap.add_argument("--ckpt-mlp", type=int, default=1,
+                    help="e2e5: recompute decoder MLPs in backward (1) or save them (0)")
     return ap.parse_args()
 
 
@@ -509,12 +516,297 @@ def run_gdn(args):
     return 0
 
 
+HQ3 = 40      # config 3 heads (Hkv = 8, D = 128)
+CFG3_TOKENS = 65536
+
+
+def run_attn3(args):
+    """Config 3: 8 agentic trees of 65,536 tokens (root prefix 8,192, 32 leaves,
+    node lengths log-uniform [32, 4096], depth <= 10), 40 q / 8 kv heads, tree
+    attention fwd+bwd.  The job's trees are fixed and dealt round robin to the
+    ranks (strong scaling); one step = fwd+bwd of every tree of this rank."""
+    import tree_training_b200 as tt
+    from tree_training_b200 import _lib
+    from tree_training_b200.attention import set_phase_timer
+    from tree_training_b200.dist import assign_trees
+    from tree_training_b200.synthetic import agentic_tree
+    world, rank, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    init_dist(world, local)
+    mine = assign_trees(args.trees, world, rank)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    mk = lambda *s: (torch.randn(*s, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    trees = []
+    for i in mine:
+        roots = agentic_tree(args.seed + i, CFG3_TOKENS)
+        meta = tt.build_dfs_tree_info(roots).attn_meta()
+        n = meta.n_q
+        q, k, v = (mk(n, h, D).requires_grad_(True) for h in (HQ3, HKV, HKV))
+        trees.append(dict(roots=roots, meta=meta, q=q, k=k, v=v, do=mk(n, HQ3, D),
+                          V=meta.visible_pairs))
+    flops = sum(14.0 * D * HQ3 * t["V"] for t in trees)
+    tokens = float(sum(t["meta"].n_q for t in trees))
+
+    def step(timer=None):
+        for t in trees:
+            if timer is not None:
+                timer.new_step()
+            t["q"].grad = t["k"].grad = t["v"].grad = None
+            tt.tree_attention(t["q"], t["k"], t["v"], t["meta"]).backward(t["do"])
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    tt.check_device_status(dev)
+    barrier(world)
+    timer = PhaseTimer()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    launches0 = _lib.lib().tt_kernel_launches()
+    set_phase_timer(timer)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda._sleep(int(2e7))
+    for a, b in ev:
+        a.record()
+        step(timer)
+        b.record()
+    set_phase_timer(None)
+    torch.cuda.synchronize()
+    launches = _lib.lib().tt_kernel_launches() - launches0
+    clk = clocks.stop()
+    tt.check_device_status(dev)
+    t_step = statistics.mean(a.elapsed_time(b) for a, b in ev) / 1e3
+    t_max = max_over_ranks(t_step, world, dev)
+    flops_all = sum_over_ranks(flops, world, dev)
+    tokens_all = sum_over_ranks(tokens, world, dev)
+    kern = timer.durations()
+
+    # end to end: host packer + uploads from one pinned buffer set + fwd/bwd + downloads
+    big = max(trees, key=lambda t: t["meta"].n_q)
+    pin = lambda x: x.detach().cpu().pin_memory()
+    qh, kh, vh, doh = pin(big["q"]), pin(big["k"]), pin(big["v"]), pin(big["do"])
+    gh = [torch.empty_like(x).pin_memory() for x in (qh, kh, vh)]
+    h2d = d2h = 0
+
+    def e2e_step():
+        nonlocal h2d, d2h
+        h2d = d2h = 0
+        for t in trees:
+            m = tt.build_dfs_tree_info(t["roots"]).attn_meta()
+            n = m.n_q
+            qd, kd, vd = (x[:n].to(dev, non_blocking=True).requires_grad_(True)
+                          for x in (qh, kh, vh))
+            tt.tree_attention(qd, kd, vd, m).backward(doh[:n].to(dev, non_blocking=True))
+            for dst, src in zip(gh, (qd, kd, vd)):
+                dst[:n].copy_(src.grad, non_blocking=True)
+            h2d += sum(x[:n].numel() * x.element_size() for x in (qh, kh, vh, doh)) + m.h2d_bytes()
+            d2h += sum(x[:n].numel() * x.element_size() for x in gh)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e_ts = []
+    for _ in range(max(1, min(args.steps, 3))):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        e2e_step()
+        b.record()
+        b.synchronize()
+        e_ts.append(a.elapsed_time(b) / 1e3)
+    t_e2e = max_over_ranks(statistics.mean(e_ts), world, dev)
+    pk, pk_src = peaks()
+    Vsum = sum(t["V"] for t in trees)
+    kflops = {"attn_fwd_tc": 4.0 * D * Vsum * HQ3, "attn_bwd_dkdv_tc": 8.0 * D * Vsum * HQ3,
+              "attn_bwd_dq_tc": 6.0 * D * Vsum * HQ3}
+    kern_step = {n: t * len(trees) for n, t in kern.items()}   # durations() is per tree
+    dominant = max((n for n in kflops if n in kern_step), key=lambda n: kern_step[n],
+                   default=None)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": flops_all / t_max / 1e12, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": t_max * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "tokens_per_s": tokens_all / t_max,
+            "config": {"workload": f"config3: {args.trees} agentic trees x 65,536 tokens (root "
+                                   "prefix 8,192, 32 leaves, node len log-uniform [32,4096], "
+                                   "depth<=10), 40 q / 8 kv heads, head_dim 128, tree attention "
+                                   "fwd+bwd, trees round robin over ranks",
+                       "trees_rank0": mine, "visible_pairs_rank0": Vsum,
+                       "l2": "inputs of each tree (1.6 GB) exceed L2; no flush",
+                       "parallelism": f"dp{world} (independent trees)"},
+            "e2e": {"value": flops_all / t_e2e / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                    "ms_per_step": t_e2e * 1e3},
+            "kernel_ms_per_step": {n: t * 1e3 for n, t in kern_step.items()},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "cpu_baseline": None,
+            "cpu_baseline_note": "a 65,536-token dense mask (4 Gi entries per head batch) is "
+                                 "impractical on the host; config 2's CPU sample stands in",
+        }
+        if dominant is not None:
+            ach = kflops[dominant] / kern_step[dominant] / 1e12
+            line["roofline"] = {"bound": "tensor", "kernel": dominant, "achieved": ach,
+                                "peak": float(pk["bf16_tflops"]), "unit": "TFLOP/s",
+                                "frac": ach / float(pk["bf16_tflops"]), "traffic": None,
+                                "peak_source": f"{pk_src} bf16 dense (burst)"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def qwen3_4b_config(layers: int = 36):
+    """Qwen3-4B architecture (36 layers, hidden 2560, 32/8 heads, head_dim 128,
+    intermediate 9728, vocab 151,936, tied embeddings, rope theta 1e6)."""
+    from transformers import Qwen3Config
+    return Qwen3Config(vocab_size=151936, hidden_size=2560, intermediate_size=9728,
+                       num_hidden_layers=layers, num_attention_heads=32, num_key_value_heads=8,
+                       head_dim=128, rope_theta=1e6, max_position_embeddings=40960,
+                       tie_word_embeddings=True, rms_norm_eps=1e-6)
+
+
+def run_e2e5(args):
+    """Config 5: random-init Qwen3-4B architecture in bf16, one 32,768-token tree
+    per GPU (2-4 branching, node lengths U[64,1024]), tree_grad_hybrid with
+    max_tokens=8192 and gateway K/V through the tcgen05 tree attention, then
+    gradient averaging over ranks (NCCL, bucketed) and an AdamW step.  Metric:
+    packed tokens per second of the whole job."""
+    from transformers import Qwen3ForCausalLM
+    import tree_training_b200 as tt
+    from tree_training_b200 import _lib
+    from tree_training_b200.dist import GradAverager, RankWatch
+    from tree_training_b200.hybrid import make_tree_loss_fn, tree_grad_hybrid
+    from tree_training_b200.synthetic import random_branching_tree
+    world, rank, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    init_dist(world, local)
+    torch.manual_seed(0)
+    cfg = qwen3_4b_config(args.layers)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev):
+        model = Qwen3ForCausalLM(cfg)
+    torch.set_default_dtype(prev)
+    model.train()
+    if args.ckpt_mlp:
+        from tree_training_b200.hybrid import checkpoint_mlps
+        checkpoint_mlps(model)
+    n_params = sum(p.numel() for p in model.parameters())
+    roots = random_branching_tree(args.seed + rank, 32768, 64, 1024)
+    info = tt.build_dfs_tree_info(roots)
+    N = info.N
+    leaves = [info.nodes[c] for c in info.leaf_chunk_ids_np.tolist()]
+    lg = torch.Generator().manual_seed(7 + rank)
+    labels = [torch.randint(0, cfg.vocab_size, (len(n.token_ids),), generator=lg) for n in leaves]
+    base_fn = make_tree_loss_fn(labels, leaves, len(leaves))
+    loss_acc = torch.zeros((), dtype=torch.float32, device=dev)
+
+    def loss_fn(logits, node):
+        l = base_fn(logits, node)
+        loss_acc.add_(l.detach().float())
+        return l
+
+    avg = GradAverager(model.parameters())
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-5, fused=True)
+    watch = None
+    if world > 1:
+        import torch.distributed as dist
+        watch = RankWatch(dist.distributed_c10d._get_default_store(), rank, world, timeout_s=120)
+    step_no = [0]
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        loss_acc.zero_()
+        tree_grad_hybrid(model, roots, loss_fn, max_tokens=8192)
+        if watch is not None:
+            watch.beat(step_no[0])
+        step_no[0] += 1
+        avg.average()
+        opt.step()
+        return float(loss_acc.item())       # the step's d2h result
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    tt.check_device_status(dev)
+    barrier(world)
+    clocks = ClockSampler(dev)
+    clocks.start()
+    launches0 = _lib.lib().tt_kernel_launches()
+    ts, losses = [], []
+    for _ in range(args.steps):
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        losses.append(step())
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b) / 1e3)
+    launches = _lib.lib().tt_kernel_launches() - launches0
+    clk = clocks.stop()
+    tt.check_device_status(dev)
+    t_step = max_over_ranks(statistics.mean(ts), world, dev)
+    tokens_all = sum_over_ranks(float(N), world, dev)
+    V = info.attn_meta().visible_pairs
+    # model FLOPs of the step: 6 * params * tokens for the dense layers (gateway
+    # recompute not counted) + 14 * D * Hq * V per layer for the attention
+    model_flops = 6.0 * n_params * N + 14.0 * D * 32 * V * cfg.num_hidden_layers
+    mflops_all = sum_over_ranks(model_flops, world, dev)
+    peak_mem = torch.cuda.max_memory_allocated(dev)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": tokens_all / t_step, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "model_tflops": mflops_all / t_step / 1e12,
+            "config": {"workload": "config5: random-init Qwen3-4B architecture "
+                                   f"({cfg.num_hidden_layers} layers, hidden 2560, 32/8 heads, "
+                                   "vocab 151,936, bf16), one 32,768-token tree per GPU (2-4 "
+                                   "branching, node len U[64,1024]), tree_grad_hybrid "
+                                   "max_tokens=8192 with gateway K/V, grad average + AdamW",
+                       "tokens_per_gpu": N, "params": n_params,
+                       "parallelism": f"dp{world} (NCCL bucketed all-reduce)",
+                       "peak_mem_gb_rank0": peak_mem / 1e9,
+                       "mlp_recompute": bool(args.ckpt_mlp)},
+            "e2e": {"value": tokens_all / t_step, "unit": "tokens/s",
+                    "h2d_bytes_per_step": None, "d2h_bytes_per_step": 4,
+                    "note": "the step starts from the host tree (packing, id/label uploads "
+                            "inside tree_grad_hybrid) and ends with the loss read back"},
+            "loss_first_last": [losses[0], losses[-1]],
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "gdn":
         return run_gdn(args)
+    if args.workload == "attn3":
+        return run_attn3(args)
+    if args.workload == "e2e5":
+        return run_e2e5(args)
     return run_ours(args)
 
 

@@ -105,11 +105,13 @@ def setup():
     return model, roots, ref, leaves, labels
 
 
+@pytest.mark.parametrize("backward", ["fused", "per_leaf"])
 @pytest.mark.parametrize("max_tokens", [1000, 20, 10])
-def test_tree_grad_hybrid_matches_flat_per_path(setup, max_tokens):
+def test_tree_grad_hybrid_matches_flat_per_path(setup, max_tokens, backward):
     model, roots, ref, leaves, labels = setup
     model.zero_grad(set_to_none=True)
-    tree_grad_hybrid(model, roots, make_tree_loss_fn(labels, leaves, len(leaves)), max_tokens)
+    tree_grad_hybrid(model, roots, make_tree_loss_fn(labels, leaves, len(leaves)), max_tokens,
+                     backward=backward)
     torch.cuda.synchronize()
     tt.check_device_status(DEV)
     assert max_rel(ref, _grads(model)) < 1e-4

@@ -250,7 +250,9 @@ def _depth_of(info, c) -> int:
     return d
 
 
-def _chain_gateway_grads(gw: SubtreeGateway, retain_graph: bool) -> None:
+def _gateway_roots(gw: SubtreeGateway):
+    """(tensors, gradients) that chain the fp32 gateway gradients a partition
+    received from its children into its own graph."""
     raws, grads = [], []
     for rk, rv, ak, av in zip(gw.raw_keys, gw.raw_vals, gw.acc_k, gw.acc_v):
         if ak[0] is not None:
@@ -259,6 +261,11 @@ def _chain_gateway_grads(gw: SubtreeGateway, retain_graph: bool) -> None:
         if av[0] is not None:
             raws.append(rv)
             grads.append(av[0].to(rv.dtype))
+    return raws, grads
+
+
+def _chain_gateway_grads(gw: SubtreeGateway, retain_graph: bool) -> None:
+    raws, grads = _gateway_roots(gw)
     if raws:
         torch.autograd.backward(raws, grads, retain_graph=retain_graph)
 
@@ -275,14 +282,25 @@ def _ensure_tree_attention(model):
 
 
 def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
-                     gateway_mask: str = "tree") -> None:
+                     gateway_mask: str = "tree", backward: str = "fused") -> None:
     """Partitioned tree forward/backward (tree_grad_hybrid.py:434-539):
     partitions run top-down, each with the gateway K/V of its cut node; then
     bottom-up, each partition backpropagates its leaf losses and chains the
     fp32 gateway gradients it received into its own graph, exactly once per
-    gateway.  Accumulates parameter gradients into ``.grad``."""
+    gateway.  Accumulates parameter gradients into ``.grad``.
+
+    ``backward="fused"`` takes each partition's leaf losses and gateway
+    gradients through ONE autograd traversal of the partition graph;
+    ``"per_leaf"`` calls backward once per leaf loss and once per gateway with
+    retain_graph, as the reference does (tree_grad_hybrid.py:521-539).  Both
+    accumulate the same sum of gradients; every per-leaf call traverses the
+    whole partition graph (each leaf's logits depend on every layer of the
+    partition), so the fused form does 1/(leaves + gateways) of the backward
+    work."""
     if gateway_mask not in ("tree", "reference"):
         raise ValueError("gateway_mask must be 'tree' or 'reference'")
+    if backward not in ("fused", "per_leaf"):
+        raise ValueError("backward must be 'fused' or 'per_leaf'")
     _ensure_tree_attention(model)
     dev = next(model.parameters()).device
     parts = partition_tree(roots, max_tokens)
@@ -320,6 +338,21 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
             if g is not None and id(g) not in seen:
                 seen.add(id(g))
                 uniq.append(g)
+        if backward == "fused":
+            outs, grads = [], []
+            for s, e, orig in leaf_chunks:
+                outs.append(leaf_loss_fn(logits[:, s:e, :], orig))
+                grads.append(None)
+            for g in uniq:
+                r, gr = _gateway_roots(g)
+                outs.extend(r)
+                grads.extend(gr)
+            if outs:
+                torch.autograd.backward(outs, [torch.ones_like(o) if g is None else g
+                                               for o, g in zip(outs, grads)])
+            del logits
+            fwd.pop(id(p))
+            continue
         remaining = len(leaf_chunks) + len(uniq)
         for s, e, orig in leaf_chunks:
             remaining -= 1
@@ -347,6 +380,34 @@ def tree_grad_ckpt_sequential(model, roots, leaf_loss_fn: Callable) -> None:
         s, e = info.chunk_bounds_np[c]
         leaf_loss_fn(logits[:, int(s):int(e), :], info.nodes[c]).backward(
             retain_graph=i < len(leaves) - 1)
+
+
+def checkpoint_mlps(model) -> int:
+    """Recompute every decoder layer's MLP in the backward pass instead of
+    saving its intermediates (torch.utils.checkpoint, non-reentrant).
+
+    tree_grad_hybrid keeps the forward graph of every partition until the
+    bottom-up backward (as the reference does, tree_grad_hybrid.py:466-539), so
+    activation memory grows with the whole tree.  The MLP is the largest saved
+    block of a Qwen3 layer (gate, up, activation and product, each
+    tokens x intermediate) and touches no cache, so recomputing it changes no
+    result.  Returns the number of MLPs wrapped."""
+    import torch.utils.checkpoint as cp
+    n = 0
+    for layer in model.model.layers:
+        mlp = getattr(layer, "mlp", None)
+        if mlp is None or getattr(mlp, "_tt_checkpointed", False):
+            continue
+        fwd = mlp.forward
+
+        def run(x, _f=fwd):
+            if torch.is_grad_enabled():
+                return cp.checkpoint(_f, x, use_reentrant=False)
+            return _f(x)
+        mlp.forward = run
+        mlp._tt_checkpointed = True
+        n += 1
+    return n
 
 
 def make_tree_loss_fn(leaf_labels, leaf_nodes, n_leaves: int, ignore_index: int = -100):
