@@ -91,27 +91,33 @@ __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
 
 // D[128 x 64] = X[128 rows] * A[64 rows]^T over K = 128 dims; X is a fixed
 // 128-row tile, A a 64-row streamed sub-tile, both K-major 128-byte swizzled.
-__device__ __forceinline__ void mma_ss_n64(uint32_t d_tmem, uint32_t x_addr, uint32_t a_addr,
+// A shared-memory descriptor moved by `off` bytes: the start field holds
+// address >> 4 and shared addresses stay below 256 KiB, so the sum never
+// carries out of the field.  Lets the MMA warp build each descriptor once and
+// add constant offsets in the issue loop.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t off) { return d + (off >> 4); }
+
+// D[128 x 64] = X[128 x 128] * A[64 x 128]^T, X a fixed tile and A a streamed
+// sub-tile, both K-major (descriptors dx, da at their first byte).
+__device__ __forceinline__ void mma_ss_n64(uint32_t d_tmem, uint64_t dx, uint64_t da,
                                            uint32_t idesc) {
 #pragma unroll
   for (int kk = 0; kk < kD / 16; ++kk) {
     const uint32_t ox = (kk >> 2) * kTileHalf + (kk & 3) * 32;
     const uint32_t oa = (kk >> 2) * kSubHalf + (kk & 3) * 32;
-    mma_ss(d_tmem, desc_sw128(x_addr + ox, 16, 1024), desc_sw128(a_addr + oa, 16, 1024), idesc,
-           kk > 0 ? 1u : 0u);
+    mma_ss(d_tmem, desc_add(dx, ox), desc_add(da, oa), idesc, kk > 0 ? 1u : 0u);
   }
 }
 
 // D[128 x 128] (+)= A[128 x 64, 16-bit in TMEM] * B[64 rows x 128 dims], B a
 // streamed sub-tile read MN-major.  A's 64 columns of K sit as two 16-column
 // groups at a_tmem and a_tmem + 32 (one per elementwise warp half).
-__device__ __forceinline__ void mma_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr,
+__device__ __forceinline__ void mma_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint64_t db,
                                            uint32_t idesc, bool accumulate) {
 #pragma unroll
   for (int kk = 0; kk < kSub / 16; ++kk) {
     const uint32_t a = a_tmem + (kk < 2 ? kk * 8 : 32 + (kk - 2) * 8);
-    mma_ts(d_tmem, a, desc_sw128(b_addr + kk * 2048, kSubHalf, 1024), idesc,
-           (accumulate || kk > 0) ? 1u : 0u);
+    mma_ts(d_tmem, a, desc_add(db, kk * 2048), idesc, (accumulate || kk > 0) ? 1u : 0u);
   }
 }
 
@@ -181,14 +187,16 @@ __device__ __forceinline__ void mma_loop(BwdBarriers* sh, const volatile int32_t
                                          uint32_t x_addr, uint32_t y_addr, uint32_t ring_a,
                                          uint32_t ring_b, uint32_t id_s, Acc acc) {
   bool ok = mbar_wait(&sh->fixed_full, 0, abort_flag);
+  const uint64_t dx = desc_sw128(x_addr, 16, 1024), dy = desc_sw128(y_addr, 16, 1024);
+  const uint64_t da = desc_sw128(ring_a, 16, 1024), db = desc_sw128(ring_b, 16, 1024);
   auto sdp = [&](int u) -> bool {
     const int s = u % kStages, b = u & 1;
     const uint32_t ph = (u / kStages) & 1;
     if (!mbar_wait(&sh->a_full[s], ph, abort_flag)) return false;
     if (!mbar_wait(&sh->b_full[s], ph, abort_flag)) return false;
     tc_fence_after();
-    mma_ss_n64(tmem + 64 * b, x_addr, ring_a + s * kSubBytes, id_s);
-    mma_ss_n64(tmem + 128 + 64 * b, y_addr, ring_b + s * kSubBytes, id_s);
+    mma_ss_n64(tmem + 64 * b, dx, desc_add(da, s * kSubBytes), id_s);
+    mma_ss_n64(tmem + 128 + 64 * b, dy, desc_add(db, s * kSubBytes), id_s);
     tc_commit(&sh->sdp_full[b]);
     return true;
   };
@@ -275,11 +283,15 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
       constexpr uint32_t id_o = idesc_f16(kBf16, kT, kD, true);
       const uint32_t q_addr = smem_u32(rQ), o_addr = smem_u32(rDO);
+      // B of dV += P^T dO and dK += dS^T Q: the ring's dO / Q sub-tiles, MN-major
+      const uint64_t d_do = desc_sw128(o_addr, kSubHalf, 1024);
+      const uint64_t d_q = desc_sw128(q_addr, kSubHalf, 1024);
       mma_loop(sh, abort_flag, status, tmem, n_u, smem_u32(sK), smem_u32(sV), q_addr, o_addr,
                id_s, [&](int s, int b, bool accumulate) {
-                 mma_ts_k64(tmem + kColDV, tmem + 64 * b, o_addr + s * kSubBytes, id_o, accumulate);
-                 mma_ts_k64(tmem + kColDK, tmem + 128 + 64 * b, q_addr + s * kSubBytes, id_o,
+                 mma_ts_k64(tmem + kColDV, tmem + 64 * b, desc_add(d_do, s * kSubBytes), id_o,
                             accumulate);
+                 mma_ts_k64(tmem + kColDK, tmem + 128 + 64 * b, desc_add(d_q, s * kSubBytes),
+                            id_o, accumulate);
                });
     }
   } else {
@@ -428,9 +440,10 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
       constexpr uint32_t id_o = idesc_f16(kBf16, kT, kD, true);
       const uint32_t k_addr = smem_u32(rK);
+      const uint64_t d_k = desc_sw128(k_addr, kSubHalf, 1024);   // B of dQ += dS K, MN-major
       mma_loop(sh, abort_flag, status, tmem, n_u, smem_u32(sQ), smem_u32(sDO), k_addr,
                smem_u32(rV), id_s, [&](int s, int b, bool accumulate) {
-                 mma_ts_k64(tmem + kColDQ, tmem + 64 * b, k_addr + s * kSubBytes, id_o,
+                 mma_ts_k64(tmem + kColDQ, tmem + 64 * b, desc_add(d_k, s * kSubBytes), id_o,
                             accumulate);
                });
     }

@@ -184,23 +184,26 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
     if (lane == 0 && n_it > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kBM, kBN, false);
       constexpr uint32_t id_o = idesc_f16(kBf16, kBM, kD, true);
-      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      // descriptors built once; an address offset o adds o >> 4 (the start
+      // field holds address >> 4 and shared addresses stay below 256 KiB)
+      const uint64_t d_q = desc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t d_k = desc_sw128(smem_u32(sK), 16, 1024);
+      const uint64_t d_v = desc_sw128(smem_u32(sV), kHalfBytes, 1024);
       auto issue_s = [&](int g, int it) {
-        const int s = it % kStages;
+        const uint64_t dq = d_q + ((g * kTileBytes) >> 4);
+        const uint64_t dk = d_k + (((it % kStages) * kTileBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          mma_ss(tmem + g * 128, desc_sw128(q_addr + g * kTileBytes + off, 16, 1024),
-                 desc_sw128(k_addr + s * kTileBytes + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
+          mma_ss(tmem + g * 128, dq + off, dk + off, id_s, kk > 0 ? 1u : 0u);
         }
         tc_commit(&sh->s_full[g]);
       };
       auto issue_pv = [&](int g, int it) {
-        const int s = it % kStages;
+        const uint64_t dv = d_v + (((it % kStages) * kTileBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
-          mma_ts(tmem + 256 + g * 128, tmem + g * 128 + kk * 8,
-                 desc_sw128(v_addr + s * kTileBytes + kk * 2048, kHalfBytes, 1024), id_o,
+          mma_ts(tmem + 256 + g * 128, tmem + g * 128 + kk * 8, dv + ((kk * 2048) >> 4), id_o,
                  (it > 0 || kk > 0) ? 1u : 0u);
         if (it == n_it - 1) tc_commit(&sh->o_done[g]);   // the final O_g
       };
