@@ -24,10 +24,11 @@
 // u+1 run while the elementwise warps process sub-tile u.  TMEM (512 cols):
 //   buffer b in {0,1}: S [64b, 64b+64), dP [128+64b, 128+64b+64)
 //   dK/dV kernel: dV [256,384), dK [384,512);  dQ kernel: dQ [256,384).
-// Warps: 0 TMA producer, 1 MMA issuer, 2..9 elementwise (two warps per TMEM
-// lane quadrant; warp half h owns columns [32h, 32h+32) of each sub-tile and
-// writes its 16-bit P / dS into the first 16 of those columns, i.e. only into
-// columns it has already read, so the two warps never race).
+// Warps: 0 TMA producer, 1 S/dP MMA issuer, 2..9 elementwise (two warps per
+// TMEM lane quadrant; warp half h owns columns [32h, 32h+32) of each sub-tile
+// and writes its 16-bit P / dS into the first 16 of those columns, i.e. only
+// into columns it has already read, so the two warps never race), 10 the
+// issuer of the accumulating MMAs.
 #include <type_traits>
 
 #include "tt_sm100.cuh"
@@ -46,7 +47,7 @@ constexpr int kSubBytes = kSub * kD * 2;    // streamed sub-tile (64 rows)
 constexpr int kSubHalf = kSubBytes / 2;     // one 64-dim swizzle block of a sub-tile
 constexpr int kAuxHalf = kSub * 4;          // 64 four-byte entries
 constexpr int kAuxBytes = 2 * kAuxHalf;     // per stage: two 64-entry arrays
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;            // 11 warps (roles below)
 constexpr int kEw = 256;                    // elementwise threads
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -58,8 +59,10 @@ struct BwdBarriers {
   uint64_t ab_empty[kStages];
   uint64_t sdp_full[2];      // S and dP of a sub-tile ready (per TMEM buffer)
   uint64_t ew_full[2];       // P / dS of a sub-tile written back (256 arrivals)
+  uint64_t buf_free[2];      // the accumulating MMAs of a TMEM buffer's sub-tile finished
   uint64_t acc_done;         // every MMA of the CTA finished
-  uint64_t drain;
+  uint64_t drain;            // abort path of the S/dP issuer
+  uint64_t drain_acc;        // abort path of the accumulation issuer
   uint32_t tmem_base;
   int32_t abort;
 };
@@ -83,8 +86,11 @@ __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
     mbar_init(&sh->sdp_full[b], 1);
     mbar_init(&sh->ew_full[b], kEw);
   }
+  mbar_init(&sh->buf_free[0], 1);
+  mbar_init(&sh->buf_free[1], 1);
   mbar_init(&sh->acc_done, 1);
   mbar_init(&sh->drain, 1);
+  mbar_init(&sh->drain_acc, 1);
   sh->abort = 0;
   fence_mbar_init();
 }
@@ -177,43 +183,63 @@ __device__ __forceinline__ void produce(BwdBarriers* sh, const volatile int32_t*
   }
 }
 
-// MMA issue loop shared by both kernels.  Sub-tile u uses ring stage
-// s = u % kStages and TMEM buffer b = u % 2:
-//   sdp(u):  S_b = X * A_s^T, dP_b = Y * B_s^T   (X, Y the fixed tiles)
-//   acc(u):  the kernel's TS products reading P_b / dS_b and the stage's tiles
-template <typename Acc>
-__device__ __forceinline__ void mma_loop(BwdBarriers* sh, const volatile int32_t* abort_flag,
-                                         int32_t* status, uint32_t tmem, int n_u,
-                                         uint32_t x_addr, uint32_t y_addr, uint32_t ring_a,
-                                         uint32_t ring_b, uint32_t id_s, Acc acc) {
+// The MMAs of both kernels come from two issuing threads.  A thread that
+// issues tcgen05.mma runs at most about one MMA ahead of the tensor pipe, so
+// every barrier wait of a single issuer leaves the pipe idle; with two
+// issuers each one's waits are covered by the other's MMAs.  Sub-tile u uses
+// ring stage s = u % kStages and TMEM buffer b = u % 2:
+//   S/dP issuer (warp 1):  S_b = X * A_s^T, dP_b = Y * B_s^T  (X, Y the fixed
+//       tiles), after the stage landed and after the accumulating MMAs of
+//       sub-tile u-2 released buffer b (buf_free);
+//   accumulation issuer (warp 10): the kernel's TS products reading P_b / dS_b
+//       once the elementwise warps wrote them back (ew_full); it alone
+//       accumulates into dK/dV or dQ, in sub-tile order, so the result does
+//       not depend on how the two instruction streams interleave.
+__device__ __forceinline__ void sdp_issuer(BwdBarriers* sh, const volatile int32_t* abort_flag,
+                                           int32_t* status, uint32_t tmem, int n_u,
+                                           uint32_t x_addr, uint32_t y_addr, uint32_t ring_a,
+                                           uint32_t ring_b, uint32_t id_s) {
   bool ok = mbar_wait(&sh->fixed_full, 0, abort_flag);
   const uint64_t dx = desc_sw128(x_addr, 16, 1024), dy = desc_sw128(y_addr, 16, 1024);
   const uint64_t da = desc_sw128(ring_a, 16, 1024), db = desc_sw128(ring_b, 16, 1024);
-  auto sdp = [&](int u) -> bool {
+  for (int u = 0; u < n_u && ok; ++u) {
     const int s = u % kStages, b = u & 1;
     const uint32_t ph = (u / kStages) & 1;
-    if (!mbar_wait(&sh->a_full[s], ph, abort_flag)) return false;
-    if (!mbar_wait(&sh->b_full[s], ph, abort_flag)) return false;
+    if (u >= 2 && !(ok = mbar_wait(&sh->buf_free[b], ((u - 2) >> 1) & 1, abort_flag))) break;
+    if (!(ok = mbar_wait(&sh->a_full[s], ph, abort_flag))) break;
+    if (!(ok = mbar_wait(&sh->b_full[s], ph, abort_flag))) break;
     tc_fence_after();
     mma_ss_n64(tmem + 64 * b, dx, desc_add(da, s * kSubBytes), id_s);
     mma_ss_n64(tmem + 128 + 64 * b, dy, desc_add(db, s * kSubBytes), id_s);
     tc_commit(&sh->sdp_full[b]);
-    return true;
-  };
-  if (ok && n_u > 0) ok = sdp(0);
-  for (int u = 0; u < n_u && ok; ++u) {
-    if (u + 1 < n_u && !(ok = sdp(u + 1))) break;
-    const int b = u & 1, s = u % kStages;
-    if (!(ok = mbar_wait(&sh->ew_full[b], (u >> 1) & 1, abort_flag))) break;
-    tc_fence_after();
-    acc(s, b, u > 0);
-    tc_commit(&sh->ab_empty[s]);
   }
-  tc_commit(&sh->acc_done);
   if (!ok) {
     raise_abort(sh, status);
     tc_commit(&sh->drain);
     mbar_wait(&sh->drain, 0, nullptr);
+  }
+}
+
+template <typename Acc>
+__device__ __forceinline__ void acc_issuer(BwdBarriers* sh, const volatile int32_t* abort_flag,
+                                           int32_t* status, int n_u, Acc acc) {
+  bool ok = true;
+  for (int u = 0; u < n_u && ok; ++u) {
+    const int b = u & 1, s = u % kStages;
+    if (!(ok = mbar_wait(&sh->ew_full[b], (u >> 1) & 1, abort_flag))) break;
+    tc_fence_after();
+    acc(s, b, u > 0);
+    tc_commit(&sh->buf_free[b]);
+    // the stage's last reader: sdp(u) completed before the elementwise warps
+    // started on sub-tile u, and acc(u) waited for them
+    tc_commit(&sh->ab_empty[s]);
+  }
+  if (ok) {
+    tc_commit(&sh->acc_done);
+  } else {
+    raise_abort(sh, status);
+    tc_commit(&sh->drain_acc);
+    mbar_wait(&sh->drain_acc, 0, nullptr);
   }
 }
 
@@ -281,18 +307,21 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   } else if (warp == 1) {
     if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
+      sdp_issuer(sh, abort_flag, status, tmem, n_u, smem_u32(sK), smem_u32(sV), smem_u32(rQ),
+                 smem_u32(rDO), id_s);
+    }
+  } else if (warp == 10) {
+    if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_o = idesc_f16(kBf16, kT, kD, true);
-      const uint32_t q_addr = smem_u32(rQ), o_addr = smem_u32(rDO);
       // B of dV += P^T dO and dK += dS^T Q: the ring's dO / Q sub-tiles, MN-major
-      const uint64_t d_do = desc_sw128(o_addr, kSubHalf, 1024);
-      const uint64_t d_q = desc_sw128(q_addr, kSubHalf, 1024);
-      mma_loop(sh, abort_flag, status, tmem, n_u, smem_u32(sK), smem_u32(sV), q_addr, o_addr,
-               id_s, [&](int s, int b, bool accumulate) {
-                 mma_ts_k64(tmem + kColDV, tmem + 64 * b, desc_add(d_do, s * kSubBytes), id_o,
-                            accumulate);
-                 mma_ts_k64(tmem + kColDK, tmem + 128 + 64 * b, desc_add(d_q, s * kSubBytes),
-                            id_o, accumulate);
-               });
+      const uint64_t d_do = desc_sw128(smem_u32(rDO), kSubHalf, 1024);
+      const uint64_t d_q = desc_sw128(smem_u32(rQ), kSubHalf, 1024);
+      acc_issuer(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
+        mma_ts_k64(tmem + kColDV, tmem + 64 * b, desc_add(d_do, s * kSubBytes), id_o,
+                   accumulate);
+        mma_ts_k64(tmem + kColDK, tmem + 128 + 64 * b, desc_add(d_q, s * kSubBytes), id_o,
+                   accumulate);
+      });
     }
   } else {
     const int quad = warp & 3;
@@ -438,14 +467,16 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   } else if (warp == 1) {
     if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
+      sdp_issuer(sh, abort_flag, status, tmem, n_u, smem_u32(sQ), smem_u32(sDO), smem_u32(rK),
+                 smem_u32(rV), id_s);
+    }
+  } else if (warp == 10) {
+    if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_o = idesc_f16(kBf16, kT, kD, true);
-      const uint32_t k_addr = smem_u32(rK);
-      const uint64_t d_k = desc_sw128(k_addr, kSubHalf, 1024);   // B of dQ += dS K, MN-major
-      mma_loop(sh, abort_flag, status, tmem, n_u, smem_u32(sQ), smem_u32(sDO), k_addr,
-               smem_u32(rV), id_s, [&](int s, int b, bool accumulate) {
-                 mma_ts_k64(tmem + kColDQ, tmem + 64 * b, desc_add(d_k, s * kSubBytes), id_o,
-                            accumulate);
-               });
+      const uint64_t d_k = desc_sw128(smem_u32(rK), kSubHalf, 1024);   // B of dQ += dS K
+      acc_issuer(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
+        mma_ts_k64(tmem + kColDQ, tmem + 64 * b, desc_add(d_k, s * kSubBytes), id_o, accumulate);
+      });
     }
   } else {
     const int quad = warp & 3;
