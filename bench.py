@@ -115,6 +115,18 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def wait_ready(self, timeout_s: float = 15.0):
+        """Block until nvidia-smi delivered its first sample: its start-up
+        queries can stall this process's CUDA calls, which must not happen
+        inside a timed region."""
+        t0 = time.monotonic()
+        while self.proc is not None and not self.lines and time.monotonic() - t0 < timeout_s:
+            time.sleep(0.05)
+
+    def reset(self):
+        """Keep only samples taken from now on (the timed region)."""
+        self.lines = []
+
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -277,6 +289,9 @@ def run_ours(args):
         out = tt.tree_attention(q, k, v, meta)
         out.backward(do)
 
+    clocks = ClockSampler(dev)
+    clocks.start()
+    clocks.wait_ready()
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
@@ -285,8 +300,7 @@ def run_ours(args):
 
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     timer = PhaseTimer()
-    clocks = ClockSampler(dev)
-    clocks.start()
+    clocks.reset()
     launches0 = _lib.lib().tt_kernel_launches()
     torch.cuda.synchronize()
     barrier(world)
@@ -469,14 +483,16 @@ def run_gdn(args):
                                                           use_qk_l2norm_in_kernel=True)
         out.backward(do)
 
+    clocks = ClockSampler(dev)
+    clocks.start()
+    clocks.wait_ready()
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
-    clocks = ClockSampler(dev)
-    clocks.start()
+    clocks.reset()
     launches0 = _lib.lib().tt_kernel_launches()
     barrier(world)
     for i in range(args.steps):
@@ -555,14 +571,16 @@ def run_attn3(args):
             t["q"].grad = t["k"].grad = t["v"].grad = None
             tt.tree_attention(t["q"], t["k"], t["v"], t["meta"]).backward(t["do"])
 
+    clocks = ClockSampler(dev)
+    clocks.start()
+    clocks.wait_ready()
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
     tt.check_device_status(dev)
     barrier(world)
     timer = PhaseTimer()
-    clocks = ClockSampler(dev)
-    clocks.start()
+    clocks.reset()
     launches0 = _lib.lib().tt_kernel_launches()
     set_phase_timer(timer)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -735,13 +753,15 @@ def run_e2e5(args):
         opt.step()
         return float(loss_acc.item())       # the step's d2h result
 
+    clocks = ClockSampler(dev)
+    clocks.start()
+    clocks.wait_ready()
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
     tt.check_device_status(dev)
     barrier(world)
-    clocks = ClockSampler(dev)
-    clocks.start()
+    clocks.reset()
     launches0 = _lib.lib().tt_kernel_launches()
     ts, losses = [], []
     for _ in range(args.steps):

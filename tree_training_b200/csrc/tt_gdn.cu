@@ -39,69 +39,115 @@ struct SegDesc {
 };
 
 constexpr int kBM = 64, kBN = 64, kBK = 16;
+constexpr int kGemmThreads = 64;            // 8 x 8 threads, 8 x 8 outputs each
+constexpr int kRowPad = 4;                  // keeps 16-byte rows, spreads banks
 
-// C[i,j] = alpha * sum_k A[i,k] B[k,j] + beta * C[i,j] for each segment and
-// head (blockIdx.z); operand element (r, c) of segment s lives at
+// Two fp32 FMAs in one instruction (IEEE, no flush to zero): d = a * b + c.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// C[i,j] = alpha * sum_k A[i,k] B[k,j] + beta * C[i,j] over a list of 64 x 64
+// output tiles (tile = {segment, tm << 16 | tn}) and heads (blockIdx.z);
+// operand element (r, c) of segment s lives at
 // base + head * h_stride + off_s + r * rs_s + c * cs_s.
-__global__ void __launch_bounds__(256)
-seg_gemm(const SegDesc* __restrict__ segs, const float* __restrict__ A, long long a_hs,
-         const float* __restrict__ B, long long b_hs, float* __restrict__ C, long long c_hs,
-         float alpha, float beta) {
-  const SegDesc sd = segs[blockIdx.y];
-  const int n_tn = (sd.N + kBN - 1) / kBN;
-  const int tm = blockIdx.x / n_tn, tn = blockIdx.x % n_tn;
-  if (tm * kBM >= sd.M || sd.N <= 0) return;
+// Register-blocked: each thread owns rows {4ty..4ty+3, 32+4ty..} and columns
+// {4tx.., 32+4tx..} of the tile, reads them as float4 from shared memory and
+// accumulates with paired FMAs; the next K slice is fetched into registers
+// while the current one is multiplied (two shared buffers).
+__global__ void __launch_bounds__(kGemmThreads)
+seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
+         const float* __restrict__ A, long long a_hs, const float* __restrict__ B, long long b_hs,
+         float* __restrict__ C, long long c_hs, float alpha, float beta) {
+  const int2 tl = tiles[blockIdx.x];
+  const SegDesc sd = segs[tl.x];
+  const int tm = tl.y >> 16, tn = tl.y & 0xFFFF;
   const int h = blockIdx.z;
   const float* a = A + h * a_hs + sd.a_off;
   const float* b = B + h * b_hs + sd.b_off;
   float* c = C + h * c_hs + sd.c_off;
-  __shared__ float sa[kBK][kBM + 4];
-  __shared__ float sb[kBK][kBN + 4];
-  const int tid = threadIdx.x;
-  const int ty = tid / 16, tx = tid % 16;
-  float acc[4][4] = {};
+  __shared__ __align__(16) float sa[2][kBK][kBM + kRowPad];
+  __shared__ __align__(16) float sb[2][kBK][kBN + kRowPad];
+  const int tid = threadIdx.x, tx = tid & 7, ty = tid >> 3;
   const int i0 = tm * kBM, j0 = tn * kBN;
+  // consecutive threads walk the operand's unit-stride dimension: element i
+  // (of 16) of this thread sits at (row r0 + i*dr, k k0 + i*dk) of the A slice
+  // and (k kb0 + i*dbk, column c0 + i*dc) of the B slice
+  const bool a_kfast = sd.a_cs == 1, b_nfast = sd.b_cs == 1;
+  const int ar0 = a_kfast ? (tid >> 4) : tid, ak0 = a_kfast ? (tid & 15) : 0;
+  const int adr = a_kfast ? 4 : 0, adk = a_kfast ? 0 : 1;
+  const int bc0 = b_nfast ? tid : (tid >> 4), bk0 = b_nfast ? 0 : (tid & 15);
+  const int bdc = b_nfast ? 0 : 4, bdk = b_nfast ? 1 : 0;
+  const int astep = adr * (int)sd.a_rs + adk * (int)sd.a_cs;
+  const int bstep = bdk * (int)sd.b_rs + bdc * (int)sd.b_cs;
+  float ra[16], rb[16];
+  auto fetch = [&](int k0) {
+    const float* pa = a + (long long)(i0 + ar0) * sd.a_rs + (long long)(k0 + ak0) * sd.a_cs;
+    const float* pb = b + (long long)(k0 + bk0) * sd.b_rs + (long long)(j0 + bc0) * sd.b_cs;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const bool in_a = i0 + ar0 + i * adr < sd.M && k0 + ak0 + i * adk < sd.K;
+      ra[i] = in_a ? pa[i * astep] : 0.f;
+      const bool in_b = k0 + bk0 + i * bdk < sd.K && j0 + bc0 + i * bdc < sd.N;
+      rb[i] = in_b ? pb[i * bstep] : 0.f;
+    }
+  };
+  auto stash = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      sa[buf][ak0 + i * adk][ar0 + i * adr] = ra[i];
+      sb[buf][bk0 + i * bdk][bc0 + i * bdc] = rb[i];
+    }
+  };
+  float2 acc[8][4];
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+#pragma unroll
+    for (int w = 0; w < 4; ++w) acc[u][w] = make_float2(0.f, 0.f);
+  fetch(0);
+  stash(0);
+  __syncthreads();
+  int buf = 0;
   for (int k0 = 0; k0 < sd.K; k0 += kBK) {
-    // A tile [kBM x kBK] (stored transposed in smem); make the fastest thread
-    // index walk the unit-stride dimension
-    for (int e = tid; e < kBM * kBK; e += 256) {
-      int r, kk;
-      if (sd.a_cs == 1) { r = e / kBK; kk = e % kBK; } else { r = e % kBM; kk = e / kBM; }
-      const int gi = i0 + r, gk = k0 + kk;
-      sa[kk][r] = (gi < sd.M && gk < sd.K) ? a[gi * sd.a_rs + gk * sd.a_cs] : 0.f;
-    }
-    for (int e = tid; e < kBK * kBN; e += 256) {
-      int kk, cc;
-      if (sd.b_cs == 1) { kk = e / kBN; cc = e % kBN; } else { kk = e % kBK; cc = e / kBK; }
-      const int gk = k0 + kk, gj = j0 + cc;
-      sb[kk][cc] = (gk < sd.K && gj < sd.N) ? b[gk * sd.b_rs + gj * sd.b_cs] : 0.f;
-    }
-    __syncthreads();
+    const bool more = k0 + kBK < sd.K;
+    if (more) fetch(k0 + kBK);
 #pragma unroll
     for (int kk = 0; kk < kBK; ++kk) {
-      float av[4], bv[4];
+      const float4 a0 = *reinterpret_cast<const float4*>(&sa[buf][kk][4 * ty]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&sa[buf][kk][32 + 4 * ty]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&sb[buf][kk][4 * tx]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&sb[buf][kk][32 + 4 * tx]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float2 bv[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
+                            make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        av[u] = sa[kk][ty + 16 * u];
-        bv[u] = sb[kk][tx + 16 * u];
+      for (int u = 0; u < 8; ++u) {
+        const float2 au = make_float2(av[u], av[u]);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) acc[u][w] = fma2(au, bv[w], acc[u][w]);
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-#pragma unroll
-        for (int w = 0; w < 4; ++w) acc[u][w] = fmaf(av[u], bv[w], acc[u][w]);
     }
+    if (more) stash(buf ^ 1);
     __syncthreads();
+    buf ^= 1;
   }
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int gi = i0 + ty + 16 * u;
+  for (int u = 0; u < 8; ++u) {
+    const int gi = i0 + (u < 4 ? 4 * ty + u : 32 + 4 * ty + (u - 4));
     if (gi >= sd.M) continue;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const int gj = j0 + tx + 16 * w;
+    for (int w = 0; w < 8; ++w) {
+      const int gj = j0 + (w < 4 ? 4 * tx + w : 32 + 4 * tx + (w - 4));
       if (gj >= sd.N) continue;
-      float* p = c + gi * sd.c_rs + gj * sd.c_cs;
-      *p = alpha * acc[u][w] + (beta != 0.f ? beta * *p : 0.f);
+      const float v = (w & 1) ? acc[u][w >> 1].y : acc[u][w >> 1].x;
+      float* pc = c + gi * sd.c_rs + gj * sd.c_cs;
+      *pc = alpha * v + (beta != 0.f ? beta * *pc : 0.f);
     }
   }
 }
@@ -556,17 +602,28 @@ struct Bufs {
   int *d_start, *d_len, *d_parent, *d_child_ptr, *d_child_idx, *d_roots, *d_level_nodes;
   long long* d_loff;
   SegDesc* d_desc;
+  int2* d_tiles;
 };
 
-// Descriptor sets: built on the host in one vector, copied once.
-struct DescSet { int first, count; };
+// Descriptor sets: built on the host in one vector, copied once, with the
+// exact list of 64 x 64 output tiles of each set (so no block of a launch
+// lands outside its segment).
+struct DescSet { int first, count, tfirst, tcount; };
 
 struct Builder {
   const Plan& p;
   std::vector<SegDesc> all;
+  std::vector<int2> tiles;
   explicit Builder(const Plan& pl) : p(pl) {}
   DescSet add(const std::vector<SegDesc>& v) {
-    DescSet d{(int)all.size(), (int)v.size()};
+    DescSet d{(int)all.size(), (int)v.size(), (int)tiles.size(), 0};
+    for (size_t i = 0; i < v.size(); ++i) {
+      const int tms = (v[i].M + kBM - 1) / kBM, tns = (v[i].N + kBN - 1) / kBN;
+      for (int tm = 0; tm < tms; ++tm)
+        for (int tn = 0; tn < tns; ++tn)
+          tiles.push_back(make_int2((int)all.size() + (int)i, (tm << 16) | tn));
+    }
+    d.tcount = (int)tiles.size() - d.tfirst;
     all.insert(all.end(), v.begin(), v.end());
     return d;
   }
@@ -582,13 +639,14 @@ SegDesc desc(int M, int N, int K, long long ao, long long ars, long long acs, lo
   return d;
 }
 
-void launch_gemm(const SegDesc* d_desc, DescSet ds, int max_m, int max_n, int H, const float* A,
+// Tiles address segments by their index in the whole descriptor array.
+void launch_gemm(const SegDesc* d_desc, const int2* d_tiles, DescSet ds, int H, const float* A,
                  long long a_hs, const float* B, long long b_hs, float* C, long long c_hs,
                  float alpha, float beta, cudaStream_t st) {
-  if (ds.count == 0 || max_m <= 0 || max_n <= 0) return;
-  const int tiles = ((max_m + kBM - 1) / kBM) * ((max_n + kBN - 1) / kBN);
-  dim3 grid(tiles, ds.count, H);
-  seg_gemm<<<grid, 256, 0, st>>>(d_desc + ds.first, A, a_hs, B, b_hs, C, c_hs, alpha, beta);
+  if (ds.tcount == 0) return;
+  dim3 grid(ds.tcount, 1, H);
+  seg_gemm<<<grid, kGemmThreads, 0, st>>>(d_desc, d_tiles + ds.tfirst, A, a_hs, B, b_hs, C, c_hs,
+                                          alpha, beta);
   tt_count_launches(1);
 }
 
@@ -742,6 +800,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   b.d_level_nodes = ar.get<int>(std::max<size_t>(1, level_nodes.size()));
   b.d_loff = ar.get<long long>(n);
   b.d_desc = ar.get<SegDesc>((long long)bd.all.size());
+  b.d_tiles = ar.get<int2>((long long)bd.tiles.size());
   if (ar.sizing) return TT_OK;
   if (ar.used > ar.cap) return TT_ERR_WORKSPACE;
   auto h2d = [&](void* dst, const void* src, size_t bytes) -> int {
@@ -759,6 +818,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   rc |= h2d(b.d_level_nodes, level_nodes.data(), level_nodes.size() * 4);
   rc |= h2d(b.d_loff, p.loff.data(), n * 8);
   rc |= h2d(b.d_desc, bd.all.data(), bd.all.size() * sizeof(SegDesc));
+  rc |= h2d(b.d_tiles, bd.tiles.data(), bd.tiles.size() * sizeof(int2));
   if (rc != TT_OK) return TT_ERR_CUDA;
 
   const int max_l = p.max_len;
@@ -772,28 +832,28 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
                                              l2norm, q_scale, b.Q, b.K, b.Vb, b.Kb, b.Kbg, b.Qg,
                                              b.Kd);
   launches += 2;
-  launch_gemm(b.d_desc, ds_kk, max_l, max_l, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, ds_kk, max_l, max_l, H, b.Q, vk, b.K, vk, b.QK, llh, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_kk, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_kk, H, b.Q, vk, b.K, vk, b.QK, llh, 1.f, 0.f, st);
   decay_masks<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.gam,
                                                  b.KK, b.QK, b.Am, b.Aqk);
   ++launches;
   // U = Vb + A Vb + A (A Vb);  W = Kbg + A Kbg + A (A Kbg)
-  launch_gemm(b.d_desc, ds_av, max_l, Dv, H, b.Am, llh, b.Vb, vv, b.T1, vv, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.Vb, vv, b.T1, vv, 1.f, 0.f, st);
   add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.Vb, b.T1, b.U);
-  launch_gemm(b.d_desc, ds_av, max_l, Dv, H, b.Am, llh, b.T1, vv, b.U, vv, 1.f, 1.f, st);
-  launch_gemm(b.d_desc, ds_ak, max_l, Dk, H, b.Am, llh, b.Kbg, vk, b.T1, vk, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.T1, vv, b.U, vv, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.Kbg, vk, b.T1, vk, 1.f, 0.f, st);
   add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.Kbg, b.T1, b.W);
-  launch_gemm(b.d_desc, ds_ak, max_l, Dk, H, b.Am, llh, b.T1, vk, b.W, vk, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.T1, vk, b.W, vk, 1.f, 1.f, st);
   copy_array<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.U, b.Vn);
   init_state<<<blocks(sh), 256, 0, st>>>(sh, init, b.states);
   launches += 4;
   for (size_t d = 0; d < p.levels.size(); ++d) {
     const int cnt = (int)p.levels[d].size();
     // states are [n+1][H][Dk][Dv]: per-head stride DkDv, segment offsets cover (c+1)*H*DkDv
-    launch_gemm(b.d_desc, ds_ws[d], max_l, Dv, H, b.W, vk, b.states, DkDv, b.Vn, vv, -1.f, 1.f, st);
-    launch_gemm(b.d_desc, ds_qs[d], max_l, Dv, H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f, st);
-    launch_gemm(b.d_desc, ds_aqv[d], max_l, Dv, H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f, st);
-    launch_gemm(b.d_desc, ds_kdv[d], Dk, Dv, H, b.Kd, vk, b.Vn, vv, b.states, DkDv, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_ws[d], H, b.W, vk, b.states, DkDv, b.Vn, vv, -1.f, 1.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_qs[d], H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_aqv[d], H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_kdv[d], H, b.Kd, vk, b.Vn, vv, b.states, DkDv, 1.f, 0.f, st);
     state_decay_add<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
         H, DkDv, n, b.d_level_nodes + level_first[d], b.d_parent, b.gl, b.states);
     ++launches;
@@ -816,32 +876,32 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     gather_dstate<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
         H, DkDv, n, b.d_level_nodes + level_first[d], b.d_child_ptr, b.d_child_idx, b.dSi, dlast,
         b.dSo);
-    launch_gemm(b.d_desc, ds_dvn1[d], max_l, Dv, H, b.Aqk, llh, b.dO, vv, b.dVn, vv, 1.f, 0.f, st);
-    launch_gemm(b.d_desc, ds_dvn2[d], max_l, Dv, H, b.Kd, vk, b.dSo, DkDv, b.dVn, vv, 1.f, 1.f, st);
-    launch_gemm(b.d_desc, ds_dsi1[d], Dk, Dv, H, b.Qg, vk, b.dO, vv, b.dSi, DkDv, 1.f, 0.f, st);
-    launch_gemm(b.d_desc, ds_dsi2[d], Dk, Dv, H, b.W, vk, b.dVn, vv, b.dSi, DkDv, -1.f, 1.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_dvn1[d], H, b.Aqk, llh, b.dO, vv, b.dVn, vv, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_dvn2[d], H, b.Kd, vk, b.dSo, DkDv, b.dVn, vv, 1.f, 1.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_dsi1[d], H, b.Qg, vk, b.dO, vv, b.dSi, DkDv, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_dsi2[d], H, b.W, vk, b.dVn, vv, b.dSi, DkDv, -1.f, 1.f, st);
     dstate_decay<<<dim3(cnt, H), 256, 0, st>>>(H, DkDv, n, b.d_level_nodes + level_first[d],
                                                b.d_parent, b.gl, b.states, b.dSo, b.dSi, b.dgl);
     launches += 2;
   }
   // per-node gradients, no more dependencies between nodes
-  launch_gemm(b.d_desc, ds_dqg, max_l, Dk, H, b.dO, vv, b.states, DkDv, b.dQg, vk, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, ds_dkd, max_l, Dk, H, b.Vn, vv, b.dSo, DkDv, b.dKd, vk, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, ds_dw, max_l, Dk, H, b.dVn, vv, b.states, DkDv, b.dW, vk, -1.f, 0.f, st);
-  launch_gemm(b.d_desc, ds_daqk, max_l, max_l, H, b.dO, vv, b.Vn, vv, b.dAqk, llh, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, ds_dt1, max_l, max_l, H, b.dVn, vv, b.Vb, vv, b.dT, llh, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, ds_dt2, max_l, max_l, H, b.dW, vk, b.Kbg, vk, b.dT, llh, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_dqg, H, b.dO, vv, b.states, DkDv, b.dQg, vk, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_dkd, H, b.Vn, vv, b.dSo, DkDv, b.dKd, vk, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_dw, H, b.dVn, vv, b.states, DkDv, b.dW, vk, -1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_daqk, H, b.dO, vv, b.Vn, vv, b.dAqk, llh, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_dt1, H, b.dVn, vv, b.Vb, vv, b.dT, llh, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_dt2, H, b.dW, vk, b.Kbg, vk, b.dT, llh, 1.f, 1.f, st);
   // dA = dT + dT A^T + A^T dT  (masked in grad_masks)
   copy_array<<<blocks(H * llh), 256, 0, st>>>(H * llh, b.dT, b.dA);
-  launch_gemm(b.d_desc, ds_x1, max_l, max_l, H, b.dT, llh, b.Am, llh, b.dA, llh, 1.f, 1.f, st);
-  launch_gemm(b.d_desc, ds_x2, max_l, max_l, H, b.Am, llh, b.dT, llh, b.dA, llh, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_x1, H, b.dT, llh, b.Am, llh, b.dA, llh, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_x2, H, b.Am, llh, b.dT, llh, b.dA, llh, 1.f, 1.f, st);
   // dVb = T^T dVn = dVn + A^T dVn + A^T (A^T dVn);  dKbg = T^T dW
-  launch_gemm(b.d_desc, ds_tvt, max_l, Dv, H, b.Am, llh, b.dVn, vv, b.T1, vv, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_tvt, H, b.Am, llh, b.dVn, vv, b.T1, vv, 1.f, 0.f, st);
   add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.dVn, b.T1, b.dVb);
-  launch_gemm(b.d_desc, ds_tvt, max_l, Dv, H, b.Am, llh, b.T1, vv, b.dVb, vv, 1.f, 1.f, st);
-  launch_gemm(b.d_desc, ds_tkt, max_l, Dk, H, b.Am, llh, b.dW, vk, b.T1, vk, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_tvt, H, b.Am, llh, b.T1, vv, b.dVb, vv, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_tkt, H, b.Am, llh, b.dW, vk, b.T1, vk, 1.f, 0.f, st);
   add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.dW, b.T1, b.dKbg);
-  launch_gemm(b.d_desc, ds_tkt, max_l, Dk, H, b.Am, llh, b.T1, vk, b.dKbg, vk, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_tkt, H, b.Am, llh, b.T1, vk, b.dKbg, vk, 1.f, 1.f, st);
   launches += 3;
   // masks: dA -> G = -dA*D, dAqk -> F = dAqk*D, dDD
   TT_CUDA_OK(cudaMemsetAsync(b.dgam, 0, (size_t)H * S * 4, st));
@@ -851,10 +911,10 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
                                                 b.dgam);
   launches += 2;
   // dKb = G K ; dK = G^T Kb + F^T Q ; dQ = F K
-  launch_gemm(b.d_desc, ds_gk, max_l, Dk, H, b.dA, llh, b.K, vk, b.dKb, vk, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, ds_gtk, max_l, Dk, H, b.dA, llh, b.Kb, vk, b.dK, vk, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, ds_gtk, max_l, Dk, H, b.dAqk, llh, b.Q, vk, b.dK, vk, 1.f, 1.f, st);
-  launch_gemm(b.d_desc, ds_gk, max_l, Dk, H, b.dAqk, llh, b.K, vk, b.dQ, vk, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_gk, H, b.dA, llh, b.K, vk, b.dKb, vk, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_gtk, H, b.dA, llh, b.Kb, vk, b.dK, vk, 1.f, 0.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_gtk, H, b.dAqk, llh, b.Q, vk, b.dK, vk, 1.f, 1.f, st);
+  launch_gemm(b.d_desc, b.d_tiles, ds_gk, H, b.dAqk, llh, b.K, vk, b.dQ, vk, 1.f, 0.f, st);
   kd_dot_kernel<<<dim3(S, H), 128, 0, st>>>(S, Dk, b.Kd, b.dKd, b.kd_dot);
   assemble_token_grads<T><<<dim3(S, H), 128, 0, st>>>(
       S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok, l2norm, q_scale, b.dQ, b.dQg, b.dK,
