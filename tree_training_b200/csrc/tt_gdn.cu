@@ -39,7 +39,7 @@ struct SegDesc {
 };
 
 constexpr int kBM = 64, kBN = 64, kBK = 16;
-constexpr int kGemmThreads = 64;            // 8 x 8 threads, 8 x 8 outputs each
+constexpr int kGemmThreads = 128;           // 16 x 8 threads, 8 x 4 outputs each
 constexpr int kRowPad = 4;                  // keeps 16-byte rows, spreads banks
 
 // Two fp32 FMAs in one instruction (IEEE, no flush to zero): d = a * b + c.
@@ -57,10 +57,10 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 // output tiles (tile = {segment, tm << 16 | tn}) and heads (blockIdx.z);
 // operand element (r, c) of segment s lives at
 // base + head * h_stride + off_s + r * rs_s + c * cs_s.
-// Register-blocked: each thread owns rows {4ty..4ty+3, 32+4ty..} and columns
-// {4tx.., 32+4tx..} of the tile, reads them as float4 from shared memory and
-// accumulates with paired FMAs; the next K slice is fetched into registers
-// while the current one is multiplied (two shared buffers).
+// Register-blocked: each of the 128 threads owns rows {4ty..4ty+3,
+// 32+4ty..} and columns {4tx..4tx+3} of the tile, reads them as float4 from
+// shared memory and accumulates with paired FMAs; the next K slice is fetched
+// into registers while the current one is multiplied (two shared buffers).
 __global__ void __launch_bounds__(kGemmThreads)
 seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
          const float* __restrict__ A, long long a_hs, const float* __restrict__ B, long long b_hs,
@@ -74,24 +74,24 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
   float* c = C + h * c_hs + sd.c_off;
   __shared__ __align__(16) float sa[2][kBK][kBM + kRowPad];
   __shared__ __align__(16) float sb[2][kBK][kBN + kRowPad];
-  const int tid = threadIdx.x, tx = tid & 7, ty = tid >> 3;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int i0 = tm * kBM, j0 = tn * kBN;
   // consecutive threads walk the operand's unit-stride dimension: element i
-  // (of 16) of this thread sits at (row r0 + i*dr, k k0 + i*dk) of the A slice
-  // and (k kb0 + i*dbk, column c0 + i*dc) of the B slice
+  // (of 8) of this thread sits at (row ar0 + i*adr, k ak0 + i*adk) of the A
+  // slice and (k bk0 + i*bdk, column bc0 + i*bdc) of the B slice
   const bool a_kfast = sd.a_cs == 1, b_nfast = sd.b_cs == 1;
-  const int ar0 = a_kfast ? (tid >> 4) : tid, ak0 = a_kfast ? (tid & 15) : 0;
-  const int adr = a_kfast ? 4 : 0, adk = a_kfast ? 0 : 1;
-  const int bc0 = b_nfast ? tid : (tid >> 4), bk0 = b_nfast ? 0 : (tid & 15);
-  const int bdc = b_nfast ? 0 : 4, bdk = b_nfast ? 1 : 0;
+  const int ar0 = a_kfast ? (tid >> 4) : (tid & 63), ak0 = a_kfast ? (tid & 15) : (tid >> 6);
+  const int adr = a_kfast ? 8 : 0, adk = a_kfast ? 0 : 2;
+  const int bc0 = b_nfast ? (tid & 63) : (tid >> 4), bk0 = b_nfast ? (tid >> 6) : (tid & 15);
+  const int bdc = b_nfast ? 0 : 8, bdk = b_nfast ? 2 : 0;
   const int astep = adr * (int)sd.a_rs + adk * (int)sd.a_cs;
   const int bstep = bdk * (int)sd.b_rs + bdc * (int)sd.b_cs;
-  float ra[16], rb[16];
+  float ra[8], rb[8];
   auto fetch = [&](int k0) {
     const float* pa = a + (long long)(i0 + ar0) * sd.a_rs + (long long)(k0 + ak0) * sd.a_cs;
     const float* pb = b + (long long)(k0 + bk0) * sd.b_rs + (long long)(j0 + bc0) * sd.b_cs;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       const bool in_a = i0 + ar0 + i * adr < sd.M && k0 + ak0 + i * adk < sd.K;
       ra[i] = in_a ? pa[i * astep] : 0.f;
       const bool in_b = k0 + bk0 + i * bdk < sd.K && j0 + bc0 + i * bdc < sd.N;
@@ -100,16 +100,14 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
   };
   auto stash = [&](int buf) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       sa[buf][ak0 + i * adk][ar0 + i * adr] = ra[i];
       sb[buf][bk0 + i * bdk][bc0 + i * bdc] = rb[i];
     }
   };
-  float2 acc[8][4];
+  float2 acc[8][2];
 #pragma unroll
-  for (int u = 0; u < 8; ++u)
-#pragma unroll
-    for (int w = 0; w < 4; ++w) acc[u][w] = make_float2(0.f, 0.f);
+  for (int u = 0; u < 8; ++u) acc[u][0] = acc[u][1] = make_float2(0.f, 0.f);
   fetch(0);
   stash(0);
   __syncthreads();
@@ -122,15 +120,13 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
       const float4 a0 = *reinterpret_cast<const float4*>(&sa[buf][kk][4 * ty]);
       const float4 a1 = *reinterpret_cast<const float4*>(&sa[buf][kk][32 + 4 * ty]);
       const float4 b0 = *reinterpret_cast<const float4*>(&sb[buf][kk][4 * tx]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&sb[buf][kk][32 + 4 * tx]);
       const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float2 bv[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
-                            make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
+      const float2 bv0 = make_float2(b0.x, b0.y), bv1 = make_float2(b0.z, b0.w);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const float2 au = make_float2(av[u], av[u]);
-#pragma unroll
-        for (int w = 0; w < 4; ++w) acc[u][w] = fma2(au, bv[w], acc[u][w]);
+        acc[u][0] = fma2(au, bv0, acc[u][0]);
+        acc[u][1] = fma2(au, bv1, acc[u][1]);
       }
     }
     if (more) stash(buf ^ 1);
@@ -142,8 +138,8 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
     const int gi = i0 + (u < 4 ? 4 * ty + u : 32 + 4 * ty + (u - 4));
     if (gi >= sd.M) continue;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      const int gj = j0 + (w < 4 ? 4 * tx + w : 32 + 4 * tx + (w - 4));
+    for (int w = 0; w < 4; ++w) {
+      const int gj = j0 + 4 * tx + w;
       if (gj >= sd.N) continue;
       const float v = (w & 1) ? acc[u][w >> 1].y : acc[u][w >> 1].x;
       float* pc = c + gi * sd.c_rs + gj * sd.c_cs;
