@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--tokens", type=int, default=16384,
                     help="tree token budget (16384 = config 2; smaller for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's SDPA + dense-mask GPU path (config 2)")
     ap.add_argument("--workload", choices=["attn", "gdn", "attn3", "e2e5"], default="attn",
                     help="attn = config 2 tree attention (the headline); gdn = config 4 tree "
                          "conv + gated delta rule; attn3 = config 3 (8 trees of 65,536 tokens, "
@@ -233,6 +235,63 @@ def cpu_baseline_sample(meta, V, hq=4, hkv=1):
             "sample": f"fwd+bwd of {hq} q heads / {hkv} kv head (of {HQ}/{HKV}) over the full "
                       f"{meta.n_q}-token tree, bf16, transformers sdpa_attention_forward with "
                       f"the dense additive mask on {torch.get_num_threads()} threads"}
+
+
+def reference_gpu_sample(meta, dev, V, reps: int = 3):
+    """The reference's own GPU path on the same tree, for comparison with the
+    tcgen05 kernels: the dense additive [1, 1, N, N] mask the reference builds
+    (dfs_tree_forward.py:548-550) handed to transformers' sdpa_attention_forward
+    (TF/integrations/sdpa_attention.py:40-104; it repeats K/V over the GQA
+    group when a mask is given), fwd + autograd bwd, all 32 q / 8 kv heads,
+    bf16.  Reports useful TFLOP/s on the same visible-pair count and which
+    SDPA backend PyTorch dispatched to."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+    N = meta.n_q
+    allowed = torch.from_numpy(meta.dense_mask()).to(dev)
+    mask = torch.zeros((1, 1, N, meta.n_kv), dtype=torch.bfloat16, device=dev)
+    mask.masked_fill_(~allowed, float("-inf"))
+    del allowed
+    g = torch.Generator(device=dev).manual_seed(7)
+    mk = lambda *sh: (torch.randn(*sh, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    q, k, v = mk(1, HQ, N, D), mk(1, HKV, meta.n_kv, D), mk(1, HKV, meta.n_kv, D)
+    do = mk(1, N, HQ, D)
+
+    class _Mod(torch.nn.Module):
+        num_key_value_groups = HQ // HKV
+        is_causal = True
+
+    mod = _Mod()
+    try:
+        from torch.nn.attention import SDPBackend
+        kr = k.repeat_interleave(HQ // HKV, dim=1)
+        choice = torch._fused_sdp_choice(q, kr, kr, attn_mask=mask, dropout_p=0.0,
+                                         is_causal=False, scale=D ** -0.5, enable_gqa=False)
+        backend = SDPBackend(choice).name
+        del kr
+    except Exception as e:  # noqa: BLE001 - informational only
+        backend = f"unknown ({type(e).__name__})"
+
+    def run():
+        qq, kk, vv = (x.detach().requires_grad_(True) for x in (q, k, v))
+        out, _ = sdpa_attention_forward(mod, qq, kk, vv, mask, dropout=0.0, scaling=D ** -0.5)
+        out.backward(do)
+
+    run()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        run()
+    b.record()
+    b.synchronize()
+    t = a.elapsed_time(b) / 1e3 / reps
+    del mask
+    torch.cuda.empty_cache()
+    return {"value": 14.0 * D * V * HQ / t / 1e12, "unit": "TFLOP/s", "ms_per_step": t * 1e3,
+            "sdpa_backend": backend,
+            "path": "transformers sdpa_attention_forward + dense additive mask (the reference's "
+                    "attention call), same tree and heads, bf16, fwd+bwd, 1 GPU"}
 
 
 def run_reference(args):
@@ -424,6 +483,8 @@ def run_ours(args):
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample(meta, V)
+        if world == 1 and not args.no_reference_gpu:
+            line["reference_gpu"] = reference_gpu_sample(meta, dev, V)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
