@@ -250,15 +250,21 @@ int tt_tree_conv_fwd(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
                      void* stream);
 
 /* dout [C, S] -> dx [C, S] (`dtype`), dweight fp32 [C, K], dbias fp32 [C] (or
- * NULL).  Deterministic: dx gathers over each token's successors (succ CSR from
- * tt_conv_successors), dweight/dbias reduce per channel without atomics. */
+ * NULL).  Deterministic: the SiLU-gradient term is computed once per (channel,
+ * token) into `workspace` (at least tt_tree_conv_bwd_workspace_size bytes,
+ * else TT_ERR_WORKSPACE), dx gathers it over each token's successors (succ
+ * CSR from tt_conv_successors), dweight/dbias sum per-block partials in a
+ * fixed order (no atomics). */
 int tt_conv_successors(int32_t S, int32_t K, const int32_t* pred, int32_t* succ_ptr,
                        int32_t* succ_tok, int32_t* succ_lag, int64_t cap);
+
+int64_t tt_tree_conv_bwd_workspace_size(int32_t C, int32_t S, int32_t K);
 
 int tt_tree_conv_bwd(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
                      const float* weight, const float* bias, const int32_t* pred,
                      const int32_t* succ_ptr, const int32_t* succ_tok, const int32_t* succ_lag,
-                     const void* dout, void* dx, float* dweight, float* dbias, void* stream);
+                     const void* dout, void* dx, float* dweight, float* dbias,
+                     void* workspace, int64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -66,8 +66,9 @@ SIGNATURES = {
     "tt_conv_predecessors": (_INT, [_I32, _P, _P, _I32, _P]),
     "tt_conv_successors": (_INT, [_I32, _I32, _P, _P, _P, _P, _I64]),
     "tt_tree_conv_fwd": (_INT, [_INT, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),
+    "tt_tree_conv_bwd_workspace_size": (_I64, [_I32, _I32, _I32]),
     "tt_tree_conv_bwd": (_INT, [_INT, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                _P, _P, _P]),
+                                _P, _P, _P, _I64, _P]),
 }
 
 _lib = None

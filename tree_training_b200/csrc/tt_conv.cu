@@ -93,67 +93,109 @@ __global__ void conv_fwd(int C, int S, int K, const T* __restrict__ x, const flo
   out[(int64_t)c * S + t] = from_f32<T>(silu(pre));
 }
 
-template <typename T>
-__device__ __forceinline__ float dpre_at(const T* xc, const T* dyc, const float* wc, float b,
-                                         const int32_t* pred, int t, int K) {
-  const float pre = conv_pre(xc, wc, b, pred, t, K);
-  const float sg = 1.f / (1.f + __expf(-pre));
-  return to_f32(dyc[t]) * sg * (1.f + pre * (1.f - sg));
-}
+constexpr int kConvTok = 256;   // tokens per block (one per thread)
+constexpr int kConvCh = 8;      // channels per thread: the token's predecessor and
+                                // successor indices are read once for all of them
+constexpr int kPartW = 9;       // per (channel, block): dw[0..K-1], db at [8]
 
+// dpre[c][t] = dy * d silu(pre)/d pre at every (channel, token), and per block
+// of 256 tokens the partial sums of dw[c][j] = sum_t dpre x[pred_{K-1-j}(t)]
+// and db[c] = sum_t dpre (reduced in a fixed order by conv_bwd_dw_reduce).
 template <typename T>
-__global__ void conv_bwd_dx(int C, int S, int K, const T* __restrict__ x,
-                            const float* __restrict__ w, const float* __restrict__ bias,
-                            const int32_t* __restrict__ pred, const int32_t* __restrict__ sp,
-                            const int32_t* __restrict__ stok, const int32_t* __restrict__ slag,
-                            const T* __restrict__ dy, T* dx) {
-  const int c = blockIdx.y;
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= S) return;
-  const T* xc = x + (int64_t)c * S;
-  const T* dyc = dy + (int64_t)c * S;
-  const float* wc = w + (int64_t)c * K;
-  const float b = bias ? bias[c] : 0.f;
-  float acc = wc[K - 1] * dpre_at(xc, dyc, wc, b, pred, t, K);
-  for (int e = sp[t]; e < sp[t + 1]; ++e)
-    acc = fmaf(wc[K - 1 - slag[e]], dpre_at(xc, dyc, wc, b, pred, stok[e], K), acc);
-  dx[(int64_t)c * S + t] = from_f32<T>(acc);
-}
-
-template <typename T>
-__global__ void conv_bwd_dw(int C, int S, int K, const T* __restrict__ x,
-                            const float* __restrict__ w, const float* __restrict__ bias,
-                            const int32_t* __restrict__ pred, const T* __restrict__ dy, float* dw,
-                            float* db) {
-  const int c = blockIdx.x;
-  const T* xc = x + (int64_t)c * S;
-  const T* dyc = dy + (int64_t)c * S;
-  const float* wc = w + (int64_t)c * K;
-  const float b = bias ? bias[c] : 0.f;
-  float acc[9] = {};
-  for (int t = threadIdx.x; t < S; t += blockDim.x) {
-    const float d = dpre_at(xc, dyc, wc, b, pred, t, K);
-    acc[K - 1] += d * to_f32(xc[t]);
-    for (int m = 1; m < K; ++m) {
-      const int p = pred[(int64_t)t * (K - 1) + m - 1];
-      if (p >= 0) acc[K - 1 - m] += d * to_f32(xc[p]);
+__global__ void __launch_bounds__(kConvTok)
+conv_bwd_dpre(int C, int S, int K, const T* __restrict__ x, const float* __restrict__ w,
+              const float* __restrict__ bias, const int32_t* __restrict__ pred,
+              const T* __restrict__ dy, float* __restrict__ dpre, float* __restrict__ part,
+              int nb) {
+  const int t = blockIdx.x * kConvTok + threadIdx.x;
+  const int c0 = blockIdx.y * kConvCh;
+  const bool live = t < S;
+  int pr[7];
+#pragma unroll
+  for (int m = 0; m < 7; ++m)
+    pr[m] = (live && m < K - 1) ? pred[(int64_t)t * (K - 1) + m] : -1;
+  __shared__ float red[kConvCh][kPartW][kConvTok / 32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int cc = 0; cc < kConvCh; ++cc) {
+    const int c = c0 + cc;
+    if (c >= C) break;                       // the same for the whole block
+    const T* xc = x + (int64_t)c * S;
+    const float* wc = w + (int64_t)c * K;
+    float xs[8], d = 0.f;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) xs[m] = 0.f;
+    if (live) {
+      xs[0] = to_f32(xc[t]);
+      float pre = (bias ? bias[c] : 0.f) + wc[K - 1] * xs[0];
+#pragma unroll
+      for (int m = 1; m < 8; ++m)
+        if (m < K && pr[m - 1] >= 0) {
+          xs[m] = to_f32(xc[pr[m - 1]]);
+          pre = fmaf(wc[K - 1 - m], xs[m], pre);
+        }
+      const float sg = 1.f / (1.f + __expf(-pre));
+      d = to_f32(dy[(int64_t)c * S + t]) * sg * (1.f + pre * (1.f - sg));
+      dpre[(int64_t)c * S + t] = d;
     }
-    acc[8] += d;
-  }
-  __shared__ float red[9][32];
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int i = 0; i < 9; ++i) {
-    float v = acc[i];
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) red[i][wid] = v;
+#pragma unroll
+    for (int j = 0; j < kPartW; ++j) {
+      // j < K: weight index j, i.e. predecessor m = K-1-j; j = 8: bias
+      float v = j == 8 ? d : (j < K ? d * xs[K - 1 - j] : 0.f);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) red[cc][j][wid] = v;
+    }
   }
   __syncthreads();
-  if (threadIdx.x < 9) {
+  const int n_ch = min(kConvCh, C - c0);
+  for (int i = threadIdx.x; i < n_ch * kPartW; i += kConvTok) {
+    const int cc = i / kPartW, j = i % kPartW;
     float v = 0.f;
-    for (int i = 0; i < nw; ++i) v += red[threadIdx.x][i];
-    if (threadIdx.x < K) dw[(int64_t)c * K + threadIdx.x] = v;
-    if (threadIdx.x == 8 && db) db[c] = v;
+#pragma unroll
+    for (int q = 0; q < kConvTok / 32; ++q) v += red[cc][j][q];
+    part[((int64_t)(c0 + cc) * nb + blockIdx.x) * kPartW + j] = v;
   }
+}
+
+__global__ void conv_bwd_dw_reduce(int C, int K, int nb, const float* __restrict__ part,
+                                   float* __restrict__ dw, float* __restrict__ db) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= C * kPartW) return;
+  const int c = i / kPartW, j = i % kPartW;
+  if (j >= K && j != 8) return;
+  if (j == 8 && !db) return;
+  float v = 0.f;
+  for (int b = 0; b < nb; ++b) v += part[((int64_t)c * nb + b) * kPartW + j];
+  if (j == 8) db[c] = v;
+  else dw[(int64_t)c * K + j] = v;
+}
+
+// dx[c][t] = w[c][K-1] dpre[c][t] + sum over the tokens u that have t as their
+// lag-l predecessor of w[c][K-1-l] dpre[c][u]  (successor CSR, fixed order).
+template <typename T>
+__global__ void __launch_bounds__(kConvTok)
+conv_bwd_dx(int C, int S, int K, const float* __restrict__ w, const float* __restrict__ dpre,
+            const int32_t* __restrict__ sp, const int32_t* __restrict__ stok,
+            const int32_t* __restrict__ slag, T* __restrict__ dx) {
+  const int t = blockIdx.x * kConvTok + threadIdx.x;
+  if (t >= S) return;
+  const int c0 = blockIdx.y * kConvCh;
+  const int n_ch = min(kConvCh, C - c0);
+  float acc[kConvCh];
+#pragma unroll
+  for (int cc = 0; cc < kConvCh; ++cc)
+    acc[cc] = cc < n_ch ? w[(int64_t)(c0 + cc) * K + K - 1] * dpre[(int64_t)(c0 + cc) * S + t] : 0.f;
+  for (int e = sp[t]; e < sp[t + 1]; ++e) {
+    const int u = stok[e], l = slag[e];
+#pragma unroll
+    for (int cc = 0; cc < kConvCh; ++cc)
+      if (cc < n_ch)
+        acc[cc] = fmaf(w[(int64_t)(c0 + cc) * K + K - 1 - l], dpre[(int64_t)(c0 + cc) * S + u],
+                       acc[cc]);
+  }
+#pragma unroll
+  for (int cc = 0; cc < kConvCh; ++cc)
+    if (cc < n_ch) dx[(int64_t)(c0 + cc) * S + t] = from_f32<T>(acc[cc]);
 }
 
 template <typename Fn>
@@ -185,24 +227,38 @@ extern "C" int tt_tree_conv_fwd(int dtype, int32_t C, int32_t S, int32_t K, cons
   });
 }
 
+extern "C" int64_t tt_tree_conv_bwd_workspace_size(int32_t C, int32_t S, int32_t K) {
+  if (C < 0 || S < 0 || K < 1 || K > 8) return -1;
+  const int64_t nb = ((int64_t)S + tt::kConvTok - 1) / tt::kConvTok;
+  return (int64_t)C * S * 4 + (int64_t)C * nb * tt::kPartW * 4 + 256;
+}
+
 extern "C" int tt_tree_conv_bwd(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
                                 const float* weight, const float* bias, const int32_t* pred,
                                 const int32_t* succ_ptr, const int32_t* succ_tok,
                                 const int32_t* succ_lag, const void* dout, void* dx,
-                                float* dweight, float* dbias, void* stream) {
+                                float* dweight, float* dbias, void* workspace,
+                                int64_t workspace_bytes, void* stream) {
   if (C < 0 || S < 0 || K < 1 || K > 8) return TT_ERR_INVALID_ARG;
   if (C == 0 || S == 0) return TT_OK;
   if (!x || !weight || !dout || !dx || !dweight || !succ_ptr || (K > 1 && !pred))
     return TT_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < tt_tree_conv_bwd_workspace_size(C, S, K))
+    return TT_ERR_WORKSPACE;
   return tt::by_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     cudaStream_t st = (cudaStream_t)stream;
-    dim3 g((S + 255) / 256, C);
-    tt::conv_bwd_dx<T><<<g, 256, 0, st>>>(C, S, K, (const T*)x, weight, bias, pred, succ_ptr,
-                                          succ_tok, succ_lag, (const T*)dout, (T*)dx);
-    tt::conv_bwd_dw<T><<<C, 256, 0, st>>>(C, S, K, (const T*)x, weight, bias, pred,
-                                          (const T*)dout, dweight, dbias);
-    tt_count_launches(2);
+    const int nb = (S + tt::kConvTok - 1) / tt::kConvTok;
+    float* dpre = static_cast<float*>(workspace);
+    float* part = dpre + (int64_t)C * S;
+    dim3 g(nb, (C + tt::kConvCh - 1) / tt::kConvCh);
+    tt::conv_bwd_dpre<T><<<g, tt::kConvTok, 0, st>>>(C, S, K, (const T*)x, weight, bias, pred,
+                                                      (const T*)dout, dpre, part, nb);
+    tt::conv_bwd_dw_reduce<<<(C * tt::kPartW + 255) / 256, 256, 0, st>>>(C, K, nb, part, dweight,
+                                                                       dbias);
+    tt::conv_bwd_dx<T><<<g, tt::kConvTok, 0, st>>>(C, S, K, weight, dpre, succ_ptr, succ_tok,
+                                                    succ_lag, (T*)dx);
+    tt_count_launches(3);
     return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
   });
 }

@@ -105,9 +105,12 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
       sb[buf][bk0 + i * bdk][bc0 + i * bdc] = rb[i];
     }
   };
-  float2 acc[8][2];
+  // acc[p][w]: rows 2p and 2p+1 of the thread's 8 rows, column w of its 4
+  float2 acc[4][4];
 #pragma unroll
-  for (int u = 0; u < 8; ++u) acc[u][0] = acc[u][1] = make_float2(0.f, 0.f);
+  for (int p = 0; p < 4; ++p)
+#pragma unroll
+    for (int w = 0; w < 4; ++w) acc[p][w] = make_float2(0.f, 0.f);
   fetch(0);
   stash(0);
   __syncthreads();
@@ -120,13 +123,15 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
       const float4 a0 = *reinterpret_cast<const float4*>(&sa[buf][kk][4 * ty]);
       const float4 a1 = *reinterpret_cast<const float4*>(&sa[buf][kk][32 + 4 * ty]);
       const float4 b0 = *reinterpret_cast<const float4*>(&sb[buf][kk][4 * tx]);
-      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float2 bv0 = make_float2(b0.x, b0.y), bv1 = make_float2(b0.z, b0.w);
+      // row pairs come straight from the float4s; one broadcast per column
+      const float2 ap[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w),
+                            make_float2(a1.x, a1.y), make_float2(a1.z, a1.w)};
+      const float bw[4] = {b0.x, b0.y, b0.z, b0.w};
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float2 au = make_float2(av[u], av[u]);
-        acc[u][0] = fma2(au, bv0, acc[u][0]);
-        acc[u][1] = fma2(au, bv1, acc[u][1]);
+      for (int w = 0; w < 4; ++w) {
+        const float2 bb = make_float2(bw[w], bw[w]);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) acc[p][w] = fma2(ap[p], bb, acc[p][w]);
       }
     }
     if (more) stash(buf ^ 1);
@@ -141,7 +146,7 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
     for (int w = 0; w < 4; ++w) {
       const int gj = j0 + 4 * tx + w;
       if (gj >= sd.N) continue;
-      const float v = (w & 1) ? acc[u][w >> 1].y : acc[u][w >> 1].x;
+      const float v = (u & 1) ? acc[u >> 1][w].y : acc[u >> 1][w].x;
       float* pc = c + gi * sd.c_rs + gj * sd.c_cs;
       *pc = alpha * v + (beta != 0.f ? beta * *pc : 0.f);
     }

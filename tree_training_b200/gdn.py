@@ -216,10 +216,12 @@ def _conv_bwd_op(dy: torch.Tensor, x: torch.Tensor, w: torch.Tensor, b: torch.Te
     dx = torch.empty_like(x)
     dw = torch.empty_like(w)
     db = torch.empty((C,) if has_b else (0,), dtype=torch.float32, device=x.device)
+    ws_bytes = int(_lib.lib().tt_tree_conv_bwd_workspace_size(C, S, K))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=x.device)
     _lib.call("tt_tree_conv_bwd", _DTYPES[x.dtype], C, S, K, x.data_ptr(), w.data_ptr(),
               b.data_ptr() if has_b else None, pred.data_ptr(), sp.data_ptr(), stok.data_ptr(),
               slag.data_ptr(), dy.contiguous().data_ptr(), dx.data_ptr(), dw.data_ptr(),
-              db.data_ptr() if has_b else None, _stream_ptr(x.device))
+              db.data_ptr() if has_b else None, ws.data_ptr(), ws_bytes, _stream_ptr(x.device))
     return dx, dw, db
 
 
