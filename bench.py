@@ -402,15 +402,23 @@ def run_ours(args):
     dvh = torch.empty_like(vh).pin_memory()
     h2d = d2h = 0
 
+    up = torch.cuda.Stream(dev)
+
     def e2e_step():
         nonlocal h2d, d2h
         inf = tt.build_dfs_tree_info(roots)          # host packer
         m = inf.attn_meta()
+        main = torch.cuda.current_stream(dev)
         qd = qh.to(dev, non_blocking=True).requires_grad_(True)
         kd = kh.to(dev, non_blocking=True).requires_grad_(True)
         vd = vh.to(dev, non_blocking=True).requires_grad_(True)
-        dod = doh.to(dev, non_blocking=True)
+        # dO is only needed by the backward: upload it while the forward runs
+        dod = torch.empty(doh.shape, dtype=doh.dtype, device=dev)
+        up.wait_stream(main)
+        with torch.cuda.stream(up):
+            dod.copy_(doh, non_blocking=True)
         o = tt.tree_attention(qd, kd, vd, m)
+        main.wait_stream(up)
         o.backward(dod)
         dqh.copy_(qd.grad, non_blocking=True)
         dkh.copy_(kd.grad, non_blocking=True)
