@@ -236,3 +236,58 @@ def test_config2_full_size_sampled_rows_and_exact_cross_check():
     assert rel(f(out)[rows], o_ref) < 2e-2
     assert rel(f(qg.grad)[rows], dq_ref) < 2e-2
     assert torch.isfinite(kg.grad).all() and torch.isfinite(vg.grad).all()
+    _check_grad_identities(do, kg.grad, vg.grad, 32 // 8)
+
+
+class _Rows:
+    """A few rows of a [n, heads, D] array, indexed by their row numbers."""
+
+    def __init__(self, rows, data):
+        self._d = {r: data[i] for i, r in enumerate(rows)}
+        self.shape = (None,) + data.shape[1:]
+
+    def __getitem__(self, i):
+        return self._d[i]
+
+
+def _check_grad_identities(do, dk, dv, rep):
+    """Size-independent checks of every dK/dV entry: each row of P sums to 1, so
+    sum_j dV_j = sum over the group's query rows and heads of dO; each row of dS
+    sums to 0, so sum_j dK_j = 0."""
+    n_q, hq, D = do.shape
+    hkv = dv.shape[1]
+    do_sum = do.float().sum(0).view(hkv, rep, D).sum(1)          # [hkv, D]
+    dv_sum = dv.float().sum(0)
+    assert float((dv_sum - do_sum).abs().max() / do_sum.abs().max()) < 1e-2
+    dk_sum = dk.float().sum(0)
+    dk_abs = dk.float().abs().sum(0)
+    assert float((dk_sum.abs() / dk_abs.clamp_min(1e-30)).max()) < 1e-2
+
+
+def test_config3_size_tree_sampled_rows_and_identities():
+    """65,536-token agentic tree (BASELINE config 3 shape), 40 q / 8 kv heads
+    (an odd group of 5: the forward pairs heads and runs one single-head CTA
+    per group), D=128, bf16."""
+    from tree_training_b200.synthetic import agentic_tree
+    info = tt.build_dfs_tree_info(agentic_tree(3000))
+    meta = info.attn_meta()
+    hq, hkv = 40, 8
+    g = torch.Generator(device=DEV).manual_seed(3)
+    mk = lambda *s: (torch.randn(*s, generator=g, device=DEV) * 0.5).to(torch.bfloat16)
+    q, k, v, do = mk(meta.n_q, hq, 128), mk(meta.n_kv, hkv, 128), mk(meta.n_kv, hkv, 128), mk(meta.n_q, hq, 128)
+    qg, kg, vg = (x.clone().requires_grad_(True) for x in (q, k, v))
+    out = tt.tree_attention(qg, kg, vg, meta)
+    out.backward(do)
+    torch.cuda.synchronize()
+    tt.check_device_status(DEV)
+    rng = random.Random(3)
+    rows = sorted(set([0, 8191, 8192, meta.n_q - 1] + rng.sample(range(meta.n_q), 8)))
+    f = lambda t: t.detach().double().cpu().numpy()
+    sel = lambda t: f(t[rows])
+    kn, vn = f(k), f(v)
+    o_ref, dq_ref = _sampled_rows_oracle(meta, _Rows(rows, sel(q)), kn, vn, _Rows(rows, sel(do)),
+                                         rows)
+    assert rel(f(out[rows]), o_ref) < 2e-2
+    assert rel(f(qg.grad[rows]), dq_ref) < 2e-2
+    assert torch.isfinite(kg.grad).all() and torch.isfinite(vg.grad).all()
+    _check_grad_identities(do, kg.grad, vg.grad, hq // hkv)
