@@ -237,6 +237,53 @@ def cpu_baseline_sample(meta, V, hq=4, hkv=1):
                       f"the dense additive mask on {torch.get_num_threads()} threads"}
 
 
+def isolated_kernel_roofline(meta, q, k, v, do, dev, V, peak, reps: int = 5):
+    """Each attention kernel timed ALONE (CUDA events, same inputs, after the
+    timed region): in the product path dK/dV and dQ share the GPU on two
+    streams, so their live durations overlap and cannot be attributed to one
+    kernel; alone they can.  Returns {kernel: {ms, achieved, frac}}."""
+    from tree_training_b200 import _lib
+    from tree_training_b200.attention import _status_word, attn_fwd_raw
+    scale = D ** -0.5
+    md = meta.device(dev, 128, 128)
+    out, lse = attn_fwd_raw(q, k, v, md, scale)
+    N = meta.n_q
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ws_bytes = int(_lib.lib().tt_tree_attn_bwd_workspace_size(1, N, meta.n_kv, HQ, HKV, D))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    args = [1, N, meta.n_kv, HQ, HKV, D, q.data_ptr(), q.stride(0), q.stride(1),
+            k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(), v.stride(0), v.stride(1),
+            out.data_ptr(), do.data_ptr(), do.stride(0), do.stride(1), lse.data_ptr(),
+            md["kv_lo"].data_ptr(), md["kv_hi"].data_ptr(), md["fwd_ptr"].data_ptr(),
+            md["fwd_list"].data_ptr(), md["bwd_ptr"].data_ptr(), md["bwd_list"].data_ptr(),
+            float(scale), dq.data_ptr(), dq.stride(0), dq.stride(1), dk.data_ptr(), dk.stride(0),
+            dk.stride(1), dv.data_ptr(), dv.stride(0), dv.stride(1), ws.data_ptr(), ws_bytes]
+    st = _status_word(dev).data_ptr()
+    cs = torch.cuda.current_stream(dev).cuda_stream
+    phase = lambda ph: _lib.call("tt_tree_attn_bwd", *args, ph, st, cs)
+    phase(_lib.TT_BWD_PREP)
+    runs = {"attn_fwd_tc": lambda: attn_fwd_raw(q, k, v, md, scale),
+            "attn_bwd_dkdv_tc": lambda: phase(_lib.TT_BWD_DKDV),
+            "attn_bwd_dq_tc": lambda: phase(_lib.TT_BWD_DQ)}
+    flops = {"attn_fwd_tc": 4.0 * D * V * HQ, "attn_bwd_dkdv_tc": 8.0 * D * V * HQ,
+             "attn_bwd_dq_tc": 6.0 * D * V * HQ}
+    res = {}
+    for name, fn in runs.items():
+        fn()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        b.synchronize()
+        t = a.elapsed_time(b) / 1e3 / reps
+        ach = flops[name] / t / 1e12
+        res[name] = {"ms": t * 1e3, "achieved": ach, "frac": ach / peak}
+    return res
+
+
 def reference_gpu_sample(meta, dev, V, reps: int = 3):
     """The reference's own GPU path on the same tree, for comparison with the
     tcgen05 kernels: the dense additive [1, 1, N, N] mask the reference builds
@@ -453,14 +500,15 @@ def run_ours(args):
     dominant = max(kflops, key=lambda n: kern.get(n, 0.0))
     achieved = kflops[dominant] / kern[dominant] / 1e12
     peak = float(pk["bf16_tflops"])
-    traffic = None
+    traffic_tab = {}      # DRAM bytes per launch from the committed ncu summary
     tp = os.path.join(ROOT, "profiles", "tree_attn_config2_dram_traffic.txt")
     if os.path.exists(tp) and args.tokens == 16384:
         with open(tp) as fh:
             for ln in fh:
                 f = ln.split()
-                if len(f) == 2 and not ln.startswith("#") and f[0] == dominant:
-                    traffic = float(f[1])
+                if len(f) == 2 and not ln.startswith("#"):
+                    traffic_tab[f[0]] = float(f[1])
+    traffic = traffic_tab.get(dominant)
 
     if rank == 0:
         line = {
@@ -489,6 +537,15 @@ def run_ours(args):
             "gpu_launches": int(launches),
             "clocks": clk,
         }
+        iso = isolated_kernel_roofline(meta, q0, k0, v0, do, dev, V, peak)
+        dom = max(iso, key=lambda n: iso[n]["ms"])
+        line["roofline_isolated"] = {
+            "bound": "tensor", "kernel": dom, "achieved": iso[dom]["achieved"], "peak": peak,
+            "unit": "TFLOP/s", "frac": iso[dom]["frac"], "traffic": traffic_tab.get(dom),
+            "per_kernel": iso,
+            "note": "each kernel timed alone on the same inputs after the timed region; the "
+                    "live roofline above spans dQ's whole run while it shares the GPU with "
+                    "dK/dV on another stream"}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample(meta, V)
         if world == 1 and not args.no_reference_gpu:

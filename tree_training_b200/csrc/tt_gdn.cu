@@ -155,53 +155,44 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
 
 // ---- elementwise kernels ---------------------------------------------------------
 
+constexpr int kTokWarps = 8;   // per-(token, head) kernels: one warp each, 8 per block
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
 // Per (head, token): normalised/scaled q and k, v, beta, and the scaled copies
 // used as GEMM operands.  gam must already hold the per-node cumsum.
 template <typename T>
-__global__ void prep_tokens(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__ q,
-                            const T* __restrict__ k, const T* __restrict__ v,
-                            const float* __restrict__ beta, const float* __restrict__ gam,
-                            const float* __restrict__ gl_tok, int l2norm, float q_scale,
-                            float* Q, float* K, float* Vb, float* Kb, float* Kbg, float* Qg,
-                            float* Kd) {
-  const int t = blockIdx.x, h = blockIdx.y;
+__global__ void __launch_bounds__(32 * kTokWarps)
+prep_tokens(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__ q,
+            const T* __restrict__ k, const T* __restrict__ v,
+            const float* __restrict__ beta, const float* __restrict__ gam,
+            const float* __restrict__ gl_tok, int l2norm, float q_scale,
+            float* Q, float* K, float* Vb, float* Kb, float* Kbg, float* Qg, float* Kd) {
+  const int t = blockIdx.x * kTokWarps + (threadIdx.x >> 5), h = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  if (t >= S) return;                        // whole warps: no block-wide syncs below
   const int hk = h / (H / Hk);
   const T* qr = q + ((long long)t * Hk + hk) * Dk;
   const T* kr = k + ((long long)t * Hk + hk) * Dk;
-  __shared__ float red[2][32];
   float sq = 0.f, sk = 0.f;
-  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+  for (int d = lane; d < Dk; d += 32) {
     const float a = to_f32(qr[d]), b = to_f32(kr[d]);
     sq += a * a;
     sk += b * b;
   }
-  for (int o = 16; o > 0; o >>= 1) {
-    sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    sk += __shfl_xor_sync(0xffffffffu, sk, o);
-  }
-  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  if (lane == 0) {
-    red[0][wid] = sq;
-    red[1][wid] = sk;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float a = 0.f, b = 0.f;
-    for (int w = 0; w < nw; ++w) {
-      a += red[0][w];
-      b += red[1][w];
-    }
-    red[0][0] = a;
-    red[1][0] = b;
-  }
-  __syncthreads();
-  const float rq = l2norm ? rsqrtf(red[0][0] + 1e-6f) : 1.f;
-  const float rk = l2norm ? rsqrtf(red[1][0] + 1e-6f) : 1.f;
+  sq = warp_sum(sq);
+  sk = warp_sum(sk);
+  const float rq = l2norm ? rsqrtf(sq + 1e-6f) : 1.f;
+  const float rk = l2norm ? rsqrtf(sk + 1e-6f) : 1.f;
   const long long ht = (long long)h * S + t;
   const float bt = beta[(long long)t * H + h];
   const float gm = gam[ht];
   const float eg = expf(gm), ed = expf(gl_tok[ht] - gm);
-  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+  for (int d = lane; d < Dk; d += 32) {
     const float qs = to_f32(qr[d]) * rq * q_scale;
     const float ks = to_f32(kr[d]) * rk;
     Q[ht * Dk + d] = qs;
@@ -212,7 +203,7 @@ __global__ void prep_tokens(int S, int Hk, int H, int Dk, int Dv, const T* __res
     Kd[ht * Dk + d] = ks * ed;
   }
   const T* vr = v + ((long long)t * H + h) * Dv;
-  for (int d = threadIdx.x; d < Dv; d += blockDim.x) Vb[ht * Dv + d] = to_f32(vr[d]) * bt;
+  for (int d = lane; d < Dv; d += 32) Vb[ht * Dv + d] = to_f32(vr[d]) * bt;
 }
 
 // Per (node, head): gam = cumsum(g) over the node's tokens, gl_tok = gam at the
@@ -390,7 +381,8 @@ __global__ void ddd_rowcol(int S, const int* __restrict__ nstart, const int* __r
 // from all k-terms except the beta-scaled ones), dKb (grad of k*beta incl.
 // dKbg*e^gam), dVb; plus gam, gl, and the Qg/Kbg/Kd-dependent dgam parts.
 template <typename T>
-__global__ void assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__ q,
+__global__ void __launch_bounds__(32 * kTokWarps)
+assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__ q,
                                      const T* __restrict__ k, const T* __restrict__ v,
                                      const float* __restrict__ beta, const float* __restrict__ gam,
                                      const float* __restrict__ gl_tok, int l2norm, float q_scale,
@@ -399,7 +391,9 @@ __global__ void assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const
                                      const float* __restrict__ dKb, const float* __restrict__ dKbg,
                                      const float* __restrict__ dVb, float* dgam, float* dq_h,
                                      float* dk_h, float* dbeta_out, T* dv_out) {
-  const int t = blockIdx.x, h = blockIdx.y;
+  const int t = blockIdx.x * kTokWarps + (threadIdx.x >> 5), h = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  if (t >= S) return;                        // whole warps: no block-wide syncs below
   const int hk = h / (H / Hk);
   const long long ht = (long long)h * S + t;
   const T* qr = q + ((long long)t * Hk + hk) * Dk;
@@ -408,30 +402,19 @@ __global__ void assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const
   const float gm = gam[ht];
   const float eg = expf(gm), ed = expf(gl_tok[ht] - gm);
   // norms again (cheap) for the normalised q/k and the l2norm backward
-  __shared__ float red[6][32];
   float sq = 0.f, sk = 0.f;
-  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+  for (int d = lane; d < Dk; d += 32) {
     const float a = to_f32(qr[d]), b = to_f32(kr[d]);
     sq += a * a;
     sk += b * b;
   }
-  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  auto block_sum = [&](float x, int slot) -> float {
-    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-    __syncthreads();
-    if (lane == 0) red[slot][wid] = x;
-    __syncthreads();
-    float a = 0.f;
-    for (int w = 0; w < nw; ++w) a += red[slot][w];
-    return a;
-  };
-  sq = block_sum(sq, 0);
-  sk = block_sum(sk, 1);
+  sq = warp_sum(sq);
+  sk = warp_sum(sk);
   const float rq = l2norm ? rsqrtf(sq + 1e-6f) : 1.f;
   const float rk = l2norm ? rsqrtf(sk + 1e-6f) : 1.f;
   // d(scaled q) = dQ + dQg e^gam ; d(k) = dK + dKd e^{gl-gam} + beta (dKb + dKbg e^gam)
   float p_qg = 0.f, p_kbg = 0.f, p_kd = 0.f, p_kb = 0.f, xdq = 0.f, xdk = 0.f;
-  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+  for (int d = lane; d < Dk; d += 32) {
     const float qn = to_f32(qr[d]) * rq, kn = to_f32(kr[d]) * rk;
     const float qs = qn * q_scale;
     const float gqs = dQ[ht * Dk + d] + dQg[ht * Dk + d] * eg;
@@ -447,14 +430,14 @@ __global__ void assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const
     dq_h[ht * Dk + d] = gqn;                  // finished below with the l2norm backward
     dk_h[ht * Dk + d] = gk;
   }
-  p_qg = block_sum(p_qg, 2);
-  p_kbg = block_sum(p_kbg, 3);
-  p_kd = block_sum(p_kd, 4);
-  p_kb = block_sum(p_kb, 5);
-  xdq = block_sum(xdq, 0);
-  xdk = block_sum(xdk, 1);
+  p_qg = warp_sum(p_qg);
+  p_kbg = warp_sum(p_kbg);
+  p_kd = warp_sum(p_kd);
+  p_kb = warp_sum(p_kb);
+  xdq = warp_sum(xdq);
+  xdk = warp_sum(xdk);
   // y = x r (r = (|x|^2+eps)^-1/2): dx = r dy - r^3 (x.dy) x = r (dy - (y.dy) y)
-  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+  for (int d = lane; d < Dk; d += 32) {
     if (l2norm) {
       const float qn = to_f32(qr[d]) * rq, kn = to_f32(kr[d]) * rk;
       dq_h[ht * Dk + d] = rq * (dq_h[ht * Dk + d] - xdq * qn);
@@ -463,13 +446,13 @@ __global__ void assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const
   }
   float p_vb = 0.f;
   const T* vr = v + ((long long)t * H + h) * Dv;
-  for (int d = threadIdx.x; d < Dv; d += blockDim.x) {
+  for (int d = lane; d < Dv; d += 32) {
     const float g = dVb[ht * Dv + d];
     p_vb += to_f32(vr[d]) * g;
     dv_out[((long long)t * H + h) * Dv + d] = from_f32<T>(g * bt);
   }
-  p_vb = block_sum(p_vb, 2);
-  if (threadIdx.x == 0) {
+  p_vb = warp_sum(p_vb);
+  if (lane == 0) {
     dbeta_out[(long long)t * H + h] = p_kb + p_vb;
     // e^gam terms of Qg, Kbg and the -gam of Kd (the +gl part goes to the node's last token)
     dgam[ht] += p_qg + p_kbg - p_kd;
@@ -829,9 +812,9 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   // ---------------------------------------------------------------- forward
   node_cumsum<<<dim3((n + 127) / 128, H), 128, 0, st>>>(S, H, n, b.d_start, b.d_len, g, b.gam,
                                                         b.gl_tok, b.gl);
-  prep_tokens<T><<<dim3(S, H), 128, 0, st>>>(S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok,
-                                             l2norm, q_scale, b.Q, b.K, b.Vb, b.Kb, b.Kbg, b.Qg,
-                                             b.Kd);
+  prep_tokens<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(
+      S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok, l2norm, q_scale, b.Q, b.K, b.Vb, b.Kb,
+      b.Kbg, b.Qg, b.Kd);
   launches += 2;
   launch_gemm(b.d_desc, b.d_tiles, ds_kk, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
   launch_gemm(b.d_desc, b.d_tiles, ds_kk, H, b.Q, vk, b.K, vk, b.QK, llh, 1.f, 0.f, st);
@@ -917,7 +900,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   launch_gemm(b.d_desc, b.d_tiles, ds_gtk, H, b.dAqk, llh, b.Q, vk, b.dK, vk, 1.f, 1.f, st);
   launch_gemm(b.d_desc, b.d_tiles, ds_gk, H, b.dAqk, llh, b.K, vk, b.dQ, vk, 1.f, 0.f, st);
   kd_dot_kernel<<<dim3(S, H), 128, 0, st>>>(S, Dk, b.Kd, b.dKd, b.kd_dot);
-  assemble_token_grads<T><<<dim3(S, H), 128, 0, st>>>(
+  assemble_token_grads<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(
       S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok, l2norm, q_scale, b.dQ, b.dQg, b.dK,
       b.dKd, b.dKb, b.dKbg, b.dVb, b.dgam, b.dq_h, b.dk_h, dbeta, (T*)dv_);
   node_dg<<<dim3((n + 127) / 128, H), 128, 0, st>>>(S, H, n, b.d_start, b.d_len, b.kd_dot, b.dgl,
