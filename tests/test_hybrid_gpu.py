@@ -105,13 +105,14 @@ def setup():
     return model, roots, ref, leaves, labels
 
 
-@pytest.mark.parametrize("backward", ["fused", "per_leaf"])
+@pytest.mark.parametrize("backward,leaf_logits_only", [("fused", True), ("fused", False),
+                                                       ("per_leaf", True)])
 @pytest.mark.parametrize("max_tokens", [1000, 20, 10])
-def test_tree_grad_hybrid_matches_flat_per_path(setup, max_tokens, backward):
+def test_tree_grad_hybrid_matches_flat_per_path(setup, max_tokens, backward, leaf_logits_only):
     model, roots, ref, leaves, labels = setup
     model.zero_grad(set_to_none=True)
     tree_grad_hybrid(model, roots, make_tree_loss_fn(labels, leaves, len(leaves)), max_tokens,
-                     backward=backward)
+                     backward=backward, leaf_logits_only=leaf_logits_only)
     torch.cuda.synchronize()
     tt.check_device_status(DEV)
     assert max_rel(ref, _grads(model)) < 1e-4

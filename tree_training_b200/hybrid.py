@@ -161,7 +161,23 @@ def _partition_forest(p: SubtreePartition):
     return [_N(n) for n in p.entry_nodes if id(n) in members]
 
 
-def _subtree_forward(model, p: SubtreePartition, gw: Optional[SubtreeGateway], dev, gateway_mask):
+def _loss_leaf_spans(info, p: SubtreePartition):
+    """(chunk, start, end) of the partition's loss leaves in DFS order."""
+    out = []
+    for c in info.leaf_chunk_ids_np.tolist():
+        if id(info.nodes[c].orig) in p.leaf_node_set:
+            s, e = info.chunk_bounds_np[c]
+            out.append((c, int(s), int(e)))
+    return out
+
+
+def _subtree_forward(model, p: SubtreePartition, gw: Optional[SubtreeGateway], dev, gateway_mask,
+                     leaf_logits_only: bool = False):
+    """Forward of one partition.  Returns (logits, info, full_kv, spans): with
+    ``leaf_logits_only`` the LM head runs only on the loss leaves' tokens (HF
+    ``logits_to_keep`` with an index tensor) and spans maps each loss leaf to
+    its rows of the compact logits; otherwise logits cover every token and the
+    spans are the leaves' own token ranges."""
     forest = _partition_forest(p)
     info = build_dfs_tree_info(forest, pos_offset=p.pos_offset)
     N = info.N
@@ -176,10 +192,22 @@ def _subtree_forward(model, p: SubtreePartition, gw: Optional[SubtreeGateway], d
     cache = GatewayCache(list(zip(gw.key_gates, gw.val_gates)) if gw is not None else [])
     dtype = next(model.parameters()).dtype
     mask = tree_mask_placeholder(meta, dtype=dtype, device=dev)
+    leaves = _loss_leaf_spans(info, p)
+    kw = {}
+    if leaf_logits_only:
+        idx = np.concatenate([np.arange(s, e) for _, s, e in leaves]) if leaves else \
+            np.zeros(0, np.int64)
+        kw["logits_to_keep"] = torch.as_tensor(idx, dtype=torch.long, device=dev)
+        spans, off = [], 0
+        for c, s, e in leaves:
+            spans.append((c, off, off + (e - s)))
+            off += e - s
+    else:
+        spans = leaves
     out = model(input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=cache,
-                use_cache=True, tree_meta=meta)
+                use_cache=True, tree_meta=meta, **kw)
     full_kv = [cache._full_kv[l] for l in sorted(cache._full_kv)]
-    return out.logits, info, full_kv
+    return out.logits, info, full_kv, spans
 
 
 def _make_child_gateways(full_kv, info, p: SubtreePartition, gw: Optional[SubtreeGateway],
@@ -282,7 +310,8 @@ def _ensure_tree_attention(model):
 
 
 def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
-                     gateway_mask: str = "tree", backward: str = "fused") -> None:
+                     gateway_mask: str = "tree", backward: str = "fused",
+                     leaf_logits_only: bool = True) -> None:
     """Partitioned tree forward/backward (tree_grad_hybrid.py:434-539):
     partitions run top-down, each with the gateway K/V of its cut node; then
     bottom-up, each partition backpropagates its leaf losses and chains the
@@ -296,7 +325,11 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
     accumulate the same sum of gradients; every per-leaf call traverses the
     whole partition graph (each leaf's logits depend on every layer of the
     partition), so the fused form does 1/(leaves + gateways) of the backward
-    work."""
+    work.
+
+    ``leaf_logits_only`` runs the LM head only on loss-leaf tokens (the loss
+    reads nothing else); ``leaf_loss_fn`` receives the same [1, len, vocab]
+    slices either way."""
     if gateway_mask not in ("tree", "reference"):
         raise ValueError("gateway_mask must be 'tree' or 'reference'")
     if backward not in ("fused", "per_leaf"):
@@ -313,8 +346,9 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
     for p in parts:
         gw = gateways.get(id(p))
         p.pos_offset = gw.pos_offset if gw is not None else 0
-        logits, info, full_kv = _subtree_forward(model, p, gw, dev, gateway_mask)
-        fwd[id(p)] = (logits, info)
+        logits, info, full_kv, spans = _subtree_forward(model, p, gw, dev, gateway_mask,
+                                                        leaf_logits_only)
+        fwd[id(p)] = (logits, info, spans)
         seen, cuts = set(), []
         for cn, _ in children_of[id(p)]:
             if id(cn) not in seen:
@@ -325,13 +359,8 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
             for cn, cp in children_of[id(p)]:
                 gateways[id(cp)] = child[id(cn)]
     for p in reversed(parts):
-        logits, info = fwd[id(p)]
-        leaf_chunks = []
-        for c in info.leaf_chunk_ids_np.tolist():
-            orig = info.nodes[c].orig
-            if id(orig) in p.leaf_node_set:
-                s, e = info.chunk_bounds_np[c]
-                leaf_chunks.append((int(s), int(e), orig))
+        logits, info, spans = fwd[id(p)]
+        leaf_chunks = [(s, e, info.nodes[c].orig) for c, s, e in spans]
         uniq, seen = [], set()
         for cn, cp in children_of[id(p)]:
             g = gateways.get(id(cp))
