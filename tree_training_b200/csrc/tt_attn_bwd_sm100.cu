@@ -348,23 +348,35 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const float4* L4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes) + half * 8;
       const float4* D4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes + kAuxHalf) + half * 8;
       uint32_t pw[16], dw[16];
+      const float2 sc2 = make_float2(scale_log2, scale_log2);
+      const float2 nlog2e = make_float2(-kLog2e, -kLog2e);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float4 l4 = L4[i], d4 = D4[i];
-        const float la[4] = {l4.x, l4.y, l4.z, l4.w};
-        const float da[4] = {d4.x, d4.y, d4.z, d4.w};
-        float p[4], ds[4];
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          float pv = fast_exp2(fmaf(sv[4 * i + w], scale_log2, -la[w] * kLog2e));
-          if (partial && !visible(lo, hi, q0 + 4 * i + w)) pv = 0.f;
-          p[w] = pv;
-          ds[w] = pv * (dp[4 * i + w] - da[w]);
+        // exponent argument s * scale - lse (log2 units), two columns per
+        // instruction; one pair in four takes the FMA-pipe exp2 so the SFU is
+        // not the only unit doing exponentials (masked columns are zeroed
+        // after, so their out-of-range arguments do not matter)
+        const float2 x01 = ffma2(make_float2(sv[4 * i], sv[4 * i + 1]), sc2,
+                                 fmul2(make_float2(l4.x, l4.y), nlog2e));
+        const float2 x23 = ffma2(make_float2(sv[4 * i + 2], sv[4 * i + 3]), sc2,
+                                 fmul2(make_float2(l4.z, l4.w), nlog2e));
+        float2 p01 = (i & 1) ? exp2_poly2(x01) : make_float2(fast_exp2(x01.x), fast_exp2(x01.y));
+        float2 p23 = make_float2(fast_exp2(x23.x), fast_exp2(x23.y));
+        if (partial) {
+          if (!visible(lo, hi, q0 + 4 * i + 0)) p01.x = 0.f;
+          if (!visible(lo, hi, q0 + 4 * i + 1)) p01.y = 0.f;
+          if (!visible(lo, hi, q0 + 4 * i + 2)) p23.x = 0.f;
+          if (!visible(lo, hi, q0 + 4 * i + 3)) p23.y = 0.f;
         }
-        pw[2 * i] = pack2<kBf16>(p[0], p[1]);
-        pw[2 * i + 1] = pack2<kBf16>(p[2], p[3]);
-        dw[2 * i] = pack2<kBf16>(ds[0], ds[1]);
-        dw[2 * i + 1] = pack2<kBf16>(ds[2], ds[3]);
+        const float2 ds01 = fmul2(p01, fadd2(make_float2(dp[4 * i], dp[4 * i + 1]),
+                                             make_float2(-d4.x, -d4.y)));
+        const float2 ds23 = fmul2(p23, fadd2(make_float2(dp[4 * i + 2], dp[4 * i + 3]),
+                                             make_float2(-d4.z, -d4.w)));
+        pw[2 * i] = pack2<kBf16>(p01.x, p01.y);
+        pw[2 * i + 1] = pack2<kBf16>(p23.x, p23.y);
+        dw[2 * i] = pack2<kBf16>(ds01.x, ds01.y);
+        dw[2 * i + 1] = pack2<kBf16>(ds23.x, ds23.y);
       }
       tmem_st16(lane_addr + cs, pw);
       tmem_st16(lane_addr + cp, dw);
@@ -499,8 +511,15 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       float sv[32], dp[32];
       tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
       float p[32];
+      const float2 sc2 = make_float2(scale_log2, scale_log2), nl2 = make_float2(-l2, -l2);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) p[i] = fast_exp2(fmaf(sv[i], scale_log2, -l2));
+      for (int i = 0; i < 16; ++i) {
+        // two columns per instruction; one pair in four on the FMA-pipe exp2
+        const float2 x = ffma2(make_float2(sv[2 * i], sv[2 * i + 1]), sc2, nl2);
+        const float2 e = (i & 3) == 3 ? exp2_poly2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        p[2 * i] = e.x;
+        p[2 * i + 1] = e.y;
+      }
       if (partial) {
         // key intervals of this sub-tile, zero-padded past n_kv (never visible)
         const int4* LO = reinterpret_cast<const int4*>(aux + s * kAuxBytes) + half * 8;
@@ -515,9 +534,13 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         }
       }
       uint32_t dw[16];
+      const float2 ndr = make_float2(-dr, -dr);
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        dw[i] = pack2<kBf16>(p[2 * i] * (dp[2 * i] - dr), p[2 * i + 1] * (dp[2 * i + 1] - dr));
+      for (int i = 0; i < 16; ++i) {
+        const float2 ds = fmul2(make_float2(p[2 * i], p[2 * i + 1]),
+                                fadd2(make_float2(dp[2 * i], dp[2 * i + 1]), ndr));
+        dw[i] = pack2<kBf16>(ds.x, ds.y);
+      }
       tmem_st16(lane_addr + cs, dw);
       tmem_st_wait();
       tc_fence_before();
