@@ -38,7 +38,10 @@ struct SegDesc {
   long long c_off, c_rs, c_cs;
 };
 
-constexpr int kBM = 64, kBN = 64, kBK = 16;
+#ifndef TT_GDN_BK
+#define TT_GDN_BK 16
+#endif
+constexpr int kBM = 64, kBN = 64, kBK = TT_GDN_BK;   // K slice depth: 16 or 32
 constexpr int kGemmThreads = 128;           // 16 x 8 threads, 8 x 4 outputs each
 constexpr int kRowPad = 4;                  // keeps 16-byte rows, spreads banks
 
@@ -77,21 +80,22 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int i0 = tm * kBM, j0 = tn * kBN;
   // consecutive threads walk the operand's unit-stride dimension: element i
-  // (of 8) of this thread sits at (row ar0 + i*adr, k ak0 + i*adk) of the A
+  // (of kBK/2) of this thread sits at (row ar0 + i*adr, k ak0 + i*adk) of the A
   // slice and (k bk0 + i*bdk, column bc0 + i*bdc) of the B slice
   const bool a_kfast = sd.a_cs == 1, b_nfast = sd.b_cs == 1;
-  const int ar0 = a_kfast ? (tid >> 4) : (tid & 63), ak0 = a_kfast ? (tid & 15) : (tid >> 6);
-  const int adr = a_kfast ? 8 : 0, adk = a_kfast ? 0 : 2;
-  const int bc0 = b_nfast ? (tid & 63) : (tid >> 4), bk0 = b_nfast ? (tid >> 6) : (tid & 15);
-  const int bdc = b_nfast ? 0 : 8, bdk = b_nfast ? 2 : 0;
+  const int ar0 = a_kfast ? (tid / kBK) : (tid & 63), ak0 = a_kfast ? (tid % kBK) : (tid >> 6);
+  const int adr = a_kfast ? kGemmThreads / kBK : 0, adk = a_kfast ? 0 : 2;
+  const int bc0 = b_nfast ? (tid & 63) : (tid / kBK), bk0 = b_nfast ? (tid >> 6) : (tid % kBK);
+  const int bdc = b_nfast ? 0 : kGemmThreads / kBK, bdk = b_nfast ? 2 : 0;
   const int astep = adr * (int)sd.a_rs + adk * (int)sd.a_cs;
   const int bstep = bdk * (int)sd.b_rs + bdc * (int)sd.b_cs;
-  float ra[8], rb[8];
+  constexpr int kPer = kBM * kBK / kGemmThreads;   // staged elements per operand per thread
+  float ra[kPer], rb[kPer];
   auto fetch = [&](int k0) {
     const float* pa = a + (long long)(i0 + ar0) * sd.a_rs + (long long)(k0 + ak0) * sd.a_cs;
     const float* pb = b + (long long)(k0 + bk0) * sd.b_rs + (long long)(j0 + bc0) * sd.b_cs;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < kPer; ++i) {
       const bool in_a = i0 + ar0 + i * adr < sd.M && k0 + ak0 + i * adk < sd.K;
       ra[i] = in_a ? pa[i * astep] : 0.f;
       const bool in_b = k0 + bk0 + i * bdk < sd.K && j0 + bc0 + i * bdc < sd.N;
@@ -100,7 +104,7 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
   };
   auto stash = [&](int buf) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < kPer; ++i) {
       sa[buf][ak0 + i * adk][ar0 + i * adr] = ra[i];
       sb[buf][bk0 + i * bdk][bc0 + i * bdc] = rb[i];
     }
