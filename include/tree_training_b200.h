@@ -59,6 +59,13 @@ int tt_set_kernel_path(int path);
  * own kernels ran inside a timed region. */
 int64_t tt_kernel_launches(void);
 
+/* Diagnostic: launches one kernel that waits, with the bounded wait every
+ * tensor-core kernel uses, on an mbarrier phase nothing completes; after the
+ * 2 s limit it records TT_ERR_DEVICE_TIMEOUT in *status (device memory) and
+ * exits.  Faults nothing; the context stays usable.  For testing the failure
+ * path only. */
+int tt_diag_bounded_wait(int32_t* status, void* stream);
+
 /* ------------------------------------------------------------------------
  * Host packer.  Replaces the position/boundary/parent/leaf part of
  * build_dfs_tree_info (dfs_tree_forward.py:91-139) and, instead of the dense
