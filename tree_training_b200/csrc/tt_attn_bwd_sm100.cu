@@ -20,10 +20,11 @@
 // Streamed sub-tiles go through a 4-stage ring (each stage: two 64 x 128
 // 16-bit sub-tiles + their 64 row terms or key intervals, bulk-copied on the
 // same mbarrier), released per sub-tile, so loads run three sub-tiles ahead.
-// Sub-tile accumulators are double buffered in TMEM so the MMAs of sub-tile
-// u+1 run while the elementwise warps process sub-tile u.  TMEM (512 cols):
-//   buffer b in {0,1}: S [64b, 64b+64), dP [128+64b, 128+64b+64)
-//   dK/dV kernel: dV [256,384), dK [384,512);  dQ kernel: dQ [256,384).
+// Sub-tile S/dP accumulators rotate through NB TMEM buffers so the MMAs of
+// later sub-tiles run while the elementwise warps process sub-tile u.  TMEM
+// (512 cols), buffer b < NB: S [64b, 64b+64), dP [64NB+64b, 64NB+64b+64);
+//   dK/dV kernel, NB = 2: dV [256,384), dK [384,512);
+//   dQ kernel, NB = 3: dQ [384,512).
 // Warps: 0 TMA producer, 1 S/dP MMA issuer, 2..9 elementwise (two warps per
 // TMEM lane quadrant; warp half h owns columns [32h, 32h+32) of each sub-tile
 // and writes its 16-bit P / dS into the first 16 of those columns, i.e. only
@@ -41,6 +42,8 @@ constexpr int kT = 128;                     // rows of the fixed tiles and of a 
 constexpr int kD = 128;                     // head dim
 constexpr int kSub = 64;                    // rows of a streamed sub-tile
 constexpr int kStages = 4;                  // streamed ring depth
+constexpr int kNbDkdv = 2;                  // S/dP TMEM buffers: dK/dV kernel (dV, dK fill the rest)
+constexpr int kNbDq = 3;                    // S/dP TMEM buffers: dQ kernel (3 x 128 + dQ 128 = 512)
 constexpr int kTileBytes = kT * kD * 2;     // fixed tile (128 rows)
 constexpr int kTileHalf = kTileBytes / 2;   // one 64-dim swizzle block of a fixed tile
 constexpr int kSubBytes = kSub * kD * 2;    // streamed sub-tile (64 rows)
@@ -57,9 +60,9 @@ struct BwdBarriers {
   uint64_t a_full[kStages];  // streamed sub-tile A (Q or K) + its aux arrays
   uint64_t b_full[kStages];  // streamed sub-tile B (dO or V)
   uint64_t ab_empty[kStages];
-  uint64_t sdp_full[2];      // S and dP of a sub-tile ready (per TMEM buffer)
-  uint64_t ew_full[2];       // P / dS of a sub-tile written back (256 arrivals)
-  uint64_t buf_free[2];      // the accumulating MMAs of a TMEM buffer's sub-tile finished
+  uint64_t sdp_full[3];      // S and dP of a sub-tile ready (per TMEM buffer)
+  uint64_t ew_full[3];       // P / dS of a sub-tile written back (256 arrivals)
+  uint64_t buf_free[3];      // the accumulating MMAs of a TMEM buffer's sub-tile finished
   uint64_t acc_done;         // every MMA of the CTA finished
   uint64_t drain;            // abort path of the S/dP issuer
   uint64_t drain_acc;        // abort path of the accumulation issuer
@@ -82,12 +85,11 @@ __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
     mbar_init(&sh->b_full[s], 1);
     mbar_init(&sh->ab_empty[s], 1);
   }
-  for (int b = 0; b < 2; ++b) {
+  for (int b = 0; b < 3; ++b) {
     mbar_init(&sh->sdp_full[b], 1);
     mbar_init(&sh->ew_full[b], kEw);
+    mbar_init(&sh->buf_free[b], 1);
   }
-  mbar_init(&sh->buf_free[0], 1);
-  mbar_init(&sh->buf_free[1], 1);
   mbar_init(&sh->acc_done, 1);
   mbar_init(&sh->drain, 1);
   mbar_init(&sh->drain_acc, 1);
@@ -195,6 +197,7 @@ __device__ __forceinline__ void produce(BwdBarriers* sh, const volatile int32_t*
 //       once the elementwise warps wrote them back (ew_full); it alone
 //       accumulates into dK/dV or dQ, in sub-tile order, so the result does
 //       not depend on how the two instruction streams interleave.
+template <int NB>
 __device__ __forceinline__ void sdp_issuer(BwdBarriers* sh, const volatile int32_t* abort_flag,
                                            int32_t* status, uint32_t tmem, int n_u,
                                            uint32_t x_addr, uint32_t y_addr, uint32_t ring_a,
@@ -203,14 +206,14 @@ __device__ __forceinline__ void sdp_issuer(BwdBarriers* sh, const volatile int32
   const uint64_t dx = desc_sw128(x_addr, 16, 1024), dy = desc_sw128(y_addr, 16, 1024);
   const uint64_t da = desc_sw128(ring_a, 16, 1024), db = desc_sw128(ring_b, 16, 1024);
   for (int u = 0; u < n_u && ok; ++u) {
-    const int s = u % kStages, b = u & 1;
+    const int s = u % kStages, b = u % NB;
     const uint32_t ph = (u / kStages) & 1;
-    if (u >= 2 && !(ok = mbar_wait(&sh->buf_free[b], ((u - 2) >> 1) & 1, abort_flag))) break;
+    if (u >= NB && !(ok = mbar_wait(&sh->buf_free[b], ((u - NB) / NB) & 1, abort_flag))) break;
     if (!(ok = mbar_wait(&sh->a_full[s], ph, abort_flag))) break;
     if (!(ok = mbar_wait(&sh->b_full[s], ph, abort_flag))) break;
     tc_fence_after();
     mma_ss_n64(tmem + 64 * b, dx, desc_add(da, s * kSubBytes), id_s);
-    mma_ss_n64(tmem + 128 + 64 * b, dy, desc_add(db, s * kSubBytes), id_s);
+    mma_ss_n64(tmem + 64 * NB + 64 * b, dy, desc_add(db, s * kSubBytes), id_s);
     tc_commit(&sh->sdp_full[b]);
   }
   if (!ok) {
@@ -220,13 +223,13 @@ __device__ __forceinline__ void sdp_issuer(BwdBarriers* sh, const volatile int32
   }
 }
 
-template <typename Acc>
+template <int NB, typename Acc>
 __device__ __forceinline__ void acc_issuer(BwdBarriers* sh, const volatile int32_t* abort_flag,
                                            int32_t* status, int n_u, Acc acc) {
   bool ok = true;
   for (int u = 0; u < n_u && ok; ++u) {
-    const int b = u & 1, s = u % kStages;
-    if (!(ok = mbar_wait(&sh->ew_full[b], (u >> 1) & 1, abort_flag))) break;
+    const int b = u % NB, s = u % kStages;
+    if (!(ok = mbar_wait(&sh->ew_full[b], (u / NB) & 1, abort_flag))) break;
     tc_fence_after();
     acc(s, b, u > 0);
     tc_commit(&sh->buf_free[b]);
@@ -307,7 +310,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   } else if (warp == 1) {
     if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
-      sdp_issuer(sh, abort_flag, status, tmem, n_u, smem_u32(sK), smem_u32(sV), smem_u32(rQ),
+      sdp_issuer<kNbDkdv>(sh, abort_flag, status, tmem, n_u, smem_u32(sK), smem_u32(sV), smem_u32(rQ),
                  smem_u32(rDO), id_s);
     }
   } else if (warp == 10) {
@@ -316,11 +319,11 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       // B of dV += P^T dO and dK += dS^T Q: the ring's dO / Q sub-tiles, MN-major
       const uint64_t d_do = desc_sw128(smem_u32(rDO), kSubHalf, 1024);
       const uint64_t d_q = desc_sw128(smem_u32(rQ), kSubHalf, 1024);
-      acc_issuer(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
+      acc_issuer<kNbDkdv>(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
         mma_ts_k64(tmem + kColDV, tmem + 64 * b, desc_add(d_do, s * kSubBytes), id_o,
                    accumulate);
-        mma_ts_k64(tmem + kColDK, tmem + 128 + 64 * b, desc_add(d_q, s * kSubBytes), id_o,
-                   accumulate);
+        mma_ts_k64(tmem + kColDK, tmem + 64 * kNbDkdv + 64 * b, desc_add(d_q, s * kSubBytes),
+                   id_o, accumulate);
       });
     }
   } else {
@@ -333,16 +336,16 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     bool ok = true;
     for (int u = 0; u < n_u; ++u) {
-      const int it = u >> 1, b = u & 1, s = u % kStages;
+      const int it = u >> 1, b = u % kNbDkdv, s = u % kStages;
       const int ent = bwd_list[e0 + it % n_list];
-      const int q0 = (ent >> 1) * kT + b * kSub + half * 32;   // first q row of this warp
+      const int q0 = (ent >> 1) * kT + (u & 1) * kSub + half * 32;   // first q row of this warp
       const bool partial = ent & 1;
-      ok = mbar_wait(&sh->sdp_full[b], (u >> 1) & 1, abort_flag);
+      ok = mbar_wait(&sh->sdp_full[b], (u / kNbDkdv) & 1, abort_flag);
       if (ok) ok = mbar_wait(&sh->a_full[s], (u / kStages) & 1, abort_flag);   // aux visible
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t cs = 64 * b + 32 * half, cp = 128 + 64 * b + 32 * half;
+      const uint32_t cs = 64 * b + 32 * half, cp = 64 * kNbDkdv + 64 * b + 32 * half;
       float sv[32], dp[32];
       tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
       const float4* L4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes) + half * 8;
@@ -456,7 +459,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
-  constexpr uint32_t kColDQ = 256;
+  constexpr uint32_t kColDQ = 128 * kNbDq;   // after the S/dP buffers
 
   if (warp == 0) {
     if (lane == 0 && n_u > 0) {
@@ -479,14 +482,14 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   } else if (warp == 1) {
     if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
-      sdp_issuer(sh, abort_flag, status, tmem, n_u, smem_u32(sQ), smem_u32(sDO), smem_u32(rK),
+      sdp_issuer<kNbDq>(sh, abort_flag, status, tmem, n_u, smem_u32(sQ), smem_u32(sDO), smem_u32(rK),
                  smem_u32(rV), id_s);
     }
   } else if (warp == 10) {
     if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_o = idesc_f16(kBf16, kT, kD, true);
       const uint64_t d_k = desc_sw128(smem_u32(rK), kSubHalf, 1024);   // B of dQ += dS K
-      acc_issuer(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
+      acc_issuer<kNbDq>(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
         mma_ts_k64(tmem + kColDQ, tmem + 64 * b, desc_add(d_k, s * kSubBytes), id_o, accumulate);
       });
     }
@@ -500,14 +503,14 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     const float dr = delta[static_cast<int64_t>(h) * ld + row];
     bool ok = true;
     for (int u = 0; u < n_u; ++u) {
-      const int b = u & 1, s = u % kStages;
+      const int b = u % kNbDq, s = u % kStages;
       const bool partial = fwd_list[e0 + (u >> 1)] & 1;
-      ok = mbar_wait(&sh->sdp_full[b], (u >> 1) & 1, abort_flag);
+      ok = mbar_wait(&sh->sdp_full[b], (u / kNbDq) & 1, abort_flag);
       if (ok && partial) ok = mbar_wait(&sh->a_full[s], (u / kStages) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t cs = 64 * b + 32 * half, cp = 128 + 64 * b + 32 * half;
+      const uint32_t cs = 64 * b + 32 * half, cp = 64 * kNbDq + 64 * b + 32 * half;
       float sv[32], dp[32];
       tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
       float p[32];
