@@ -39,7 +39,9 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=200,
+                    help="timed steps (config 2: ~4 ms each, so the clock sampler sees the "
+                         "timed region)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=1000)
@@ -106,7 +108,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", self._gpu_id()],
+                 "-lms", "100", "-i", self._gpu_id()],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -442,53 +444,71 @@ def run_ours(args):
     value = flops_all / t_max / 1e12
 
     # ---- end to end through the public API from pinned host buffers ----
+    # Run as a training loop with a prefetching input stage runs it: step i+1's
+    # inputs upload on `up` while step i computes on the main stream, and step
+    # i's gradients download on `down` (two device input sets, two pinned host
+    # output sets).  Every step's copies and host packing are inside the timed
+    # region; the per-step time is the region's length over its steps.  Each
+    # step moves more than L2 holds (inputs 335 MB), so no flush is needed.
     pin = lambda t: t.detach().cpu().pin_memory()
-    qh, kh, vh, doh = pin(q0), pin(k0), pin(v0), pin(do)
-    dqh = torch.empty_like(qh).pin_memory()
-    dkh = torch.empty_like(kh).pin_memory()
-    dvh = torch.empty_like(vh).pin_memory()
+    host_in = {"q": pin(q0), "k": pin(k0), "v": pin(v0), "do": pin(do)}
+    host_out = [[torch.empty_like(host_in[n]).pin_memory() for n in ("q", "k", "v")]
+                for _ in range(2)]
+    dev_in = [{n: torch.empty_like(t, device=dev) for n, t in host_in.items()} for _ in range(2)]
+    main = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [None, None]
     h2d = d2h = 0
 
-    up = torch.cuda.Stream(dev)
+    def upload(i):
+        st = i % 2
+        if in_free[st] is not None:
+            up.wait_event(in_free[st])
+        with torch.cuda.stream(up):
+            for n, t in host_in.items():
+                dev_in[st][n].copy_(t, non_blocking=True)
+        in_ready[st].record(up)
 
-    def e2e_step():
+    def compute(i):
         nonlocal h2d, d2h
+        st = i % 2
         inf = tt.build_dfs_tree_info(roots)          # host packer
         m = inf.attn_meta()
-        main = torch.cuda.current_stream(dev)
-        qd = qh.to(dev, non_blocking=True).requires_grad_(True)
-        kd = kh.to(dev, non_blocking=True).requires_grad_(True)
-        vd = vh.to(dev, non_blocking=True).requires_grad_(True)
-        # dO is only needed by the backward: upload it while the forward runs
-        dod = torch.empty(doh.shape, dtype=doh.dtype, device=dev)
-        up.wait_stream(main)
-        with torch.cuda.stream(up):
-            dod.copy_(doh, non_blocking=True)
+        main.wait_event(in_ready[st])
+        d = dev_in[st]
+        qd, kd, vd = (d[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
         o = tt.tree_attention(qd, kd, vd, m)
-        main.wait_stream(up)
-        o.backward(dod)
-        dqh.copy_(qd.grad, non_blocking=True)
-        dkh.copy_(kd.grad, non_blocking=True)
-        dvh.copy_(vd.grad, non_blocking=True)
-        h2d = (sum(x.numel() * x.element_size() for x in (qh, kh, vh, doh)) + m.h2d_bytes())
-        d2h = sum(x.numel() * x.element_size() for x in (dqh, dkh, dvh))
+        o.backward(d["do"])
+        ev = torch.cuda.Event()
+        ev.record(main)
+        in_free[st] = ev
+        down.wait_event(ev)
+        with torch.cuda.stream(down):
+            for g, hb in zip((qd.grad, kd.grad, vd.grad), host_out[st]):
+                hb.copy_(g, non_blocking=True)
+                g.record_stream(down)
+        h2d = sum(t.numel() * t.element_size() for t in host_in.values()) + m.h2d_bytes()
+        d2h = sum(t.numel() * t.element_size() for t in host_out[st])
 
-    for _ in range(2):
-        e2e_step()
+    def e2e_run(n):
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                upload(i + 1)
+            compute(i)
+        main.wait_stream(down)
+
+    e2e_run(2)
     torch.cuda.synchronize()
     barrier(world)
-    e_ts = []
-    for _ in range(args.steps):
-        flush.zero_()
-        torch.cuda.synchronize()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record()
-        e2e_step()
-        b.record()
-        b.synchronize()
-        e_ts.append(a.elapsed_time(b) / 1e3)
-    t_e2e = max_over_ranks(statistics.mean(e_ts), world, dev)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(main)
+    e2e_run(args.steps)
+    b.record(main)
+    b.synchronize()
+    t_e2e = max_over_ranks(a.elapsed_time(b) / 1e3 / args.steps, world, dev)
     e2e_value = flops_all / t_e2e / 1e12
 
     pk, pk_src = peaks()
@@ -527,7 +547,9 @@ def run_ours(args):
             "fwd_tflops": f_fwd / t_fwd / 1e12, "bwd_tflops": f_bwd / t_bwd / 1e12,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": t_e2e * 1e3,
-                    "tokens_per_s": tokens_all / t_e2e},
+                    "tokens_per_s": tokens_all / t_e2e,
+                    "schedule": "pipelined: next step's upload and this step's download "
+                                "overlap compute (two input sets, three streams)"},
             "kernel_ms": {n: t * 1e3 for n, t in kern.items()},
             "host_enqueue_ms_per_step": host_enqueue_ms,
             "roofline": {"bound": "tensor", "kernel": dominant,
