@@ -39,9 +39,10 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200,
-                    help="timed steps (config 2: ~4 ms each, so the clock sampler sees the "
-                         "timed region)")
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps; default per workload: attn 200 (~4 ms each, so the "
+                         "clock sampler sees the timed region), attn3 5, gdn 20, e2e5 3; "
+                         "--impl reference sizes each step so the run takes ~2 minutes")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=1000)
@@ -344,29 +345,45 @@ def reference_gpu_sample(meta, dev, V, reps: int = 3):
 
 
 def run_reference(args):
+    """The reference's own CPU path for config 2 (HF sdpa_attention_forward +
+    the dense additive mask, fwd + autograd bwd) on the host cores: each step a
+    bounded sample of the workload, one GQA group (4 q heads / 1 kv head) over
+    every k-th query row of the tree, k chosen so the whole --steps/--warmup run
+    takes about two minutes.  Query rows are independent, so the sample is an
+    exact slice of the full computation; its useful FLOPs are 14 * D * (visible
+    pairs of the sampled rows) * 4."""
     world, rank, local = dist_env()
     if rank != 0:
         return 0
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     _, info, meta, V = workload(0, args.seed, args.tokens)
-    from oracle.ref_cpu import time_sample
-    for _ in range(args.warmup):
-        time_sample(meta, 4, 1, D, torch.bfloat16)
-    ts = [time_sample(meta, 4, 1, D, torch.bfloat16) for _ in range(args.steps)]
+    from oracle.ref_cpu import sample_rows, time_sample, visible_pairs
+    steps, warm = max(1, args.steps), max(0, args.warmup)
+    budget = max(0.5, 120.0 / (steps + warm + 1))       # seconds per step
+    probe = sample_rows(meta.n_q, 16)
+    t_probe = time_sample(meta, 4, 1, D, torch.bfloat16, rows=probe)   # also a warm-up
+    stride = max(1, int(np.ceil(16 * t_probe / budget)))
+    rows = sample_rows(meta.n_q, stride)
+    Vs = visible_pairs(meta, rows)
+    for _ in range(warm):
+        time_sample(meta, 4, 1, D, torch.bfloat16, rows=rows)
+    ts = [time_sample(meta, 4, 1, D, torch.bfloat16, rows=rows) for _ in range(steps)]
     t = statistics.mean(ts)
-    fl = 14.0 * D * V * 4
+    fl = 14.0 * D * Vs * 4
     val = fl / t / 1e12
-    sample = (f"each step: fwd+bwd of 4 q heads / 1 kv head (of {HQ}/{HKV}) over the full "
-              f"{meta.n_q}-token config-2 tree, bf16, transformers sdpa_attention_forward with "
+    sample = (f"each step: fwd+bwd of 4 q heads / 1 kv head (of {HQ}/{HKV}) on query rows "
+              f"0, {stride}, {2 * stride}, ... ({len(rows)} of {meta.n_q}, {Vs} visible pairs) of the "
+              f"config-2 tree against all keys, bf16, transformers sdpa_attention_forward with "
               f"the reference's dense additive mask, {torch.get_num_threads()} threads")
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "n_gpus": args.gpus, "steps": steps, "warmup": warm,
             "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "tokens_per_s": meta.n_q * (4 / HQ) / t,
+            "tokens_per_s": len(rows) * (4 / HQ) / t,
             "config": {"workload": "config2: one 16k-token DFS tree, 32/8 heads, D=128, "
                                    "tree attention fwd+bwd", "tokens": meta.n_q,
-                       "visible_pairs": V, "sample_heads": "4 of 32"},
+                       "visible_pairs": V, "sample_heads": "4 of 32",
+                       "sample_rows_stride": stride},
             "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
                              "kind": "port", "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -965,8 +982,13 @@ def run_e2e5(args):
     return 0
 
 
+DEFAULT_STEPS = {"attn": 200, "attn3": 5, "gdn": 20, "e2e5": 3}
+
+
 def main():
     args = parse()
+    if args.steps is None:
+        args.steps = 10 if args.impl == "reference" else DEFAULT_STEPS[args.workload]
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "gdn":

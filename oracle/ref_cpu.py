@@ -45,16 +45,32 @@ def sdpa_tree_fwd_bwd(q, k, v, dout, mask, scale):
     return out.detach(), q.grad, k.grad, v.grad
 
 
+def sample_rows(n_q: int, stride: int) -> np.ndarray:
+    """Every ``stride``-th query row (spread over the whole tree, so the
+    sample sees root, interior and leaf rows in proportion)."""
+    return np.arange(0, n_q, max(1, int(stride)))
+
+
+def visible_pairs(meta, rows=None) -> int:
+    """Visible (query, key) pairs of the given query rows (all rows if None)."""
+    allowed = meta.dense_mask()
+    return int(allowed.sum() if rows is None else allowed[rows].sum())
+
+
 def time_sample(meta, hq: int, hkv: int, D: int, dtype=torch.bfloat16, seed: int = 0,
-                repeats: int = 1):
-    """Time fwd+bwd of the reference CPU path on all n_q rows for ``hq`` query
-    heads sharing ``hkv`` kv heads.  Returns seconds per repeat (best)."""
+                repeats: int = 1, rows=None):
+    """Time fwd+bwd of the reference CPU path for ``hq`` query heads sharing
+    ``hkv`` kv heads, on all n_q query rows or on the subset ``rows`` (each
+    query row's attention is independent, so a row subset is an exact slice of
+    the same computation, with every key).  Returns seconds per repeat (best)."""
     g = torch.Generator().manual_seed(seed)
-    q = (torch.randn(1, hq, meta.n_q, D, generator=g) * 0.5).to(dtype)
+    nr = meta.n_q if rows is None else len(rows)
+    q = (torch.randn(1, hq, nr, D, generator=g) * 0.5).to(dtype)
     k = (torch.randn(1, hkv, meta.n_kv, D, generator=g) * 0.5).to(dtype)
     v = (torch.randn(1, hkv, meta.n_kv, D, generator=g) * 0.5).to(dtype)
-    do = (torch.randn(1, meta.n_q, hq, D, generator=g) * 0.5).to(dtype)
-    mask = dense_additive_mask(meta.dense_mask(), dtype)
+    do = (torch.randn(1, nr, hq, D, generator=g) * 0.5).to(dtype)
+    allowed = meta.dense_mask()
+    mask = dense_additive_mask(allowed if rows is None else allowed[rows], dtype)
     best = float("inf")
     for _ in range(repeats):
         t0 = time.perf_counter()
