@@ -1,6 +1,6 @@
 """The reference's attention path on host cores (CPU baseline of bench.py).
 
-TEST / BASELINE INFRASTRUCTURE ONLY: used by ``bench.py``'s cpu_baseline leg
+TEST AND CPU-BASELINE INFRASTRUCTURE ONLY: used by ``bench.py``'s cpu_baseline leg
 and ``--impl reference`` arm, never by the product package.
 
 This is the call the reference makes for every attention layer, run on CPU:

@@ -216,7 +216,7 @@ def _sampled_rows_oracle(meta, q, k, v, do, rows):
 
 
 def test_config2_full_size_sampled_rows_and_exact_cross_check():
-    """16k-token tree, 32/8 heads, D=128, bf16."""
+    """16k-token tree, 32/8 heads, D=128, bf16 (the benchmark's config 2)."""
     rng = random.Random(2024)
     roots = random_tree(rng, 16384, 64, 512, root_len=2048)
     info = tt.build_dfs_tree_info(roots)
@@ -265,7 +265,7 @@ def _check_grad_identities(do, dk, dv, rep):
 
 
 def test_config3_size_tree_sampled_rows_and_identities():
-    """65,536-token agentic tree (BASELINE config 3 shape), 40 q / 8 kv heads
+    """65,536-token agentic tree (the benchmark's config 3 shape), 40 q / 8 kv heads
     (an odd group of 5: the forward pairs heads and runs one single-head CTA
     per group), D=128, bf16."""
     from tree_training_b200.synthetic import agentic_tree

@@ -1,4 +1,4 @@
-"""BASELINE config 1 on a B200: the drivers with the tree_sm100 attention vs a
+"""Benchmark config 1 (the 47-token forest, 2-layer Qwen3) on a B200: the drivers with the tree_sm100 attention vs a
 flat per-path forward, gradients of a random-init 2-layer Qwen3 in fp32.
 
 The flat per-path forward runs each root-to-leaf path on its own with stock
