@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Tree-attention fwd+bwd benchmark (BASELINE config 2 by default).
+"""Tree-attention fwd+bwd benchmark (config 2 of the benchmark suite by default; configs 3, 4 and 5 via --workload).
 
 One step = tree attention forward + backward over one DFS-packed tree:
 16,384 tokens (root prompt 2048, 2-4 children, node lengths U[64,512], depth
