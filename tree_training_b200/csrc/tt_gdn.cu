@@ -277,16 +277,20 @@ __global__ void init_state(long long n, const float* __restrict__ init, float* s
 }
 
 template <typename T>
-__global__ void store_out(int S, int H, int Dv, const float* __restrict__ O, T* out) {
-  const int t = blockIdx.x, h = blockIdx.y;
-  for (int d = threadIdx.x; d < Dv; d += blockDim.x)
+__global__ void __launch_bounds__(32 * kTokWarps)
+store_out(int S, int H, int Dv, const float* __restrict__ O, T* out) {
+  const int t = blockIdx.x * kTokWarps + (threadIdx.x >> 5), h = blockIdx.y;
+  if (t >= S) return;
+  for (int d = threadIdx.x & 31; d < Dv; d += 32)
     out[((long long)t * H + h) * Dv + d] = from_f32<T>(O[((long long)h * S + t) * Dv + d]);
 }
 
 template <typename T>
-__global__ void load_dout(int S, int H, int Dv, const T* __restrict__ dout, float* dO) {
-  const int t = blockIdx.x, h = blockIdx.y;
-  for (int d = threadIdx.x; d < Dv; d += blockDim.x)
+__global__ void __launch_bounds__(32 * kTokWarps)
+load_dout(int S, int H, int Dv, const T* __restrict__ dout, float* dO) {
+  const int t = blockIdx.x * kTokWarps + (threadIdx.x >> 5), h = blockIdx.y;
+  if (t >= S) return;
+  for (int d = threadIdx.x & 31; d < Dv; d += 32)
     dO[((long long)h * S + t) * Dv + d] = to_f32(dout[((long long)t * H + h) * Dv + d]);
 }
 
@@ -484,27 +488,25 @@ __global__ void node_dg(int S, int H, int n_nodes, const int* __restrict__ nstar
 }
 
 // kd_dot[h][t] = kn_t e^{gl-gam_t} . dKd_t  (per token, reduced over Dk)
-__global__ void kd_dot_kernel(int S, int Dk, const float* __restrict__ Kd,
-                              const float* __restrict__ dKd, float* out) {
-  const long long ht = (long long)blockIdx.y * S + blockIdx.x;
+__global__ void __launch_bounds__(32 * kTokWarps)
+kd_dot_kernel(int S, int Dk, const float* __restrict__ Kd, const float* __restrict__ dKd,
+              float* out) {
+  const int t = blockIdx.x * kTokWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= S) return;
+  const long long ht = (long long)blockIdx.y * S + t;
   float acc = 0.f;
-  for (int d = threadIdx.x; d < Dk; d += blockDim.x) acc += Kd[ht * Dk + d] * dKd[ht * Dk + d];
-  __shared__ float red[32];
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float a = 0.f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a += red[w];
-    out[ht] = a;
-  }
+  for (int d = lane; d < Dk; d += 32) acc += Kd[ht * Dk + d] * dKd[ht * Dk + d];
+  acc = warp_sum(acc);
+  if (lane == 0) out[ht] = acc;
 }
 
 // dq/dk per k-head: sum the per-v-head gradients of each GQA group, cast.
 template <typename T>
-__global__ void reduce_gqa(int S, int Hk, int H, int Dk, const float* __restrict__ src, T* dst) {
-  const int t = blockIdx.x, hk = blockIdx.y, rep = H / Hk;
-  for (int d = threadIdx.x; d < Dk; d += blockDim.x) {
+__global__ void __launch_bounds__(32 * kTokWarps)
+reduce_gqa(int S, int Hk, int H, int Dk, const float* __restrict__ src, T* dst) {
+  const int t = blockIdx.x * kTokWarps + (threadIdx.x >> 5), hk = blockIdx.y, rep = H / Hk;
+  if (t >= S) return;
+  for (int d = threadIdx.x & 31; d < Dk; d += 32) {
     float a = 0.f;
     for (int r = 0; r < rep; ++r) a += src[(((long long)(hk * rep + r)) * S + t) * Dk + d];
     dst[((long long)t * Hk + hk) * Dk + d] = from_f32<T>(a);
@@ -839,15 +841,19 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     const int cnt = (int)p.levels[d].size();
     // states are [n+1][H][Dk][Dv]: per-head stride DkDv, segment offsets cover (c+1)*H*DkDv
     launch_gemm(b.d_desc, b.d_tiles, ds_ws[d], H, b.W, vk, b.states, DkDv, b.Vn, vv, -1.f, 1.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_qs[d], H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_aqv[d], H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f, st);
+    if (!backward) {   // the output; the backward (which recomputes this pass) never reads it
+      launch_gemm(b.d_desc, b.d_tiles, ds_qs[d], H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f,
+                  st);
+      launch_gemm(b.d_desc, b.d_tiles, ds_aqv[d], H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f,
+                  st);
+    }
     launch_gemm(b.d_desc, b.d_tiles, ds_kdv[d], H, b.Kd, vk, b.Vn, vv, b.states, DkDv, 1.f, 0.f, st);
     state_decay_add<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
         H, DkDv, n, b.d_level_nodes + level_first[d], b.d_parent, b.gl, b.states);
     ++launches;
   }
   if (!backward) {
-    store_out<T><<<dim3(S, H), 128, 0, st>>>(S, H, Dv, b.O, (T*)out_);
+    store_out<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(S, H, Dv, b.O, (T*)out_);
     ++launches;
     if (last_state) {
       TT_CUDA_OK(cudaMemcpyAsync(last_state, b.states + (long long)n * sh, sh * 4,
@@ -857,7 +863,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
   }
   // ---------------------------------------------------------------- backward
-  load_dout<T><<<dim3(S, H), 128, 0, st>>>(S, H, Dv, (const T*)dout_, b.dO);
+  load_dout<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(S, H, Dv, (const T*)dout_, b.dO);
   ++launches;
   for (int d = (int)p.levels.size() - 1; d >= 0; --d) {
     const int cnt = (int)p.levels[d].size();
@@ -903,14 +909,14 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   launch_gemm(b.d_desc, b.d_tiles, ds_gtk, H, b.dA, llh, b.Kb, vk, b.dK, vk, 1.f, 0.f, st);
   launch_gemm(b.d_desc, b.d_tiles, ds_gtk, H, b.dAqk, llh, b.Q, vk, b.dK, vk, 1.f, 1.f, st);
   launch_gemm(b.d_desc, b.d_tiles, ds_gk, H, b.dAqk, llh, b.K, vk, b.dQ, vk, 1.f, 0.f, st);
-  kd_dot_kernel<<<dim3(S, H), 128, 0, st>>>(S, Dk, b.Kd, b.dKd, b.kd_dot);
+  kd_dot_kernel<<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(S, Dk, b.Kd, b.dKd, b.kd_dot);
   assemble_token_grads<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(
       S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok, l2norm, q_scale, b.dQ, b.dQg, b.dK,
       b.dKd, b.dKb, b.dKbg, b.dVb, b.dgam, b.dq_h, b.dk_h, dbeta, (T*)dv_);
   node_dg<<<dim3((n + 127) / 128, H), 128, 0, st>>>(S, H, n, b.d_start, b.d_len, b.kd_dot, b.dgl,
                                                     b.dgam, dg);
-  reduce_gqa<T><<<dim3(S, Hk), 128, 0, st>>>(S, Hk, H, Dk, b.dq_h, (T*)dq_);
-  reduce_gqa<T><<<dim3(S, Hk), 128, 0, st>>>(S, Hk, H, Dk, b.dk_h, (T*)dk_);
+  reduce_gqa<T><<<dim3((S + kTokWarps - 1) / kTokWarps, Hk), 32 * kTokWarps, 0, st>>>(S, Hk, H, Dk, b.dq_h, (T*)dq_);
+  reduce_gqa<T><<<dim3((S + kTokWarps - 1) / kTokWarps, Hk), 32 * kTokWarps, 0, st>>>(S, Hk, H, Dk, b.dk_h, (T*)dk_);
   launches += 5;
   if (dinit) {
     dinit_kernel<<<blocks(sh), 256, 0, st>>>(H, DkDv, (int)p.roots.size(), b.d_roots, b.dSi, dinit);
