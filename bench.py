@@ -34,6 +34,8 @@ import torch  # noqa: E402
 METRIC = "Tree-attn fwd+bwd useful TFLOP/s & tokens/s at 1/2/4/8 B200"
 HQ, HKV, D = 32, 8, 128
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# nominal fp32 FMA rate: 148 SMs x 128 lanes x 2 flop x 1.965 GHz (not a measured figure)
+FP32_FMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 
 
 def parse():
@@ -659,6 +661,7 @@ def run_gdn(args):
           for _ in range(args.steps)]
     clocks.reset()
     launches0 = _lib.lib().tt_kernel_launches()
+    gemm0 = _lib.lib().tt_gdn_gemm_flops()
     barrier(world)
     for i in range(args.steps):
         flush.zero_()
@@ -667,6 +670,7 @@ def run_gdn(args):
         ev[i][1].record()
     torch.cuda.synchronize()
     launches = _lib.lib().tt_kernel_launches() - launches0
+    gemm_flops = (_lib.lib().tt_gdn_gemm_flops() - gemm0) / args.steps
     clk = clocks.stop()
     t = statistics.mean(a.elapsed_time(b) for a, b in ev) / 1e3
     t_max = max_over_ranks(t, world, dev)
@@ -688,6 +692,12 @@ def run_gdn(args):
                              "frac": achieved / float(pk["hbm_gbs"]), "traffic": None,
                              "algorithmic_bytes_per_token": gdn_bytes_per_token(),
                              "peak_source": pk_src},
+                # the step is dominated by fp32 segmented GEMMs: their algorithmic
+                # flops per step, and that work's rate over the whole step (a lower
+                # bound on the GEMM kernel's own rate)
+                "seg_gemm": {"gflop_per_step": gemm_flops / 1e9,
+                             "tflops_over_step": gemm_flops / t / 1e12,
+                             "fp32_fma_peak_tflops": FP32_FMA_PEAK_TFLOPS},
                 "gpu_launches": int(launches), "clocks": clk}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -59,6 +59,11 @@ int tt_set_kernel_path(int path);
  * own kernels ran inside a timed region. */
 int64_t tt_kernel_launches(void);
 
+/* Floating-point operations (2 M N K per segment and head) of the tree GDN's
+ * segmented GEMMs launched since the library was loaded: the algorithmic
+ * GEMM work, excluding the padding of partial 64 x 64 tiles. */
+int64_t tt_gdn_gemm_flops(void);
+
 /* Diagnostic: launches one kernel that waits, with the bounded wait every
  * tensor-core kernel uses, on an mbarrier phase nothing completes; after the
  * 2 s limit it records TT_ERR_DEVICE_TIMEOUT in *status (device memory) and

@@ -37,6 +37,7 @@ SIGNATURES = {
     "tt_abi_version": (_INT, []),
     "tt_set_kernel_path": (_INT, [_INT]),
     "tt_kernel_launches": (_I64, []),
+    "tt_gdn_gemm_flops": (_I64, []),
     "tt_diag_bounded_wait": (_INT, [_P, _P]),
     "tt_pack_forest": (_INT, [_I32, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _P, _P]),
     "tt_gateway_intervals_from_bias": (_INT, [_I32, _P, _I32, _P, _P]),

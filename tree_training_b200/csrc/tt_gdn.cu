@@ -22,6 +22,7 @@
 // atomics.  Internal layout: per-token vectors [H][S][D] fp32, per-node LxL
 // matrices packed per node ([H][sum L^2]), states [n_nodes+1][H][Dk][Dv].
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <vector>
 
@@ -598,7 +599,10 @@ struct Bufs {
 // Descriptor sets: built on the host in one vector, copied once, with the
 // exact list of 64 x 64 output tiles of each set (so no block of a launch
 // lands outside its segment).
-struct DescSet { int first, count, tfirst, tcount; };
+struct DescSet {
+  int first, count, tfirst, tcount;
+  double flops;   // 2 M N K summed over the set's segments, one head
+};
 
 struct Builder {
   const Plan& p;
@@ -606,8 +610,9 @@ struct Builder {
   std::vector<int2> tiles;
   explicit Builder(const Plan& pl) : p(pl) {}
   DescSet add(const std::vector<SegDesc>& v) {
-    DescSet d{(int)all.size(), (int)v.size(), (int)tiles.size(), 0};
+    DescSet d{(int)all.size(), (int)v.size(), (int)tiles.size(), 0, 0.0};
     for (size_t i = 0; i < v.size(); ++i) {
+      d.flops += 2.0 * v[i].M * v[i].N * v[i].K;
       const int tms = (v[i].M + kBM - 1) / kBM, tns = (v[i].N + kBN - 1) / kBN;
       for (int tm = 0; tm < tms; ++tm)
         for (int tn = 0; tn < tns; ++tn)
@@ -629,6 +634,8 @@ SegDesc desc(int M, int N, int K, long long ao, long long ars, long long acs, lo
   return d;
 }
 
+std::atomic<int64_t> g_gemm_flops{0};
+
 // Tiles address segments by their index in the whole descriptor array.
 void launch_gemm(const SegDesc* d_desc, const int2* d_tiles, DescSet ds, int H, const float* A,
                  long long a_hs, const float* B, long long b_hs, float* C, long long c_hs,
@@ -638,6 +645,7 @@ void launch_gemm(const SegDesc* d_desc, const int2* d_tiles, DescSet ds, int H, 
   seg_gemm<<<grid, kGemmThreads, 0, st>>>(d_desc, d_tiles + ds.tfirst, A, a_hs, B, b_hs, C, c_hs,
                                           alpha, beta);
   tt_count_launches(1);
+  g_gemm_flops.fetch_add(static_cast<int64_t>(ds.flops * H), std::memory_order_relaxed);
 }
 
 template <typename T>
@@ -1006,4 +1014,8 @@ extern "C" int tt_gdn_tree_bwd(int dtype, int32_t S, int32_t Hk, int32_t H, int3
                            nullptr, dout, dlast, dq, dk, dv, dg, dbeta, dinit,
                            (cudaStream_t)stream);
   });
+}
+
+extern "C" int64_t tt_gdn_gemm_flops(void) {
+  return tt::gdn::g_gemm_flops.load(std::memory_order_relaxed);
 }
