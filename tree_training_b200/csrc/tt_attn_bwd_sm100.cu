@@ -10,26 +10,29 @@
 //                 marks visible, as 64-row sub-tiles of Q and dO.
 //                 S^T = K Q^T and dP^T = V dO^T (A, B from shared memory); the
 //                 elementwise warps turn them into P^T and dS^T = P^T (dP^T -
-//                 delta), written back into TMEM as 16-bit; then dV += P^T dO
-//                 and dK += dS^T Q read A from TMEM.
-//   dQ kernel     one CTA per (q head, 128-row tile) holding Q and dO; streams
-//                 the visible kv tiles as 64-key sub-tiles of K and V:
-//                 S = Q K^T, dP = dO V^T, dS = P (dP - delta) into TMEM,
-//                 dQ += dS K.
+//                 delta), written as 16-bit tiles to shared memory; then
+//                 dV += P^T dO and dK += dS^T Q.
+//   dQ kernel     one CTA per (q head, 128-row tile); Q and dO are copied once
+//                 into TMEM as 16-bit A operands; streams the visible kv tiles
+//                 as 64-key sub-tiles of K and V: S = Q K^T, dP = dO V^T (A from
+//                 TMEM, B from shared memory), dS = P (dP - delta) as a 16-bit
+//                 tile in shared memory (the Q tile's space), dQ += dS K.
 //
-// Streamed sub-tiles go through a 4-stage ring (each stage: two 64 x 128
-// 16-bit sub-tiles + their 64 row terms or key intervals, bulk-copied on the
-// same mbarrier), released per sub-tile, so loads run three sub-tiles ahead.
-// Sub-tile S/dP accumulators rotate through NB TMEM buffers so the MMAs of
-// later sub-tiles run while the elementwise warps process sub-tile u.  TMEM
-// (512 cols), buffer b < NB: S [64b, 64b+64), dP [64NB+64b, 64NB+64b+64);
-//   dK/dV kernel, NB = 2: dV [256,384), dK [384,512);
-//   dQ kernel, NB = 3: dQ [384,512).
+// Streamed sub-tiles go through a ring (dK/dV 3 stages, dQ 4; each stage: two
+// 64 x 128 16-bit sub-tiles + their 64 row terms or key intervals, bulk-copied
+// on the same mbarrier), released per sub-tile.  Sub-tile S/dP accumulators
+// rotate through two TMEM buffers, each released as soon as the elementwise
+// warps have loaded it (not when the MMAs that consume P / dS finish), so the
+// S/dP MMAs of sub-tile u+2 can run while the elementwise warps still compute
+// sub-tile u.  P / dS tiles rotate through two shared-memory buffers, released
+// by the commit of the MMAs that read them.  TMEM (512 cols), buffer b < 2:
+// S [64b, 64b+64), dP [128+64b, 128+64b+64);
+//   dK/dV kernel: dV [256,384), dK [384,512);
+//   dQ kernel: dQ [256,384), Q [384,448), dO [448,512) (16-bit pairs).
 // Warps: 0 TMA producer, 1 S/dP MMA issuer, 2..9 elementwise (two warps per
 // TMEM lane quadrant; warp half h owns columns [32h, 32h+32) of each sub-tile
-// and writes its 16-bit P / dS into the first 16 of those columns, i.e. only
-// into columns it has already read, so the two warps never race), 10 the
-// issuer of the accumulating MMAs.
+// and the matching 64-byte half of each P / dS tile row), 10 the issuer of the
+// accumulating MMAs.
 #include <type_traits>
 
 #include "tt_sm100.cuh"
@@ -41,15 +44,18 @@ namespace {
 constexpr int kT = 128;                     // rows of the fixed tiles and of a list tile
 constexpr int kD = 128;                     // head dim
 constexpr int kSub = 64;                    // rows of a streamed sub-tile
-constexpr int kStages = 4;                  // streamed ring depth
+constexpr int kMaxStages = 4;               // streamed ring depth: dQ kernel 4, dK/dV kernel 3
+constexpr int kStagesDkdv = 3;
+constexpr int kStagesDq = 4;
 constexpr int kNbDkdv = 2;                  // S/dP TMEM buffers: dK/dV kernel (dV, dK fill the rest)
-constexpr int kNbDq = 3;                    // S/dP TMEM buffers: dQ kernel (3 x 128 + dQ 128 = 512)
+constexpr int kNbDq = 2;                    // S/dP TMEM buffers: dQ kernel (2 x 128 + dQ + Q/dO = 512)
 constexpr int kTileBytes = kT * kD * 2;     // fixed tile (128 rows)
 constexpr int kTileHalf = kTileBytes / 2;   // one 64-dim swizzle block of a fixed tile
 constexpr int kSubBytes = kSub * kD * 2;    // streamed sub-tile (64 rows)
 constexpr int kSubHalf = kSubBytes / 2;     // one 64-dim swizzle block of a sub-tile
 constexpr int kAuxHalf = kSub * 4;          // 64 four-byte entries
 constexpr int kAuxBytes = 2 * kAuxHalf;     // per stage: two 64-entry arrays
+constexpr int kPTile = kT * kSub * 2;       // 128 x 64 16-bit P / dS tile (A operand in smem)
 constexpr int kThreads = 352;            // 11 warps (roles below)
 constexpr int kEw = 256;                    // elementwise threads
 constexpr uint32_t kTmemCols = 512;
@@ -57,12 +63,14 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdBarriers {
   uint64_t fixed_full;       // the two tiles loaded once (K,V or Q,dO)
-  uint64_t a_full[kStages];  // streamed sub-tile A (Q or K) + its aux arrays
-  uint64_t b_full[kStages];  // streamed sub-tile B (dO or V)
-  uint64_t ab_empty[kStages];
-  uint64_t sdp_full[3];      // S and dP of a sub-tile ready (per TMEM buffer)
-  uint64_t ew_full[3];       // P / dS of a sub-tile written back (256 arrivals)
-  uint64_t buf_free[3];      // the accumulating MMAs of a TMEM buffer's sub-tile finished
+  uint64_t x_tmem_full;      // dQ kernel: Q and dO copied into TMEM (256 arrivals)
+  uint64_t a_full[kMaxStages];  // streamed sub-tile A (Q or K) + its aux arrays
+  uint64_t b_full[kMaxStages];  // streamed sub-tile B (dO or V)
+  uint64_t ab_empty[kMaxStages];
+  uint64_t sdp_full[2];      // S and dP of a sub-tile ready (per TMEM buffer)
+  uint64_t sdp_free[2];      // the elementwise warps loaded S and dP (256 arrivals)
+  uint64_t ew_full[2];       // P / dS of a sub-tile written to shared memory (256 arrivals)
+  uint64_t pa_free[2];       // the accumulating MMAs reading a P / dS buffer finished
   uint64_t acc_done;         // every MMA of the CTA finished
   uint64_t drain;            // abort path of the S/dP issuer
   uint64_t drain_acc;        // abort path of the accumulation issuer
@@ -70,8 +78,14 @@ struct BwdBarriers {
   int32_t abort;
 };
 
-constexpr size_t kSmemBytes = 1024 + 2 * kTileBytes + 2 * kStages * kSubBytes +
-                              kStages * kAuxBytes + sizeof(BwdBarriers);
+// dK/dV: K, V, the ring, P^T and dS^T tiles per buffer; dQ: Q, dO (whose space
+// holds the dS tiles once Q and dO sit in TMEM), the ring.
+constexpr size_t kSmemDkdv = 1024 + 2 * kTileBytes + kStagesDkdv * (2 * kSubBytes + kAuxBytes) +
+                             2 * kNbDkdv * kPTile + sizeof(BwdBarriers);
+constexpr size_t kSmemDq = 1024 + 2 * kTileBytes + kStagesDq * (2 * kSubBytes + kAuxBytes) +
+                           sizeof(BwdBarriers);
+static_assert(kSmemDkdv <= 232448 && kSmemDq <= 232448, "shared memory per block");
+static_assert(kNbDq * kPTile <= kTileBytes, "dS tiles alias the Q tile");
 
 __device__ __forceinline__ void raise_abort(BwdBarriers* sh, int32_t* status) {
   set_status(status, TT_ERR_DEVICE_TIMEOUT);
@@ -80,15 +94,17 @@ __device__ __forceinline__ void raise_abort(BwdBarriers* sh, int32_t* status) {
 
 __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
   mbar_init(&sh->fixed_full, 1);
-  for (int s = 0; s < kStages; ++s) {
+  mbar_init(&sh->x_tmem_full, kEw);
+  for (int s = 0; s < kMaxStages; ++s) {
     mbar_init(&sh->a_full[s], 1);
     mbar_init(&sh->b_full[s], 1);
     mbar_init(&sh->ab_empty[s], 1);
   }
-  for (int b = 0; b < 3; ++b) {
+  for (int b = 0; b < 2; ++b) {
     mbar_init(&sh->sdp_full[b], 1);
+    mbar_init(&sh->sdp_free[b], kEw);
     mbar_init(&sh->ew_full[b], kEw);
-    mbar_init(&sh->buf_free[b], 1);
+    mbar_init(&sh->pa_free[b], 1);
   }
   mbar_init(&sh->acc_done, 1);
   mbar_init(&sh->drain, 1);
@@ -117,16 +133,54 @@ __device__ __forceinline__ void mma_ss_n64(uint32_t d_tmem, uint64_t dx, uint64_
   }
 }
 
-// D[128 x 128] (+)= A[128 x 64, 16-bit in TMEM] * B[64 rows x 128 dims], B a
-// streamed sub-tile read MN-major.  A's 64 columns of K sit as two 16-column
-// groups at a_tmem and a_tmem + 32 (one per elementwise warp half).
-__device__ __forceinline__ void mma_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint64_t db,
+// D[128 x 64] = X[128 x 128, 16-bit in TMEM] * A[64 x 128]^T: X's dims d sit
+// as 16-bit pairs in columns x_tmem + d/2, A is a streamed K-major sub-tile.
+__device__ __forceinline__ void mma_ts_n64(uint32_t d_tmem, uint32_t x_tmem, uint64_t da,
+                                           uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < kD / 16; ++kk) {
+    const uint32_t oa = (kk >> 2) * kSubHalf + (kk & 3) * 32;
+    mma_ts(d_tmem, x_tmem + kk * 8, desc_add(da, oa), idesc, kk > 0 ? 1u : 0u);
+  }
+}
+
+// Copies row r, dims [64 half, 64 half + 64), of a fixed 128-row tile (K-major,
+// 128-byte swizzle: 16-byte chunk j of row r at chunk j ^ (r & 7)) into 32
+// TMEM columns of the calling thread's lane, two 16-bit dims per column.
+__device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int r, int half,
+                                                 uint32_t taddr) {
+  const uint8_t* row = tile + half * kTileHalf + r * 128;
+  uint32_t w[32];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint4 c = *reinterpret_cast<const uint4*>(row + ((j ^ (r & 7)) << 4));
+    w[4 * j] = c.x;
+    w[4 * j + 1] = c.y;
+    w[4 * j + 2] = c.z;
+    w[4 * j + 3] = c.w;
+  }
+  tmem_st32(taddr, w);
+}
+
+// D[128 x 128] (+)= A[128 x 64] * B[64 rows x 128 dims]: A a P / dS tile in
+// shared memory (K-major, 128-byte swizzle), B a streamed sub-tile read MN-major.
+__device__ __forceinline__ void mma_ss_k64(uint32_t d_tmem, uint64_t da, uint64_t db,
                                            uint32_t idesc, bool accumulate) {
 #pragma unroll
-  for (int kk = 0; kk < kSub / 16; ++kk) {
-    const uint32_t a = a_tmem + (kk < 2 ? kk * 8 : 32 + (kk - 2) * 8);
-    mma_ts(d_tmem, a, desc_add(db, kk * 2048), idesc, (accumulate || kk > 0) ? 1u : 0u);
-  }
+  for (int kk = 0; kk < kSub / 16; ++kk)
+    mma_ss(d_tmem, desc_add(da, kk * 32), desc_add(db, kk * 2048), idesc,
+           (accumulate || kk > 0) ? 1u : 0u);
+}
+
+// Writes 32 16-bit values (w: 16 pairs) as columns [32 half, 32 half + 32) of
+// row r of a P / dS tile: 128-byte rows, 16-byte chunk j stored at j ^ (r & 7).
+__device__ __forceinline__ void store_tile_row(uint8_t* tile, int r, int half,
+                                               const uint32_t (&w)[16]) {
+  uint8_t* row = tile + r * 128;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    *reinterpret_cast<uint4*>(row + (((4 * half + c) ^ (r & 7)) << 4)) =
+        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
 }
 
 template <bool kBf16>
@@ -147,16 +201,16 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // Streams `n_u` (A, B) sub-tile pairs through the ring; `coord(u, &row,
 // &head, &aux_a, &aux_b)` gives the sub-tile's first row / head and the two
 // 256-byte arrays to bulk-copy with sub-tile A.
-template <typename Coord>
+template <int KS, typename Coord>
 __device__ __forceinline__ void produce(BwdBarriers* sh, const volatile int32_t* abort_flag,
                                         int32_t* status, int n_u, uint8_t* ringA, uint8_t* ringB,
                                         uint8_t* aux, const CUtensorMap* ta,
                                         const CUtensorMap* tb, Coord coord) {
-  int issued[kStages] = {0, 0, 0, 0};
+  int issued[KS] = {};
   bool ok = true;
   for (int u = 0; u < n_u; ++u) {
-    const int s = u % kStages;
-    if (u >= kStages) ok = mbar_wait(&sh->ab_empty[s], ((u / kStages) - 1) & 1, abort_flag);
+    const int s = u % KS;
+    if (u >= KS) ok = mbar_wait(&sh->ab_empty[s], ((u / KS) - 1) & 1, abort_flag);
     if (!ok) break;
     int row, head;
     const void *xa, *xb;
@@ -177,7 +231,7 @@ __device__ __forceinline__ void produce(BwdBarriers* sh, const volatile int32_t*
   if (!ok) {
     raise_abort(sh, status);
     mbar_wait(&sh->fixed_full, 0, nullptr);
-    for (int s = 0; s < kStages; ++s)
+    for (int s = 0; s < KS; ++s)
       if (issued[s] > 0) {
         mbar_wait(&sh->a_full[s], (issued[s] - 1) & 1, nullptr);
         mbar_wait(&sh->b_full[s], (issued[s] - 1) & 1, nullptr);
@@ -189,31 +243,39 @@ __device__ __forceinline__ void produce(BwdBarriers* sh, const volatile int32_t*
 // issues tcgen05.mma runs at most about one MMA ahead of the tensor pipe, so
 // every barrier wait of a single issuer leaves the pipe idle; with two
 // issuers each one's waits are covered by the other's MMAs.  Sub-tile u uses
-// ring stage s = u % kStages and TMEM buffer b = u % 2:
+// ring stage s = u % KS and buffer b = u % 2:
 //   S/dP issuer (warp 1):  S_b = X * A_s^T, dP_b = Y * B_s^T  (X, Y the fixed
-//       tiles), after the stage landed and after the accumulating MMAs of
-//       sub-tile u-2 released buffer b (buf_free);
-//   accumulation issuer (warp 10): the kernel's TS products reading P_b / dS_b
-//       once the elementwise warps wrote them back (ew_full); it alone
+//       tiles), after the stage landed and after the elementwise warps loaded
+//       sub-tile u-2's S/dP out of TMEM buffer b (sdp_free);
+//   accumulation issuer (warp 10): the kernel's products reading the P / dS
+//       tiles once the elementwise warps wrote them (ew_full); it alone
 //       accumulates into dK/dV or dQ, in sub-tile order, so the result does
-//       not depend on how the two instruction streams interleave.
-template <int NB>
+//       not depend on how the two instruction streams interleave.  Its commit
+//       releases the P / dS buffer (pa_free) and the ring stage (ab_empty).
+// kXTmem: the fixed tiles X, Y are A operands in TMEM (x_addr, y_addr are TMEM
+// column addresses, filled by the elementwise warps) instead of shared memory.
+template <int NB, int KS, bool kXTmem>
 __device__ __forceinline__ void sdp_issuer(BwdBarriers* sh, const volatile int32_t* abort_flag,
                                            int32_t* status, uint32_t tmem, int n_u,
                                            uint32_t x_addr, uint32_t y_addr, uint32_t ring_a,
                                            uint32_t ring_b, uint32_t id_s) {
-  bool ok = mbar_wait(&sh->fixed_full, 0, abort_flag);
+  bool ok = mbar_wait(kXTmem ? &sh->x_tmem_full : &sh->fixed_full, 0, abort_flag);
   const uint64_t dx = desc_sw128(x_addr, 16, 1024), dy = desc_sw128(y_addr, 16, 1024);
   const uint64_t da = desc_sw128(ring_a, 16, 1024), db = desc_sw128(ring_b, 16, 1024);
   for (int u = 0; u < n_u && ok; ++u) {
-    const int s = u % kStages, b = u % NB;
-    const uint32_t ph = (u / kStages) & 1;
-    if (u >= NB && !(ok = mbar_wait(&sh->buf_free[b], ((u - NB) / NB) & 1, abort_flag))) break;
+    const int s = u % KS, b = u % NB;
+    const uint32_t ph = (u / KS) & 1;
+    if (u >= NB && !(ok = mbar_wait(&sh->sdp_free[b], ((u - NB) / NB) & 1, abort_flag))) break;
     if (!(ok = mbar_wait(&sh->a_full[s], ph, abort_flag))) break;
     if (!(ok = mbar_wait(&sh->b_full[s], ph, abort_flag))) break;
     tc_fence_after();
-    mma_ss_n64(tmem + 64 * b, dx, desc_add(da, s * kSubBytes), id_s);
-    mma_ss_n64(tmem + 64 * NB + 64 * b, dy, desc_add(db, s * kSubBytes), id_s);
+    if (kXTmem) {
+      mma_ts_n64(tmem + 64 * b, x_addr, desc_add(da, s * kSubBytes), id_s);
+      mma_ts_n64(tmem + 64 * NB + 64 * b, y_addr, desc_add(db, s * kSubBytes), id_s);
+    } else {
+      mma_ss_n64(tmem + 64 * b, dx, desc_add(da, s * kSubBytes), id_s);
+      mma_ss_n64(tmem + 64 * NB + 64 * b, dy, desc_add(db, s * kSubBytes), id_s);
+    }
     tc_commit(&sh->sdp_full[b]);
   }
   if (!ok) {
@@ -223,16 +285,16 @@ __device__ __forceinline__ void sdp_issuer(BwdBarriers* sh, const volatile int32
   }
 }
 
-template <int NB, typename Acc>
+template <int NB, int KS, typename Acc>
 __device__ __forceinline__ void acc_issuer(BwdBarriers* sh, const volatile int32_t* abort_flag,
                                            int32_t* status, int n_u, Acc acc) {
   bool ok = true;
   for (int u = 0; u < n_u && ok; ++u) {
-    const int b = u % NB, s = u % kStages;
+    const int b = u % NB, s = u % KS;
     if (!(ok = mbar_wait(&sh->ew_full[b], (u / NB) & 1, abort_flag))) break;
     tc_fence_after();
     acc(s, b, u > 0);
-    tc_commit(&sh->buf_free[b]);
+    tc_commit(&sh->pa_free[b]);
     // the stage's last reader: sdp(u) completed before the elementwise warps
     // started on sub-tile u, and acc(u) waited for them
     tc_commit(&sh->ab_empty[s]);
@@ -262,10 +324,13 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   uint8_t* base = align1024(smem_raw);
   uint8_t* sK = base;
   uint8_t* sV = sK + kTileBytes;
-  uint8_t* rQ = sV + kTileBytes;                 // kStages x Q sub-tile
-  uint8_t* rDO = rQ + kStages * kSubBytes;       // kStages x dO sub-tile
-  uint8_t* aux = rDO + kStages * kSubBytes;      // kStages x (LSE[64], delta[64])
-  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + kStages * kAuxBytes);
+  constexpr int KS = kStagesDkdv;
+  uint8_t* rQ = sV + kTileBytes;                 // KS x Q sub-tile
+  uint8_t* rDO = rQ + KS * kSubBytes;            // KS x dO sub-tile
+  uint8_t* sPt = rDO + KS * kSubBytes;           // kNbDkdv x P^T tile
+  uint8_t* sDSt = sPt + kNbDkdv * kPTile;        // kNbDkdv x dS^T tile
+  uint8_t* aux = sDSt + kNbDkdv * kPTile;        // KS x (LSE[64], delta[64])
+  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + KS * kAuxBytes);
   const volatile int32_t* abort_flag = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -296,7 +361,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tma_load_3d(sK + kTileHalf, &tm_k, &sh->fixed_full, 64, kt * kT, hk);
       tma_load_3d(sV, &tm_v, &sh->fixed_full, 0, kt * kT, hk);
       tma_load_3d(sV + kTileHalf, &tm_v, &sh->fixed_full, 64, kt * kT, hk);
-      produce(sh, abort_flag, status, n_u, rQ, rDO, aux, &tm_q, &tm_do,
+      produce<KS>(sh, abort_flag, status, n_u, rQ, rDO, aux, &tm_q, &tm_do,
               [&](int u, int* row, int* head, const void** xa, const void** xb) {
                 const int it = u >> 1;
                 const int h = hk * rep + it / n_list;
@@ -310,7 +375,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   } else if (warp == 1) {
     if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
-      sdp_issuer<kNbDkdv>(sh, abort_flag, status, tmem, n_u, smem_u32(sK), smem_u32(sV), smem_u32(rQ),
+      sdp_issuer<kNbDkdv, KS, false>(sh, abort_flag, status, tmem, n_u, smem_u32(sK), smem_u32(sV), smem_u32(rQ),
                  smem_u32(rDO), id_s);
     }
   } else if (warp == 10) {
@@ -319,10 +384,13 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       // B of dV += P^T dO and dK += dS^T Q: the ring's dO / Q sub-tiles, MN-major
       const uint64_t d_do = desc_sw128(smem_u32(rDO), kSubHalf, 1024);
       const uint64_t d_q = desc_sw128(smem_u32(rQ), kSubHalf, 1024);
-      acc_issuer<kNbDkdv>(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
-        mma_ts_k64(tmem + kColDV, tmem + 64 * b, desc_add(d_do, s * kSubBytes), id_o,
-                   accumulate);
-        mma_ts_k64(tmem + kColDK, tmem + 64 * kNbDkdv + 64 * b, desc_add(d_q, s * kSubBytes),
+      // A of dV += P^T dO and dK += dS^T Q: the P^T / dS^T tiles, K-major
+      const uint64_t d_pt = desc_sw128(smem_u32(sPt), 16, 1024);
+      const uint64_t d_dst = desc_sw128(smem_u32(sDSt), 16, 1024);
+      acc_issuer<kNbDkdv, KS>(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
+        mma_ss_k64(tmem + kColDV, desc_add(d_pt, b * kPTile), desc_add(d_do, s * kSubBytes),
+                   id_o, accumulate);
+        mma_ss_k64(tmem + kColDK, desc_add(d_dst, b * kPTile), desc_add(d_q, s * kSubBytes),
                    id_o, accumulate);
       });
     }
@@ -336,18 +404,20 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     bool ok = true;
     for (int u = 0; u < n_u; ++u) {
-      const int it = u >> 1, b = u % kNbDkdv, s = u % kStages;
+      const int it = u >> 1, b = u % kNbDkdv, s = u % KS;
       const int ent = bwd_list[e0 + it % n_list];
       const int q0 = (ent >> 1) * kT + (u & 1) * kSub + half * 32;   // first q row of this warp
       const bool partial = ent & 1;
       ok = mbar_wait(&sh->sdp_full[b], (u / kNbDkdv) & 1, abort_flag);
-      if (ok) ok = mbar_wait(&sh->a_full[s], (u / kStages) & 1, abort_flag);   // aux visible
+      if (ok) ok = mbar_wait(&sh->a_full[s], (u / KS) & 1, abort_flag);   // aux visible
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       const uint32_t cs = 64 * b + 32 * half, cp = 64 * kNbDkdv + 64 * b + 32 * half;
       float sv[32], dp[32];
       tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
+      tc_fence_before();
+      mbar_arrive(&sh->sdp_free[b]);           // the S/dP buffer may be overwritten
       const float4* L4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes) + half * 8;
       const float4* D4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes + kAuxHalf) + half * 8;
       uint32_t pw[16], dw[16];
@@ -381,10 +451,14 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         dw[2 * i] = pack2<kBf16>(ds01.x, ds01.y);
         dw[2 * i + 1] = pack2<kBf16>(ds23.x, ds23.y);
       }
-      tmem_st16(lane_addr + cs, pw);
-      tmem_st16(lane_addr + cp, dw);
-      tmem_st_wait();
-      tc_fence_before();
+      if (u >= kNbDkdv) {                      // the MMAs of sub-tile u - 2 read this buffer
+        ok = mbar_wait(&sh->pa_free[b], ((u - kNbDkdv) / kNbDkdv) & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+      }
+      store_tile_row(sPt + b * kPTile, r, half, pw);
+      store_tile_row(sDSt + b * kPTile, r, half, dw);
+      fence_proxy_async_smem();
       mbar_arrive(&sh->ew_full[b]);
     }
     if (ok && n_u > 0) {
@@ -436,10 +510,12 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   uint8_t* base = align1024(smem_raw);
   uint8_t* sQ = base;
   uint8_t* sDO = sQ + kTileBytes;
-  uint8_t* rK = sDO + kTileBytes;                // kStages x K sub-tile
-  uint8_t* rV = rK + kStages * kSubBytes;        // kStages x V sub-tile
-  uint8_t* aux = rV + kStages * kSubBytes;       // kStages x (kv_lo[64], kv_hi[64])
-  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + kStages * kAuxBytes);
+  constexpr int KS = kStagesDq;
+  uint8_t* rK = sDO + kTileBytes;                // KS x K sub-tile
+  uint8_t* rV = rK + KS * kSubBytes;             // KS x V sub-tile
+  uint8_t* aux = rV + KS * kSubBytes;            // KS x (kv_lo[64], kv_hi[64])
+  uint8_t* sDS = sQ;                             // kNbDq x dS tile, once Q is in TMEM
+  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + KS * kAuxBytes);
   const volatile int32_t* abort_flag = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -460,6 +536,8 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
   constexpr uint32_t kColDQ = 128 * kNbDq;   // after the S/dP buffers
+  constexpr uint32_t kColQ = kColDQ + 128, kColDO = kColQ + 64;   // Q, dO as 16-bit pairs
+  static_assert(kColDO + 64 == kTmemCols, "dQ kernel TMEM map");
 
   if (warp == 0) {
     if (lane == 0 && n_u > 0) {
@@ -470,7 +548,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tma_load_3d(sQ + kTileHalf, &tm_q, &sh->fixed_full, 64, qt * kT, h);
       tma_load_3d(sDO, &tm_do, &sh->fixed_full, 0, qt * kT, h);
       tma_load_3d(sDO + kTileHalf, &tm_do, &sh->fixed_full, 64, qt * kT, h);
-      produce(sh, abort_flag, status, n_u, rK, rV, aux, &tm_k, &tm_v,
+      produce<KS>(sh, abort_flag, status, n_u, rK, rV, aux, &tm_k, &tm_v,
               [&](int u, int* row, int* head, const void** xa, const void** xb) {
                 const int j0 = (fwd_list[e0 + (u >> 1)] >> 1) * kT + (u & 1) * kSub;
                 *row = j0;
@@ -482,15 +560,17 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   } else if (warp == 1) {
     if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
-      sdp_issuer<kNbDq>(sh, abort_flag, status, tmem, n_u, smem_u32(sQ), smem_u32(sDO), smem_u32(rK),
-                 smem_u32(rV), id_s);
+      sdp_issuer<kNbDq, KS, true>(sh, abort_flag, status, tmem, n_u, tmem + kColQ, tmem + kColDO,
+                              smem_u32(rK), smem_u32(rV), id_s);
     }
   } else if (warp == 10) {
     if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_o = idesc_f16(kBf16, kT, kD, true);
       const uint64_t d_k = desc_sw128(smem_u32(rK), kSubHalf, 1024);   // B of dQ += dS K
-      acc_issuer<kNbDq>(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
-        mma_ts_k64(tmem + kColDQ, tmem + 64 * b, desc_add(d_k, s * kSubBytes), id_o, accumulate);
+      const uint64_t d_ds = desc_sw128(smem_u32(sDS), 16, 1024);        // A: the dS tiles
+      acc_issuer<kNbDq, KS>(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
+        mma_ss_k64(tmem + kColDQ, desc_add(d_ds, b * kPTile), desc_add(d_k, s * kSubBytes), id_o,
+                   accumulate);
       });
     }
   } else {
@@ -502,17 +582,35 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     const float l2 = lse[static_cast<int64_t>(h) * ld + row] * kLog2e;   // padded rows: +inf
     const float dr = delta[static_cast<int64_t>(h) * ld + row];
     bool ok = true;
-    for (int u = 0; u < n_u; ++u) {
-      const int b = u % kNbDq, s = u % kStages;
+    if (n_u > 0) {
+      // Q and dO rows into TMEM, where S = Q K^T and dP = dO V^T read their A
+      // operand (shared memory then only feeds the streamed K / V sub-tiles)
+      ok = mbar_wait(&sh->fixed_full, 0, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tile_row_to_tmem(sQ, r, half, lane_addr + kColQ + 32 * half);
+        tile_row_to_tmem(sDO, r, half, lane_addr + kColDO + 32 * half);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sh->x_tmem_full);
+      }
+      // every elementwise thread has read its Q rows before any dS row lands
+      // in the Q tile's space (all 256 reach this point: the wait is bounded)
+      asm volatile("bar.sync 1, %0;" ::"n"(kEw) : "memory");
+    }
+    for (int u = 0; u < n_u && ok; ++u) {
+      const int b = u % kNbDq, s = u % KS;
       const bool partial = fwd_list[e0 + (u >> 1)] & 1;
       ok = mbar_wait(&sh->sdp_full[b], (u / kNbDq) & 1, abort_flag);
-      if (ok && partial) ok = mbar_wait(&sh->a_full[s], (u / kStages) & 1, abort_flag);
+      if (ok && partial) ok = mbar_wait(&sh->a_full[s], (u / KS) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       const uint32_t cs = 64 * b + 32 * half, cp = 64 * kNbDq + 64 * b + 32 * half;
       float sv[32], dp[32];
       tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
+      tc_fence_before();
+      mbar_arrive(&sh->sdp_free[b]);           // the S/dP buffer may be overwritten
       float p[32];
       const float2 sc2 = make_float2(scale_log2, scale_log2), nl2 = make_float2(-l2, -l2);
 #pragma unroll
@@ -544,9 +642,13 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
                                 fadd2(make_float2(dp[2 * i], dp[2 * i + 1]), ndr));
         dw[i] = pack2<kBf16>(ds.x, ds.y);
       }
-      tmem_st16(lane_addr + cs, dw);
-      tmem_st_wait();
-      tc_fence_before();
+      if (u >= kNbDq) {                        // the MMAs of sub-tile u - 2 read this buffer
+        ok = mbar_wait(&sh->pa_free[b], ((u - kNbDq) / kNbDq) & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+      }
+      store_tile_row(sDS + b * kPTile, r, half, dw);
+      fence_proxy_async_smem();
       mbar_arrive(&sh->ew_full[b]);
     }
     if (ok && n_u > 0) {
@@ -711,9 +813,9 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
     if ((rc = make_map(&mdo, bf16, dout, n_q, hq, do_st, do_sh, kSub)) != TT_OK) return rc;
     auto kdkdv = bf16 ? attn_bwd_dkdv_tc<true> : attn_bwd_dkdv_tc<false>;
     TT_CUDA_OK(cudaFuncSetAttribute(kdkdv, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)kSmemBytes));
+                                    (int)kSmemDkdv));
     dim3 g(hkv, (n_kv + kT - 1) / kT);
-    kdkdv<<<g, kThreads, kSmemBytes, st>>>(mq, mk, mv, mdo, n_q, n_kv, rep, kv_lo, kv_hi,
+    kdkdv<<<g, kThreads, kSmemDkdv, st>>>(mq, mk, mv, mdo, n_q, n_kv, rep, kv_lo, kv_hi,
                                            bwd_ptr, bwd_list, lse, delta, scale_log2, scale, dk,
                                            dk_st, dk_sh, dv, dv_st, dv_sh, status);
     ++launches;
@@ -727,9 +829,9 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
     if ((rc = make_map(&mdo, bf16, dout, n_q, hq, do_st, do_sh, kT)) != TT_OK) return rc;
     auto kdq = bf16 ? attn_bwd_dq_tc<true> : attn_bwd_dq_tc<false>;
     TT_CUDA_OK(cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)kSmemBytes));
+                                    (int)kSmemDq));
     dim3 g(hq, (n_q + kT - 1) / kT);
-    kdq<<<g, kThreads, kSmemBytes, st>>>(mq, mk, mv, mdo, n_q, n_kv, rep, kv_lo, kv_hi, fwd_ptr,
+    kdq<<<g, kThreads, kSmemDq, st>>>(mq, mk, mv, mdo, n_q, n_kv, rep, kv_lo, kv_hi, fwd_ptr,
                                          fwd_list, lse, delta, scale_log2, scale, dq, dq_st,
                                          dq_sh, status);
     ++launches;
