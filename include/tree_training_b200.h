@@ -219,16 +219,24 @@ int64_t tt_tree_attn_bwd_noalloc_max_row_terms(void);
  * [bounds[2i], bounds[2i+1]), parent < i or -1, pre-order).  initial_state:
  * fp32 [H, Dk, Dv] or NULL (zeros).  out: [S, H, Dv] in `dtype`; last_state:
  * fp32 [H, Dk, Dv] = state after the LAST DFS node (tree_dfs_ssm.py:155), or
- * NULL.  use_qk_l2norm: x * rsqrt(sum x^2 + 1e-6) on q and k first (:67-69).
- * Dk, Dv <= 256.  Workspace: tt_gdn_tree_workspace_size(..., backward=0/1).
+ * NULL.  flags: TT_GDN_QK_L2NORM = x * rsqrt(sum x^2 + 1e-6) on q and k first
+ * (the reference's use_qk_l2norm_in_kernel, :67-69); TT_GDN_EXACT_INVERSE =
+ * replace the reference's truncated correction by the delta rule's exact
+ * T = (I - A)^-1 per node (the token-by-token recurrence's result, which the
+ * reference approximates); any other bit is TT_ERR_INVALID_ARG.
+ * Dk, Dv <= 256.  Workspace: tt_gdn_tree_workspace_size(..., backward=0/1),
+ * the same for either flag.
  */
+#define TT_GDN_QK_L2NORM 1
+#define TT_GDN_EXACT_INVERSE 2
+
 int64_t tt_gdn_tree_workspace_size(int32_t S, int32_t H, int32_t Dk, int32_t Dv,
                                    int32_t n_nodes, const int32_t* bounds, int backward);
 
 int tt_gdn_tree_fwd(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
                     const void* q, const void* k, const void* v, const float* g,
                     const float* beta, int32_t n_nodes, const int32_t* bounds,
-                    const int32_t* parents, const float* initial_state, int use_qk_l2norm,
+                    const int32_t* parents, const float* initial_state, int flags,
                     void* out, float* last_state, void* workspace, int64_t workspace_bytes,
                     void* stream);
 
@@ -240,7 +248,7 @@ int tt_gdn_tree_fwd(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int
 int tt_gdn_tree_bwd(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
                     const void* q, const void* k, const void* v, const float* g,
                     const float* beta, int32_t n_nodes, const int32_t* bounds,
-                    const int32_t* parents, const float* initial_state, int use_qk_l2norm,
+                    const int32_t* parents, const float* initial_state, int flags,
                     const void* dout, const float* dlast, void* dq, void* dk, void* dv,
                     float* dg, float* dbeta, float* dinit, void* workspace,
                     int64_t workspace_bytes, void* stream);

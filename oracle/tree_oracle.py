@@ -311,8 +311,20 @@ def _gqa_expand(q, hv):
     return np.repeat(q, hv // hq, axis=2)
 
 
+def _correction(A, exact_inverse):
+    """The intra-node operator T applied to beta*v and beta*k*e^gam.  The
+    reference's row loop (tree_dfs_ssm.py:119-126) uses uncorrected earlier
+    rows, which is exactly T = I + A + A^2; ``exact_inverse`` gives the delta
+    rule's exact T = (I - A)^-1 (what the in-place row loop of
+    transformers' torch_chunk_gated_delta_rule computes)."""
+    L = A.shape[-1]
+    if exact_inverse:
+        return np.linalg.inv(np.eye(L) - A)
+    return np.eye(L) + A + A @ A
+
+
 def gdn_tree_fwd(query, key, value, g, beta, bounds, parents, initial_state=None,
-                 use_qk_l2norm=False):
+                 use_qk_l2norm=False, exact_inverse=False):
     """Tree-routed chunk gated delta rule, one chunk per tree node.
 
     query/key [B,S,Hk,Dk] (Hk == H, or H // Hk v-heads per k-head), value
@@ -353,7 +365,7 @@ def gdn_tree_fwd(query, key, value, g, beta, bounds, parents, initial_state=None
         kb = ki * bi[..., None]
         vb = vi * bi[..., None]
         A = np.where(low_excl, -(kb @ np.swapaxes(ki, -1, -2)) * decay, 0.0)     # :116
-        T = np.eye(L) + A + A @ A                                         # :119-126
+        T = _correction(A, exact_inverse)                                 # :119-126
         U = T @ vb                                                        # :127
         W = T @ (kb * np.exp(gam)[..., None])                             # :128
         Sin = states[parents[i] + 1]                                      # :131-132
@@ -368,7 +380,8 @@ def gdn_tree_fwd(query, key, value, g, beta, bounds, parents, initial_state=None
 
 
 def gdn_tree_bwd(query, key, value, g, beta, bounds, parents, dout,
-                 initial_state=None, use_qk_l2norm=False, dlast_state=None):
+                 initial_state=None, use_qk_l2norm=False, dlast_state=None,
+                 exact_inverse=False):
     """Analytic gradients of :func:`gdn_tree_fwd` (the reference relies on
     torch autograd through tree_dfs_ssm.py:92-156; this restates that
     gradient).  ``dlast_state`` is the gradient of ``last_state`` = the state
@@ -391,7 +404,7 @@ def gdn_tree_bwd(query, key, value, g, beta, bounds, parents, dout,
     sc = Dk ** -0.5
     qs = q * sc
     _, states = gdn_tree_fwd(query, key, value, g, beta, bounds, parents,
-                             initial_state, use_qk_l2norm)
+                             initial_state, use_qk_l2norm, exact_inverse)
     n = len(bounds)
     dstate = [np.zeros((B, H, Dk, Dv)) for _ in range(n + 1)]
     if dlast_state is not None:
@@ -417,7 +430,7 @@ def gdn_tree_bwd(query, key, value, g, beta, bounds, parents, dout,
         vb = vi * bi[..., None]
         KK = kb @ np.swapaxes(ki, -1, -2)
         A = np.where(le, -KK * D, 0.0)
-        T = np.eye(L) + A + A @ A
+        T = _correction(A, exact_inverse)
         Kbg = kb * eg[..., None]
         U = T @ vb
         W = T @ Kbg
@@ -439,7 +452,10 @@ def gdn_tree_bwd(query, key, value, g, beta, bounds, parents, dout,
         dT = dVn @ tr(vb) + dW @ tr(Kbg)
         dvb = tr(T) @ dVn
         dKbg = tr(T) @ dW
-        dA = np.where(le, dT + dT @ tr(A) + tr(A) @ dT, 0.0)
+        if exact_inverse:       # T = (I - A)^-1: dL/dA = T^T dT T^T
+            dA = np.where(le, tr(T) @ dT @ tr(T), 0.0)
+        else:                   # T = I + A + A^2
+            dA = np.where(le, dT + dT @ tr(A) + tr(A) @ dT, 0.0)
         dgam = np.zeros_like(gam)
         # A = -(kb k^T) * D on the strict lower triangle
         Gm = -dA * D
@@ -493,6 +509,47 @@ def gdn_tree_bwd(query, key, value, g, beta, bounds, parents, dout,
         dk = _l2norm_bwd(k0, dk)
     return (dq, dk, dv.transpose(0, 2, 1, 3), dg.transpose(0, 2, 1),
             dbt.transpose(0, 2, 1), dstate[0])
+
+
+def gdn_tree_recurrent(query, key, value, g, beta, bounds, parents, initial_state=None,
+                       use_qk_l2norm=False):
+    """The gated delta rule token by token along each root-to-node path, in
+    float64: the per-token recurrence of transformers'
+    torch_recurrent_gated_delta_rule (models/qwen3_5_moe/modeling_qwen3_5_moe.py,
+    lines 315-354: S <- S e^g; delta = beta (v - S^T k); S <- S + k delta^T;
+    o = S^T q with q scaled by Dk^-1/2), each node starting from the state
+    after its parent node.  Independent of how tokens are grouped into nodes,
+    so it is the exact operator the chunked forms approximate (reference,
+    T = I + A + A^2) or reproduce (exact inverse).  Same shapes and return
+    value as :func:`gdn_tree_fwd`."""
+    H = value.shape[2]
+    q = np.asarray(query, np.float64)
+    k = np.asarray(key, np.float64)
+    if use_qk_l2norm:
+        q = _l2norm(q)
+        k = _l2norm(k)
+    q = _gqa_expand(q, H).transpose(0, 2, 1, 3)
+    k = _gqa_expand(k, H).transpose(0, 2, 1, 3)
+    v = np.asarray(value, np.float64).transpose(0, 2, 1, 3)
+    bt = np.asarray(beta, np.float64).transpose(0, 2, 1)
+    gg = np.asarray(g, np.float64).transpose(0, 2, 1)
+    B, _, S, Dk = k.shape
+    Dv = v.shape[-1]
+    q = q * (Dk ** -0.5)
+    init = (np.zeros((B, H, Dk, Dv)) if initial_state is None
+            else np.asarray(initial_state, np.float64))
+    states = [init]
+    out = np.zeros((B, H, S, Dv))
+    for i, (cs, ce) in enumerate(bounds):
+        St = states[parents[i] + 1].copy()
+        for t in range(cs, ce):
+            St = St * np.exp(gg[:, :, t])[..., None, None]
+            kv = np.einsum("bhkv,bhk->bhv", St, k[:, :, t])
+            delta = (v[:, :, t] - kv) * bt[:, :, t][..., None]
+            St = St + k[:, :, t][..., :, None] * delta[..., None, :]
+            out[:, :, t] = np.einsum("bhkv,bhk->bhv", St, q[:, :, t])
+        states.append(St)
+    return out.transpose(0, 2, 1, 3), np.stack(states)
 
 
 # ---------------------------------------------------------------------------

@@ -247,6 +247,37 @@ __global__ void decay_masks(int S, const int* __restrict__ nstart, const int* __
   }
 }
 
+// Exact-inverse mode, first step: each 64 x 64 diagonal block of a node's A
+// (the trailing block may be smaller) is replaced in place by
+// T_ii = (I - A_ii)^-1, by forward substitution T = I + A T.  Column c of
+// T_ii depends only on column c of the rows above it, so thread c owns it.
+constexpr int kInvB = 64;
+__global__ void __launch_bounds__(kInvB)
+tri_inv_diag(const int2* __restrict__ blocks, const int* __restrict__ nlen,
+             const long long* __restrict__ loff, long long l_hs, float* Am) {
+  const int2 bl = blocks[blockIdx.x];
+  const int c = bl.x, i0 = bl.y * kInvB, h = blockIdx.y;
+  const int L = nlen[c];
+  const int bs = min(kInvB, L - i0);
+  float* base = Am + h * l_hs + loff[c] + (long long)i0 * L + i0;
+  __shared__ float sA[kInvB][kInvB + 1];
+  __shared__ float sT[kInvB][kInvB + 1];
+  for (int idx = threadIdx.x; idx < bs * bs; idx += blockDim.x)
+    sA[idx / bs][idx % bs] = base[(long long)(idx / bs) * L + idx % bs];
+  __syncthreads();
+  const int col = threadIdx.x;
+  if (col < bs) {
+    for (int r = 0; r < bs; ++r) {
+      float t = r == col ? 1.f : 0.f;
+      for (int j = col; j < r; ++j) t = fmaf(sA[r][j], sT[j][col], t);
+      sT[r][col] = r >= col ? t : 0.f;
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < bs * bs; idx += blockDim.x)
+    base[(long long)(idx / bs) * L + idx % bs] = sT[idx / bs][idx % bs];
+}
+
 __global__ void add_arrays(long long n, const float* __restrict__ a, const float* __restrict__ b,
                            float* out) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -594,6 +625,7 @@ struct Bufs {
   long long* d_loff;
   SegDesc* d_desc;
   int2* d_tiles;
+  int2* d_inv_blocks;   // (node, diagonal block) pairs of the exact-inverse mode
 };
 
 // Descriptor sets: built on the host in one vector, copied once, with the
@@ -650,12 +682,14 @@ void launch_gemm(const SegDesc* d_desc, const int2* d_tiles, DescSet ds, int H, 
 
 template <typename T>
 int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_, const void* v_,
-        const float* g, const float* beta, const float* init, int l2norm, void* out_,
+        const float* g, const float* beta, const float* init, int flags, void* out_,
         float* last_state, const void* dout_, const float* dlast, void* dq_, void* dk_,
         void* dv_, float* dg, float* dbeta, float* dinit, cudaStream_t st) {
   const T* q = (const T*)q_;
   const T* k = (const T*)k_;
   const T* v = (const T*)v_;
+  const int l2norm = flags & TT_GDN_QK_L2NORM;
+  const bool exact = (flags & TT_GDN_EXACT_INVERSE) != 0;
   const int S = p.S, H = p.H, Dk = p.Dk, Dv = p.Dv, n = p.n, Hk = p.Hk;
   const long long vk = (long long)S * Dk, vv = (long long)S * Dv;   // head strides
   const long long llh = p.ll_total;
@@ -668,7 +702,10 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   b.Q = ar.get<float>(H * vk); b.K = ar.get<float>(H * vk); b.Vb = ar.get<float>(H * vv);
   b.Kb = ar.get<float>(H * vk); b.Kbg = ar.get<float>(H * vk); b.Qg = ar.get<float>(H * vk);
   b.Kd = ar.get<float>(H * vk); b.U = ar.get<float>(H * vv); b.W = ar.get<float>(H * vk);
-  b.T1 = ar.get<float>(H * std::max(vk, vv)); b.Vn = ar.get<float>(H * vv);
+  // T1: scratch of the T = I + A + A^2 products, and of the exact inverse's
+  // block rows (64 x L per node at offset 64 * start)
+  const long long t1_hs = std::max(std::max(vk, vv), 64LL * S);
+  b.T1 = ar.get<float>(H * t1_hs); b.Vn = ar.get<float>(H * vv);
   b.O = ar.get<float>(H * vv);
   b.KK = ar.get<float>(H * llh); b.QK = ar.get<float>(H * llh);
   b.Am = ar.get<float>(H * llh); b.Aqk = ar.get<float>(H * llh);
@@ -717,7 +754,30 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
       lv_kdv[d].push_back(desc(Dk, Dv, L, tk, 1, Dk, tv, Dv, 1, sout, Dv, 1));
     }
   }
+  // exact inverse, block row i >= 1 of each node with more than i blocks:
+  //   X = A[i0:i1, 0:i0] T[0:i0, 0:i0] ;  T[i0:i1, 0:i0] = T[i0:i1, i0:i1] X
+  // (T's rows above i0 are final by then; X lives in T1 at 64 * start)
+  const int max_nb = (p.max_len + kInvB - 1) / kInvB;
+  std::vector<int2> inv_blocks;
+  std::vector<std::vector<SegDesc>> li_x(std::max(0, max_nb - 1)), li_t(std::max(0, max_nb - 1));
+  for (int c = 0; c < n; ++c) {
+    const int L = p.len[c];
+    const long long lo = p.loff[c], xo = 64LL * p.start[c];
+    for (int i = 0; i * kInvB < L; ++i) {
+      inv_blocks.push_back(make_int2(c, i));
+      if (i == 0) continue;
+      const int i0 = i * kInvB, bs = std::min(kInvB, L - i0);
+      li_x[i - 1].push_back(desc(bs, i0, i0, lo + (long long)i0 * L, L, 1, lo, L, 1, xo, L, 1));
+      li_t[i - 1].push_back(desc(bs, i0, bs, lo + (long long)i0 * L + i0, L, 1, xo, L, 1,
+                                 lo + (long long)i0 * L, L, 1));
+    }
+  }
   DescSet ds_kk = bd.add(v_kk), ds_av = bd.add(v_av), ds_ak = bd.add(v_ak);
+  std::vector<DescSet> ds_inv_x, ds_inv_t;
+  for (int i = 0; i + 1 < max_nb; ++i) {
+    ds_inv_x.push_back(bd.add(li_x[i]));
+    ds_inv_t.push_back(bd.add(li_t[i]));
+  }
   std::vector<DescSet> ds_ws, ds_qs, ds_aqv, ds_kdv;
   for (size_t d = 0; d < p.levels.size(); ++d) {
     ds_ws.push_back(bd.add(lv_ws[d]));
@@ -799,6 +859,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   b.d_loff = ar.get<long long>(n);
   b.d_desc = ar.get<SegDesc>((long long)bd.all.size());
   b.d_tiles = ar.get<int2>((long long)bd.tiles.size());
+  b.d_inv_blocks = ar.get<int2>(std::max<long long>(1, (long long)inv_blocks.size()));
   if (ar.sizing) return TT_OK;
   if (ar.used > ar.cap) return TT_ERR_WORKSPACE;
   auto h2d = [&](void* dst, const void* src, size_t bytes) -> int {
@@ -817,6 +878,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   rc |= h2d(b.d_loff, p.loff.data(), n * 8);
   rc |= h2d(b.d_desc, bd.all.data(), bd.all.size() * sizeof(SegDesc));
   rc |= h2d(b.d_tiles, bd.tiles.data(), bd.tiles.size() * sizeof(int2));
+  if (exact) rc |= h2d(b.d_inv_blocks, inv_blocks.data(), inv_blocks.size() * sizeof(int2));
   if (rc != TT_OK) return TT_ERR_CUDA;
 
   const int max_l = p.max_len;
@@ -835,16 +897,34 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   decay_masks<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.gam,
                                                  b.KK, b.QK, b.Am, b.Aqk);
   ++launches;
-  // U = Vb + A Vb + A (A Vb);  W = Kbg + A Kbg + A (A Kbg)
-  launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.Vb, vv, b.T1, vv, 1.f, 0.f, st);
-  add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.Vb, b.T1, b.U);
-  launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.T1, vv, b.U, vv, 1.f, 1.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.Kbg, vk, b.T1, vk, 1.f, 0.f, st);
-  add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.Kbg, b.T1, b.W);
-  launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.T1, vk, b.W, vk, 1.f, 1.f, st);
+  if (exact) {
+    // Am <- T = (I - A)^-1 in place: diagonal blocks, then block rows in order
+    tri_inv_diag<<<dim3((unsigned)inv_blocks.size(), H), kInvB, 0, st>>>(
+        b.d_inv_blocks, b.d_len, b.d_loff, llh, b.Am);
+    ++launches;
+    for (size_t i = 0; i < ds_inv_x.size(); ++i) {
+      launch_gemm(b.d_desc, b.d_tiles, ds_inv_x[i], H, b.Am, llh, b.Am, llh, b.T1, t1_hs, 1.f,
+                  0.f, st);
+      launch_gemm(b.d_desc, b.d_tiles, ds_inv_t[i], H, b.Am, llh, b.T1, t1_hs, b.Am, llh, 1.f,
+                  0.f, st);
+    }
+    // U = T Vb;  W = T Kbg
+    launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.Vb, vv, b.U, vv, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.Kbg, vk, b.W, vk, 1.f, 0.f, st);
+  } else {
+    // U = Vb + A Vb + A (A Vb);  W = Kbg + A Kbg + A (A Kbg)
+    // (T1 packed with head stride vv / vk here: add_arrays reads it flat)
+    launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.Vb, vv, b.T1, vv, 1.f, 0.f, st);
+    add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.Vb, b.T1, b.U);
+    launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.T1, vv, b.U, vv, 1.f, 1.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.Kbg, vk, b.T1, vk, 1.f, 0.f, st);
+    add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.Kbg, b.T1, b.W);
+    launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.T1, vk, b.W, vk, 1.f, 1.f, st);
+    launches += 2;
+  }
   copy_array<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.U, b.Vn);
   init_state<<<blocks(sh), 256, 0, st>>>(sh, init, b.states);
-  launches += 4;
+  launches += 2;
   for (size_t d = 0; d < p.levels.size(); ++d) {
     const int cnt = (int)p.levels[d].size();
     // states are [n+1][H][Dk][Dv]: per-head stride DkDv, segment offsets cover (c+1)*H*DkDv
@@ -893,18 +973,27 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   launch_gemm(b.d_desc, b.d_tiles, ds_daqk, H, b.dO, vv, b.Vn, vv, b.dAqk, llh, 1.f, 0.f, st);
   launch_gemm(b.d_desc, b.d_tiles, ds_dt1, H, b.dVn, vv, b.Vb, vv, b.dT, llh, 1.f, 0.f, st);
   launch_gemm(b.d_desc, b.d_tiles, ds_dt2, H, b.dW, vk, b.Kbg, vk, b.dT, llh, 1.f, 1.f, st);
-  // dA = dT + dT A^T + A^T dT  (masked in grad_masks)
-  copy_array<<<blocks(H * llh), 256, 0, st>>>(H * llh, b.dT, b.dA);
-  launch_gemm(b.d_desc, b.d_tiles, ds_x1, H, b.dT, llh, b.Am, llh, b.dA, llh, 1.f, 1.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_x2, H, b.Am, llh, b.dT, llh, b.dA, llh, 1.f, 1.f, st);
-  // dVb = T^T dVn = dVn + A^T dVn + A^T (A^T dVn);  dKbg = T^T dW
-  launch_gemm(b.d_desc, b.d_tiles, ds_tvt, H, b.Am, llh, b.dVn, vv, b.T1, vv, 1.f, 0.f, st);
-  add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.dVn, b.T1, b.dVb);
-  launch_gemm(b.d_desc, b.d_tiles, ds_tvt, H, b.Am, llh, b.T1, vv, b.dVb, vv, 1.f, 1.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_tkt, H, b.Am, llh, b.dW, vk, b.T1, vk, 1.f, 0.f, st);
-  add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.dW, b.T1, b.dKbg);
-  launch_gemm(b.d_desc, b.d_tiles, ds_tkt, H, b.Am, llh, b.T1, vk, b.dKbg, vk, 1.f, 1.f, st);
-  launches += 3;
+  if (exact) {
+    // Am holds T = (I - A)^-1:  dA = T^T dT T^T (masked in grad_masks);
+    // dVb = T^T dVn;  dKbg = T^T dW
+    launch_gemm(b.d_desc, b.d_tiles, ds_x2, H, b.Am, llh, b.dT, llh, b.X, llh, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_x1, H, b.X, llh, b.Am, llh, b.dA, llh, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_tvt, H, b.Am, llh, b.dVn, vv, b.dVb, vv, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_tkt, H, b.Am, llh, b.dW, vk, b.dKbg, vk, 1.f, 0.f, st);
+  } else {
+    // dA = dT + dT A^T + A^T dT  (masked in grad_masks)
+    copy_array<<<blocks(H * llh), 256, 0, st>>>(H * llh, b.dT, b.dA);
+    launch_gemm(b.d_desc, b.d_tiles, ds_x1, H, b.dT, llh, b.Am, llh, b.dA, llh, 1.f, 1.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_x2, H, b.Am, llh, b.dT, llh, b.dA, llh, 1.f, 1.f, st);
+    // dVb = T^T dVn = dVn + A^T dVn + A^T (A^T dVn);  dKbg = T^T dW
+    launch_gemm(b.d_desc, b.d_tiles, ds_tvt, H, b.Am, llh, b.dVn, vv, b.T1, vv, 1.f, 0.f, st);
+    add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.dVn, b.T1, b.dVb);
+    launch_gemm(b.d_desc, b.d_tiles, ds_tvt, H, b.Am, llh, b.T1, vv, b.dVb, vv, 1.f, 1.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_tkt, H, b.Am, llh, b.dW, vk, b.T1, vk, 1.f, 0.f, st);
+    add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.dW, b.T1, b.dKbg);
+    launch_gemm(b.d_desc, b.d_tiles, ds_tkt, H, b.Am, llh, b.T1, vk, b.dKbg, vk, 1.f, 1.f, st);
+    launches += 3;
+  }
   // masks: dA -> G = -dA*D, dAqk -> F = dAqk*D, dDD
   TT_CUDA_OK(cudaMemsetAsync(b.dgam, 0, (size_t)H * S * 4, st));
   grad_masks<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.gam,
@@ -968,8 +1057,8 @@ extern "C" int64_t tt_gdn_tree_workspace_size(int32_t S, int32_t H, int32_t Dk, 
 }
 
 static int gdn_check(int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv, int32_t n_nodes,
-                     const int32_t* bounds, const int32_t* parents) {
-  if (S < 0 || Hk <= 0 || H <= 0 || H % Hk || Dk <= 0 || Dv <= 0 || Dk > 256 || Dv > 256 ||
+                     const int32_t* bounds, const int32_t* parents, int flags) {
+  if ((flags & ~(TT_GDN_QK_L2NORM | TT_GDN_EXACT_INVERSE)) != 0 || S < 0 || Hk <= 0 || H <= 0 || H % Hk || Dk <= 0 || Dv <= 0 || Dk > 256 || Dv > 256 ||
       n_nodes < 0 || (n_nodes > 0 && (!bounds || !parents)))
     return TT_ERR_INVALID_ARG;
   return TT_OK;
@@ -979,9 +1068,9 @@ extern "C" int tt_gdn_tree_fwd(int dtype, int32_t S, int32_t Hk, int32_t H, int3
                                const void* q, const void* k, const void* v, const float* g,
                                const float* beta, int32_t n_nodes, const int32_t* bounds,
                                const int32_t* parents, const float* initial_state,
-                               int use_qk_l2norm, void* out, float* last_state, void* workspace,
+                               int flags, void* out, float* last_state, void* workspace,
                                int64_t workspace_bytes, void* stream) {
-  int rc = gdn_check(S, Hk, H, Dk, Dv, n_nodes, bounds, parents);
+  int rc = gdn_check(S, Hk, H, Dk, Dv, n_nodes, bounds, parents, flags);
   if (rc != TT_OK) return rc;
   if (S == 0 || n_nodes == 0) return TT_OK;
   Plan p;
@@ -989,7 +1078,7 @@ extern "C" int tt_gdn_tree_fwd(int dtype, int32_t S, int32_t Hk, int32_t H, int3
   Arena ar{(char*)workspace, workspace_bytes, 0, false};
   return tt::gdn::dispatch(dtype, [&](auto tag) {
     using T = decltype(tag);
-    return tt::gdn::run<T>(p, false, ar, q, k, v, g, beta, initial_state, use_qk_l2norm, out,
+    return tt::gdn::run<T>(p, false, ar, q, k, v, g, beta, initial_state, flags, out,
                            last_state, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
                            nullptr, nullptr, (cudaStream_t)stream);
   });
@@ -999,10 +1088,10 @@ extern "C" int tt_gdn_tree_bwd(int dtype, int32_t S, int32_t Hk, int32_t H, int3
                                const void* q, const void* k, const void* v, const float* g,
                                const float* beta, int32_t n_nodes, const int32_t* bounds,
                                const int32_t* parents, const float* initial_state,
-                               int use_qk_l2norm, const void* dout, const float* dlast, void* dq,
+                               int flags, const void* dout, const float* dlast, void* dq,
                                void* dk, void* dv, float* dg, float* dbeta, float* dinit,
                                void* workspace, int64_t workspace_bytes, void* stream) {
-  int rc = gdn_check(S, Hk, H, Dk, Dv, n_nodes, bounds, parents);
+  int rc = gdn_check(S, Hk, H, Dk, Dv, n_nodes, bounds, parents, flags);
   if (rc != TT_OK) return rc;
   if (S == 0 || n_nodes == 0) return TT_OK;
   Plan p;
@@ -1010,7 +1099,7 @@ extern "C" int tt_gdn_tree_bwd(int dtype, int32_t S, int32_t Hk, int32_t H, int3
   Arena ar{(char*)workspace, workspace_bytes, 0, false};
   return tt::gdn::dispatch(dtype, [&](auto tag) {
     using T = decltype(tag);
-    return tt::gdn::run<T>(p, true, ar, q, k, v, g, beta, initial_state, use_qk_l2norm, nullptr,
+    return tt::gdn::run<T>(p, true, ar, q, k, v, g, beta, initial_state, flags, nullptr,
                            nullptr, dout, dlast, dq, dk, dv, dg, dbeta, dinit,
                            (cudaStream_t)stream);
   });

@@ -19,6 +19,10 @@ from . import _lib
 from .attention import _DTYPES, _stream_ptr
 
 
+GDN_QK_L2NORM = 1        # TT_GDN_QK_L2NORM
+GDN_EXACT_INVERSE = 2    # TT_GDN_EXACT_INVERSE
+
+
 def _tree_arrays(chunk_boundaries, chunk_parent_map) -> Tuple[torch.Tensor, torch.Tensor]:
     """bounds [n, 2] / parents [n] as int32 CPU tensors (lists, arrays or tensors)."""
     if isinstance(chunk_boundaries, torch.Tensor):
@@ -48,11 +52,12 @@ def _ws(S, H, Dk, Dv, bounds: torch.Tensor, backward: bool, device) -> Tuple[tor
 @torch.library.custom_op("tt_b200::gdn_tree_fwd", mutates_args=())
 def _gdn_fwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
                 beta: torch.Tensor, bounds: torch.Tensor, parents: torch.Tensor,
-                init: torch.Tensor, has_init: bool, l2norm: bool,
+                init: torch.Tensor, has_init: bool, flags: int,
                 want_last: bool) -> Tuple[torch.Tensor, torch.Tensor]:
     """q/k [S, Hk, Dk], v [S, H, Dv] (one dtype), g/beta fp32 [S, H],
-    bounds int32 [n, 2], parents int32 [n] (CPU) -> out [S, H, Dv], last fp32
-    [H, Dk, Dv] (zeros-shaped when not requested)."""
+    bounds int32 [n, 2], parents int32 [n] (CPU), flags (GDN_QK_L2NORM |
+    GDN_EXACT_INVERSE) -> out [S, H, Dv], last fp32 [H, Dk, Dv] (zeros-shaped
+    when not requested)."""
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
     out = torch.empty((S, H, Dv), dtype=q.dtype, device=q.device)
@@ -61,13 +66,13 @@ def _gdn_fwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tens
     _lib.call("tt_gdn_tree_fwd", _DTYPES[q.dtype], S, Hk, H, Dk, Dv, q.data_ptr(), k.data_ptr(),
               v.data_ptr(), g.data_ptr(), beta.data_ptr(), int(bounds.shape[0]),
               bounds.data_ptr(), parents.data_ptr(), init.data_ptr() if has_init else None,
-              int(l2norm), out.data_ptr(), last.data_ptr() if want_last else None,
+              int(flags), out.data_ptr(), last.data_ptr() if want_last else None,
               ws.data_ptr(), nbytes, _stream_ptr(q.device))
     return out, last
 
 
 @_gdn_fwd_op.register_fake
-def _(q, k, v, g, beta, bounds, parents, init, has_init, l2norm, want_last):
+def _(q, k, v, g, beta, bounds, parents, init, has_init, flags, want_last):
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
     return (q.new_empty((S, H, Dv)),
@@ -78,7 +83,7 @@ def _(q, k, v, g, beta, bounds, parents, init, has_init, l2norm, want_last):
 def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: torch.Tensor,
                 k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
                 bounds: torch.Tensor, parents: torch.Tensor, init: torch.Tensor, has_init: bool,
-                l2norm: bool) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                flags: int) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
                                        torch.Tensor, torch.Tensor]:
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
@@ -90,7 +95,7 @@ def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: tor
     _lib.call("tt_gdn_tree_bwd", _DTYPES[q.dtype], S, Hk, H, Dk, Dv, q.data_ptr(), k.data_ptr(),
               v.data_ptr(), g.data_ptr(), beta.data_ptr(), int(bounds.shape[0]),
               bounds.data_ptr(), parents.data_ptr(), init.data_ptr() if has_init else None,
-              int(l2norm), dout.contiguous().data_ptr(),
+              int(flags), dout.contiguous().data_ptr(),
               dlast.contiguous().data_ptr() if has_dlast else None, dq.data_ptr(),
               dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), db.data_ptr(),
               dinit.data_ptr() if has_init else None, ws.data_ptr(), nbytes,
@@ -99,7 +104,7 @@ def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: tor
 
 
 @_gdn_bwd_op.register_fake
-def _(dout, dlast, has_dlast, q, k, v, g, beta, bounds, parents, init, has_init, l2norm):
+def _(dout, dlast, has_dlast, q, k, v, g, beta, bounds, parents, init, has_init, flags):
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
     f = lambda *s: q.new_empty(s, dtype=torch.float32)
@@ -108,9 +113,9 @@ def _(dout, dlast, has_dlast, q, k, v, g, beta, bounds, parents, init, has_init,
 
 
 def _gdn_setup(ctx, inputs, output):
-    q, k, v, g, beta, bounds, parents, init, has_init, l2norm, want_last = inputs
+    q, k, v, g, beta, bounds, parents, init, has_init, flags, want_last = inputs
     ctx.save_for_backward(q, k, v, g, beta, bounds, parents, init)
-    ctx.has_init, ctx.l2norm, ctx.want_last = has_init, l2norm, want_last
+    ctx.has_init, ctx.flags, ctx.want_last = has_init, flags, want_last
 
 
 def _gdn_backward(ctx, dout, dlast):
@@ -120,7 +125,7 @@ def _gdn_backward(ctx, dout, dlast):
         dout = torch.zeros((q.shape[0], v.shape[1], v.shape[2]), dtype=q.dtype, device=q.device)
     dq, dk, dv, dg, db, dinit = _gdn_bwd_op(
         dout, dlast if has_dlast else dout.new_empty(0, dtype=torch.float32), bool(has_dlast),
-        q, k, v, g, beta, bounds, parents, init, ctx.has_init, ctx.l2norm)
+        q, k, v, g, beta, bounds, parents, init, ctx.has_init, ctx.flags)
     return (dq, dk, dv, dg, db, None, None, dinit if ctx.has_init else None, None, None, None)
 
 
@@ -130,14 +135,21 @@ _gdn_fwd_op.register_autograd(_gdn_backward, setup_context=_gdn_setup)
 def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_boundaries,
                                              chunk_parent_map, initial_state=None,
                                              output_final_state=False,
-                                             use_qk_l2norm_in_kernel=False):
+                                             use_qk_l2norm_in_kernel=False,
+                                             exact_inverse=False):
     """Drop-in for tree_dfs_ssm.py:38-156.
 
     query/key [B, S, Hk, Dk] (Hk == H, or a divisor of H: v-head h then uses
     k-head h // (H // Hk)), value [B, S, H, Dv], g/beta [B, S, H];
     chunk_boundaries / chunk_parent_map as lists or tensors.  Returns
     (core_out [B, S, H, Dv] in query's dtype, last_state [B, H, Dk, Dv] fp32 or
-    None) with gradients for every tensor input."""
+    None) with gradients for every tensor input.
+
+    ``exact_inverse=False`` reproduces the reference, whose intra-node
+    correction is the truncated T = I + A + A^2 (tree_dfs_ssm.py:119-126).
+    ``exact_inverse=True`` (an addition, not in the reference's signature) uses
+    T = (I - A)^-1, i.e. the gated delta rule's token-by-token recurrence along
+    each root-to-node path, independent of where node boundaries fall."""
     if query.dtype not in _DTYPES or key.dtype != query.dtype or value.dtype != query.dtype:
         raise TypeError("tree GDN: query, key, value must share one of float32/bfloat16/float16")
     if not query.is_cuda:
@@ -154,8 +166,10 @@ def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_b
         has_init = initial_state is not None
         init = (initial_state[b].float().contiguous() if has_init
                 else q.new_empty(0, dtype=torch.float32))
-        o, last = _gdn_fwd_op(q, k, v, gg, bt, bounds, parents, init, has_init,
-                              bool(use_qk_l2norm_in_kernel), bool(output_final_state))
+        flags = ((GDN_QK_L2NORM if use_qk_l2norm_in_kernel else 0)
+                 | (GDN_EXACT_INVERSE if exact_inverse else 0))
+        o, last = _gdn_fwd_op(q, k, v, gg, bt, bounds, parents, init, has_init, flags,
+                              bool(output_final_state))
         outs.append(o)
         lasts.append(last)
     core = torch.stack(outs, 0)
