@@ -60,6 +60,9 @@ def parse():
                          "Qwen3-4B architecture, tree_grad_hybrid on one 32k-token tree per GPU, "
                          "gradient averaging, AdamW)")
     ap.add_argument("--trees", type=int, default=8, help="attn3: number of trees in the job")
+    ap.add_argument("--gdn-exact", action="store_true",
+                    help="gdn: exact-inverse correction T = (I - A)^-1 instead of the "
+                         "reference's I + A + A^2")
     ap.add_argument("--layers", type=int, default=36, help="e2e5: decoder layers (36 = Qwen3-4B)")
     ap.add_argument("--ckpt-mlp", type=int, default=1,
                     help="e2e5: recompute decoder MLPs in backward (1) or save them (0)")
@@ -647,7 +650,8 @@ def run_gdn(args):
         k = yt[..., GDN_HK * GDN_D:2 * GDN_HK * GDN_D].reshape(1, S, GDN_HK, GDN_D)
         v = yt[..., 2 * GDN_HK * GDN_D:].reshape(1, S, GDN_H, GDN_D)
         out, _ = torch_chunk_gated_delta_rule_tree_varlen(q, k, v, gg, bt, bounds, parents,
-                                                          use_qk_l2norm_in_kernel=True)
+                                                          use_qk_l2norm_in_kernel=True,
+                                                          exact_inverse=args.gdn_exact)
         out.backward(do)
 
     clocks = ClockSampler(dev)
@@ -686,6 +690,8 @@ def run_gdn(args):
                 "config": {"workload": "config4: one DFS tree per GPU, random 2-4 branching, "
                                        "node len U[16,300], 16 qk / 32 v heads, D=128, conv K=4, "
                                        "q/k l2norm", "tokens": S, "nodes": info.n_chunks,
+                           "correction": ("exact (I - A)^-1" if args.gdn_exact
+                                          else "reference I + A + A^2"),
                            "l2": "flushed between steps"},
                 "roofline": {"bound": "hbm", "kernel": "whole step",
                              "achieved": achieved, "peak": float(pk["hbm_gbs"]), "unit": "GB/s",

@@ -253,6 +253,31 @@ int tt_gdn_tree_bwd(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int
                     float* dg, float* dbeta, float* dinit, void* workspace,
                     int64_t workspace_bytes, void* stream);
 
+/* Forward and backward of the tree GDN that also hand out the states after a
+ * chosen set of nodes, the recurrent half of the reference's SSM gateway
+ * (_ssm_varlen_capture, tree_grad_hybrid_ssm.py:48-135: captured[i] = the
+ * state after node capture_nodes[i]).  capture_nodes: HOST int32 [n_capture],
+ * distinct node indices; captured: fp32 [n_capture, H, Dk, Dv].  The
+ * backward takes their gradients, dcaptured fp32 [n_capture, H, Dk, Dv] (or
+ * NULL), and adds each to the gradient of the node's output state.  With
+ * n_capture = 0 these are tt_gdn_tree_fwd / tt_gdn_tree_bwd. */
+int tt_gdn_tree_fwd_ex(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
+                       const void* q, const void* k, const void* v, const float* g,
+                       const float* beta, int32_t n_nodes, const int32_t* bounds,
+                       const int32_t* parents, const float* initial_state, int flags,
+                       void* out, float* last_state, int32_t n_capture,
+                       const int32_t* capture_nodes, float* captured, void* workspace,
+                       int64_t workspace_bytes, void* stream);
+
+int tt_gdn_tree_bwd_ex(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
+                       const void* q, const void* k, const void* v, const float* g,
+                       const float* beta, int32_t n_nodes, const int32_t* bounds,
+                       const int32_t* parents, const float* initial_state, int flags,
+                       const void* dout, const float* dlast, int32_t n_capture,
+                       const int32_t* capture_nodes, const float* dcaptured, void* dq, void* dk,
+                       void* dv, float* dg, float* dbeta, float* dinit, void* workspace,
+                       int64_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * Tree-correct depthwise causal conv + SiLU.  Replaces _tree_correct_conv_varlen
  * (tree_dfs_ssm.py:285-348; dfs_tree_forward.py:191-246): each token's window

@@ -331,11 +331,14 @@ load_dout(int S, int H, int Dv, const T* __restrict__ dout, float* dO) {
 __global__ void gather_dstate(int H, int DkDv, int n_nodes, const int* __restrict__ nodes,
                               const int* __restrict__ child_ptr, const int* __restrict__ child_idx,
                               const float* __restrict__ dSi, const float* __restrict__ dlast,
+                              const int* __restrict__ cap_slot, const float* __restrict__ dcap,
                               float* dSo) {
   const int c = nodes[blockIdx.y], h = blockIdx.z;
   const long long hs = (long long)H * DkDv;
+  const int slot = dcap ? cap_slot[c] : -1;   // gradient of a captured state, if any
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < DkDv; i += gridDim.x * blockDim.x) {
     float a = (dlast && c == n_nodes - 1) ? dlast[(long long)h * DkDv + i] : 0.f;
+    if (slot >= 0) a += dcap[(long long)slot * hs + (long long)h * DkDv + i];
     for (int e = child_ptr[c]; e < child_ptr[c + 1]; ++e)
       a += dSi[(long long)child_idx[e] * hs + (long long)h * DkDv + i];
     dSo[(long long)c * hs + (long long)h * DkDv + i] = a;
@@ -403,16 +406,18 @@ __global__ void ddd_rowcol(int S, const int* __restrict__ nstart, const int* __r
   const int L = nlen[c];
   if (j >= L) return;
   const float* base = dDD + h * l_hs + loff[c];
-  float acc = 0.f;
-  for (int m = threadIdx.x; m < L; m += blockDim.x) acc += base[(long long)j * L + m] - base[(long long)m * L + j];
-  __shared__ float red[32];
+  // the row and column sums cancel to a small difference: accumulate in fp64
+  double acc = 0.0;
+  for (int m = threadIdx.x; m < L; m += blockDim.x)
+    acc += (double)base[(long long)j * L + m] - (double)base[(long long)m * L + j];
+  __shared__ double red[32];
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
   __syncthreads();
   if (threadIdx.x == 0) {
-    float a = 0.f;
+    double a = 0.0;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a += red[w];
-    dgam[(long long)h * S + nstart[c] + j] += a;
+    dgam[(long long)h * S + nstart[c] + j] += (float)a;
   }
 }
 
@@ -509,13 +514,13 @@ __global__ void node_dg(int S, int H, int n_nodes, const int* __restrict__ nstar
   if (c >= n_nodes) return;
   const int s = nstart[c], L = nlen[c];
   if (L == 0) return;
-  float tail = dgl[(long long)h * n_nodes + c];
+  // fp64 sums: dg is a reverse cumulative sum of terms that largely cancel
+  double tail = dgl[(long long)h * n_nodes + c];
   for (int j = 0; j < L; ++j) tail += kd_dot[(long long)h * S + s + j];
-  dgam[(long long)h * S + s + L - 1] += tail;
-  float acc = 0.f;
+  double acc = tail;
   for (int j = L - 1; j >= 0; --j) {
     acc += dgam[(long long)h * S + s + j];
-    dg[(long long)(s + j) * H + h] = acc;
+    dg[(long long)(s + j) * H + h] = (float)acc;
   }
 }
 
@@ -626,6 +631,7 @@ struct Bufs {
   SegDesc* d_desc;
   int2* d_tiles;
   int2* d_inv_blocks;   // (node, diagonal block) pairs of the exact-inverse mode
+  int* d_cap_slot;      // per node: index into the captured states, or -1
 };
 
 // Descriptor sets: built on the host in one vector, copied once, with the
@@ -684,7 +690,9 @@ template <typename T>
 int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_, const void* v_,
         const float* g, const float* beta, const float* init, int flags, void* out_,
         float* last_state, const void* dout_, const float* dlast, void* dq_, void* dk_,
-        void* dv_, float* dg, float* dbeta, float* dinit, cudaStream_t st) {
+        void* dv_, float* dg, float* dbeta, float* dinit, cudaStream_t st, int n_cap = 0,
+        const int32_t* cap_nodes = nullptr, float* captured = nullptr,
+        const float* dcaptured = nullptr) {
   const T* q = (const T*)q_;
   const T* k = (const T*)k_;
   const T* v = (const T*)v_;
@@ -860,6 +868,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   b.d_desc = ar.get<SegDesc>((long long)bd.all.size());
   b.d_tiles = ar.get<int2>((long long)bd.tiles.size());
   b.d_inv_blocks = ar.get<int2>(std::max<long long>(1, (long long)inv_blocks.size()));
+  b.d_cap_slot = ar.get<int>(n);
   if (ar.sizing) return TT_OK;
   if (ar.used > ar.cap) return TT_ERR_WORKSPACE;
   auto h2d = [&](void* dst, const void* src, size_t bytes) -> int {
@@ -879,6 +888,9 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   rc |= h2d(b.d_desc, bd.all.data(), bd.all.size() * sizeof(SegDesc));
   rc |= h2d(b.d_tiles, bd.tiles.data(), bd.tiles.size() * sizeof(int2));
   if (exact) rc |= h2d(b.d_inv_blocks, inv_blocks.data(), inv_blocks.size() * sizeof(int2));
+  std::vector<int> cap_slot(n, -1);
+  for (int i = 0; i < n_cap; ++i) cap_slot[cap_nodes[i]] = i;
+  if (backward && dcaptured) rc |= h2d(b.d_cap_slot, cap_slot.data(), n * 4);
   if (rc != TT_OK) return TT_ERR_CUDA;
 
   const int max_l = p.max_len;
@@ -947,6 +959,10 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
       TT_CUDA_OK(cudaMemcpyAsync(last_state, b.states + (long long)n * sh, sh * 4,
                                  cudaMemcpyDeviceToDevice, st));
     }
+    for (int i = 0; i < n_cap && captured; ++i)   // state after each captured node
+      TT_CUDA_OK(cudaMemcpyAsync(captured + (long long)i * sh,
+                                 b.states + (long long)(cap_nodes[i] + 1) * sh, sh * 4,
+                                 cudaMemcpyDeviceToDevice, st));
     tt_count_launches(launches);
     return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
   }
@@ -957,7 +973,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     const int cnt = (int)p.levels[d].size();
     gather_dstate<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
         H, DkDv, n, b.d_level_nodes + level_first[d], b.d_child_ptr, b.d_child_idx, b.dSi, dlast,
-        b.dSo);
+        b.d_cap_slot, dcaptured, b.dSo);
     launch_gemm(b.d_desc, b.d_tiles, ds_dvn1[d], H, b.Aqk, llh, b.dO, vv, b.dVn, vv, 1.f, 0.f, st);
     launch_gemm(b.d_desc, b.d_tiles, ds_dvn2[d], H, b.Kd, vk, b.dSo, DkDv, b.dVn, vv, 1.f, 1.f, st);
     launch_gemm(b.d_desc, b.d_tiles, ds_dsi1[d], H, b.Qg, vk, b.dO, vv, b.dSi, DkDv, 1.f, 0.f, st);
@@ -1064,14 +1080,29 @@ static int gdn_check(int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv, i
   return TT_OK;
 }
 
-extern "C" int tt_gdn_tree_fwd(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
-                               const void* q, const void* k, const void* v, const float* g,
-                               const float* beta, int32_t n_nodes, const int32_t* bounds,
-                               const int32_t* parents, const float* initial_state,
-                               int flags, void* out, float* last_state, void* workspace,
-                               int64_t workspace_bytes, void* stream) {
+static int gdn_check_capture(int32_t n_nodes, int32_t n_capture, const int32_t* capture_nodes) {
+  if (n_capture < 0 || (n_capture > 0 && !capture_nodes)) return TT_ERR_INVALID_ARG;
+  std::vector<char> seen(n_nodes, 0);
+  for (int i = 0; i < n_capture; ++i) {
+    const int c = capture_nodes[i];
+    if (c < 0 || c >= n_nodes || seen[c]) return TT_ERR_INVALID_ARG;
+    seen[c] = 1;
+  }
+  return TT_OK;
+}
+
+extern "C" int tt_gdn_tree_fwd_ex(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk,
+                                  int32_t Dv, const void* q, const void* k, const void* v,
+                                  const float* g, const float* beta, int32_t n_nodes,
+                                  const int32_t* bounds, const int32_t* parents,
+                                  const float* initial_state, int flags, void* out,
+                                  float* last_state, int32_t n_capture,
+                                  const int32_t* capture_nodes, float* captured, void* workspace,
+                                  int64_t workspace_bytes, void* stream) {
   int rc = gdn_check(S, Hk, H, Dk, Dv, n_nodes, bounds, parents, flags);
   if (rc != TT_OK) return rc;
+  if ((rc = gdn_check_capture(n_nodes, n_capture, capture_nodes)) != TT_OK) return rc;
+  if (n_capture > 0 && !captured) return TT_ERR_INVALID_ARG;
   if (S == 0 || n_nodes == 0) return TT_OK;
   Plan p;
   if ((rc = tt::gdn::make_plan(p, S, H, Hk, Dk, Dv, n_nodes, bounds, parents)) != TT_OK) return rc;
@@ -1080,7 +1111,44 @@ extern "C" int tt_gdn_tree_fwd(int dtype, int32_t S, int32_t Hk, int32_t H, int3
     using T = decltype(tag);
     return tt::gdn::run<T>(p, false, ar, q, k, v, g, beta, initial_state, flags, out,
                            last_state, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
-                           nullptr, nullptr, (cudaStream_t)stream);
+                           nullptr, nullptr, (cudaStream_t)stream, n_capture, capture_nodes,
+                           captured, nullptr);
+  });
+}
+
+extern "C" int tt_gdn_tree_fwd(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
+                               const void* q, const void* k, const void* v, const float* g,
+                               const float* beta, int32_t n_nodes, const int32_t* bounds,
+                               const int32_t* parents, const float* initial_state,
+                               int flags, void* out, float* last_state, void* workspace,
+                               int64_t workspace_bytes, void* stream) {
+  return tt_gdn_tree_fwd_ex(dtype, S, Hk, H, Dk, Dv, q, k, v, g, beta, n_nodes, bounds, parents,
+                            initial_state, flags, out, last_state, 0, nullptr, nullptr,
+                            workspace, workspace_bytes, stream);
+}
+
+extern "C" int tt_gdn_tree_bwd_ex(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk,
+                                  int32_t Dv, const void* q, const void* k, const void* v,
+                                  const float* g, const float* beta, int32_t n_nodes,
+                                  const int32_t* bounds, const int32_t* parents,
+                                  const float* initial_state, int flags, const void* dout,
+                                  const float* dlast, int32_t n_capture,
+                                  const int32_t* capture_nodes, const float* dcaptured, void* dq,
+                                  void* dk, void* dv, float* dg, float* dbeta, float* dinit,
+                                  void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = gdn_check(S, Hk, H, Dk, Dv, n_nodes, bounds, parents, flags);
+  if (rc != TT_OK) return rc;
+  if ((rc = gdn_check_capture(n_nodes, n_capture, capture_nodes)) != TT_OK) return rc;
+  if (S == 0 || n_nodes == 0) return TT_OK;
+  Plan p;
+  if ((rc = tt::gdn::make_plan(p, S, H, Hk, Dk, Dv, n_nodes, bounds, parents)) != TT_OK) return rc;
+  Arena ar{(char*)workspace, workspace_bytes, 0, false};
+  return tt::gdn::dispatch(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    return tt::gdn::run<T>(p, true, ar, q, k, v, g, beta, initial_state, flags, nullptr,
+                           nullptr, dout, dlast, dq, dk, dv, dg, dbeta, dinit,
+                           (cudaStream_t)stream, n_capture, capture_nodes, nullptr,
+                           n_capture > 0 ? dcaptured : nullptr);
   });
 }
 
@@ -1091,18 +1159,9 @@ extern "C" int tt_gdn_tree_bwd(int dtype, int32_t S, int32_t Hk, int32_t H, int3
                                int flags, const void* dout, const float* dlast, void* dq,
                                void* dk, void* dv, float* dg, float* dbeta, float* dinit,
                                void* workspace, int64_t workspace_bytes, void* stream) {
-  int rc = gdn_check(S, Hk, H, Dk, Dv, n_nodes, bounds, parents, flags);
-  if (rc != TT_OK) return rc;
-  if (S == 0 || n_nodes == 0) return TT_OK;
-  Plan p;
-  if ((rc = tt::gdn::make_plan(p, S, H, Hk, Dk, Dv, n_nodes, bounds, parents)) != TT_OK) return rc;
-  Arena ar{(char*)workspace, workspace_bytes, 0, false};
-  return tt::gdn::dispatch(dtype, [&](auto tag) {
-    using T = decltype(tag);
-    return tt::gdn::run<T>(p, true, ar, q, k, v, g, beta, initial_state, flags, nullptr,
-                           nullptr, dout, dlast, dq, dk, dv, dg, dbeta, dinit,
-                           (cudaStream_t)stream);
-  });
+  return tt_gdn_tree_bwd_ex(dtype, S, Hk, H, Dk, Dv, q, k, v, g, beta, n_nodes, bounds, parents,
+                            initial_state, flags, dout, dlast, 0, nullptr, nullptr, dq, dk, dv,
+                            dg, dbeta, dinit, workspace, workspace_bytes, stream);
 }
 
 extern "C" int64_t tt_gdn_gemm_flops(void) {

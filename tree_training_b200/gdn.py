@@ -21,6 +21,7 @@ from .attention import _DTYPES, _stream_ptr
 
 GDN_QK_L2NORM = 1        # TT_GDN_QK_L2NORM
 GDN_EXACT_INVERSE = 2    # TT_GDN_EXACT_INVERSE
+_NO_CAPTURE = torch.zeros(0, dtype=torch.int32)
 
 
 def _tree_arrays(chunk_boundaries, chunk_parent_map) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -52,38 +53,44 @@ def _ws(S, H, Dk, Dv, bounds: torch.Tensor, backward: bool, device) -> Tuple[tor
 @torch.library.custom_op("tt_b200::gdn_tree_fwd", mutates_args=())
 def _gdn_fwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
                 beta: torch.Tensor, bounds: torch.Tensor, parents: torch.Tensor,
-                init: torch.Tensor, has_init: bool, flags: int,
-                want_last: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+                init: torch.Tensor, has_init: bool, flags: int, want_last: bool,
+                capture: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """q/k [S, Hk, Dk], v [S, H, Dv] (one dtype), g/beta fp32 [S, H],
     bounds int32 [n, 2], parents int32 [n] (CPU), flags (GDN_QK_L2NORM |
-    GDN_EXACT_INVERSE) -> out [S, H, Dv], last fp32 [H, Dk, Dv] (zeros-shaped
-    when not requested)."""
+    GDN_EXACT_INVERSE), capture int32 [m] (CPU, distinct node indices) ->
+    out [S, H, Dv], last fp32 [H, Dk, Dv] (zeros-shaped when not requested),
+    captured fp32 [m, H, Dk, Dv] = the state after each captured node."""
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
+    m = int(capture.numel())
     out = torch.empty((S, H, Dv), dtype=q.dtype, device=q.device)
     last = torch.empty((H, Dk, Dv) if want_last else (0,), dtype=torch.float32, device=q.device)
+    cap = torch.empty((m, H, Dk, Dv), dtype=torch.float32, device=q.device)
     ws, nbytes = _ws(S, H, Dk, Dv, bounds, False, q.device)
-    _lib.call("tt_gdn_tree_fwd", _DTYPES[q.dtype], S, Hk, H, Dk, Dv, q.data_ptr(), k.data_ptr(),
-              v.data_ptr(), g.data_ptr(), beta.data_ptr(), int(bounds.shape[0]),
+    _lib.call("tt_gdn_tree_fwd_ex", _DTYPES[q.dtype], S, Hk, H, Dk, Dv, q.data_ptr(),
+              k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), int(bounds.shape[0]),
               bounds.data_ptr(), parents.data_ptr(), init.data_ptr() if has_init else None,
-              int(flags), out.data_ptr(), last.data_ptr() if want_last else None,
+              int(flags), out.data_ptr(), last.data_ptr() if want_last else None, m,
+              capture.data_ptr() if m else None, cap.data_ptr() if m else None,
               ws.data_ptr(), nbytes, _stream_ptr(q.device))
-    return out, last
+    return out, last, cap
 
 
 @_gdn_fwd_op.register_fake
-def _(q, k, v, g, beta, bounds, parents, init, has_init, flags, want_last):
+def _(q, k, v, g, beta, bounds, parents, init, has_init, flags, want_last, capture):
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
     return (q.new_empty((S, H, Dv)),
-            q.new_empty((H, Dk, Dv) if want_last else (0,), dtype=torch.float32))
+            q.new_empty((H, Dk, Dv) if want_last else (0,), dtype=torch.float32),
+            q.new_empty((capture.numel(), H, Dk, Dv), dtype=torch.float32))
 
 
 @torch.library.custom_op("tt_b200::gdn_tree_bwd", mutates_args=())
 def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: torch.Tensor,
                 k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
                 bounds: torch.Tensor, parents: torch.Tensor, init: torch.Tensor, has_init: bool,
-                flags: int) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                flags: int, capture: torch.Tensor, dcap: torch.Tensor,
+                has_dcap: bool) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
                                        torch.Tensor, torch.Tensor]:
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
@@ -92,11 +99,14 @@ def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: tor
     db = torch.empty((S, H), dtype=torch.float32, device=q.device)
     dinit = torch.zeros((H, Dk, Dv) if has_init else (0,), dtype=torch.float32, device=q.device)
     ws, nbytes = _ws(S, H, Dk, Dv, bounds, True, q.device)
-    _lib.call("tt_gdn_tree_bwd", _DTYPES[q.dtype], S, Hk, H, Dk, Dv, q.data_ptr(), k.data_ptr(),
-              v.data_ptr(), g.data_ptr(), beta.data_ptr(), int(bounds.shape[0]),
+    m = int(capture.numel())
+    _lib.call("tt_gdn_tree_bwd_ex", _DTYPES[q.dtype], S, Hk, H, Dk, Dv, q.data_ptr(),
+              k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), int(bounds.shape[0]),
               bounds.data_ptr(), parents.data_ptr(), init.data_ptr() if has_init else None,
               int(flags), dout.contiguous().data_ptr(),
-              dlast.contiguous().data_ptr() if has_dlast else None, dq.data_ptr(),
+              dlast.contiguous().data_ptr() if has_dlast else None, m,
+              capture.data_ptr() if m else None,
+              dcap.contiguous().data_ptr() if (m and has_dcap) else None, dq.data_ptr(),
               dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), db.data_ptr(),
               dinit.data_ptr() if has_init else None, ws.data_ptr(), nbytes,
               _stream_ptr(q.device))
@@ -104,7 +114,8 @@ def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: tor
 
 
 @_gdn_bwd_op.register_fake
-def _(dout, dlast, has_dlast, q, k, v, g, beta, bounds, parents, init, has_init, flags):
+def _(dout, dlast, has_dlast, q, k, v, g, beta, bounds, parents, init, has_init, flags, capture,
+      dcap, has_dcap):
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
     f = lambda *s: q.new_empty(s, dtype=torch.float32)
@@ -113,20 +124,24 @@ def _(dout, dlast, has_dlast, q, k, v, g, beta, bounds, parents, init, has_init,
 
 
 def _gdn_setup(ctx, inputs, output):
-    q, k, v, g, beta, bounds, parents, init, has_init, flags, want_last = inputs
-    ctx.save_for_backward(q, k, v, g, beta, bounds, parents, init)
+    q, k, v, g, beta, bounds, parents, init, has_init, flags, want_last, capture = inputs
+    ctx.save_for_backward(q, k, v, g, beta, bounds, parents, init, capture)
     ctx.has_init, ctx.flags, ctx.want_last = has_init, flags, want_last
 
 
-def _gdn_backward(ctx, dout, dlast):
-    q, k, v, g, beta, bounds, parents, init = ctx.saved_tensors
+def _gdn_backward(ctx, dout, dlast, dcap):
+    q, k, v, g, beta, bounds, parents, init, capture = ctx.saved_tensors
     has_dlast = ctx.want_last and dlast is not None and dlast.numel() > 0
+    has_dcap = dcap is not None and dcap.numel() > 0
     if dout is None:
         dout = torch.zeros((q.shape[0], v.shape[1], v.shape[2]), dtype=q.dtype, device=q.device)
+    empty = dout.new_empty(0, dtype=torch.float32)
     dq, dk, dv, dg, db, dinit = _gdn_bwd_op(
-        dout, dlast if has_dlast else dout.new_empty(0, dtype=torch.float32), bool(has_dlast),
-        q, k, v, g, beta, bounds, parents, init, ctx.has_init, ctx.flags)
-    return (dq, dk, dv, dg, db, None, None, dinit if ctx.has_init else None, None, None, None)
+        dout, dlast if has_dlast else empty, bool(has_dlast),
+        q, k, v, g, beta, bounds, parents, init, ctx.has_init, ctx.flags, capture,
+        dcap if has_dcap else empty, bool(has_dcap))
+    return (dq, dk, dv, dg, db, None, None, dinit if ctx.has_init else None, None, None, None,
+            None)
 
 
 _gdn_fwd_op.register_autograd(_gdn_backward, setup_context=_gdn_setup)
@@ -168,8 +183,8 @@ def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_b
                 else q.new_empty(0, dtype=torch.float32))
         flags = ((GDN_QK_L2NORM if use_qk_l2norm_in_kernel else 0)
                  | (GDN_EXACT_INVERSE if exact_inverse else 0))
-        o, last = _gdn_fwd_op(q, k, v, gg, bt, bounds, parents, init, has_init, flags,
-                              bool(output_final_state))
+        o, last, _ = _gdn_fwd_op(q, k, v, gg, bt, bounds, parents, init, has_init, flags,
+                                 bool(output_final_state), _NO_CAPTURE)
         outs.append(o)
         lasts.append(last)
     core = torch.stack(outs, 0)

@@ -1,4 +1,5 @@
-"""Tree-training drivers on the B200 attention path (pure-attention models).
+"""Tree-training drivers on the B200 attention path (pure-attention models, and
+hybrid models whose linear-attention layers run the tree GDN of ``ssm``).
 
 Drop-ins for the reference drivers that call the hot path:
 
@@ -18,7 +19,11 @@ Differences from the reference, all on the plumbing side of the op:
   own gateway is made visible again — with two cut levels that lets a DFS
   sibling of the parent partition leak into the child partition;
 * gateway gradients are accumulated in fp32 on the device (the reference
-  copies each one to host memory in fp32, tree_grad_hybrid.py:220-225).
+  copies each one to host memory in fp32, tree_grad_hybrid.py:220-225);
+* with linear-attention layers, each gateway also carries the recurrent state
+  and conv context after the cut node (tree_grad_hybrid.py:232-250), and a
+  partition that received them both injects them and captures its own
+  (``ssm`` module docstring).
 """
 from __future__ import annotations
 
@@ -31,6 +36,7 @@ import torch.nn.functional as F
 
 from .attention import ATTN_IMPL_NAME, register_hf_attention, tree_mask_placeholder
 from .packer import TreeNode, build_dfs_tree_info  # noqa: F401  (TreeNode re-export)
+from .ssm import SSMPartitionState, has_ssm_layers, patch_ssm_layers
 
 
 # ---------------------------------------------------------------------------
@@ -94,12 +100,12 @@ class GatewayCache:
     own K/V in every attention layer and records the result for gradient
     chaining (tree_grad_ckpt_opath.py:66-133)."""
 
-    def __init__(self, gate_kv: List[Tuple[torch.Tensor, torch.Tensor]]):
-        self._gate_kv = gate_kv
+    def __init__(self, gate_kv: Dict[int, Tuple[torch.Tensor, torch.Tensor]]):
+        self._gate_kv = gate_kv            # attention layer index -> gateway (K, V)
         self._full_kv: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
 
     def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
-        if layer_idx < len(self._gate_kv) and self._gate_kv[layer_idx][0] is not None:
+        if layer_idx in self._gate_kv:
             gk, gv = self._gate_kv[layer_idx]
             full_k = torch.cat([gk, key_states], dim=-2)
             full_v = torch.cat([gv, value_states], dim=-2)
@@ -108,13 +114,19 @@ class GatewayCache:
         self._full_kv[layer_idx] = (full_k, full_v)
         return full_k, full_v
 
-    def get_seq_length(self, layer_idx: int = 0) -> int:
-        if layer_idx < len(self._gate_kv) and self._gate_kv[layer_idx][0] is not None:
+    def get_seq_length(self, layer_idx: Optional[int] = None) -> int:
+        if layer_idx is None:               # any attention layer: all carry the same keys
+            layer_idx = min(self._gate_kv) if self._gate_kv else 0
+        if layer_idx in self._gate_kv:
             return self._gate_kv[layer_idx][0].shape[-2]
         return 0
 
-    def get_mask_sizes(self, cache_position, layer_idx: int = 0):
+    def get_mask_sizes(self, cache_position, layer_idx: Optional[int] = None):
         return self.get_seq_length(layer_idx) + cache_position.shape[0], 0
+
+    def has_previous_state(self, layer_idx: Optional[int] = None) -> bool:
+        """No decode-step recurrent state: hybrid models' mask code asks."""
+        return False
 
 
 @dataclass
@@ -129,6 +141,13 @@ class SubtreeGateway:
     gw_lo: np.ndarray           # key intervals of the gateway keys (rows of the child)
     gw_visible: np.ndarray      # bool per gateway key
     pos_offset: int
+    kv_layers: List[int] = field(default_factory=list)   # attention layer of each K/V entry
+    # linear-attention layers: layer index -> (recurrent state, conv context)
+    # leaves injected into the child, the tensors they were cut from, and the
+    # fp32 accumulators of their gradients
+    ssm_inject: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = field(default_factory=dict)
+    ssm_raw: List[torch.Tensor] = field(default_factory=list)
+    ssm_acc: List[list] = field(default_factory=list)
 
 
 def _fp32_accumulator_hook(acc: list):
@@ -172,12 +191,13 @@ def _loss_leaf_spans(info, p: SubtreePartition):
 
 
 def _subtree_forward(model, p: SubtreePartition, gw: Optional[SubtreeGateway], dev, gateway_mask,
-                     leaf_logits_only: bool = False):
-    """Forward of one partition.  Returns (logits, info, full_kv, spans): with
-    ``leaf_logits_only`` the LM head runs only on the loss leaves' tokens (HF
-    ``logits_to_keep`` with an index tensor) and spans maps each loss leaf to
-    its rows of the compact logits; otherwise logits cover every token and the
-    spans are the leaves' own token ranges."""
+                     leaf_logits_only: bool = False, cut_nodes=(), ssm_exact: bool = False):
+    """Forward of one partition.  Returns (logits, info, full_kv, spans, ssm):
+    with ``leaf_logits_only`` the LM head runs only on the loss leaves' tokens
+    (HF ``logits_to_keep`` with an index tensor) and spans maps each loss leaf
+    to its rows of the compact logits; otherwise logits cover every token and
+    the spans are the leaves' own token ranges.  ``ssm`` holds the captured
+    linear-attention states at ``cut_nodes`` (None without such layers)."""
     forest = _partition_forest(p)
     info = build_dfs_tree_info(forest, pos_offset=p.pos_offset)
     N = info.N
@@ -189,7 +209,8 @@ def _subtree_forward(model, p: SubtreePartition, gw: Optional[SubtreeGateway], d
         meta = info.attn_meta()
     ids = torch.as_tensor(info.dfs_token_ids_np, device=dev).unsqueeze(0)
     pos = torch.as_tensor(info.dfs_pos_ids_np.astype(np.int64), device=dev).unsqueeze(0)
-    cache = GatewayCache(list(zip(gw.key_gates, gw.val_gates)) if gw is not None else [])
+    cache = GatewayCache({l: kv for l, kv in zip(gw.kv_layers, zip(gw.key_gates, gw.val_gates))}
+                         if gw is not None else {})
     dtype = next(model.parameters()).dtype
     mask = tree_mask_placeholder(meta, dtype=dtype, device=dev)
     leaves = _loss_leaf_spans(info, p)
@@ -204,14 +225,25 @@ def _subtree_forward(model, p: SubtreePartition, gw: Optional[SubtreeGateway], d
             off += e - s
     else:
         spans = leaves
-    out = model(input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=cache,
-                use_cache=True, tree_meta=meta, **kw)
-    full_kv = [cache._full_kv[l] for l in sorted(cache._full_kv)]
-    return out.logits, info, full_kv, spans
+    ssm = None
+    if has_ssm_layers(model):
+        node_idx = {id(n.orig): i for i, n in enumerate(info.nodes)}
+        ssm = SSMPartitionState(info.chunk_boundaries, info.chunk_parent_map,
+                                inject=gw.ssm_inject if gw is not None else None,
+                                capture_at=[node_idx[id(cn)] for cn in cut_nodes],
+                                exact_inverse=ssm_exact)
+        with patch_ssm_layers(model, ssm):
+            out = model(input_ids=ids, attention_mask=mask, position_ids=pos,
+                        past_key_values=cache, use_cache=True, tree_meta=meta, **kw)
+    else:
+        out = model(input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=cache,
+                    use_cache=True, tree_meta=meta, **kw)
+    full_kv = {l: cache._full_kv[l] for l in sorted(cache._full_kv)}
+    return out.logits, info, full_kv, spans, ssm
 
 
 def _make_child_gateways(full_kv, info, p: SubtreePartition, gw: Optional[SubtreeGateway],
-                         cut_nodes, gateway_mask: str) -> Dict[int, SubtreeGateway]:
+                         cut_nodes, gateway_mask: str, ssm=None) -> Dict[int, SubtreeGateway]:
     """Gateway of each cut node (tree_grad_hybrid.py:174-250): the parent's
     keys up to the end of the cut node, visible where they are the cut node's
     ancestors (or, for the parent's own gateway keys, where the parent saw
@@ -223,7 +255,7 @@ def _make_child_gateways(full_kv, info, p: SubtreePartition, gw: Optional[Subtre
             info, node_idx[id(cn)], p.pos_offset, gw.gw_visible if gw is not None else None,
             gateway_mask)
         kg, vg, rk, rv, ak, av = [], [], [], [], [], []
-        for fk, fv in full_kv:
+        for fk, fv in full_kv.values():
             k_raw = fk[:, :, :total, :]
             v_raw = fv[:, :, :total, :]
             gk = k_raw.detach().requires_grad_(True)
@@ -237,8 +269,21 @@ def _make_child_gateways(full_kv, info, p: SubtreePartition, gw: Optional[Subtre
             rv.append(v_raw)
             ak.append(acc_k)
             av.append(acc_v)
-        out[id(cn)] = SubtreeGateway(kg, vg, rk, rv, ak, av, total, np.zeros(total, np.int32),
-                                     vis, pos_off)
+        g = SubtreeGateway(kg, vg, rk, rv, ak, av, total, np.zeros(total, np.int32), vis, pos_off,
+                           kv_layers=list(full_kv))
+        if ssm is not None:
+            c = node_idx[id(cn)]
+            for layer in sorted(ssm.rec):
+                pair = []
+                for raw in (ssm.rec[layer][c], ssm.conv[layer][c]):
+                    leaf = raw.detach().requires_grad_(True)
+                    acc = [None]
+                    leaf.register_hook(_fp32_accumulator_hook(acc))
+                    g.ssm_raw.append(raw)
+                    g.ssm_acc.append(acc)
+                    pair.append(leaf)
+                g.ssm_inject[layer] = (pair[0], pair[1])
+        out[id(cn)] = g
     return out
 
 
@@ -289,6 +334,10 @@ def _gateway_roots(gw: SubtreeGateway):
         if av[0] is not None:
             raws.append(rv)
             grads.append(av[0].to(rv.dtype))
+    for raw, acc in zip(gw.ssm_raw, gw.ssm_acc):
+        if acc[0] is not None and raw.requires_grad:
+            raws.append(raw)
+            grads.append(acc[0].to(raw.dtype))
     return raws, grads
 
 
@@ -311,7 +360,7 @@ def _ensure_tree_attention(model):
 
 def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
                      gateway_mask: str = "tree", backward: str = "fused",
-                     leaf_logits_only: bool = True) -> None:
+                     leaf_logits_only: bool = True, ssm_exact_inverse: bool = False) -> None:
     """Partitioned tree forward/backward (tree_grad_hybrid.py:434-539):
     partitions run top-down, each with the gateway K/V of its cut node; then
     bottom-up, each partition backpropagates its leaf losses and chains the
@@ -329,7 +378,11 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
 
     ``leaf_logits_only`` runs the LM head only on loss-leaf tokens (the loss
     reads nothing else); ``leaf_loss_fn`` receives the same [1, len, vocab]
-    slices either way."""
+    slices either way.
+
+    Models with linear-attention layers run them as tree GDN layers with SSM
+    gateways; ``ssm_exact_inverse`` selects the exact delta-rule correction
+    (T = (I - A)^-1) instead of the reference's truncated one."""
     if gateway_mask not in ("tree", "reference"):
         raise ValueError("gateway_mask must be 'tree' or 'reference'")
     if backward not in ("fused", "per_leaf"):
@@ -346,16 +399,16 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
     for p in parts:
         gw = gateways.get(id(p))
         p.pos_offset = gw.pos_offset if gw is not None else 0
-        logits, info, full_kv, spans = _subtree_forward(model, p, gw, dev, gateway_mask,
-                                                        leaf_logits_only)
-        fwd[id(p)] = (logits, info, spans)
         seen, cuts = set(), []
         for cn, _ in children_of[id(p)]:
             if id(cn) not in seen:
                 seen.add(id(cn))
                 cuts.append(cn)
+        logits, info, full_kv, spans, ssm = _subtree_forward(
+            model, p, gw, dev, gateway_mask, leaf_logits_only, cuts, ssm_exact_inverse)
+        fwd[id(p)] = (logits, info, spans)
         if cuts:
-            child = _make_child_gateways(full_kv, info, p, gw, cuts, gateway_mask)
+            child = _make_child_gateways(full_kv, info, p, gw, cuts, gateway_mask, ssm)
             for cn, cp in children_of[id(p)]:
                 gateways[id(cp)] = child[id(cn)]
     for p in reversed(parts):
@@ -391,9 +444,11 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
             _chain_gateway_grads(g, retain_graph=remaining > 0)
 
 
-def tree_grad_ckpt_sequential(model, roots, leaf_loss_fn: Callable) -> None:
+def tree_grad_ckpt_sequential(model, roots, leaf_loss_fn: Callable,
+                              ssm_exact_inverse: bool = False) -> None:
     """One packed forward over the whole forest, then per-leaf backward with
-    retain_graph on all but the last leaf (tree_grad_ckpt.py:39-107)."""
+    retain_graph on all but the last leaf (tree_grad_ckpt.py:39-107).
+    Linear-attention layers run as tree GDN layers (dfs_tree_forward.py:253-353)."""
     _ensure_tree_attention(model)
     dev = next(model.parameters()).device
     info = build_dfs_tree_info(roots)
@@ -402,8 +457,15 @@ def tree_grad_ckpt_sequential(model, roots, leaf_loss_fn: Callable) -> None:
     pos = torch.as_tensor(info.dfs_pos_ids_np.astype(np.int64), device=dev).unsqueeze(0)
     dtype = next(model.parameters()).dtype
     mask = tree_mask_placeholder(meta, dtype=dtype, device=dev)
-    logits = model(input_ids=ids, attention_mask=mask, position_ids=pos, use_cache=False,
-                   tree_meta=meta).logits
+    if has_ssm_layers(model):
+        with patch_ssm_layers(model, SSMPartitionState(info.chunk_boundaries,
+                                                        info.chunk_parent_map,
+                                                        exact_inverse=ssm_exact_inverse)):
+            logits = model(input_ids=ids, attention_mask=mask, position_ids=pos,
+                           use_cache=False, tree_meta=meta).logits
+    else:
+        logits = model(input_ids=ids, attention_mask=mask, position_ids=pos, use_cache=False,
+                       tree_meta=meta).logits
     leaves = info.leaf_chunk_ids_np.tolist()
     for i, c in enumerate(leaves):
         s, e = info.chunk_bounds_np[c]
