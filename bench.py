@@ -60,6 +60,9 @@ def parse():
                          "Qwen3-4B architecture, tree_grad_hybrid on one 32k-token tree per GPU, "
                          "gradient averaging, AdamW)")
     ap.add_argument("--trees", type=int, default=8, help="attn3: number of trees in the job")
+    ap.add_argument("--fused-ce", type=int, default=1,
+                    help="e2e5: leaf losses by the chunked fused LM-head cross-entropy (1) "
+                         "or from leaf-only logits (0)")
     ap.add_argument("--gdn-exact", action="store_true",
                     help="gdn: exact-inverse correction T = (I - A)^-1 instead of the "
                          "reference's I + A + A^2")
@@ -907,13 +910,7 @@ def run_e2e5(args):
     leaves = [info.nodes[c] for c in info.leaf_chunk_ids_np.tolist()]
     lg = torch.Generator().manual_seed(7 + rank)
     labels = [torch.randint(0, cfg.vocab_size, (len(n.token_ids),), generator=lg) for n in leaves]
-    base_fn = make_tree_loss_fn(labels, leaves, len(leaves))
-    loss_acc = torch.zeros((), dtype=torch.float32, device=dev)
-
-    def loss_fn(logits, node):
-        l = base_fn(logits, node)
-        loss_acc.add_(l.detach().float())
-        return l
+    loss_fn = make_tree_loss_fn(labels, leaves, len(leaves))
 
     avg = GradAverager(model.parameters())
     opt = torch.optim.AdamW(model.parameters(), lr=1e-5, fused=True)
@@ -925,14 +922,14 @@ def run_e2e5(args):
 
     def step():
         opt.zero_grad(set_to_none=True)
-        loss_acc.zero_()
-        tree_grad_hybrid(model, roots, loss_fn, max_tokens=8192)
+        loss = tree_grad_hybrid(model, roots, loss_fn, max_tokens=8192,
+                                fused_ce=bool(args.fused_ce))
         if watch is not None:
             watch.beat(step_no[0])
         step_no[0] += 1
         avg.average()
         opt.step()
-        return float(loss_acc.item())       # the step's d2h result
+        return float(loss.item())           # the step's d2h result
 
     clocks = ClockSampler(dev)
     clocks.start()
@@ -980,7 +977,9 @@ def run_e2e5(args):
                        "tokens_per_gpu": N, "params": n_params,
                        "parallelism": f"dp{world} (NCCL bucketed all-reduce)",
                        "peak_mem_gb_rank0": peak_mem / 1e9,
-                       "mlp_recompute": bool(args.ckpt_mlp)},
+                       "mlp_recompute": bool(args.ckpt_mlp),
+                       "leaf_loss": ("fused chunked LM head + CE (no logits)" if args.fused_ce
+                                     else "leaf-only logits + CE")},
             "e2e": {"value": tokens_all / t_step, "unit": "tokens/s",
                     "h2d_bytes_per_step": None, "d2h_bytes_per_step": 4,
                     "note": "the step starts from the host tree (packing, id/label uploads "

@@ -279,6 +279,20 @@ int tt_gdn_tree_bwd_ex(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, 
                        int64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Leaf-token cross-entropy fused with its gradient (the per-leaf
+ * F.cross_entropy of make_tree_loss_fn, tree_grad_hybrid.py:546-558, and its
+ * autograd, for a chunk of LM-head logits).  logits: [n_rows, ld] in `dtype`
+ * (first `vocab` columns used); with write_grad != 0 overwritten with
+ * weights[r] * (softmax(row) - onehot(labels[r])), else left alone; labels:
+ * device int64 [n_rows] (ignore_index, negative or >= vocab: zero loss and
+ * gradient); weights: device fp32 [n_rows]; loss: device fp32 [n_rows] =
+ * weights[r] * (logsumexp(row) - row[label]).
+ */
+int tt_ce_fwd_grad(int dtype, int32_t n_rows, int32_t vocab, void* logits, int64_t ld,
+                   const int64_t* labels, const float* weights, int64_t ignore_index,
+                   float* loss, int write_grad, void* stream);
+
+/* ------------------------------------------------------------------------
  * Tree-correct depthwise causal conv + SiLU.  Replaces _tree_correct_conv_varlen
  * (tree_dfs_ssm.py:285-348; dfs_tree_forward.py:191-246): each token's window
  * is the K-1 tokens before it on its root-to-node path (the reference's saved

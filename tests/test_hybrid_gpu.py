@@ -118,6 +118,19 @@ def test_tree_grad_hybrid_matches_flat_per_path(setup, max_tokens, backward, lea
     assert max_rel(ref, _grads(model)) < 1e-4
 
 
+@pytest.mark.parametrize("max_tokens", [1000, 10])
+def test_tree_grad_hybrid_fused_ce_matches_flat_per_path(setup, max_tokens):
+    """Leaf losses from the final hidden states through the chunked fused
+    LM-head cross-entropy (no logits)."""
+    model, roots, ref, leaves, labels = setup
+    model.zero_grad(set_to_none=True)
+    tree_grad_hybrid(model, roots, make_tree_loss_fn(labels, leaves, len(leaves)), max_tokens,
+                     fused_ce=True)
+    torch.cuda.synchronize()
+    tt.check_device_status(DEV)
+    assert max_rel(ref, _grads(model)) < 1e-4
+
+
 def test_tree_grad_ckpt_sequential_matches_flat_per_path(setup):
     model, roots, ref, leaves, labels = setup
     model.zero_grad(set_to_none=True)

@@ -70,6 +70,7 @@ SIGNATURES = {
     "tt_gdn_tree_bwd_ex": (_INT, [_INT, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P,
                                   _I32, _P, _P, _P, _INT, _P, _P, _I32, _P, _P, _P, _P, _P,
                                   _P, _P, _P, _P, _I64, _P]),
+    "tt_ce_fwd_grad": (_INT, [_INT, _I32, _I32, _P, _I64, _P, _P, _I64, _P, _INT, _P]),
     "tt_conv_predecessors": (_INT, [_I32, _P, _P, _I32, _P]),
     "tt_conv_successors": (_INT, [_I32, _I32, _P, _P, _P, _P, _I64]),
     "tt_tree_conv_fwd": (_INT, [_INT, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),

@@ -36,6 +36,7 @@ import torch.nn.functional as F
 
 from .attention import ATTN_IMPL_NAME, register_hf_attention, tree_mask_placeholder
 from .packer import TreeNode, build_dfs_tree_info  # noqa: F401  (TreeNode re-export)
+from .ce import fused_linear_cross_entropy
 from .ssm import SSMPartitionState, has_ssm_layers, patch_ssm_layers
 
 
@@ -191,13 +192,17 @@ def _loss_leaf_spans(info, p: SubtreePartition):
 
 
 def _subtree_forward(model, p: SubtreePartition, gw: Optional[SubtreeGateway], dev, gateway_mask,
-                     leaf_logits_only: bool = False, cut_nodes=(), ssm_exact: bool = False):
+                     leaf_logits_only: bool = False, cut_nodes=(), ssm_exact: bool = False,
+                     fused_loss: Optional[TreeLeafLoss] = None):
     """Forward of one partition.  Returns (logits, info, full_kv, spans, ssm):
     with ``leaf_logits_only`` the LM head runs only on the loss leaves' tokens
     (HF ``logits_to_keep`` with an index tensor) and spans maps each loss leaf
     to its rows of the compact logits; otherwise logits cover every token and
     the spans are the leaves' own token ranges.  ``ssm`` holds the captured
-    linear-attention states at ``cut_nodes`` (None without such layers)."""
+    linear-attention states at ``cut_nodes`` (None without such layers).
+    With ``fused_loss`` the first element is instead the partition's summed
+    leaf loss, computed from the final hidden states by the fused LM-head
+    cross-entropy (no logits), and spans is empty."""
     forest = _partition_forest(p)
     info = build_dfs_tree_info(forest, pos_offset=p.pos_offset)
     N = info.N
@@ -215,7 +220,9 @@ def _subtree_forward(model, p: SubtreePartition, gw: Optional[SubtreeGateway], d
     mask = tree_mask_placeholder(meta, dtype=dtype, device=dev)
     leaves = _loss_leaf_spans(info, p)
     kw = {}
-    if leaf_logits_only:
+    if fused_loss is not None:
+        spans = []
+    elif leaf_logits_only:
         idx = np.concatenate([np.arange(s, e) for _, s, e in leaves]) if leaves else \
             np.zeros(0, np.int64)
         kw["logits_to_keep"] = torch.as_tensor(idx, dtype=torch.long, device=dev)
@@ -226,6 +233,9 @@ def _subtree_forward(model, p: SubtreePartition, gw: Optional[SubtreeGateway], d
     else:
         spans = leaves
     ssm = None
+    net = _base_model(model) if fused_loss is not None else model
+    args = dict(input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=cache,
+                use_cache=True, tree_meta=meta, **kw)
     if has_ssm_layers(model):
         node_idx = {id(n.orig): i for i, n in enumerate(info.nodes)}
         ssm = SSMPartitionState(info.chunk_boundaries, info.chunk_parent_map,
@@ -233,13 +243,38 @@ def _subtree_forward(model, p: SubtreePartition, gw: Optional[SubtreeGateway], d
                                 capture_at=[node_idx[id(cn)] for cn in cut_nodes],
                                 exact_inverse=ssm_exact)
         with patch_ssm_layers(model, ssm):
-            out = model(input_ids=ids, attention_mask=mask, position_ids=pos,
-                        past_key_values=cache, use_cache=True, tree_meta=meta, **kw)
+            out = net(**args)
     else:
-        out = model(input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=cache,
-                    use_cache=True, tree_meta=meta, **kw)
+        out = net(**args)
     full_kv = {l: cache._full_kv[l] for l in sorted(cache._full_kv)}
-    return out.logits, info, full_kv, spans, ssm
+    if fused_loss is None:
+        return out.logits, info, full_kv, spans, ssm
+    return _fused_leaf_loss(model, out.last_hidden_state[0], info, leaves, fused_loss), info, \
+        full_kv, spans, ssm
+
+
+def _base_model(model):
+    """The decoder stack under an HF causal-LM head (``model.model``)."""
+    base = getattr(model, "model", None)
+    if base is None or not hasattr(model, "lm_head"):
+        raise ValueError("fused_ce needs an HF causal LM with .model and .lm_head")
+    return base
+
+
+def _fused_leaf_loss(model, hidden, info, leaves, loss: TreeLeafLoss) -> torch.Tensor:
+    """sum over the partition's loss leaves of CE(leaf logits) / n_leaves from
+    the final hidden states [N, H], without materialising the logits."""
+    if not leaves:
+        return hidden.sum() * 0.0
+    idx = np.concatenate([np.arange(s, e) for _, s, e in leaves])
+    labs, wts = [], []
+    for c, s, e in leaves:
+        lab = loss.labels(info.nodes[c]).to(hidden.device)
+        labs.append(lab)
+        wts.append(loss.token_weights(lab))
+    h = hidden.index_select(0, torch.as_tensor(idx, dtype=torch.long, device=hidden.device))
+    return fused_linear_cross_entropy(h, model.lm_head.weight, torch.cat(labs), torch.cat(wts),
+                                      ignore_index=loss.ignore_index)
 
 
 def _make_child_gateways(full_kv, info, p: SubtreePartition, gw: Optional[SubtreeGateway],
@@ -360,7 +395,8 @@ def _ensure_tree_attention(model):
 
 def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
                      gateway_mask: str = "tree", backward: str = "fused",
-                     leaf_logits_only: bool = True, ssm_exact_inverse: bool = False) -> None:
+                     leaf_logits_only: bool = True, ssm_exact_inverse: bool = False,
+                     fused_ce: bool = False) -> torch.Tensor:
     """Partitioned tree forward/backward (tree_grad_hybrid.py:434-539):
     partitions run top-down, each with the gateway K/V of its cut node; then
     bottom-up, each partition backpropagates its leaf losses and chains the
@@ -369,6 +405,9 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
 
     ``backward="fused"`` takes each partition's leaf losses and gateway
     gradients through ONE autograd traversal of the partition graph;
+    with ``fused_ce`` (a ``make_tree_loss_fn`` loss, ``backward="fused"``) the
+    leaf losses come from the final hidden states through the chunked LM-head
+    cross-entropy of ``ce`` and no logits are formed;
     ``"per_leaf"`` calls backward once per leaf loss and once per gateway with
     retain_graph, as the reference does (tree_grad_hybrid.py:521-539).  Both
     accumulate the same sum of gradients; every per-leaf call traverses the
@@ -382,11 +421,15 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
 
     Models with linear-attention layers run them as tree GDN layers with SSM
     gateways; ``ssm_exact_inverse`` selects the exact delta-rule correction
-    (T = (I - A)^-1) instead of the reference's truncated one."""
+    (T = (I - A)^-1) instead of the reference's truncated one.
+
+    Returns the summed leaf loss (a detached fp32 scalar on the device)."""
     if gateway_mask not in ("tree", "reference"):
         raise ValueError("gateway_mask must be 'tree' or 'reference'")
     if backward not in ("fused", "per_leaf"):
         raise ValueError("backward must be 'fused' or 'per_leaf'")
+    if fused_ce and (backward != "fused" or not isinstance(leaf_loss_fn, TreeLeafLoss)):
+        raise ValueError("fused_ce needs backward='fused' and a make_tree_loss_fn loss")
     _ensure_tree_attention(model)
     dev = next(model.parameters()).device
     parts = partition_tree(roots, max_tokens)
@@ -396,6 +439,7 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
             children_of[id(p.parent)].append((p.parent_cut_node, p))
     gateways: Dict[int, SubtreeGateway] = {}
     fwd: Dict[int, tuple] = {}
+    total = torch.zeros((), dtype=torch.float32, device=dev)
     for p in parts:
         gw = gateways.get(id(p))
         p.pos_offset = gw.pos_offset if gw is not None else 0
@@ -405,7 +449,8 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
                 seen.add(id(cn))
                 cuts.append(cn)
         logits, info, full_kv, spans, ssm = _subtree_forward(
-            model, p, gw, dev, gateway_mask, leaf_logits_only, cuts, ssm_exact_inverse)
+            model, p, gw, dev, gateway_mask, leaf_logits_only, cuts, ssm_exact_inverse,
+            leaf_loss_fn if fused_ce else None)
         fwd[id(p)] = (logits, info, spans)
         if cuts:
             child = _make_child_gateways(full_kv, info, p, gw, cuts, gateway_mask, ssm)
@@ -422,9 +467,14 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
                 uniq.append(g)
         if backward == "fused":
             outs, grads = [], []
+            if fused_ce:
+                outs.append(logits)          # the partition's summed leaf loss
+                grads.append(None)
             for s, e, orig in leaf_chunks:
                 outs.append(leaf_loss_fn(logits[:, s:e, :], orig))
                 grads.append(None)
+            for o in outs:
+                total += o.detach().float()
             for g in uniq:
                 r, gr = _gateway_roots(g)
                 outs.extend(r)
@@ -438,10 +488,13 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
         remaining = len(leaf_chunks) + len(uniq)
         for s, e, orig in leaf_chunks:
             remaining -= 1
-            leaf_loss_fn(logits[:, s:e, :], orig).backward(retain_graph=remaining > 0)
+            l = leaf_loss_fn(logits[:, s:e, :], orig)
+            total += l.detach().float()
+            l.backward(retain_graph=remaining > 0)
         for g in uniq:
             remaining -= 1
             _chain_gateway_grads(g, retain_graph=remaining > 0)
+    return total
 
 
 def tree_grad_ckpt_sequential(model, roots, leaf_loss_fn: Callable,
@@ -501,11 +554,32 @@ def checkpoint_mlps(model) -> int:
     return n
 
 
+class TreeLeafLoss:
+    """Per-leaf CE / n_leaves (tree_grad_hybrid.py:546-558): called as
+    ``loss_fn(logits [1, len, vocab], node)``.  The drivers' ``fused_ce``
+    option recognises it and computes the same sum from the final hidden
+    states with ``ce.fused_linear_cross_entropy`` instead of the logits."""
+
+    def __init__(self, leaf_labels, leaf_nodes, n_leaves: int, ignore_index: int = -100):
+        self.label_map = {id(n): lab for n, lab in zip(leaf_nodes, leaf_labels)}
+        self.n_leaves = n_leaves
+        self.ignore_index = ignore_index
+
+    def labels(self, node) -> torch.Tensor:
+        return self.label_map[id(getattr(node, "orig", node))]
+
+    def __call__(self, logits, node):
+        labels = self.labels(node).to(logits.device)
+        return F.cross_entropy(logits[0], labels, ignore_index=self.ignore_index) / self.n_leaves
+
+    def token_weights(self, labels: torch.Tensor) -> torch.Tensor:
+        """w_t of the fused form: 1 / (valid tokens of the leaf * n_leaves), 0
+        for ignored tokens (F.cross_entropy's mean over non-ignored targets)."""
+        valid = labels != self.ignore_index
+        n = int(valid.sum())
+        return valid.float() / (max(n, 1) * self.n_leaves)
+
+
 def make_tree_loss_fn(leaf_labels, leaf_nodes, n_leaves: int, ignore_index: int = -100):
     """Per-leaf CE / n_leaves (tree_grad_hybrid.py:546-558)."""
-    label_map = {id(n): lab for n, lab in zip(leaf_nodes, leaf_labels)}
-
-    def _fn(logits, node):
-        labels = label_map[id(getattr(node, "orig", node))].to(logits.device)
-        return F.cross_entropy(logits[0], labels, ignore_index=ignore_index) / n_leaves
-    return _fn
+    return TreeLeafLoss(leaf_labels, leaf_nodes, n_leaves, ignore_index)
