@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--fused-ce", type=int, default=1,
                     help="e2e5: leaf losses by the chunked fused LM-head cross-entropy (1) "
                          "or from leaf-only logits (0)")
+    ap.add_argument("--gdn-keep", type=int, default=1,
+                    help="gdn: keep the forward's intermediates for the backward (1) or "
+                         "recompute them (0)")
     ap.add_argument("--gdn-exact", action="store_true",
                     help="gdn: exact-inverse correction T = (I - A)^-1 instead of the "
                          "reference's I + A + A^2")
@@ -654,7 +657,8 @@ def run_gdn(args):
         v = yt[..., 2 * GDN_HK * GDN_D:].reshape(1, S, GDN_H, GDN_D)
         out, _ = torch_chunk_gated_delta_rule_tree_varlen(q, k, v, gg, bt, bounds, parents,
                                                           use_qk_l2norm_in_kernel=True,
-                                                          exact_inverse=args.gdn_exact)
+                                                          exact_inverse=args.gdn_exact,
+                                                          keep_forward=bool(args.gdn_keep))
         out.backward(do)
 
     clocks = ClockSampler(dev)
@@ -695,6 +699,9 @@ def run_gdn(args):
                                        "q/k l2norm", "tokens": S, "nodes": info.n_chunks,
                            "correction": ("exact (I - A)^-1" if args.gdn_exact
                                           else "reference I + A + A^2"),
+                           "backward": ("reads the kept forward intermediates" if args.gdn_keep
+                                        else "recomputes the forward"),
+                           "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9,
                            "l2": "flushed between steps"},
                 "roofline": {"bound": "hbm", "kernel": "whole step",
                              "achieved": achieved, "peak": float(pk["hbm_gbs"]), "unit": "GB/s",

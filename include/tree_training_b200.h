@@ -223,12 +223,18 @@ int64_t tt_tree_attn_bwd_noalloc_max_row_terms(void);
  * (the reference's use_qk_l2norm_in_kernel, :67-69); TT_GDN_EXACT_INVERSE =
  * replace the reference's truncated correction by the delta rule's exact
  * T = (I - A)^-1 per node (the token-by-token recurrence's result, which the
- * reference approximates); any other bit is TT_ERR_INVALID_ARG.
+ * reference approximates); TT_GDN_SAVED_FORWARD (backward only) = the
+ * workspace still holds what tt_gdn_tree_fwd computed: the backward then skips
+ * recomputing the forward.  For that, call tt_gdn_tree_fwd with a workspace
+ * sized by tt_gdn_tree_workspace_size(..., backward=1), leave it untouched, and
+ * call tt_gdn_tree_bwd with the same workspace, inputs and other flags.  Any
+ * other bit is TT_ERR_INVALID_ARG.
  * Dk, Dv <= 256.  Workspace: tt_gdn_tree_workspace_size(..., backward=0/1),
  * the same for either flag.
  */
 #define TT_GDN_QK_L2NORM 1
 #define TT_GDN_EXACT_INVERSE 2
+#define TT_GDN_SAVED_FORWARD 4
 
 int64_t tt_gdn_tree_workspace_size(int32_t S, int32_t H, int32_t Dk, int32_t Dv,
                                    int32_t n_nodes, const int32_t* bounds, int backward);

@@ -150,6 +150,32 @@ def test_gdn_exact_inverse_is_segmentation_invariant():
     assert rel(ra["out"], rec) > 1e-4
 
 
+@pytest.mark.parametrize("exact", [False, True])
+def test_gdn_keep_forward_gives_identical_gradients(exact):
+    """keep_forward=True: the backward reads the forward's workspace instead of
+    recomputing it; the kernels are deterministic, so every output and
+    gradient is bitwise equal to the recomputing path, also for a second
+    backward through the same graph."""
+    info, q, k, v, gg, bt, s0, do, dl = _case(8, 900, 2, 4, 64, 16, 300, True)
+    res = []
+    for keep in (False, True):
+        T = lambda x: torch.tensor(x, dtype=torch.float32, device=DEV, requires_grad=True)
+        ts = [T(x) for x in (q, k, v, gg, bt, s0)]
+        out, last = torch_chunk_gated_delta_rule_tree_varlen(
+            *ts[:5], info.chunk_boundaries, info.chunk_parent_map, initial_state=ts[5],
+            output_final_state=True, use_qk_l2norm_in_kernel=True, exact_inverse=exact,
+            keep_forward=keep)
+        loss = (out * torch.tensor(do, dtype=torch.float32, device=DEV)).sum() + \
+            (last * torch.tensor(dl, dtype=torch.float32, device=DEV)).sum()
+        g1 = torch.autograd.grad(loss, ts, retain_graph=True)
+        g2 = torch.autograd.grad(loss, ts)
+        res.append((out.detach(), g1, g2))
+    (o0, a0, b0), (o1, a1, b1) = res
+    assert torch.equal(o0, o1)
+    for x, y, z in zip(a0, a1, b1):
+        assert torch.equal(x, y) and torch.equal(y, z)
+
+
 def test_gdn_config4_size_head_slice_vs_oracle():
     """Config-4 shape (16k tokens, 16/32 heads, D=128); the oracle checks k-head 0 and its v-heads 0, 1."""
     S, Hk, H, D = 16384, 16, 32, 128

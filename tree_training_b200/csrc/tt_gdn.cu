@@ -698,6 +698,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   const T* v = (const T*)v_;
   const int l2norm = flags & TT_GDN_QK_L2NORM;
   const bool exact = (flags & TT_GDN_EXACT_INVERSE) != 0;
+  const bool reuse = backward && (flags & TT_GDN_SAVED_FORWARD) != 0;
   const int S = p.S, H = p.H, Dk = p.Dk, Dv = p.Dv, n = p.n, Hk = p.Hk;
   const long long vk = (long long)S * Dk, vv = (long long)S * Dv;   // head strides
   const long long llh = p.ll_total;
@@ -898,59 +899,62 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   auto blocks = [](long long nel) { return (unsigned)((nel + 255) / 256); };
   int launches = 0;
   // ---------------------------------------------------------------- forward
-  node_cumsum<<<dim3((n + 127) / 128, H), 128, 0, st>>>(S, H, n, b.d_start, b.d_len, g, b.gam,
-                                                        b.gl_tok, b.gl);
-  prep_tokens<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(
-      S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok, l2norm, q_scale, b.Q, b.K, b.Vb, b.Kb,
-      b.Kbg, b.Qg, b.Kd);
-  launches += 2;
-  launch_gemm(b.d_desc, b.d_tiles, ds_kk, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_kk, H, b.Q, vk, b.K, vk, b.QK, llh, 1.f, 0.f, st);
-  decay_masks<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.gam,
-                                                 b.KK, b.QK, b.Am, b.Aqk);
-  ++launches;
-  if (exact) {
-    // Am <- T = (I - A)^-1 in place: diagonal blocks, then block rows in order
-    tri_inv_diag<<<dim3((unsigned)inv_blocks.size(), H), kInvB, 0, st>>>(
-        b.d_inv_blocks, b.d_len, b.d_loff, llh, b.Am);
-    ++launches;
-    for (size_t i = 0; i < ds_inv_x.size(); ++i) {
-      launch_gemm(b.d_desc, b.d_tiles, ds_inv_x[i], H, b.Am, llh, b.Am, llh, b.T1, t1_hs, 1.f,
-                  0.f, st);
-      launch_gemm(b.d_desc, b.d_tiles, ds_inv_t[i], H, b.Am, llh, b.T1, t1_hs, b.Am, llh, 1.f,
-                  0.f, st);
-    }
-    // U = T Vb;  W = T Kbg
-    launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.Vb, vv, b.U, vv, 1.f, 0.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.Kbg, vk, b.W, vk, 1.f, 0.f, st);
-  } else {
-    // U = Vb + A Vb + A (A Vb);  W = Kbg + A Kbg + A (A Kbg)
-    // (T1 packed with head stride vv / vk here: add_arrays reads it flat)
-    launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.Vb, vv, b.T1, vv, 1.f, 0.f, st);
-    add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.Vb, b.T1, b.U);
-    launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.T1, vv, b.U, vv, 1.f, 1.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.Kbg, vk, b.T1, vk, 1.f, 0.f, st);
-    add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.Kbg, b.T1, b.W);
-    launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.T1, vk, b.W, vk, 1.f, 1.f, st);
+  // (skipped when the workspace still holds this pass from tt_gdn_tree_fwd)
+  if (!reuse) {
+    node_cumsum<<<dim3((n + 127) / 128, H), 128, 0, st>>>(S, H, n, b.d_start, b.d_len, g, b.gam,
+                                                          b.gl_tok, b.gl);
+    prep_tokens<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(
+        S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok, l2norm, q_scale, b.Q, b.K, b.Vb, b.Kb,
+        b.Kbg, b.Qg, b.Kd);
     launches += 2;
-  }
-  copy_array<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.U, b.Vn);
-  init_state<<<blocks(sh), 256, 0, st>>>(sh, init, b.states);
-  launches += 2;
-  for (size_t d = 0; d < p.levels.size(); ++d) {
-    const int cnt = (int)p.levels[d].size();
-    // states are [n+1][H][Dk][Dv]: per-head stride DkDv, segment offsets cover (c+1)*H*DkDv
-    launch_gemm(b.d_desc, b.d_tiles, ds_ws[d], H, b.W, vk, b.states, DkDv, b.Vn, vv, -1.f, 1.f, st);
-    if (!backward) {   // the output; the backward (which recomputes this pass) never reads it
-      launch_gemm(b.d_desc, b.d_tiles, ds_qs[d], H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f,
-                  st);
-      launch_gemm(b.d_desc, b.d_tiles, ds_aqv[d], H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f,
-                  st);
-    }
-    launch_gemm(b.d_desc, b.d_tiles, ds_kdv[d], H, b.Kd, vk, b.Vn, vv, b.states, DkDv, 1.f, 0.f, st);
-    state_decay_add<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
-        H, DkDv, n, b.d_level_nodes + level_first[d], b.d_parent, b.gl, b.states);
+    launch_gemm(b.d_desc, b.d_tiles, ds_kk, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
+    launch_gemm(b.d_desc, b.d_tiles, ds_kk, H, b.Q, vk, b.K, vk, b.QK, llh, 1.f, 0.f, st);
+    decay_masks<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.gam,
+                                                   b.KK, b.QK, b.Am, b.Aqk);
     ++launches;
+    if (exact) {
+      // Am <- T = (I - A)^-1 in place: diagonal blocks, then block rows in order
+      tri_inv_diag<<<dim3((unsigned)inv_blocks.size(), H), kInvB, 0, st>>>(
+          b.d_inv_blocks, b.d_len, b.d_loff, llh, b.Am);
+      ++launches;
+      for (size_t i = 0; i < ds_inv_x.size(); ++i) {
+        launch_gemm(b.d_desc, b.d_tiles, ds_inv_x[i], H, b.Am, llh, b.Am, llh, b.T1, t1_hs, 1.f,
+                    0.f, st);
+        launch_gemm(b.d_desc, b.d_tiles, ds_inv_t[i], H, b.Am, llh, b.T1, t1_hs, b.Am, llh, 1.f,
+                    0.f, st);
+      }
+      // U = T Vb;  W = T Kbg
+      launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.Vb, vv, b.U, vv, 1.f, 0.f, st);
+      launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.Kbg, vk, b.W, vk, 1.f, 0.f, st);
+    } else {
+      // U = Vb + A Vb + A (A Vb);  W = Kbg + A Kbg + A (A Kbg)
+      // (T1 packed with head stride vv / vk here: add_arrays reads it flat)
+      launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.Vb, vv, b.T1, vv, 1.f, 0.f, st);
+      add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.Vb, b.T1, b.U);
+      launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.T1, vv, b.U, vv, 1.f, 1.f, st);
+      launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.Kbg, vk, b.T1, vk, 1.f, 0.f, st);
+      add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.Kbg, b.T1, b.W);
+      launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.T1, vk, b.W, vk, 1.f, 1.f, st);
+      launches += 2;
+    }
+    copy_array<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.U, b.Vn);
+    init_state<<<blocks(sh), 256, 0, st>>>(sh, init, b.states);
+    launches += 2;
+    for (size_t d = 0; d < p.levels.size(); ++d) {
+      const int cnt = (int)p.levels[d].size();
+      // states are [n+1][H][Dk][Dv]: per-head stride DkDv, segment offsets cover (c+1)*H*DkDv
+      launch_gemm(b.d_desc, b.d_tiles, ds_ws[d], H, b.W, vk, b.states, DkDv, b.Vn, vv, -1.f, 1.f, st);
+      if (!backward) {   // the output; the backward (which recomputes this pass) never reads it
+        launch_gemm(b.d_desc, b.d_tiles, ds_qs[d], H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f,
+                    st);
+        launch_gemm(b.d_desc, b.d_tiles, ds_aqv[d], H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f,
+                    st);
+      }
+      launch_gemm(b.d_desc, b.d_tiles, ds_kdv[d], H, b.Kd, vk, b.Vn, vv, b.states, DkDv, 1.f, 0.f, st);
+      state_decay_add<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
+          H, DkDv, n, b.d_level_nodes + level_first[d], b.d_parent, b.gl, b.states);
+      ++launches;
+    }
   }
   if (!backward) {
     store_out<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(S, H, Dv, b.O, (T*)out_);
@@ -1074,7 +1078,7 @@ extern "C" int64_t tt_gdn_tree_workspace_size(int32_t S, int32_t H, int32_t Dk, 
 
 static int gdn_check(int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv, int32_t n_nodes,
                      const int32_t* bounds, const int32_t* parents, int flags) {
-  if ((flags & ~(TT_GDN_QK_L2NORM | TT_GDN_EXACT_INVERSE)) != 0 || S < 0 || Hk <= 0 || H <= 0 || H % Hk || Dk <= 0 || Dv <= 0 || Dk > 256 || Dv > 256 ||
+  if ((flags & ~(TT_GDN_QK_L2NORM | TT_GDN_EXACT_INVERSE | TT_GDN_SAVED_FORWARD)) != 0 || S < 0 || Hk <= 0 || H <= 0 || H % Hk || Dk <= 0 || Dv <= 0 || Dk > 256 || Dv > 256 ||
       n_nodes < 0 || (n_nodes > 0 && (!bounds || !parents)))
     return TT_ERR_INVALID_ARG;
   return TT_OK;

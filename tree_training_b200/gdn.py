@@ -21,6 +21,7 @@ from .attention import _DTYPES, _stream_ptr
 
 GDN_QK_L2NORM = 1        # TT_GDN_QK_L2NORM
 GDN_EXACT_INVERSE = 2    # TT_GDN_EXACT_INVERSE
+GDN_SAVED_FORWARD = 4    # TT_GDN_SAVED_FORWARD
 _NO_CAPTURE = torch.zeros(0, dtype=torch.int32)
 
 
@@ -54,43 +55,47 @@ def _ws(S, H, Dk, Dv, bounds: torch.Tensor, backward: bool, device) -> Tuple[tor
 def _gdn_fwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
                 beta: torch.Tensor, bounds: torch.Tensor, parents: torch.Tensor,
                 init: torch.Tensor, has_init: bool, flags: int, want_last: bool,
-                capture: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+                capture: torch.Tensor, keep: bool
+                ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     """q/k [S, Hk, Dk], v [S, H, Dv] (one dtype), g/beta fp32 [S, H],
     bounds int32 [n, 2], parents int32 [n] (CPU), flags (GDN_QK_L2NORM |
     GDN_EXACT_INVERSE), capture int32 [m] (CPU, distinct node indices) ->
     out [S, H, Dv], last fp32 [H, Dk, Dv] (zeros-shaped when not requested),
-    captured fp32 [m, H, Dk, Dv] = the state after each captured node."""
+    captured fp32 [m, H, Dk, Dv] = the state after each captured node, and
+    with ``keep`` the workspace holding the forward pass (sized for the
+    backward, which then skips recomputing it), else an empty tensor."""
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
     m = int(capture.numel())
     out = torch.empty((S, H, Dv), dtype=q.dtype, device=q.device)
     last = torch.empty((H, Dk, Dv) if want_last else (0,), dtype=torch.float32, device=q.device)
     cap = torch.empty((m, H, Dk, Dv), dtype=torch.float32, device=q.device)
-    ws, nbytes = _ws(S, H, Dk, Dv, bounds, False, q.device)
+    ws, nbytes = _ws(S, H, Dk, Dv, bounds, keep, q.device)
     _lib.call("tt_gdn_tree_fwd_ex", _DTYPES[q.dtype], S, Hk, H, Dk, Dv, q.data_ptr(),
               k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), int(bounds.shape[0]),
               bounds.data_ptr(), parents.data_ptr(), init.data_ptr() if has_init else None,
               int(flags), out.data_ptr(), last.data_ptr() if want_last else None, m,
               capture.data_ptr() if m else None, cap.data_ptr() if m else None,
               ws.data_ptr(), nbytes, _stream_ptr(q.device))
-    return out, last, cap
+    return out, last, cap, (ws if keep else ws.new_empty(0))
 
 
 @_gdn_fwd_op.register_fake
-def _(q, k, v, g, beta, bounds, parents, init, has_init, flags, want_last, capture):
+def _(q, k, v, g, beta, bounds, parents, init, has_init, flags, want_last, capture, keep):
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
     return (q.new_empty((S, H, Dv)),
             q.new_empty((H, Dk, Dv) if want_last else (0,), dtype=torch.float32),
-            q.new_empty((capture.numel(), H, Dk, Dv), dtype=torch.float32))
+            q.new_empty((capture.numel(), H, Dk, Dv), dtype=torch.float32),
+            q.new_empty(0, dtype=torch.uint8))
 
 
-@torch.library.custom_op("tt_b200::gdn_tree_bwd", mutates_args=())
+@torch.library.custom_op("tt_b200::gdn_tree_bwd", mutates_args=("kept",))
 def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: torch.Tensor,
                 k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
                 bounds: torch.Tensor, parents: torch.Tensor, init: torch.Tensor, has_init: bool,
                 flags: int, capture: torch.Tensor, dcap: torch.Tensor,
-                has_dcap: bool) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                has_dcap: bool, kept: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
                                        torch.Tensor, torch.Tensor]:
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
@@ -98,7 +103,11 @@ def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: tor
     dg = torch.empty((S, H), dtype=torch.float32, device=q.device)
     db = torch.empty((S, H), dtype=torch.float32, device=q.device)
     dinit = torch.zeros((H, Dk, Dv) if has_init else (0,), dtype=torch.float32, device=q.device)
-    ws, nbytes = _ws(S, H, Dk, Dv, bounds, True, q.device)
+    if kept.numel():                     # the forward's workspace, still holding its pass
+        ws, nbytes = kept, int(kept.numel())
+        flags = int(flags) | GDN_SAVED_FORWARD
+    else:
+        ws, nbytes = _ws(S, H, Dk, Dv, bounds, True, q.device)
     m = int(capture.numel())
     _lib.call("tt_gdn_tree_bwd_ex", _DTYPES[q.dtype], S, Hk, H, Dk, Dv, q.data_ptr(),
               k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), int(bounds.shape[0]),
@@ -115,7 +124,7 @@ def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: tor
 
 @_gdn_bwd_op.register_fake
 def _(dout, dlast, has_dlast, q, k, v, g, beta, bounds, parents, init, has_init, flags, capture,
-      dcap, has_dcap):
+      dcap, has_dcap, kept):
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
     f = lambda *s: q.new_empty(s, dtype=torch.float32)
@@ -124,13 +133,17 @@ def _(dout, dlast, has_dlast, q, k, v, g, beta, bounds, parents, init, has_init,
 
 
 def _gdn_setup(ctx, inputs, output):
-    q, k, v, g, beta, bounds, parents, init, has_init, flags, want_last, capture = inputs
+    q, k, v, g, beta, bounds, parents, init, has_init, flags, want_last, capture, keep = inputs
     ctx.save_for_backward(q, k, v, g, beta, bounds, parents, init, capture)
+    # the kept workspace: its forward part is read, its backward part written
+    # by every backward call, so it is held outside autograd's version checks
+    ctx.kept = output[3]
     ctx.has_init, ctx.flags, ctx.want_last = has_init, flags, want_last
 
 
-def _gdn_backward(ctx, dout, dlast, dcap):
+def _gdn_backward(ctx, dout, dlast, dcap, _dkept):
     q, k, v, g, beta, bounds, parents, init, capture = ctx.saved_tensors
+    kept = ctx.kept
     has_dlast = ctx.want_last and dlast is not None and dlast.numel() > 0
     has_dcap = dcap is not None and dcap.numel() > 0
     if dout is None:
@@ -139,9 +152,9 @@ def _gdn_backward(ctx, dout, dlast, dcap):
     dq, dk, dv, dg, db, dinit = _gdn_bwd_op(
         dout, dlast if has_dlast else empty, bool(has_dlast),
         q, k, v, g, beta, bounds, parents, init, ctx.has_init, ctx.flags, capture,
-        dcap if has_dcap else empty, bool(has_dcap))
+        dcap if has_dcap else empty, bool(has_dcap), kept)
     return (dq, dk, dv, dg, db, None, None, dinit if ctx.has_init else None, None, None, None,
-            None)
+            None, None)
 
 
 _gdn_fwd_op.register_autograd(_gdn_backward, setup_context=_gdn_setup)
@@ -151,7 +164,7 @@ def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_b
                                              chunk_parent_map, initial_state=None,
                                              output_final_state=False,
                                              use_qk_l2norm_in_kernel=False,
-                                             exact_inverse=False):
+                                             exact_inverse=False, keep_forward=False):
     """Drop-in for tree_dfs_ssm.py:38-156.
 
     query/key [B, S, Hk, Dk] (Hk == H, or a divisor of H: v-head h then uses
@@ -164,7 +177,10 @@ def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_b
     correction is the truncated T = I + A + A^2 (tree_dfs_ssm.py:119-126).
     ``exact_inverse=True`` (an addition, not in the reference's signature) uses
     T = (I - A)^-1, i.e. the gated delta rule's token-by-token recurrence along
-    each root-to-node path, independent of where node boundaries fall."""
+    each root-to-node path, independent of where node boundaries fall.
+    ``keep_forward=True`` keeps the forward's fp32 intermediates on the device
+    until the backward (a workspace of ``tt_gdn_tree_workspace_size(...,
+    backward=1)`` bytes), which then skips recomputing the forward."""
     if query.dtype not in _DTYPES or key.dtype != query.dtype or value.dtype != query.dtype:
         raise TypeError("tree GDN: query, key, value must share one of float32/bfloat16/float16")
     if not query.is_cuda:
@@ -183,8 +199,8 @@ def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_b
                 else q.new_empty(0, dtype=torch.float32))
         flags = ((GDN_QK_L2NORM if use_qk_l2norm_in_kernel else 0)
                  | (GDN_EXACT_INVERSE if exact_inverse else 0))
-        o, last, _ = _gdn_fwd_op(q, k, v, gg, bt, bounds, parents, init, has_init, flags,
-                                 bool(output_final_state), _NO_CAPTURE)
+        o, last, _, _ = _gdn_fwd_op(q, k, v, gg, bt, bounds, parents, init, has_init, flags,
+                                    bool(output_final_state), _NO_CAPTURE, bool(keep_forward))
         outs.append(o)
         lasts.append(last)
     core = torch.stack(outs, 0)

@@ -72,9 +72,10 @@ def ssm_varlen_capture(query, key, value, g, beta, chunk_boundaries, chunk_paren
         has_init = initial_state is not None
         init = (initial_state[b].float().contiguous() if has_init
                 else query.new_empty(0, dtype=torch.float32))
-        o, _, c = _gdn_fwd_op(query[b].contiguous(), key[b].contiguous(), value[b].contiguous(),
-                              g[b].float().contiguous(), beta[b].float().contiguous(), bounds,
-                              parents, init, has_init, flags, False, cap)
+        o, _, c, _ = _gdn_fwd_op(query[b].contiguous(), key[b].contiguous(),
+                                 value[b].contiguous(), g[b].float().contiguous(),
+                                 beta[b].float().contiguous(), bounds, parents, init, has_init,
+                                 flags, False, cap, False)
         outs.append(o)
         caps.append(c)
     core = torch.stack(outs, 0)
