@@ -60,6 +60,9 @@ def parse():
                          "Qwen3-4B architecture, tree_grad_hybrid on one 32k-token tree per GPU, "
                          "gradient averaging, AdamW)")
     ap.add_argument("--trees", type=int, default=8, help="attn3: number of trees in the job")
+    ap.add_argument("--fused-prologue", type=int, default=1,
+                    help="e2e5: q/k RMSNorm + rotary in one fused kernel (1) or the model's "
+                         "own ops (0)")
     ap.add_argument("--fused-ce", type=int, default=1,
                     help="e2e5: leaf losses by the chunked fused LM-head cross-entropy (1) "
                          "or from leaf-only logits (0)")
@@ -910,6 +913,9 @@ def run_e2e5(args):
     if args.ckpt_mlp:
         from tree_training_b200.hybrid import checkpoint_mlps
         checkpoint_mlps(model)
+    if args.fused_prologue:
+        from tree_training_b200.prologue import fuse_attention_prologue
+        fuse_attention_prologue(model)
     n_params = sum(p.numel() for p in model.parameters())
     roots = random_branching_tree(args.seed + rank, 32768, 64, 1024)
     info = tt.build_dfs_tree_info(roots)
@@ -986,7 +992,9 @@ def run_e2e5(args):
                        "peak_mem_gb_rank0": peak_mem / 1e9,
                        "mlp_recompute": bool(args.ckpt_mlp),
                        "leaf_loss": ("fused chunked LM head + CE (no logits)" if args.fused_ce
-                                     else "leaf-only logits + CE")},
+                                     else "leaf-only logits + CE"),
+                       "qk_prologue": ("fused q/k RMSNorm + rotary kernel" if args.fused_prologue
+                                       else "model's own ops")},
             "e2e": {"value": tokens_all / t_step, "unit": "tokens/s",
                     "h2d_bytes_per_step": None, "d2h_bytes_per_step": 4,
                     "note": "the step starts from the host tree (packing, id/label uploads "

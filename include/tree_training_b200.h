@@ -299,6 +299,24 @@ int tt_ce_fwd_grad(int dtype, int32_t n_rows, int32_t vocab, void* logits, int64
                    float* loss, int write_grad, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Fused attention prologue: per-head RMSNorm of q or k (weight [D] fp32, eps)
+ * then the rotary embedding with the tokens' cos / sin rows (the tree's
+ * depth-based positions), replacing q_norm / k_norm + apply_rotary_pos_emb of
+ * transformers' Qwen3 attention (models/qwen3/modeling_qwen3.py:263-268).
+ * x, y, dy, dx: [n_tok, H, D] contiguous in `dtype`; cos, sin: [n_tok, D] in
+ * `dtype`; D in {64, 128, 256}.  The backward recomputes the norm from x and
+ * writes per-block weight-gradient partials dw_part [blocks, D] fp32 (sum the
+ * rows for dw); blocks from tt_qk_norm_rope_bwd_blocks(n_tok * H).
+ */
+int tt_qk_norm_rope_fwd(int dtype, int64_t n_tok, int32_t H, int32_t D, const void* x,
+                        const float* weight, const void* cos_, const void* sin_, float eps,
+                        void* y, void* stream);
+int tt_qk_norm_rope_bwd_blocks(int64_t rows);
+int tt_qk_norm_rope_bwd(int dtype, int64_t n_tok, int32_t H, int32_t D, const void* x,
+                        const float* weight, const void* cos_, const void* sin_, float eps,
+                        const void* dy, void* dx, float* dw_part, int32_t blocks, void* stream);
+
+/* ------------------------------------------------------------------------
  * Tree-correct depthwise causal conv + SiLU.  Replaces _tree_correct_conv_varlen
  * (tree_dfs_ssm.py:285-348; dfs_tree_forward.py:191-246): each token's window
  * is the K-1 tokens before it on its root-to-node path (the reference's saved
