@@ -5,12 +5,13 @@
 // computed without atomics in two kernels that recompute P from the saved
 // row log-sum-exp:
 //
-//   dK/dV kernel  one CTA per (kv head, 128-key tile) holding K and V; streams
-//                 the q heads of its GQA group x the q tiles the work list
-//                 marks visible, as 64-row sub-tiles of Q and dO.
-//                 S^T = K Q^T and dP^T = V dO^T (A, B from shared memory); the
-//                 elementwise warps turn them into P^T and dS^T = P^T (dP^T -
-//                 delta), written as 16-bit tiles to shared memory; then
+//   dK/dV kernel  one CTA per (kv head, 128-key tile); K and V are copied once
+//                 into TMEM as 16-bit A operands; streams the q heads of its
+//                 GQA group x the q tiles the work list marks visible, as
+//                 64-row sub-tiles of Q and dO.  S^T = K Q^T and dP^T = V dO^T
+//                 (A from TMEM, B from shared memory); the elementwise warps
+//                 turn them into P^T and dS^T = P^T (dP^T - delta), written as
+//                 16-bit tiles to shared memory (the K / V tiles' space); then
 //                 dV += P^T dO and dK += dS^T Q.
 //   dQ kernel     one CTA per (q head, 128-row tile); Q and dO are copied once
 //                 into TMEM as 16-bit A operands; streams the visible kv tiles
@@ -18,17 +19,20 @@
 //                 TMEM, B from shared memory), dS = P (dP - delta) as a 16-bit
 //                 tile in shared memory (the Q tile's space), dQ += dS K.
 //
-// Streamed sub-tiles go through a ring (dK/dV 3 stages, dQ 4; each stage: two
-// 64 x 128 16-bit sub-tiles + their 64 row terms or key intervals, bulk-copied
-// on the same mbarrier), released per sub-tile.  Sub-tile S/dP accumulators
-// rotate through two TMEM buffers, each released as soon as the elementwise
-// warps have loaded it (not when the MMAs that consume P / dS finish), so the
-// S/dP MMAs of sub-tile u+2 can run while the elementwise warps still compute
-// sub-tile u.  P / dS tiles rotate through two shared-memory buffers, released
-// by the commit of the MMAs that read them.  TMEM (512 cols), buffer b < 2:
-// S [64b, 64b+64), dP [128+64b, 128+64b+64);
-//   dK/dV kernel: dV [256,384), dK [384,512);
-//   dQ kernel: dQ [256,384), Q [384,448), dO [448,512) (16-bit pairs).
+// Streamed sub-tiles go through a 4-stage ring (each stage: two 64 x 128
+// 16-bit sub-tiles + their 64 row terms or key intervals, bulk-copied on the
+// same mbarrier), released per sub-tile.  S/dP accumulators sit in NB TMEM
+// buffers (dK/dV 1, dQ 2), each released as soon as the elementwise warps have
+// loaded it (not when the MMAs that consume P / dS finish), so the next S/dP
+// MMAs run while the elementwise warps still compute.  P / dS tiles rotate
+// through two shared-memory buffers, released by the commit of the MMAs that
+// read them.  Reading the fixed operand from TMEM keeps the S/dP MMAs off the
+// shared-memory port, which the streamed operands, the P / dS tiles and the
+// accumulating MMAs share.  TMEM (512 cols), buffer b < NB:
+//   dK/dV kernel: S [0,64), dP [64,128), K [128,192), V [192,256) (16-bit
+//                 pairs), dV [256,384), dK [384,512);
+//   dQ kernel:    S [64b, 64b+64), dP [128+64b, ...), dQ [256,384),
+//                 Q [384,448), dO [448,512) (16-bit pairs).
 // Warps: 0 TMA producer, 1 S/dP MMA issuer, 2..9 elementwise (two warps per
 // TMEM lane quadrant; warp half h owns columns [32h, 32h+32) of each sub-tile
 // and the matching 64-byte half of each P / dS tile row), 10 the issuer of the
@@ -44,10 +48,11 @@ namespace {
 constexpr int kT = 128;                     // rows of the fixed tiles and of a list tile
 constexpr int kD = 128;                     // head dim
 constexpr int kSub = 64;                    // rows of a streamed sub-tile
-constexpr int kMaxStages = 4;               // streamed ring depth: dQ kernel 4, dK/dV kernel 3
-constexpr int kStagesDkdv = 3;
+constexpr int kMaxStages = 4;               // streamed ring depth
+constexpr int kStagesDkdv = 4;
 constexpr int kStagesDq = 4;
-constexpr int kNbDkdv = 2;                  // S/dP TMEM buffers: dK/dV kernel (dV, dK fill the rest)
+constexpr int kNbDkdv = 1;                  // S/dP TMEM buffers: dK/dV kernel (K, V, dV, dK fill the rest)
+constexpr int kNbPDkdv = 2;                 // P^T / dS^T shared-memory buffers: dK/dV kernel
 constexpr int kNbDq = 2;                    // S/dP TMEM buffers: dQ kernel (2 x 128 + dQ + Q/dO = 512)
 constexpr int kTileBytes = kT * kD * 2;     // fixed tile (128 rows)
 constexpr int kTileHalf = kTileBytes / 2;   // one 64-dim swizzle block of a fixed tile
@@ -58,12 +63,13 @@ constexpr int kAuxBytes = 2 * kAuxHalf;     // per stage: two 64-entry arrays
 constexpr int kPTile = kT * kSub * 2;       // 128 x 64 16-bit P / dS tile (A operand in smem)
 constexpr int kThreads = 352;            // 11 warps (roles below)
 constexpr int kEw = 256;                    // elementwise threads
+constexpr int kEwWarps = kEw / 32;          // arrivals on the elementwise warps' barriers
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdBarriers {
   uint64_t fixed_full;       // the two tiles loaded once (K,V or Q,dO)
-  uint64_t x_tmem_full;      // dQ kernel: Q and dO copied into TMEM (256 arrivals)
+  uint64_t x_tmem_full;      // the fixed tiles copied into TMEM (256 arrivals)
   uint64_t a_full[kMaxStages];  // streamed sub-tile A (Q or K) + its aux arrays
   uint64_t b_full[kMaxStages];  // streamed sub-tile B (dO or V)
   uint64_t ab_empty[kMaxStages];
@@ -78,14 +84,23 @@ struct BwdBarriers {
   int32_t abort;
 };
 
-// dK/dV: K, V, the ring, P^T and dS^T tiles per buffer; dQ: Q, dO (whose space
-// holds the dS tiles once Q and dO sit in TMEM), the ring.
+// dK/dV: K, V (whose space holds the P^T and dS^T tiles once K and V sit in
+// TMEM), the ring; dQ: Q, dO (whose space holds the dS tiles once Q and dO sit
+// in TMEM), the ring.
 constexpr size_t kSmemDkdv = 1024 + 2 * kTileBytes + kStagesDkdv * (2 * kSubBytes + kAuxBytes) +
-                             2 * kNbDkdv * kPTile + sizeof(BwdBarriers);
+                             sizeof(BwdBarriers);
+static_assert(2 * kNbPDkdv * kPTile <= 2 * kTileBytes, "P^T / dS^T tiles alias the K, V tiles");
 constexpr size_t kSmemDq = 1024 + 2 * kTileBytes + kStagesDq * (2 * kSubBytes + kAuxBytes) +
                            sizeof(BwdBarriers);
 static_assert(kSmemDkdv <= 232448 && kSmemDq <= 232448, "shared memory per block");
 static_assert(kNbDq * kPTile <= kTileBytes, "dS tiles alias the Q tile");
+
+// One arrival per warp: every lane has fenced its own tcgen05 / shared-memory
+// accesses, the warp synchronises, and lane 0 arrives for all 32.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
 
 __device__ __forceinline__ void raise_abort(BwdBarriers* sh, int32_t* status) {
   set_status(status, TT_ERR_DEVICE_TIMEOUT);
@@ -94,7 +109,7 @@ __device__ __forceinline__ void raise_abort(BwdBarriers* sh, int32_t* status) {
 
 __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
   mbar_init(&sh->fixed_full, 1);
-  mbar_init(&sh->x_tmem_full, kEw);
+  mbar_init(&sh->x_tmem_full, kEwWarps);
   for (int s = 0; s < kMaxStages; ++s) {
     mbar_init(&sh->a_full[s], 1);
     mbar_init(&sh->b_full[s], 1);
@@ -102,8 +117,8 @@ __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
   }
   for (int b = 0; b < 2; ++b) {
     mbar_init(&sh->sdp_full[b], 1);
-    mbar_init(&sh->sdp_free[b], kEw);
-    mbar_init(&sh->ew_full[b], kEw);
+    mbar_init(&sh->sdp_free[b], kEwWarps);
+    mbar_init(&sh->ew_full[b], kEwWarps);
     mbar_init(&sh->pa_free[b], 1);
   }
   mbar_init(&sh->acc_done, 1);
@@ -327,9 +342,9 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   constexpr int KS = kStagesDkdv;
   uint8_t* rQ = sV + kTileBytes;                 // KS x Q sub-tile
   uint8_t* rDO = rQ + KS * kSubBytes;            // KS x dO sub-tile
-  uint8_t* sPt = rDO + KS * kSubBytes;           // kNbDkdv x P^T tile
-  uint8_t* sDSt = sPt + kNbDkdv * kPTile;        // kNbDkdv x dS^T tile
-  uint8_t* aux = sDSt + kNbDkdv * kPTile;        // KS x (LSE[64], delta[64])
+  uint8_t* sPt = sK;                             // kNbPDkdv x P^T tile, once K is in TMEM
+  uint8_t* sDSt = sK + kNbPDkdv * kPTile;        // kNbPDkdv x dS^T tile, once V is in TMEM
+  uint8_t* aux = rDO + KS * kSubBytes;           // KS x (LSE[64], delta[64])
   BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + KS * kAuxBytes);
   const volatile int32_t* abort_flag = &sh->abort;
 
@@ -350,7 +365,9 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
+  constexpr uint32_t kColK = 128, kColV = 192;   // K, V as 16-bit pairs (A of S^T, dP^T)
   constexpr uint32_t kColDV = 256, kColDK = 384;
+  static_assert(64 * kNbDkdv * 2 <= kColK, "dK/dV kernel TMEM map");
 
   if (warp == 0) {
     if (lane == 0 && n_u > 0) {
@@ -375,8 +392,8 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   } else if (warp == 1) {
     if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
-      sdp_issuer<kNbDkdv, KS, false>(sh, abort_flag, status, tmem, n_u, smem_u32(sK), smem_u32(sV), smem_u32(rQ),
-                 smem_u32(rDO), id_s);
+      sdp_issuer<kNbDkdv, KS, true>(sh, abort_flag, status, tmem, n_u, tmem + kColK,
+                                    tmem + kColV, smem_u32(rQ), smem_u32(rDO), id_s);
     }
   } else if (warp == 10) {
     if (lane == 0 && n_u > 0) {
@@ -387,7 +404,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       // A of dV += P^T dO and dK += dS^T Q: the P^T / dS^T tiles, K-major
       const uint64_t d_pt = desc_sw128(smem_u32(sPt), 16, 1024);
       const uint64_t d_dst = desc_sw128(smem_u32(sDSt), 16, 1024);
-      acc_issuer<kNbDkdv, KS>(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
+      acc_issuer<kNbPDkdv, KS>(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
         mma_ss_k64(tmem + kColDV, desc_add(d_pt, b * kPTile), desc_add(d_do, s * kSubBytes),
                    id_o, accumulate);
         mma_ss_k64(tmem + kColDK, desc_add(d_dst, b * kPTile), desc_add(d_q, s * kSubBytes),
@@ -403,8 +420,24 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const int hi = j < n_kv ? kv_hi[j] : 0;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     bool ok = true;
-    for (int u = 0; u < n_u; ++u) {
-      const int it = u >> 1, b = u % kNbDkdv, s = u % KS;
+    if (n_u > 0) {
+      // K and V rows into TMEM, where S^T = K Q^T and dP^T = V dO^T read their
+      // A operand; their shared-memory tiles then hold the P^T / dS^T tiles
+      ok = mbar_wait(&sh->fixed_full, 0, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tile_row_to_tmem(sK, r, half, lane_addr + kColK + 32 * half);
+        tile_row_to_tmem(sV, r, half, lane_addr + kColV + 32 * half);
+        tmem_st_wait();
+        tc_fence_before();
+        warp_arrive(&sh->x_tmem_full, lane);
+      }
+      // every elementwise thread has read its K / V rows before any P^T / dS^T
+      // row lands there (all 256 reach this point: the wait is bounded)
+      asm volatile("bar.sync 1, %0;" ::"n"(kEw) : "memory");
+    }
+    for (int u = 0; u < n_u && ok; ++u) {
+      const int it = u >> 1, b = u % kNbDkdv, s = u % KS, pb = u % kNbPDkdv;
       const int ent = bwd_list[e0 + it % n_list];
       const int q0 = (ent >> 1) * kT + (u & 1) * kSub + half * 32;   // first q row of this warp
       const bool partial = ent & 1;
@@ -417,7 +450,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       float sv[32], dp[32];
       tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
       tc_fence_before();
-      mbar_arrive(&sh->sdp_free[b]);           // the S/dP buffer may be overwritten
+      warp_arrive(&sh->sdp_free[b], lane);     // the S/dP buffer may be overwritten
       const float4* L4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes) + half * 8;
       const float4* D4 = reinterpret_cast<const float4*>(aux + s * kAuxBytes + kAuxHalf) + half * 8;
       uint32_t pw[16], dw[16];
@@ -451,15 +484,15 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         dw[2 * i] = pack2<kBf16>(ds01.x, ds01.y);
         dw[2 * i + 1] = pack2<kBf16>(ds23.x, ds23.y);
       }
-      if (u >= kNbDkdv) {                      // the MMAs of sub-tile u - 2 read this buffer
-        ok = mbar_wait(&sh->pa_free[b], ((u - kNbDkdv) / kNbDkdv) & 1, abort_flag);
+      if (u >= kNbPDkdv) {                     // the MMAs of sub-tile u - 2 read this buffer
+        ok = mbar_wait(&sh->pa_free[pb], ((u - kNbPDkdv) / kNbPDkdv) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
       }
-      store_tile_row(sPt + b * kPTile, r, half, pw);
-      store_tile_row(sDSt + b * kPTile, r, half, dw);
+      store_tile_row(sPt + pb * kPTile, r, half, pw);
+      store_tile_row(sDSt + pb * kPTile, r, half, dw);
       fence_proxy_async_smem();
-      mbar_arrive(&sh->ew_full[b]);
+      warp_arrive(&sh->ew_full[pb], lane);
     }
     if (ok && n_u > 0) {
       ok = mbar_wait(&sh->acc_done, 0, abort_flag);
@@ -592,7 +625,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         tile_row_to_tmem(sDO, r, half, lane_addr + kColDO + 32 * half);
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&sh->x_tmem_full);
+        warp_arrive(&sh->x_tmem_full, lane);
       }
       // every elementwise thread has read its Q rows before any dS row lands
       // in the Q tile's space (all 256 reach this point: the wait is bounded)
@@ -610,7 +643,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       float sv[32], dp[32];
       tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
       tc_fence_before();
-      mbar_arrive(&sh->sdp_free[b]);           // the S/dP buffer may be overwritten
+      warp_arrive(&sh->sdp_free[b], lane);     // the S/dP buffer may be overwritten
       float p[32];
       const float2 sc2 = make_float2(scale_log2, scale_log2), nl2 = make_float2(-l2, -l2);
 #pragma unroll
@@ -649,7 +682,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       }
       store_tile_row(sDS + b * kPTile, r, half, dw);
       fence_proxy_async_smem();
-      mbar_arrive(&sh->ew_full[b]);
+      warp_arrive(&sh->ew_full[b], lane);
     }
     if (ok && n_u > 0) {
       ok = mbar_wait(&sh->acc_done, 0, abort_flag);
