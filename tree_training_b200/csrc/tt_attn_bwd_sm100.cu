@@ -76,7 +76,6 @@ struct BwdBarriers {
   uint64_t sdp_full[2];      // S and dP of a sub-tile ready (per TMEM buffer)
   uint64_t sdp_free[2];      // the elementwise warps loaded S and dP (256 arrivals)
   uint64_t ew_full[2];       // P / dS of a sub-tile written to shared memory (256 arrivals)
-  uint64_t pa_free[2];       // the accumulating MMAs reading a P / dS buffer finished
   uint64_t acc_done;         // every MMA of the CTA finished
   uint64_t drain;            // abort path of the S/dP issuer
   uint64_t drain_acc;        // abort path of the accumulation issuer
@@ -93,6 +92,8 @@ static_assert(2 * kNbPDkdv * kPTile <= 2 * kTileBytes, "P^T / dS^T tiles alias t
 constexpr size_t kSmemDq = 1024 + 2 * kTileBytes + kStagesDq * (2 * kSubBytes + kAuxBytes) +
                            sizeof(BwdBarriers);
 static_assert(kSmemDkdv <= 232448 && kSmemDq <= 232448, "shared memory per block");
+// a P / dS buffer is released with the ring stage of the sub-tile that read it
+static_assert(kStagesDkdv % kNbPDkdv == 0 && kStagesDq % kNbDq == 0, "buffer / stage rotation");
 static_assert(kNbDq * kPTile <= kTileBytes, "dS tiles alias the Q tile");
 
 // One arrival per warp: every lane has fenced its own tcgen05 / shared-memory
@@ -119,7 +120,6 @@ __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
     mbar_init(&sh->sdp_full[b], 1);
     mbar_init(&sh->sdp_free[b], kEwWarps);
     mbar_init(&sh->ew_full[b], kEwWarps);
-    mbar_init(&sh->pa_free[b], 1);
   }
   mbar_init(&sh->acc_done, 1);
   mbar_init(&sh->drain, 1);
@@ -266,7 +266,9 @@ __device__ __forceinline__ void produce(BwdBarriers* sh, const volatile int32_t*
 //       tiles once the elementwise warps wrote them (ew_full); it alone
 //       accumulates into dK/dV or dQ, in sub-tile order, so the result does
 //       not depend on how the two instruction streams interleave.  Its commit
-//       releases the P / dS buffer (pa_free) and the ring stage (ab_empty).
+//       releases the ring stage (ab_empty) and with it the P / dS buffer of
+//       the sub-tile: one commit per sub-tile (each commit waits for the
+//       tensor pipe to drain, so they are kept few).
 // kXTmem: the fixed tiles X, Y are A operands in TMEM (x_addr, y_addr are TMEM
 // column addresses, filled by the elementwise warps) instead of shared memory.
 template <int NB, int KS, bool kXTmem>
@@ -309,7 +311,6 @@ __device__ __forceinline__ void acc_issuer(BwdBarriers* sh, const volatile int32
     if (!(ok = mbar_wait(&sh->ew_full[b], (u / NB) & 1, abort_flag))) break;
     tc_fence_after();
     acc(s, b, u > 0);
-    tc_commit(&sh->pa_free[b]);
     // the stage's last reader: sdp(u) completed before the elementwise warps
     // started on sub-tile u, and acc(u) waited for them
     tc_commit(&sh->ab_empty[s]);
@@ -485,7 +486,9 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         dw[2 * i + 1] = pack2<kBf16>(ds23.x, ds23.y);
       }
       if (u >= kNbPDkdv) {                     // the MMAs of sub-tile u - 2 read this buffer
-        ok = mbar_wait(&sh->pa_free[pb], ((u - kNbPDkdv) / kNbPDkdv) & 1, abort_flag);
+        // (buffer pb was last read by sub-tile u - 2, whose MMAs' commit
+        // releases ring stage (u - 2) % KS)
+        ok = mbar_wait(&sh->ab_empty[(u - kNbPDkdv) % KS], ((u - kNbPDkdv) / KS) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
       }
@@ -676,7 +679,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         dw[i] = pack2<kBf16>(ds.x, ds.y);
       }
       if (u >= kNbDq) {                        // the MMAs of sub-tile u - 2 read this buffer
-        ok = mbar_wait(&sh->pa_free[b], ((u - kNbDq) / kNbDq) & 1, abort_flag);
+        ok = mbar_wait(&sh->ab_empty[(u - kNbDq) % KS], ((u - kNbDq) / KS) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
       }
