@@ -57,14 +57,31 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   return d;
 }
 
+// 4-byte asynchronous global -> shared copy; `valid` false writes a zero.
+__device__ __forceinline__ void cp_async4(float* smem, const float* gmem, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem))), "l"(gmem),
+               "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+constexpr int kGemmStages = 3;              // K slices in flight
+
 // C[i,j] = alpha * sum_k A[i,k] B[k,j] + beta * C[i,j] over a list of 64 x 64
 // output tiles (tile = {segment, tm << 16 | tn}) and heads (blockIdx.z);
 // operand element (r, c) of segment s lives at
 // base + head * h_stride + off_s + r * rs_s + c * cs_s.
 // Register-blocked: each of the 128 threads owns rows {4ty..4ty+3,
 // 32+4ty..} and columns {4tx..4tx+3} of the tile, reads them as float4 from
-// shared memory and accumulates with paired FMAs; the next K slice is fetched
-// into registers while the current one is multiplied (two shared buffers).
+// shared memory and accumulates with paired FMAs.  K slices stream into a
+// 3-stage shared-memory ring with asynchronous 4-byte copies (any stride,
+// zero-filled outside the segment), two slices ahead of the multiply.
 __global__ void __launch_bounds__(kGemmThreads)
 seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
          const float* __restrict__ A, long long a_hs, const float* __restrict__ B, long long b_hs,
@@ -76,8 +93,8 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
   const float* a = A + h * a_hs + sd.a_off;
   const float* b = B + h * b_hs + sd.b_off;
   float* c = C + h * c_hs + sd.c_off;
-  __shared__ __align__(16) float sa[2][kBK][kBM + kRowPad];
-  __shared__ __align__(16) float sb[2][kBK][kBN + kRowPad];
+  __shared__ __align__(16) float sa[kGemmStages][kBK][kBM + kRowPad];
+  __shared__ __align__(16) float sb[kGemmStages][kBK][kBN + kRowPad];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int i0 = tm * kBM, j0 = tn * kBN;
   // consecutive threads walk the operand's unit-stride dimension: element i
@@ -91,23 +108,15 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
   const int astep = adr * (int)sd.a_rs + adk * (int)sd.a_cs;
   const int bstep = bdk * (int)sd.b_rs + bdc * (int)sd.b_cs;
   constexpr int kPer = kBM * kBK / kGemmThreads;   // staged elements per operand per thread
-  float ra[kPer], rb[kPer];
-  auto fetch = [&](int k0) {
+  auto issue = [&](int k0, int st) {
     const float* pa = a + (long long)(i0 + ar0) * sd.a_rs + (long long)(k0 + ak0) * sd.a_cs;
     const float* pb = b + (long long)(k0 + bk0) * sd.b_rs + (long long)(j0 + bc0) * sd.b_cs;
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       const bool in_a = i0 + ar0 + i * adr < sd.M && k0 + ak0 + i * adk < sd.K;
-      ra[i] = in_a ? pa[i * astep] : 0.f;
+      cp_async4(&sa[st][ak0 + i * adk][ar0 + i * adr], in_a ? pa + i * astep : a, in_a);
       const bool in_b = k0 + bk0 + i * bdk < sd.K && j0 + bc0 + i * bdc < sd.N;
-      rb[i] = in_b ? pb[i * bstep] : 0.f;
-    }
-  };
-  auto stash = [&](int buf) {
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      sa[buf][ak0 + i * adk][ar0 + i * adr] = ra[i];
-      sb[buf][bk0 + i * bdk][bc0 + i * bdc] = rb[i];
+      cp_async4(&sb[st][bk0 + i * bdk][bc0 + i * bdc], in_b ? pb + i * bstep : b, in_b);
     }
   };
   // acc[p][w]: rows 2p and 2p+1 of the thread's 8 rows, column w of its 4
@@ -116,13 +125,20 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
   for (int p = 0; p < 4; ++p)
 #pragma unroll
     for (int w = 0; w < 4; ++w) acc[p][w] = make_float2(0.f, 0.f);
-  fetch(0);
-  stash(0);
-  __syncthreads();
-  int buf = 0;
-  for (int k0 = 0; k0 < sd.K; k0 += kBK) {
-    const bool more = k0 + kBK < sd.K;
-    if (more) fetch(k0 + kBK);
+  const int nk = (sd.K + kBK - 1) / kBK;
+  // one commit group per slice (empty past the end), so wait_group counts slices
+#pragma unroll
+  for (int t = 0; t < kGemmStages - 1; ++t) {
+    if (t < nk) issue(t * kBK, t);
+    cp_async_commit();
+  }
+  for (int t = 0; t < nk; ++t) {
+    cp_async_wait<kGemmStages - 2>();   // slice t has landed (this thread's copies)
+    __syncthreads();                    // ... and everyone's; slice t-1 is consumed
+    if (t + kGemmStages - 1 < nk)
+      issue((t + kGemmStages - 1) * kBK, (t + kGemmStages - 1) % kGemmStages);
+    cp_async_commit();
+    const int buf = t % kGemmStages;
 #pragma unroll
     for (int kk = 0; kk < kBK; ++kk) {
       const float4 a0 = *reinterpret_cast<const float4*>(&sa[buf][kk][4 * ty]);
@@ -139,10 +155,8 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
         for (int p = 0; p < 4; ++p) acc[p][w] = fma2(ap[p], bb, acc[p][w]);
       }
     }
-    if (more) stash(buf ^ 1);
-    __syncthreads();
-    buf ^= 1;
   }
+  cp_async_wait<0>();
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
     const int gi = i0 + (u < 4 ? 4 * ty + u : 32 + 4 * ty + (u - 4));
