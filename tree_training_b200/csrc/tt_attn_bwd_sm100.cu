@@ -128,25 +128,11 @@ __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
   fence_mbar_init();
 }
 
-// D[128 x 64] = X[128 rows] * A[64 rows]^T over K = 128 dims; X is a fixed
-// 128-row tile, A a 64-row streamed sub-tile, both K-major 128-byte swizzled.
 // A shared-memory descriptor moved by `off` bytes: the start field holds
 // address >> 4 and shared addresses stay below 256 KiB, so the sum never
 // carries out of the field.  Lets the MMA warp build each descriptor once and
 // add constant offsets in the issue loop.
 __device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t off) { return d + (off >> 4); }
-
-// D[128 x 64] = X[128 x 128] * A[64 x 128]^T, X a fixed tile and A a streamed
-// sub-tile, both K-major (descriptors dx, da at their first byte).
-__device__ __forceinline__ void mma_ss_n64(uint32_t d_tmem, uint64_t dx, uint64_t da,
-                                           uint32_t idesc) {
-#pragma unroll
-  for (int kk = 0; kk < kD / 16; ++kk) {
-    const uint32_t ox = (kk >> 2) * kTileHalf + (kk & 3) * 32;
-    const uint32_t oa = (kk >> 2) * kSubHalf + (kk & 3) * 32;
-    mma_ss(d_tmem, desc_add(dx, ox), desc_add(da, oa), idesc, kk > 0 ? 1u : 0u);
-  }
-}
 
 // D[128 x 64] = X[128 x 128, 16-bit in TMEM] * A[64 x 128]^T: X's dims d sit
 // as 16-bit pairs in columns x_tmem + d/2, A is a streamed K-major sub-tile.
@@ -267,17 +253,15 @@ __device__ __forceinline__ void produce(BwdBarriers* sh, const volatile int32_t*
 //       accumulates into dK/dV or dQ, in sub-tile order, so the result does
 //       not depend on how the two instruction streams interleave.  Its commit
 //       releases the ring stage (ab_empty) and with it the P / dS buffer of
-//       the sub-tile: one commit per sub-tile (each commit waits for the
-//       tensor pipe to drain, so they are kept few).
-// kXTmem: the fixed tiles X, Y are A operands in TMEM (x_addr, y_addr are TMEM
-// column addresses, filled by the elementwise warps) instead of shared memory.
-template <int NB, int KS, bool kXTmem>
+//       the sub-tile: one commit per sub-tile.
+// The fixed tiles X, Y are A operands in TMEM (x_addr, y_addr: TMEM column
+// addresses, filled by the elementwise warps before x_tmem_full completes).
+template <int NB, int KS>
 __device__ __forceinline__ void sdp_issuer(BwdBarriers* sh, const volatile int32_t* abort_flag,
                                            int32_t* status, uint32_t tmem, int n_u,
                                            uint32_t x_addr, uint32_t y_addr, uint32_t ring_a,
                                            uint32_t ring_b, uint32_t id_s) {
-  bool ok = mbar_wait(kXTmem ? &sh->x_tmem_full : &sh->fixed_full, 0, abort_flag);
-  const uint64_t dx = desc_sw128(x_addr, 16, 1024), dy = desc_sw128(y_addr, 16, 1024);
+  bool ok = mbar_wait(&sh->x_tmem_full, 0, abort_flag);
   const uint64_t da = desc_sw128(ring_a, 16, 1024), db = desc_sw128(ring_b, 16, 1024);
   for (int u = 0; u < n_u && ok; ++u) {
     const int s = u % KS, b = u % NB;
@@ -286,13 +270,8 @@ __device__ __forceinline__ void sdp_issuer(BwdBarriers* sh, const volatile int32
     if (!(ok = mbar_wait(&sh->a_full[s], ph, abort_flag))) break;
     if (!(ok = mbar_wait(&sh->b_full[s], ph, abort_flag))) break;
     tc_fence_after();
-    if (kXTmem) {
-      mma_ts_n64(tmem + 64 * b, x_addr, desc_add(da, s * kSubBytes), id_s);
-      mma_ts_n64(tmem + 64 * NB + 64 * b, y_addr, desc_add(db, s * kSubBytes), id_s);
-    } else {
-      mma_ss_n64(tmem + 64 * b, dx, desc_add(da, s * kSubBytes), id_s);
-      mma_ss_n64(tmem + 64 * NB + 64 * b, dy, desc_add(db, s * kSubBytes), id_s);
-    }
+    mma_ts_n64(tmem + 64 * b, x_addr, desc_add(da, s * kSubBytes), id_s);
+    mma_ts_n64(tmem + 64 * NB + 64 * b, y_addr, desc_add(db, s * kSubBytes), id_s);
     tc_commit(&sh->sdp_full[b]);
   }
   if (!ok) {
@@ -393,7 +372,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   } else if (warp == 1) {
     if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
-      sdp_issuer<kNbDkdv, KS, true>(sh, abort_flag, status, tmem, n_u, tmem + kColK,
+      sdp_issuer<kNbDkdv, KS>(sh, abort_flag, status, tmem, n_u, tmem + kColK,
                                     tmem + kColV, smem_u32(rQ), smem_u32(rDO), id_s);
     }
   } else if (warp == 10) {
@@ -596,7 +575,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   } else if (warp == 1) {
     if (lane == 0 && n_u > 0) {
       constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
-      sdp_issuer<kNbDq, KS, true>(sh, abort_flag, status, tmem, n_u, tmem + kColQ, tmem + kColDO,
+      sdp_issuer<kNbDq, KS>(sh, abort_flag, status, tmem, n_u, tmem + kColQ, tmem + kColDO,
                               smem_u32(rK), smem_u32(rV), id_s);
     }
   } else if (warp == 10) {
