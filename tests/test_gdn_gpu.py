@@ -122,6 +122,32 @@ def test_gdn_exact_inverse_vs_oracle_and_recurrence(lo, hi):
     assert rel(got["last"], rec_states[-1]) < 5e-5
 
 
+def test_gdn_exact_inverse_block_edges():
+    """Node lengths at the 64-token block edges of the inverse (1, 63, 64, 65,
+    128, 129, 192) against the float64 recurrence."""
+    lens = [64, 1, 63, 65, 128, 129, 192, 2]
+    parents = [-1, 0, 0, 2, 3, 1, 4, 6]
+    bounds, s0 = [], 0
+    for L in lens:
+        bounds.append((s0, s0 + L))
+        s0 += L
+    S, H, D = s0, 2, 32
+    g_ = np.random.default_rng(21)
+    q = g_.standard_normal((1, S, 1, D))
+    k = g_.standard_normal((1, S, 1, D))
+    v = g_.standard_normal((1, S, H, D)) * 0.5
+    gg = -np.log1p(np.exp(-g_.standard_normal((1, S, H))))
+    bt = 1.0 / (1.0 + np.exp(-g_.standard_normal((1, S, H))))
+    do = g_.standard_normal((1, S, H, D))
+    got = run_gdn(q, k, v, gg, bt, bounds, parents, None, True, do, None, torch.float32,
+                  exact=True)
+    rec, _ = O.gdn_tree_recurrent(q, k, v, gg, bt, bounds, parents, None, True)
+    assert rel(got["out"], rec) < 5e-5
+    grads = O.gdn_tree_bwd(q, k, v, gg, bt, bounds, parents, do, None, True, None, True)
+    for key, ref in zip(("dq", "dk", "dv", "dg", "dbeta"), grads[:5]):
+        assert rel(got[key], ref) < 5e-5, key
+
+
 def test_gdn_exact_inverse_is_segmentation_invariant():
     """One 600-token path as a single node, and as a chain of 4 nodes: the
     exact mode gives the same output (the reference's truncated correction
