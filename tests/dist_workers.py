@@ -1,4 +1,5 @@
-"""Rank bodies for the world-size-2 gloo tests of tree_training_b200.dist.
+"""Rank bodies for the world-size-2 tests of tree_training_b200.dist (gloo on
+CPU; NCCL on two GPUs with NVLS off).
 
 Each worker runs in a spawned process with the process group already set up by
 ``run_ranks``; it returns a picklable result or raises."""
@@ -20,23 +21,32 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def _entry(rank, world, port, fn_name, args, pg_timeout, q):
+# bodies after which a rank may be gone: the survivors do not tear the group down
+_PEER_MAY_BE_GONE = ("fail_rank1", "nccl_fail_rank1")
+
+
+def _entry(rank, world, port, fn_name, args, pg_timeout, q, backend):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     try:
-        dist.init_process_group("gloo", rank=rank, world_size=world,
-                                timeout=datetime.timedelta(seconds=pg_timeout))
+        kw = {}
+        if backend == "nccl":
+            os.environ["NCCL_NVLS_ENABLE"] = "0"      # no NVLink multicast objects
+            torch.cuda.set_device(rank)
+            kw["device_id"] = torch.device("cuda", rank)
+        dist.init_process_group(backend, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=pg_timeout), **kw)
         res = globals()[fn_name](rank, world, *args)
         q.put((rank, "ok", res))
     except BaseException as e:  # noqa: BLE001 - reported to the parent
         q.put((rank, "err", f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
     finally:
-        if dist.is_initialized() and fn_name != "fail_rank1":
+        if dist.is_initialized() and fn_name not in _PEER_MAY_BE_GONE:
             dist.destroy_process_group()
 
 
 def run_ranks(fn_name: str, world: int = 2, args=(), pg_timeout: float = 20.0,
-              limit_s: float = 120.0, expect=None):
+              limit_s: float = 120.0, expect=None, backend: str = "gloo"):
     """Start ``world`` spawned ranks running ``fn_name``; return {rank: (status,
     result)} for the ranks that reported within ``limit_s`` (waiting only for
     the ranks in ``expect``, default all)."""
@@ -45,7 +55,8 @@ def run_ranks(fn_name: str, world: int = 2, args=(), pg_timeout: float = 20.0,
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_entry, args=(r, world, port, fn_name, args, pg_timeout, q))
+    procs = [ctx.Process(target=_entry,
+                         args=(r, world, port, fn_name, args, pg_timeout, q, backend))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -157,4 +168,86 @@ def fail_rank1(rank, world):
     except Exception as e:  # noqa: BLE001 - the error type depends on the backend
         out["collective"] = type(e).__name__
     out["collective_s"] = time.monotonic() - t0
+    return out
+
+
+# ---------------------------------------------------------------------------
+# NCCL rank bodies (one GPU per rank)
+# ---------------------------------------------------------------------------
+
+def _attn_model(dev):
+    torch.manual_seed(0)
+    m = torch.nn.ModuleDict({"emb": torch.nn.Embedding(256, 64),
+                             "q": torch.nn.Linear(64, 4 * 128), "k": torch.nn.Linear(64, 128),
+                             "v": torch.nn.Linear(64, 128)})
+    return m.to(dev)
+
+
+def _attn_tree_loss(model, roots, dev):
+    """Tree attention (bf16, tcgen05 path) over one packed tree; scalar loss."""
+    import tree_training_b200 as tt
+    info = tt.build_dfs_tree_info(roots)
+    meta = info.attn_meta()
+    ids = torch.as_tensor(info.dfs_token_ids_np % 256, dtype=torch.long, device=dev)
+    x = model["emb"](ids)
+    n = ids.shape[0]
+    q = model["q"](x).view(n, 4, 128).to(torch.bfloat16)
+    k = model["k"](x).view(n, 1, 128).to(torch.bfloat16)
+    v = model["v"](x).view(n, 1, 128).to(torch.bfloat16)
+    out = tt.tree_attention(q, k, v, meta)
+    return out.float().square().mean()
+
+
+def _attn_trees():
+    from tree_training_b200.synthetic import bfs_tree
+    return [bfs_tree(300 + i, 2048, 32, 256, 256) for i in range(2)]
+
+
+def nccl_dp_attention_step(rank, world):
+    """Each rank backpropagates the tree attention of its own tree and the
+    gradients are averaged over NCCL; each rank also computes both trees'
+    gradients alone on its GPU.  Returns the largest relative difference."""
+    from tree_training_b200.dist import GradAverager, RankWatch
+    dev = torch.device("cuda", rank)
+    trees = _attn_trees()
+    watch = RankWatch(dist.distributed_c10d._get_default_store(), rank, world, timeout_s=20.0)
+    model = _attn_model(dev)
+    watch.beat(0)
+    (_attn_tree_loss(model, trees[rank], dev) / world).backward()
+    GradAverager(model.parameters()).average()
+    got = [p.grad.detach().clone() for p in model.parameters()]
+    ref_model = _attn_model(dev)
+    for roots in trees:
+        # the average divides the sum over ranks by W again
+        (_attn_tree_loss(ref_model, roots, dev) / (world * world)).backward()
+    torch.cuda.synchronize(dev)
+    diff = max(float((g - p.grad).abs().max() / (p.grad.abs().max() + 1e-30))
+               for g, p in zip(got, ref_model.parameters()))
+    watch.beat(1)
+    return diff
+
+
+def nccl_fail_rank1(rank, world):
+    """After one data-parallel step, rank 1 leaves between steps (its kernels
+    and collectives finished); rank 0 learns of it from the heartbeat before
+    launching anything for the next step, and issues no collective."""
+    import time
+    from tree_training_b200.dist import GradAverager, RankFailure, RankWatch
+    dev = torch.device("cuda", rank)
+    watch = RankWatch(dist.distributed_c10d._get_default_store(), rank, world, timeout_s=3.0)
+    model = _attn_model(dev)
+    watch.beat(0)
+    _attn_tree_loss(model, _attn_trees()[rank], dev).backward()
+    GradAverager(model.parameters()).average()
+    torch.cuda.synchronize(dev)
+    if rank == 1:
+        os._exit(0)
+    out = {}
+    t0 = time.monotonic()
+    try:
+        watch.beat(1)
+        out["heartbeat"] = "no error"
+    except RankFailure as e:
+        out["heartbeat"] = f"RankFailure {e.missing}"
+    out["heartbeat_s"] = time.monotonic() - t0
     return out
