@@ -149,8 +149,11 @@ int tt_tree_attn_fwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t h
                      const int32_t* fwd_ptr, const int32_t* fwd_list, float scale, void* out,
                      float* lse, int32_t* status, void* stream);
 
-/* Workspace bytes tt_tree_attn_bwd needs (fp32 row terms; dQ accumulator
- * for the tcgen05 path). */
+/* Workspace bytes for tt_tree_attn_bwd: the fp32 row terms (delta), then one
+ * int32 per 128-key tile, in which the tcgen05 path orders the dK/dV tiles by
+ * work, longest first (less tail on the GPU).  A workspace holding only the
+ * row terms (hq * round_up(n_q, 128) floats, rounded up to 256 bytes) is also
+ * accepted; the tiles then run in key order.  Results are the same either way. */
 int64_t tt_tree_attn_bwd_workspace_size(int dtype, int32_t n_q, int32_t n_kv, int32_t hq,
                                         int32_t hkv, int32_t head_dim);
 

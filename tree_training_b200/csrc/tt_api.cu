@@ -87,12 +87,12 @@ extern "C" int tt_tree_attn_fwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq
 extern "C" int64_t tt_tree_attn_bwd_workspace_size(int dtype, int32_t n_q, int32_t n_kv,
                                                    int32_t hq, int32_t hkv, int32_t D) {
   (void)dtype;
-  (void)n_kv;
   (void)hkv;
   (void)D;
-  // fp32 delta = rowsum(dO * O) per (head, row), rows padded like the LSE
-  int64_t bytes = (int64_t)hq * tt::lse_ld(n_q) * 4;
-  return (bytes + 255) / 256 * 256;
+  // fp32 delta = rowsum(dO * O) per (head, row), rows padded like the LSE;
+  // then the dK/dV tile order (one int32 per 128-key tile)
+  const int64_t order = ((int64_t)(n_kv + 127) / 128 * 4 + 255) / 256 * 256;
+  return tt_attn_bwd_delta_bytes(n_q, hq) + order;
 }
 
 extern "C" int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv,
@@ -108,8 +108,13 @@ extern "C" int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq
                                 void* workspace, int64_t workspace_bytes, int phases,
                                 int32_t* status, void* stream) {
   if (!valid_dims(n_q, n_kv, hq, hkv, D)) return TT_ERR_INVALID_ARG;
-  if (workspace_bytes < tt_tree_attn_bwd_workspace_size(dtype, n_q, n_kv, hq, hkv, D))
-    return TT_ERR_WORKSPACE;
+  // the row terms are required; the tile-order part is used when present
+  const int64_t delta_bytes = tt_attn_bwd_delta_bytes(n_q, hq);
+  if (workspace_bytes < delta_bytes) return TT_ERR_WORKSPACE;
+  int32_t* kt_order =
+      workspace_bytes >= tt_tree_attn_bwd_workspace_size(dtype, n_q, n_kv, hq, hkv, D)
+          ? reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + delta_bytes)
+          : nullptr;
   if ((n_q > 0 && (!q || !out || !dout || !lse || !dq || !fwd_ptr)) ||
       (n_kv > 0 && (!k || !v || !dk || !dv || !kv_lo || !kv_hi || !bwd_ptr)))
     return TT_ERR_INVALID_ARG;
@@ -117,8 +122,8 @@ extern "C" int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq
     return tt_launch_attn_bwd_sm100(dtype, n_q, n_kv, hq, hkv, D, q, q_st, q_sh, k, k_st, k_sh, v,
                                     v_st, v_sh, out, dout, do_st, do_sh, lse, kv_lo, kv_hi,
                                     fwd_ptr, fwd_list, bwd_ptr, bwd_list, scale, dq, dq_st, dq_sh,
-                                    dk, dk_st, dk_sh, dv, dv_st, dv_sh, (float*)workspace, phases, status,
-                                    (cudaStream_t)stream);
+                                    dk, dk_st, dk_sh, dv, dv_st, dv_sh, (float*)workspace, kt_order,
+                                    phases, status, (cudaStream_t)stream);
   return tt_launch_attn_bwd_simt(dtype, n_q, n_kv, hq, hkv, D, q, q_st, q_sh, k, k_st, k_sh, v,
                                  v_st, v_sh, out, dout, do_st, do_sh, lse, kv_lo, kv_hi, fwd_ptr,
                                  fwd_list, bwd_ptr, bwd_list, scale, dq, dq_st, dq_sh, dk, dk_st,

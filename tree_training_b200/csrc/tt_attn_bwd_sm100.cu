@@ -313,7 +313,8 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                  const int32_t* __restrict__ bwd_list, const float* __restrict__ lse,
                  const float* __restrict__ delta, float scale_log2, float scale,
                  void* __restrict__ dk_, int64_t dk_st, int64_t dk_sh, void* __restrict__ dv_,
-                 int64_t dv_st, int64_t dv_sh, int32_t* status) {
+                 int64_t dv_st, int64_t dv_sh, const int32_t* __restrict__ kt_order,
+                 int32_t* status) {
   using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
@@ -330,7 +331,9 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hk = blockIdx.x;
-  const int kt = blockIdx.y;                 // root-side tiles (longest lists) first
+  // key tile: in work order (longest list first) when the order is given,
+  // else in key order, where the root-side tiles with the longest lists come first
+  const int kt = kt_order ? kt_order[blockIdx.y] : static_cast<int>(blockIdx.y);
   const int e0 = bwd_ptr[kt];
   const int n_list = bwd_ptr[kt + 1] - e0;
   const int n_u = 2 * rep * n_list;          // 64-row sub-tiles
@@ -696,6 +699,22 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   }
 }
 
+// order[r] = the key tile with the r-th longest work list (ties: lower tile
+// first), so the dK/dV CTAs that take longest are dispatched first.  Thread i
+// counts the tiles that sort before tile i; n_tiles^2 comparisons in all.
+__global__ void order_tiles_by_work(int n_tiles, const int32_t* __restrict__ ptr,
+                                   int32_t* __restrict__ order) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_tiles) return;
+  const int wi = ptr[i + 1] - ptr[i];
+  int rank = 0;
+  for (int j = 0; j < n_tiles; ++j) {
+    const int wj = ptr[j + 1] - ptr[j];
+    rank += (wj > wi || (wj == wi && j < i)) ? 1 : 0;
+  }
+  order[rank] = i;
+}
+
 // delta[h, i] = sum_d O[i,h,d] dO[i,h,d] over the padded [hq, ld] layout
 // (one warp per (row, head), 4 dims per lane).
 template <typename T>
@@ -785,8 +804,8 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
                              const int32_t* fwd_list, const int32_t* bwd_ptr,
                              const int32_t* bwd_list, float scale, void* dq, int64_t dq_st,
                              int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
-                             int64_t dv_st, int64_t dv_sh, float* delta, int phases,
-                             int32_t* status, cudaStream_t st) {
+                             int64_t dv_st, int64_t dv_sh, float* delta, int32_t* kt_order,
+                             int phases, int32_t* status, cudaStream_t st) {
   using namespace tt::sm100;
   if (D != kD || (dtype != TT_BF16 && dtype != TT_F16)) return TT_ERR_UNSUPPORTED;
   if (!aligned16(kv_lo) || !aligned16(kv_hi) || !aligned16(lse) || !aligned16(delta) ||
@@ -829,10 +848,15 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
     auto kdkdv = bf16 ? attn_bwd_dkdv_tc<true> : attn_bwd_dkdv_tc<false>;
     TT_CUDA_OK(cudaFuncSetAttribute(kdkdv, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemDkdv));
-    dim3 g(hkv, (n_kv + kT - 1) / kT);
+    const int n_tiles = (n_kv + kT - 1) / kT;
+    if (kt_order) {
+      order_tiles_by_work<<<(n_tiles + 255) / 256, 256, 0, st>>>(n_tiles, bwd_ptr, kt_order);
+      ++launches;
+    }
+    dim3 g(hkv, n_tiles);
     kdkdv<<<g, kThreads, kSmemDkdv, st>>>(mq, mk, mv, mdo, n_q, n_kv, rep, kv_lo, kv_hi,
                                            bwd_ptr, bwd_list, lse, delta, scale_log2, scale, dk,
-                                           dk_st, dk_sh, dv, dv_st, dv_sh, status);
+                                           dk_st, dk_sh, dv, dv_st, dv_sh, kt_order, status);
     ++launches;
   }
   if (phases & TT_BWD_DQ) {

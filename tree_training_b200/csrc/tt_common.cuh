@@ -93,5 +93,11 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
                              const int32_t* fwd_list, const int32_t* bwd_ptr,
                              const int32_t* bwd_list, float scale, void* dq, int64_t dq_st,
                              int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
-                             int64_t dv_st, int64_t dv_sh, float* delta, int phases,
-                             int32_t* status, cudaStream_t stream);
+                             int64_t dv_st, int64_t dv_sh, float* delta, int32_t* kt_order,
+                             int phases, int32_t* status, cudaStream_t stream);
+
+// Bytes of the fp32 row terms (delta) at the start of the backward workspace.
+inline int64_t tt_attn_bwd_delta_bytes(int32_t n_q, int32_t hq) {
+  const int64_t bytes = (int64_t)hq * tt::lse_ld(n_q) * 4;
+  return (bytes + 255) / 256 * 256;
+}
