@@ -15,28 +15,29 @@
 //                 dV += P^T dO and dK += dS^T Q.
 //   dQ kernel     one CTA per (q head, 128-row tile); Q and dO are copied once
 //                 into TMEM as 16-bit A operands; streams the visible kv tiles
-//                 as 64-key sub-tiles of K and V: S = Q K^T, dP = dO V^T (A from
-//                 TMEM, B from shared memory), dS = P (dP - delta) as a 16-bit
-//                 tile in shared memory (the Q tile's space), dQ += dS K.
+//                 whole (128 keys): S = Q K^T, dP = dO V^T (A from TMEM, B from
+//                 shared memory, N = 128), dS = P (dP - delta) as a 16-bit tile
+//                 in shared memory (the Q / dO tiles' space), dQ += dS K.
 //
-// Streamed sub-tiles go through a 4-stage ring (each stage: two 64 x 128
-// 16-bit sub-tiles + their 64 row terms or key intervals, bulk-copied on the
-// same mbarrier), released per sub-tile.  S/dP accumulators sit in NB TMEM
-// buffers (dK/dV 1, dQ 2), each released as soon as the elementwise warps have
-// loaded it (not when the MMAs that consume P / dS finish), so the next S/dP
-// MMAs run while the elementwise warps still compute.  P / dS tiles rotate
-// through two shared-memory buffers, released by the commit of the MMAs that
-// read them.  Reading the fixed operand from TMEM keeps the S/dP MMAs off the
+// dK/dV streams its sub-tiles through a 4-stage ring (each stage: two 64 x
+// 128 16-bit sub-tiles + their 64 row terms, bulk-copied on the same
+// mbarrier), dQ its kv tiles through a 2-stage ring of 128-row tiles with
+// their key intervals; stages are released per (sub-)tile.  Each kernel keeps
+// one S/dP TMEM buffer, released as soon as the elementwise warps have loaded
+// it (not when the MMAs that consume P / dS finish), so the next S/dP MMAs run
+// while the elementwise warps still compute.  P / dS tiles rotate through two
+// shared-memory buffers, released by the commit of the MMAs that read them.
+// Reading the fixed operand from TMEM keeps the S/dP MMAs off the
 // shared-memory port, which the streamed operands, the P / dS tiles and the
-// accumulating MMAs share.  TMEM (512 cols), buffer b < NB:
+// accumulating MMAs share.  TMEM (512 cols):
 //   dK/dV kernel: S [0,64), dP [64,128), K [128,192), V [192,256) (16-bit
 //                 pairs), dV [256,384), dK [384,512);
-//   dQ kernel:    S [64b, 64b+64), dP [128+64b, ...), dQ [256,384),
-//                 Q [384,448), dO [448,512) (16-bit pairs).
+//   dQ kernel:    S [0,128), dP [128,256), dQ [256,384), Q [384,448),
+//                 dO [448,512) (16-bit pairs).
 // Warps: 0 TMA producer, 1 S/dP MMA issuer, 2..9 elementwise (two warps per
-// TMEM lane quadrant; warp half h owns columns [32h, 32h+32) of each sub-tile
-// and the matching 64-byte half of each P / dS tile row), 10 the issuer of the
-// accumulating MMAs.
+// TMEM lane quadrant; in dK/dV warp half h owns columns [32h, 32h+32) of each
+// sub-tile, in dQ keys [64h, 64h+64) of each tile, and the matching part of
+// each P / dS tile row), 10 the issuer of the accumulating MMAs.
 #include <type_traits>
 
 #include "tt_sm100.cuh"
@@ -50,10 +51,8 @@ constexpr int kD = 128;                     // head dim
 constexpr int kSub = 64;                    // rows of a streamed sub-tile
 constexpr int kMaxStages = 4;               // streamed ring depth
 constexpr int kStagesDkdv = 4;
-constexpr int kStagesDq = 4;
 constexpr int kNbDkdv = 1;                  // S/dP TMEM buffers: dK/dV kernel (K, V, dV, dK fill the rest)
 constexpr int kNbPDkdv = 2;                 // P^T / dS^T shared-memory buffers: dK/dV kernel
-constexpr int kNbDq = 2;                    // S/dP TMEM buffers: dQ kernel (2 x 128 + dQ + Q/dO = 512)
 constexpr int kTileBytes = kT * kD * 2;     // fixed tile (128 rows)
 constexpr int kTileHalf = kTileBytes / 2;   // one 64-dim swizzle block of a fixed tile
 constexpr int kSubBytes = kSub * kD * 2;    // streamed sub-tile (64 rows)
@@ -89,12 +88,9 @@ struct BwdBarriers {
 constexpr size_t kSmemDkdv = 1024 + 2 * kTileBytes + kStagesDkdv * (2 * kSubBytes + kAuxBytes) +
                              sizeof(BwdBarriers);
 static_assert(2 * kNbPDkdv * kPTile <= 2 * kTileBytes, "P^T / dS^T tiles alias the K, V tiles");
-constexpr size_t kSmemDq = 1024 + 2 * kTileBytes + kStagesDq * (2 * kSubBytes + kAuxBytes) +
-                           sizeof(BwdBarriers);
-static_assert(kSmemDkdv <= 232448 && kSmemDq <= 232448, "shared memory per block");
+static_assert(kSmemDkdv <= 232448, "shared memory per block");
 // a P / dS buffer is released with the ring stage of the sub-tile that read it
-static_assert(kStagesDkdv % kNbPDkdv == 0 && kStagesDq % kNbDq == 0, "buffer / stage rotation");
-static_assert(kNbDq * kPTile <= kTileBytes, "dS tiles alias the Q tile");
+static_assert(kStagesDkdv % kNbPDkdv == 0, "buffer / stage rotation");
 
 // One arrival per warp: every lane has fenced its own tcgen05 / shared-memory
 // accesses, the warp synchronises, and lane 0 arrives for all 32.
@@ -514,6 +510,32 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 }
 
 // ======================================================================== dQ
+// Whole 128-key kv tiles per step (N = 128 MMAs), one S/dP TMEM buffer, a
+// 2-stage ring of K / V tiles.  Tile u of the CTA's list:
+//   S = Q K^T, dP = dO V^T            (warp 1; A = Q / dO from TMEM)
+//   dS = P (dP - delta) -> smem tile  (warps 2-9; each thread loads the 64
+//                                      keys of its row at once, which frees
+//                                      the S/dP buffer, then computes them as
+//                                      two 32-key passes)
+//   dQ += dS K                        (warp 10; A = dS, B = K from smem)
+constexpr int kStagesDq2 = 2;
+constexpr int kAuxQ = kT * 4;               // 128 four-byte key intervals
+constexpr size_t kSmemDq2 = 1024 + 2 * kTileBytes + kStagesDq2 * (2 * kTileBytes + 2 * kAuxQ) +
+                            sizeof(BwdBarriers);
+static_assert(kSmemDq2 <= 232448, "shared memory per block");
+static_assert(kStagesDq2 <= kMaxStages, "ring barriers");
+
+// D[128 x 128] = X[128 x 128, 16-bit in TMEM] * A[128 x 128]^T, A a K-major
+// 128-row tile in shared memory (two 64-dim swizzle blocks).
+__device__ __forceinline__ void mma_ts_n128(uint32_t d_tmem, uint32_t x_tmem, uint64_t da,
+                                            uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < kD / 16; ++kk) {
+    const uint32_t oa = (kk >> 2) * kTileHalf + (kk & 3) * 32;
+    mma_ts(d_tmem, x_tmem + kk * 8, desc_add(da, oa), idesc, kk > 0 ? 1u : 0u);
+  }
+}
+
 template <bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -524,16 +546,16 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
                const float* __restrict__ delta, float scale_log2, float scale,
                void* __restrict__ dq_, int64_t dq_st, int64_t dq_sh, int32_t* status) {
   using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
+  constexpr int KS = kStagesDq2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sQ = base;
   uint8_t* sDO = sQ + kTileBytes;
-  constexpr int KS = kStagesDq;
-  uint8_t* rK = sDO + kTileBytes;                // KS x K sub-tile
-  uint8_t* rV = rK + KS * kSubBytes;             // KS x V sub-tile
-  uint8_t* aux = rV + KS * kSubBytes;            // KS x (kv_lo[64], kv_hi[64])
-  uint8_t* sDS = sQ;                             // kNbDq x dS tile, once Q is in TMEM
-  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + KS * kAuxBytes);
+  uint8_t* rK = sDO + kTileBytes;                // KS x K tile
+  uint8_t* rV = rK + KS * kTileBytes;            // KS x V tile
+  uint8_t* aux = rV + KS * kTileBytes;           // KS x (kv_lo[128], kv_hi[128])
+  uint8_t* sDS = sQ;                             // 2 x dS tile, once Q and dO are in TMEM
+  BwdBarriers* sh = reinterpret_cast<BwdBarriers*>(aux + KS * 2 * kAuxQ);
   const volatile int32_t* abort_flag = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -541,7 +563,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   const int qt = gridDim.y - 1 - blockIdx.y;
   const int hk = h / rep;
   const int e0 = fwd_ptr[qt];
-  const int n_u = 2 * (fwd_ptr[qt + 1] - e0);
+  const int n_u = fwd_ptr[qt + 1] - e0;          // kv tiles
   const int ld = lse_ld(n_q);
 
   if (threadIdx.x == 0) init_barriers(sh);
@@ -553,9 +575,8 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
-  constexpr uint32_t kColDQ = 128 * kNbDq;   // after the S/dP buffers
-  constexpr uint32_t kColQ = kColDQ + 128, kColDO = kColQ + 64;   // Q, dO as 16-bit pairs
-  static_assert(kColDO + 64 == kTmemCols, "dQ kernel TMEM map");
+  constexpr uint32_t kColS = 0, kColP = 128, kColDQ = 256;
+  constexpr uint32_t kColQ = 384, kColDO = 448;   // Q, dO as 16-bit pairs
 
   if (warp == 0) {
     if (lane == 0 && n_u > 0) {
@@ -566,34 +587,91 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tma_load_3d(sQ + kTileHalf, &tm_q, &sh->fixed_full, 64, qt * kT, h);
       tma_load_3d(sDO, &tm_do, &sh->fixed_full, 0, qt * kT, h);
       tma_load_3d(sDO + kTileHalf, &tm_do, &sh->fixed_full, 64, qt * kT, h);
-      produce<KS>(sh, abort_flag, status, n_u, rK, rV, aux, &tm_k, &tm_v,
-              [&](int u, int* row, int* head, const void** xa, const void** xb) {
-                const int j0 = (fwd_list[e0 + (u >> 1)] >> 1) * kT + (u & 1) * kSub;
-                *row = j0;
-                *head = hk;
-                *xa = kv_lo + j0;
-                *xb = kv_hi + j0;
-              });
+      int issued[KS] = {};
+      bool ok = true;
+      for (int u = 0; u < n_u; ++u) {
+        const int s = u % KS;
+        if (u >= KS && !(ok = mbar_wait(&sh->ab_empty[s], ((u / KS) - 1) & 1, abort_flag))) break;
+        const int j0 = (fwd_list[e0 + u] >> 1) * kT;
+        uint8_t* k_dst = rK + s * kTileBytes;
+        uint8_t* v_dst = rV + s * kTileBytes;
+        uint8_t* x_dst = aux + s * 2 * kAuxQ;
+        mbar_arrive_expect_tx(&sh->a_full[s], kTileBytes + 2 * kAuxQ);
+        tma_load_3d(k_dst, &tm_k, &sh->a_full[s], 0, j0, hk);
+        tma_load_3d(k_dst + kTileHalf, &tm_k, &sh->a_full[s], 64, j0, hk);
+        bulk_load(x_dst, kv_lo + j0, kAuxQ, &sh->a_full[s]);
+        bulk_load(x_dst + kAuxQ, kv_hi + j0, kAuxQ, &sh->a_full[s]);
+        mbar_arrive_expect_tx(&sh->b_full[s], kTileBytes);
+        tma_load_3d(v_dst, &tm_v, &sh->b_full[s], 0, j0, hk);
+        tma_load_3d(v_dst + kTileHalf, &tm_v, &sh->b_full[s], 64, j0, hk);
+        issued[s] += 1;
+      }
+      if (!ok) {
+        raise_abort(sh, status);
+        mbar_wait(&sh->fixed_full, 0, nullptr);
+        for (int s = 0; s < KS; ++s)
+          if (issued[s] > 0) {
+            mbar_wait(&sh->a_full[s], (issued[s] - 1) & 1, nullptr);
+            mbar_wait(&sh->b_full[s], (issued[s] - 1) & 1, nullptr);
+          }
+      }
     }
   } else if (warp == 1) {
     if (lane == 0 && n_u > 0) {
-      constexpr uint32_t id_s = idesc_f16(kBf16, kT, kSub, false);
-      sdp_issuer<kNbDq, KS>(sh, abort_flag, status, tmem, n_u, tmem + kColQ, tmem + kColDO,
-                              smem_u32(rK), smem_u32(rV), id_s);
+      // S / dP issuer: tile u waits for the elementwise warps to have loaded
+      // tile u-1 out of the single S/dP buffer, and for its K / V stage
+      constexpr uint32_t id_s = idesc_f16(kBf16, kT, kT, false);
+      const uint64_t dk = desc_sw128(smem_u32(rK), 16, 1024);
+      const uint64_t dv = desc_sw128(smem_u32(rV), 16, 1024);
+      bool ok = mbar_wait(&sh->x_tmem_full, 0, abort_flag);
+      for (int u = 0; u < n_u && ok; ++u) {
+        const int s = u % KS;
+        const uint32_t ph = (u / KS) & 1;
+        if (u >= 1 && !(ok = mbar_wait(&sh->sdp_free[0], (u - 1) & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(&sh->a_full[s], ph, abort_flag))) break;
+        if (!(ok = mbar_wait(&sh->b_full[s], ph, abort_flag))) break;
+        tc_fence_after();
+        mma_ts_n128(tmem + kColS, tmem + kColQ, desc_add(dk, s * kTileBytes), id_s);
+        mma_ts_n128(tmem + kColP, tmem + kColDO, desc_add(dv, s * kTileBytes), id_s);
+        tc_commit(&sh->sdp_full[0]);
+      }
+      if (!ok) {
+        raise_abort(sh, status);
+        tc_commit(&sh->drain);
+        mbar_wait(&sh->drain, 0, nullptr);
+      }
     }
   } else if (warp == 10) {
     if (lane == 0 && n_u > 0) {
+      // dQ += dS K, in tile order (the only accumulating MMAs: deterministic);
+      // the commit releases the K / V stage and the dS buffer of tile u
       constexpr uint32_t id_o = idesc_f16(kBf16, kT, kD, true);
-      const uint64_t d_k = desc_sw128(smem_u32(rK), kSubHalf, 1024);   // B of dQ += dS K
-      const uint64_t d_ds = desc_sw128(smem_u32(sDS), 16, 1024);        // A: the dS tiles
-      acc_issuer<kNbDq, KS>(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
-        mma_ss_k64(tmem + kColDQ, desc_add(d_ds, b * kPTile), desc_add(d_k, s * kSubBytes), id_o,
-                   accumulate);
-      });
+      const uint64_t d_k = desc_sw128(smem_u32(rK), kTileHalf, 1024);   // B, MN-major
+      const uint64_t d_ds = desc_sw128(smem_u32(sDS), 16, 1024);        // A, K-major
+      bool ok = true;
+      for (int u = 0; u < n_u && ok; ++u) {
+        const int s = u % KS, b = u & 1;
+        if (!(ok = mbar_wait(&sh->ew_full[b], (u >> 1) & 1, abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kT / 16; ++kk) {
+          const uint32_t oa = b * kTileBytes + (kk >> 2) * kTileHalf + (kk & 3) * 32;
+          mma_ss(tmem + kColDQ, desc_add(d_ds, oa), desc_add(d_k, s * kTileBytes + kk * 2048),
+                 id_o, (u > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&sh->ab_empty[s]);
+      }
+      if (ok) {
+        tc_commit(&sh->acc_done);
+      } else {
+        raise_abort(sh, status);
+        tc_commit(&sh->drain_acc);
+        mbar_wait(&sh->drain_acc, 0, nullptr);
+      }
     }
   } else {
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = (warp - 2) >> 2;              // keys [64 half, 64 half + 64) of a tile
     const int r = quad * 32 + lane;
     const int row = qt * kT + r;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
@@ -602,7 +680,7 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     bool ok = true;
     if (n_u > 0) {
       // Q and dO rows into TMEM, where S = Q K^T and dP = dO V^T read their A
-      // operand (shared memory then only feeds the streamed K / V sub-tiles)
+      // operand; their shared-memory tiles then hold the dS tiles
       ok = mbar_wait(&sh->fixed_full, 0, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
@@ -612,60 +690,66 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         tc_fence_before();
         warp_arrive(&sh->x_tmem_full, lane);
       }
-      // every elementwise thread has read its Q rows before any dS row lands
-      // in the Q tile's space (all 256 reach this point: the wait is bounded)
+      // every elementwise thread has read its Q / dO rows before any dS row
+      // lands in their space (all 256 reach this point: the wait is bounded)
       asm volatile("bar.sync 1, %0;" ::"n"(kEw) : "memory");
     }
+    const float2 sc2 = make_float2(scale_log2, scale_log2), nl2 = make_float2(-l2, -l2);
+    const float2 ndr = make_float2(-dr, -dr);
     for (int u = 0; u < n_u && ok; ++u) {
-      const int b = u % kNbDq, s = u % KS;
-      const bool partial = fwd_list[e0 + (u >> 1)] & 1;
-      ok = mbar_wait(&sh->sdp_full[b], (u / kNbDq) & 1, abort_flag);
+      const int s = u % KS, b = u & 1;
+      const bool partial = fwd_list[e0 + u] & 1;
+      ok = mbar_wait(&sh->sdp_full[0], u & 1, abort_flag);
       if (ok && partial) ok = mbar_wait(&sh->a_full[s], (u / KS) & 1, abort_flag);
+      if (ok && u >= 2)   // the dQ MMAs of tile u - 2 read dS buffer b
+        ok = mbar_wait(&sh->ab_empty[(u - 2) % KS], ((u - 2) / KS) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t cs = 64 * b + 32 * half, cp = 64 * kNbDq + 64 * b + 32 * half;
-      float sv[32], dp[32];
-      tmem_ld32x2(lane_addr + cs, lane_addr + cp, sv, dp);
+      uint8_t* ds_box = sDS + b * kTileBytes + half * kTileHalf;
+      float sva[2][32], dpa[2][32];
+      tmem_ld32x2(lane_addr + kColS + 64 * half, lane_addr + kColP + 64 * half, sva[0], dpa[0]);
+      tmem_ld32x2(lane_addr + kColS + 64 * half + 32, lane_addr + kColP + 64 * half + 32, sva[1],
+                  dpa[1]);
       tc_fence_before();
-      warp_arrive(&sh->sdp_free[b], lane);     // the S/dP buffer may be overwritten
-      float p[32];
-      const float2 sc2 = make_float2(scale_log2, scale_log2), nl2 = make_float2(-l2, -l2);
+      warp_arrive(&sh->sdp_free[0], lane);       // S/dP fully loaded: next tile's MMAs may run
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        // two columns per instruction; one pair in four on the FMA-pipe exp2
-        const float2 x = ffma2(make_float2(sv[2 * i], sv[2 * i + 1]), sc2, nl2);
-        const float2 e = (i & 3) == 3 ? exp2_poly2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
-        p[2 * i] = e.x;
-        p[2 * i + 1] = e.y;
-      }
-      if (partial) {
-        // key intervals of this sub-tile, zero-padded past n_kv (never visible)
-        const int4* LO = reinterpret_cast<const int4*>(aux + s * kAuxBytes) + half * 8;
-        const int4* HI = reinterpret_cast<const int4*>(aux + s * kAuxBytes + kAuxHalf) + half * 8;
+      for (int pass = 0; pass < 2; ++pass) {
+        const uint32_t c0 = 64 * half + 32 * pass;
+        float (&sv)[32] = sva[pass];
+        float (&dp)[32] = dpa[pass];
+        float p[32];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int4 a = LO[i], z = HI[i];
-          if (!visible(a.x, z.x, row)) p[4 * i + 0] = 0.f;
-          if (!visible(a.y, z.y, row)) p[4 * i + 1] = 0.f;
-          if (!visible(a.z, z.z, row)) p[4 * i + 2] = 0.f;
-          if (!visible(a.w, z.w, row)) p[4 * i + 3] = 0.f;
+        for (int i = 0; i < 16; ++i) {
+          // two columns per instruction; one pair in four on the FMA-pipe exp2
+          const float2 x = ffma2(make_float2(sv[2 * i], sv[2 * i + 1]), sc2, nl2);
+          const float2 e =
+              (i & 3) == 3 ? exp2_poly2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          p[2 * i] = e.x;
+          p[2 * i + 1] = e.y;
         }
-      }
-      uint32_t dw[16];
-      const float2 ndr = make_float2(-dr, -dr);
+        if (partial) {
+          // key intervals of these 32 keys, zero-padded past n_kv (never visible)
+          const int4* LO = reinterpret_cast<const int4*>(aux + s * 2 * kAuxQ + c0 * 4);
+          const int4* HI = reinterpret_cast<const int4*>(aux + s * 2 * kAuxQ + kAuxQ + c0 * 4);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float2 ds = fmul2(make_float2(p[2 * i], p[2 * i + 1]),
-                                fadd2(make_float2(dp[2 * i], dp[2 * i + 1]), ndr));
-        dw[i] = pack2<kBf16>(ds.x, ds.y);
+          for (int i = 0; i < 8; ++i) {
+            const int4 a = LO[i], z = HI[i];
+            if (!visible(a.x, z.x, row)) p[4 * i + 0] = 0.f;
+            if (!visible(a.y, z.y, row)) p[4 * i + 1] = 0.f;
+            if (!visible(a.z, z.z, row)) p[4 * i + 2] = 0.f;
+            if (!visible(a.w, z.w, row)) p[4 * i + 3] = 0.f;
+          }
+        }
+        uint32_t dw[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 ds = fmul2(make_float2(p[2 * i], p[2 * i + 1]),
+                                  fadd2(make_float2(dp[2 * i], dp[2 * i + 1]), ndr));
+          dw[i] = pack2<kBf16>(ds.x, ds.y);
+        }
+        store_tile_row(ds_box, r, pass, dw);
       }
-      if (u >= kNbDq) {                        // the MMAs of sub-tile u - 2 read this buffer
-        ok = mbar_wait(&sh->ab_empty[(u - kNbDq) % KS], ((u - kNbDq) / KS) & 1, abort_flag);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-      }
-      store_tile_row(sDS + b * kPTile, r, half, dw);
       fence_proxy_async_smem();
       warp_arrive(&sh->ew_full[b], lane);
     }
@@ -863,14 +947,14 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
     // fixed Q/dO tiles (128 rows), streamed K/V sub-tiles (64 rows)
     CUtensorMap mq, mk, mv, mdo;
     if ((rc = make_map(&mq, bf16, q, n_q, hq, q_st, q_sh, kT)) != TT_OK) return rc;
-    if ((rc = make_map(&mk, bf16, k, n_kv, hkv, k_st, k_sh, kSub)) != TT_OK) return rc;
-    if ((rc = make_map(&mv, bf16, v, n_kv, hkv, v_st, v_sh, kSub)) != TT_OK) return rc;
+    if ((rc = make_map(&mk, bf16, k, n_kv, hkv, k_st, k_sh, kT)) != TT_OK) return rc;
+    if ((rc = make_map(&mv, bf16, v, n_kv, hkv, v_st, v_sh, kT)) != TT_OK) return rc;
     if ((rc = make_map(&mdo, bf16, dout, n_q, hq, do_st, do_sh, kT)) != TT_OK) return rc;
     auto kdq = bf16 ? attn_bwd_dq_tc<true> : attn_bwd_dq_tc<false>;
     TT_CUDA_OK(cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)kSmemDq));
+                                    (int)kSmemDq2));
     dim3 g(hq, (n_q + kT - 1) / kT);
-    kdq<<<g, kThreads, kSmemDq, st>>>(mq, mk, mv, mdo, n_q, n_kv, rep, kv_lo, kv_hi, fwd_ptr,
+    kdq<<<g, kThreads, kSmemDq2, st>>>(mq, mk, mv, mdo, n_q, n_kv, rep, kv_lo, kv_hi, fwd_ptr,
                                          fwd_list, lse, delta, scale_log2, scale, dq, dq_st,
                                          dq_sh, status);
     ++launches;
