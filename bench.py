@@ -490,22 +490,28 @@ def run_ours(args):
     up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     in_ready = [torch.cuda.Event() for _ in range(2)]
     in_free = [None, None]
+    metas = [None, None]
     h2d = d2h = 0
 
     def upload(i):
+        # the prefetch stage: pack the step's tree on the host and upload its
+        # metadata with its inputs on `up`, so the compute stream never waits
+        # for a small copy queued behind the previous step's large upload
         st = i % 2
         if in_free[st] is not None:
             up.wait_event(in_free[st])
+        m = tt.build_dfs_tree_info(roots).attn_meta()          # host packer
         with torch.cuda.stream(up):
+            tt.prefetch_tree_meta(m, dev, q0.dtype, D)
             for n, t in host_in.items():
                 dev_in[st][n].copy_(t, non_blocking=True)
+        metas[st] = m
         in_ready[st].record(up)
 
     def compute(i):
         nonlocal h2d, d2h
         st = i % 2
-        inf = tt.build_dfs_tree_info(roots)          # host packer
-        m = inf.attn_meta()
+        m = metas[st]
         main.wait_event(in_ready[st])
         d = dev_in[st]
         qd, kd, vd = (d[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
@@ -541,6 +547,45 @@ def run_ours(args):
     b.synchronize()
     t_e2e = max_over_ranks(a.elapsed_time(b) / 1e3 / args.steps, world, dev)
     e2e_value = flops_all / t_e2e / 1e12
+
+    # What bounds the e2e number: the same per-step copies with no compute
+    # (uploads on `up`, downloads of the previous step's gradients on `down`,
+    # both directions at once), and the host packer's CPU time per step.
+    grads = [torch.empty_like(dev_in[0][n]) for n in ("q", "k", "v")]
+
+    def copies_only(n):
+        for i in range(n):
+            st = i % 2
+            with torch.cuda.stream(up):
+                for nm, t in host_in.items():
+                    dev_in[st][nm].copy_(t, non_blocking=True)
+            with torch.cuda.stream(down):
+                for g, hb in zip(grads, host_out[st]):
+                    hb.copy_(g, non_blocking=True)
+        main.wait_stream(up)
+        main.wait_stream(down)
+
+    def copy_time(fn, n):
+        fn(1)
+        torch.cuda.synchronize()
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        c0.record(main)
+        fn(n)
+        c1.record(main)
+        c1.synchronize()
+        return c0.elapsed_time(c1) / 1e3 / n
+
+    n_copy = min(args.steps, 20)
+    in_bytes = sum(t.numel() * t.element_size() for t in host_in.values())
+    t_copy = max_over_ranks(copy_time(copies_only, n_copy), world, dev)
+    t_up = max_over_ranks(copy_time(lambda n: [dev_in[0][nm].copy_(t, non_blocking=True)
+                                               for _ in range(n) for nm, t in host_in.items()],
+                                    n_copy), world, dev)
+    p0 = time.perf_counter()
+    for _ in range(n_copy):
+        tt.build_dfs_tree_info(roots).attn_meta()
+    t_pack = (time.perf_counter() - p0) / n_copy
 
     pk, pk_src = peaks()
     # algorithmic FLOPs of each kernel as designed (2*D per visible pair and GEMM):
@@ -588,7 +633,14 @@ def run_ours(args):
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": t_e2e * 1e3,
                     "tokens_per_s": tokens_all / t_e2e,
                     "schedule": "pipelined: next step's upload and this step's download "
-                                "overlap compute (two input sets, three streams)"},
+                                "overlap compute (two input sets, three streams)",
+                    "copy_bound": {"ms_per_step": t_copy * 1e3,
+                                   "h2d_only_ms_per_step": t_up * 1e3,
+                                   "h2d_gbs": in_bytes / t_up / 1e9,
+                                   "frac": t_copy / t_e2e,
+                                   "note": "the same per-step pinned copies, both directions "
+                                           "at once, no compute; frac = this / e2e step"},
+                    "host_packer_ms_per_step": t_pack * 1e3},
             "kernel_ms": {n: t * 1e3 for n, t in kern.items()},
             "host_enqueue_ms_per_step": host_enqueue_ms,
             "roofline": {"bound": "tensor", "kernel": dominant,

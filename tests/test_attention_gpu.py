@@ -291,3 +291,35 @@ def test_config3_size_tree_sampled_rows_and_identities():
     assert rel(f(qg.grad[rows]), dq_ref) < 2e-2
     assert torch.isfinite(kg.grad).all() and torch.isfinite(vg.grad).all()
     _check_grad_identities(do, kg.grad, vg.grad, hq // hkv)
+
+
+def test_metadata_prefetched_on_upload_stream_matches_lazy_upload():
+    """prefetch_tree_meta uploads the kernel metadata on a side stream (a
+    training loop's prefetch stage); after the compute stream waits for that
+    stream, the op's outputs and gradients are bit-identical to those of a
+    call that uploads the metadata itself."""
+    meta, q, k, v, do = make_case(21, 2000, 8, 2, 128, 32, 300, root_len=400)
+    q, k, v, do = map(bf16_round, (q, k, v, do))
+    ref = run(q, k, v, meta, do, torch.bfloat16)
+    meta2 = tt.TreeAttnMeta(meta.n_q, meta.kv_lo, meta.kv_hi)
+    up = torch.cuda.Stream(DEV)
+    main = torch.cuda.current_stream(DEV)
+    with torch.cuda.stream(up):
+        assert tt.prefetch_tree_meta(meta2, DEV, torch.bfloat16, 128) is meta2
+        # the large input copies of the same stage, then the inputs
+        qt, kt, vt, dot = (torch.tensor(x, dtype=torch.bfloat16).pin_memory()
+                           .to(DEV, non_blocking=True) for x in (q, k, v, do))
+    main.wait_stream(up)
+    for t in (qt, kt, vt, dot):
+        t.record_stream(main)
+    assert meta2.prefetched
+    qt, kt, vt = (t.requires_grad_(True) for t in (qt, kt, vt))
+    out = tt.tree_attention(qt, kt, vt, meta2)
+    out.backward(dot)
+    del meta2                      # the memory stays reserved for the compute stream's kernels
+    torch.cuda.synchronize()
+    tt.check_device_status(DEV)
+    f = lambda t: t.detach().double().cpu().numpy()
+    for name, a, b in zip(("out", "dq", "dk", "dv"), (f(out), f(qt.grad), f(kt.grad),
+                                                      f(vt.grad)), ref):
+        assert np.array_equal(a, b), name

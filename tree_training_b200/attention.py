@@ -236,10 +236,30 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, meta: Tree
     q, k, v = (_aligned(t) for t in (q, k, v))
     md = meta.device(q.device, *tile_shape(q.dtype, D, 0))
     mb = meta.device(q.device, *tile_shape(q.dtype, D, 1))
+    if meta.prefetched:
+        # uploaded on another stream (prefetch_tree_meta): keep the caching
+        # allocator from reusing the memory while this stream's kernels read it
+        cur = torch.cuda.current_stream(q.device)
+        for x in (md["kv_lo"], md["fwd_ptr"], mb["fwd_ptr"]):
+            x.record_stream(cur)
     out, _ = _tree_attn_fwd_op(q, k, v, md["kv_lo"], md["kv_hi"], md["fwd_ptr"], md["fwd_list"],
                                mb["fwd_ptr"], mb["fwd_list"], mb["bwd_ptr"], mb["bwd_list"],
                                float(scale))
     return out
+
+
+def prefetch_tree_meta(meta: TreeAttnMeta, device: torch.device, dtype: torch.dtype,
+                       head_dim: int) -> TreeAttnMeta:
+    """Upload the tree's kernel metadata for ``tree_attention`` on ``device``
+    on the CURRENT stream, ahead of the call: a training loop's prefetch stage
+    calls it on its upload stream beside the step's q/k/v copies (and orders
+    the compute stream after that stream, as for the inputs), so the compute
+    stream never waits for a copy queued behind a large upload.  Returns
+    ``meta``."""
+    for kind in (0, 1):
+        meta.device(device, *tile_shape(dtype, head_dim, kind))
+    meta.prefetched = True
+    return meta
 
 
 def _aligned(t: torch.Tensor) -> torch.Tensor:

@@ -177,6 +177,17 @@ def build_dfs_tree_info(roots: Sequence, pos_offset: int = 0) -> DFSTreeInfo:
     return info
 
 
+def _upload(a: np.ndarray, device: torch.device) -> torch.Tensor:
+    """Host array -> device tensor on the current stream, staged through
+    pinned memory so the copy is asynchronous (a pageable source can make the
+    call wait for the stream; torch's pinned-buffer cache keeps the staging
+    buffer until the copy has run)."""
+    h = torch.from_numpy(a)
+    if torch.device(device).type == "cuda":
+        h = h.pin_memory()
+    return h.to(device, non_blocking=True)
+
+
 class TreeAttnMeta:
     """Per-key visible-row intervals of one attention call plus the tile work
     lists and device copies the kernels need (cached per device and tile
@@ -189,6 +200,7 @@ class TreeAttnMeta:
         self.n_kv = int(self.kv_lo.shape[0])
         self._dev: Dict[object, object] = {}
         self._tiles: Dict[Tuple[int, int], dict] = {}
+        self.prefetched = False     # device copies made on a caller's upload stream
 
     def tiles(self, tile_q: int, tile_kv: int) -> dict:
         key = (tile_q, tile_kv)
@@ -216,7 +228,8 @@ class TreeAttnMeta:
         return self.tiles(128, 128)["visible_pairs"]
 
     def device(self, device: torch.device, tile_q: int, tile_kv: int) -> dict:
-        """Device tensors for one tile shape (copied once, then cached)."""
+        """Device tensors for one tile shape (copied once, on the current
+        stream, then cached)."""
         key = (device, tile_q, tile_kv)
         d = self._dev.get(key)
         if d is None:
@@ -228,12 +241,12 @@ class TreeAttnMeta:
                 lohi = np.zeros((2, self.n_kv + pad), np.int32)
                 lohi[0, : self.n_kv] = self.kv_lo
                 lohi[1, : self.n_kv] = self.kv_hi
-                g = torch.from_numpy(lohi).to(device, non_blocking=True)
+                g = _upload(lohi, device)
                 iv = (g[0], g[1])
                 self._dev[ivk] = iv
             t = self.tiles(tile_q, tile_kv)
             cat = np.concatenate([t["fwd_ptr"], t["fwd_list"], t["bwd_ptr"], t["bwd_list"]])
-            g = torch.from_numpy(cat).to(device, non_blocking=True)
+            g = _upload(cat, device)
             o1 = t["fwd_ptr"].size
             o2 = o1 + t["fwd_list"].size
             o3 = o2 + t["bwd_ptr"].size
