@@ -320,6 +320,23 @@ int tt_qk_norm_rope_bwd(int dtype, int64_t n_tok, int32_t H, int32_t D, const vo
                         const void* dy, void* dx, float* dw_part, int32_t blocks, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Fused gated RMSNorm of the GDN output: y = x * rsqrt(mean(x^2) + eps) * w *
+ * silu(z) over rows of D values, replacing the layer's gated norm on the tree
+ * GDN output (dfs_tree_forward.py:420-433; transformers models/qwen3_5_moe/
+ * modeling_qwen3_5_moe.py Qwen3_5MoeRMSNormGated).  x, z, y, dy, dx, dz:
+ * [rows, D] contiguous in `dtype`; weight [D] fp32; D in {32, 64, 128, 256}.
+ * The backward recomputes the norm and writes per-block weight-gradient partials
+ * dw_part [blocks, D] fp32 (sum the rows for dw); blocks from
+ * tt_gated_rmsnorm_bwd_blocks(rows).
+ */
+int tt_gated_rmsnorm_fwd(int dtype, int64_t rows, int32_t D, const void* x, const void* z,
+                         const float* weight, float eps, void* y, void* stream);
+int tt_gated_rmsnorm_bwd_blocks(int64_t rows);
+int tt_gated_rmsnorm_bwd(int dtype, int64_t rows, int32_t D, const void* x, const void* z,
+                         const float* weight, float eps, const void* dy, void* dx, void* dz,
+                         float* dw_part, int32_t blocks, void* stream);
+
+/* ------------------------------------------------------------------------
  * Tree-correct depthwise causal conv + SiLU.  Replaces _tree_correct_conv_varlen
  * (tree_dfs_ssm.py:285-348; dfs_tree_forward.py:191-246): each token's window
  * is the K-1 tokens before it on its root-to-node path (the reference's saved

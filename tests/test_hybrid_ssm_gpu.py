@@ -30,6 +30,8 @@ import tree_training_b200 as tt
 from tree_training_b200.hybrid import (make_tree_loss_fn, partition_tree,
                                        tree_grad_ckpt_sequential, tree_grad_hybrid)
 
+from tree_training_b200.gated_norm import fusable
+
 pytestmark = pytest.mark.gpu
 
 DEV = torch.device("cuda", 0)
@@ -65,6 +67,7 @@ def _model():
         la.causal_conv1d_update = M.torch_causal_conv1d_update
         if not isinstance(la.norm, M.Qwen3_5MoeRMSNormGated):
             la.norm = M.Qwen3_5MoeRMSNormGated(la.head_v_dim, eps=la.layer_norm_epsilon).to(DEV)
+        assert fusable(la.norm)     # the tree path runs the fused gated-norm kernels
     m.train()
     return m
 

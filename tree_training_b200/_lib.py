@@ -75,6 +75,10 @@ SIGNATURES = {
     "tt_qk_norm_rope_bwd_blocks": (_INT, [_I64]),
     "tt_qk_norm_rope_bwd": (_INT, [_INT, _I64, _I32, _I32, _P, _P, _P, _P, _F32, _P, _P, _P,
                                    _I32, _P]),
+    "tt_gated_rmsnorm_fwd": (_INT, [_INT, _I64, _I32, _P, _P, _P, _F32, _P, _P]),
+    "tt_gated_rmsnorm_bwd_blocks": (_INT, [_I64]),
+    "tt_gated_rmsnorm_bwd": (_INT, [_INT, _I64, _I32, _P, _P, _P, _F32, _P, _P, _P, _P, _I32,
+                                    _P]),
     "tt_conv_predecessors": (_INT, [_I32, _P, _P, _I32, _P]),
     "tt_conv_successors": (_INT, [_I32, _I32, _P, _P, _P, _P, _I64]),
     "tt_tree_conv_fwd": (_INT, [_INT, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),

@@ -8,7 +8,9 @@ tree_grad_hybrid.py (lines 232-250, 325-362).  Per linear-attention layer and
 partition:
 
 * the token projections, gated RMSNorm and output projection are per token,
-  so they run once over the whole DFS sequence;
+  so they run once over the whole DFS sequence (the gated RMSNorm as one fused
+  kernel each way, ``gated_norm.gated_rmsnorm``, for transformers' torch
+  ``*RMSNormGated`` modules);
 * the depthwise conv reads each token's K-1 predecessors on its
   root-to-node path (``gdn.tree_conv``); the partition's root chunks continue
   the gateway's conv context (the last K-1 pre-conv inputs on the path to the
@@ -30,6 +32,7 @@ from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 import torch
 import torch.nn.functional as F
 
+from .gated_norm import fusable, gated_rmsnorm
 from .gdn import (GDN_EXACT_INVERSE, GDN_QK_L2NORM, _gdn_fwd_op, _tree_arrays, tree_conv)
 
 
@@ -150,12 +153,14 @@ class SSMPartitionState:
 
     def __init__(self, chunk_boundaries, chunk_parent_map,
                  inject: Optional[Dict[int, Tuple[torch.Tensor, torch.Tensor]]] = None,
-                 capture_at: Sequence[int] = (), exact_inverse: bool = False):
+                 capture_at: Sequence[int] = (), exact_inverse: bool = False,
+                 fused_norm: bool = True):
         self.bounds = [tuple(int(x) for x in b) for b in chunk_boundaries]
         self.parents = [int(p) for p in chunk_parent_map]
         self.inject = inject or {}
         self.capture_at = sorted(set(int(c) for c in capture_at))
         self.exact_inverse = exact_inverse
+        self.fused_norm = fused_norm      # gated RMSNorm by tt_gated_rmsnorm_fwd/bwd
         self.rec: Dict[int, Dict[int, torch.Tensor]] = {}    # layer -> {chunk: state}
         self.conv: Dict[int, Dict[int, torch.Tensor]] = {}   # layer -> {chunk: context}
 
@@ -185,7 +190,11 @@ def tree_ssm_forward(layer, hidden_states: torch.Tensor, st: SSMPartitionState) 
     if st.capture_at:
         st.rec[li] = rec_cap
         st.conv[li] = conv_cap
-    core = layer.norm(core.reshape(-1, layer.head_v_dim), z.reshape(-1, layer.head_v_dim))
+    core2, z2 = core.reshape(-1, layer.head_v_dim), z.reshape(-1, layer.head_v_dim)
+    if st.fused_norm and fusable(layer.norm) and core2.dtype == z2.dtype:
+        core = gated_rmsnorm(core2, z2, layer.norm.weight, layer.norm.variance_epsilon)
+    else:
+        core = layer.norm(core2, z2)
     return layer.out_proj(core.reshape(B, S, -1))
 
 
