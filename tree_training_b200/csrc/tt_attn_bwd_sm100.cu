@@ -799,28 +799,50 @@ __global__ void order_tiles_by_work(int n_tiles, const int32_t* __restrict__ ptr
   order[rank] = i;
 }
 
-// delta[h, i] = sum_d O[i,h,d] dO[i,h,d] over the padded [hq, ld] layout
-// (one warp per (row, head), 4 dims per lane).
+// delta[h, i] = sum_d O[i,h,d] dO[i,h,d] over the padded [hq, ld] layout.
+// Half a warp per (row, head) pair, 8 dims (16 bytes) per lane, and each warp
+// issues the loads of its kDeltaPairs pairs before any arithmetic, so enough
+// bytes are in flight to stream O and dO at HBM rate.  Rows i >= n_q write 0.
+constexpr int kDeltaPairs = 4;
+
 template <typename T>
 __global__ void attn_bwd_delta_tc(int n_q, int hq, const T* __restrict__ out,
                                   const T* __restrict__ dout, int64_t do_st, int64_t do_sh,
                                   float* __restrict__ delta) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  constexpr int kPass = kDeltaPairs / 2;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31, l16 = lane & 15;
   const int ld = lse_ld(n_q);
-  if (w >= ld * hq) return;
-  const int i = w / hq, h = w % hq;
-  float acc = 0.f;
-  if (i < n_q) {
-    const uint2 a = *reinterpret_cast<const uint2*>(out + (static_cast<int64_t>(i) * hq + h) * kD + lane * 4);
-    const uint2 b = *reinterpret_cast<const uint2*>(dout + i * do_st + h * do_sh + lane * 4);
-    const T* pa = reinterpret_cast<const T*>(&a);
-    const T* pb = reinterpret_cast<const T*>(&b);
+  const int64_t total = static_cast<int64_t>(ld) * hq;
+  uint4 a[kPass], b[kPass];
+  int64_t pair[kPass];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) acc = fmaf(to_f32(pa[u]), to_f32(pb[u]), acc);
+  for (int k = 0; k < kPass; ++k) {
+    pair[k] = warp * kDeltaPairs + 2 * k + (lane >> 4);
+    a[k] = b[k] = make_uint4(0u, 0u, 0u, 0u);
+    if (pair[k] < total) {
+      const int i = static_cast<int>(pair[k] / hq), h = static_cast<int>(pair[k] % hq);
+      if (i < n_q) {
+        a[k] = *reinterpret_cast<const uint4*>(out + (static_cast<int64_t>(i) * hq + h) * kD +
+                                               l16 * 8);
+        b[k] = *reinterpret_cast<const uint4*>(dout + i * do_st + h * do_sh + l16 * 8);
+      }
+    }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) delta[static_cast<int64_t>(h) * ld + i] = acc;
+  for (int k = 0; k < kPass; ++k) {
+    const T* pa = reinterpret_cast<const T*>(&a[k]);
+    const T* pb = reinterpret_cast<const T*>(&b[k]);
+    float acc = 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = fmaf(to_f32(pa[u]), to_f32(pb[u]), acc);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (l16 == 0 && pair[k] < total) {
+      const int i = static_cast<int>(pair[k] / hq), h = static_cast<int>(pair[k] % hq);
+      delta[static_cast<int64_t>(h) * ld + i] = acc;
+    }
+  }
 }
 
 // ---- host side ---------------------------------------------------------------
@@ -893,7 +915,7 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
   using namespace tt::sm100;
   if (D != kD || (dtype != TT_BF16 && dtype != TT_F16)) return TT_ERR_UNSUPPORTED;
   if (!aligned16(kv_lo) || !aligned16(kv_hi) || !aligned16(lse) || !aligned16(delta) ||
-      !aligned16(out) || !aligned16(dq) || !aligned16(dk) || !aligned16(dv) ||
+      !aligned16(out) || !aligned16(dout) || !aligned16(dq) || !aligned16(dk) || !aligned16(dv) ||
       (dq_st * 2) % 16 || (dq_sh * 2) % 16 || (dk_st * 2) % 16 || (dk_sh * 2) % 16 ||
       (dv_st * 2) % 16 || (dv_sh * 2) % 16 || (do_st * 2) % 16 || (do_sh * 2) % 16)
     return TT_ERR_UNSUPPORTED;
@@ -908,14 +930,15 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
     return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
   }
   const int ld = tt::lse_ld(n_q);
-  const int warps = ld * hq;
+  const int64_t warps = (static_cast<int64_t>(ld) * hq + kDeltaPairs - 1) / kDeltaPairs;
   int launches = 0;
   if (warps > 0 && (phases & TT_BWD_PREP)) {
+    const unsigned blocks = static_cast<unsigned>((warps + 7) / 8);
     if (bf16)
-      attn_bwd_delta_tc<__nv_bfloat16><<<(warps + 7) / 8, 256, 0, st>>>(
+      attn_bwd_delta_tc<__nv_bfloat16><<<blocks, 256, 0, st>>>(
           n_q, hq, (const __nv_bfloat16*)out, (const __nv_bfloat16*)dout, do_st, do_sh, delta);
     else
-      attn_bwd_delta_tc<__half><<<(warps + 7) / 8, 256, 0, st>>>(
+      attn_bwd_delta_tc<__half><<<blocks, 256, 0, st>>>(
           n_q, hq, (const __half*)out, (const __half*)dout, do_st, do_sh, delta);
     ++launches;
   }
