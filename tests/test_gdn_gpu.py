@@ -253,22 +253,30 @@ def test_tree_conv_matches_reference_fixture(name):
     assert rel(f(ssm.conv1d.weight.grad)[:, 0], d["dweight"]) < 1e-5
 
 
-def test_tree_conv_random_tree_with_bias_vs_oracle():
+@pytest.mark.parametrize("C,K,dtype,tol", [(64, 4, torch.float32, 1e-5),
+                                            (13, 2, torch.float32, 1e-5),
+                                            (21, 3, torch.float32, 1e-5),
+                                            (9, 8, torch.float32, 1e-5),
+                                            (40, 4, torch.bfloat16, 2e-2)])
+def test_tree_conv_random_tree_with_bias_vs_oracle(C, K, dtype, tol):
+    """Channel counts off the kernels' 8-channel blocks, every window length
+    class, and bf16 (inputs rounded to bf16 for the float64 oracle too)."""
     info = tt.build_dfs_tree_info(random_branching_tree(9, 3000, 1, 40))
-    g_ = np.random.default_rng(9)
-    C, K = 64, 4
+    g_ = np.random.default_rng(9 + C + K)
     x = g_.standard_normal((2, C, info.N))
     w = g_.standard_normal((C, K)) * 0.5
     b = g_.standard_normal(C) * 0.1
     dy = g_.standard_normal((2, C, info.N))
+    if dtype == torch.bfloat16:
+        x, dy = (torch.tensor(a).to(dtype).double().numpy() for a in (x, dy))
     ssm = _Conv(w, b)
-    xt = torch.tensor(x, dtype=torch.float32, device=DEV, requires_grad=True)
+    xt = torch.tensor(x, dtype=dtype, device=DEV, requires_grad=True)
     y = _tree_correct_conv_varlen(ssm, xt, info.chunk_boundaries, info.chunk_parent_map)
-    y.backward(torch.tensor(dy, dtype=torch.float32, device=DEV))
+    y.backward(torch.tensor(dy, dtype=dtype, device=DEV))
     ref_y, _ = O.tree_conv_fwd(x, w, info.chunk_boundaries, info.chunk_parent_map, b)
     dx, dw, db = O.tree_conv_bwd(x, w, info.chunk_boundaries, info.chunk_parent_map, dy, b)
     f = lambda t: t.detach().double().cpu().numpy()
-    assert rel(f(y), ref_y) < 1e-5
-    assert rel(f(xt.grad), dx) < 1e-5
-    assert rel(f(ssm.conv1d.weight.grad)[:, 0], dw) < 1e-5
-    assert rel(f(ssm.conv1d.bias.grad), db) < 1e-5
+    assert rel(f(y), ref_y) < tol
+    assert rel(f(xt.grad), dx) < tol
+    assert rel(f(ssm.conv1d.weight.grad)[:, 0], dw) < tol
+    assert rel(f(ssm.conv1d.bias.grad), db) < tol

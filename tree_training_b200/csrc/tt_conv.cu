@@ -8,6 +8,7 @@
 // host turns the tree into pred[t][m-1] (token m steps back, or -1) once;
 // the kernels are then plain gathers, and the backward gathers over the
 // inverse map (successor CSR) so dx needs no atomics.
+#include <type_traits>
 #include <vector>
 
 #include "tt_common.cuh"
@@ -69,78 +70,104 @@ extern "C" int tt_conv_successors(int32_t S, int32_t K, const int32_t* pred, int
 namespace tt {
 namespace {
 
-// pre[c][t] = bias + sum_{m=0}^{K-1} w[c][K-1-m] x[c][pred_m(t)]   (pred_0 = t)
-template <typename T>
-__device__ __forceinline__ float conv_pre(const T* __restrict__ xc, const float* __restrict__ wc,
-                                          float b, const int32_t* __restrict__ pr, int t, int K) {
-  float acc = b + wc[K - 1] * to_f32(xc[t]);
-  for (int m = 1; m < K; ++m) {
-    const int p = pr[(int64_t)t * (K - 1) + m - 1];
-    if (p >= 0) acc = fmaf(wc[K - 1 - m], to_f32(xc[p]), acc);
-  }
-  return acc;
-}
-
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
-
-template <typename T>
-__global__ void conv_fwd(int C, int S, int K, const T* __restrict__ x, const float* __restrict__ w,
-                         const float* __restrict__ bias, const int32_t* __restrict__ pred, T* out) {
-  const int c = blockIdx.y;
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= S) return;
-  const float pre = conv_pre(x + (int64_t)c * S, w + (int64_t)c * K, bias ? bias[c] : 0.f, pred, t, K);
-  out[(int64_t)c * S + t] = from_f32<T>(silu(pre));
-}
 
 constexpr int kConvTok = 256;   // tokens per block (one per thread)
 constexpr int kConvCh = 8;      // channels per thread: the token's predecessor and
                                 // successor indices are read once for all of them
 constexpr int kPartW = 9;       // per (channel, block): dw[0..K-1], db at [8]
+constexpr int kSuccAhead = 8;   // successors whose indices conv_bwd_dx fetches up front
+
+// The window of token t in channel c: xs[m] = x[c][pred_m(t)] for m < K
+// (pred_0 = t, 0 where the path is shorter).  Every channel's loads are issued
+// before any arithmetic, so a thread keeps kConvCh * K gathers in flight; rows
+// past C read row C - 1 and are never used.
+template <typename T, int K>
+__device__ __forceinline__ void load_windows(const T* __restrict__ x, int C, int S, int c0, int t,
+                                             bool live, const int (&pr)[K > 1 ? K - 1 : 1],
+                                             float (&xs)[kConvCh][K]) {
+#pragma unroll
+  for (int cc = 0; cc < kConvCh; ++cc) {
+    const T* xc = x + (int64_t)min(c0 + cc, C - 1) * S;
+    xs[cc][0] = live ? to_f32(xc[t]) : 0.f;
+#pragma unroll
+    for (int m = 1; m < K; ++m) xs[cc][m] = (live && pr[m - 1] >= 0) ? to_f32(xc[pr[m - 1]]) : 0.f;
+  }
+}
+
+template <int K>
+__device__ __forceinline__ void load_pred(const int32_t* __restrict__ pred, int t, bool live,
+                                          int (&pr)[K > 1 ? K - 1 : 1]) {
+  pr[0] = -1;
+#pragma unroll
+  for (int m = 0; m < K - 1; ++m) pr[m] = live ? pred[(int64_t)t * (K - 1) + m] : -1;
+}
+
+// pre[c][t] = bias + sum_{m=0}^{K-1} w[c][K-1-m] x[c][pred_m(t)],  out = silu(pre)
+template <typename T, int K>
+__global__ void __launch_bounds__(kConvTok)
+conv_fwd(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
+         const float* __restrict__ bias, const int32_t* __restrict__ pred, T* __restrict__ out) {
+  const int t = blockIdx.x * kConvTok + threadIdx.x;
+  const int c0 = blockIdx.y * kConvCh;
+  if (t >= S) return;
+  int pr[K > 1 ? K - 1 : 1];
+  load_pred<K>(pred, t, true, pr);
+  float xs[kConvCh][K];
+  load_windows<T, K>(x, C, S, c0, t, true, pr, xs);
+#pragma unroll
+  for (int cc = 0; cc < kConvCh; ++cc) {
+    const int c = c0 + cc;
+    if (c >= C) break;
+    const float* wc = w + (int64_t)c * K;
+    float pre = bias ? bias[c] : 0.f;
+#pragma unroll
+    for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[cc][m], pre);
+    out[(int64_t)c * S + t] = from_f32<T>(silu(pre));
+  }
+}
 
 // dpre[c][t] = dy * d silu(pre)/d pre at every (channel, token), and per block
 // of 256 tokens the partial sums of dw[c][j] = sum_t dpre x[pred_{K-1-j}(t)]
 // and db[c] = sum_t dpre (reduced in a fixed order by conv_bwd_dw_reduce).
-template <typename T>
+template <typename T, int K>
 __global__ void __launch_bounds__(kConvTok)
-conv_bwd_dpre(int C, int S, int K, const T* __restrict__ x, const float* __restrict__ w,
+conv_bwd_dpre(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
               const float* __restrict__ bias, const int32_t* __restrict__ pred,
               const T* __restrict__ dy, float* __restrict__ dpre, float* __restrict__ part,
               int nb) {
   const int t = blockIdx.x * kConvTok + threadIdx.x;
   const int c0 = blockIdx.y * kConvCh;
   const bool live = t < S;
-  int pr[7];
+  int pr[K > 1 ? K - 1 : 1];
+  load_pred<K>(pred, t, live, pr);
+  float xs[kConvCh][K], g[kConvCh];
+  load_windows<T, K>(x, C, S, c0, t, live, pr, xs);
 #pragma unroll
-  for (int m = 0; m < 7; ++m)
-    pr[m] = (live && m < K - 1) ? pred[(int64_t)t * (K - 1) + m] : -1;
+  for (int cc = 0; cc < kConvCh; ++cc)
+    g[cc] = live ? to_f32(dy[(int64_t)min(c0 + cc, C - 1) * S + t]) : 0.f;
   __shared__ float red[kConvCh][kPartW][kConvTok / 32];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
   for (int cc = 0; cc < kConvCh; ++cc) {
     const int c = c0 + cc;
     if (c >= C) break;                       // the same for the whole block
-    const T* xc = x + (int64_t)c * S;
     const float* wc = w + (int64_t)c * K;
-    float xs[8], d = 0.f;
+    float pre = bias ? bias[c] : 0.f;
 #pragma unroll
-    for (int m = 0; m < 8; ++m) xs[m] = 0.f;
-    if (live) {
-      xs[0] = to_f32(xc[t]);
-      float pre = (bias ? bias[c] : 0.f) + wc[K - 1] * xs[0];
-#pragma unroll
-      for (int m = 1; m < 8; ++m)
-        if (m < K && pr[m - 1] >= 0) {
-          xs[m] = to_f32(xc[pr[m - 1]]);
-          pre = fmaf(wc[K - 1 - m], xs[m], pre);
-        }
-      const float sg = 1.f / (1.f + __expf(-pre));
-      d = to_f32(dy[(int64_t)c * S + t]) * sg * (1.f + pre * (1.f - sg));
-      dpre[(int64_t)c * S + t] = d;
-    }
+    for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[cc][m], pre);
+    const float sg = 1.f / (1.f + __expf(-pre));
+    const float d = live ? g[cc] * sg * (1.f + pre * (1.f - sg)) : 0.f;
+    if (live) dpre[(int64_t)c * S + t] = d;
 #pragma unroll
     for (int j = 0; j < kPartW; ++j) {
-      // j < K: weight index j, i.e. predecessor m = K-1-j; j = 8: bias
-      float v = j == 8 ? d : (j < K ? d * xs[K - 1 - j] : 0.f);
+      // j < K: weight index j, i.e. predecessor m = K-1-j; j = 8: bias; the
+      // slots K..7 are never read and hold 0
+      if (j >= K && j != 8) {
+        if (lane == 0) red[cc][j][wid] = 0.f;
+        continue;
+      }
+      float v = j == 8 ? d : d * xs[cc][j < K ? K - 1 - j : 0];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       if (lane == 0) red[cc][j][wid] = v;
@@ -172,30 +199,68 @@ __global__ void conv_bwd_dw_reduce(int C, int K, int nb, const float* __restrict
 
 // dx[c][t] = w[c][K-1] dpre[c][t] + sum over the tokens u that have t as their
 // lag-l predecessor of w[c][K-1-l] dpre[c][u]  (successor CSR, fixed order).
-template <typename T>
+// The first kSuccAhead successors' indices are fetched together, then all
+// their dpre loads; longer lists (the last tokens of a node with many
+// children) continue one successor at a time.
+template <typename T, int K>
 __global__ void __launch_bounds__(kConvTok)
-conv_bwd_dx(int C, int S, int K, const float* __restrict__ w, const float* __restrict__ dpre,
+conv_bwd_dx(int C, int S, const float* __restrict__ w, const float* __restrict__ dpre,
             const int32_t* __restrict__ sp, const int32_t* __restrict__ stok,
             const int32_t* __restrict__ slag, T* __restrict__ dx) {
   const int t = blockIdx.x * kConvTok + threadIdx.x;
   if (t >= S) return;
   const int c0 = blockIdx.y * kConvCh;
   const int n_ch = min(kConvCh, C - c0);
+  const int e0 = sp[t], e1 = sp[t + 1];
+  int us[kSuccAhead], ls[kSuccAhead];
+#pragma unroll
+  for (int i = 0; i < kSuccAhead; ++i) {
+    const bool has = e0 + i < e1;
+    us[i] = has ? stok[e0 + i] : -1;
+    ls[i] = has ? slag[e0 + i] : 0;
+  }
   float acc[kConvCh];
 #pragma unroll
-  for (int cc = 0; cc < kConvCh; ++cc)
-    acc[cc] = cc < n_ch ? w[(int64_t)(c0 + cc) * K + K - 1] * dpre[(int64_t)(c0 + cc) * S + t] : 0.f;
-  for (int e = sp[t]; e < sp[t + 1]; ++e) {
+  for (int cc = 0; cc < kConvCh; ++cc) {
+    const int64_t c = min(c0 + cc, C - 1);
+    acc[cc] = w[c * K + K - 1] * dpre[c * S + t];
+  }
+#pragma unroll
+  for (int i = 0; i < kSuccAhead; ++i) {
+    if (us[i] < 0) break;
+#pragma unroll
+    for (int cc = 0; cc < kConvCh; ++cc) {
+      const int64_t c = min(c0 + cc, C - 1);
+      acc[cc] = fmaf(w[c * K + K - 1 - ls[i]], dpre[c * S + us[i]], acc[cc]);
+    }
+  }
+  for (int e = e0 + kSuccAhead; e < e1; ++e) {
     const int u = stok[e], l = slag[e];
 #pragma unroll
-    for (int cc = 0; cc < kConvCh; ++cc)
-      if (cc < n_ch)
-        acc[cc] = fmaf(w[(int64_t)(c0 + cc) * K + K - 1 - l], dpre[(int64_t)(c0 + cc) * S + u],
-                       acc[cc]);
+    for (int cc = 0; cc < kConvCh; ++cc) {
+      const int64_t c = min(c0 + cc, C - 1);
+      acc[cc] = fmaf(w[c * K + K - 1 - l], dpre[c * S + u], acc[cc]);
+    }
   }
 #pragma unroll
   for (int cc = 0; cc < kConvCh; ++cc)
     if (cc < n_ch) dx[(int64_t)(c0 + cc) * S + t] = from_f32<T>(acc[cc]);
+}
+
+// f(std::integral_constant<int, K>()) for the runtime window length K in 1..8
+template <typename Fn>
+int by_k(int K, Fn fn) {
+  switch (K) {
+    case 1: return fn(std::integral_constant<int, 1>());
+    case 2: return fn(std::integral_constant<int, 2>());
+    case 3: return fn(std::integral_constant<int, 3>());
+    case 4: return fn(std::integral_constant<int, 4>());
+    case 5: return fn(std::integral_constant<int, 5>());
+    case 6: return fn(std::integral_constant<int, 6>());
+    case 7: return fn(std::integral_constant<int, 7>());
+    case 8: return fn(std::integral_constant<int, 8>());
+    default: return TT_ERR_INVALID_ARG;
+  }
 }
 
 template <typename Fn>
@@ -219,11 +284,14 @@ extern "C" int tt_tree_conv_fwd(int dtype, int32_t C, int32_t S, int32_t K, cons
   if (!x || !weight || !out || (K > 1 && !pred)) return TT_ERR_INVALID_ARG;
   return tt::by_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
-    dim3 g((S + 255) / 256, C);
-    tt::conv_fwd<T><<<g, 256, 0, (cudaStream_t)stream>>>(C, S, K, (const T*)x, weight, bias, pred,
-                                                          (T*)out);
-    tt_count_launches(1);
-    return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
+    return tt::by_k(K, [&](auto kc) {
+      constexpr int KK = decltype(kc)::value;
+      dim3 g((S + tt::kConvTok - 1) / tt::kConvTok, (C + tt::kConvCh - 1) / tt::kConvCh);
+      tt::conv_fwd<T, KK><<<g, tt::kConvTok, 0, (cudaStream_t)stream>>>(
+          C, S, (const T*)x, weight, bias, pred, (T*)out);
+      tt_count_launches(1);
+      return cudaGetLastError() == cudaSuccess ? (int)TT_OK : (int)TT_ERR_CUDA;
+    });
   });
 }
 
@@ -252,13 +320,16 @@ extern "C" int tt_tree_conv_bwd(int dtype, int32_t C, int32_t S, int32_t K, cons
     float* dpre = static_cast<float*>(workspace);
     float* part = dpre + (int64_t)C * S;
     dim3 g(nb, (C + tt::kConvCh - 1) / tt::kConvCh);
-    tt::conv_bwd_dpre<T><<<g, tt::kConvTok, 0, st>>>(C, S, K, (const T*)x, weight, bias, pred,
-                                                      (const T*)dout, dpre, part, nb);
-    tt::conv_bwd_dw_reduce<<<(C * tt::kPartW + 255) / 256, 256, 0, st>>>(C, K, nb, part, dweight,
-                                                                       dbias);
-    tt::conv_bwd_dx<T><<<g, tt::kConvTok, 0, st>>>(C, S, K, weight, dpre, succ_ptr, succ_tok,
-                                                    succ_lag, (T*)dx);
-    tt_count_launches(3);
-    return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
+    return tt::by_k(K, [&](auto kc) {
+      constexpr int KK = decltype(kc)::value;
+      tt::conv_bwd_dpre<T, KK><<<g, tt::kConvTok, 0, st>>>(C, S, (const T*)x, weight, bias, pred,
+                                                           (const T*)dout, dpre, part, nb);
+      tt::conv_bwd_dw_reduce<<<(C * tt::kPartW + 255) / 256, 256, 0, st>>>(C, K, nb, part,
+                                                                         dweight, dbias);
+      tt::conv_bwd_dx<T, KK><<<g, tt::kConvTok, 0, st>>>(C, S, weight, dpre, succ_ptr, succ_tok,
+                                                         succ_lag, (T*)dx);
+      tt_count_launches(3);
+      return cudaGetLastError() == cudaSuccess ? (int)TT_OK : (int)TT_ERR_CUDA;
+    });
   });
 }
