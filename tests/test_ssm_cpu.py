@@ -5,6 +5,7 @@ conv_states[c] = last K-1 of (parent context ++ chunk), zero padded at
 roots), including through an injected gateway context."""
 import numpy as np
 import pytest
+import torch
 
 from tree_training_b200.ssm import _path_tail
 
@@ -57,3 +58,20 @@ def test_path_tail_continues_into_injected_context():
         got = _path_tail(ext_bounds, ext_parents, c + 1, K - 1)
         got = [init[t] if t < off else t - off for t in got]
         assert got == ref[c], c
+
+
+def test_fused_gated_norm_selection():
+    """The hybrid layers run the fused gated-RMSNorm kernels only for
+    transformers' torch gated norms of a supported width; anything else keeps
+    its own forward, and the fused op itself refuses CPU tensors."""
+    from transformers.models.qwen3_5_moe.modeling_qwen3_5_moe import Qwen3_5MoeRMSNormGated
+
+    from tree_training_b200.gated_norm import fusable, gated_rmsnorm
+    for d in (32, 64, 128, 256):
+        assert fusable(Qwen3_5MoeRMSNormGated(d))
+    assert not fusable(Qwen3_5MoeRMSNormGated(48))
+    assert not fusable(torch.nn.LayerNorm(64))
+    assert not fusable(torch.nn.RMSNorm(64))
+    x = torch.randn(4, 64)
+    with pytest.raises(RuntimeError):
+        gated_rmsnorm(x, x, torch.ones(64), 1e-6)
