@@ -254,6 +254,21 @@ def cpu_baseline_sample(meta, V, hq=4, hkv=1):
                       f"the dense additive mask on {torch.get_num_threads()} threads"}
 
 
+def reference_packer_sample(roots, V, max_pairs: int = 1_000_000):
+    """The reference's build_dfs_tree_info (dfs_tree_forward.py:91-184) on the
+    same tree, on host cores: its element-by-element mask loop (:157-172) run
+    over the first ~1M visible pairs in DFS order and extrapolated to all V;
+    beside it, this package's packer (e2e.host_packer_ms_per_step)."""
+    from oracle import tree_oracle as O
+    from oracle.workloads import time_reference_mask_loop
+    info = O.build_dfs_tree_info(roots)
+    secs, pairs = time_reference_mask_loop(info, max_pairs)
+    return {"seconds_extrapolated": secs * V / pairs, "sample_pairs": pairs,
+            "sample_seconds": secs, "kind": "port", "cores": 1,
+            "sample": f"the reference packer's mask loop over the first {pairs} of {V} "
+                      "visible pairs, scaled by V / pairs"}
+
+
 def isolated_kernel_roofline(meta, q, k, v, do, dev, V, peak, reps: int = 5):
     """Each attention kernel timed ALONE (CUDA events, same inputs, after the
     timed region): in the product path dK/dV and dQ share the GPU on two
@@ -283,7 +298,9 @@ def isolated_kernel_roofline(meta, q, k, v, do, dev, V, peak, reps: int = 5):
             "attn_bwd_dkdv_tc": lambda: phase(_lib.TT_BWD_DKDV),
             "attn_bwd_dq_tc": lambda: phase(_lib.TT_BWD_DQ)}
     flops = {"attn_fwd_tc": 4.0 * D * V * HQ, "attn_bwd_dkdv_tc": 8.0 * D * V * HQ,
-             "attn_bwd_dq_tc": 6.0 * D * V * HQ}
+             "attn_bwd_dq_tc": 2.0 * D * V * HQ}       # useful: dQ's dS K only
+    executed = {"attn_fwd_tc": 4.0 * D * V * HQ, "attn_bwd_dkdv_tc": 8.0 * D * V * HQ,
+                "attn_bwd_dq_tc": 6.0 * D * V * HQ}
     res = {}
     for name, fn in runs.items():
         fn()
@@ -297,7 +314,8 @@ def isolated_kernel_roofline(meta, q, k, v, do, dev, V, peak, reps: int = 5):
         b.synchronize()
         t = a.elapsed_time(b) / 1e3 / reps
         ach = flops[name] / t / 1e12
-        res[name] = {"ms": t * 1e3, "achieved": ach, "frac": ach / peak}
+        res[name] = {"ms": t * 1e3, "achieved": ach, "frac": ach / peak,
+                     "executed_frac": executed[name] / t / 1e12 / peak}
     return res
 
 
@@ -365,20 +383,25 @@ def run_reference(args):
     every k-th query row of the tree, k chosen so the whole --steps/--warmup run
     takes about two minutes.  Query rows are independent, so the sample is an
     exact slice of the full computation; its useful FLOPs are 14 * D * (visible
-    pairs of the sampled rows) * 4."""
+    pairs of the sampled rows) * 4.  The tree and its mask come from oracle/
+    (the same tree as the product arm's, checked by
+    tests/test_oracle_workloads_cpu.py), so this process never loads this
+    repository's compiled library."""
     world, rank, local = dist_env()
     if rank != 0:
         return 0
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    _, info, meta, V = workload(0, args.seed, args.tokens)
-    from oracle.ref_cpu import sample_rows, time_sample, visible_pairs
+    from oracle.ref_cpu import sample_rows, time_sample
+    from oracle.workloads import OracleAttnMeta, bfs_tree
+    meta = OracleAttnMeta(bfs_tree(args.seed, args.tokens, 64, 512, min(2048, args.tokens // 8)))
+    V = meta.visible_pairs
     steps, warm = max(1, args.steps), max(0, args.warmup)
     budget = max(0.5, 120.0 / (steps + warm + 1))       # seconds per step
     probe = sample_rows(meta.n_q, 16)
     t_probe = time_sample(meta, 4, 1, D, torch.bfloat16, rows=probe)   # also a warm-up
     stride = max(1, int(np.ceil(16 * t_probe / budget)))
     rows = sample_rows(meta.n_q, stride)
-    Vs = visible_pairs(meta, rows)
+    Vs = meta.visible_pairs_of_rows(rows)
     for _ in range(warm):
         time_sample(meta, 4, 1, D, torch.bfloat16, rows=rows)
     ts = [time_sample(meta, 4, 1, D, torch.bfloat16, rows=rows) for _ in range(steps)]
@@ -389,15 +412,20 @@ def run_reference(args):
               f"0, {stride}, {2 * stride}, ... ({len(rows)} of {meta.n_q}, {Vs} visible pairs) of the "
               f"config-2 tree against all keys, bf16, transformers sdpa_attention_forward with "
               f"the reference's dense additive mask, {torch.get_num_threads()} threads")
+    full_s = t * (V / Vs) * (HQ / 4)
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s",
             "n_gpus": args.gpus, "steps": steps, "warmup": warm,
             "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "tokens_per_s": len(rows) * (4 / HQ) / t,
+            "tokens_per_s": meta.n_q / full_s,
             "config": {"workload": "config2: one 16k-token DFS tree, 32/8 heads, D=128, "
                                    "tree attention fwd+bwd", "tokens": meta.n_q,
                        "visible_pairs": V, "sample_heads": "4 of 32",
-                       "sample_rows_stride": stride},
+                       "sample_rows_stride": stride, "sample_visible_pairs": Vs},
+            "extrapolated_full_step": {
+                "seconds": full_s, "tokens_per_s": meta.n_q / full_s,
+                "how": "sample seconds x (all visible pairs / sampled visible pairs) x "
+                       f"({HQ} / 4 heads): the full config-2 fwd+bwd on these host cores"},
             "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
                              "kind": "port", "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -586,23 +614,35 @@ def run_ours(args):
     for _ in range(n_copy):
         tt.build_dfs_tree_info(roots).attn_meta()
     t_pack = (time.perf_counter() - p0) / n_copy
+    # every rank's host<->device bytes per step over the slowest rank's e2e step:
+    # the host side all GPUs share
+    host_gbs_all = sum_over_ranks(float(h2d + d2h), world, dev) / t_e2e / 1e9
 
     pk, pk_src = peaks()
-    # algorithmic FLOPs of each kernel as designed (2*D per visible pair and GEMM):
-    # forward 2 GEMMs, dK/dV 4 (S^T, dP^T, dV, dK), dQ 3 (S, dP, dQ)
+    # USEFUL FLOPs (the metric's basis: fwd 4*D*V, bwd 10*D*V per head) by
+    # kernel: the forward's 2 GEMMs; dK/dV's 4 (S^T, dP^T, dV, dK) are the
+    # backward's recompute + dV + dK; dQ's one useful GEMM is dS K (it also
+    # re-executes S and dP, counted only under "executed" below)
     kflops = {"attn_fwd_tc": 4.0 * D * V * HQ, "attn_bwd_dkdv_tc": 8.0 * D * V * HQ,
-              "attn_bwd_dq_tc": 6.0 * D * V * HQ}
+              "attn_bwd_dq_tc": 2.0 * D * V * HQ}
+    kexec = {"attn_fwd_tc": 4.0 * D * V * HQ, "attn_bwd_dkdv_tc": 8.0 * D * V * HQ,
+             "attn_bwd_dq_tc": 6.0 * D * V * HQ}
     kern["attn_fwd_tc"] = t_fwd
     # dK/dV and dQ run concurrently on two streams, so the live unit of the
     # backward is the pair: both kernels' FLOPs over the span of the longer one
     # (each kernel alone is timed separately below, in roofline_isolated)
     pair = ("attn_bwd_dkdv_tc", "attn_bwd_dq_tc")
     t_pair = max(kern.get(n, 0.0) for n in pair)
+    pair_name = "attn_bwd_dkdv_tc + attn_bwd_dq_tc"
     units = {"attn_fwd_tc": (kflops["attn_fwd_tc"], t_fwd),
-             "attn_bwd_dkdv_tc + attn_bwd_dq_tc": (kflops[pair[0]] + kflops[pair[1]], t_pair)}
+             pair_name: (kflops[pair[0]] + kflops[pair[1]], t_pair)}
+    units_exec = {"attn_fwd_tc": kexec["attn_fwd_tc"],
+                  pair_name: kexec[pair[0]] + kexec[pair[1]]}
     dominant = max(units, key=lambda n: units[n][1])
     achieved = units[dominant][0] / units[dominant][1] / 1e12
+    achieved_exec = units_exec[dominant] / units[dominant][1] / 1e12
     peak = float(pk["bf16_tflops"])
+    peak_sus = float(pk.get("bf16_tflops_sustained", peak))
     traffic_tab = {}      # DRAM bytes per launch from the committed ncu summary
     tp = os.path.join(ROOT, "profiles", "tree_attn_config2_dram_traffic.txt")
     if os.path.exists(tp) and args.tokens == 16384:
@@ -640,13 +680,30 @@ def run_ours(args):
                                    "frac": t_copy / t_e2e,
                                    "note": "the same per-step pinned copies, both directions "
                                            "at once, no compute; frac = this / e2e step"},
+                    "host_copy_gbs_this_gpu": (h2d + d2h) / t_e2e / 1e9,
+                    "host_copy_gbs_all_gpus": host_gbs_all,
+                    "host_bound": bool(t_copy / t_e2e > 0.9),
                     "host_packer_ms_per_step": t_pack * 1e3},
             "kernel_ms": {n: t * 1e3 for n, t in kern.items()},
             "host_enqueue_ms_per_step": host_enqueue_ms,
             "roofline": {"bound": "tensor", "kernel": dominant,
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": f"{pk_src} bf16 dense (burst)"},
+                         "flops_basis": "useful (fwd 4*D*V, bwd 10*D*V per head): the "
+                                        "backward pair counts dK/dV's 8*D*V and dQ's 2*D*V",
+                         "traffic_source": ("constant: ncu dram__bytes_read.sum + "
+                                            "dram__bytes_write.sum of an 8k-token capture "
+                                            "scaled by visible pairs "
+                                            "(profiles/tree_attn_config2_dram_traffic.txt), "
+                                            "not measured in this run"),
+                         "peak_source": f"{pk_src} bf16 dense (burst)",
+                         "frac_of_sustained": achieved / peak_sus},
+            "roofline_executed": {"kernel": dominant, "achieved": achieved_exec,
+                                  "frac": achieved_exec / peak,
+                                  "note": "executed FLOPs over the same span: dQ's "
+                                          "re-executed S and dP included (14*D*V per head "
+                                          "for the pair)"},
+            "step_useful_frac": value / world / peak,
             "gpu_launches": int(launches),
             "clocks": clk,
         }
@@ -661,6 +718,7 @@ def run_ours(args):
                     "concurrently on two streams"}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample(meta, V)
+            line["e2e"]["reference_packer"] = reference_packer_sample(roots, V)
         if world == 1 and not args.no_reference_gpu:
             line["reference_gpu"] = reference_gpu_sample(meta, dev, V)
         print(json.dumps(line), flush=True)
@@ -688,6 +746,30 @@ def gdn_bytes_per_token():
     C = 2 * GDN_HK * GDN_D + GDN_H * GDN_D
     fwd = C * 2 * 2 + (2 * GDN_HK * GDN_D + GDN_H * GDN_D) * 2 + 2 * GDN_H * 4 + GDN_H * GDN_D * 2
     return 3 * fwd
+
+
+def gdn_cpu_baseline(info, min_tokens: int = 4096):
+    """The reference's hybrid-layer core on host cores (oracle/gdn_torch.py:
+    tree conv + tree GDN with the reference's row loop, fwd + autograd bwd,
+    all 16/32 heads), on the first nodes of the tree in DFS order up to
+    ``min_tokens`` tokens: a prefix of a pre-order is itself a valid tree, and
+    the node lengths are drawn independently, so its tokens/s stands for the
+    whole tree's."""
+    from oracle.gdn_torch import time_gdn_step_sample
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    n = 0
+    while n < info.n_chunks and info.chunk_boundaries[n][0] < min_tokens:
+        n += 1
+    bounds = info.chunk_boundaries[:n]
+    Sp = bounds[-1][1]
+    secs = time_gdn_step_sample(bounds, info.chunk_parent_map[:n], Sp, GDN_HK, GDN_H, GDN_D,
+                                GDN_K)
+    return {"value": Sp / secs, "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port", "seconds": secs,
+            "sample": f"first {n} nodes ({Sp} of {info.N} tokens) of the config-4 tree in DFS "
+                      f"order, all {GDN_HK}/{GDN_H} heads: tree conv + tree GDN (the "
+                      "reference's row loop) fwd + autograd bwd in fp32 torch, "
+                      f"{torch.get_num_threads()} threads"}
 
 
 def run_gdn(args):
@@ -751,6 +833,45 @@ def run_gdn(args):
     tokens_all = sum_over_ranks(float(S), world, dev)
     pk, pk_src = peaks()
     achieved = S * gdn_bytes_per_token() / t / 1e9
+
+    # ---- end to end through the public API from pinned host buffers: each
+    # step uploads the conv input, conv weight, g, beta and dO, runs conv + GDN
+    # fwd + bwd, and reads back dx, dw, dg and dbeta (one stream, no overlap)
+    pin = lambda x_: x_.detach().cpu().pin_memory()
+    h_in = [pin(x), pin(w), pin(gg), pin(bt), pin(do)]
+    h_out = [torch.empty_like(h).pin_memory() for h in h_in[:4]]
+    d_in = [torch.empty_like(h, device=dev) for h in h_in]
+
+    def e2e_step():
+        for dst, src in zip(d_in, h_in):
+            dst.copy_(src, non_blocking=True)
+        xs, ws, gs, bs = (t_.detach().requires_grad_(True) for t_ in d_in[:4])
+        y = tree_conv(xs, ws, None, bounds, parents)
+        yt = y.transpose(1, 2)
+        q = yt[..., :GDN_HK * GDN_D].reshape(1, S, GDN_HK, GDN_D)
+        k = yt[..., GDN_HK * GDN_D:2 * GDN_HK * GDN_D].reshape(1, S, GDN_HK, GDN_D)
+        v = yt[..., 2 * GDN_HK * GDN_D:].reshape(1, S, GDN_H, GDN_D)
+        out, _ = torch_chunk_gated_delta_rule_tree_varlen(q, k, v, gs, bs, bounds, parents,
+                                                          use_qk_l2norm_in_kernel=True,
+                                                          exact_inverse=args.gdn_exact,
+                                                          keep_forward=bool(args.gdn_keep))
+        out.backward(d_in[4])
+        for dst, src in zip(h_out, (xs, ws, gs, bs)):
+            dst.copy_(src.grad, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    n_e2e = max(1, min(args.steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record()
+    e1.synchronize()
+    t_e2e = max_over_ranks(e0.elapsed_time(e1) / 1e3 / n_e2e, world, dev)
+    h2d_b = sum(h.numel() * h.element_size() for h in h_in)
+    d2h_b = sum(h.numel() * h.element_size() for h in h_out)
     if rank == 0:
         line = {"metric": "Tree GDN (conv + gated delta rule) fwd+bwd tokens/s",
                 "value": tokens_all / t_max, "unit": "tokens/s", "n_gpus": world,
@@ -777,7 +898,13 @@ def run_gdn(args):
                 "seg_gemm": {"gflop_per_step": gemm_flops / 1e9,
                              "tflops_over_step": gemm_flops / t / 1e12,
                              "fp32_fma_peak_tflops": FP32_FMA_PEAK_TFLOPS},
-                "gpu_launches": int(launches), "clocks": clk}
+                "gpu_launches": int(launches), "clocks": clk,
+                "e2e": {"value": tokens_all / t_e2e, "unit": "tokens/s",
+                        "h2d_bytes_per_step": int(h2d_b), "d2h_bytes_per_step": int(d2h_b),
+                        "ms_per_step": t_e2e * 1e3,
+                        "schedule": "one stream: upload, conv + GDN fwd + bwd, download"}}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = gdn_cpu_baseline(info)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

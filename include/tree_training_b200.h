@@ -188,14 +188,18 @@ enum tt_bwd_phase { TT_BWD_PREP = 1, TT_BWD_DKDV = 2, TT_BWD_DQ = 4, TT_BWD_ALL 
  * workspace and phases; no counterpart in the reference).  For callers that
  * cannot pass a scratch buffer and must not have the library call cudaMalloc
  * (a binding that mirrors the reference's inputs-and-outputs call, or a
- * runtime whose device memory belongs to its own pooling allocator).  Scratch
- * lives in a fixed 8 MiB array inside the library's device image, held by
- * every GPU that loads the library until exit: problems with
- * hq * round_up(n_q, 128) > tt_tree_attn_bwd_noalloc_max_row_terms() are
- * rejected with TT_ERR_WORKSPACE before anything runs.  The first call on a
- * device looks the array up (make it before any stream capture; the device of
- * the pointers must be current); every call shares the array, so calls whose
- * kernels overlap on the GPU race.  Calls no allocating routine. */
+ * runtime whose device memory belongs to its own pooling allocator).  Its
+ * workspace (row terms and dK/dV tile order, as tt_tree_attn_bwd_workspace_size
+ * sizes it) lives in a fixed 8 MiB + 64 KiB array inside the library's device
+ * image, held by every GPU that loads the library until exit, so it runs the
+ * same kernels in the same tile order and gives bit-identical results.
+ * Problems with hq * round_up(n_q, 128) > tt_tree_attn_bwd_noalloc_max_row_terms()
+ * or n_kv > 2,097,152 keys are rejected with TT_ERR_WORKSPACE before anything
+ * runs.  The first call on a device looks the array up and caches its address
+ * for the process (make it before any stream capture; the device of the
+ * pointers must be current; not supported after a cudaDeviceReset); every
+ * call shares the array, so calls whose kernels overlap on the GPU race.
+ * Calls no allocating routine. */
 int tt_tree_attn_bwd_noalloc(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv,
                              int32_t head_dim, const void* q, int64_t q_st, int64_t q_sh,
                              const void* k, int64_t k_st, int64_t k_sh, const void* v,
