@@ -64,6 +64,45 @@ int64_t tt_kernel_launches(void);
  * GEMM work, excluding the padding of partial 64 x 64 tiles. */
 int64_t tt_gdn_gemm_flops(void);
 
+/* The part of tt_gdn_gemm_flops that ran on the tensor cores (tcgen05.mma
+ * kind::tf32). */
+int64_t tt_gdn_gemm_tc_flops(void);
+
+/* Selects the tree GDN's GEMM engine; returns the previous mode.
+ * 0 (default, or environment TT_GDN_GEMM unset): tensor cores, with 3xTF32
+ *   products (hi*hi + hi*lo + lo*hi of the rounded TF32 head and tail of each
+ *   fp32 operand) when the GDN's inputs are fp32 and TF32 products when they
+ *   are bf16/fp16;
+ * 1: tensor cores with 3xTF32 products for every input type;
+ * 2: the CUDA-core fp32 FMA GEMM.
+ * Launches whose operands are not 16-byte aligned use the CUDA-core GEMM. */
+int tt_gdn_set_gemm_mode(int mode);
+
+/* One segmented GEMM of the tree GDN's engine, for testing the engines
+ * against each other: C = alpha * A B + beta * C per segment and head.
+ * segs: n_segs rows of 13 int64 (M, N, K, kmode, a_off, a_rs, a_cs, b_off,
+ * b_rs, b_cs, c_off, c_rs, c_cs), element (r, c) of A at A + h * a_hs +
+ * a_off + r * a_rs + c * a_cs, likewise B and C; kmode 0 multiplies the whole
+ * K range, 1-4 skip the K slices a triangular operand leaves zero (1: A lower,
+ * 2: A upper, 3: B upper, 4: B lower triangular).  engine 0 = CUDA-core fp32
+ * FMA, 1 = tensor cores with TF32 products, 3 = tensor cores with 3xTF32
+ * products (TT_ERR_UNSUPPORTED unless every base is 16-byte aligned, every
+ * offset and non-unit stride a multiple of 4, and c_cs == 1).  Device
+ * pointers; synchronises the stream before returning.  Workspace:
+ * tt_gdn_segmented_gemm_workspace_size(n_segs, segs) bytes.  No counterpart
+ * in the reference (a test hook of the engine behind tt_gdn_tree_fwd/_bwd). */
+int64_t tt_gdn_segmented_gemm_workspace_size(int32_t n_segs, const int64_t* segs);
+int tt_gdn_segmented_gemm(int engine, int32_t n_segs, const int64_t* segs, int32_t H,
+                          const float* A, int64_t a_hs, const float* B, int64_t b_hs, float* C,
+                          int64_t c_hs, float alpha, float beta, void* workspace,
+                          int64_t workspace_bytes, void* stream);
+
+/* Copies into *out, then clears, the first error recorded by a tree-GDN
+ * tensor-core kernel on the current device since the last call
+ * (TT_ERR_DEVICE_TIMEOUT when a bounded wait expired; 0 = none).
+ * Synchronises with the device. */
+int tt_gdn_take_device_status(int32_t* out);
+
 /* Diagnostic: launches one kernel that waits, with the bounded wait every
  * tensor-core kernel uses, on an mbarrier phase nothing completes; after the
  * 2 s limit it records TT_ERR_DEVICE_TIMEOUT in *status (device memory) and

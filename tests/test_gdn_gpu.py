@@ -293,3 +293,65 @@ def test_tree_conv_random_tree_with_bias_vs_oracle(C, K, dtype, tol):
     assert rel(f(xt.grad), dx) < tol
     assert rel(f(ssm.conv1d.weight.grad)[:, 0], dw) < tol
     assert rel(f(ssm.conv1d.bias.grad), db) < tol
+
+
+def _gemm_mode(mode):
+    from tree_training_b200 import _lib
+    return _lib.lib().tt_gdn_set_gemm_mode(mode)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 2e-5), (torch.bfloat16, 1e-2)])
+def test_gdn_tensor_core_gemm_matches_cuda_core_gemm(dtype, tol):
+    """The same forward and backward with the segmented GEMMs on the tensor
+    cores (default: 3xTF32 products for fp32 inputs, TF32 for bf16) and on
+    the CUDA cores (fp32 FMA).  The tree has an empty node, one-token nodes,
+    and nodes past one 128-row tile (up to 300 tokens), D = 128 and GQA 2:4."""
+    lens = [300, 0, 1, 129, 7, 128, 64, 1, 250, 33]
+    parents = [-1, 0, 0, 2, 3, 3, 1, 6, 0, 8]
+    bounds, s0 = [], 0
+    for L in lens:
+        bounds.append((s0, s0 + L))
+        s0 += L
+    S, Hk, H, D = s0, 2, 4, 128
+    g_ = np.random.default_rng(31)
+    q = g_.standard_normal((1, S, Hk, D))
+    k = g_.standard_normal((1, S, Hk, D))
+    v = g_.standard_normal((1, S, H, D)) * 0.5
+    gg = -np.log1p(np.exp(-g_.standard_normal((1, S, H))))
+    bt = 1.0 / (1.0 + np.exp(-g_.standard_normal((1, S, H))))
+    s0_ = g_.standard_normal((1, H, D, D)) * 0.05
+    do = g_.standard_normal((1, S, H, D))
+    dl = g_.standard_normal((1, H, D, D))
+    res = []
+    for mode in (0, 2):
+        prev = _gemm_mode(mode)
+        try:
+            res.append(run_gdn(q, k, v, gg, bt, bounds, parents, s0_, True, do, dl, dtype))
+        finally:
+            _gemm_mode(prev)
+    tt.check_device_status(DEV)
+    for key in ("out", "last", "dq", "dk", "dv", "dg", "dbeta", "dinit"):
+        assert np.isfinite(res[0][key]).all(), key
+        assert rel(res[0][key], res[1][key]) < tol, (key, rel(res[0][key], res[1][key]))
+    # and the tensor-core result against the float64 oracle at the GDN bar, on
+    # the same tree without its empty node (which the reference's algorithm,
+    # like the oracle, cannot take: it reads the node's last cumulative gate)
+    if dtype == torch.float32:
+        keep = [i for i, L in enumerate(lens) if L > 0]
+        remap = {old: new for new, old in enumerate(keep)}
+        b2 = [bounds[i] for i in keep]
+        p2 = []
+        for i in keep:
+            par = parents[i]
+            while par >= 0 and lens[par] == 0:      # an empty node passes its parent's state on
+                par = parents[par]
+            p2.append(remap[par] if par >= 0 else -1)
+        got = run_gdn(q, k, v, gg, bt, b2, p2, s0_, True, do, dl, dtype)
+        ref = _oracle(_Info(b2, p2), q, k, v, gg, bt, s0_, do, dl)
+        for key in ("out", "last", "dq", "dk", "dv", "dg", "dbeta", "dinit"):
+            assert rel(got[key], ref[key]) < 2e-5, (key, rel(got[key], ref[key]))
+
+
+class _Info:
+    def __init__(self, bounds, parents):
+        self.chunk_boundaries, self.chunk_parent_map = bounds, parents

@@ -38,6 +38,12 @@ SIGNATURES = {
     "tt_set_kernel_path": (_INT, [_INT]),
     "tt_kernel_launches": (_I64, []),
     "tt_gdn_gemm_flops": (_I64, []),
+    "tt_gdn_gemm_tc_flops": (_I64, []),
+    "tt_gdn_set_gemm_mode": (_INT, [_INT]),
+    "tt_gdn_take_device_status": (_INT, [_P]),
+    "tt_gdn_segmented_gemm_workspace_size": (_I64, [_I32, _P]),
+    "tt_gdn_segmented_gemm": (_INT, [_INT, _I32, _P, _I32, _P, _I64, _P, _I64, _P, _I64, _F32,
+                                     _F32, _P, _I64, _P]),
     "tt_diag_bounded_wait": (_INT, [_P, _P]),
     "tt_pack_forest": (_INT, [_I32, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _P, _P]),
     "tt_gateway_intervals_from_bias": (_INT, [_I32, _P, _I32, _P, _P]),

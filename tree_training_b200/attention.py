@@ -41,6 +41,12 @@ def check_device_status(device: Optional[torch.device] = None) -> None:
         if code:
             s.zero_()
             raise _lib.TTError("device kernel", code)
+    # the tree GDN's tensor-core kernels record into a word of their own
+    word = np.zeros(1, np.int32)
+    with torch.cuda.device(dev):
+        _lib.call("tt_gdn_take_device_status", word.ctypes.data)
+    if int(word[0]):
+        raise _lib.TTError("tree GDN kernel", int(word[0]))
 
 
 def lse_ld(n_q: int) -> int:

@@ -69,6 +69,8 @@ __device__ __forceinline__ void raise_abort(FwdBarriers* sh, int32_t* status) {
   *reinterpret_cast<volatile int32_t*>(&sh->abort) = 1;
 }
 
+// 10 warps share the SM's 4 register-file partitions (16K registers each), so
+// a partition holds up to 3 warps: 168 registers per thread at most.
 template <bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -134,7 +136,10 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
         tma_load_3d(sQ + g * kTileBytes, &tm_q, &sh->q_full, 0, qt * kBM, h0 + g);
         tma_load_3d(sQ + g * kTileBytes + kHalfBytes, &tm_q, &sh->q_full, 64, qt * kBM, h0 + g);
       }
-      int n_k[kStages] = {0}, n_v[kStages] = {0}, n_aux[kAuxStages] = {0};
+      // loads issued so far, kept as totals and bit masks (no per-stage
+      // arrays: indexed at run time they would live in local memory)
+      int k_issued = 0, v_issued = 0;
+      uint32_t aux_any = 0, aux_par = 0;   // bit a: stage a loaded / odd count
       bool ok = true;
       // K of tile it reuses the stage once the score MMAs of tile it-2 are
       // done, V once its PV MMAs are; those releases come in the order
@@ -149,7 +154,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
         mbar_arrive_expect_tx(&sh->k_full[s], kTileBytes);
         tma_load_3d(k_dst, &tm_k, &sh->k_full[s], 0, kt * kBN, hk);
         tma_load_3d(k_dst + kHalfBytes, &tm_k, &sh->k_full[s], 64, kt * kBN, hk);
-        n_k[s] += 1;
+        ++k_issued;
         if (ent & 1) {
           // the key intervals of a partial tile: read by the softmax warps,
           // whose progress past tile it is implied by the release of K(it+2)
@@ -158,25 +163,30 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
           mbar_arrive_expect_tx(&sh->aux_full[a], kAuxBytes);
           bulk_load(a_dst, kv_lo + kt * kBN, kAuxBytes / 2, &sh->aux_full[a]);
           bulk_load(a_dst + kAuxBytes / 2, kv_hi + kt * kBN, kAuxBytes / 2, &sh->aux_full[a]);
-          n_aux[a] += 1;
+          aux_any |= 1u << a;
+          aux_par ^= 1u << a;
         }
         if (it >= kStages) ok = mbar_wait(&sh->v_empty[s], ((it / kStages) - 1) & 1, abort_flag);
         if (!ok) break;
         mbar_arrive_expect_tx(&sh->v_full[s], kTileBytes);
         tma_load_3d(sV + s * kTileBytes, &tm_v, &sh->v_full[s], 0, kt * kBN, hk);
         tma_load_3d(sV + s * kTileBytes + kHalfBytes, &tm_v, &sh->v_full[s], 64, kt * kBN, hk);
-        n_v[s] += 1;
+        ++v_issued;
       }
       if (!ok) {
         raise_abort(sh, status);
-        // let the copies already in flight land before the CTA exits
+        // let the copies already in flight land before the CTA exits: stage s
+        // received loads it = s, s + kStages, ... < issued, the last of which
+        // completes phase (count - 1) & 1
         mbar_wait(&sh->q_full, 0, nullptr);
         for (int s = 0; s < kStages; ++s) {
-          if (n_k[s] > 0) mbar_wait(&sh->k_full[s], (n_k[s] - 1) & 1, nullptr);
-          if (n_v[s] > 0) mbar_wait(&sh->v_full[s], (n_v[s] - 1) & 1, nullptr);
+          const int nk = k_issued > s ? (k_issued - 1 - s) / kStages + 1 : 0;
+          const int nv = v_issued > s ? (v_issued - 1 - s) / kStages + 1 : 0;
+          if (nk > 0) mbar_wait(&sh->k_full[s], (nk - 1) & 1, nullptr);
+          if (nv > 0) mbar_wait(&sh->v_full[s], (nv - 1) & 1, nullptr);
         }
         for (int a = 0; a < kAuxStages; ++a)
-          if (n_aux[a] > 0) mbar_wait(&sh->aux_full[a], (n_aux[a] - 1) & 1, nullptr);
+          if ((aux_any >> a) & 1u) mbar_wait(&sh->aux_full[a], ((aux_par >> a) & 1u) ^ 1u, nullptr);
       }
     }
   } else if (warp == 1) {
@@ -306,14 +316,15 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
         if (__any_sync(0xffffffffu, need)) {
           // PV_g(it-1) has completed: the commit that signalled S_g(it) was
           // issued after it, and a commit tracks every earlier MMA.
+          // (16 columns at a time: the score row stays live across this)
 #pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
-            float o[32];
-            uint32_t w[32];
-            tmem_ld32(lane_addr + col_o + c * 32, o);
+          for (int c = 0; c < kD / 16; ++c) {
+            float o[16];
+            uint32_t w[16];
+            tmem_ld16(lane_addr + col_o + c * 16, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * alpha);
-            tmem_st32(lane_addr + col_o + c * 32, w);
+            for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(o[i] * alpha);
+            tmem_st16(lane_addr + col_o + c * 16, w);
           }
           tmem_st_wait();
         }
@@ -324,12 +335,15 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
         // rest on the SFU; 4 independent paired partial sums
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                          make_float2(0.f, 0.f)};
+        // (P goes back to TMEM a quarter row at a time: 16 packed registers
+        // live beside the score row instead of 32, which keeps the thread
+        // within its 168 registers)
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t pk[32];
+        for (int qq = 0; qq < 4; ++qq) {
+          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float2 x = ffma2(make_float2(sv[hf * 64 + 2 * i], sv[hf * 64 + 2 * i + 1]), sc2, nmb2);
+          for (int i = 0; i < 16; ++i) {
+            const float2 x = ffma2(make_float2(sv[qq * 32 + 2 * i], sv[qq * 32 + 2 * i + 1]), sc2, nmb2);
             float2 pr;
             if ((i & 7) < kEmuPer8) {
               pr = exp2_poly2(x);
@@ -340,7 +354,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
             acc[i & 3] = fadd2(acc[i & 3], pr);
             pk[i] = pack2<kBf16>(pr.x, pr.y);
           }
-          tmem_st32(lane_addr + col_s + hf * 32, pk);
+          tmem_st16(lane_addr + col_s + qq * 16, pk);
         }
         const float2 a01 = fadd2(acc[0], acc[1]), a23 = fadd2(acc[2], acc[3]);
         l_run += (a01.x + a23.x) + (a01.y + a23.y);

@@ -23,21 +23,16 @@
 // matrices packed per node ([H][sum L^2]), states [n_nodes+1][H][Dk][Dv].
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
+#include <type_traits>
 #include <vector>
 
-#include "tt_common.cuh"
+#include "tt_gdn_gemm.cuh"
 
 namespace tt {
 namespace gdn {
 namespace {
-
-struct SegDesc {
-  int M, N, K, pad;
-  long long a_off, a_rs, a_cs;
-  long long b_off, b_rs, b_cs;
-  long long c_off, c_rs, c_cs;
-};
 
 #ifndef TT_GDN_BK
 #define TT_GDN_BK 16
@@ -73,7 +68,7 @@ __device__ __forceinline__ void cp_async_wait() {
 
 constexpr int kGemmStages = 3;              // K slices in flight
 
-// C[i,j] = alpha * sum_k A[i,k] B[k,j] + beta * C[i,j] over a list of 64 x 64
+// C[i,j] = alpha * sum_k A[i,k] B[k,j] + beta * Cin[i,j] over a list of 64 x 64
 // output tiles (tile = {segment, tm << 16 | tn}) and heads (blockIdx.z);
 // operand element (r, c) of segment s lives at
 // base + head * h_stride + off_s + r * rs_s + c * cs_s.
@@ -85,7 +80,7 @@ constexpr int kGemmStages = 3;              // K slices in flight
 __global__ void __launch_bounds__(kGemmThreads)
 seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
          const float* __restrict__ A, long long a_hs, const float* __restrict__ B, long long b_hs,
-         float* __restrict__ C, long long c_hs, float alpha, float beta) {
+         float* C, long long c_hs, float alpha, float beta, const float* Cin) {
   const int2 tl = tiles[blockIdx.x];
   const SegDesc sd = segs[tl.x];
   const int tm = tl.y >> 16, tn = tl.y & 0xFFFF;
@@ -93,6 +88,7 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
   const float* a = A + h * a_hs + sd.a_off;
   const float* b = B + h * b_hs + sd.b_off;
   float* c = C + h * c_hs + sd.c_off;
+  const float* cin = (Cin ? Cin : C) + h * c_hs + sd.c_off;   // Cin: C's layout
   __shared__ __align__(16) float sa[kGemmStages][kBK][kBM + kRowPad];
   __shared__ __align__(16) float sb[kGemmStages][kBK][kBN + kRowPad];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -166,11 +162,16 @@ seg_gemm(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles,
       const int gj = j0 + 4 * tx + w;
       if (gj >= sd.N) continue;
       const float v = (u & 1) ? acc[u >> 1][w].y : acc[u >> 1][w].x;
-      float* pc = c + gi * sd.c_rs + gj * sd.c_cs;
-      *pc = alpha * v + (beta != 0.f ? beta * *pc : 0.f);
+      const long long o = gi * sd.c_rs + gj * sd.c_cs;
+      c[o] = alpha * v + (beta != 0.f ? beta * cin[o] : 0.f);
     }
   }
 }
+
+// Row stride of a node's L x L matrices: L rounded up to 4 floats, so that
+// every row starts on a 16-byte boundary (the tensor-core GEMM stages rows
+// with 16-byte copies).  Columns [L, Lp) are padding that no kernel reads.
+__host__ __device__ __forceinline__ int row_stride(int L) { return (L + 3) & ~3; }
 
 // ---- elementwise kernels ---------------------------------------------------------
 
@@ -252,7 +253,7 @@ __global__ void decay_masks(int S, const int* __restrict__ nstart, const int* __
   const int c = blockIdx.y, h = blockIdx.z, j = blockIdx.x;
   const int L = nlen[c];
   if (j >= L) return;
-  const long long base = h * l_hs + loff[c] + (long long)j * L;
+  const long long base = h * l_hs + loff[c] + (long long)j * row_stride(L);
   const float gj = gam[(long long)h * S + nstart[c] + j];
   for (int m = threadIdx.x; m < L; m += blockDim.x) {
     const float d = m <= j ? expf(gj - gam[(long long)h * S + nstart[c] + m]) : 0.f;
@@ -271,13 +272,13 @@ tri_inv_diag(const int2* __restrict__ blocks, const int* __restrict__ nlen,
              const long long* __restrict__ loff, long long l_hs, float* Am) {
   const int2 bl = blocks[blockIdx.x];
   const int c = bl.x, i0 = bl.y * kInvB, h = blockIdx.y;
-  const int L = nlen[c];
+  const int L = nlen[c], Lp = row_stride(L);
   const int bs = min(kInvB, L - i0);
-  float* base = Am + h * l_hs + loff[c] + (long long)i0 * L + i0;
+  float* base = Am + h * l_hs + loff[c] + (long long)i0 * Lp + i0;
   __shared__ float sA[kInvB][kInvB + 1];
   __shared__ float sT[kInvB][kInvB + 1];
   for (int idx = threadIdx.x; idx < bs * bs; idx += blockDim.x)
-    sA[idx / bs][idx % bs] = base[(long long)(idx / bs) * L + idx % bs];
+    sA[idx / bs][idx % bs] = base[(long long)(idx / bs) * Lp + idx % bs];
   __syncthreads();
   const int col = threadIdx.x;
   if (col < bs) {
@@ -289,18 +290,7 @@ tri_inv_diag(const int2* __restrict__ blocks, const int* __restrict__ nlen,
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < bs * bs; idx += blockDim.x)
-    base[(long long)(idx / bs) * L + idx % bs] = sT[idx / bs][idx % bs];
-}
-
-__global__ void add_arrays(long long n, const float* __restrict__ a, const float* __restrict__ b,
-                           float* out) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) out[i] = a[i] + b[i];
-}
-
-__global__ void copy_array(long long n, const float* __restrict__ a, float* out) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) out[i] = a[i];
+    base[(long long)(idx / bs) * Lp + idx % bs] = sT[idx / bs][idx % bs];
 }
 
 // states[c+1][h] += exp(gl[h][c]) * states[parent+1][h]   for the level's nodes
@@ -400,7 +390,7 @@ __global__ void grad_masks(int S, const int* __restrict__ nstart, const int* __r
   const int c = blockIdx.y, h = blockIdx.z, j = blockIdx.x;
   const int L = nlen[c];
   if (j >= L) return;
-  const long long base = h * l_hs + loff[c] + (long long)j * L;
+  const long long base = h * l_hs + loff[c] + (long long)j * row_stride(L);
   const float gj = gam[(long long)h * S + nstart[c] + j];
   for (int m = threadIdx.x; m < L; m += blockDim.x) {
     const float d = m <= j ? expf(gj - gam[(long long)h * S + nstart[c] + m]) : 0.f;
@@ -417,13 +407,13 @@ __global__ void ddd_rowcol(int S, const int* __restrict__ nstart, const int* __r
                            const long long* __restrict__ loff, long long l_hs,
                            const float* __restrict__ dDD, float* dgam) {
   const int c = blockIdx.y, h = blockIdx.z, j = blockIdx.x;
-  const int L = nlen[c];
+  const int L = nlen[c], Lp = row_stride(L);
   if (j >= L) return;
   const float* base = dDD + h * l_hs + loff[c];
   // the row and column sums cancel to a small difference: accumulate in fp64
   double acc = 0.0;
   for (int m = threadIdx.x; m < L; m += blockDim.x)
-    acc += (double)base[(long long)j * L + m] - (double)base[(long long)m * L + j];
+    acc += (double)base[(long long)j * Lp + m] - (double)base[(long long)m * Lp + j];
   __shared__ double red[32];
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
@@ -581,8 +571,10 @@ __global__ void dinit_kernel(int H, int DkDv, int n_roots, const int* __restrict
 struct Plan {
   int S, H, Hk, Dk, Dv, n;
   std::vector<int> start, len, parent, depth;
-  std::vector<long long> loff;     // packed LxL offset per node
-  long long ll_total = 0;          // sum L^2
+  std::vector<long long> loff;     // packed L x Lp offset per node (Lp = row_stride(L))
+  std::vector<long long> xoff;     // 64 x Lp scratch block per node (exact inverse)
+  long long ll_total = 0;          // sum L * Lp
+  long long lp_total = 0;          // sum Lp
   int max_len = 0, max_depth = 0;
   std::vector<std::vector<int>> levels;
   std::vector<int> child_ptr, child_idx, roots;
@@ -592,6 +584,7 @@ int make_plan(Plan& p, int S, int H, int Hk, int Dk, int Dv, int n, const int32_
               const int32_t* parents) {
   p.S = S; p.H = H; p.Hk = Hk; p.Dk = Dk; p.Dv = Dv; p.n = n;
   p.start.resize(n); p.len.resize(n); p.parent.resize(n); p.depth.resize(n); p.loff.resize(n);
+  p.xoff.resize(n);
   int expect = 0;
   for (int c = 0; c < n; ++c) {
     const int s = bounds[2 * c], e = bounds[2 * c + 1], par = parents[c];
@@ -600,7 +593,9 @@ int make_plan(Plan& p, int S, int H, int Hk, int Dk, int Dv, int n, const int32_
     p.start[c] = s; p.len[c] = e - s; p.parent[c] = par;
     p.depth[c] = par < 0 ? 0 : p.depth[par] + 1;
     p.loff[c] = p.ll_total;
-    p.ll_total += (long long)(e - s) * (e - s);
+    p.ll_total += (long long)(e - s) * row_stride(e - s);
+    p.xoff[c] = 64LL * p.lp_total;
+    p.lp_total += row_stride(e - s);
     p.max_len = std::max(p.max_len, e - s);
     p.max_depth = std::max(p.max_depth, p.depth[c]);
   }
@@ -644,6 +639,7 @@ struct Bufs {
   long long* d_loff;
   SegDesc* d_desc;
   int2* d_tiles;
+  int2* d_tiles_tc;
   int2* d_inv_blocks;   // (node, diagonal block) pairs of the exact-inverse mode
   int* d_cap_slot;      // per node: index into the captured states, or -1
 };
@@ -653,33 +649,40 @@ struct Bufs {
 // lands outside its segment).
 struct DescSet {
   int first, count, tfirst, tcount;
+  int tc_first, tc_count;   // the same segments as 128 x 128 tensor-core tiles
   double flops;   // 2 M N K summed over the set's segments, one head
 };
 
 struct Builder {
   const Plan& p;
   std::vector<SegDesc> all;
-  std::vector<int2> tiles;
+  std::vector<int2> tiles;      // 64 x 64 tiles (CUDA-core GEMM)
+  std::vector<int2> tiles_tc;   // kTcTile x kTcTile tiles (tensor-core GEMM)
   explicit Builder(const Plan& pl) : p(pl) {}
   DescSet add(const std::vector<SegDesc>& v) {
-    DescSet d{(int)all.size(), (int)v.size(), (int)tiles.size(), 0, 0.0};
+    DescSet d{(int)all.size(), (int)v.size(), (int)tiles.size(), 0, (int)tiles_tc.size(), 0, 0.0};
     for (size_t i = 0; i < v.size(); ++i) {
       d.flops += 2.0 * v[i].M * v[i].N * v[i].K;
+      const int seg = (int)all.size() + (int)i;
       const int tms = (v[i].M + kBM - 1) / kBM, tns = (v[i].N + kBN - 1) / kBN;
       for (int tm = 0; tm < tms; ++tm)
-        for (int tn = 0; tn < tns; ++tn)
-          tiles.push_back(make_int2((int)all.size() + (int)i, (tm << 16) | tn));
+        for (int tn = 0; tn < tns; ++tn) tiles.push_back(make_int2(seg, (tm << 16) | tn));
+      const int ums = (v[i].M + kTcTile - 1) / kTcTile, uns = (v[i].N + kTcTile - 1) / kTcTile;
+      for (int tm = 0; tm < ums; ++tm)
+        for (int tn = 0; tn < uns; ++tn) tiles_tc.push_back(make_int2(seg, (tm << 16) | tn));
     }
     d.tcount = (int)tiles.size() - d.tfirst;
+    d.tc_count = (int)tiles_tc.size() - d.tc_first;
     all.insert(all.end(), v.begin(), v.end());
     return d;
   }
 };
 
 SegDesc desc(int M, int N, int K, long long ao, long long ars, long long acs, long long bo,
-             long long brs, long long bcs, long long co, long long crs, long long ccs) {
+             long long brs, long long bcs, long long co, long long crs, long long ccs,
+             int kmode = kKFull) {
   SegDesc d;
-  d.M = M; d.N = N; d.K = K; d.pad = 0;
+  d.M = M; d.N = N; d.K = K; d.kmode = kmode;
   d.a_off = ao; d.a_rs = ars; d.a_cs = acs;
   d.b_off = bo; d.b_rs = brs; d.b_cs = bcs;
   d.c_off = co; d.c_rs = crs; d.c_cs = ccs;
@@ -687,15 +690,56 @@ SegDesc desc(int M, int N, int K, long long ao, long long ars, long long acs, lo
 }
 
 std::atomic<int64_t> g_gemm_flops{0};
+std::atomic<int64_t> g_gemm_tc_flops{0};
+
+// Which GEMM runs the segments: 0 = automatic (tensor cores: 3xTF32 products
+// for fp32 inputs, TF32 products for 16-bit inputs), 1 = tensor cores with
+// 3xTF32 products for any input, 2 = the CUDA-core fp32 GEMM.  Initialised
+// from TT_GDN_GEMM; tt_gdn_set_gemm_mode changes it.
+std::atomic<int> g_gemm_mode{-1};
+
+int gemm_mode() {
+  int m = g_gemm_mode.load();
+  if (m < 0) {
+    const char* e = std::getenv("TT_GDN_GEMM");
+    m = (e && (e[0] == '1' || e[0] == '2')) ? e[0] - '0' : 0;
+    g_gemm_mode.store(m);
+  }
+  return m;
+}
+
+// One GEMM launch context: the device descriptor/tile arrays, the host copy
+// of the descriptors (for the tensor-core kernel's layout check) and the
+// product split the run uses (0 = CUDA cores, 1 = TF32, 3 = 3xTF32).
+struct GemmCtx {
+  const SegDesc* d_desc;
+  const int2* d_tiles;
+  const int2* d_tiles_tc;
+  const std::vector<SegDesc>* h_desc;
+  int split;
+  int rc = TT_OK;
+};
 
 // Tiles address segments by their index in the whole descriptor array.
-void launch_gemm(const SegDesc* d_desc, const int2* d_tiles, DescSet ds, int H, const float* A,
-                 long long a_hs, const float* B, long long b_hs, float* C, long long c_hs,
-                 float alpha, float beta, cudaStream_t st) {
+// C = alpha A B + beta Cin (Cin defaults to C; it has C's offsets and strides)
+void launch_gemm(GemmCtx& g, DescSet ds, int H, const float* A, long long a_hs, const float* B,
+                 long long b_hs, float* C, long long c_hs, float alpha, float beta,
+                 cudaStream_t st, const float* Cin = nullptr) {
   if (ds.tcount == 0) return;
+  if (g.split != 0 && tt_gdn_tc_gemm_supported(g.h_desc->data(), ds.first, ds.count, A, a_hs, B,
+                                               b_hs, C, c_hs) &&
+      (Cin == nullptr || (reinterpret_cast<uintptr_t>(Cin) & 15u) == 0)) {
+    const int rc = tt_gdn_seg_gemm_tc(g.d_desc, g.d_tiles_tc + ds.tc_first, ds.tc_count, H, A,
+                                      a_hs, B, b_hs, C, c_hs, alpha, beta, Cin, g.split, st);
+    if (rc != TT_OK) g.rc = rc;
+    tt_count_launches(1);
+    g_gemm_flops.fetch_add(static_cast<int64_t>(ds.flops * H), std::memory_order_relaxed);
+    g_gemm_tc_flops.fetch_add(static_cast<int64_t>(ds.flops * H), std::memory_order_relaxed);
+    return;
+  }
   dim3 grid(ds.tcount, 1, H);
-  seg_gemm<<<grid, kGemmThreads, 0, st>>>(d_desc, d_tiles + ds.tfirst, A, a_hs, B, b_hs, C, c_hs,
-                                          alpha, beta);
+  seg_gemm<<<grid, kGemmThreads, 0, st>>>(g.d_desc, g.d_tiles + ds.tfirst, A, a_hs, B, b_hs, C,
+                                          c_hs, alpha, beta, Cin);
   tt_count_launches(1);
   g_gemm_flops.fetch_add(static_cast<int64_t>(ds.flops * H), std::memory_order_relaxed);
 }
@@ -727,7 +771,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   b.Kd = ar.get<float>(H * vk); b.U = ar.get<float>(H * vv); b.W = ar.get<float>(H * vk);
   // T1: scratch of the T = I + A + A^2 products, and of the exact inverse's
   // block rows (64 x L per node at offset 64 * start)
-  const long long t1_hs = std::max(std::max(vk, vv), 64LL * S);
+  const long long t1_hs = std::max(std::max(vk, vv), 64LL * p.lp_total);
   b.T1 = ar.get<float>(H * t1_hs); b.Vn = ar.get<float>(H * vv);
   b.O = ar.get<float>(H * vv);
   b.KK = ar.get<float>(H * llh); b.QK = ar.get<float>(H * llh);
@@ -754,11 +798,12 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     const int L = p.len[c];
     const long long tk = (long long)p.start[c] * Dk, tv = (long long)p.start[c] * Dv;
     const long long lo = p.loff[c];
+    const int Lp = row_stride(L);
     // KK = Kb K^T, QK = Q K^T : [L x L], K = Dk
-    v_kk.push_back(desc(L, L, Dk, tk, Dk, 1, tk, 1, Dk, lo, L, 1));
+    v_kk.push_back(desc(L, L, Dk, tk, Dk, 1, tk, 1, Dk, lo, Lp, 1));
     // A * X for X = [L x Dv] (U) / [L x Dk] (W)
-    v_av.push_back(desc(L, Dv, L, lo, L, 1, tv, Dv, 1, tv, Dv, 1));
-    v_ak.push_back(desc(L, Dk, L, lo, L, 1, tk, Dk, 1, tk, Dk, 1));
+    v_av.push_back(desc(L, Dv, L, lo, Lp, 1, tv, Dv, 1, tv, Dv, 1, kKToRow));
+    v_ak.push_back(desc(L, Dk, L, lo, Lp, 1, tk, Dk, 1, tk, Dk, 1, kKToRow));
   }
   const long long st_off = sh;   // states[c+1] offset base (per-head stride added by kernel)
   for (size_t d = 0; d < p.levels.size(); ++d) {
@@ -772,7 +817,8 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
       // O = Qg S_in
       lv_qs[d].push_back(desc(L, Dv, Dk, tk, Dk, 1, sin, Dv, 1, tv, Dv, 1));
       // O += Aqk Vn
-      lv_aqv[d].push_back(desc(L, Dv, L, p.loff[c], L, 1, tv, Dv, 1, tv, Dv, 1));
+      lv_aqv[d].push_back(desc(L, Dv, L, p.loff[c], row_stride(L), 1, tv, Dv, 1, tv, Dv, 1,
+                               kKToRow));
       // S_out = Kd^T Vn : [Dk x Dv] = [Dk x L][L x Dv]
       lv_kdv[d].push_back(desc(Dk, Dv, L, tk, 1, Dk, tv, Dv, 1, sout, Dv, 1));
     }
@@ -785,14 +831,16 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   std::vector<std::vector<SegDesc>> li_x(std::max(0, max_nb - 1)), li_t(std::max(0, max_nb - 1));
   for (int c = 0; c < n; ++c) {
     const int L = p.len[c];
-    const long long lo = p.loff[c], xo = 64LL * p.start[c];
+    const long long lo = p.loff[c], xo = p.xoff[c];
+    const int Lp = row_stride(L);
     for (int i = 0; i * kInvB < L; ++i) {
       inv_blocks.push_back(make_int2(c, i));
       if (i == 0) continue;
       const int i0 = i * kInvB, bs = std::min(kInvB, L - i0);
-      li_x[i - 1].push_back(desc(bs, i0, i0, lo + (long long)i0 * L, L, 1, lo, L, 1, xo, L, 1));
-      li_t[i - 1].push_back(desc(bs, i0, bs, lo + (long long)i0 * L + i0, L, 1, xo, L, 1,
-                                 lo + (long long)i0 * L, L, 1));
+      li_x[i - 1].push_back(desc(bs, i0, i0, lo + (long long)i0 * Lp, Lp, 1, lo, Lp, 1, xo, Lp, 1,
+                                 kKFromCol));
+      li_t[i - 1].push_back(desc(bs, i0, bs, lo + (long long)i0 * Lp + i0, Lp, 1, xo, Lp, 1,
+                                 lo + (long long)i0 * Lp, Lp, 1, kKToRow));
     }
   }
   DescSet ds_kk = bd.add(v_kk), ds_av = bd.add(v_av), ds_ak = bd.add(v_ak);
@@ -821,7 +869,8 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
         const long long lo = p.loff[c];
         const long long so = (long long)c * st_off;
         // dVn = Aqk^T dO : [L x Dv] = [L x L]^T [L x Dv]
-        lb_dvn1[d].push_back(desc(L, Dv, L, lo, 1, L, tv, Dv, 1, tv, Dv, 1));
+        lb_dvn1[d].push_back(desc(L, Dv, L, lo, 1, row_stride(L), tv, Dv, 1, tv, Dv, 1,
+                                  kKFromRow));
         // dVn += Kd dSo : [L x Dv] = [L x Dk][Dk x Dv]
         lb_dvn2[d].push_back(desc(L, Dv, Dk, tk, Dk, 1, so, Dv, 1, tv, Dv, 1));
         // dSi = Qg^T dO : [Dk x Dv] = [Dk x L][L x Dv]
@@ -834,6 +883,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
       const int L = p.len[c];
       const long long tk = (long long)p.start[c] * Dk, tv = (long long)p.start[c] * Dv;
       const long long lo = p.loff[c];
+      const int Lp = row_stride(L);
       const long long sin = (long long)(p.parent[c] + 1) * st_off;
       const long long so = (long long)c * st_off;
       // dQg = dO S_in^T : [L x Dk] = [L x Dv][Dv x Dk]
@@ -843,19 +893,19 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
       // dW = -dVn S_in^T
       b_dw.push_back(desc(L, Dk, Dv, tv, Dv, 1, sin, 1, Dv, tk, Dk, 1));
       // dAqk = dO Vn^T : [L x L]
-      b_daqk.push_back(desc(L, L, Dv, tv, Dv, 1, tv, 1, Dv, lo, L, 1));
+      b_daqk.push_back(desc(L, L, Dv, tv, Dv, 1, tv, 1, Dv, lo, Lp, 1));
       // dT = dVn Vb^T + dW Kbg^T
-      b_dt1.push_back(desc(L, L, Dv, tv, Dv, 1, tv, 1, Dv, lo, L, 1));
-      b_dt2.push_back(desc(L, L, Dk, tk, Dk, 1, tk, 1, Dk, lo, L, 1));
+      b_dt1.push_back(desc(L, L, Dv, tv, Dv, 1, tv, 1, Dv, lo, Lp, 1));
+      b_dt2.push_back(desc(L, L, Dk, tk, Dk, 1, tk, 1, Dk, lo, Lp, 1));
       // X = dT A^T : [L x L] = [L x L][L x L]^T ; X += A^T dT
-      b_x1.push_back(desc(L, L, L, lo, L, 1, lo, 1, L, lo, L, 1));
-      b_x2.push_back(desc(L, L, L, lo, 1, L, lo, L, 1, lo, L, 1));
+      b_x1.push_back(desc(L, L, L, lo, Lp, 1, lo, 1, Lp, lo, Lp, 1, kKToCol));
+      b_x2.push_back(desc(L, L, L, lo, 1, Lp, lo, Lp, 1, lo, Lp, 1, kKFromRow));
       // T^T y = y + A^T y + A^T (A^T y)  for y = dVn [L x Dv] and dW [L x Dk]
-      b_tvt.push_back(desc(L, Dv, L, lo, 1, L, tv, Dv, 1, tv, Dv, 1));
-      b_tkt.push_back(desc(L, Dk, L, lo, 1, L, tk, Dk, 1, tk, Dk, 1));
+      b_tvt.push_back(desc(L, Dv, L, lo, 1, Lp, tv, Dv, 1, tv, Dv, 1, kKFromRow));
+      b_tkt.push_back(desc(L, Dk, L, lo, 1, Lp, tk, Dk, 1, tk, Dk, 1, kKFromRow));
       // G K (dKb += G K), G^T Kb (dK += G^T Kb), F K (dQ += F K), F^T Q (dK += F^T Q)
-      b_gk.push_back(desc(L, Dk, L, lo, L, 1, tk, Dk, 1, tk, Dk, 1));
-      b_gtk.push_back(desc(L, Dk, L, lo, 1, L, tk, Dk, 1, tk, Dk, 1));
+      b_gk.push_back(desc(L, Dk, L, lo, Lp, 1, tk, Dk, 1, tk, Dk, 1, kKToRow));
+      b_gtk.push_back(desc(L, Dk, L, lo, 1, Lp, tk, Dk, 1, tk, Dk, 1, kKFromRow));
     }
   }
   DescSet ds_dqg = bd.add(b_dqg), ds_dkd = bd.add(b_dkd), ds_dw = bd.add(b_dw),
@@ -882,6 +932,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   b.d_loff = ar.get<long long>(n);
   b.d_desc = ar.get<SegDesc>((long long)bd.all.size());
   b.d_tiles = ar.get<int2>((long long)bd.tiles.size());
+  b.d_tiles_tc = ar.get<int2>((long long)bd.tiles_tc.size());
   b.d_inv_blocks = ar.get<int2>(std::max<long long>(1, (long long)inv_blocks.size()));
   b.d_cap_slot = ar.get<int>(n);
   if (ar.sizing) return TT_OK;
@@ -902,6 +953,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   rc |= h2d(b.d_loff, p.loff.data(), n * 8);
   rc |= h2d(b.d_desc, bd.all.data(), bd.all.size() * sizeof(SegDesc));
   rc |= h2d(b.d_tiles, bd.tiles.data(), bd.tiles.size() * sizeof(int2));
+  rc |= h2d(b.d_tiles_tc, bd.tiles_tc.data(), bd.tiles_tc.size() * sizeof(int2));
   if (exact) rc |= h2d(b.d_inv_blocks, inv_blocks.data(), inv_blocks.size() * sizeof(int2));
   std::vector<int> cap_slot(n, -1);
   for (int i = 0; i < n_cap; ++i) cap_slot[cap_nodes[i]] = i;
@@ -910,6 +962,9 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
 
   const int max_l = p.max_len;
   const float q_scale = 1.f / sqrtf((float)Dk);
+  const int mode = gemm_mode();
+  GemmCtx gc{b.d_desc, b.d_tiles, b.d_tiles_tc, &bd.all,
+             mode == 2 ? 0 : (mode == 1 || std::is_same<T, float>::value) ? 3 : 1};
   auto blocks = [](long long nel) { return (unsigned)((nel + 255) / 256); };
   int launches = 0;
   // ---------------------------------------------------------------- forward
@@ -921,8 +976,8 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
         S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok, l2norm, q_scale, b.Q, b.K, b.Vb, b.Kb,
         b.Kbg, b.Qg, b.Kd);
     launches += 2;
-    launch_gemm(b.d_desc, b.d_tiles, ds_kk, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_kk, H, b.Q, vk, b.K, vk, b.QK, llh, 1.f, 0.f, st);
+    launch_gemm(gc, ds_kk, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
+    launch_gemm(gc, ds_kk, H, b.Q, vk, b.K, vk, b.QK, llh, 1.f, 0.f, st);
     decay_masks<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.gam,
                                                    b.KK, b.QK, b.Am, b.Aqk);
     ++launches;
@@ -932,39 +987,37 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
           b.d_inv_blocks, b.d_len, b.d_loff, llh, b.Am);
       ++launches;
       for (size_t i = 0; i < ds_inv_x.size(); ++i) {
-        launch_gemm(b.d_desc, b.d_tiles, ds_inv_x[i], H, b.Am, llh, b.Am, llh, b.T1, t1_hs, 1.f,
+        launch_gemm(gc, ds_inv_x[i], H, b.Am, llh, b.Am, llh, b.T1, t1_hs, 1.f,
                     0.f, st);
-        launch_gemm(b.d_desc, b.d_tiles, ds_inv_t[i], H, b.Am, llh, b.T1, t1_hs, b.Am, llh, 1.f,
+        launch_gemm(gc, ds_inv_t[i], H, b.Am, llh, b.T1, t1_hs, b.Am, llh, 1.f,
                     0.f, st);
       }
       // U = T Vb;  W = T Kbg
-      launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.Vb, vv, b.U, vv, 1.f, 0.f, st);
-      launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.Kbg, vk, b.W, vk, 1.f, 0.f, st);
+      launch_gemm(gc, ds_av, H, b.Am, llh, b.Vb, vv, b.U, vv, 1.f, 0.f, st);
+      launch_gemm(gc, ds_ak, H, b.Am, llh, b.Kbg, vk, b.W, vk, 1.f, 0.f, st);
     } else {
-      // U = Vb + A Vb + A (A Vb);  W = Kbg + A Kbg + A (A Kbg)
-      // (T1 packed with head stride vv / vk here: add_arrays reads it flat)
-      launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.Vb, vv, b.T1, vv, 1.f, 0.f, st);
-      add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.Vb, b.T1, b.U);
-      launch_gemm(b.d_desc, b.d_tiles, ds_av, H, b.Am, llh, b.T1, vv, b.U, vv, 1.f, 1.f, st);
-      launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.Kbg, vk, b.T1, vk, 1.f, 0.f, st);
-      add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.Kbg, b.T1, b.W);
-      launch_gemm(b.d_desc, b.d_tiles, ds_ak, H, b.Am, llh, b.T1, vk, b.W, vk, 1.f, 1.f, st);
-      launches += 2;
+      // U = T Vb = Vb + A (Vb + A Vb);  W = T Kbg likewise (T = I + A + A^2):
+      // T1 = X + A X first, then X + A T1, both as GEMMs with X as the
+      // epilogue's input (T1 has head stride vv / vk here)
+      launch_gemm(gc, ds_av, H, b.Am, llh, b.Vb, vv, b.T1, vv, 1.f, 1.f, st, b.Vb);
+      launch_gemm(gc, ds_av, H, b.Am, llh, b.T1, vv, b.U, vv, 1.f, 1.f, st, b.Vb);
+      launch_gemm(gc, ds_ak, H, b.Am, llh, b.Kbg, vk, b.T1, vk, 1.f, 1.f, st, b.Kbg);
+      launch_gemm(gc, ds_ak, H, b.Am, llh, b.T1, vk, b.W, vk, 1.f, 1.f, st, b.Kbg);
     }
-    copy_array<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.U, b.Vn);
     init_state<<<blocks(sh), 256, 0, st>>>(sh, init, b.states);
-    launches += 2;
+    ++launches;
     for (size_t d = 0; d < p.levels.size(); ++d) {
       const int cnt = (int)p.levels[d].size();
       // states are [n+1][H][Dk][Dv]: per-head stride DkDv, segment offsets cover (c+1)*H*DkDv
-      launch_gemm(b.d_desc, b.d_tiles, ds_ws[d], H, b.W, vk, b.states, DkDv, b.Vn, vv, -1.f, 1.f, st);
+      // Vn = U - W S_in (every node's rows are written by its own level)
+      launch_gemm(gc, ds_ws[d], H, b.W, vk, b.states, DkDv, b.Vn, vv, -1.f, 1.f, st, b.U);
       if (!backward) {   // the output; the backward (which recomputes this pass) never reads it
-        launch_gemm(b.d_desc, b.d_tiles, ds_qs[d], H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f,
+        launch_gemm(gc, ds_qs[d], H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f,
                     st);
-        launch_gemm(b.d_desc, b.d_tiles, ds_aqv[d], H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f,
+        launch_gemm(gc, ds_aqv[d], H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f,
                     st);
       }
-      launch_gemm(b.d_desc, b.d_tiles, ds_kdv[d], H, b.Kd, vk, b.Vn, vv, b.states, DkDv, 1.f, 0.f, st);
+      launch_gemm(gc, ds_kdv[d], H, b.Kd, vk, b.Vn, vv, b.states, DkDv, 1.f, 0.f, st);
       state_decay_add<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
           H, DkDv, n, b.d_level_nodes + level_first[d], b.d_parent, b.gl, b.states);
       ++launches;
@@ -982,6 +1035,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
                                  b.states + (long long)(cap_nodes[i] + 1) * sh, sh * 4,
                                  cudaMemcpyDeviceToDevice, st));
     tt_count_launches(launches);
+    if (gc.rc != TT_OK) return gc.rc;
     return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
   }
   // ---------------------------------------------------------------- backward
@@ -992,41 +1046,37 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     gather_dstate<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
         H, DkDv, n, b.d_level_nodes + level_first[d], b.d_child_ptr, b.d_child_idx, b.dSi, dlast,
         b.d_cap_slot, dcaptured, b.dSo);
-    launch_gemm(b.d_desc, b.d_tiles, ds_dvn1[d], H, b.Aqk, llh, b.dO, vv, b.dVn, vv, 1.f, 0.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_dvn2[d], H, b.Kd, vk, b.dSo, DkDv, b.dVn, vv, 1.f, 1.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_dsi1[d], H, b.Qg, vk, b.dO, vv, b.dSi, DkDv, 1.f, 0.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_dsi2[d], H, b.W, vk, b.dVn, vv, b.dSi, DkDv, -1.f, 1.f, st);
+    launch_gemm(gc, ds_dvn1[d], H, b.Aqk, llh, b.dO, vv, b.dVn, vv, 1.f, 0.f, st);
+    launch_gemm(gc, ds_dvn2[d], H, b.Kd, vk, b.dSo, DkDv, b.dVn, vv, 1.f, 1.f, st);
+    launch_gemm(gc, ds_dsi1[d], H, b.Qg, vk, b.dO, vv, b.dSi, DkDv, 1.f, 0.f, st);
+    launch_gemm(gc, ds_dsi2[d], H, b.W, vk, b.dVn, vv, b.dSi, DkDv, -1.f, 1.f, st);
     dstate_decay<<<dim3(cnt, H), 256, 0, st>>>(H, DkDv, n, b.d_level_nodes + level_first[d],
                                                b.d_parent, b.gl, b.states, b.dSo, b.dSi, b.dgl);
     launches += 2;
   }
   // per-node gradients, no more dependencies between nodes
-  launch_gemm(b.d_desc, b.d_tiles, ds_dqg, H, b.dO, vv, b.states, DkDv, b.dQg, vk, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_dkd, H, b.Vn, vv, b.dSo, DkDv, b.dKd, vk, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_dw, H, b.dVn, vv, b.states, DkDv, b.dW, vk, -1.f, 0.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_daqk, H, b.dO, vv, b.Vn, vv, b.dAqk, llh, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_dt1, H, b.dVn, vv, b.Vb, vv, b.dT, llh, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_dt2, H, b.dW, vk, b.Kbg, vk, b.dT, llh, 1.f, 1.f, st);
+  launch_gemm(gc, ds_dqg, H, b.dO, vv, b.states, DkDv, b.dQg, vk, 1.f, 0.f, st);
+  launch_gemm(gc, ds_dkd, H, b.Vn, vv, b.dSo, DkDv, b.dKd, vk, 1.f, 0.f, st);
+  launch_gemm(gc, ds_dw, H, b.dVn, vv, b.states, DkDv, b.dW, vk, -1.f, 0.f, st);
+  launch_gemm(gc, ds_daqk, H, b.dO, vv, b.Vn, vv, b.dAqk, llh, 1.f, 0.f, st);
+  launch_gemm(gc, ds_dt1, H, b.dVn, vv, b.Vb, vv, b.dT, llh, 1.f, 0.f, st);
+  launch_gemm(gc, ds_dt2, H, b.dW, vk, b.Kbg, vk, b.dT, llh, 1.f, 1.f, st);
   if (exact) {
     // Am holds T = (I - A)^-1:  dA = T^T dT T^T (masked in grad_masks);
     // dVb = T^T dVn;  dKbg = T^T dW
-    launch_gemm(b.d_desc, b.d_tiles, ds_x2, H, b.Am, llh, b.dT, llh, b.X, llh, 1.f, 0.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_x1, H, b.X, llh, b.Am, llh, b.dA, llh, 1.f, 0.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_tvt, H, b.Am, llh, b.dVn, vv, b.dVb, vv, 1.f, 0.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_tkt, H, b.Am, llh, b.dW, vk, b.dKbg, vk, 1.f, 0.f, st);
+    launch_gemm(gc, ds_x2, H, b.Am, llh, b.dT, llh, b.X, llh, 1.f, 0.f, st);
+    launch_gemm(gc, ds_x1, H, b.X, llh, b.Am, llh, b.dA, llh, 1.f, 0.f, st);
+    launch_gemm(gc, ds_tvt, H, b.Am, llh, b.dVn, vv, b.dVb, vv, 1.f, 0.f, st);
+    launch_gemm(gc, ds_tkt, H, b.Am, llh, b.dW, vk, b.dKbg, vk, 1.f, 0.f, st);
   } else {
     // dA = dT + dT A^T + A^T dT  (masked in grad_masks)
-    copy_array<<<blocks(H * llh), 256, 0, st>>>(H * llh, b.dT, b.dA);
-    launch_gemm(b.d_desc, b.d_tiles, ds_x1, H, b.dT, llh, b.Am, llh, b.dA, llh, 1.f, 1.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_x2, H, b.Am, llh, b.dT, llh, b.dA, llh, 1.f, 1.f, st);
-    // dVb = T^T dVn = dVn + A^T dVn + A^T (A^T dVn);  dKbg = T^T dW
-    launch_gemm(b.d_desc, b.d_tiles, ds_tvt, H, b.Am, llh, b.dVn, vv, b.T1, vv, 1.f, 0.f, st);
-    add_arrays<<<blocks(H * vv), 256, 0, st>>>(H * vv, b.dVn, b.T1, b.dVb);
-    launch_gemm(b.d_desc, b.d_tiles, ds_tvt, H, b.Am, llh, b.T1, vv, b.dVb, vv, 1.f, 1.f, st);
-    launch_gemm(b.d_desc, b.d_tiles, ds_tkt, H, b.Am, llh, b.dW, vk, b.T1, vk, 1.f, 0.f, st);
-    add_arrays<<<blocks(H * vk), 256, 0, st>>>(H * vk, b.dW, b.T1, b.dKbg);
-    launch_gemm(b.d_desc, b.d_tiles, ds_tkt, H, b.Am, llh, b.T1, vk, b.dKbg, vk, 1.f, 1.f, st);
-    launches += 3;
+    launch_gemm(gc, ds_x1, H, b.dT, llh, b.Am, llh, b.dA, llh, 1.f, 1.f, st, b.dT);
+    launch_gemm(gc, ds_x2, H, b.Am, llh, b.dT, llh, b.dA, llh, 1.f, 1.f, st);
+    // dVb = T^T dVn = dVn + A^T (dVn + A^T dVn);  dKbg = T^T dW likewise
+    launch_gemm(gc, ds_tvt, H, b.Am, llh, b.dVn, vv, b.T1, vv, 1.f, 1.f, st, b.dVn);
+    launch_gemm(gc, ds_tvt, H, b.Am, llh, b.T1, vv, b.dVb, vv, 1.f, 1.f, st, b.dVn);
+    launch_gemm(gc, ds_tkt, H, b.Am, llh, b.dW, vk, b.T1, vk, 1.f, 1.f, st, b.dW);
+    launch_gemm(gc, ds_tkt, H, b.Am, llh, b.T1, vk, b.dKbg, vk, 1.f, 1.f, st, b.dW);
   }
   // masks: dA -> G = -dA*D, dAqk -> F = dAqk*D, dDD
   TT_CUDA_OK(cudaMemsetAsync(b.dgam, 0, (size_t)H * S * 4, st));
@@ -1036,10 +1086,10 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
                                                 b.dgam);
   launches += 2;
   // dKb = G K ; dK = G^T Kb + F^T Q ; dQ = F K
-  launch_gemm(b.d_desc, b.d_tiles, ds_gk, H, b.dA, llh, b.K, vk, b.dKb, vk, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_gtk, H, b.dA, llh, b.Kb, vk, b.dK, vk, 1.f, 0.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_gtk, H, b.dAqk, llh, b.Q, vk, b.dK, vk, 1.f, 1.f, st);
-  launch_gemm(b.d_desc, b.d_tiles, ds_gk, H, b.dAqk, llh, b.K, vk, b.dQ, vk, 1.f, 0.f, st);
+  launch_gemm(gc, ds_gk, H, b.dA, llh, b.K, vk, b.dKb, vk, 1.f, 0.f, st);
+  launch_gemm(gc, ds_gtk, H, b.dA, llh, b.Kb, vk, b.dK, vk, 1.f, 0.f, st);
+  launch_gemm(gc, ds_gtk, H, b.dAqk, llh, b.Q, vk, b.dK, vk, 1.f, 1.f, st);
+  launch_gemm(gc, ds_gk, H, b.dAqk, llh, b.K, vk, b.dQ, vk, 1.f, 0.f, st);
   kd_dot_kernel<<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(S, Dk, b.Kd, b.dKd, b.kd_dot);
   assemble_token_grads<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(
       S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok, l2norm, q_scale, b.dQ, b.dQg, b.dK,
@@ -1054,6 +1104,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     ++launches;
   }
   tt_count_launches(launches);
+  if (gc.rc != TT_OK) return gc.rc;
   return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
 }
 
@@ -1073,6 +1124,63 @@ int dispatch(int dtype, Fn fn) {
 
 using tt::gdn::Arena;
 using tt::gdn::Plan;
+
+extern "C" int64_t tt_gdn_segmented_gemm_workspace_size(int32_t n_segs, const int64_t* segs) {
+  if (n_segs < 0 || (n_segs > 0 && !segs)) return -1;
+  int64_t tiles = 0;
+  for (int i = 0; i < n_segs; ++i) {
+    const int64_t M = segs[13 * i], N = segs[13 * i + 1];
+    if (M < 0 || N < 0 || M > 65535 * 64 || N > 65535 * 64) return -1;
+    tiles += ((M + 63) / 64) * ((N + 63) / 64);
+  }
+  return ((int64_t)n_segs * (int64_t)sizeof(tt::gdn::SegDesc) + 255) / 256 * 256 +
+         (tiles * 8 + 255) / 256 * 256 * 2;
+}
+
+extern "C" int tt_gdn_segmented_gemm(int engine, int32_t n_segs, const int64_t* segs, int32_t H,
+                                     const float* A, int64_t a_hs, const float* B, int64_t b_hs,
+                                     float* C, int64_t c_hs, float alpha, float beta,
+                                     void* workspace, int64_t workspace_bytes, void* stream) {
+  using namespace tt::gdn;
+  if (engine < 0 || engine > 3 || engine == 2 || n_segs < 0 || H <= 0 ||
+      (n_segs > 0 && (!segs || !A || !B || !C)))
+    return TT_ERR_INVALID_ARG;
+  const int64_t need = tt_gdn_segmented_gemm_workspace_size(n_segs, segs);
+  if (need < 0) return TT_ERR_INVALID_ARG;
+  if (workspace_bytes < need || (n_segs > 0 && !workspace)) return TT_ERR_WORKSPACE;
+  if (n_segs == 0) return TT_OK;
+  Plan dummy;
+  Builder bd(dummy);
+  std::vector<SegDesc> v(n_segs);
+  for (int i = 0; i < n_segs; ++i) {
+    const int64_t* e = segs + 13 * i;
+    if (e[2] < 0 || e[3] < kKFull || e[3] > kKFromCol) return TT_ERR_INVALID_ARG;
+    v[i] = desc((int)e[0], (int)e[1], (int)e[2], e[4], e[5], e[6], e[7], e[8], e[9], e[10],
+                e[11], e[12], (int)e[3]);
+  }
+  const DescSet ds = bd.add(v);
+  Arena ar{(char*)workspace, workspace_bytes, 0, false};
+  SegDesc* d_desc = ar.get<SegDesc>(n_segs);
+  int2* d_tiles = ar.get<int2>((long long)bd.tiles.size());
+  int2* d_tiles_tc = ar.get<int2>((long long)bd.tiles_tc.size());
+  cudaStream_t st = (cudaStream_t)stream;
+  TT_CUDA_OK(cudaMemcpyAsync(d_desc, bd.all.data(), n_segs * sizeof(SegDesc),
+                             cudaMemcpyHostToDevice, st));
+  if (!bd.tiles.empty())
+    TT_CUDA_OK(cudaMemcpyAsync(d_tiles, bd.tiles.data(), bd.tiles.size() * sizeof(int2),
+                               cudaMemcpyHostToDevice, st));
+  if (!bd.tiles_tc.empty())
+    TT_CUDA_OK(cudaMemcpyAsync(d_tiles_tc, bd.tiles_tc.data(), bd.tiles_tc.size() * sizeof(int2),
+                               cudaMemcpyHostToDevice, st));
+  // engine 0 = CUDA cores; 1 / 3 = tensor cores with TF32 / 3xTF32 products
+  GemmCtx gc{d_desc, d_tiles, d_tiles_tc, &bd.all, engine};
+  if (engine != 0 && !tt_gdn_tc_gemm_supported(bd.all.data(), 0, n_segs, A, a_hs, B, b_hs, C, c_hs))
+    return TT_ERR_UNSUPPORTED;
+  launch_gemm(gc, ds, H, A, a_hs, B, b_hs, C, c_hs, alpha, beta, st);
+  if (gc.rc != TT_OK) return gc.rc;
+  TT_CUDA_OK(cudaStreamSynchronize(st));
+  return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
+}
 
 extern "C" int64_t tt_gdn_tree_workspace_size(int32_t S, int32_t H, int32_t Dk, int32_t Dv,
                                               int32_t n_nodes, const int32_t* bounds,
@@ -1184,4 +1292,14 @@ extern "C" int tt_gdn_tree_bwd(int dtype, int32_t S, int32_t Hk, int32_t H, int3
 
 extern "C" int64_t tt_gdn_gemm_flops(void) {
   return tt::gdn::g_gemm_flops.load(std::memory_order_relaxed);
+}
+
+extern "C" int64_t tt_gdn_gemm_tc_flops(void) {
+  return tt::gdn::g_gemm_tc_flops.load(std::memory_order_relaxed);
+}
+
+extern "C" int tt_gdn_set_gemm_mode(int mode) {
+  const int prev = tt::gdn::gemm_mode();
+  tt::gdn::g_gemm_mode.store(mode == 1 || mode == 2 ? mode : 0);
+  return prev;
 }

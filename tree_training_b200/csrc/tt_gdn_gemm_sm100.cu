@@ -1,0 +1,501 @@
+// Segmented fp32 GEMM of the tree GDN on the 5th-generation tensor cores.
+//
+// The tree GDN (tt_gdn.cu) expresses each node's chunk step as small GEMMs
+// over that node's tokens (L x L, L x D and D x D products, any node length),
+// batched over all nodes of a level and all heads as one list of 128 x 128
+// output tiles.  This kernel runs such a list with tcgen05.mma kind::tf32:
+//
+//   warps 0-3  producers: stream each tile's K range as 32-wide slices of A
+//              (128 x 32) and B (32 x 128) into a ring of shared-memory
+//              stages with 16-byte cp.async copies (zero-filled past the
+//              segment's edges), laid out in the swizzled canonical forms
+//              the MMA reads: K-major (128-byte swizzle) when the operand is
+//              contiguous along K in global memory, MN-major (128-byte
+//              swizzle on a 32-byte base, the one MN-major form for 32-bit
+//              operands) when it is contiguous along M (or N).  In 3xTF32 mode each producer then splits the
+//              elements it copied into a TF32 head (round to nearest) and a
+//              TF32 tail, written to a second copy of the stage.
+//   warp 8     MMA issuer: 4 MMAs of 128 x 128 x 8 per slice (12 in 3xTF32
+//              mode: lo*hi, hi*lo, hi*hi) into one of two TMEM accumulators,
+//              then releases the stage; at the end of a tile it hands the
+//              accumulator to the epilogue and moves on to the next tile in
+//              the other one.
+//   warps 4-7  epilogue: one thread per accumulator row (TMEM lane): C =
+//              alpha * acc + beta * Cin (Cin defaults to C) with 16-byte
+//              loads and stores.
+//
+// The CTAs are persistent (one per SM, tiles x heads dealt round robin), so
+// the slices of the next tile stream in while the current one finishes.
+// Every wait is bounded (2 s); on expiry the kernel records
+// TT_ERR_DEVICE_TIMEOUT in a device status word, drains its copies and MMAs,
+// frees its tensor memory and returns.
+#include <mutex>
+
+#include "tt_gdn_gemm.cuh"
+#include "tt_sm100.cuh"
+
+namespace tt {
+namespace gdn {
+namespace {
+
+using namespace tt::sm100;
+
+constexpr int kTM = kTcTile, kTN = kTcTile, kTK = 32;   // tile, K slice (fp32 elements)
+constexpr int kProducerWarps = 4, kEpilogueWarps = 4;
+constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;   // warp 8
+constexpr int kThreads = (kMmaWarp + 1) * 32;
+constexpr int kProducers = kProducerWarps * 32;
+constexpr int kOpBytes = kTM * kTK * 4;                 // one 128 x 32 fp32 operand slice
+constexpr int kChunksPerThread = kOpBytes / 16 / kProducers;   // 16-byte chunks (8)
+constexpr uint32_t kTmemCols = 256;                     // two 128-column accumulators
+constexpr int kMaxStages = 6;
+
+template <int kSplit>
+struct Ring {
+  static constexpr int kStageBytes = (kSplit == 3 ? 4 : 2) * kOpBytes;   // A, B (+ lo copies)
+  static constexpr int kStages = kSplit == 3 ? 3 : 6;
+  static constexpr int kLag = kStages - 1;   // slices in flight per producer thread
+};
+
+struct Bars {
+  uint64_t full[kMaxStages];    // producers -> MMA (kProducers arrivals)
+  uint64_t empty[kMaxStages];   // MMA -> producers (commit)
+  uint64_t acc_full[2];         // MMA -> epilogue (commit)
+  uint64_t acc_empty[2];        // epilogue -> MMA (128 arrivals)
+  uint64_t drain;
+  uint32_t tmem_base;
+  int32_t abort;
+};
+
+template <int kSplit>
+constexpr size_t smem_bytes() {
+  return 1024 + (size_t)Ring<kSplit>::kStages * Ring<kSplit>::kStageBytes + sizeof(Bars);
+}
+
+__device__ int32_t g_status;   // first error of any launch since the last take
+
+__device__ __forceinline__ void record_error(Bars* sh, int32_t code) {
+  atomicCAS(&g_status, 0, code);
+  *reinterpret_cast<volatile int32_t*>(&sh->abort) = 1;
+}
+
+// 16-byte global -> shared copy of `bytes` (0, 4, 8, 12 or 16) source bytes;
+// the rest of the 16 destination bytes is zero-filled.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// The K slices [k_begin, k_begin + n * kTK) of a tile that can hold nonzero
+// products (the segment's triangular structure, kKFull ... kKFromCol).
+__device__ __forceinline__ void k_range(const SegDesc& sd, int i0, int j0, int& kb, int& n) {
+  int ke = sd.K;
+  kb = 0;
+  switch (sd.kmode) {
+    case kKToRow: ke = min(ke, i0 + kTM); break;
+    case kKFromRow: kb = i0; break;
+    case kKToCol: ke = min(ke, j0 + kTN); break;
+    case kKFromCol: kb = j0; break;
+    default: break;
+  }
+  n = ke > kb ? (ke - kb + kTK - 1) / kTK : 0;
+}
+
+// x rounded to TF32 (nearest, ties away), as an fp32 bit pattern: the
+// conversion leaves the 13 low mantissa bits unspecified, so they are cleared.
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r & 0xFFFFE000u;
+}
+
+// kind::tf32 instruction descriptor: fp32 accumulator, TF32 A and B, M = N = 128.
+__device__ __forceinline__ uint32_t idesc_tf32(bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) |
+         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(kTN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// Byte offset, within one operand slice, of this thread's i-th 16-byte chunk
+// and the (mn, k) coordinates of its first element.
+//   K-major (128-byte swizzle): 128 rows (mn) of 32 k, 128-byte rows, 8-row
+//     atoms of 1 KiB; 16-byte chunk c of row r sits at chunk c ^ (r & 7).
+//   MN-major (128-byte swizzle on a 32-byte base, the layout the tensor core
+//     takes for 32-bit MN-major operands): four 32-element mn blocks 4 KiB
+//     apart, each 32 k-rows of 128 bytes in 4-row atoms of 512 bytes; 32-byte
+//     granule g of row k sits at granule g ^ (k & 3).
+__device__ __forceinline__ uint32_t chunk_at(bool k_contig, int q, int& mn, int& k) {
+  if (k_contig) {
+    const int r = q >> 3, kc = q & 7;
+    mn = r;
+    k = kc * 4;
+    return (uint32_t)(r * 128 + ((kc ^ (r & 7)) << 4));
+  }
+  const int kr = q >> 5, mc = q & 31, j = mc & 7;
+  mn = mc * 4;
+  k = kr;
+  return (uint32_t)((mc >> 3) * 4096 + kr * 128 + ((((j >> 1) ^ (kr & 3)) << 5) | ((j & 1) << 4)));
+}
+
+// Shared-memory descriptor of an MN-major 32-bit operand in the layout above:
+// lead = bytes between 32-element mn blocks, stride = bytes between 4-row k
+// atoms, layout type 1 (128-byte swizzle, 32-byte base).
+__device__ __forceinline__ uint64_t desc_mn32(uint32_t saddr, uint32_t lbo_bytes,
+                                              uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  d |= (uint64_t)1 << 61;  // SWIZZLE_128B_BASE32B
+  return d;
+}
+
+// Descriptor of operand slice `addr` for the MMA of K step kk (8 k each).
+__device__ __forceinline__ uint64_t op_desc(uint32_t addr, bool k_contig, int kk) {
+  // K-major: +32 bytes per K step inside the 128-byte rows; MN-major: +8 rows
+  return k_contig ? desc_sw128(addr + kk * 32, 16, 1024)
+                  : desc_mn32(addr + kk * 1024, 4096, 512);
+}
+
+// Issue this thread's copies of one operand slice: element (mn, k) of the
+// operand at base + mn * mn_st + k * k_st, mn < mn_ext, k < k_ext.
+__device__ __forceinline__ void copy_slice(uint32_t dst, const float* base, int mn0, int mn_ext,
+                                           int k0, int k_ext, long long mn_st, long long k_st,
+                                           bool k_contig, int tid) {
+#pragma unroll
+  for (int i = 0; i < kChunksPerThread; ++i) {
+    int mn, k;
+    const uint32_t off = chunk_at(k_contig, i * kProducers + tid, mn, k);
+    mn += mn0;
+    k += k0;
+    int n_el;
+    if (k_contig)
+      n_el = mn < mn_ext ? min(max(k_ext - k, 0), 4) : 0;
+    else
+      n_el = k < k_ext ? min(max(mn_ext - mn, 0), 4) : 0;
+    const float* src = n_el > 0 ? base + (long long)mn * mn_st + (long long)k * k_st : base;
+    cp_async16(dst + off, src, (uint32_t)n_el * 4u);
+  }
+}
+
+// 3xTF32: replace this thread's chunks of an operand slice by their rounded
+// TF32 heads and write the TF32 tails 2 * kOpBytes further on.
+__device__ __forceinline__ void split_slice(uint8_t* op, bool k_contig, int tid) {
+#pragma unroll
+  for (int i = 0; i < kChunksPerThread; ++i) {
+    int mn, k;
+    const uint32_t off = chunk_at(k_contig, i * kProducers + tid, mn, k);
+    float4* hp = reinterpret_cast<float4*>(op + off);
+    float4* lp = reinterpret_cast<float4*>(op + off + 2 * kOpBytes);
+    const float4 a = *hp;
+    const uint32_t h0 = to_tf32(a.x), h1 = to_tf32(a.y), h2 = to_tf32(a.z), h3 = to_tf32(a.w);
+    const float4 hi = make_float4(__uint_as_float(h0), __uint_as_float(h1), __uint_as_float(h2),
+                                  __uint_as_float(h3));
+    const float4 lo = make_float4(__uint_as_float(to_tf32(a.x - hi.x)),
+                                  __uint_as_float(to_tf32(a.y - hi.y)),
+                                  __uint_as_float(to_tf32(a.z - hi.z)),
+                                  __uint_as_float(to_tf32(a.w - hi.w)));
+    *hp = hi;
+    *lp = lo;
+  }
+}
+
+template <int kSplit>
+__global__ void __launch_bounds__(kThreads, 1)
+seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, int n_tiles, int H,
+            const float* __restrict__ A, long long a_hs, const float* __restrict__ B,
+            long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin) {
+  using R = Ring<kSplit>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  Bars* sh = reinterpret_cast<Bars*>(ring + (size_t)R::kStages * R::kStageBytes);
+  const volatile int32_t* abort_flag = &sh->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_items = n_tiles * H;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < R::kStages; ++s) {
+      mbar_init(&sh->full[s], kProducers);
+      mbar_init(&sh->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh->acc_full[b], 1);
+      mbar_init(&sh->acc_empty[b], kEpilogueWarps * 32);
+    }
+    mbar_init(&sh->drain, 1);
+    sh->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&sh->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+
+  if (warp < kProducerWarps) {
+    // -------------------------------------------------------------- producers
+    const int tid = threadIdx.x;
+    uint32_t slot = 0;       // slices issued so far (all items)
+    uint32_t done = 0;       // slices handed to the MMA so far
+    uint32_t layouts = 0;    // 2 bits per ring stage: A K-contiguous, B K-contiguous
+    bool ok = true;
+    // hand slice `done` to the MMA once this thread's copies of it landed
+    auto finish = [&](void) {
+      const int s = done % R::kStages;
+      if constexpr (kSplit == 3) {
+        uint8_t* st = ring + (size_t)s * R::kStageBytes;
+        const uint32_t lay = layouts >> (2 * s);
+        split_slice(st, lay & 1u, tid);
+        split_slice(st + kOpBytes, (lay >> 1) & 1u, tid);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&sh->full[s]);
+      ++done;
+    };
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const int2 tl = tiles[item / H];
+      const int h = item % H;
+      const SegDesc sd = segs[tl.x];
+      const int i0 = (tl.y >> 16) * kTM, j0 = (tl.y & 0xFFFF) * kTN;
+      const float* a = A + h * a_hs + sd.a_off;
+      const float* b = B + h * b_hs + sd.b_off;
+      const bool a_kc = sd.a_cs == 1, b_kc = sd.b_rs == 1;
+      int kb, nk;
+      k_range(sd, i0, j0, kb, nk);
+      for (int t = 0; t < nk; ++t, ++slot) {
+        const int s = slot % R::kStages;
+        if (slot >= (uint32_t)R::kStages &&
+            !mbar_wait(&sh->empty[s], ((slot / R::kStages) - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t st = smem_u32(ring + (size_t)s * R::kStageBytes);
+        // A(r, k) at r * a_rs + k * a_cs; B(k, n) at k * b_rs + n * b_cs
+        copy_slice(st, a, i0, sd.M, kb + t * kTK, sd.K, sd.a_rs, sd.a_cs, a_kc, tid);
+        copy_slice(st + kOpBytes, b, j0, sd.N, kb + t * kTK, sd.K, sd.b_cs, sd.b_rs, b_kc, tid);
+        cp_async_commit();
+        layouts = (layouts & ~(3u << (2 * s))) | ((a_kc ? 1u : 0u) << (2 * s)) |
+                  ((b_kc ? 2u : 0u) << (2 * s));
+        if (slot + 1 - done > (uint32_t)R::kLag) {
+          cp_async_wait<R::kLag - 1>();
+          finish();
+        }
+      }
+    }
+    cp_async_wait<0>();
+    if (ok) {
+      while (done < slot) finish();
+    } else {
+      record_error(sh, TT_ERR_DEVICE_TIMEOUT);
+    }
+  } else if (warp == kMmaWarp) {
+    // -------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      uint32_t slot = 0;
+      int acc_i = 0;
+      bool ok = true;
+      const uint32_t ring0 = smem_u32(ring);
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++acc_i) {
+        const int2 tl = tiles[item / H];
+        const SegDesc sd = segs[tl.x];
+        const bool a_kc = sd.a_cs == 1, b_kc = sd.b_rs == 1;
+        int kb, nk;
+        k_range(sd, (tl.y >> 16) * kTM, (tl.y & 0xFFFF) * kTN, kb, nk);
+        const int buf = acc_i & 1;
+        if (acc_i >= 2 && !mbar_wait(&sh->acc_empty[buf], ((acc_i >> 1) - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * kTN;
+        const uint32_t idesc = idesc_tf32(!a_kc, !b_kc);
+        for (int t = 0; t < nk; ++t, ++slot) {
+          const int s = slot % R::kStages;
+          if (!mbar_wait(&sh->full[s], (slot / R::kStages) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = ring0 + s * R::kStageBytes, sb = sa + kOpBytes;
+#pragma unroll
+          for (int kk = 0; kk < kTK / 8; ++kk) {
+            const uint64_t da = op_desc(sa, a_kc, kk);
+            const uint64_t db = op_desc(sb, b_kc, kk);
+            const uint32_t acc0 = (t > 0 || kk > 0) ? 1u : 0u;
+            if constexpr (kSplit == 3) {
+              const uint64_t da_lo = op_desc(sa + 2 * kOpBytes, a_kc, kk);
+              const uint64_t db_lo = op_desc(sb + 2 * kOpBytes, b_kc, kk);
+              mma_tf32(d, da_lo, db, idesc, acc0);
+              mma_tf32(d, da, db_lo, idesc, 1u);
+              mma_tf32(d, da, db, idesc, 1u);
+            } else {
+              mma_tf32(d, da, db, idesc, acc0);
+            }
+          }
+          tc_commit(&sh->empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&sh->acc_full[buf]);
+      }
+      if (!ok) record_error(sh, TT_ERR_DEVICE_TIMEOUT);
+      // every MMA issued has completed before the accumulators are freed
+      tc_commit(&sh->drain);
+      mbar_wait(&sh->drain, 0, nullptr);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int quad = warp & 3;                 // TMEM lane quadrant of this warp
+    const int r = quad * 32 + lane;            // accumulator row
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    int acc_i = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++acc_i) {
+      const int2 tl = tiles[item / H];
+      const int h = item % H;
+      const SegDesc sd = segs[tl.x];
+      const int i0 = (tl.y >> 16) * kTM, j0 = (tl.y & 0xFFFF) * kTN;
+      const int buf = acc_i & 1;
+      bool ok = mbar_wait(&sh->acc_full[buf], (acc_i >> 1) & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        record_error(sh, TT_ERR_DEVICE_TIMEOUT);
+        break;
+      }
+      tc_fence_after();
+      int kb, nk;
+      k_range(sd, i0, j0, kb, nk);
+      const bool empty_k = nk == 0;            // no MMA wrote this accumulator
+      const int gi = i0 + r;
+      float* crow = C + h * c_hs + sd.c_off + (long long)gi * sd.c_rs;
+      const float* cinrow = (Cin ? Cin : C) + h * c_hs + sd.c_off + (long long)gi * sd.c_rs;
+#pragma unroll 1
+      for (int cc = 0; cc < kTN / 32; ++cc) {
+        float v[32];
+        tmem_ld32(lane_addr + buf * kTN + cc * 32, v);
+        if (gi < sd.M) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int gj = j0 + cc * 32 + j * 4;
+            if (gj < sd.N) {
+              float4 o = empty_k ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                 : make_float4(alpha * v[4 * j], alpha * v[4 * j + 1],
+                                               alpha * v[4 * j + 2], alpha * v[4 * j + 3]);
+              float4* cp = reinterpret_cast<float4*>(crow + gj);
+              if (beta != 0.f) {
+                const float4 old = *reinterpret_cast<const float4*>(cinrow + gj);
+                o.x += beta * old.x;
+                o.y += beta * old.y;
+                o.z += beta * old.z;
+                o.w += beta * old.w;
+              }
+              *cp = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sh->acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+constexpr int kMaxDevices = 64;
+int g_sms[kMaxDevices];
+bool g_attr_set[kMaxDevices][2];
+std::mutex g_mu;
+
+}  // namespace
+}  // namespace gdn
+}  // namespace tt
+
+using tt::gdn::SegDesc;
+
+bool tt_gdn_tc_gemm_supported(const SegDesc* d, int first, int count, const float* A,
+                              long long a_hs, const float* B, long long b_hs, const float* C,
+                              long long c_hs) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al(A) || !al(B) || !al(C) || (a_hs & 3) || (b_hs & 3) || (c_hs & 3)) return false;
+  for (int i = first; i < first + count; ++i) {
+    const SegDesc& s = d[i];
+    const bool a_ok = (s.a_cs == 1 && (s.a_rs & 3) == 0) || (s.a_rs == 1 && (s.a_cs & 3) == 0);
+    const bool b_ok = (s.b_rs == 1 && (s.b_cs & 3) == 0) || (s.b_cs == 1 && (s.b_rs & 3) == 0);
+    if (!a_ok || !b_ok || s.c_cs != 1 || (s.c_rs & 3) || (s.a_off & 3) || (s.b_off & 3) ||
+        (s.c_off & 3))
+      return false;
+  }
+  return true;
+}
+
+int tt_gdn_seg_gemm_tc(const SegDesc* d_desc, const int2* d_tiles, int n_tiles, int H,
+                       const float* A, long long a_hs, const float* B, long long b_hs, float* C,
+                       long long c_hs, float alpha, float beta, const float* Cin, int split,
+                       cudaStream_t st) {
+  using namespace tt::gdn;
+  if (n_tiles <= 0 || H <= 0) return TT_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TT_ERR_CUDA;
+  const int si = split == 3 ? 1 : 0;
+  const size_t smem = split == 3 ? smem_bytes<3>() : smem_bytes<1>();
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_sms[dev] == 0 &&
+        cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return TT_ERR_CUDA;
+    if (!g_attr_set[dev][si]) {
+      const cudaError_t e =
+          split == 3 ? cudaFuncSetAttribute(seg_gemm_tc<3>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                     : cudaFuncSetAttribute(seg_gemm_tc<1>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return TT_ERR_CUDA;
+      g_attr_set[dev][si] = true;
+    }
+  }
+  const long long items = (long long)n_tiles * H;
+  const int grid = (int)std::min<long long>(items, g_sms[dev]);
+  if (split == 3)
+    seg_gemm_tc<3><<<grid, kThreads, smem, st>>>(d_desc, d_tiles, n_tiles, H, A, a_hs, B, b_hs,
+                                                  C, c_hs, alpha, beta, Cin);
+  else
+    seg_gemm_tc<1><<<grid, kThreads, smem, st>>>(d_desc, d_tiles, n_tiles, H, A, a_hs, B, b_hs,
+                                                  C, c_hs, alpha, beta, Cin);
+  return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
+}
+
+extern "C" int tt_gdn_take_device_status(int32_t* out) {
+  if (!out) return TT_ERR_INVALID_ARG;
+  int32_t v = 0;
+  if (cudaMemcpyFromSymbol(&v, tt::gdn::g_status, sizeof(v)) != cudaSuccess) return TT_ERR_CUDA;
+  if (v != 0) {
+    const int32_t zero = 0;
+    if (cudaMemcpyToSymbol(tt::gdn::g_status, &zero, sizeof(zero)) != cudaSuccess)
+      return TT_ERR_CUDA;
+  }
+  *out = v;
+  return TT_OK;
+}

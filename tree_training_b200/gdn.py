@@ -203,8 +203,11 @@ def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_b
                                     bool(output_final_state), _NO_CAPTURE, bool(keep_forward))
         outs.append(o)
         lasts.append(last)
-    core = torch.stack(outs, 0)
-    last_state = torch.stack(lasts, 0) if output_final_state else None
+    # batch 1 (every tree of the reference): a view, not a copy
+    core = outs[0].unsqueeze(0) if B == 1 else torch.stack(outs, 0)
+    last_state = None
+    if output_final_state:
+        last_state = lasts[0].unsqueeze(0) if B == 1 else torch.stack(lasts, 0)
     return core, last_state
 
 
@@ -306,7 +309,7 @@ def tree_conv(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor
     b = bias.float().contiguous() if has_b else w.new_empty(0)
     outs = [_conv_fwd_op(x[i].contiguous(), w, b, has_b, plan.pred, plan.succ_ptr,
                          plan.succ_tok, plan.succ_lag) for i in range(x.shape[0])]
-    return torch.stack(outs, 0)
+    return outs[0].unsqueeze(0) if len(outs) == 1 else torch.stack(outs, 0)
 
 
 def _tree_correct_conv_varlen(ssm, mixed_qkv_raw, chunk_boundaries, chunk_parent_map):
