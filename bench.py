@@ -34,8 +34,6 @@ import torch  # noqa: E402
 METRIC = "Tree-attn fwd+bwd useful TFLOP/s & tokens/s at 1/2/4/8 B200"
 HQ, HKV, D = 32, 8, 128
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# nominal fp32 FMA rate: 148 SMs x 128 lanes x 2 flop x 1.965 GHz (not a measured figure)
-FP32_FMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 
 
 def parse():
@@ -748,6 +746,16 @@ def gdn_bytes_per_token():
     return 3 * fwd
 
 
+def _split_qkv(y, S):
+    """The conv output [1, C, S] as q, k [1, S, Hk, D] and v [1, S, H, D], the
+    way the Qwen3.5 GatedDeltaNet layer splits it (transpose, torch.split on
+    the channel dim, reshape per head)."""
+    q, k, v = torch.split(y.transpose(1, 2), [GDN_HK * GDN_D, GDN_HK * GDN_D, GDN_H * GDN_D],
+                          dim=-1)
+    return (q.reshape(1, S, GDN_HK, GDN_D), k.reshape(1, S, GDN_HK, GDN_D),
+            v.reshape(1, S, GDN_H, GDN_D))
+
+
 def gdn_cpu_baseline(info, min_tokens: int = 4096):
     """The reference's hybrid-layer core on host cores (oracle/gdn_torch.py:
     tree conv + tree GDN with the reference's row loop, fwd + autograd bwd,
@@ -796,10 +804,7 @@ def run_gdn(args):
         for t in (x, w, gg, bt):
             t.grad = None
         y = tree_conv(x, w, None, bounds, parents)            # [1, C, S]
-        yt = y.transpose(1, 2)
-        q = yt[..., :GDN_HK * GDN_D].reshape(1, S, GDN_HK, GDN_D)
-        k = yt[..., GDN_HK * GDN_D:2 * GDN_HK * GDN_D].reshape(1, S, GDN_HK, GDN_D)
-        v = yt[..., 2 * GDN_HK * GDN_D:].reshape(1, S, GDN_H, GDN_D)
+        q, k, v = _split_qkv(y, S)
         out, _ = torch_chunk_gated_delta_rule_tree_varlen(q, k, v, gg, bt, bounds, parents,
                                                           use_qk_l2norm_in_kernel=True,
                                                           exact_inverse=args.gdn_exact,
@@ -818,6 +823,7 @@ def run_gdn(args):
     clocks.reset()
     launches0 = _lib.lib().tt_kernel_launches()
     gemm0 = _lib.lib().tt_gdn_gemm_flops()
+    gemm_tc0 = _lib.lib().tt_gdn_gemm_tc_flops()
     barrier(world)
     for i in range(args.steps):
         flush.zero_()
@@ -827,6 +833,7 @@ def run_gdn(args):
     torch.cuda.synchronize()
     launches = _lib.lib().tt_kernel_launches() - launches0
     gemm_flops = (_lib.lib().tt_gdn_gemm_flops() - gemm0) / args.steps
+    gemm_tc_flops = (_lib.lib().tt_gdn_gemm_tc_flops() - gemm_tc0) / args.steps
     clk = clocks.stop()
     t = statistics.mean(a.elapsed_time(b) for a, b in ev) / 1e3
     t_max = max_over_ranks(t, world, dev)
@@ -847,10 +854,7 @@ def run_gdn(args):
             dst.copy_(src, non_blocking=True)
         xs, ws, gs, bs = (t_.detach().requires_grad_(True) for t_ in d_in[:4])
         y = tree_conv(xs, ws, None, bounds, parents)
-        yt = y.transpose(1, 2)
-        q = yt[..., :GDN_HK * GDN_D].reshape(1, S, GDN_HK, GDN_D)
-        k = yt[..., GDN_HK * GDN_D:2 * GDN_HK * GDN_D].reshape(1, S, GDN_HK, GDN_D)
-        v = yt[..., 2 * GDN_HK * GDN_D:].reshape(1, S, GDN_H, GDN_D)
+        q, k, v = _split_qkv(y, S)
         out, _ = torch_chunk_gated_delta_rule_tree_varlen(q, k, v, gs, bs, bounds, parents,
                                                           use_qk_l2norm_in_kernel=True,
                                                           exact_inverse=args.gdn_exact,
@@ -892,12 +896,22 @@ def run_gdn(args):
                              "frac": achieved / float(pk["hbm_gbs"]), "traffic": None,
                              "algorithmic_bytes_per_token": gdn_bytes_per_token(),
                              "peak_source": pk_src},
-                # the step is dominated by fp32 segmented GEMMs: their algorithmic
-                # flops per step, and that work's rate over the whole step (a lower
-                # bound on the GEMM kernel's own rate)
+                # the segmented GEMMs (per node: L x L, L x D, D x D products) run on
+                # the tensor cores as TF32 (16-bit inputs) or 3xTF32 (fp32 inputs):
+                # their work per step over the whole step, against the TF32 dense
+                # rate (half the bf16 rate per clock: the measured bf16 burst / 2)
+                "roofline_tensor": {
+                    "bound": "tensor", "kernel": "seg_gemm_tc (all launches of the step)",
+                    "achieved": gemm_tc_flops / t / 1e12,
+                    "peak": float(pk["bf16_tflops"]) / 2, "unit": "TFLOP/s",
+                    "frac": gemm_tc_flops / t / 1e12 / (float(pk["bf16_tflops"]) / 2),
+                    "peak_source": f"{pk_src} bf16 dense burst / 2 (TF32 rate)",
+                    "gflop_per_step": gemm_tc_flops / 1e9,
+                    "note": "GEMM flops = 2 M N K per segment and head, over the whole "
+                            "step's time (a lower bound on the GEMM kernel's own rate)"},
                 "seg_gemm": {"gflop_per_step": gemm_flops / 1e9,
-                             "tflops_over_step": gemm_flops / t / 1e12,
-                             "fp32_fma_peak_tflops": FP32_FMA_PEAK_TFLOPS},
+                             "tensor_core_gflop_per_step": gemm_tc_flops / 1e9,
+                             "tflops_over_step": gemm_flops / t / 1e12},
                 "gpu_launches": int(launches), "clocks": clk,
                 "e2e": {"value": tokens_all / t_e2e, "unit": "tokens/s",
                         "h2d_bytes_per_step": int(h2d_b), "d2h_bytes_per_step": int(d2h_b),

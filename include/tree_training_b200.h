@@ -74,7 +74,9 @@ int64_t tt_gdn_gemm_tc_flops(void);
  *   fp32 operand) when the GDN's inputs are fp32 and TF32 products when they
  *   are bf16/fp16;
  * 1: tensor cores with 3xTF32 products for every input type;
- * 2: the CUDA-core fp32 FMA GEMM.
+ * 2: the CUDA-core fp32 FMA GEMM;
+ * adding 4 to mode 0 or 1 stages the tensor cores' operands with cp.async
+ * copies instead of TMA tile copies (for comparisons).
  * Launches whose operands are not 16-byte aligned use the CUDA-core GEMM. */
 int tt_gdn_set_gemm_mode(int mode);
 
@@ -86,8 +88,9 @@ int tt_gdn_set_gemm_mode(int mode);
  * K range, 1-4 skip the K slices a triangular operand leaves zero (1: A lower,
  * 2: A upper, 3: B upper, 4: B lower triangular).  engine 0 = CUDA-core fp32
  * FMA, 1 = tensor cores with TF32 products, 3 = tensor cores with 3xTF32
- * products (TT_ERR_UNSUPPORTED unless every base is 16-byte aligned, every
- * offset and non-unit stride a multiple of 4, and c_cs == 1).  Device
+ * products, operands staged by TMA; 5 / 7 = the same with cp.async staging
+ * (TT_ERR_UNSUPPORTED unless A's and B's bases are 16-byte aligned,
+ * their offsets and non-unit strides multiples of 4, and c_cs == 1).  Device
  * pointers; synchronises the stream before returning.  Workspace:
  * tt_gdn_segmented_gemm_workspace_size(n_segs, segs) bytes.  No counterpart
  * in the reference (a test hook of the engine behind tt_gdn_tree_fwd/_bwd). */

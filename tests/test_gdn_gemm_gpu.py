@@ -2,8 +2,9 @@
 
 ``tt_gdn_segmented_gemm`` runs one list of segments (C = alpha A B + beta C per
 segment and head) on the CUDA cores (engine 0), or on the tensor cores with
-TF32 (1) or 3xTF32 (3) products: the engine behind every product of
-tt_gdn_tree_fwd/_bwd.  The segments cover both storage orders of A and B
+TF32 (1) or 3xTF32 (3) products, operands staged by TMA through per-segment
+tensor maps (5 and 7: the same staged by cp.async copies): the engine behind
+every product of tt_gdn_tree_fwd/_bwd.  The segments cover both storage orders of A and B
 (contiguous along K or along M/N), ragged sizes around the 128-row tile and
 the 32-wide K slice, empty K, and the triangular K ranges (kmode 1-4) with
 operands that are triangular.
@@ -102,7 +103,7 @@ def _segments(rng, H):
     return np.asarray(rows, np.int64), A.build(H), B.build(H), C.build(H), checks
 
 
-@pytest.mark.parametrize("engine,tol", [(0, 1e-5), (3, 1e-5), (1, 5e-3)])
+@pytest.mark.parametrize("engine,tol", [(0, 1e-5), (3, 1e-5), (1, 5e-3), (7, 1e-5), (5, 5e-3)])
 def test_segmented_gemm_engines_vs_float64(engine, tol):
     H = 2
     rng = np.random.default_rng(engine + 7)

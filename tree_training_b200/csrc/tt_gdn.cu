@@ -245,14 +245,15 @@ __global__ void node_cumsum(int S, int H, int n_nodes, const int* __restrict__ n
 }
 
 // In place on the packed LxL matrices of every node: A = -KK * D (strict
-// lower), Aqk = QK * D (lower incl.).  Raw products are kept in KK/QK.
+// lower), Aqk = QK * D (lower incl.).  Raw products are kept in KK/QK.  One
+// block per (token, head): row j of the token's node.
 __global__ void decay_masks(int S, const int* __restrict__ nstart, const int* __restrict__ nlen,
+                            const int* __restrict__ tok_node,
                             const long long* __restrict__ loff, long long l_hs,
                             const float* __restrict__ gam, const float* __restrict__ KK,
                             const float* __restrict__ QK, float* Am, float* Aqk) {
-  const int c = blockIdx.y, h = blockIdx.z, j = blockIdx.x;
+  const int t = blockIdx.x, h = blockIdx.y, c = tok_node[t], j = t - nstart[c];
   const int L = nlen[c];
-  if (j >= L) return;
   const long long base = h * l_hs + loff[c] + (long long)j * row_stride(L);
   const float gj = gam[(long long)h * S + nstart[c] + j];
   for (int m = threadIdx.x; m < L; m += blockDim.x) {
@@ -384,12 +385,12 @@ __global__ void dstate_decay(int H, int DkDv, int n_nodes, const int* __restrict
 //   F   = dAqk * D (lower incl.; -> dQ += F K, dK += F^T Q)
 //   dDD = (-dA * KK + dAqk * QK) * D, whose row/col sums give dgam.
 __global__ void grad_masks(int S, const int* __restrict__ nstart, const int* __restrict__ nlen,
+                           const int* __restrict__ tok_node,
                            const long long* __restrict__ loff, long long l_hs,
                            const float* __restrict__ gam, const float* __restrict__ KK,
                            const float* __restrict__ QK, float* dA, float* dAqk, float* dDD) {
-  const int c = blockIdx.y, h = blockIdx.z, j = blockIdx.x;
+  const int t = blockIdx.x, h = blockIdx.y, c = tok_node[t], j = t - nstart[c];
   const int L = nlen[c];
-  if (j >= L) return;
   const long long base = h * l_hs + loff[c] + (long long)j * row_stride(L);
   const float gj = gam[(long long)h * S + nstart[c] + j];
   for (int m = threadIdx.x; m < L; m += blockDim.x) {
@@ -402,26 +403,35 @@ __global__ void grad_masks(int S, const int* __restrict__ nstart, const int* __r
   }
 }
 
-// dgam_j += sum_m dDD[j, m] - sum_i dDD[i, j]  (per node, per head)
-__global__ void ddd_rowcol(int S, const int* __restrict__ nstart, const int* __restrict__ nlen,
-                           const long long* __restrict__ loff, long long l_hs,
-                           const float* __restrict__ dDD, float* dgam) {
-  const int c = blockIdx.y, h = blockIdx.z, j = blockIdx.x;
-  const int L = nlen[c], Lp = row_stride(L);
-  if (j >= L) return;
+// dgam_j += sum_m dDD[j, m] - sum_i dDD[i, j]  (per node, per head; dDD is
+// lower triangular).  One block per (node, head): warps take rows (coalesced
+// row sums into `rowsum`), then threads take columns and walk down the rows,
+// so every read of the node's matrix is a coalesced row segment.  The two
+// sums cancel to a small difference: both accumulate in fp64.
+constexpr int kRowColThreads = 256;
+__global__ void __launch_bounds__(kRowColThreads)
+ddd_rowcol(int S, const int* __restrict__ nstart, const int* __restrict__ nlen,
+           const long long* __restrict__ loff, long long l_hs, const float* __restrict__ dDD,
+           double* rowsum, float* dgam) {
+  const int c = blockIdx.x, h = blockIdx.y;
+  const int L = nlen[c], Lp = row_stride(L), s0 = nstart[c];
   const float* base = dDD + h * l_hs + loff[c];
-  // the row and column sums cancel to a small difference: accumulate in fp64
-  double acc = 0.0;
-  for (int m = threadIdx.x; m < L; m += blockDim.x)
-    acc += (double)base[(long long)j * Lp + m] - (double)base[(long long)m * Lp + j];
-  __shared__ double red[32];
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
-  __syncthreads();
-  if (threadIdx.x == 0) {
+  double* rs = rowsum + (long long)h * S + s0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int j = warp; j < L; j += kRowColThreads / 32) {
+    const float* row = base + (long long)j * Lp;
     double a = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a += red[w];
-    dgam[(long long)h * S + nstart[c] + j] += (float)a;
+    for (int m = lane; m <= j; m += 32) a += (double)row[m];
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) rs[j] = a;
+  }
+  __syncthreads();
+  for (int m = threadIdx.x; m < L; m += kRowColThreads) {
+    double col = 0.0;
+    const float* p = base + (long long)m * Lp + m;
+#pragma unroll 4
+    for (int j = m; j < L; ++j, p += Lp) col += (double)*p;
+    dgam[(long long)h * S + s0 + m] += (float)(rs[m] - col);
   }
 }
 
@@ -571,6 +581,7 @@ __global__ void dinit_kernel(int H, int DkDv, int n_roots, const int* __restrict
 struct Plan {
   int S, H, Hk, Dk, Dv, n;
   std::vector<int> start, len, parent, depth;
+  std::vector<int> tok_node;       // node of each token
   std::vector<long long> loff;     // packed L x Lp offset per node (Lp = row_stride(L))
   std::vector<long long> xoff;     // 64 x Lp scratch block per node (exact inverse)
   long long ll_total = 0;          // sum L * Lp
@@ -600,6 +611,9 @@ int make_plan(Plan& p, int S, int H, int Hk, int Dk, int Dv, int n, const int32_
     p.max_depth = std::max(p.max_depth, p.depth[c]);
   }
   if (expect != S) return TT_ERR_INVALID_ARG;
+  p.tok_node.resize(S);
+  for (int c = 0; c < n; ++c)
+    for (int t = p.start[c]; t < p.start[c] + p.len[c]; ++t) p.tok_node[t] = c;
   p.levels.assign(p.max_depth + 1, {});
   for (int c = 0; c < n; ++c) p.levels[p.depth[c]].push_back(c);
   p.child_ptr.assign(n + 1, 0);
@@ -635,6 +649,8 @@ struct Bufs {
   // backward
   float *dO, *dVn, *dQg, *dKd, *dW, *dT, *dA, *dAqk, *dDD, *X, *dVb, *dKbg, *dKb, *dQ, *dK;
   float *dSo, *dSi, *dgl, *dgam, *kd_dot, *dq_h, *dk_h;
+  double* rowsum;   // fp64 row sums of dDD per (head, token)
+  int *d_tok_node;
   int *d_start, *d_len, *d_parent, *d_child_ptr, *d_child_idx, *d_roots, *d_level_nodes;
   long long* d_loff;
   SegDesc* d_desc;
@@ -694,15 +710,17 @@ std::atomic<int64_t> g_gemm_tc_flops{0};
 
 // Which GEMM runs the segments: 0 = automatic (tensor cores: 3xTF32 products
 // for fp32 inputs, TF32 products for 16-bit inputs), 1 = tensor cores with
-// 3xTF32 products for any input, 2 = the CUDA-core fp32 GEMM.  Initialised
-// from TT_GDN_GEMM; tt_gdn_set_gemm_mode changes it.
+// 3xTF32 products for any input, 2 = the CUDA-core fp32 GEMM; plus 4 = stage
+// the tensor cores' operands with cp.async copies instead of TMA.
+// Initialised from TT_GDN_GEMM; tt_gdn_set_gemm_mode changes it.
 std::atomic<int> g_gemm_mode{-1};
 
 int gemm_mode() {
   int m = g_gemm_mode.load();
   if (m < 0) {
     const char* e = std::getenv("TT_GDN_GEMM");
-    m = (e && (e[0] == '1' || e[0] == '2')) ? e[0] - '0' : 0;
+    m = e ? std::atoi(e) & 7 : 0;
+    if ((m & 3) == 3) m = 0;
     g_gemm_mode.store(m);
   }
   return m;
@@ -716,7 +734,9 @@ struct GemmCtx {
   const int2* d_tiles;
   const int2* d_tiles_tc;
   const std::vector<SegDesc>* h_desc;
+  const std::vector<int2>* h_tiles_tc;
   int split;
+  bool tma;
   int rc = TT_OK;
 };
 
@@ -727,12 +747,35 @@ void launch_gemm(GemmCtx& g, DescSet ds, int H, const float* A, long long a_hs, 
                  cudaStream_t st, const float* Cin = nullptr) {
   if (ds.tcount == 0) return;
   if (g.split != 0 && tt_gdn_tc_gemm_supported(g.h_desc->data(), ds.first, ds.count, A, a_hs, B,
-                                               b_hs, C, c_hs) &&
-      (Cin == nullptr || (reinterpret_cast<uintptr_t>(Cin) & 15u) == 0)) {
-    const int rc = tt_gdn_seg_gemm_tc(g.d_desc, g.d_tiles_tc + ds.tc_first, ds.tc_count, H, A,
-                                      a_hs, B, b_hs, C, c_hs, alpha, beta, Cin, g.split, st);
-    if (rc != TT_OK) g.rc = rc;
-    tt_count_launches(1);
+                                               b_hs, C, c_hs)) {
+    int launches = 0;
+    if (g.tma) {
+      // chunks of at most kTmaMaxSegs segments (their tensor maps travel as
+      // kernel parameters), each with the tiles of exactly its segments
+      int t = ds.tc_first;
+      const int t_end = ds.tc_first + ds.tc_count;
+      for (int c0 = 0; c0 < ds.count; c0 += kTmaMaxSegs) {
+        const int c1 = std::min(ds.count, c0 + kTmaMaxSegs);
+        const int seg_end = ds.first + c1;
+        int t1 = t;
+        while (t1 < t_end && (*g.h_tiles_tc)[t1].x < seg_end) ++t1;
+        int rc = tt_gdn_seg_gemm_tma(g.h_desc->data() + ds.first + c0, ds.first + c0, c1 - c0,
+                                     g.d_desc, g.d_tiles_tc + t, t1 - t, H, A, a_hs, B, b_hs, C,
+                                     c_hs, alpha, beta, Cin, g.split, st);
+        if (rc == TT_ERR_UNSUPPORTED)
+          rc = tt_gdn_seg_gemm_tc(g.d_desc, g.d_tiles_tc + t, t1 - t, H, A, a_hs, B, b_hs, C,
+                                  c_hs, alpha, beta, Cin, g.split, st);
+        if (rc != TT_OK) g.rc = rc;
+        if (t1 > t) ++launches;
+        t = t1;
+      }
+    } else {
+      const int rc = tt_gdn_seg_gemm_tc(g.d_desc, g.d_tiles_tc + ds.tc_first, ds.tc_count, H, A,
+                                        a_hs, B, b_hs, C, c_hs, alpha, beta, Cin, g.split, st);
+      if (rc != TT_OK) g.rc = rc;
+      launches = 1;
+    }
+    tt_count_launches(launches);
     g_gemm_flops.fetch_add(static_cast<int64_t>(ds.flops * H), std::memory_order_relaxed);
     g_gemm_tc_flops.fetch_add(static_cast<int64_t>(ds.flops * H), std::memory_order_relaxed);
     return;
@@ -787,6 +830,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     b.dSo = ar.get<float>((long long)n * sh); b.dSi = ar.get<float>((long long)n * sh);
     b.dgl = ar.get<float>((long long)H * n); b.dgam = ar.get<float>((long long)H * S);
     b.kd_dot = ar.get<float>((long long)H * S);
+    b.rowsum = ar.get<double>((long long)H * S);
     b.dq_h = ar.get<float>(H * vk); b.dk_h = ar.get<float>(H * vk);
   }
   // metadata + descriptors
@@ -925,6 +969,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     level_first.push_back((int)level_nodes.size());
     level_nodes.insert(level_nodes.end(), l.begin(), l.end());
   }
+  b.d_tok_node = ar.get<int>(S);
   b.d_start = ar.get<int>(n); b.d_len = ar.get<int>(n); b.d_parent = ar.get<int>(n);
   b.d_child_ptr = ar.get<int>(n + 1); b.d_child_idx = ar.get<int>(std::max<size_t>(1, p.child_idx.size()));
   b.d_roots = ar.get<int>(std::max<size_t>(1, p.roots.size()));
@@ -943,6 +988,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
                                                                                         : TT_ERR_CUDA;
   };
   int rc = TT_OK;
+  rc |= h2d(b.d_tok_node, p.tok_node.data(), (size_t)S * 4);
   rc |= h2d(b.d_start, p.start.data(), n * 4);
   rc |= h2d(b.d_len, p.len.data(), n * 4);
   rc |= h2d(b.d_parent, p.parent.data(), n * 4);
@@ -960,11 +1006,11 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   if (backward && dcaptured) rc |= h2d(b.d_cap_slot, cap_slot.data(), n * 4);
   if (rc != TT_OK) return TT_ERR_CUDA;
 
-  const int max_l = p.max_len;
   const float q_scale = 1.f / sqrtf((float)Dk);
   const int mode = gemm_mode();
-  GemmCtx gc{b.d_desc, b.d_tiles, b.d_tiles_tc, &bd.all,
-             mode == 2 ? 0 : (mode == 1 || std::is_same<T, float>::value) ? 3 : 1};
+  GemmCtx gc{b.d_desc, b.d_tiles, b.d_tiles_tc, &bd.all, &bd.tiles_tc,
+             (mode & 3) == 2 ? 0 : ((mode & 3) == 1 || std::is_same<T, float>::value) ? 3 : 1,
+             (mode & 4) == 0};
   auto blocks = [](long long nel) { return (unsigned)((nel + 255) / 256); };
   int launches = 0;
   // ---------------------------------------------------------------- forward
@@ -978,8 +1024,8 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     launches += 2;
     launch_gemm(gc, ds_kk, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
     launch_gemm(gc, ds_kk, H, b.Q, vk, b.K, vk, b.QK, llh, 1.f, 0.f, st);
-    decay_masks<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.gam,
-                                                   b.KK, b.QK, b.Am, b.Aqk);
+    decay_masks<<<dim3(S, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_tok_node, b.d_loff, llh,
+                                             b.gam, b.KK, b.QK, b.Am, b.Aqk);
     ++launches;
     if (exact) {
       // Am <- T = (I - A)^-1 in place: diagonal blocks, then block rows in order
@@ -1080,10 +1126,10 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   }
   // masks: dA -> G = -dA*D, dAqk -> F = dAqk*D, dDD
   TT_CUDA_OK(cudaMemsetAsync(b.dgam, 0, (size_t)H * S * 4, st));
-  grad_masks<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.gam,
-                                                b.KK, b.QK, b.dA, b.dAqk, b.dDD);
-  ddd_rowcol<<<dim3(max_l, n, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh, b.dDD,
-                                                b.dgam);
+  grad_masks<<<dim3(S, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_tok_node, b.d_loff, llh,
+                                            b.gam, b.KK, b.QK, b.dA, b.dAqk, b.dDD);
+  ddd_rowcol<<<dim3(n, H), kRowColThreads, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh,
+                                                     b.dDD, b.rowsum, b.dgam);
   launches += 2;
   // dKb = G K ; dK = G^T Kb + F^T Q ; dQ = F K
   launch_gemm(gc, ds_gk, H, b.dA, llh, b.K, vk, b.dKb, vk, 1.f, 0.f, st);
@@ -1142,7 +1188,7 @@ extern "C" int tt_gdn_segmented_gemm(int engine, int32_t n_segs, const int64_t* 
                                      float* C, int64_t c_hs, float alpha, float beta,
                                      void* workspace, int64_t workspace_bytes, void* stream) {
   using namespace tt::gdn;
-  if (engine < 0 || engine > 3 || engine == 2 || n_segs < 0 || H <= 0 ||
+  if (engine < 0 || engine > 7 || (engine & 3) == 2 || engine == 4 || n_segs < 0 || H <= 0 ||
       (n_segs > 0 && (!segs || !A || !B || !C)))
     return TT_ERR_INVALID_ARG;
   const int64_t need = tt_gdn_segmented_gemm_workspace_size(n_segs, segs);
@@ -1173,8 +1219,8 @@ extern "C" int tt_gdn_segmented_gemm(int engine, int32_t n_segs, const int64_t* 
     TT_CUDA_OK(cudaMemcpyAsync(d_tiles_tc, bd.tiles_tc.data(), bd.tiles_tc.size() * sizeof(int2),
                                cudaMemcpyHostToDevice, st));
   // engine 0 = CUDA cores; 1 / 3 = tensor cores with TF32 / 3xTF32 products
-  GemmCtx gc{d_desc, d_tiles, d_tiles_tc, &bd.all, engine};
-  if (engine != 0 && !tt_gdn_tc_gemm_supported(bd.all.data(), 0, n_segs, A, a_hs, B, b_hs, C, c_hs))
+  GemmCtx gc{d_desc, d_tiles, d_tiles_tc, &bd.all, &bd.tiles_tc, engine & 3, (engine & 4) == 0};
+  if ((engine & 3) != 0 && !tt_gdn_tc_gemm_supported(bd.all.data(), 0, n_segs, A, a_hs, B, b_hs, C, c_hs))
     return TT_ERR_UNSUPPORTED;
   launch_gemm(gc, ds, H, A, a_hs, B, b_hs, C, c_hs, alpha, beta, st);
   if (gc.rc != TT_OK) return gc.rc;
@@ -1300,6 +1346,7 @@ extern "C" int64_t tt_gdn_gemm_tc_flops(void) {
 
 extern "C" int tt_gdn_set_gemm_mode(int mode) {
   const int prev = tt::gdn::gemm_mode();
-  tt::gdn::g_gemm_mode.store(mode == 1 || mode == 2 ? mode : 0);
+  mode &= 7;
+  tt::gdn::g_gemm_mode.store((mode & 3) == 3 ? 0 : mode);
   return prev;
 }

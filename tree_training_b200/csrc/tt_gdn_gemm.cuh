@@ -40,16 +40,27 @@ constexpr int kTcTile = 128;
 // split = 1 multiplies the operands as TF32 (10-bit mantissas), split = 3
 // as the sum of three TF32 products (hi*hi + hi*lo + lo*hi, hi/lo the
 // rounded TF32 head and tail of each fp32 value: close to fp32 products).
-// Requirements (checked by tt_gdn_tc_gemm_supported): 16-byte aligned
-// bases, every offset and non-unit stride a multiple of 4 floats, C
-// row-major (c_cs == 1) with at least round_up(N, 4) writable columns per
-// row.  Bounded waits report TT_ERR_DEVICE_TIMEOUT through
+// Requirements (checked by tt_gdn_tc_gemm_supported): A and B with 16-byte
+// aligned bases and every offset and non-unit stride a multiple of 4 floats
+// (the operands are staged with 16-byte copies); C row-major (c_cs == 1).  Bounded waits report TT_ERR_DEVICE_TIMEOUT through
 // tt_gdn_take_device_status.
 // C = alpha A B + beta Cin, Cin (nullptr: C itself) with C's layout.
 int tt_gdn_seg_gemm_tc(const tt::gdn::SegDesc* d_desc, const int2* d_tiles, int n_tiles, int H,
                        const float* A, long long a_hs, const float* B, long long b_hs, float* C,
                        long long c_hs, float alpha, float beta, const float* Cin, int split,
                        cudaStream_t st);
+// The same GEMM with the operand slices staged by TMA tile copies through
+// tensor maps encoded here for each segment (the faster staging): segments
+// seg_first .. seg_first + seg_count - 1 (at most 120; h_segs their host
+// copies) and the tiles of exactly those segments.  TT_ERR_UNSUPPORTED when
+// a segment's layout has no tensor map (the caller then uses
+// tt_gdn_seg_gemm_tc).
+int tt_gdn_seg_gemm_tma(const tt::gdn::SegDesc* h_segs, int seg_first, int seg_count,
+                        const tt::gdn::SegDesc* d_desc, const int2* d_tiles, int n_tiles, int H,
+                        const float* A, long long a_hs, const float* B, long long b_hs, float* C,
+                        long long c_hs, float alpha, float beta, const float* Cin, int split,
+                        cudaStream_t st);
+constexpr int kTmaMaxSegs = 120;
 bool tt_gdn_tc_gemm_supported(const tt::gdn::SegDesc* h_desc, int first, int count,
                               const float* A, long long a_hs, const float* B, long long b_hs,
                               const float* C, long long c_hs);

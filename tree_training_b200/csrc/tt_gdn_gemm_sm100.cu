@@ -20,15 +20,17 @@
 //              then releases the stage; at the end of a tile it hands the
 //              accumulator to the epilogue and moves on to the next tile in
 //              the other one.
-//   warps 4-7  epilogue: one thread per accumulator row (TMEM lane): C =
-//              alpha * acc + beta * Cin (Cin defaults to C) with 16-byte
-//              loads and stores.
+//   warps 4-7  epilogue: C = alpha * acc + beta * Cin (Cin defaults to C).
+//              Each warp reads its 32 accumulator rows (TMEM lanes) 32
+//              columns at a time, transposes them through shared memory and
+//              stores whole 128-byte row segments.
 //
 // The CTAs are persistent (one per SM, tiles x heads dealt round robin), so
 // the slices of the next tile stream in while the current one finishes.
 // Every wait is bounded (2 s); on expiry the kernel records
 // TT_ERR_DEVICE_TIMEOUT in a device status word, drains its copies and MMAs,
 // frees its tensor memory and returns.
+#include <cstring>
 #include <mutex>
 
 #include "tt_gdn_gemm.cuh"
@@ -58,7 +60,8 @@ struct Ring {
 };
 
 struct Bars {
-  uint64_t full[kMaxStages];    // producers -> MMA (kProducers arrivals)
+  uint64_t full[kMaxStages];    // producers -> MMA (kProducers arrivals; TMA + TF32: one + bytes)
+  uint64_t landed[kMaxStages];  // TMA + 3xTF32: the stage's copies landed (bytes)
   uint64_t empty[kMaxStages];   // MMA -> producers (commit)
   uint64_t acc_full[2];         // MMA -> epilogue (commit)
   uint64_t acc_empty[2];        // epilogue -> MMA (128 arrivals)
@@ -67,9 +70,15 @@ struct Bars {
   int32_t abort;
 };
 
+// Epilogue staging: per epilogue warp a 32 x 32 block of the accumulator,
+// padded to 33 columns (conflict-free row writes and column reads).
+constexpr int kStgPitch = 33;
+constexpr int kStgBytes = kEpilogueWarps * 32 * kStgPitch * 4;
+
 template <int kSplit>
 constexpr size_t smem_bytes() {
-  return 1024 + (size_t)Ring<kSplit>::kStages * Ring<kSplit>::kStageBytes + sizeof(Bars);
+  return 1024 + (size_t)Ring<kSplit>::kStages * Ring<kSplit>::kStageBytes + kStgBytes +
+         sizeof(Bars);
 }
 
 __device__ int32_t g_status;   // first error of any launch since the last take
@@ -216,23 +225,78 @@ __device__ __forceinline__ void split_slice(uint8_t* op, bool k_contig, int tid)
   }
 }
 
-template <int kSplit>
-__global__ void __launch_bounds__(kThreads, 1)
-seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, int n_tiles, int H,
-            const float* __restrict__ A, long long a_hs, const float* __restrict__ B,
-            long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin) {
+// A CTA's items (tile x head, strided by the grid) with their descriptors
+// fetched one item ahead: the next item's tile record is loaded as an item
+// starts and its segment descriptor once the item's work has been issued, so
+// neither dependent load stalls the item in flight.
+struct ItemFetch {
+  const SegDesc* segs;
+  const int2* tiles;
+  int H, n_items, stride, next;
+  int2 tl_next;
+  SegDesc sd_next;
+  __device__ __forceinline__ ItemFetch(const SegDesc* s, const int2* t, int h, int n, int first,
+                                       int st)
+      : segs(s), tiles(t), H(h), n_items(n), stride(st), next(first) {
+    if (next < n_items) {
+      tl_next = tiles[next / H];
+      sd_next = segs[tl_next.x];
+    }
+  }
+  __device__ __forceinline__ void advance(int2& tl, SegDesc& sd) {
+    tl = tl_next;
+    sd = sd_next;
+    next += stride;
+    if (next < n_items) tl_next = tiles[next / H];
+  }
+  __device__ __forceinline__ void fetch_seg() {
+    if (next < n_items) sd_next = segs[tl_next.x];
+  }
+};
+
+// Tensor maps of one launch's segments (kernel parameter space): map 2 i is
+// operand A of segment seg_first + i, map 2 i + 1 its operand B.
+constexpr int kMaxSegsPerLaunch = 120;
+struct MapPack {
+  CUtensorMap m[2 * kMaxSegsPerLaunch];
+};
+
+// TMA copy of one operand slice into its stage: K-contiguous operands are one
+// 32 x 128 box (128-byte swizzle), MN-contiguous ones four 32 x 32 boxes
+// (128-byte swizzle, 32-byte atoms), one per 32-element mn block.  Elements
+// outside the segment are zero-filled by the copy.
+__device__ __forceinline__ void tma_slice(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
+                                          bool k_contig, int k0, int mn0, int h) {
+  if (k_contig) {
+    tma_load_3d(dst, map, bar, k0, mn0, h);
+  } else {
+#pragma unroll
+    for (int blk = 0; blk < 4; ++blk) tma_load_3d(dst + blk * 4096, map, bar, mn0 + 32 * blk, k0, h);
+  }
+}
+
+template <int kSplit, bool kTma>
+__device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
+                                          const int2* __restrict__ tiles, int n_tiles, int H,
+                                          const float* __restrict__ A, long long a_hs,
+                                          const float* __restrict__ B, long long b_hs, float* C,
+                                          long long c_hs, float alpha, float beta,
+                                          const float* Cin, const CUtensorMap* maps,
+                                          int seg_first) {
   using R = Ring<kSplit>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  Bars* sh = reinterpret_cast<Bars*>(ring + (size_t)R::kStages * R::kStageBytes);
+  float* stg_all = reinterpret_cast<float*>(ring + (size_t)R::kStages * R::kStageBytes);
+  Bars* sh = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(stg_all) + kStgBytes);
   const volatile int32_t* abort_flag = &sh->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_items = n_tiles * H;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < R::kStages; ++s) {
-      mbar_init(&sh->full[s], kProducers);
+      mbar_init(&sh->full[s], (kTma && kSplit == 1) ? 1 : kProducers);
+      mbar_init(&sh->landed[s], 1);
       mbar_init(&sh->empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -252,8 +316,80 @@ seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, in
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
 
-  if (warp < kProducerWarps) {
-    // -------------------------------------------------------------- producers
+  if (kTma && warp < kProducerWarps) {
+    // ------------------------------------------------------- producers (TMA)
+    // thread 0 issues each slice's copies; with 3xTF32 every producer thread
+    // then splits its share of the landed stage into TF32 heads and tails
+    const int tid = threadIdx.x;
+    uint32_t slot = 0;
+    uint32_t issued = 0, parity = 0;   // per stage: loaded at least once / parity of last use
+    bool ok = true;
+    ItemFetch f(segs, tiles, H, n_items, blockIdx.x, gridDim.x);
+    // with TF32 products only thread 0 has work here
+    for (int item = blockIdx.x; item < n_items && ok && (kSplit == 3 || tid == 0);
+         item += gridDim.x) {
+      int2 tl;
+      SegDesc sd;
+      f.advance(tl, sd);
+      const int h = item % H;
+      const int i0 = (tl.y >> 16) * kTM, j0 = (tl.y & 0xFFFF) * kTN;
+      const bool a_kc = sd.a_cs == 1, b_kc = sd.b_rs == 1;
+      const CUtensorMap* ma = maps + 2 * (tl.x - seg_first);
+      int kb, nk;
+      k_range(sd, i0, j0, kb, nk);
+      for (int t = 0; t < nk; ++t, ++slot) {
+        const int s = slot % R::kStages;
+        const uint32_t use = slot / R::kStages;
+        uint8_t* st = ring + (size_t)s * R::kStageBytes;
+        if (tid == 0) {
+          if (slot >= (uint32_t)R::kStages &&
+              !mbar_wait(&sh->empty[s], (use - 1) & 1, abort_flag)) {
+            ok = false;
+          } else {
+            uint64_t* bar = kSplit == 3 ? &sh->landed[s] : &sh->full[s];
+            mbar_arrive_expect_tx(bar, 2 * kOpBytes);
+            tma_slice(st, ma, bar, a_kc, kb + t * kTK, i0, h);
+            tma_slice(st + kOpBytes, ma + 1, bar, b_kc, kb + t * kTK, j0, h);
+            issued |= 1u << s;
+            parity = (parity & ~(1u << s)) | ((use & 1u) << s);
+          }
+        }
+        if constexpr (kSplit == 3) {
+          if (ok && mbar_wait(&sh->landed[s], use & 1, abort_flag)) {
+            float4* p = reinterpret_cast<float4*>(st);
+#pragma unroll 4
+            for (int i = 0; i < 2 * kOpBytes / 16 / kProducers; ++i) {
+              const int q = i * kProducers + tid;
+              const float4 a = p[q];
+              const float4 hi = make_float4(
+                  __uint_as_float(to_tf32(a.x)), __uint_as_float(to_tf32(a.y)),
+                  __uint_as_float(to_tf32(a.z)), __uint_as_float(to_tf32(a.w)));
+              p[q] = hi;
+              p[q + 2 * kOpBytes / 16] = make_float4(
+                  __uint_as_float(to_tf32(a.x - hi.x)), __uint_as_float(to_tf32(a.y - hi.y)),
+                  __uint_as_float(to_tf32(a.z - hi.z)), __uint_as_float(to_tf32(a.w - hi.w)));
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&sh->full[s]);
+          } else {
+            ok = false;
+          }
+        }
+        if (!ok) break;
+      }
+      f.fetch_seg();
+    }
+    if (!ok) {
+      record_error(sh, TT_ERR_DEVICE_TIMEOUT);
+      if (tid == 0) {
+        // the last copies into each stage land before the CTA exits
+        for (int s = 0; s < R::kStages; ++s)
+          if ((issued >> s) & 1u)
+            mbar_wait(kSplit == 3 ? &sh->landed[s] : &sh->full[s], (parity >> s) & 1u, nullptr);
+      }
+    }
+  } else if (warp < kProducerWarps) {
+    // -------------------------------------------------- producers (cp.async)
     const int tid = threadIdx.x;
     uint32_t slot = 0;       // slices issued so far (all items)
     uint32_t done = 0;       // slices handed to the MMA so far
@@ -272,10 +408,12 @@ seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, in
       mbar_arrive(&sh->full[s]);
       ++done;
     };
+    ItemFetch f(segs, tiles, H, n_items, blockIdx.x, gridDim.x);
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      const int2 tl = tiles[item / H];
+      int2 tl;
+      SegDesc sd;
+      f.advance(tl, sd);
       const int h = item % H;
-      const SegDesc sd = segs[tl.x];
       const int i0 = (tl.y >> 16) * kTM, j0 = (tl.y & 0xFFFF) * kTN;
       const float* a = A + h * a_hs + sd.a_off;
       const float* b = B + h * b_hs + sd.b_off;
@@ -301,6 +439,7 @@ seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, in
           finish();
         }
       }
+      f.fetch_seg();
     }
     cp_async_wait<0>();
     if (ok) {
@@ -315,9 +454,11 @@ seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, in
       int acc_i = 0;
       bool ok = true;
       const uint32_t ring0 = smem_u32(ring);
+      ItemFetch f(segs, tiles, H, n_items, blockIdx.x, gridDim.x);
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++acc_i) {
-        const int2 tl = tiles[item / H];
-        const SegDesc sd = segs[tl.x];
+        int2 tl;
+        SegDesc sd;
+        f.advance(tl, sd);
         const bool a_kc = sd.a_cs == 1, b_kc = sd.b_rs == 1;
         int kb, nk;
         k_range(sd, (tl.y >> 16) * kTM, (tl.y & 0xFFFF) * kTN, kb, nk);
@@ -356,6 +497,7 @@ seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, in
         }
         if (!ok) break;
         tc_commit(&sh->acc_full[buf]);
+        f.fetch_seg();
       }
       if (!ok) record_error(sh, TT_ERR_DEVICE_TIMEOUT);
       // every MMA issued has completed before the accumulators are freed
@@ -365,13 +507,14 @@ seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, in
   } else {
     // -------------------------------------------------------------- epilogue
     const int quad = warp & 3;                 // TMEM lane quadrant of this warp
-    const int r = quad * 32 + lane;            // accumulator row
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     int acc_i = 0;
+    ItemFetch f(segs, tiles, H, n_items, blockIdx.x, gridDim.x);
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++acc_i) {
-      const int2 tl = tiles[item / H];
+      int2 tl;
+      SegDesc sd;
+      f.advance(tl, sd);
       const int h = item % H;
-      const SegDesc sd = segs[tl.x];
       const int i0 = (tl.y >> 16) * kTM, j0 = (tl.y & 0xFFFF) * kTN;
       const int buf = acc_i & 1;
       bool ok = mbar_wait(&sh->acc_full[buf], (acc_i >> 1) & 1, abort_flag);
@@ -384,36 +527,49 @@ seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, in
       int kb, nk;
       k_range(sd, i0, j0, kb, nk);
       const bool empty_k = nk == 0;            // no MMA wrote this accumulator
-      const int gi = i0 + r;
-      float* crow = C + h * c_hs + sd.c_off + (long long)gi * sd.c_rs;
-      const float* cinrow = (Cin ? Cin : C) + h * c_hs + sd.c_off + (long long)gi * sd.c_rs;
+      // each 32 x 32 block goes through shared memory so that the warp
+      // stores (and reads C_in) one 128-byte row segment per instruction
+      float* stg = stg_all + quad * 32 * kStgPitch;
+      const float* cin = Cin ? Cin : C;
+      const long long hoff = h * c_hs + sd.c_off;
 #pragma unroll 1
       for (int cc = 0; cc < kTN / 32; ++cc) {
         float v[32];
         tmem_ld32(lane_addr + buf * kTN + cc * 32, v);
-        if (gi < sd.M) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int gj = j0 + cc * 32 + j * 4;
-            if (gj < sd.N) {
-              float4 o = empty_k ? make_float4(0.f, 0.f, 0.f, 0.f)
-                                 : make_float4(alpha * v[4 * j], alpha * v[4 * j + 1],
-                                               alpha * v[4 * j + 2], alpha * v[4 * j + 3]);
-              float4* cp = reinterpret_cast<float4*>(crow + gj);
-              if (beta != 0.f) {
-                const float4 old = *reinterpret_cast<const float4*>(cinrow + gj);
-                o.x += beta * old.x;
-                o.y += beta * old.y;
-                o.z += beta * old.z;
-                o.w += beta * old.w;
+        for (int i = 0; i < 32; ++i) stg[lane * kStgPitch + i] = empty_k ? 0.f : alpha * v[i];
+        __syncwarp();
+        const int gj = j0 + cc * 32 + lane;
+        const int rows = sd.M - (i0 + quad * 32);      // rows of this warp's block in C
+        if (gj < sd.N && rows > 0) {
+          const long long o0 = hoff + (long long)(i0 + quad * 32) * sd.c_rs + gj;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            float cv[16];
+            if (beta != 0.f) {
+              // 16 rows' C_in loads in flight before the first store
+#pragma unroll
+              for (int rr = 0; rr < 16; ++rr) {
+                const int r = half * 16 + rr;
+                cv[rr] = r < rows ? cin[o0 + (long long)r * sd.c_rs] : 0.f;
               }
-              *cp = o;
+            }
+#pragma unroll
+            for (int rr = 0; rr < 16; ++rr) {
+              const int r = half * 16 + rr;
+              if (r < rows) {
+                float x = stg[r * kStgPitch + lane];
+                if (beta != 0.f) x += beta * cv[rr];
+                C[o0 + (long long)r * sd.c_rs] = x;
+              }
             }
           }
         }
+        __syncwarp();
       }
       tc_fence_before();
       mbar_arrive(&sh->acc_empty[buf]);
+      f.fetch_seg();
     }
   }
   tc_fence_before();
@@ -424,10 +580,74 @@ seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, in
   }
 }
 
+// Operands staged with 16-byte cp.async copies (any segment layout the
+// tensor maps cannot describe).
+template <int kSplit>
+__global__ void __launch_bounds__(kThreads, 1)
+seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, int n_tiles, int H,
+            const float* __restrict__ A, long long a_hs, const float* __restrict__ B,
+            long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin) {
+  gemm_body<kSplit, false>(segs, tiles, n_tiles, H, A, a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
+                           nullptr, 0);
+}
+
+// Operands staged with TMA tile copies through per-segment tensor maps.
+template <int kSplit>
+__global__ void __launch_bounds__(kThreads, 1)
+seg_gemm_tma(const __grid_constant__ MapPack mp, int seg_first,
+             const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, int n_tiles, int H,
+             const float* __restrict__ A, long long a_hs, const float* __restrict__ B,
+             long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin) {
+  gemm_body<kSplit, true>(segs, tiles, n_tiles, H, A, a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
+                          mp.m, seg_first);
+}
+
 constexpr int kMaxDevices = 64;
 int g_sms[kMaxDevices];
-bool g_attr_set[kMaxDevices][2];
+bool g_attr_set[kMaxDevices][4];
 std::mutex g_mu;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Tensor map of one operand of one segment (3-D: inner, outer, head), or false
+// when the driver does not accept the layout.  K-contiguous: inner = K, outer =
+// M (or N), 32 x 128 boxes, 128-byte swizzle.  MN-contiguous: inner = M (or
+// N), outer = K, 32 x 32 boxes, 128-byte swizzle on 32-byte atoms.
+bool encode_operand(EncodeTiledFn fn, CUtensorMap* m, const float* base, bool k_contig,
+                    long long mn_ext, long long k_ext, long long outer_stride, long long head_stride,
+                    int H) {
+  const long long inner = k_contig ? k_ext : mn_ext, outer = k_contig ? mn_ext : k_ext;
+  if (inner <= 0 || outer <= 0 || H <= 0) return false;
+  long long hs = head_stride;
+  if (H == 1 || hs <= 0) hs = ((outer * outer_stride * 4 + 15) / 16) * 4;   // unused dim
+  const cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)H};
+  const cuuint64_t strides[2] = {(cuuint64_t)outer_stride * 4, (cuuint64_t)hs * 4};
+  const cuuint32_t box[3] = {32u, k_contig ? (cuuint32_t)kTM : 32u, 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r =
+      fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE,
+         k_contig ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
 
 }  // namespace
 }  // namespace gdn
@@ -439,14 +659,14 @@ bool tt_gdn_tc_gemm_supported(const SegDesc* d, int first, int count, const floa
                               long long a_hs, const float* B, long long b_hs, const float* C,
                               long long c_hs) {
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  if (!al(A) || !al(B) || !al(C) || (a_hs & 3) || (b_hs & 3) || (c_hs & 3)) return false;
+  (void)C;
+  (void)c_hs;
+  if (!al(A) || !al(B) || (a_hs & 3) || (b_hs & 3)) return false;
   for (int i = first; i < first + count; ++i) {
     const SegDesc& s = d[i];
     const bool a_ok = (s.a_cs == 1 && (s.a_rs & 3) == 0) || (s.a_rs == 1 && (s.a_cs & 3) == 0);
     const bool b_ok = (s.b_rs == 1 && (s.b_cs & 3) == 0) || (s.b_cs == 1 && (s.b_rs & 3) == 0);
-    if (!a_ok || !b_ok || s.c_cs != 1 || (s.c_rs & 3) || (s.a_off & 3) || (s.b_off & 3) ||
-        (s.c_off & 3))
-      return false;
+    if (!a_ok || !b_ok || s.c_cs != 1 || (s.a_off & 3) || (s.b_off & 3)) return false;
   }
   return true;
 }
@@ -484,6 +704,58 @@ int tt_gdn_seg_gemm_tc(const SegDesc* d_desc, const int2* d_tiles, int n_tiles, 
   else
     seg_gemm_tc<1><<<grid, kThreads, smem, st>>>(d_desc, d_tiles, n_tiles, H, A, a_hs, B, b_hs,
                                                   C, c_hs, alpha, beta, Cin);
+  return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
+}
+
+int tt_gdn_seg_gemm_tma(const SegDesc* h_segs, int seg_first, int seg_count,
+                        const SegDesc* d_desc, const int2* d_tiles, int n_tiles, int H,
+                        const float* A, long long a_hs, const float* B, long long b_hs, float* C,
+                        long long c_hs, float alpha, float beta, const float* Cin, int split,
+                        cudaStream_t st) {
+  using namespace tt::gdn;
+  if (n_tiles <= 0 || H <= 0) return TT_OK;
+  if (seg_count > kMaxSegsPerLaunch) return TT_ERR_INVALID_ARG;
+  const EncodeTiledFn fn = encoder();
+  if (!fn) return TT_ERR_UNSUPPORTED;
+  MapPack mp;
+  std::memset(&mp, 0, sizeof(mp));
+  for (int i = 0; i < seg_count; ++i) {
+    const SegDesc& d = h_segs[i];
+    if (d.M <= 0 || d.N <= 0 || d.K <= 0) continue;   // no tiles, or no slices to load
+    const bool a_kc = d.a_cs == 1, b_kc = d.b_rs == 1;
+    if (!encode_operand(fn, &mp.m[2 * i], A + d.a_off, a_kc, d.M, d.K, a_kc ? d.a_rs : d.a_cs,
+                        a_hs, H) ||
+        !encode_operand(fn, &mp.m[2 * i + 1], B + d.b_off, b_kc, d.N, d.K, b_kc ? d.b_cs : d.b_rs,
+                        b_hs, H))
+      return TT_ERR_UNSUPPORTED;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TT_ERR_CUDA;
+  const int si = 2 + (split == 3 ? 1 : 0);
+  const size_t smem = split == 3 ? smem_bytes<3>() : smem_bytes<1>();
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_sms[dev] == 0 &&
+        cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return TT_ERR_CUDA;
+    if (!g_attr_set[dev][si]) {
+      const cudaError_t e =
+          split == 3 ? cudaFuncSetAttribute(seg_gemm_tma<3>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                     : cudaFuncSetAttribute(seg_gemm_tma<1>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return TT_ERR_CUDA;
+      g_attr_set[dev][si] = true;
+    }
+  }
+  const long long items = (long long)n_tiles * H;
+  const int grid = (int)std::min<long long>(items, g_sms[dev]);
+  if (split == 3)
+    seg_gemm_tma<3><<<grid, kThreads, smem, st>>>(mp, seg_first, d_desc, d_tiles, n_tiles, H, A,
+                                                   a_hs, B, b_hs, C, c_hs, alpha, beta, Cin);
+  else
+    seg_gemm_tma<1><<<grid, kThreads, smem, st>>>(mp, seg_first, d_desc, d_tiles, n_tiles, H, A,
+                                                   a_hs, B, b_hs, C, c_hs, alpha, beta, Cin);
   return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
 }
 

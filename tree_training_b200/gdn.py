@@ -136,8 +136,12 @@ def _gdn_setup(ctx, inputs, output):
     q, k, v, g, beta, bounds, parents, init, has_init, flags, want_last, capture, keep = inputs
     ctx.save_for_backward(q, k, v, g, beta, bounds, parents, init, capture)
     # the kept workspace: its forward part is read, its backward part written
-    # by every backward call, so it is held outside autograd's version checks
+    # by every backward call, so it is held outside autograd's version checks;
+    # it has no gradient, and no zero gradient is built for it (or for any
+    # other output the loss does not reach: the backward takes None for those)
     ctx.kept = output[3]
+    ctx.mark_non_differentiable(output[3])
+    ctx.set_materialize_grads(False)
     ctx.has_init, ctx.flags, ctx.want_last = has_init, flags, want_last
 
 
