@@ -18,6 +18,10 @@ What is captured (all seeded, all small):
                      (tree_dfs_ssm.py:38-156)
   * conv_*.npz       _tree_correct_conv_varlen fwd + autograd
                      (tree_dfs_ssm.py:285-348)
+  * ref_driver_calls.npz  every attention call tree_grad_hybrid
+                     (tree_grad_hybrid.py:434-539) and dfs_tree_forward
+                     (dfs_tree_forward.py:513-576) make on the config-1 model,
+                     and tree_grad_hybrid's gradient fingerprints
 """
 import argparse
 import os
@@ -258,6 +262,54 @@ def save_conv(name, tds, bounds, parents, B, C, K, seed):
         chunk_parent_map=np.array(parents, np.int64))
 
 
+def save_driver_calls(dft, tgh):
+    """The reference's unmodified drivers on the config-1 model with a
+    recording attention function registered through transformers'
+    AttentionInterface (the same hook tree_sm100 uses): every attention call's
+    inputs exactly as the drivers pass them (dense additive mask, gateway K/V
+    prefix from GatewayCache, scaling), and the parameter-gradient fingerprints
+    of tree_grad_hybrid at max_tokens 1000 / 20 / 10.  SDPA computes each call."""
+    from transformers import AttentionInterface
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+    sys.path.insert(0, os.path.dirname(HERE))
+    from golden_util import config1_forest, config1_model, grad_projections
+    calls = []
+
+    def recorder(module, query, key, value, attention_mask, dropout=0.0, scaling=None,
+                 sliding_window=None, **kwargs):
+        calls.append(dict(q=query.detach().numpy().copy(), k=key.detach().numpy().copy(),
+                          v=value.detach().numpy().copy(),
+                          mask=attention_mask.detach().numpy().copy(),
+                          scaling=float(scaling), groups=int(module.num_key_value_groups),
+                          layer=int(module.layer_idx)))
+        return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,
+                                      scaling=scaling, sliding_window=sliding_window, **kwargs)
+
+    AttentionInterface.register("tt_recorder", recorder)
+    model = config1_model()
+    model.config._attn_implementation = "tt_recorder"
+    roots, leaves, labels = config1_forest(dft.TreeNode)
+    out = {}
+    runs = [("hybrid_%d" % mt, mt) for mt in (1000, 20, 10)] + [("dfs_forward", None)]
+    for tag, mt in runs:
+        calls.clear()
+        model.zero_grad(set_to_none=True)
+        if mt is not None:
+            tgh.tree_grad_hybrid(model, roots=roots, max_tokens=mt,
+                                 leaf_loss_fn=tgh.make_tree_loss_fn(labels, leaves, len(leaves)))
+            for name, v in grad_projections(model).items():
+                out[f"{tag}/grad/{name}"] = v
+        else:
+            with torch.no_grad():
+                dft.dfs_tree_forward(model, roots)
+        out[f"{tag}/n_calls"] = np.array(len(calls))
+        for i, c in enumerate(calls):
+            for key in ("q", "k", "v", "mask"):
+                out[f"{tag}/{i}/{key}"] = c[key]
+            out[f"{tag}/{i}/meta"] = np.array([c["scaling"], c["groups"], c["layer"]])
+    np.savez_compressed(os.path.join(HERE, "ref_driver_calls.npz"), **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True)
@@ -321,6 +373,8 @@ def main():
     save_conv("tree", tds, info.chunk_boundaries, info.chunk_parent_map, 1, 6, 4, 31)
     ch = dft.build_dfs_tree_info(random_forest(TreeNode, random.Random(8), 2, 4, (1, 3), 1, 3))
     save_conv("short_nodes", tds, ch.chunk_boundaries, ch.chunk_parent_map, 2, 3, 4, 32)
+    # ---- the reference's drivers with a recording attention function ----
+    save_driver_calls(dft, tgh)
     print("golden vectors written to", HERE)
 
 
