@@ -1131,24 +1131,32 @@ def run_e2e5(args):
     labels = [torch.randint(0, cfg.vocab_size, (len(n.token_ids),), generator=lg) for n in leaves]
     loss_fn = make_tree_loss_fn(labels, leaves, len(leaves))
 
-    avg = GradAverager(model.parameters())
+    avg = GradAverager(model.parameters()).attach()
     opt = torch.optim.AdamW(model.parameters(), lr=1e-5, fused=True)
     watch = None
     if world > 1:
         import torch.distributed as dist
         watch = RankWatch(dist.distributed_c10d._get_default_store(), rank, world, timeout_s=120)
     step_no = [0]
+    ar_ms, ar_issued = [], []
 
     def step():
-        opt.zero_grad(set_to_none=True)
-        loss = tree_grad_hybrid(model, roots, loss_fn, max_tokens=8192,
-                                fused_ce=bool(args.fused_ce))
+        # heartbeat first: the all-reduce starts inside the last partition's backward
         if watch is not None:
             watch.beat(step_no[0])
         step_no[0] += 1
-        avg.average()
+        opt.zero_grad(set_to_none=True)
+        loss = tree_grad_hybrid(model, roots, loss_fn, max_tokens=8192,
+                                fused_ce=bool(args.fused_ce), before_last_backward=avg.arm)
+        ar_issued.append(avg.issued_during_backward())
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        avg.average()                        # what remains of the all-reduce after the backward
+        e1.record()
         opt.step()
-        return float(loss.item())           # the step's d2h result
+        out = float(loss.item())             # the step's d2h result
+        ar_ms.append(e0.elapsed_time(e1))
+        return out
 
     clocks = ClockSampler(dev)
     clocks.start()
@@ -1161,6 +1169,8 @@ def run_e2e5(args):
     clocks.reset()
     launches0 = _lib.lib().tt_kernel_launches()
     ts, losses = [], []
+    ar_ms.clear()
+    ar_issued.clear()
     for _ in range(args.steps):
         torch.cuda.synchronize()
         a = torch.cuda.Event(enable_timing=True)
@@ -1173,6 +1183,18 @@ def run_e2e5(args):
     launches = _lib.lib().tt_kernel_launches() - launches0
     clk = clocks.stop()
     tt.check_device_status(dev)
+    exposed_ms = max_over_ranks(statistics.mean(ar_ms), world, dev)
+    # the same all-reduce issued as one block after the step, for comparison
+    standalone_ms = 0.0
+    if world > 1:
+        torch.cuda.synchronize()
+        barrier(world)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        avg.average()
+        s1.record()
+        s1.synchronize()
+        standalone_ms = max_over_ranks(s0.elapsed_time(s1), world, dev)
     t_step = max_over_ranks(statistics.mean(ts), world, dev)
     tokens_all = sum_over_ranks(float(N), world, dev)
     V = info.attn_meta().visible_pairs
@@ -1206,6 +1228,15 @@ def run_e2e5(args):
                     "note": "the step starts from the host tree (packing, id/label uploads "
                             "inside tree_grad_hybrid) and ends with the loss read back"},
             "loss_first_last": [losses[0], losses[-1]],
+            "allreduce": {"bytes_per_step": avg.bytes_per_step(), "buckets": len(avg.buckets),
+                          "issued_during_last_backward": min(ar_issued) if ar_issued else 0,
+                          "exposed_ms_per_step": exposed_ms,
+                          "standalone_ms": standalone_ms,
+                          "note": "buckets are all-reduced (NCCL, sum then / W) from gradient "
+                                  "hooks during the last partition's backward; exposed = the "
+                                  "time average() still takes after the backward (max over "
+                                  "ranks); standalone = the same buckets all-reduced after "
+                                  "the step with nothing to overlap"},
             "gpu_launches": int(launches),
             "clocks": clk,
             "cpu_baseline": None,

@@ -114,6 +114,25 @@ def dp_tree_step(rank, world, n_trees, bucket_bytes):
     return {"assigned": mine, "grads": [p.grad.clone() for p in model.parameters()]}
 
 
+def dp_overlap_step(rank, world, n_trees, bucket_bytes):
+    """As dp_tree_step, with the all-reduce overlapped: the averager is armed
+    before each rank's last backward, so the hooks issue the buckets during it."""
+    from tree_training_b200.dist import GradAverager, assign_trees
+    model = _toy_model()
+    avg = GradAverager(model.parameters(), bucket_bytes=bucket_bytes).attach()
+    trees = _trees(n_trees)
+    mine = assign_trees(n_trees, world, rank)
+    for j, i in enumerate(mine):
+        if j == len(mine) - 1:
+            avg.arm()
+        (_tree_loss(model, trees[i]) * (world / n_trees)).backward()
+    issued = avg.issued_during_backward()
+    avg.average()
+    avg.detach()
+    return {"grads": [p.grad.clone() for p in model.parameters()], "issued": issued,
+            "buckets": len(avg.buckets)}
+
+
 def single_process_grads(n_trees):
     model = _toy_model()
     for roots in _trees(n_trees):

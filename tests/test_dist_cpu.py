@@ -33,6 +33,22 @@ def test_dp_step_matches_single_process(bucket_bytes):
             torch.testing.assert_close(g, e, rtol=1e-12, atol=1e-14)
 
 
+@pytest.mark.parametrize("bucket_bytes", [64, 1 << 20])
+def test_overlapped_average_matches_single_process(bucket_bytes):
+    """Buckets all-reduced from the gradient hooks during each rank's last
+    backward (the ranks run different numbers of trees) give the same averaged
+    gradients as the single-process run."""
+    n_trees = 5
+    out = W.run_ranks("dp_overlap_step", 2, (n_trees, bucket_bytes))
+    ref = W.single_process_grads(n_trees)
+    for r in (0, 1):
+        assert out[r][0] == "ok", out[r][1]
+        res = out[r][1]
+        assert res["issued"] == res["buckets"]      # all issued before average()
+        for g, e in zip(res["grads"], ref):
+            torch.testing.assert_close(g, e, rtol=1e-12, atol=1e-14)
+
+
 def test_average_counts_missing_grad_as_zero():
     out = W.run_ranks("average_with_missing_grad", 2)
     for r in (0, 1):

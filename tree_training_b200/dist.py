@@ -10,7 +10,9 @@ supplies the rest for the multi-GPU configurations:
   no communication inside the attention or GDN operators);
 * ``GradAverager`` — bucketed all-reduce of the gradients (sum, then / W) over
   flat per-dtype buffers in a fixed parameter order, so every rank issues the
-  same collectives in the same order;
+  same collectives in the same order; optionally overlapped with the last
+  backward pass (``attach`` + ``arm``: each bucket is reduced as soon as all
+  of its gradients are final);
 * ``RankWatch`` — host-side liveness check through the process group's store:
   before a step's collectives each rank posts a heartbeat and waits, with a
   short limit, for everyone else's, so a rank that died between steps is
@@ -59,10 +61,26 @@ class GradAverager:
     all-reduced with SUM and divided by the world size, then copied back.
     Parameters whose ``.grad`` is None on this rank contribute zeros, so every
     rank issues identical collectives even when a partition did not touch a
-    parameter."""
+    parameter.
+
+    Overlap with the backward: after ``attach()`` (post-accumulate-grad hooks
+    on every parameter), ``arm()`` declares that the NEXT gradient accumulation
+    of each parameter is its last of the step (``tree_grad_hybrid`` calls it
+    through ``before_last_backward`` before the last partition's single
+    backward traversal).  From then on a bucket is packed and its all-reduce
+    issued (asynchronously, on NCCL's stream) once all of its parameters have
+    their final gradient, and buckets are issued strictly from the last to the
+    first, so that every rank issues the same collectives in the same order.
+    ``average()`` issues whatever is left in the same order, waits, divides and
+    copies back."""
 
     def __init__(self, params: Iterable[torch.nn.Parameter], bucket_bytes: int = 256 << 20):
         self.params = [p for p in params if p.requires_grad]
+        self._hooks: list = []
+        self._armed = False
+        self._ready: List[set] = []
+        self._next = -1
+        self._pending: list = []
         self.buckets: List[List[torch.nn.Parameter]] = []
         cur: List[torch.nn.Parameter] = []
         cur_bytes = 0
@@ -82,18 +100,68 @@ class GradAverager:
     def bytes_per_step(self) -> int:
         return sum(p.numel() * p.element_size() for p in self.params)
 
+    def _active(self, group=None) -> bool:
+        return dist.is_initialized() and dist.get_world_size(group) > 1
+
+    def attach(self) -> "GradAverager":
+        """Register the hooks that let ``arm()`` overlap the all-reduce with the
+        backward (no effect on a single process)."""
+        if self._hooks or not self._active():
+            return self
+        where = {}
+        for bi, bucket in enumerate(self.buckets):
+            for p in bucket:
+                where[id(p)] = bi
+        for p in self.params:
+            self._hooks.append(p.register_post_accumulate_grad_hook(
+                lambda q, _bi=where[id(p)]: self._on_grad(_bi, q)))
+        return self
+
+    def detach(self) -> None:
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []
+
+    def arm(self) -> None:
+        """The next accumulation of every parameter's gradient is its last one
+        of this step (see the class docstring)."""
+        if not self._hooks:
+            return
+        self._armed = True
+        self._ready = [set() for _ in self.buckets]
+        self._next = len(self.buckets) - 1
+        self._pending = []
+
+    def _on_grad(self, bi: int, p: torch.nn.Parameter) -> None:
+        if not self._armed:
+            return
+        self._ready[bi].add(id(p))
+        while self._next >= 0 and len(self._ready[self._next]) == len(self.buckets[self._next]):
+            self._issue(self._next)
+            self._next -= 1
+
+    def _issue(self, bi: int, group=None) -> None:
+        bucket = self.buckets[bi]
+        flat = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1)
+                          for p in bucket])
+        work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group, async_op=True)
+        self._pending.append((bucket, flat, work))
+
+    def issued_during_backward(self) -> int:
+        """Buckets whose all-reduce the hooks issued before ``average()``."""
+        return len(self._pending) if self._armed else 0
+
     def average(self, group=None) -> None:
-        if not dist.is_initialized():
+        if not self._active(group):
+            self._armed = False
             return                      # a single process: nothing to average
         world = dist.get_world_size(group)
-        if world == 1:
-            return
-        pending = []
-        for bucket in self.buckets:
-            flat = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1)
-                              for p in bucket])
-            work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group, async_op=True)
-            pending.append((bucket, flat, work))
+        if not self._armed:
+            self._pending, self._next = [], len(self.buckets) - 1
+        while self._next >= 0:          # what the hooks did not issue, same order
+            self._issue(self._next, group)
+            self._next -= 1
+        pending, self._pending, self._armed = self._pending, [], False
         for bucket, flat, work in pending:
             work.wait()
             flat.div_(world)

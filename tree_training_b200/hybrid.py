@@ -396,7 +396,8 @@ def _ensure_tree_attention(model):
 def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
                      gateway_mask: str = "tree", backward: str = "fused",
                      leaf_logits_only: bool = True, ssm_exact_inverse: bool = False,
-                     fused_ce: bool = False) -> torch.Tensor:
+                     fused_ce: bool = False,
+                     before_last_backward: Optional[Callable[[], None]] = None) -> torch.Tensor:
     """Partitioned tree forward/backward (tree_grad_hybrid.py:434-539):
     partitions run top-down, each with the gateway K/V of its cut node; then
     bottom-up, each partition backpropagates its leaf losses and chains the
@@ -423,7 +424,15 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
     gateways; ``ssm_exact_inverse`` selects the exact delta-rule correction
     (T = (I - A)^-1) instead of the reference's truncated one.
 
+    ``before_last_backward`` (``backward="fused"`` only) is called right before
+    the last partition's backward traversal, the one that gives every
+    parameter its final gradient of the step: ``dist.GradAverager.arm`` there
+    lets the gradient all-reduce run during that traversal.
+
     Returns the summed leaf loss (a detached fp32 scalar on the device)."""
+    if before_last_backward is not None and backward != "fused":
+        raise ValueError("before_last_backward needs backward='fused' (one traversal per "
+                         "partition)")
     if gateway_mask not in ("tree", "reference"):
         raise ValueError("gateway_mask must be 'tree' or 'reference'")
     if backward not in ("fused", "per_leaf"):
@@ -479,6 +488,8 @@ def tree_grad_hybrid(model, roots, leaf_loss_fn: Callable, max_tokens: int,
                 r, gr = _gateway_roots(g)
                 outs.extend(r)
                 grads.extend(gr)
+            if before_last_backward is not None and p is parts[0]:
+                before_last_backward()
             if outs:
                 torch.autograd.backward(outs, [torch.ones_like(o) if g is None else g
                                                for o, g in zip(outs, grads)])
