@@ -188,13 +188,27 @@ class PhaseTimer:
         self.steps[-1][name] = e
 
     def durations(self):
-        out = {"attn_bwd_delta_tc": [], "attn_bwd_dkdv_tc": [], "attn_bwd_dq_tc": []}
+        """Seconds per kernel.  Stored-dS schedule (a "dq_start" mark): delta
+        (+ entry map and tile order), the dS-storing dK/dV kernel and the
+        dQ-from-dS kernel run one after another on one stream; recompute
+        schedule: dK/dV and the recomputing dQ kernel run side by side on two
+        streams from the same start."""
+        out = {"attn_bwd_delta_tc": [], "attn_bwd_dkdv_tc": [], "attn_bwd_dq_tc": [],
+               "attn_bwd_dkdv_ds_tc": [], "attn_bwd_dq_ds_tc": [], "attn_bwd_stored_passes": []}
         for st in self.steps:
             if "bwd_start" not in st:
                 continue
+            if "bwd_all_done" in st:      # stored schedule in several kv-head passes
+                out["attn_bwd_stored_passes"].append(
+                    st["bwd_start"].elapsed_time(st["bwd_all_done"]))
+                continue
             out["attn_bwd_delta_tc"].append(st["bwd_start"].elapsed_time(st["prep_done"]))
-            out["attn_bwd_dkdv_tc"].append(st["prep_done"].elapsed_time(st["dkdv_done"]))
-            out["attn_bwd_dq_tc"].append(st["prep_done"].elapsed_time(st["dq_done"]))
+            if "dq_start" in st:
+                out["attn_bwd_dkdv_ds_tc"].append(st["prep_done"].elapsed_time(st["dkdv_done"]))
+                out["attn_bwd_dq_ds_tc"].append(st["dq_start"].elapsed_time(st["dq_done"]))
+            else:
+                out["attn_bwd_dkdv_tc"].append(st["prep_done"].elapsed_time(st["dkdv_done"]))
+                out["attn_bwd_dq_tc"].append(st["prep_done"].elapsed_time(st["dq_done"]))
         return {k: statistics.mean(v) / 1e3 for k, v in out.items() if v}
 
 
@@ -269,17 +283,24 @@ def reference_packer_sample(roots, V, max_pairs: int = 1_000_000):
 
 def isolated_kernel_roofline(meta, q, k, v, do, dev, V, peak, reps: int = 5):
     """Each attention kernel timed ALONE (CUDA events, same inputs, after the
-    timed region): in the product path dK/dV and dQ share the GPU on two
-    streams, so their live durations overlap and cannot be attributed to one
-    kernel; alone they can.  Returns {kernel: {ms, achieved, frac}}."""
+    timed region), under the product's backward schedule: the stored-dS
+    schedule's phases (delta, dS-storing dK/dV, dQ from dS) one call each, or
+    the recompute schedule's dK/dV and dQ, which share the GPU on two streams
+    in the product path.  Returns {kernel: {ms, achieved, frac}}."""
     from tree_training_b200 import _lib
-    from tree_training_b200.attention import _status_word, attn_fwd_raw
+    from tree_training_b200.attention import _status_word, _stored_plan, attn_fwd_raw
     scale = D ** -0.5
     md = meta.device(dev, 128, 128)
     out, lse = attn_fwd_raw(q, k, v, md, scale)
     N = meta.n_q
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    ws_bytes = int(_lib.lib().tt_tree_attn_bwd_workspace_size(1, N, meta.n_kv, HQ, HKV, D))
+    n_pairs = int(md["fwd_list"].numel())
+    plan = _stored_plan(1, N, meta.n_kv, HQ, HKV, D, n_pairs)
+    stored = plan is not None and plan[0] == HKV
+    if stored:
+        ws_bytes = plan[1]
+    else:
+        ws_bytes = int(_lib.lib().tt_tree_attn_bwd_workspace_size(1, N, meta.n_kv, HQ, HKV, D))
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
     args = [1, N, meta.n_kv, HQ, HKV, D, q.data_ptr(), q.stride(0), q.stride(1),
             k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(), v.stride(0), v.stride(1),
@@ -287,18 +308,26 @@ def isolated_kernel_roofline(meta, q, k, v, do, dev, V, peak, reps: int = 5):
             md["kv_lo"].data_ptr(), md["kv_hi"].data_ptr(), md["fwd_ptr"].data_ptr(),
             md["fwd_list"].data_ptr(), md["bwd_ptr"].data_ptr(), md["bwd_list"].data_ptr(),
             float(scale), dq.data_ptr(), dq.stride(0), dq.stride(1), dk.data_ptr(), dk.stride(0),
-            dk.stride(1), dv.data_ptr(), dv.stride(0), dv.stride(1), ws.data_ptr(), ws_bytes]
+            dk.stride(1), dv.data_ptr(), dv.stride(0), dv.stride(1)]
     st = _status_word(dev).data_ptr()
     cs = torch.cuda.current_stream(dev).cuda_stream
-    phase = lambda ph: _lib.call("tt_tree_attn_bwd", *args, ph, st, cs)
+    if stored:
+        phase = lambda ph: _lib.call("tt_tree_attn_bwd_stored", *args, n_pairs, HKV,
+                                     ws.data_ptr(), ws_bytes, ph, st, cs)
+        names = ("attn_bwd_dkdv_ds_tc", "attn_bwd_dq_ds_tc")
+    else:
+        phase = lambda ph: _lib.call("tt_tree_attn_bwd", *args, ws.data_ptr(), ws_bytes, ph,
+                                     st, cs)
+        names = ("attn_bwd_dkdv_tc", "attn_bwd_dq_tc")
     phase(_lib.TT_BWD_PREP)
     runs = {"attn_fwd_tc": lambda: attn_fwd_raw(q, k, v, md, scale),
-            "attn_bwd_dkdv_tc": lambda: phase(_lib.TT_BWD_DKDV),
-            "attn_bwd_dq_tc": lambda: phase(_lib.TT_BWD_DQ)}
-    flops = {"attn_fwd_tc": 4.0 * D * V * HQ, "attn_bwd_dkdv_tc": 8.0 * D * V * HQ,
-             "attn_bwd_dq_tc": 2.0 * D * V * HQ}       # useful: dQ's dS K only
-    executed = {"attn_fwd_tc": 4.0 * D * V * HQ, "attn_bwd_dkdv_tc": 8.0 * D * V * HQ,
-                "attn_bwd_dq_tc": 6.0 * D * V * HQ}
+            names[0]: lambda: phase(_lib.TT_BWD_DKDV),
+            names[1]: lambda: phase(_lib.TT_BWD_DQ)}
+    flops = {"attn_fwd_tc": 4.0 * D * V * HQ, names[0]: 8.0 * D * V * HQ,
+             names[1]: 2.0 * D * V * HQ}       # useful: dQ's dS K only
+    executed = dict(flops)
+    if not stored:
+        executed[names[1]] = 6.0 * D * V * HQ
     res = {}
     for name, fn in runs.items():
         fn()
@@ -619,23 +648,32 @@ def run_ours(args):
     pk, pk_src = peaks()
     # USEFUL FLOPs (the metric's basis: fwd 4*D*V, bwd 10*D*V per head) by
     # kernel: the forward's 2 GEMMs; dK/dV's 4 (S^T, dP^T, dV, dK) are the
-    # backward's recompute + dV + dK; dQ's one useful GEMM is dS K (it also
-    # re-executes S and dP, counted only under "executed" below)
+    # backward's recompute + dV + dK; dQ's one useful GEMM is dS K (the
+    # recompute schedule's dQ kernel also re-executes S and dP, counted only
+    # under "executed" below; the stored schedule's reads dS back instead)
     kflops = {"attn_fwd_tc": 4.0 * D * V * HQ, "attn_bwd_dkdv_tc": 8.0 * D * V * HQ,
-              "attn_bwd_dq_tc": 2.0 * D * V * HQ}
-    kexec = {"attn_fwd_tc": 4.0 * D * V * HQ, "attn_bwd_dkdv_tc": 8.0 * D * V * HQ,
-             "attn_bwd_dq_tc": 6.0 * D * V * HQ}
+              "attn_bwd_dq_tc": 2.0 * D * V * HQ, "attn_bwd_dkdv_ds_tc": 8.0 * D * V * HQ,
+              "attn_bwd_dq_ds_tc": 2.0 * D * V * HQ}
+    kexec = dict(kflops, attn_bwd_dq_tc=6.0 * D * V * HQ)
     kern["attn_fwd_tc"] = t_fwd
-    # dK/dV and dQ run concurrently on two streams, so the live unit of the
-    # backward is the pair: both kernels' FLOPs over the span of the longer one
-    # (each kernel alone is timed separately below, in roofline_isolated)
-    pair = ("attn_bwd_dkdv_tc", "attn_bwd_dq_tc")
-    t_pair = max(kern.get(n, 0.0) for n in pair)
-    pair_name = "attn_bwd_dkdv_tc + attn_bwd_dq_tc"
-    units = {"attn_fwd_tc": (kflops["attn_fwd_tc"], t_fwd),
-             pair_name: (kflops[pair[0]] + kflops[pair[1]], t_pair)}
-    units_exec = {"attn_fwd_tc": kexec["attn_fwd_tc"],
-                  pair_name: kexec[pair[0]] + kexec[pair[1]]}
+    stored = "attn_bwd_dkdv_ds_tc" in kern
+    units = {"attn_fwd_tc": (kflops["attn_fwd_tc"], t_fwd)}
+    units_exec = {"attn_fwd_tc": kexec["attn_fwd_tc"]}
+    if stored:
+        # one stream: every kernel's live duration is its own
+        pair = ("attn_bwd_dkdv_ds_tc", "attn_bwd_dq_ds_tc")
+        for n in pair:
+            units[n] = (kflops[n], kern[n])
+            units_exec[n] = kexec[n]
+    else:
+        # dK/dV and dQ run concurrently on two streams, so the live unit of the
+        # backward is the pair: both kernels' FLOPs over the span of the longer
+        # one (each kernel alone is timed separately below, in roofline_isolated)
+        pair = ("attn_bwd_dkdv_tc", "attn_bwd_dq_tc")
+        t_pair = max(kern.get(n, 0.0) for n in pair)
+        pair_name = "attn_bwd_dkdv_tc + attn_bwd_dq_tc"
+        units[pair_name] = (kflops[pair[0]] + kflops[pair[1]], t_pair)
+        units_exec[pair_name] = kexec[pair[0]] + kexec[pair[1]]
     dominant = max(units, key=lambda n: units[n][1])
     achieved = units[dominant][0] / units[dominant][1] / 1e12
     achieved_exec = units_exec[dominant] / units[dominant][1] / 1e12
@@ -687,8 +725,12 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "kernel": dominant,
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "flops_basis": "useful (fwd 4*D*V, bwd 10*D*V per head): the "
-                                        "backward pair counts dK/dV's 8*D*V and dQ's 2*D*V",
+                         "flops_basis": ("useful (fwd 4*D*V, bwd 10*D*V per head): dK/dV "
+                                         "counts 8*D*V, dQ 2*D*V"),
+                         "backward_schedule": ("stored dS: dK/dV stores each dS tile, dQ "
+                                               "sums dS K from them (one stream)" if stored
+                                               else "recompute: dQ recomputes S and dP, "
+                                                    "beside dK/dV on a second stream"),
                          "traffic_source": ("constant: ncu dram__bytes_read.sum + "
                                             "dram__bytes_write.sum of an 8k-token capture "
                                             "scaled by visible pairs "
@@ -698,9 +740,12 @@ def run_ours(args):
                          "frac_of_sustained": achieved / peak_sus},
             "roofline_executed": {"kernel": dominant, "achieved": achieved_exec,
                                   "frac": achieved_exec / peak,
-                                  "note": "executed FLOPs over the same span: dQ's "
-                                          "re-executed S and dP included (14*D*V per head "
-                                          "for the pair)"},
+                                  "note": ("executed FLOPs over the same span (the stored "
+                                           "schedule executes only the useful products)"
+                                           if stored else
+                                           "executed FLOPs over the same span: dQ's "
+                                           "re-executed S and dP included (14*D*V per head "
+                                           "for the pair)")},
             "step_useful_frac": value / world / peak,
             "gpu_launches": int(launches),
             "clocks": clk,
@@ -711,9 +756,8 @@ def run_ours(args):
             "bound": "tensor", "kernel": dom, "achieved": iso[dom]["achieved"], "peak": peak,
             "unit": "TFLOP/s", "frac": iso[dom]["frac"], "traffic": traffic_tab.get(dom),
             "per_kernel": iso,
-            "note": "each kernel timed alone on the same inputs after the timed region; the "
-                    "live roofline above is the backward's dK/dV + dQ pair, which run "
-                    "concurrently on two streams"}
+            "note": "each kernel timed alone on the same inputs after the timed region "
+                    "(the product's backward schedule)"}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample(meta, V)
             line["e2e"]["reference_packer"] = reference_packer_sample(roots, V)
@@ -1035,7 +1079,11 @@ def run_attn3(args):
     pk, pk_src = peaks()
     Vsum = sum(t["V"] for t in trees)
     kflops = {"attn_fwd_tc": 4.0 * D * Vsum * HQ3, "attn_bwd_dkdv_tc": 8.0 * D * Vsum * HQ3,
-              "attn_bwd_dq_tc": 6.0 * D * Vsum * HQ3}
+              "attn_bwd_dq_tc": 6.0 * D * Vsum * HQ3,
+              "attn_bwd_dkdv_ds_tc": 8.0 * D * Vsum * HQ3,
+              "attn_bwd_dq_ds_tc": 2.0 * D * Vsum * HQ3,
+              # the stored schedule in kv-head passes: delta + every pass's dK/dV and dQ
+              "attn_bwd_stored_passes": 10.0 * D * Vsum * HQ3}
     kern_step = {n: t * len(trees) for n, t in kern.items()}   # durations() is per tree
     # as for config 2: dK/dV and dQ run concurrently, so they are one live unit
     pair = ("attn_bwd_dkdv_tc", "attn_bwd_dq_tc")

@@ -226,6 +226,43 @@ int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t h
  * run them on two streams after PREP. */
 enum tt_bwd_phase { TT_BWD_PREP = 1, TT_BWD_DKDV = 2, TT_BWD_DQ = 4, TT_BWD_ALL = 7 };
 
+/* Workspace bytes for tt_tree_attn_bwd_stored: tt_tree_attn_bwd's workspace,
+ * one int32 per tile-list entry, and one 32 KB dS slot per (q head of a pass,
+ * tile-list entry), where a pass covers kv_heads_per_pass kv heads and their
+ * hq/hkv q heads each.  n_tile_pairs: at least the number of (q tile, kv tile)
+ * entries of the fwd lists (fwd_ptr[n_q tiles]).  Off the tcgen05 path (fp32,
+ * head_dim != 128) this is tt_tree_attn_bwd_workspace_size; -1 for an invalid
+ * n_tile_pairs / kv_heads_per_pass. */
+int64_t tt_tree_attn_bwd_stored_workspace_size(int dtype, int32_t n_q, int32_t n_kv, int32_t hq,
+                                               int32_t hkv, int32_t head_dim,
+                                               int64_t n_tile_pairs, int32_t kv_heads_per_pass);
+
+/* The same gradients as tt_tree_attn_bwd (all phases), scheduled without
+ * recomputing S and dP for dQ: the dK/dV kernel stores every 16-bit dS tile it
+ * forms into the workspace, and a second kernel sums dQ = scale * dS K over
+ * each q tile's kv list from those tiles.  Both sums run in a fixed order, so
+ * results are deterministic (dK/dV bit-identical to tt_tree_attn_bwd's).  The
+ * kv heads are processed kv_heads_per_pass at a time, which bounds the dS
+ * slots the workspace needs (tt_tree_attn_bwd_stored_workspace_size).  Off the
+ * tcgen05 path it runs tt_tree_attn_bwd.  phases: TT_BWD_ALL, or, when
+ * kv_heads_per_pass == hkv (one pass), PREP, DKDV and DQ as separate calls in
+ * that order with the same workspace (DQ reads the dS tiles DKDV stored, so
+ * unlike tt_tree_attn_bwd's the two are not independent).  Replaces the same
+ * autograd of the reference's SDPA call as tt_tree_attn_bwd
+ * (tree_grad_hybrid.py:533-535). */
+int tt_tree_attn_bwd_stored(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv,
+                            int32_t head_dim, const void* q, int64_t q_st, int64_t q_sh,
+                            const void* k, int64_t k_st, int64_t k_sh, const void* v,
+                            int64_t v_st, int64_t v_sh, const void* out, const void* dout,
+                            int64_t do_st, int64_t do_sh, const float* lse,
+                            const int32_t* kv_lo, const int32_t* kv_hi, const int32_t* fwd_ptr,
+                            const int32_t* fwd_list, const int32_t* bwd_ptr,
+                            const int32_t* bwd_list, float scale, void* dq, int64_t dq_st,
+                            int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
+                            int64_t dv_st, int64_t dv_sh, int64_t n_tile_pairs,
+                            int32_t kv_heads_per_pass, void* workspace, int64_t workspace_bytes,
+                            int phases, int32_t* status, void* stream);
+
 /* Allocation-free variant of tt_tree_attn_bwd (same arguments without the
  * workspace and phases; no counterpart in the reference).  For callers that
  * cannot pass a scratch buffer and must not have the library call cudaMalloc

@@ -129,6 +129,12 @@ def test_tile_lists_match_brute_force(seed, tq, tk):
             got_b[(int(e) >> 1, b)] = (int(e) & 1) == 0
     assert got_f == ref
     assert got_b == ref
+    # each kv tile's q tiles ascend: the stored-dS backward finds a (q tile,
+    # kv tile) pair's bwd entry from its fwd entry by binary search
+    for b in range(len(t["bwd_ptr"]) - 1):
+        qts = [int(e) >> 1 for e in t["bwd_list"][t["bwd_ptr"][b]:t["bwd_ptr"][b + 1]]]
+        assert qts == sorted(set(qts))
+    assert int(t["fwd_ptr"][-1]) == int(t["bwd_ptr"][-1])
     # full tiles must be really full: the kernels skip the mask test on them
     for (a, b), full in ref.items():
         assert got_f[(a, b)] == full

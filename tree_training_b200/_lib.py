@@ -59,6 +59,13 @@ SIGNATURES = {
                                 _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _F32,
                                 _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
                                 _P, _I64, _INT, _P, _P]),
+    "tt_tree_attn_bwd_stored_workspace_size": (_I64, [_INT, _I32, _I32, _I32, _I32, _I32,
+                                                      _I64, _I32]),
+    "tt_tree_attn_bwd_stored": (_INT, [_INT, _I32, _I32, _I32, _I32, _I32,
+                                       _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
+                                       _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _F32,
+                                       _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
+                                       _I64, _I32, _P, _I64, _INT, _P, _P]),
     "tt_tree_attn_bwd_noalloc": (_INT, [_INT, _I32, _I32, _I32, _I32, _I32,
                                         _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
                                         _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _F32,

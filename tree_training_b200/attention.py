@@ -10,6 +10,7 @@ tensor or a missing library raises.
 """
 from __future__ import annotations
 
+import os
 from typing import Optional, Tuple
 
 import numpy as np
@@ -103,6 +104,44 @@ def attn_fwd_raw(q, k, v, meta_dev, scale: float):
     return out, lse
 
 
+# Backward schedule on the tcgen05 path: "stored" (default) keeps every dS tile
+# the dK/dV kernel forms in a workspace and sums dQ from it; "recompute" runs
+# the dQ kernel that recomputes S and dP beside dK/dV on a second stream.
+_BWD_SCHEDULE = os.environ.get("TT_ATTN_BWD_SCHEDULE", "stored")
+# Most workspace bytes the stored schedule's dS slots may take; larger problems
+# run in passes over the kv heads (one pass needs rep * n_tile_pairs * 32 KB).
+_DS_WORKSPACE_CAP = int(float(os.environ.get("TT_ATTN_DS_WORKSPACE_GB", "16")) * (1 << 30))
+
+
+def set_backward_schedule(schedule: str) -> str:
+    """Select the tcgen05 backward schedule ("stored" or "recompute");
+    returns the previous one.  Both are deterministic and give dK/dV bit for
+    bit equal; dQ differs only by the rounding of its recomputed dS."""
+    global _BWD_SCHEDULE
+    if schedule not in ("stored", "recompute"):
+        raise ValueError(f"unknown backward schedule {schedule!r}")
+    prev, _BWD_SCHEDULE = _BWD_SCHEDULE, schedule
+    return prev
+
+
+def _stored_plan(dt, n_q, n_kv, hq, hkv, D, n_pairs):
+    """(kv heads per pass, workspace bytes) of the stored schedule: the most kv
+    heads whose dS slots fit the cap.  None when the schedule is off, the
+    problem is off the tcgen05 path, or one pass alone exceeds the cap (the
+    recompute schedule then runs)."""
+    if _BWD_SCHEDULE != "stored" or n_q == 0 or n_kv == 0:
+        return None
+    L = _lib.lib()
+    regular = int(L.tt_tree_attn_bwd_workspace_size(dt, n_q, n_kv, hq, hkv, D))
+    for p in range(hkv, 0, -1):
+        b = int(L.tt_tree_attn_bwd_stored_workspace_size(dt, n_q, n_kv, hq, hkv, D, n_pairs, p))
+        if b <= regular:
+            return None            # off the tcgen05 path: nothing is stored
+        if b - regular <= _DS_WORKSPACE_CAP:
+            return p, b
+    return None
+
+
 def attn_bwd_raw(dout, q, k, v, out, lse, meta_dev, scale: float):
     for n, t in (("dout", dout), ("q", q), ("k", k), ("v", v)):
         _check_tensor(n, t)
@@ -112,7 +151,12 @@ def attn_bwd_raw(dout, q, k, v, out, lse, meta_dev, scale: float):
     dq = torch.empty((n_q, hq, D), dtype=q.dtype, device=q.device)
     dk = torch.empty((n_kv, hkv, D), dtype=k.dtype, device=k.device)
     dv = torch.empty((n_kv, hkv, D), dtype=v.dtype, device=v.device)
-    ws_bytes = int(_lib.lib().tt_tree_attn_bwd_workspace_size(dt, n_q, n_kv, hq, hkv, D))
+    n_pairs = int(meta_dev["fwd_list"].numel())
+    plan = _stored_plan(dt, n_q, n_kv, hq, hkv, D, n_pairs)
+    if plan is not None:
+        ws_bytes = plan[1]
+    else:
+        ws_bytes = int(_lib.lib().tt_tree_attn_bwd_workspace_size(dt, n_q, n_kv, hq, hkv, D))
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)
     out = out.contiguous()
     args = [dt, n_q, n_kv, hq, hkv, D,
@@ -123,10 +167,34 @@ def attn_bwd_raw(dout, q, k, v, out, lse, meta_dev, scale: float):
             meta_dev["fwd_list"].data_ptr(), meta_dev["bwd_ptr"].data_ptr(),
             meta_dev["bwd_list"].data_ptr(), float(scale),
             dq.data_ptr(), dq.stride(0), dq.stride(1), dk.data_ptr(), dk.stride(0),
-            dk.stride(1), dv.data_ptr(), dv.stride(0), dv.stride(1), ws.data_ptr(), ws_bytes]
+            dk.stride(1), dv.data_ptr(), dv.stride(0), dv.stride(1)]
     status = _status_word(q.device).data_ptr()
     main = torch.cuda.current_stream(q.device)
     timer = _PHASE_TIMER
+    if plan is not None:
+        sargs = args + [n_pairs, plan[0], ws.data_ptr(), ws_bytes]
+        if plan[0] == hkv and timer is not None:
+            # one pass: the phases as separate calls, with events between them
+            timer.mark(main, "bwd_start")
+            _lib.call("tt_tree_attn_bwd_stored", *sargs, _lib.TT_BWD_PREP, status,
+                      main.cuda_stream)
+            timer.mark(main, "prep_done")
+            _lib.call("tt_tree_attn_bwd_stored", *sargs, _lib.TT_BWD_DKDV, status,
+                      main.cuda_stream)
+            timer.mark(main, "dkdv_done")
+            timer.mark(main, "dq_start")
+            _lib.call("tt_tree_attn_bwd_stored", *sargs, _lib.TT_BWD_DQ, status,
+                      main.cuda_stream)
+            timer.mark(main, "dq_done")
+        else:
+            if timer is not None:
+                timer.mark(main, "bwd_start")
+            _lib.call("tt_tree_attn_bwd_stored", *sargs, _lib.TT_BWD_ALL, status,
+                      main.cuda_stream)
+            if timer is not None:
+                timer.mark(main, "bwd_all_done")
+        return dq, dk, dv
+    args += [ws.data_ptr(), ws_bytes]
     if timer is not None:
         timer.mark(main, "bwd_start")
     _lib.call("tt_tree_attn_bwd", *args, _lib.TT_BWD_PREP, status, main.cuda_stream)

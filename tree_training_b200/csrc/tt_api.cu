@@ -130,3 +130,59 @@ extern "C" int tt_tree_attn_bwd(int dtype, int32_t n_q, int32_t n_kv, int32_t hq
                                  dk_sh, dv, dv_st, dv_sh, (float*)workspace, phases,
                                  (cudaStream_t)stream);
 }
+
+namespace {
+int64_t round256(int64_t b) { return (b + 255) / 256 * 256; }
+constexpr int64_t kDsSlotBytes = 32768;   // one 16-bit 128 x 128 dS tile
+}  // namespace
+
+extern "C" int64_t tt_tree_attn_bwd_stored_workspace_size(int dtype, int32_t n_q, int32_t n_kv,
+                                                          int32_t hq, int32_t hkv, int32_t D,
+                                                          int64_t n_tile_pairs,
+                                                          int32_t kv_heads_per_pass) {
+  const int64_t regular = tt_tree_attn_bwd_workspace_size(dtype, n_q, n_kv, hq, hkv, D);
+  if (!valid_dims(n_q, n_kv, hq, hkv, D) || !tc_path(dtype, D) || n_q == 0 || n_kv == 0)
+    return regular;
+  if (n_tile_pairs < 1 || kv_heads_per_pass < 1 || kv_heads_per_pass > hkv) return -1;
+  return regular + round256(n_tile_pairs * 4) +
+         static_cast<int64_t>(hq / hkv) * kv_heads_per_pass * n_tile_pairs * kDsSlotBytes;
+}
+
+extern "C" int tt_tree_attn_bwd_stored(
+    int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv, int32_t D, const void* q,
+    int64_t q_st, int64_t q_sh, const void* k, int64_t k_st, int64_t k_sh, const void* v,
+    int64_t v_st, int64_t v_sh, const void* out, const void* dout, int64_t do_st, int64_t do_sh,
+    const float* lse, const int32_t* kv_lo, const int32_t* kv_hi, const int32_t* fwd_ptr,
+    const int32_t* fwd_list, const int32_t* bwd_ptr, const int32_t* bwd_list, float scale,
+    void* dq, int64_t dq_st, int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
+    int64_t dv_st, int64_t dv_sh, int64_t n_tile_pairs, int32_t kv_heads_per_pass,
+    void* workspace, int64_t workspace_bytes, int phases, int32_t* status, void* stream) {
+  if (!valid_dims(n_q, n_kv, hq, hkv, D)) return TT_ERR_INVALID_ARG;
+  if (!tc_path(dtype, D) || n_q == 0 || n_kv == 0)
+    return tt_tree_attn_bwd(dtype, n_q, n_kv, hq, hkv, D, q, q_st, q_sh, k, k_st, k_sh, v, v_st,
+                            v_sh, out, dout, do_st, do_sh, lse, kv_lo, kv_hi, fwd_ptr, fwd_list,
+                            bwd_ptr, bwd_list, scale, dq, dq_st, dq_sh, dk, dk_st, dk_sh, dv,
+                            dv_st, dv_sh, workspace, workspace_bytes, phases, status, stream);
+  if (n_tile_pairs < 1 || kv_heads_per_pass < 1 || kv_heads_per_pass > hkv)
+    return TT_ERR_INVALID_ARG;
+  const int64_t need = tt_tree_attn_bwd_stored_workspace_size(dtype, n_q, n_kv, hq, hkv, D,
+                                                              n_tile_pairs, kv_heads_per_pass);
+  if (need < 0) return TT_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < need) return TT_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) || !q || !out || !dout || !lse || !dq ||
+      !fwd_ptr || !fwd_list || !k || !v || !dk || !dv || !kv_lo || !kv_hi || !bwd_ptr ||
+      !bwd_list)
+    return TT_ERR_INVALID_ARG;
+  char* ws = static_cast<char*>(workspace);
+  const int64_t delta_bytes = tt_attn_bwd_delta_bytes(n_q, hq);
+  const int64_t regular = tt_tree_attn_bwd_workspace_size(dtype, n_q, n_kv, hq, hkv, D);
+  int32_t* kt_order = reinterpret_cast<int32_t*>(ws + delta_bytes);
+  int32_t* e2f = reinterpret_cast<int32_t*>(ws + regular);
+  void* ds = ws + regular + round256(n_tile_pairs * 4);
+  return tt_launch_attn_bwd_sm100_stored(
+      dtype, n_q, n_kv, hq, hkv, D, q, q_st, q_sh, k, k_st, k_sh, v, v_st, v_sh, out, dout, do_st,
+      do_sh, lse, kv_lo, kv_hi, fwd_ptr, fwd_list, bwd_ptr, bwd_list, scale, dq, dq_st, dq_sh, dk,
+      dk_st, dk_sh, dv, dv_st, dv_sh, reinterpret_cast<float*>(ws), kt_order, e2f, ds,
+      n_tile_pairs, kv_heads_per_pass, phases, status, static_cast<cudaStream_t>(stream));
+}
+

@@ -75,6 +75,7 @@ struct BwdBarriers {
   uint64_t sdp_full[2];      // S and dP of a sub-tile ready (per TMEM buffer)
   uint64_t sdp_free[2];      // the elementwise warps loaded S and dP (256 arrivals)
   uint64_t ew_full[2];       // P / dS of a sub-tile written to shared memory (256 arrivals)
+  uint64_t pds_free[2];      // dK/dV storing dS: a P / dS buffer's MMAs and dS store are done
   uint64_t acc_done;         // every MMA of the CTA finished
   uint64_t drain;            // abort path of the S/dP issuer
   uint64_t drain_acc;        // abort path of the accumulation issuer
@@ -116,6 +117,7 @@ __device__ __forceinline__ void init_barriers(BwdBarriers* sh) {
     mbar_init(&sh->sdp_full[b], 1);
     mbar_init(&sh->sdp_free[b], kEwWarps);
     mbar_init(&sh->ew_full[b], kEwWarps);
+    mbar_init(&sh->pds_free[b], 2);   // the MMAs' commit + the dS store's read
   }
   mbar_init(&sh->acc_done, 1);
   mbar_init(&sh->drain, 1);
@@ -300,7 +302,12 @@ __device__ __forceinline__ void acc_issuer(BwdBarriers* sh, const volatile int32
 }
 
 // ===================================================================== dK/dV
-template <bool kBf16>
+// kStoreDS: the CTA also stores each 16-bit dS^T sub-tile it computes into the
+// workspace slot of its (q head, q tile, kv tile) triple, where the dQ-from-dS
+// kernel reads it back (ds_ws: the slots of q heads hk0 * rep ...; e2f: the
+// fwd-list index of every bwd-list entry; n_pairs: slots per q head).  The
+// CTA's kv head is hk0 + blockIdx.x.
+template <bool kBf16, bool kStoreDS>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -310,7 +317,8 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                  const float* __restrict__ delta, float scale_log2, float scale,
                  void* __restrict__ dk_, int64_t dk_st, int64_t dk_sh, void* __restrict__ dv_,
                  int64_t dv_st, int64_t dv_sh, const int32_t* __restrict__ kt_order,
-                 int32_t* status) {
+                 int32_t* status, int hk0, uint8_t* __restrict__ ds_ws,
+                 const int32_t* __restrict__ e2f, int64_t n_pairs) {
   using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
@@ -326,7 +334,7 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   const volatile int32_t* abort_flag = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hk = blockIdx.x;
+  const int hk = hk0 + static_cast<int>(blockIdx.x);
   // key tile: in work order (longest list first) when the order is given,
   // else in key order, where the root-side tiles with the longest lists come first
   const int kt = kt_order ? kt_order[blockIdx.y] : static_cast<int>(blockIdx.y);
@@ -383,12 +391,57 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       // A of dV += P^T dO and dK += dS^T Q: the P^T / dS^T tiles, K-major
       const uint64_t d_pt = desc_sw128(smem_u32(sPt), 16, 1024);
       const uint64_t d_dst = desc_sw128(smem_u32(sDSt), 16, 1024);
-      acc_issuer<kNbPDkdv, KS>(sh, abort_flag, status, n_u, [&](int s, int b, bool accumulate) {
+      auto acc = [&](int s, int b, bool accumulate) {
         mma_ss_k64(tmem + kColDV, desc_add(d_pt, b * kPTile), desc_add(d_do, s * kSubBytes),
                    id_o, accumulate);
         mma_ss_k64(tmem + kColDK, desc_add(d_dst, b * kPTile), desc_add(d_q, s * kSubBytes),
                    id_o, accumulate);
-      });
+      };
+      if constexpr (!kStoreDS) {
+        acc_issuer<kNbPDkdv, KS>(sh, abort_flag, status, n_u, acc);
+      } else {
+        // As acc_issuer, and after the MMAs of sub-tile u this thread also
+        // bulk-stores its dS^T buffer (16 KB, in the swizzled layout the dQ
+        // kernel's MMAs read) into the sub-tile's half of the workspace slot.
+        // Buffer b is rewritten two sub-tiles later, once pds_free[b] saw
+        // both the MMAs' commit and, one iteration on, the end of the
+        // store's shared-memory read.  The slot index of entry it + 1 is
+        // loaded one entry ahead.
+        const int n_it = n_u >> 1;
+        int f = 0, f_next = e2f[e0];
+        bool ok = true;
+        for (int u = 0; u < n_u && ok; ++u) {
+          const int b = u % kNbPDkdv, s = u % KS, it = u >> 1;
+          if ((u & 1) == 0) {
+            f = f_next;
+            if (it + 1 < n_it) f_next = e2f[e0 + (it + 1) % n_list];
+          }
+          if (!(ok = mbar_wait(&sh->ew_full[b], (u / kNbPDkdv) & 1, abort_flag))) break;
+          tc_fence_after();
+          acc(s, b, u > 0);
+          tc_commit(&sh->ab_empty[s]);
+          tc_commit(&sh->pds_free[b]);
+          if (f >= 0 && f < n_pairs) {
+            const int hl = hk * rep + it / n_list - hk0 * rep;   // q head within the pass
+            uint8_t* dst = ds_ws + (static_cast<int64_t>(hl) * n_pairs + f) * (2 * kPTile) +
+                           (u & 1) * kPTile;
+            bulk_store(dst, sDSt + b * kPTile, kPTile);
+          } else {
+            set_status(status, TT_ERR_WORKSPACE);   // a list entry without a slot
+          }
+          bulk_commit();
+          bulk_wait_read<1>();
+          if (u >= 1) mbar_arrive(&sh->pds_free[(u - 1) % kNbPDkdv]);
+        }
+        bulk_wait<0>();   // every store landed before the CTA's shared memory goes
+        if (ok) {
+          tc_commit(&sh->acc_done);
+        } else {
+          raise_abort(sh, status);
+          tc_commit(&sh->drain_acc);
+          mbar_wait(&sh->drain_acc, 0, nullptr);
+        }
+      }
     }
   } else {
     const int quad = warp & 3;
@@ -465,8 +518,12 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
       if (u >= kNbPDkdv) {                     // the MMAs of sub-tile u - 2 read this buffer
         // (buffer pb was last read by sub-tile u - 2, whose MMAs' commit
-        // releases ring stage (u - 2) % KS)
-        ok = mbar_wait(&sh->ab_empty[(u - kNbPDkdv) % KS], ((u - kNbPDkdv) / KS) & 1, abort_flag);
+        // releases ring stage (u - 2) % KS; storing dS, its store read it too)
+        if constexpr (kStoreDS)
+          ok = mbar_wait(&sh->pds_free[pb], ((u - kNbPDkdv) / kNbPDkdv) & 1, abort_flag);
+        else
+          ok = mbar_wait(&sh->ab_empty[(u - kNbPDkdv) % KS], ((u - kNbPDkdv) / KS) & 1,
+                         abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
       }
@@ -783,6 +840,186 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   }
 }
 
+// ================================================================ dQ from dS
+// The stored-dS backward's second kernel: dQ = scale * sum over the q tile's
+// kv list of dS K, where dS is read back from the workspace slots the dK/dV
+// kernel stored (no recompute of S and dP).  One CTA per (q head, 128-row q
+// tile), q tiles in reverse order (the deepest tiles, with the longest lists,
+// first).  Warp 0 streams (dS slot, K tile) pairs through a 3-stage ring (the
+// 32 KB slot by one bulk copy, K by TMA), warp 1 issues dQ += dS K
+// (M = 128 rows, N = 128 dims, K = 128 keys: A = dS, MN-major, read from the
+// two 64-row dS^T sub-tiles of the slot; B = K, MN-major), in list order, so
+// the sum is deterministic; warps 2-5 write dQ.
+constexpr int kStagesDqs = 3;
+constexpr int kThreadsDqs = 192;
+struct DqsBarriers {
+  uint64_t full[kStagesDqs];
+  uint64_t empty[kStagesDqs];
+  uint64_t acc_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int32_t abort;
+};
+constexpr size_t kSmemDqs = 1024 + kStagesDqs * 2 * kTileBytes + sizeof(DqsBarriers);
+static_assert(kSmemDqs <= 232448, "shared memory per block");
+
+template <bool kBf16>
+__global__ void __launch_bounds__(kThreadsDqs, 1)
+attn_bwd_dq_ds_tc(const __grid_constant__ CUtensorMap tm_k, int n_q, int rep, int h0,
+                  const int32_t* __restrict__ fwd_ptr, const int32_t* __restrict__ fwd_list,
+                  const uint8_t* __restrict__ ds_ws, int64_t n_pairs, float scale,
+                  void* __restrict__ dq_, int64_t dq_st, int64_t dq_sh, int32_t* status) {
+  using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
+  constexpr int KS = kStagesDqs;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  uint8_t* rDS = base;                          // KS x dS slot (two 64-row dS^T sub-tiles)
+  uint8_t* rK = rDS + KS * kTileBytes;          // KS x K tile
+  DqsBarriers* sh = reinterpret_cast<DqsBarriers*>(rK + KS * kTileBytes);
+  const volatile int32_t* abort_flag = &sh->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hl = static_cast<int>(blockIdx.x);  // q head within the pass
+  const int h = h0 + hl, hk = h / rep;
+  const int qt = gridDim.y - 1 - blockIdx.y;
+  const int e0 = fwd_ptr[qt];
+  int n_u = fwd_ptr[qt + 1] - e0;                // kv tiles
+  if (e0 < 0 || static_cast<int64_t>(e0) + n_u > n_pairs) {
+    if (threadIdx.x == 0) set_status(status, TT_ERR_WORKSPACE);   // list past the slots
+    n_u = 0;
+  }
+  const uint8_t* slots = ds_ws + (static_cast<int64_t>(hl) * n_pairs + e0) * kTileBytes;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&sh->full[s], 1);
+      mbar_init(&sh->empty[s], 1);
+    }
+    mbar_init(&sh->acc_done, 1);
+    mbar_init(&sh->drain, 1);
+    sh->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sh->tmem_base, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0 && n_u > 0) {
+      prefetch_tmap(&tm_k);
+      int issued[KS] = {};
+      bool ok = true;
+      for (int u = 0; u < n_u; ++u) {
+        const int s = u % KS;
+        if (u >= KS && !(ok = mbar_wait(&sh->empty[s], ((u / KS) - 1) & 1, abort_flag))) break;
+        const int j0 = (fwd_list[e0 + u] >> 1) * kT;
+        mbar_arrive_expect_tx(&sh->full[s], 2 * kTileBytes);
+        bulk_load(rDS + s * kTileBytes, slots + static_cast<int64_t>(u) * kTileBytes, kTileBytes,
+                  &sh->full[s]);
+        tma_load_3d(rK + s * kTileBytes, &tm_k, &sh->full[s], 0, j0, hk);
+        tma_load_3d(rK + s * kTileBytes + kTileHalf, &tm_k, &sh->full[s], 64, j0, hk);
+        issued[s] += 1;
+      }
+      if (!ok) {
+        set_status(status, TT_ERR_DEVICE_TIMEOUT);
+        *reinterpret_cast<volatile int32_t*>(&sh->abort) = 1;
+        for (int s = 0; s < KS; ++s)
+          if (issued[s] > 0) mbar_wait(&sh->full[s], (issued[s] - 1) & 1, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_u > 0) {
+      constexpr uint32_t id = idesc_f16_ab(kBf16, kT, kD, true, true);
+      const uint64_t d_ds = desc_sw128(smem_u32(rDS), kPTile, 1024);   // A, MN-major
+      const uint64_t d_k = desc_sw128(smem_u32(rK), kTileHalf, 1024);  // B, MN-major
+      bool ok = true;
+      for (int u = 0; u < n_u && ok; ++u) {
+        const int s = u % KS;
+        if (!(ok = mbar_wait(&sh->full[s], (u / KS) & 1, abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kT / 16; ++kk)
+          mma_ss(tmem, desc_add(d_ds, s * kTileBytes + kk * 2048),
+                 desc_add(d_k, s * kTileBytes + kk * 2048), id, (u > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&sh->empty[s]);
+      }
+      if (ok) {
+        tc_commit(&sh->acc_done);
+      } else {
+        set_status(status, TT_ERR_DEVICE_TIMEOUT);
+        *reinterpret_cast<volatile int32_t*>(&sh->abort) = 1;
+        tc_commit(&sh->drain);
+        mbar_wait(&sh->drain, 0, nullptr);
+      }
+    }
+  } else if (warp >= 2 && warp < 6) {
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;              // q row within the tile = TMEM lane
+    const int row = qt * kT + r;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    bool ok = true;
+    if (n_u > 0) {
+      ok = mbar_wait(&sh->acc_done, 0, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      T* dq = reinterpret_cast<T*>(dq_) + static_cast<int64_t>(row) * dq_st + h * dq_sh;
+#pragma unroll 1
+      for (int c = 0; c < kD / 32; ++c) {
+        float a[32];
+        if (n_u > 0) {
+          tmem_ld32(lane_addr + c * 32, a);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) a[i] = 0.f;
+        }
+        if (row < n_q) store_row32<kBf16>(dq + c * 32, a, scale);
+      }
+    } else {
+      set_status(status, TT_ERR_DEVICE_TIMEOUT);
+      *reinterpret_cast<volatile int32_t*>(&sh->abort) = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+// e2f[e] = the index in the fwd lists of bwd-list entry e (the same
+// (q tile, kv tile) pair): a bwd list holds its q tiles in ascending order, so
+// each fwd entry finds its bwd entry by binary search.  Entries left unset
+// keep the caller's -1, which the storing dK/dV kernel reports instead of
+// storing.  One block per q tile.
+__global__ void map_bwd_to_fwd(int n_qt, const int32_t* __restrict__ fwd_ptr,
+                               const int32_t* __restrict__ fwd_list,
+                               const int32_t* __restrict__ bwd_ptr,
+                               const int32_t* __restrict__ bwd_list, int n_kt,
+                               int32_t* __restrict__ e2f) {
+  const int qt = blockIdx.x;
+  if (qt >= n_qt) return;
+  for (int f = fwd_ptr[qt] + threadIdx.x; f < fwd_ptr[qt + 1]; f += blockDim.x) {
+    const int kt = fwd_list[f] >> 1;
+    if (kt < 0 || kt >= n_kt) continue;
+    int lo = bwd_ptr[kt], hi = bwd_ptr[kt + 1];
+    const int end = hi;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if ((bwd_list[mid] >> 1) < qt) lo = mid + 1;
+      else hi = mid;
+    }
+    if (lo < end && (bwd_list[lo] >> 1) == qt) e2f[lo] = f;
+  }
+}
+
 // order[r] = the key tile with the r-th longest work list (ties: lower tile
 // first), so the dK/dV CTAs that take longest are dispatched first.  Thread i
 // counts the tiles that sort before tile i; n_tiles^2 comparisons in all.
@@ -952,7 +1189,7 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
     if ((rc = make_map(&mk, bf16, k, n_kv, hkv, k_st, k_sh, kT)) != TT_OK) return rc;
     if ((rc = make_map(&mv, bf16, v, n_kv, hkv, v_st, v_sh, kT)) != TT_OK) return rc;
     if ((rc = make_map(&mdo, bf16, dout, n_q, hq, do_st, do_sh, kSub)) != TT_OK) return rc;
-    auto kdkdv = bf16 ? attn_bwd_dkdv_tc<true> : attn_bwd_dkdv_tc<false>;
+    auto kdkdv = bf16 ? attn_bwd_dkdv_tc<true, false> : attn_bwd_dkdv_tc<false, false>;
     TT_CUDA_OK(cudaFuncSetAttribute(kdkdv, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemDkdv));
     const int n_tiles = (n_kv + kT - 1) / kT;
@@ -963,7 +1200,8 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
     dim3 g(hkv, n_tiles);
     kdkdv<<<g, kThreads, kSmemDkdv, st>>>(mq, mk, mv, mdo, n_q, n_kv, rep, kv_lo, kv_hi,
                                            bwd_ptr, bwd_list, lse, delta, scale_log2, scale, dk,
-                                           dk_st, dk_sh, dv, dv_st, dv_sh, kt_order, status);
+                                           dk_st, dk_sh, dv, dv_st, dv_sh, kt_order, status,
+                                           0, nullptr, nullptr, 0);
     ++launches;
   }
   if (phases & TT_BWD_DQ) {
@@ -981,6 +1219,86 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
                                          fwd_list, lse, delta, scale_log2, scale, dq, dq_st,
                                          dq_sh, status);
     ++launches;
+  }
+  tt_count_launches(launches);
+  return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
+}
+
+// The stored-dS backward (tt_tree_attn_bwd_stored): PREP = delta, the
+// bwd -> fwd entry map and the work order of the key tiles; then per pass of
+// kv_heads_per_pass kv heads DKDV = the storing dK/dV kernel and DQ = the
+// dQ-from-dS kernel of the pass's q heads.  ds_ws holds
+// rep * kv_heads_per_pass * n_pairs slots of 32 KB (n_pairs >= the number of
+// tile-list entries), e2f n_pairs int32.  With one pass the phases may be
+// launched by separate calls, in the order PREP, DKDV, DQ.
+int tt_launch_attn_bwd_sm100_stored(
+    int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv, int32_t D, const void* q,
+    int64_t q_st, int64_t q_sh, const void* k, int64_t k_st, int64_t k_sh, const void* v,
+    int64_t v_st, int64_t v_sh, const void* out, const void* dout, int64_t do_st, int64_t do_sh,
+    const float* lse, const int32_t* kv_lo, const int32_t* kv_hi, const int32_t* fwd_ptr,
+    const int32_t* fwd_list, const int32_t* bwd_ptr, const int32_t* bwd_list, float scale,
+    void* dq, int64_t dq_st, int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
+    int64_t dv_st, int64_t dv_sh, float* delta, int32_t* kt_order, int32_t* e2f, void* ds_ws,
+    int64_t n_pairs, int32_t kv_heads_per_pass, int phases, int32_t* status, cudaStream_t st) {
+  using namespace tt::sm100;
+  if (D != kD || (dtype != TT_BF16 && dtype != TT_F16)) return TT_ERR_UNSUPPORTED;
+  if (n_q == 0 || n_kv == 0)   // one side empty: the regular path zeroes the other side
+    return tt_launch_attn_bwd_sm100(dtype, n_q, n_kv, hq, hkv, D, q, q_st, q_sh, k, k_st, k_sh,
+                                    v, v_st, v_sh, out, dout, do_st, do_sh, lse, kv_lo, kv_hi,
+                                    fwd_ptr, fwd_list, bwd_ptr, bwd_list, scale, dq, dq_st, dq_sh,
+                                    dk, dk_st, dk_sh, dv, dv_st, dv_sh, delta, kt_order,
+                                    TT_BWD_ALL, status, st);
+  if (kv_heads_per_pass < 1 || kv_heads_per_pass > hkv || n_pairs < 1 || !e2f || !ds_ws ||
+      (reinterpret_cast<uintptr_t>(ds_ws) & 15) || !aligned16(e2f) || !kt_order ||
+      (phases & ~TT_BWD_ALL) != 0 || phases == 0 ||
+      (phases != TT_BWD_ALL && kv_heads_per_pass != hkv))
+    return TT_ERR_INVALID_ARG;
+  int rc = TT_OK;
+  const bool bf16 = dtype == TT_BF16;
+  const float scale_log2 = scale * 1.4426950408889634f;
+  const int rep = hq / hkv;
+  const int n_kt = (n_kv + kT - 1) / kT, n_qt = (n_q + kT - 1) / kT;
+  int launches = 0;
+  if (phases & TT_BWD_PREP) {
+    // delta (and the argument checks) as in the regular backward, then the
+    // entry map and the work order of the key tiles
+    rc = tt_launch_attn_bwd_sm100(dtype, n_q, n_kv, hq, hkv, D, q, q_st, q_sh, k, k_st, k_sh, v,
+                                  v_st, v_sh, out, dout, do_st, do_sh, lse, kv_lo, kv_hi,
+                                  fwd_ptr, fwd_list, bwd_ptr, bwd_list, scale, dq, dq_st, dq_sh,
+                                  dk, dk_st, dk_sh, dv, dv_st, dv_sh, delta, kt_order,
+                                  TT_BWD_PREP, status, st);
+    if (rc != TT_OK) return rc;
+    TT_CUDA_OK(cudaMemsetAsync(e2f, 0xFF, static_cast<size_t>(n_pairs) * 4, st));
+    map_bwd_to_fwd<<<n_qt, 128, 0, st>>>(n_qt, fwd_ptr, fwd_list, bwd_ptr, bwd_list, n_kt, e2f);
+    order_tiles_by_work<<<(n_kt + 255) / 256, 256, 0, st>>>(n_kt, bwd_ptr, kt_order);
+    launches += 2;
+  }
+  CUtensorMap mq, mk, mv, mdo;
+  if ((rc = make_map(&mq, bf16, q, n_q, hq, q_st, q_sh, kSub)) != TT_OK) return rc;
+  if ((rc = make_map(&mk, bf16, k, n_kv, hkv, k_st, k_sh, kT)) != TT_OK) return rc;
+  if ((rc = make_map(&mv, bf16, v, n_kv, hkv, v_st, v_sh, kT)) != TT_OK) return rc;
+  if ((rc = make_map(&mdo, bf16, dout, n_q, hq, do_st, do_sh, kSub)) != TT_OK) return rc;
+  auto kdkdv = bf16 ? attn_bwd_dkdv_tc<true, true> : attn_bwd_dkdv_tc<false, true>;
+  auto kdq = bf16 ? attn_bwd_dq_ds_tc<true> : attn_bwd_dq_ds_tc<false>;
+  TT_CUDA_OK(cudaFuncSetAttribute(kdkdv, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kSmemDkdv));
+  TT_CUDA_OK(cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kSmemDqs));
+  for (int g0 = 0; g0 < hkv; g0 += kv_heads_per_pass) {
+    const int ng = hkv - g0 < kv_heads_per_pass ? hkv - g0 : kv_heads_per_pass;
+    if (phases & TT_BWD_DKDV) {
+      kdkdv<<<dim3(ng, n_kt), kThreads, kSmemDkdv, st>>>(
+          mq, mk, mv, mdo, n_q, n_kv, rep, kv_lo, kv_hi, bwd_ptr, bwd_list, lse, delta,
+          scale_log2, scale, dk, dk_st, dk_sh, dv, dv_st, dv_sh, kt_order, status, g0,
+          static_cast<uint8_t*>(ds_ws), e2f, n_pairs);
+      ++launches;
+    }
+    if (phases & TT_BWD_DQ) {
+      kdq<<<dim3(ng * rep, n_qt), kThreadsDqs, kSmemDqs, st>>>(
+          mk, n_q, rep, g0 * rep, fwd_ptr, fwd_list, static_cast<const uint8_t*>(ds_ws),
+          n_pairs, scale, dq, dq_st, dq_sh, status);
+      ++launches;
+    }
   }
   tt_count_launches(launches);
   return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;

@@ -95,6 +95,16 @@ int tt_launch_attn_bwd_sm100(int dtype, int32_t n_q, int32_t n_kv, int32_t hq, i
                              int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
                              int64_t dv_st, int64_t dv_sh, float* delta, int32_t* kt_order,
                              int phases, int32_t* status, cudaStream_t stream);
+int tt_launch_attn_bwd_sm100_stored(
+    int dtype, int32_t n_q, int32_t n_kv, int32_t hq, int32_t hkv, int32_t D, const void* q,
+    int64_t q_st, int64_t q_sh, const void* k, int64_t k_st, int64_t k_sh, const void* v,
+    int64_t v_st, int64_t v_sh, const void* out, const void* dout, int64_t do_st, int64_t do_sh,
+    const float* lse, const int32_t* kv_lo, const int32_t* kv_hi, const int32_t* fwd_ptr,
+    const int32_t* fwd_list, const int32_t* bwd_ptr, const int32_t* bwd_list, float scale,
+    void* dq, int64_t dq_st, int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh, void* dv,
+    int64_t dv_st, int64_t dv_sh, float* delta, int32_t* kt_order, int32_t* e2f, void* ds_ws,
+    int64_t n_pairs, int32_t kv_heads_per_pass, int phases, int32_t* status,
+    cudaStream_t stream);
 
 // Bytes of the fp32 row terms (delta) at the start of the backward workspace.
 inline int64_t tt_attn_bwd_delta_bytes(int32_t n_q, int32_t hq) {

@@ -95,6 +95,30 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// 1-D bulk copy this CTA's shared memory -> global, tracked by the issuing
+// thread's bulk group (bulk_commit / bulk_wait_read / bulk_wait).  Both
+// addresses 16-byte aligned, size % 16 == 0.
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(dst)),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most N of this thread's committed bulk groups still read
+// their shared-memory source (the source may be overwritten after this).
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until at most N of this thread's committed bulk groups are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -157,6 +181,11 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool ab_bf16, int M, int N, boo
          | (0u << 15)                               // A K-major
          | ((b_mn ? 1u : 0u) << 16)                 // B major
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// The same with A MN-major as well (a_mn: A's M index is the contiguous one).
+__host__ __device__ constexpr uint32_t idesc_f16_ab(bool ab_bf16, int M, int N, bool a_mn,
+                                                    bool b_mn) {
+  return idesc_f16(ab_bf16, M, N, b_mn) | ((a_mn ? 1u : 0u) << 15);
 }
 
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
