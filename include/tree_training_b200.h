@@ -352,13 +352,21 @@ int tt_gdn_tree_bwd(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int
  * distinct node indices; captured: fp32 [n_capture, H, Dk, Dv].  The
  * backward takes their gradients, dcaptured fp32 [n_capture, H, Dk, Dv] (or
  * NULL), and adds each to the gradient of the node's output state.  With
- * n_capture = 0 these are tt_gdn_tree_fwd / tt_gdn_tree_bwd. */
+ * n_capture = 0 these are tt_gdn_tree_fwd / tt_gdn_tree_bwd.
+ * q_token_stride, k_token_stride, v_token_stride: elements from one token's
+ * q / k / v row to the next (each row still [heads, dim] contiguous), 0 for
+ * packed rows; a nonzero stride below the packed row (Hk * Dk, Hk * Dk,
+ * H * Dv) is TT_ERR_INVALID_ARG.  This reads q, k and v in place as the
+ * columns of one token-major [S, 2 Hk Dk + H Dv] buffer, the split the
+ * reference's layer makes of the conv output (dfs_tree_forward.py:403-410).
+ * dq, dk, dv stay packed. */
 int tt_gdn_tree_fwd_ex(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
                        const void* q, const void* k, const void* v, const float* g,
                        const float* beta, int32_t n_nodes, const int32_t* bounds,
                        const int32_t* parents, const float* initial_state, int flags,
                        void* out, float* last_state, int32_t n_capture,
-                       const int32_t* capture_nodes, float* captured, void* workspace,
+                       const int32_t* capture_nodes, float* captured, int64_t q_token_stride,
+                       int64_t k_token_stride, int64_t v_token_stride, void* workspace,
                        int64_t workspace_bytes, void* stream);
 
 int tt_gdn_tree_bwd_ex(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv,
@@ -367,7 +375,8 @@ int tt_gdn_tree_bwd_ex(int dtype, int32_t S, int32_t Hk, int32_t H, int32_t Dk, 
                        const int32_t* parents, const float* initial_state, int flags,
                        const void* dout, const float* dlast, int32_t n_capture,
                        const int32_t* capture_nodes, const float* dcaptured, void* dq, void* dk,
-                       void* dv, float* dg, float* dbeta, float* dinit, void* workspace,
+                       void* dv, float* dg, float* dbeta, float* dinit, int64_t q_token_stride,
+                       int64_t k_token_stride, int64_t v_token_stride, void* workspace,
                        int64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
@@ -451,6 +460,25 @@ int tt_tree_conv_bwd(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
                      const int32_t* succ_ptr, const int32_t* succ_tok, const int32_t* succ_lag,
                      const void* dout, void* dx, float* dweight, float* dbias,
                      void* workspace, int64_t workspace_bytes, void* stream);
+
+/* The conv with its output (forward) or output gradient (backward) in
+ * token-major memory, [S, C] with channel rows contiguous: the layout the
+ * reference's layer reads after transposing the conv output and splitting it
+ * into q / k / v (dfs_tree_forward.py:403-410), so those views need no
+ * transposing copy.  x and dx stay [C, S].  With out_token_major /
+ * dout_token_major = 0 these are tt_tree_conv_fwd / tt_tree_conv_bwd.  The
+ * token-major forms need S % 4 == 0, C % 8 == 0 and 16-byte aligned x, out,
+ * dout, dx and workspace (else TT_ERR_UNSUPPORTED). */
+int tt_tree_conv_fwd_ex(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
+                        const float* weight, const float* bias, const int32_t* pred, void* out,
+                        int32_t out_token_major, void* stream);
+
+int tt_tree_conv_bwd_ex(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
+                        const float* weight, const float* bias, const int32_t* pred,
+                        const int32_t* succ_ptr, const int32_t* succ_tok,
+                        const int32_t* succ_lag, const void* dout, int32_t dout_token_major,
+                        void* dx, float* dweight, float* dbias, void* workspace,
+                        int64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -355,3 +355,105 @@ def test_gdn_tensor_core_gemm_matches_cuda_core_gemm(dtype, tol):
 class _Info:
     def __init__(self, bounds, parents):
         self.chunk_boundaries, self.chunk_parent_map = bounds, parents
+
+
+@pytest.mark.parametrize("K,dtype", [(4, torch.bfloat16), (4, torch.float32), (2, torch.float32),
+                                     (5, torch.bfloat16), (7, torch.float32)])
+def test_tree_conv_four_token_kernels_match_one_token_kernels(K, dtype):
+    """The conv kernels that take 4 tokens per thread (S % 4 == 0, 16-byte
+    aligned rows) against the 1-token kernels on the same data placed one
+    element off alignment: the same arithmetic per output, so out, dx and the
+    input gradient of the SiLU agree bit for bit; dw and db are summed in
+    another order."""
+    from tree_training_b200 import _lib
+    from tree_training_b200.gdn import TreeConvPlan, _tree_arrays
+    info = tt.build_dfs_tree_info(random_branching_tree(17, 4000, 1, 60))
+    S, C = info.N, 24
+    assert S % 4 == 0
+    bounds, parents = _tree_arrays(info.chunk_boundaries, info.chunk_parent_map)
+    plan = TreeConvPlan(bounds, parents, K, DEV)
+    g = torch.Generator(device=DEV).manual_seed(K)
+    x = torch.randn(C * S, generator=g, device=DEV).to(dtype)
+    dy = torch.randn(C * S, generator=g, device=DEV).to(dtype)
+    w = torch.randn(C, K, generator=g, device=DEV) * 0.5
+    b = torch.randn(C, generator=g, device=DEV) * 0.1
+    dt = {torch.float32: _lib.TT_F32, torch.bfloat16: _lib.TT_BF16}[dtype]
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+
+    def run(off):
+        xb = torch.zeros(C * S + off, dtype=dtype, device=DEV)
+        dyb = torch.zeros_like(xb)
+        xb[off:] = x
+        dyb[off:] = dy
+        out = torch.zeros_like(xb)
+        dx = torch.zeros_like(xb)
+        dw = torch.zeros(C, K, device=DEV)
+        db = torch.zeros(C, device=DEV)
+        ws_bytes = int(_lib.lib().tt_tree_conv_bwd_workspace_size(C, S, K))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=DEV)
+        es = xb.element_size()
+        _lib.call("tt_tree_conv_fwd", dt, C, S, K, xb.data_ptr() + off * es, w.data_ptr(),
+                  b.data_ptr(), plan.pred.data_ptr(), out.data_ptr() + off * es, stream)
+        _lib.call("tt_tree_conv_bwd", dt, C, S, K, xb.data_ptr() + off * es, w.data_ptr(),
+                  b.data_ptr(), plan.pred.data_ptr(), plan.succ_ptr.data_ptr(),
+                  plan.succ_tok.data_ptr(), plan.succ_lag.data_ptr(),
+                  dyb.data_ptr() + off * es, dx.data_ptr() + off * es, dw.data_ptr(),
+                  db.data_ptr(), ws.data_ptr(), ws_bytes, stream)
+        torch.cuda.synchronize()
+        return out[off:], dx[off:], dw, db
+
+    quad, single = run(0), run(1)
+    assert torch.equal(quad[0], single[0])
+    assert torch.equal(quad[1], single[1])
+    for a, r in zip(quad[2:], single[2:]):
+        assert rel(a.cpu().numpy(), r.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_token_major_conv_and_in_place_gdn_rows_match_packed(dtype):
+    """The layer's path with the conv output in token-major memory (q / k / v
+    split off it as views, read in place by the GDN, the conv gradient read
+    token-major) against the same path with every tensor packed: the conv
+    output, the GDN output and dq/dk/dv/dg/dbeta and dx agree bit for bit (the
+    same arithmetic per element); dw is summed over other token blocks."""
+    from tree_training_b200.gdn import _conv_plan, _conv_fwd_op, _tree_arrays
+    Hk, H, D, K = 2, 4, 64, 4
+    C = 2 * Hk * D + H * D
+    info = tt.build_dfs_tree_info(random_branching_tree(23, 1200, 16, 120))
+    S = info.N
+    if S % 4:
+        pytest.skip("tree size not a multiple of 4")
+    bounds, parents = _tree_arrays(info.chunk_boundaries, info.chunk_parent_map)
+    plan = _conv_plan(bounds, parents, K, DEV)
+    gen = torch.Generator(device=DEV).manual_seed(5)
+    x0 = torch.randn(C, S, generator=gen, device=DEV).to(dtype)
+    w0 = torch.randn(C, K, generator=gen, device=DEV) * 0.5
+    g0 = torch.nn.functional.logsigmoid(torch.randn(S, H, generator=gen, device=DEV))
+    b0 = torch.sigmoid(torch.randn(S, H, generator=gen, device=DEV))
+    do = torch.randn(1, S, H, D, generator=gen, device=DEV).to(dtype)
+
+    def run(token_major):
+        x = x0.clone().requires_grad_(True)
+        w = w0.clone().requires_grad_(True)
+        gg = g0.clone().unsqueeze(0).requires_grad_(True)
+        bt = b0.clone().unsqueeze(0).requires_grad_(True)
+        y = _conv_fwd_op(x, w, w.new_empty(0), False, plan.pred, plan.succ_ptr, plan.succ_tok,
+                         plan.succ_lag, token_major)
+        assert (y.stride() == (1, C)) == token_major
+        q, k, v = torch.split(y.t().unsqueeze(0), [Hk * D, Hk * D, H * D], dim=-1)
+        q, k, v = q.reshape(1, S, Hk, D), k.reshape(1, S, Hk, D), v.reshape(1, S, H, D)
+        if not token_major:
+            q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        else:
+            assert q.stride(1) == C and not q.is_contiguous()
+        out, _ = torch_chunk_gated_delta_rule_tree_varlen(
+            q, k, v, gg, bt, bounds, parents, use_qk_l2norm_in_kernel=True)
+        out.backward(do)
+        torch.cuda.synchronize()
+        return y.detach().contiguous(), out.detach(), x.grad, w.grad, gg.grad, bt.grad
+
+    tm, pk = run(True), run(False)
+    for a, b in zip(tm[:3], pk[:3]):        # conv out, GDN out, conv dx
+        assert torch.equal(a, b)
+    assert torch.equal(tm[4], pk[4]) and torch.equal(tm[5], pk[5])   # dg, dbeta
+    assert rel(tm[3].cpu().numpy(), pk[3].cpu().numpy()) < 1e-5       # dw

@@ -79,10 +79,11 @@ SIGNATURES = {
                                _I32, _P, _P, _P, _INT, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                _I64, _P]),
     "tt_gdn_tree_fwd_ex": (_INT, [_INT, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P,
-                                  _I32, _P, _P, _P, _INT, _P, _P, _I32, _P, _P, _P, _I64, _P]),
+                                  _I32, _P, _P, _P, _INT, _P, _P, _I32, _P, _P, _I64, _I64,
+                                  _I64, _P, _I64, _P]),
     "tt_gdn_tree_bwd_ex": (_INT, [_INT, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P,
                                   _I32, _P, _P, _P, _INT, _P, _P, _I32, _P, _P, _P, _P, _P,
-                                  _P, _P, _P, _P, _I64, _P]),
+                                  _P, _P, _P, _I64, _I64, _I64, _P, _I64, _P]),
     "tt_ce_fwd_grad": (_INT, [_INT, _I32, _I32, _P, _I64, _P, _P, _I64, _P, _INT, _P]),
     "tt_qk_norm_rope_fwd": (_INT, [_INT, _I64, _I32, _I32, _P, _P, _P, _P, _F32, _P, _P]),
     "tt_qk_norm_rope_bwd_blocks": (_INT, [_I64]),
@@ -95,9 +96,12 @@ SIGNATURES = {
     "tt_conv_predecessors": (_INT, [_I32, _P, _P, _I32, _P]),
     "tt_conv_successors": (_INT, [_I32, _I32, _P, _P, _P, _P, _I64]),
     "tt_tree_conv_fwd": (_INT, [_INT, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),
+    "tt_tree_conv_fwd_ex": (_INT, [_INT, _I32, _I32, _I32, _P, _P, _P, _P, _P, _I32, _P]),
     "tt_tree_conv_bwd_workspace_size": (_I64, [_I32, _I32, _I32]),
     "tt_tree_conv_bwd": (_INT, [_INT, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                 _P, _P, _P, _I64, _P]),
+    "tt_tree_conv_bwd_ex": (_INT, [_INT, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P,
+                                   _I32, _P, _P, _P, _P, _I64, _P]),
 }
 
 _lib = None

@@ -843,19 +843,25 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
 // ================================================================ dQ from dS
 // The stored-dS backward's second kernel: dQ = scale * sum over the q tile's
 // kv list of dS K, where dS is read back from the workspace slots the dK/dV
-// kernel stored (no recompute of S and dP).  One CTA per (q head, 128-row q
-// tile), q tiles in reverse order (the deepest tiles, with the longest lists,
-// first).  Warp 0 streams (dS slot, K tile) pairs through a 3-stage ring (the
-// 32 KB slot by one bulk copy, K by TMA), warp 1 issues dQ += dS K
-// (M = 128 rows, N = 128 dims, K = 128 keys: A = dS, MN-major, read from the
-// two 64-row dS^T sub-tiles of the slot; B = K, MN-major), in list order, so
-// the sum is deterministic; warps 2-5 write dQ.
+// kernel stored (no recompute of S and dP).  Persistent: one CTA per SM walks
+// the work items (q head of the pass, 128-row q tile), item i = q tile
+// n_qt - 1 - i / n_heads (the deepest tiles, with the longest lists, first;
+// the heads of one q tile next to each other, so their K tiles meet in L2),
+// head i % n_heads, CTA c taking items c, c + grid, ...  Warp 0 streams the
+// (dS slot, K tile) pairs of all its items through a 3-stage ring (the 32 KB
+// slot by one bulk copy, K by TMA); warp 1 issues dQ += dS K (M = 128 rows,
+// N = 128 dims, K = 128 keys: A = dS, MN-major, read from the two 64-row dS^T
+// sub-tiles of the slot; B = K, MN-major) in list order, so the sum is
+// deterministic, into one of two TMEM accumulators (item parity); warps 2-5
+// write an item's dQ while the next item accumulates in the other one.
 constexpr int kStagesDqs = 3;
 constexpr int kThreadsDqs = 192;
+constexpr int kEpiWarpsDqs = 4;
 struct DqsBarriers {
   uint64_t full[kStagesDqs];
   uint64_t empty[kStagesDqs];
-  uint64_t acc_done;
+  uint64_t acc_full[2];      // an item's accumulation finished (MMA commit)
+  uint64_t acc_empty[2];     // the epilogue read the accumulator (4 warp arrivals)
   uint64_t drain;
   uint32_t tmem_base;
   int32_t abort;
@@ -866,9 +872,10 @@ static_assert(kSmemDqs <= 232448, "shared memory per block");
 template <bool kBf16>
 __global__ void __launch_bounds__(kThreadsDqs, 1)
 attn_bwd_dq_ds_tc(const __grid_constant__ CUtensorMap tm_k, int n_q, int rep, int h0,
-                  const int32_t* __restrict__ fwd_ptr, const int32_t* __restrict__ fwd_list,
-                  const uint8_t* __restrict__ ds_ws, int64_t n_pairs, float scale,
-                  void* __restrict__ dq_, int64_t dq_st, int64_t dq_sh, int32_t* status) {
+                  int n_heads, int n_qt, const int32_t* __restrict__ fwd_ptr,
+                  const int32_t* __restrict__ fwd_list, const uint8_t* __restrict__ ds_ws,
+                  int64_t n_pairs, float scale, void* __restrict__ dq_, int64_t dq_st,
+                  int64_t dq_sh, int32_t* status) {
   using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
   constexpr int KS = kStagesDqs;
   extern __shared__ uint8_t smem_raw[];
@@ -876,32 +883,42 @@ attn_bwd_dq_ds_tc(const __grid_constant__ CUtensorMap tm_k, int n_q, int rep, in
   uint8_t* rDS = base;                          // KS x dS slot (two 64-row dS^T sub-tiles)
   uint8_t* rK = rDS + KS * kTileBytes;          // KS x K tile
   DqsBarriers* sh = reinterpret_cast<DqsBarriers*>(rK + KS * kTileBytes);
-  const volatile int32_t* abort_flag = &sh->abort;
+  volatile int32_t* abort_flag = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hl = static_cast<int>(blockIdx.x);  // q head within the pass
-  const int h = h0 + hl, hk = h / rep;
-  const int qt = gridDim.y - 1 - blockIdx.y;
-  const int e0 = fwd_ptr[qt];
-  int n_u = fwd_ptr[qt + 1] - e0;                // kv tiles
-  if (e0 < 0 || static_cast<int64_t>(e0) + n_u > n_pairs) {
-    if (threadIdx.x == 0) set_status(status, TT_ERR_WORKSPACE);   // list past the slots
-    n_u = 0;
-  }
-  const uint8_t* slots = ds_ws + (static_cast<int64_t>(hl) * n_pairs + e0) * kTileBytes;
+  const int n_items = n_heads * n_qt;
+  // an item's q tile, q head within the pass and kv list [e0, e0 + n)
+  // (a list that would run past the slots is reported and treated as empty)
+  auto item = [&](int i, int* qt, int* hl, int* e0, int* n) {
+    *qt = n_qt - 1 - i / n_heads;
+    *hl = i % n_heads;
+    *e0 = fwd_ptr[*qt];
+    *n = fwd_ptr[*qt + 1] - *e0;
+    if (*e0 < 0 || *n < 0 || static_cast<int64_t>(*e0) + *n > n_pairs) {
+      set_status(status, TT_ERR_WORKSPACE);
+      *n = 0;
+    }
+  };
+  auto give_up = [&]() {
+    set_status(status, TT_ERR_DEVICE_TIMEOUT);
+    *abort_flag = 1;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < KS; ++s) {
       mbar_init(&sh->full[s], 1);
       mbar_init(&sh->empty[s], 1);
     }
-    mbar_init(&sh->acc_done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh->acc_full[b], 1);
+      mbar_init(&sh->acc_empty[b], kEpiWarpsDqs);
+    }
     mbar_init(&sh->drain, 1);
     sh->abort = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(&sh->tmem_base, 128);
+    tmem_alloc(&sh->tmem_base, 256);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -910,87 +927,105 @@ attn_bwd_dq_ds_tc(const __grid_constant__ CUtensorMap tm_k, int n_q, int rep, in
   const uint32_t tmem = sh->tmem_base;
 
   if (warp == 0) {
-    if (lane == 0 && n_u > 0) {
+    if (lane == 0) {
       prefetch_tmap(&tm_k);
       int issued[KS] = {};
       bool ok = true;
-      for (int u = 0; u < n_u; ++u) {
-        const int s = u % KS;
-        if (u >= KS && !(ok = mbar_wait(&sh->empty[s], ((u / KS) - 1) & 1, abort_flag))) break;
-        const int j0 = (fwd_list[e0 + u] >> 1) * kT;
-        mbar_arrive_expect_tx(&sh->full[s], 2 * kTileBytes);
-        bulk_load(rDS + s * kTileBytes, slots + static_cast<int64_t>(u) * kTileBytes, kTileBytes,
-                  &sh->full[s]);
-        tma_load_3d(rK + s * kTileBytes, &tm_k, &sh->full[s], 0, j0, hk);
-        tma_load_3d(rK + s * kTileBytes + kTileHalf, &tm_k, &sh->full[s], 64, j0, hk);
-        issued[s] += 1;
+      int u = 0;                                 // ring position over all items
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+        int qt, hl, e0, n;
+        item(i, &qt, &hl, &e0, &n);
+        const int hk = (h0 + hl) / rep;
+        const uint8_t* slots = ds_ws + (static_cast<int64_t>(hl) * n_pairs + e0) * kTileBytes;
+        for (int j = 0; j < n; ++j, ++u) {
+          const int s = u % KS;
+          if (u >= KS && !(ok = mbar_wait(&sh->empty[s], ((u / KS) - 1) & 1, abort_flag))) break;
+          const int j0 = (fwd_list[e0 + j] >> 1) * kT;
+          mbar_arrive_expect_tx(&sh->full[s], 2 * kTileBytes);
+          bulk_load(rDS + s * kTileBytes, slots + static_cast<int64_t>(j) * kTileBytes,
+                    kTileBytes, &sh->full[s]);
+          tma_load_3d(rK + s * kTileBytes, &tm_k, &sh->full[s], 0, j0, hk);
+          tma_load_3d(rK + s * kTileBytes + kTileHalf, &tm_k, &sh->full[s], 64, j0, hk);
+          issued[s] += 1;
+        }
       }
       if (!ok) {
-        set_status(status, TT_ERR_DEVICE_TIMEOUT);
-        *reinterpret_cast<volatile int32_t*>(&sh->abort) = 1;
+        give_up();
         for (int s = 0; s < KS; ++s)
           if (issued[s] > 0) mbar_wait(&sh->full[s], (issued[s] - 1) & 1, nullptr);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && n_u > 0) {
+    if (lane == 0) {
       constexpr uint32_t id = idesc_f16_ab(kBf16, kT, kD, true, true);
       const uint64_t d_ds = desc_sw128(smem_u32(rDS), kPTile, 1024);   // A, MN-major
       const uint64_t d_k = desc_sw128(smem_u32(rK), kTileHalf, 1024);  // B, MN-major
       bool ok = true;
-      for (int u = 0; u < n_u && ok; ++u) {
-        const int s = u % KS;
-        if (!(ok = mbar_wait(&sh->full[s], (u / KS) & 1, abort_flag))) break;
+      int u = 0, it = 0;
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++it) {
+        int qt, hl, e0, n;
+        item(i, &qt, &hl, &e0, &n);
+        const int b = it & 1;
+        // the epilogue has read this accumulator's previous item
+        if (it >= 2 && !(ok = mbar_wait(&sh->acc_empty[b], ((it >> 1) - 1) & 1, abort_flag)))
+          break;
         tc_fence_after();
+        for (int j = 0; j < n; ++j, ++u) {
+          const int s = u % KS;
+          if (!(ok = mbar_wait(&sh->full[s], (u / KS) & 1, abort_flag))) break;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kT / 16; ++kk)
-          mma_ss(tmem, desc_add(d_ds, s * kTileBytes + kk * 2048),
-                 desc_add(d_k, s * kTileBytes + kk * 2048), id, (u > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&sh->empty[s]);
+          for (int kk = 0; kk < kT / 16; ++kk)
+            mma_ss(tmem + 128 * b, desc_add(d_ds, s * kTileBytes + kk * 2048),
+                   desc_add(d_k, s * kTileBytes + kk * 2048), id, (j > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&sh->empty[s]);
+        }
+        if (ok) tc_commit(&sh->acc_full[b]);
       }
-      if (ok) {
-        tc_commit(&sh->acc_done);
-      } else {
-        set_status(status, TT_ERR_DEVICE_TIMEOUT);
-        *reinterpret_cast<volatile int32_t*>(&sh->abort) = 1;
+      if (!ok) {
+        give_up();
         tc_commit(&sh->drain);
         mbar_wait(&sh->drain, 0, nullptr);
       }
     }
-  } else if (warp >= 2 && warp < 6) {
+  } else if (warp < 2 + kEpiWarpsDqs) {
     const int quad = warp & 3;
     const int r = quad * 32 + lane;              // q row within the tile = TMEM lane
-    const int row = qt * kT + r;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    bool ok = true;
-    if (n_u > 0) {
-      ok = mbar_wait(&sh->acc_done, 0, abort_flag);
+    int it = 0;
+    for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++it) {
+      int qt, hl, e0, n;
+      item(i, &qt, &hl, &e0, &n);
+      const int b = it & 1;
+      bool ok = mbar_wait(&sh->acc_full[b], (it >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok) {
+      if (!ok) {
+        give_up();
+        break;
+      }
       tc_fence_after();
-      T* dq = reinterpret_cast<T*>(dq_) + static_cast<int64_t>(row) * dq_st + h * dq_sh;
+      const int row = qt * kT + r;
+      T* dq = reinterpret_cast<T*>(dq_) + static_cast<int64_t>(row) * dq_st + (h0 + hl) * dq_sh;
 #pragma unroll 1
       for (int c = 0; c < kD / 32; ++c) {
         float a[32];
-        if (n_u > 0) {
-          tmem_ld32(lane_addr + c * 32, a);
+        if (n > 0) {
+          tmem_ld32(lane_addr + 128 * b + c * 32, a);
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) a[i] = 0.f;
+          for (int x = 0; x < 32; ++x) a[x] = 0.f;
         }
         if (row < n_q) store_row32<kBf16>(dq + c * 32, a, scale);
       }
-    } else {
-      set_status(status, TT_ERR_DEVICE_TIMEOUT);
-      *reinterpret_cast<volatile int32_t*>(&sh->abort) = 1;
+      tc_fence_before();
+      warp_arrive(&sh->acc_empty[b], lane);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 256);
   }
 }
 
@@ -1284,6 +1319,9 @@ int tt_launch_attn_bwd_sm100_stored(
                                   (int)kSmemDkdv));
   TT_CUDA_OK(cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)kSmemDqs));
+  int dev = 0, n_sm = 0;
+  TT_CUDA_OK(cudaGetDevice(&dev));
+  TT_CUDA_OK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
   for (int g0 = 0; g0 < hkv; g0 += kv_heads_per_pass) {
     const int ng = hkv - g0 < kv_heads_per_pass ? hkv - g0 : kv_heads_per_pass;
     if (phases & TT_BWD_DKDV) {
@@ -1294,9 +1332,10 @@ int tt_launch_attn_bwd_sm100_stored(
       ++launches;
     }
     if (phases & TT_BWD_DQ) {
-      kdq<<<dim3(ng * rep, n_qt), kThreadsDqs, kSmemDqs, st>>>(
-          mk, n_q, rep, g0 * rep, fwd_ptr, fwd_list, static_cast<const uint8_t*>(ds_ws),
-          n_pairs, scale, dq, dq_st, dq_sh, status);
+      const int n_items = ng * rep * n_qt;
+      kdq<<<n_items < n_sm ? n_items : n_sm, kThreadsDqs, kSmemDqs, st>>>(
+          mk, n_q, rep, g0 * rep, ng * rep, n_qt, fwd_ptr, fwd_list,
+          static_cast<const uint8_t*>(ds_ws), n_pairs, scale, dq, dq_st, dq_sh, status);
       ++launches;
     }
   }

@@ -247,6 +247,356 @@ conv_bwd_dx(int C, int S, const float* __restrict__ w, const float* __restrict__
     if (cc < n_ch) dx[(int64_t)(c0 + cc) * S + t] = from_f32<T>(acc[cc]);
 }
 
+// ---- four tokens per thread --------------------------------------------------
+// The two backward kernels with each thread on 4 consecutive tokens (one 8- or
+// 16-byte access per channel row instead of four 2- or 4-byte ones) for
+// S % 4 == 0 and 16-byte aligned rows.  (The forward keeps one token per
+// thread: on the config-4 tree its 4-token form measured 0.56 ms against
+// 0.37 ms.)  A group whose 4 tokens all have the
+// plain window pred_m(t) = t - m (the inside of a node, K <= 5) reads its
+// whole window as two quads x[t0-4 .. t0+3]; other groups gather per token as
+// above.  Per output the arithmetic and its order are those of the kernels
+// above; the dw partials add each thread's 4 tokens before the warp sum.
+constexpr int kConvThr4 = kConvTok / 4;     // threads per block: still 256 tokens
+
+template <typename T>
+struct alignas(4 * sizeof(T)) Quad {
+  T v[4];
+};
+
+template <typename T>
+__device__ __forceinline__ void ld_quad(const T* p, float* out) {
+  const Quad<T> q = *reinterpret_cast<const Quad<T>*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) out[i] = to_f32(q.v[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void st_quad(T* p, const float* in) {
+  Quad<T> q;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q.v[i] = from_f32<T>(in[i]);
+  *reinterpret_cast<Quad<T>*>(p) = q;
+}
+
+// pr[i][m] = pred_{m+1}(t0 + i); returns whether all four windows are plain.
+template <int K>
+__device__ __forceinline__ bool load_pred4(const int32_t* __restrict__ pred, int t0,
+                                           int (&pr)[4][K > 1 ? K - 1 : 1]) {
+  bool plain = K <= 5 && t0 >= 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    pr[i][0] = -1;
+#pragma unroll
+    for (int m = 0; m < K - 1; ++m) {
+      pr[i][m] = pred[(int64_t)(t0 + i) * (K - 1) + m];
+      plain &= pr[i][m] == t0 + i - 1 - m;
+    }
+  }
+  return plain;
+}
+
+// The 4-token kernels hold the windows of half their channels at a time
+// (registers: 4 channels x 4 tokens x K floats).
+constexpr int kHalfCh = kConvCh / 2;
+
+// xs[cc][i][m] = x[c0 + cc][pred_m(t0 + i)] (0 where the path is shorter)
+template <typename T, int K>
+__device__ __forceinline__ void load_windows4(const T* __restrict__ x, int C, int S, int c0,
+                                              int t0, bool plain,
+                                              const int (&pr)[4][K > 1 ? K - 1 : 1],
+                                              float (&xs)[kHalfCh][4][K]) {
+#pragma unroll
+  for (int cc = 0; cc < kHalfCh; ++cc) {
+    const T* xc = x + (int64_t)min(c0 + cc, C - 1) * S;
+    if (plain) {
+      float q[8];
+      ld_quad(xc + t0 - 4, q);
+      ld_quad(xc + t0, q + 4);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int m = 0; m < K; ++m) xs[cc][i][m] = q[4 + i - m];
+    } else {
+      float q[4];
+      ld_quad(xc + t0, q);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        xs[cc][i][0] = q[i];
+#pragma unroll
+        for (int m = 1; m < K; ++m)
+          xs[cc][i][m] = pr[i][m - 1] >= 0 ? to_f32(xc[pr[i][m - 1]]) : 0.f;
+      }
+    }
+  }
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kConvThr4)
+conv_bwd_dpre4(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
+               const float* __restrict__ bias, const int32_t* __restrict__ pred,
+               const T* __restrict__ dy, float* __restrict__ dpre, float* __restrict__ part,
+               int nb) {
+  const int t0 = (blockIdx.x * kConvThr4 + threadIdx.x) * 4;
+  const int c0 = blockIdx.y * kConvCh;
+  const bool live = t0 < S;                 // S % 4 == 0: a live group is whole
+  const int tl = live ? t0 : 0;
+  int pr[4][K > 1 ? K - 1 : 1];
+  const bool plain = load_pred4<K>(pred, tl, pr);
+  __shared__ float red[kConvCh][kPartW][kConvThr4 / 32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll 1
+  for (int hc = 0; hc < kConvCh; hc += kHalfCh) {
+    float xs[kHalfCh][4][K], g[kHalfCh][4];
+    load_windows4<T, K>(x, C, S, c0 + hc, tl, plain, pr, xs);
+#pragma unroll
+    for (int cc = 0; cc < kHalfCh; ++cc)
+      ld_quad(dy + (int64_t)min(c0 + hc + cc, C - 1) * S + tl, g[cc]);
+#pragma unroll
+    for (int cc = 0; cc < kHalfCh; ++cc) {
+      const int c = c0 + hc + cc;
+      if (c >= C) break;                     // the same for the whole block
+      const float* wc = w + (int64_t)c * K;
+      float d[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float pre = bias ? bias[c] : 0.f;
+#pragma unroll
+        for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[cc][i][m], pre);
+        const float sg = 1.f / (1.f + __expf(-pre));
+        d[i] = live ? g[cc][i] * sg * (1.f + pre * (1.f - sg)) : 0.f;
+      }
+      if (live)
+        *reinterpret_cast<float4*>(dpre + (int64_t)c * S + t0) = make_float4(d[0], d[1], d[2], d[3]);
+#pragma unroll
+      for (int j = 0; j < kPartW; ++j) {
+        if (j >= K && j != 8) {
+          if (lane == 0) red[hc + cc][j][wid] = 0.f;
+          continue;
+        }
+        float v = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v += j == 8 ? d[i] : d[i] * xs[cc][i][j < K ? K - 1 - j : 0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[hc + cc][j][wid] = v;
+      }
+    }
+  }
+  __syncthreads();
+  const int n_ch = min(kConvCh, C - c0);
+  for (int i = threadIdx.x; i < n_ch * kPartW; i += kConvThr4) {
+    const int cc = i / kPartW, j = i % kPartW;
+    float v = 0.f;
+#pragma unroll
+    for (int q = 0; q < kConvThr4 / 32; ++q) v += red[cc][j][q];
+    part[((int64_t)(c0 + cc) * nb + blockIdx.x) * kPartW + j] = v;
+  }
+}
+
+// dx of 4 tokens: a group whose tokens' successors are exactly t+1 .. t+K-1
+// (lags 1 .. K-1, in that order: the inside of a node) reads dpre[t0 .. t0+7]
+// as two quads; other groups walk each token's successor list as conv_bwd_dx.
+template <typename T, int K>
+__global__ void __launch_bounds__(kConvThr4)
+conv_bwd_dx4(int C, int S, const float* __restrict__ w, const float* __restrict__ dpre,
+             const int32_t* __restrict__ sp, const int32_t* __restrict__ stok,
+             const int32_t* __restrict__ slag, T* __restrict__ dx) {
+  const int t0 = (blockIdx.x * kConvThr4 + threadIdx.x) * 4;
+  if (t0 >= S) return;
+  const int c0 = blockIdx.y * kConvCh;
+  const int n_ch = min(kConvCh, C - c0);
+  int e[5];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) e[i] = sp[t0 + i];
+  bool plain = K <= 5 && t0 + 8 <= S;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    plain &= e[i + 1] - e[i] == K - 1;
+#pragma unroll
+    for (int m = 0; m < K - 1; ++m)
+      if (plain) plain &= stok[e[i] + m] == t0 + i + 1 + m && slag[e[i] + m] == m + 1;
+  }
+  float acc[kConvCh][4];
+  if (plain) {
+#pragma unroll
+    for (int cc = 0; cc < kConvCh; ++cc) {
+      const int64_t c = min(c0 + cc, C - 1);
+      const float4 a = *reinterpret_cast<const float4*>(dpre + c * S + t0);
+      const float4 b = *reinterpret_cast<const float4*>(dpre + c * S + t0 + 4);
+      const float q[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float s = w[c * K + K - 1] * q[i];
+#pragma unroll
+        for (int l = 1; l < K; ++l) s = fmaf(w[c * K + K - 1 - l], q[i + l], s);
+        acc[cc][i] = s;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int cc = 0; cc < kConvCh; ++cc) {
+      const int64_t c = min(c0 + cc, C - 1);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[cc][i] = w[c * K + K - 1] * dpre[c * S + t0 + i];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      for (int ee = e[i]; ee < e[i + 1]; ++ee) {
+        const int u = stok[ee], l = slag[ee];
+#pragma unroll
+        for (int cc = 0; cc < kConvCh; ++cc) {
+          const int64_t c = min(c0 + cc, C - 1);
+          acc[cc][i] = fmaf(w[c * K + K - 1 - l], dpre[c * S + u], acc[cc][i]);
+        }
+      }
+  }
+#pragma unroll
+  for (int cc = 0; cc < kConvCh; ++cc)
+    if (cc < n_ch) st_quad(dx + (int64_t)(c0 + cc) * S + t0, acc[cc]);
+}
+
+// ---- token-major side ----------------------------------------------------------
+// The conv output and its gradient in token-major memory ([S, C], channel rows
+// contiguous: what the layer's transpose + split into q / k / v reads without a
+// transposing copy).  One block per 64 channels x 128 tokens: warp w computes
+// channels 8w .. 8w+7 of the tile, lane l tokens 4l .. 4l+3 (the loads of x
+// along tokens as in the 4-token kernels), and the tile is transposed through
+// shared memory (channel rows padded by 4 bytes: the column reads of the other
+// side fall in distinct banks), so the token-major side moves whole 128-byte
+// (16-bit) or 256-byte (fp32) channel segments per token.  Needs S % 4 == 0,
+// C % 8 == 0 and 16-byte aligned bases.
+constexpr int kTmCh = 64;                    // channels per tile (8 warps x kConvCh)
+constexpr int kTmTok = 128;                  // tokens per tile (32 lanes x 4)
+constexpr int kTmThreads = 256;
+
+template <typename T>
+struct TmTile {
+  static constexpr int kLd = kTmTok + 4 / static_cast<int>(sizeof(T));   // padded row (elements)
+  T v[kTmCh][kLd];
+};
+
+// Channels [c0, c0 + 64) x tokens [t0, t0 + 128) of tile `sm` <-> token-major
+// rows: warp w takes tokens t0 + w, t0 + w + 8, ...; lane l channels 2l, 2l+1.
+template <typename T, bool kToGlobal>
+__device__ __forceinline__ void tm_tile_rows(TmTile<T>& sm, T* tm, int C, int S, int c0, int t0) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = c0 + 2 * lane;
+  if (c >= C) return;                        // C % 8 == 0: channel pairs are whole
+  struct alignas(2 * sizeof(T)) Pair {
+    T a, b;
+  };
+  for (int r = warp; r < kTmTok; r += kTmThreads / 32) {
+    const int t = t0 + r;
+    if (t >= S) break;
+    Pair* g = reinterpret_cast<Pair*>(tm + (int64_t)t * C + c);
+    if (kToGlobal) {
+      *g = Pair{sm.v[2 * lane][r], sm.v[2 * lane + 1][r]};
+    } else {
+      const Pair p = *g;
+      sm.v[2 * lane][r] = p.a;
+      sm.v[2 * lane + 1][r] = p.b;
+    }
+  }
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kTmThreads)
+conv_fwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
+            const float* __restrict__ bias, const int32_t* __restrict__ pred,
+            T* __restrict__ out_tm) {
+  __shared__ TmTile<T> sm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cb = blockIdx.y * kTmCh, tb = blockIdx.x * kTmTok;
+  const int c0 = cb + warp * kConvCh, t0 = tb + lane * 4;
+  if (t0 < S && c0 < C) {
+    int pr[4][K > 1 ? K - 1 : 1];
+    const bool plain = load_pred4<K>(pred, t0, pr);
+#pragma unroll 1
+    for (int hc = 0; hc < kConvCh; hc += kHalfCh) {
+      float xs[kHalfCh][4][K];
+      load_windows4<T, K>(x, C, S, c0 + hc, t0, plain, pr, xs);
+#pragma unroll
+      for (int cc = 0; cc < kHalfCh; ++cc) {
+        const int c = min(c0 + hc + cc, C - 1);
+        const float* wc = w + (int64_t)c * K;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float pre = bias ? bias[c] : 0.f;
+#pragma unroll
+          for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[cc][i][m], pre);
+          sm.v[warp * kConvCh + hc + cc][lane * 4 + i] = from_f32<T>(silu(pre));
+        }
+      }
+    }
+  }
+  __syncthreads();
+  tm_tile_rows<T, true>(sm, out_tm, C, S, cb, tb);
+}
+
+// dpre (channel-major fp32) from x (channel-major) and dy (token-major), and
+// per (channel, 128-token block) the dw / db partials.  Each warp owns its 8
+// channels, so a partial is one warp sum, written by lane 0.
+template <typename T, int K>
+__global__ void __launch_bounds__(kTmThreads)
+conv_bwd_dpre_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
+                 const float* __restrict__ bias, const int32_t* __restrict__ pred,
+                 const T* __restrict__ dy_tm, float* __restrict__ dpre, float* __restrict__ part,
+                 int nb) {
+  __shared__ TmTile<T> sm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cb = blockIdx.y * kTmCh, tb = blockIdx.x * kTmTok;
+  const int c0 = cb + warp * kConvCh, t0 = tb + lane * 4;
+  tm_tile_rows<T, false>(sm, const_cast<T*>(dy_tm), C, S, cb, tb);
+  __syncthreads();
+  if (c0 >= C) return;                       // whole warps: no block-wide syncs below
+  const bool live = t0 < S;                  // S % 4 == 0: a live group is whole
+  const int tl = live ? t0 : 0;
+  int pr[4][K > 1 ? K - 1 : 1];
+  const bool plain = load_pred4<K>(pred, tl, pr);
+#pragma unroll 1
+  for (int hc = 0; hc < kConvCh; hc += kHalfCh) {
+    float xs[kHalfCh][4][K];
+    load_windows4<T, K>(x, C, S, c0 + hc, tl, plain, pr, xs);
+#pragma unroll
+    for (int cc = 0; cc < kHalfCh; ++cc) {
+      const int c = c0 + hc + cc;
+      if (c >= C) break;                     // the same for the whole warp
+      const float* wc = w + (int64_t)c * K;
+      float d[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float pre = bias ? bias[c] : 0.f;
+#pragma unroll
+        for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[cc][i][m], pre);
+        const float sg = 1.f / (1.f + __expf(-pre));
+        const float g = live ? to_f32(sm.v[warp * kConvCh + hc + cc][lane * 4 + i]) : 0.f;
+        d[i] = live ? g * sg * (1.f + pre * (1.f - sg)) : 0.f;
+      }
+      if (live)
+        *reinterpret_cast<float4*>(dpre + (int64_t)c * S + t0) =
+            make_float4(d[0], d[1], d[2], d[3]);
+#pragma unroll
+      for (int j = 0; j < kPartW; ++j) {
+        float v = 0.f;
+        if (j < K || j == 8) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            v += j == 8 ? d[i] : d[i] * xs[cc][i][j < K ? K - 1 - j : 0];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        }
+        if (lane == 0) part[((int64_t)c * nb + blockIdx.x) * kPartW + j] = v;
+      }
+    }
+  }
+}
+
+inline bool quad_ok(int S, const void* a, const void* b, const void* c) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return S % 4 == 0 && al(a) && al(b) && al(c);
+}
+
 // f(std::integral_constant<int, K>()) for the runtime window length K in 1..8
 template <typename Fn>
 int by_k(int K, Fn fn) {
@@ -276,16 +626,30 @@ int by_dtype(int dtype, Fn fn) {
 }  // namespace
 }  // namespace tt
 
-extern "C" int tt_tree_conv_fwd(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
-                                const float* weight, const float* bias, const int32_t* pred,
-                                void* out, void* stream) {
+namespace {
+bool tm_ok(int C, int S, const void* a, const void* b, const void* c) {
+  return C % 8 == 0 && tt::quad_ok(S, a, b, c);
+}
+}  // namespace
+
+extern "C" int tt_tree_conv_fwd_ex(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
+                                   const float* weight, const float* bias, const int32_t* pred,
+                                   void* out, int32_t out_token_major, void* stream) {
   if (C < 0 || S < 0 || K < 1 || K > 8) return TT_ERR_INVALID_ARG;
   if (C == 0 || S == 0) return TT_OK;
   if (!x || !weight || !out || (K > 1 && !pred)) return TT_ERR_INVALID_ARG;
+  if (out_token_major && !tm_ok(C, S, x, out, out)) return TT_ERR_UNSUPPORTED;
   return tt::by_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     return tt::by_k(K, [&](auto kc) {
       constexpr int KK = decltype(kc)::value;
+      if (out_token_major) {
+        dim3 g((S + tt::kTmTok - 1) / tt::kTmTok, (C + tt::kTmCh - 1) / tt::kTmCh);
+        tt::conv_fwd_tm<T, KK><<<g, tt::kTmThreads, 0, (cudaStream_t)stream>>>(
+            C, S, (const T*)x, weight, bias, pred, (T*)out);
+        tt_count_launches(1);
+        return cudaGetLastError() == cudaSuccess ? (int)TT_OK : (int)TT_ERR_CUDA;
+      }
       dim3 g((S + tt::kConvTok - 1) / tt::kConvTok, (C + tt::kConvCh - 1) / tt::kConvCh);
       tt::conv_fwd<T, KK><<<g, tt::kConvTok, 0, (cudaStream_t)stream>>>(
           C, S, (const T*)x, weight, bias, pred, (T*)out);
@@ -295,10 +659,72 @@ extern "C" int tt_tree_conv_fwd(int dtype, int32_t C, int32_t S, int32_t K, cons
   });
 }
 
+extern "C" int tt_tree_conv_fwd(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
+                                const float* weight, const float* bias, const int32_t* pred,
+                                void* out, void* stream) {
+  return tt_tree_conv_fwd_ex(dtype, C, S, K, x, weight, bias, pred, out, 0, stream);
+}
+
 extern "C" int64_t tt_tree_conv_bwd_workspace_size(int32_t C, int32_t S, int32_t K) {
   if (C < 0 || S < 0 || K < 1 || K > 8) return -1;
-  const int64_t nb = ((int64_t)S + tt::kConvTok - 1) / tt::kConvTok;
+  // dpre, then the dw / db partials per (channel, block of 128 tokens: the
+  // token-major kernels' blocks; the channel-major ones use 256-token blocks)
+  const int64_t nb = ((int64_t)S + tt::kTmTok - 1) / tt::kTmTok;
   return (int64_t)C * S * 4 + (int64_t)C * nb * tt::kPartW * 4 + 256;
+}
+
+extern "C" int tt_tree_conv_bwd_ex(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
+                                   const float* weight, const float* bias, const int32_t* pred,
+                                   const int32_t* succ_ptr, const int32_t* succ_tok,
+                                   const int32_t* succ_lag, const void* dout,
+                                   int32_t dout_token_major, void* dx, float* dweight,
+                                   float* dbias, void* workspace, int64_t workspace_bytes,
+                                   void* stream) {
+  if (C < 0 || S < 0 || K < 1 || K > 8) return TT_ERR_INVALID_ARG;
+  if (C == 0 || S == 0) return TT_OK;
+  if (!x || !weight || !dout || !dx || !dweight || !succ_ptr || (K > 1 && !pred))
+    return TT_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < tt_tree_conv_bwd_workspace_size(C, S, K))
+    return TT_ERR_WORKSPACE;
+  if (dout_token_major && !(tm_ok(C, S, x, dout, dx) &&
+                            (reinterpret_cast<uintptr_t>(workspace) & 15) == 0))
+    return TT_ERR_UNSUPPORTED;
+  return tt::by_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int tok = dout_token_major ? tt::kTmTok : tt::kConvTok;
+    const int nb = (S + tok - 1) / tok;
+    float* dpre = static_cast<float*>(workspace);
+    float* part = dpre + (int64_t)C * S;
+    dim3 g(nb, (C + tt::kConvCh - 1) / tt::kConvCh);
+    return tt::by_k(K, [&](auto kc) {
+      constexpr int KK = decltype(kc)::value;
+      // the 4-token kernels also move dpre by 16 bytes
+      const bool q4 = tt::quad_ok(S, x, dout, dx) &&
+                      (reinterpret_cast<uintptr_t>(workspace) & 15) == 0;
+      if (dout_token_major)
+        tt::conv_bwd_dpre_tm<T, KK><<<dim3(nb, (C + tt::kTmCh - 1) / tt::kTmCh), tt::kTmThreads,
+                                      0, st>>>(C, S, (const T*)x, weight, bias, pred,
+                                               (const T*)dout, dpre, part, nb);
+      else if (q4)
+        tt::conv_bwd_dpre4<T, KK><<<g, tt::kConvThr4, 0, st>>>(
+            C, S, (const T*)x, weight, bias, pred, (const T*)dout, dpre, part, nb);
+      else
+        tt::conv_bwd_dpre<T, KK><<<g, tt::kConvTok, 0, st>>>(
+            C, S, (const T*)x, weight, bias, pred, (const T*)dout, dpre, part, nb);
+      tt::conv_bwd_dw_reduce<<<(C * tt::kPartW + 255) / 256, 256, 0, st>>>(C, K, nb, part,
+                                                                         dweight, dbias);
+      const dim3 gx((S + tt::kConvTok - 1) / tt::kConvTok, (C + tt::kConvCh - 1) / tt::kConvCh);
+      if (q4)
+        tt::conv_bwd_dx4<T, KK><<<gx, tt::kConvThr4, 0, st>>>(C, S, weight, dpre, succ_ptr,
+                                                              succ_tok, succ_lag, (T*)dx);
+      else
+        tt::conv_bwd_dx<T, KK><<<gx, tt::kConvTok, 0, st>>>(C, S, weight, dpre, succ_ptr,
+                                                            succ_tok, succ_lag, (T*)dx);
+      tt_count_launches(3);
+      return cudaGetLastError() == cudaSuccess ? (int)TT_OK : (int)TT_ERR_CUDA;
+    });
+  });
 }
 
 extern "C" int tt_tree_conv_bwd(int dtype, int32_t C, int32_t S, int32_t K, const void* x,
@@ -307,29 +733,6 @@ extern "C" int tt_tree_conv_bwd(int dtype, int32_t C, int32_t S, int32_t K, cons
                                 const int32_t* succ_lag, const void* dout, void* dx,
                                 float* dweight, float* dbias, void* workspace,
                                 int64_t workspace_bytes, void* stream) {
-  if (C < 0 || S < 0 || K < 1 || K > 8) return TT_ERR_INVALID_ARG;
-  if (C == 0 || S == 0) return TT_OK;
-  if (!x || !weight || !dout || !dx || !dweight || !succ_ptr || (K > 1 && !pred))
-    return TT_ERR_INVALID_ARG;
-  if (!workspace || workspace_bytes < tt_tree_conv_bwd_workspace_size(C, S, K))
-    return TT_ERR_WORKSPACE;
-  return tt::by_dtype(dtype, [&](auto tag) {
-    using T = decltype(tag);
-    cudaStream_t st = (cudaStream_t)stream;
-    const int nb = (S + tt::kConvTok - 1) / tt::kConvTok;
-    float* dpre = static_cast<float*>(workspace);
-    float* part = dpre + (int64_t)C * S;
-    dim3 g(nb, (C + tt::kConvCh - 1) / tt::kConvCh);
-    return tt::by_k(K, [&](auto kc) {
-      constexpr int KK = decltype(kc)::value;
-      tt::conv_bwd_dpre<T, KK><<<g, tt::kConvTok, 0, st>>>(C, S, (const T*)x, weight, bias, pred,
-                                                           (const T*)dout, dpre, part, nb);
-      tt::conv_bwd_dw_reduce<<<(C * tt::kPartW + 255) / 256, 256, 0, st>>>(C, K, nb, part,
-                                                                         dweight, dbias);
-      tt::conv_bwd_dx<T, KK><<<g, tt::kConvTok, 0, st>>>(C, S, weight, dpre, succ_ptr, succ_tok,
-                                                         succ_lag, (T*)dx);
-      tt_count_launches(3);
-      return cudaGetLastError() == cudaSuccess ? (int)TT_OK : (int)TT_ERR_CUDA;
-    });
-  });
+  return tt_tree_conv_bwd_ex(dtype, C, S, K, x, weight, bias, pred, succ_ptr, succ_tok, succ_lag,
+                             dout, 0, dx, dweight, dbias, workspace, workspace_bytes, stream);
 }

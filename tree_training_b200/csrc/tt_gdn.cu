@@ -188,7 +188,8 @@ __device__ __forceinline__ float warp_sum(float x) {
 template <typename T>
 __global__ void __launch_bounds__(32 * kTokWarps)
 prep_tokens(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__ q,
-            const T* __restrict__ k, const T* __restrict__ v,
+            const T* __restrict__ k, const T* __restrict__ v, long long q_ts, long long k_ts,
+            long long v_ts,
             const float* __restrict__ beta, const float* __restrict__ gam,
             const float* __restrict__ gl_tok, int l2norm, float q_scale,
             float* Q, float* K, float* Vb, float* Kb, float* Kbg, float* Qg, float* Kd) {
@@ -196,8 +197,8 @@ prep_tokens(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__ q,
   const int lane = threadIdx.x & 31;
   if (t >= S) return;                        // whole warps: no block-wide syncs below
   const int hk = h / (H / Hk);
-  const T* qr = q + ((long long)t * Hk + hk) * Dk;
-  const T* kr = k + ((long long)t * Hk + hk) * Dk;
+  const T* qr = q + (long long)t * q_ts + (long long)hk * Dk;
+  const T* kr = k + (long long)t * k_ts + (long long)hk * Dk;
   float sq = 0.f, sk = 0.f;
   for (int d = lane; d < Dk; d += 32) {
     const float a = to_f32(qr[d]), b = to_f32(kr[d]);
@@ -222,7 +223,7 @@ prep_tokens(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__ q,
     Qg[ht * Dk + d] = qs * eg;
     Kd[ht * Dk + d] = ks * ed;
   }
-  const T* vr = v + ((long long)t * H + h) * Dv;
+  const T* vr = v + (long long)t * v_ts + (long long)h * Dv;
   for (int d = lane; d < Dv; d += 32) Vb[ht * Dv + d] = to_f32(vr[d]) * bt;
 }
 
@@ -443,6 +444,7 @@ template <typename T>
 __global__ void __launch_bounds__(32 * kTokWarps)
 assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__ q,
                                      const T* __restrict__ k, const T* __restrict__ v,
+                                     long long q_ts, long long k_ts, long long v_ts,
                                      const float* __restrict__ beta, const float* __restrict__ gam,
                                      const float* __restrict__ gl_tok, int l2norm, float q_scale,
                                      const float* __restrict__ dQ, const float* __restrict__ dQg,
@@ -455,8 +457,8 @@ assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__
   if (t >= S) return;                        // whole warps: no block-wide syncs below
   const int hk = h / (H / Hk);
   const long long ht = (long long)h * S + t;
-  const T* qr = q + ((long long)t * Hk + hk) * Dk;
-  const T* kr = k + ((long long)t * Hk + hk) * Dk;
+  const T* qr = q + (long long)t * q_ts + (long long)hk * Dk;
+  const T* kr = k + (long long)t * k_ts + (long long)hk * Dk;
   const float bt = beta[(long long)t * H + h];
   const float gm = gam[ht];
   const float eg = expf(gm), ed = expf(gl_tok[ht] - gm);
@@ -504,7 +506,7 @@ assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__
     }
   }
   float p_vb = 0.f;
-  const T* vr = v + ((long long)t * H + h) * Dv;
+  const T* vr = v + (long long)t * v_ts + (long long)h * Dv;
   for (int d = lane; d < Dv; d += 32) {
     const float g = dVb[ht * Dv + d];
     p_vb += to_f32(vr[d]) * g;
@@ -580,6 +582,9 @@ __global__ void dinit_kernel(int H, int DkDv, int n_roots, const int* __restrict
 
 struct Plan {
   int S, H, Hk, Dk, Dv, n;
+  // elements from one token's q / k / v row to the next (0: packed rows of
+  // Hk * Dk, Hk * Dk and H * Dv elements)
+  long long q_ts = 0, k_ts = 0, v_ts = 0;
   std::vector<int> start, len, parent, depth;
   std::vector<int> tok_node;       // node of each token
   std::vector<long long> loff;     // packed L x Lp offset per node (Lp = row_stride(L))
@@ -801,6 +806,9 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   const bool exact = (flags & TT_GDN_EXACT_INVERSE) != 0;
   const bool reuse = backward && (flags & TT_GDN_SAVED_FORWARD) != 0;
   const int S = p.S, H = p.H, Dk = p.Dk, Dv = p.Dv, n = p.n, Hk = p.Hk;
+  const long long q_ts = p.q_ts ? p.q_ts : (long long)Hk * Dk;
+  const long long k_ts = p.k_ts ? p.k_ts : (long long)Hk * Dk;
+  const long long v_ts = p.v_ts ? p.v_ts : (long long)H * Dv;
   const long long vk = (long long)S * Dk, vv = (long long)S * Dv;   // head strides
   const long long llh = p.ll_total;
   const int DkDv = Dk * Dv;
@@ -1019,7 +1027,8 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     node_cumsum<<<dim3((n + 127) / 128, H), 128, 0, st>>>(S, H, n, b.d_start, b.d_len, g, b.gam,
                                                           b.gl_tok, b.gl);
     prep_tokens<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(
-        S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok, l2norm, q_scale, b.Q, b.K, b.Vb, b.Kb,
+        S, Hk, H, Dk, Dv, q, k, v, q_ts, k_ts, v_ts, beta, b.gam, b.gl_tok, l2norm, q_scale, b.Q,
+        b.K, b.Vb, b.Kb,
         b.Kbg, b.Qg, b.Kd);
     launches += 2;
     launch_gemm(gc, ds_kk, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
@@ -1138,7 +1147,8 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   launch_gemm(gc, ds_gk, H, b.dAqk, llh, b.K, vk, b.dQ, vk, 1.f, 0.f, st);
   kd_dot_kernel<<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(S, Dk, b.Kd, b.dKd, b.kd_dot);
   assemble_token_grads<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(
-      S, Hk, H, Dk, Dv, q, k, v, beta, b.gam, b.gl_tok, l2norm, q_scale, b.dQ, b.dQg, b.dK,
+      S, Hk, H, Dk, Dv, q, k, v, q_ts, k_ts, v_ts, beta, b.gam, b.gl_tok, l2norm, q_scale, b.dQ,
+      b.dQg, b.dK,
       b.dKd, b.dKb, b.dKbg, b.dVb, b.dgam, b.dq_h, b.dk_h, dbeta, (T*)dv_);
   node_dg<<<dim3((n + 127) / 128, H), 128, 0, st>>>(S, H, n, b.d_start, b.d_len, b.kd_dot, b.dgl,
                                                     b.dgam, dg);
@@ -1252,6 +1262,16 @@ static int gdn_check(int32_t S, int32_t Hk, int32_t H, int32_t Dk, int32_t Dv, i
   return TT_OK;
 }
 
+// q / k / v token strides: 0 (packed) or at least one packed row, so the rows
+// of different tokens never overlap
+static int gdn_check_strides(int32_t Hk, int32_t H, int32_t Dk, int32_t Dv, int64_t q_ts,
+                             int64_t k_ts, int64_t v_ts) {
+  const int64_t qk_row = (int64_t)Hk * Dk, v_row = (int64_t)H * Dv;
+  if ((q_ts != 0 && q_ts < qk_row) || (k_ts != 0 && k_ts < qk_row) || (v_ts != 0 && v_ts < v_row))
+    return TT_ERR_INVALID_ARG;
+  return TT_OK;
+}
+
 static int gdn_check_capture(int32_t n_nodes, int32_t n_capture, const int32_t* capture_nodes) {
   if (n_capture < 0 || (n_capture > 0 && !capture_nodes)) return TT_ERR_INVALID_ARG;
   std::vector<char> seen(n_nodes, 0);
@@ -1269,15 +1289,23 @@ extern "C" int tt_gdn_tree_fwd_ex(int dtype, int32_t S, int32_t Hk, int32_t H, i
                                   const int32_t* bounds, const int32_t* parents,
                                   const float* initial_state, int flags, void* out,
                                   float* last_state, int32_t n_capture,
-                                  const int32_t* capture_nodes, float* captured, void* workspace,
+                                  const int32_t* capture_nodes, float* captured,
+                                  int64_t q_token_stride, int64_t k_token_stride,
+                                  int64_t v_token_stride, void* workspace,
                                   int64_t workspace_bytes, void* stream) {
   int rc = gdn_check(S, Hk, H, Dk, Dv, n_nodes, bounds, parents, flags);
   if (rc != TT_OK) return rc;
   if ((rc = gdn_check_capture(n_nodes, n_capture, capture_nodes)) != TT_OK) return rc;
   if (n_capture > 0 && !captured) return TT_ERR_INVALID_ARG;
+  if ((rc = gdn_check_strides(Hk, H, Dk, Dv, q_token_stride, k_token_stride,
+                              v_token_stride)) != TT_OK)
+    return rc;
   if (S == 0 || n_nodes == 0) return TT_OK;
   Plan p;
   if ((rc = tt::gdn::make_plan(p, S, H, Hk, Dk, Dv, n_nodes, bounds, parents)) != TT_OK) return rc;
+  p.q_ts = q_token_stride;
+  p.k_ts = k_token_stride;
+  p.v_ts = v_token_stride;
   Arena ar{(char*)workspace, workspace_bytes, 0, false};
   return tt::gdn::dispatch(dtype, [&](auto tag) {
     using T = decltype(tag);
@@ -1295,7 +1323,7 @@ extern "C" int tt_gdn_tree_fwd(int dtype, int32_t S, int32_t Hk, int32_t H, int3
                                int flags, void* out, float* last_state, void* workspace,
                                int64_t workspace_bytes, void* stream) {
   return tt_gdn_tree_fwd_ex(dtype, S, Hk, H, Dk, Dv, q, k, v, g, beta, n_nodes, bounds, parents,
-                            initial_state, flags, out, last_state, 0, nullptr, nullptr,
+                            initial_state, flags, out, last_state, 0, nullptr, nullptr, 0, 0, 0,
                             workspace, workspace_bytes, stream);
 }
 
@@ -1307,13 +1335,21 @@ extern "C" int tt_gdn_tree_bwd_ex(int dtype, int32_t S, int32_t Hk, int32_t H, i
                                   const float* dlast, int32_t n_capture,
                                   const int32_t* capture_nodes, const float* dcaptured, void* dq,
                                   void* dk, void* dv, float* dg, float* dbeta, float* dinit,
-                                  void* workspace, int64_t workspace_bytes, void* stream) {
+                                  int64_t q_token_stride, int64_t k_token_stride,
+                                  int64_t v_token_stride, void* workspace,
+                                  int64_t workspace_bytes, void* stream) {
   int rc = gdn_check(S, Hk, H, Dk, Dv, n_nodes, bounds, parents, flags);
   if (rc != TT_OK) return rc;
   if ((rc = gdn_check_capture(n_nodes, n_capture, capture_nodes)) != TT_OK) return rc;
+  if ((rc = gdn_check_strides(Hk, H, Dk, Dv, q_token_stride, k_token_stride,
+                              v_token_stride)) != TT_OK)
+    return rc;
   if (S == 0 || n_nodes == 0) return TT_OK;
   Plan p;
   if ((rc = tt::gdn::make_plan(p, S, H, Hk, Dk, Dv, n_nodes, bounds, parents)) != TT_OK) return rc;
+  p.q_ts = q_token_stride;
+  p.k_ts = k_token_stride;
+  p.v_ts = v_token_stride;
   Arena ar{(char*)workspace, workspace_bytes, 0, false};
   return tt::gdn::dispatch(dtype, [&](auto tag) {
     using T = decltype(tag);
@@ -1333,7 +1369,7 @@ extern "C" int tt_gdn_tree_bwd(int dtype, int32_t S, int32_t Hk, int32_t H, int3
                                void* workspace, int64_t workspace_bytes, void* stream) {
   return tt_gdn_tree_bwd_ex(dtype, S, Hk, H, Dk, Dv, q, k, v, g, beta, n_nodes, bounds, parents,
                             initial_state, flags, dout, dlast, 0, nullptr, nullptr, dq, dk, dv,
-                            dg, dbeta, dinit, workspace, workspace_bytes, stream);
+                            dg, dbeta, dinit, 0, 0, 0, workspace, workspace_bytes, stream);
 }
 
 extern "C" int64_t tt_gdn_gemm_flops(void) {

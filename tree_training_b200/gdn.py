@@ -51,6 +51,19 @@ def _ws(S, H, Dk, Dv, bounds: torch.Tensor, backward: bool, device) -> Tuple[tor
     return torch.empty(max(nbytes, 16), dtype=torch.uint8, device=device), nbytes
 
 
+def _rows_in_place(t: torch.Tensor) -> bool:
+    """t [S, heads, dim] whose token rows the kernels can read in place: each
+    row [heads, dim] contiguous, rows at a fixed stride of at least a row."""
+    S, nh, d = t.shape
+    return t.stride(2) == 1 and t.stride(1) == d and (S <= 1 or t.stride(0) >= nh * d)
+
+
+def _token_strides(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Tuple[int, int, int]:
+    """The token strides the C ABI takes (0 = packed rows)."""
+    st = lambda t: 0 if t.is_contiguous() else int(t.stride(0))
+    return st(q), st(k), st(v)
+
+
 @torch.library.custom_op("tt_b200::gdn_tree_fwd", mutates_args=())
 def _gdn_fwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
                 beta: torch.Tensor, bounds: torch.Tensor, parents: torch.Tensor,
@@ -76,7 +89,7 @@ def _gdn_fwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tens
               bounds.data_ptr(), parents.data_ptr(), init.data_ptr() if has_init else None,
               int(flags), out.data_ptr(), last.data_ptr() if want_last else None, m,
               capture.data_ptr() if m else None, cap.data_ptr() if m else None,
-              ws.data_ptr(), nbytes, _stream_ptr(q.device))
+              *_token_strides(q, k, v), ws.data_ptr(), nbytes, _stream_ptr(q.device))
     return out, last, cap, (ws if keep else ws.new_empty(0))
 
 
@@ -99,7 +112,8 @@ def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: tor
                                        torch.Tensor, torch.Tensor]:
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    packed = lambda t: torch.empty(t.shape, dtype=t.dtype, device=t.device)
+    dq, dk, dv = packed(q), packed(k), packed(v)
     dg = torch.empty((S, H), dtype=torch.float32, device=q.device)
     db = torch.empty((S, H), dtype=torch.float32, device=q.device)
     dinit = torch.zeros((H, Dk, Dv) if has_init else (0,), dtype=torch.float32, device=q.device)
@@ -117,8 +131,8 @@ def _gdn_bwd_op(dout: torch.Tensor, dlast: torch.Tensor, has_dlast: bool, q: tor
               capture.data_ptr() if m else None,
               dcap.contiguous().data_ptr() if (m and has_dcap) else None, dq.data_ptr(),
               dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), db.data_ptr(),
-              dinit.data_ptr() if has_init else None, ws.data_ptr(), nbytes,
-              _stream_ptr(q.device))
+              dinit.data_ptr() if has_init else None, *_token_strides(q, k, v), ws.data_ptr(),
+              nbytes, _stream_ptr(q.device))
     return dq, dk, dv, dg, db, dinit
 
 
@@ -128,7 +142,8 @@ def _(dout, dlast, has_dlast, q, k, v, g, beta, bounds, parents, init, has_init,
     S, Hk, Dk = q.shape
     H, Dv = v.shape[1], v.shape[2]
     f = lambda *s: q.new_empty(s, dtype=torch.float32)
-    return (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), f(S, H), f(S, H),
+    packed = lambda t: t.new_empty(t.shape)
+    return (packed(q), packed(k), packed(v), f(S, H), f(S, H),
             f(H, Dk, Dv) if has_init else f(0))
 
 
@@ -168,7 +183,7 @@ def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_b
                                              chunk_parent_map, initial_state=None,
                                              output_final_state=False,
                                              use_qk_l2norm_in_kernel=False,
-                                             exact_inverse=False, keep_forward=False):
+                                             exact_inverse=False, keep_forward=None):
     """Drop-in for tree_dfs_ssm.py:38-156.
 
     query/key [B, S, Hk, Dk] (Hk == H, or a divisor of H: v-head h then uses
@@ -184,7 +199,15 @@ def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_b
     each root-to-node path, independent of where node boundaries fall.
     ``keep_forward=True`` keeps the forward's fp32 intermediates on the device
     until the backward (a workspace of ``tt_gdn_tree_workspace_size(...,
-    backward=1)`` bytes), which then skips recomputing the forward."""
+    backward=1)`` bytes), which then skips recomputing the forward; ``False``
+    holds only the output and recomputes in the backward (about half the
+    device memory, a slower backward).  The default (None) keeps them whenever
+    autograd will run the backward (grad enabled and an input requires grad),
+    as torch autograd keeps the reference loop's intermediates."""
+    if keep_forward is None:
+        keep_forward = torch.is_grad_enabled() and any(
+            isinstance(t, torch.Tensor) and t.requires_grad
+            for t in (query, key, value, g, beta, initial_state))
     if query.dtype not in _DTYPES or key.dtype != query.dtype or value.dtype != query.dtype:
         raise TypeError("tree GDN: query, key, value must share one of float32/bfloat16/float16")
     if not query.is_cuda:
@@ -193,9 +216,10 @@ def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_b
     B = query.shape[0]
     outs, lasts = [], []
     for b in range(B):
-        q = query[b].contiguous()
-        k = key[b].contiguous()
-        v = value[b].contiguous()
+        # rows read in place where the layout allows (the q / k / v views the
+        # layer splits off a token-major conv output), else packed copies
+        q, k, v = (t[b] if _rows_in_place(t[b]) else t[b].contiguous()
+                   for t in (query, key, value))
         gg = g[b].float().contiguous()
         bt = beta[b].float().contiguous()
         has_init = initial_state is not None
@@ -220,7 +244,11 @@ def torch_chunk_gated_delta_rule_tree_varlen(query, key, value, g, beta, chunk_b
 # -----------------------------------------------------------------------------
 
 class TreeConvPlan:
-    """Predecessor / successor tables of one tree for a width-K conv (device)."""
+    """Predecessor / successor tables of one tree for a width-K conv (device).
+
+    The four tables travel in one pinned host buffer by one asynchronous copy:
+    a copy from pageable memory would synchronise the stream, so the host
+    would wait for every kernel queued before it."""
 
     def __init__(self, bounds: torch.Tensor, parents: torch.Tensor, K: int, device):
         n = int(bounds.shape[0])
@@ -235,28 +263,73 @@ class TreeConvPlan:
         slag = np.zeros(cap, np.int32)
         _lib.call("tt_conv_successors", S, K, pred.ctypes.data, sp.ctypes.data, stok.ctypes.data,
                   slag.ctypes.data, cap)
-        self.pred = torch.from_numpy(pred).to(device)
-        self.succ_ptr = torch.from_numpy(sp).to(device)
-        self.succ_tok = torch.from_numpy(stok).to(device)
-        self.succ_lag = torch.from_numpy(slag).to(device)
+        # each table starts on a 16-byte boundary (the 4-token kernels read
+        # the predecessor rows of 4 tokens at once)
+        parts = [pred.reshape(-1), sp, stok, slag]
+        offs, total = [], 0
+        for a in parts:
+            offs.append(total)
+            total += (a.size + 3) // 4 * 4
+        pinned = torch.device(device).type == "cuda"
+        host = torch.zeros(total, dtype=torch.int32, pin_memory=pinned)
+        hv = host.numpy()
+        for o, a in zip(offs, parts):
+            hv[o:o + a.size] = a
+        dev = host.to(device, non_blocking=pinned)
+        self._host = host
+        self.pred = dev[offs[0]:offs[0] + pred.size].view(pred.shape)
+        self.succ_ptr = dev[offs[1]:offs[1] + sp.size]
+        self.succ_tok = dev[offs[2]:offs[2] + cap]
+        self.succ_lag = dev[offs[3]:offs[3] + cap]
+
+
+_conv_plans: "dict" = {}
+_CONV_PLAN_CACHE = 16
+
+
+def _conv_plan(bounds: torch.Tensor, parents: torch.Tensor, K: int, device) -> TreeConvPlan:
+    """The plan of a tree, reused while the same tree (same node bounds and
+    parents) comes back: a training step calls the conv on one tree once per
+    layer."""
+    key = (bounds.numpy().tobytes(), parents.numpy().tobytes(), int(K), str(torch.device(device)))
+    plan = _conv_plans.pop(key, None)
+    if plan is None:
+        plan = TreeConvPlan(bounds, parents, K, device)
+        while len(_conv_plans) >= _CONV_PLAN_CACHE:
+            _conv_plans.pop(next(iter(_conv_plans)))
+    _conv_plans[key] = plan      # most recently used last
+    return plan
+
+
+def _token_major_ok(t: torch.Tensor) -> bool:
+    """t [C, S] held token-major (strides (1, C)) with the alignment the
+    token-major conv kernels need (S % 4 == 0, C % 8 == 0, 16-byte base)."""
+    C, S = t.shape
+    return (t.stride() == (1, C) and C % 8 == 0 and S % 4 == 0 and t.data_ptr() % 16 == 0)
+
+
+def _conv_out(x: torch.Tensor, token_major: bool) -> torch.Tensor:
+    """The conv output [C, S]: token-major memory (strides (1, C)) or plain."""
+    C, S = x.shape
+    return x.new_empty((S, C)).t() if token_major else torch.empty_like(x)
 
 
 @torch.library.custom_op("tt_b200::tree_conv_fwd", mutates_args=())
 def _conv_fwd_op(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, has_b: bool,
                  pred: torch.Tensor, sp: torch.Tensor, stok: torch.Tensor,
-                 slag: torch.Tensor) -> torch.Tensor:
+                 slag: torch.Tensor, token_major: bool) -> torch.Tensor:
     C, S = x.shape
     K = w.shape[1]
-    out = torch.empty_like(x)
-    _lib.call("tt_tree_conv_fwd", _DTYPES[x.dtype], C, S, K, x.data_ptr(), w.data_ptr(),
+    out = _conv_out(x, token_major)
+    _lib.call("tt_tree_conv_fwd_ex", _DTYPES[x.dtype], C, S, K, x.data_ptr(), w.data_ptr(),
               b.data_ptr() if has_b else None, pred.data_ptr(), out.data_ptr(),
-              _stream_ptr(x.device))
+              int(token_major), _stream_ptr(x.device))
     return out
 
 
 @_conv_fwd_op.register_fake
-def _(x, w, b, has_b, pred, sp, stok, slag):
-    return torch.empty_like(x)
+def _(x, w, b, has_b, pred, sp, stok, slag, token_major):
+    return _conv_out(x, token_major)
 
 
 @torch.library.custom_op("tt_b200::tree_conv_bwd", mutates_args=())
@@ -270,9 +343,14 @@ def _conv_bwd_op(dy: torch.Tensor, x: torch.Tensor, w: torch.Tensor, b: torch.Te
     db = torch.empty((C,) if has_b else (0,), dtype=torch.float32, device=x.device)
     ws_bytes = int(_lib.lib().tt_tree_conv_bwd_workspace_size(C, S, K))
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=x.device)
-    _lib.call("tt_tree_conv_bwd", _DTYPES[x.dtype], C, S, K, x.data_ptr(), w.data_ptr(),
+    # a gradient in token-major memory (what autograd hands back through the
+    # layer's transpose + split of a token-major output) is read in place
+    tm = _token_major_ok(dy) and x.data_ptr() % 16 == 0
+    if not tm:
+        dy = dy.contiguous()
+    _lib.call("tt_tree_conv_bwd_ex", _DTYPES[x.dtype], C, S, K, x.data_ptr(), w.data_ptr(),
               b.data_ptr() if has_b else None, pred.data_ptr(), sp.data_ptr(), stok.data_ptr(),
-              slag.data_ptr(), dy.contiguous().data_ptr(), dx.data_ptr(), dw.data_ptr(),
+              slag.data_ptr(), dy.data_ptr(), int(tm), dx.data_ptr(), dw.data_ptr(),
               db.data_ptr() if has_b else None, ws.data_ptr(), ws_bytes, _stream_ptr(x.device))
     return dx, dw, db
 
@@ -284,7 +362,7 @@ def _(dy, x, w, b, has_b, pred, sp, stok, slag):
 
 
 def _conv_setup(ctx, inputs, output):
-    x, w, b, has_b, pred, sp, stok, slag = inputs
+    x, w, b, has_b, pred, sp, stok, slag, _token_major = inputs
     ctx.save_for_backward(x, w, b, pred, sp, stok, slag)
     ctx.has_b = has_b
 
@@ -292,7 +370,7 @@ def _conv_setup(ctx, inputs, output):
 def _conv_backward(ctx, dy):
     x, w, b, pred, sp, stok, slag = ctx.saved_tensors
     dx, dw, db = _conv_bwd_op(dy, x, w, b, ctx.has_b, pred, sp, stok, slag)
-    return dx, dw, (db if ctx.has_b else None), None, None, None, None, None
+    return dx, dw, (db if ctx.has_b else None), None, None, None, None, None, None
 
 
 _conv_fwd_op.register_autograd(_conv_backward, setup_context=_conv_setup)
@@ -308,11 +386,19 @@ def tree_conv(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor
         raise TypeError("tree conv: float32/bfloat16/float16 input required")
     w = weight.reshape(weight.shape[0], -1).float().contiguous()
     bounds, parents = _tree_arrays(chunk_boundaries, chunk_parent_map)
-    plan = TreeConvPlan(bounds, parents, int(w.shape[1]), x.device)
+    plan = _conv_plan(bounds, parents, int(w.shape[1]), x.device)
     has_b = bias is not None
     b = bias.float().contiguous() if has_b else w.new_empty(0)
-    outs = [_conv_fwd_op(x[i].contiguous(), w, b, has_b, plan.pred, plan.succ_ptr,
-                         plan.succ_tok, plan.succ_lag) for i in range(x.shape[0])]
+    # batch 1 (every tree of the reference): the output in token-major memory
+    # when the kernels allow it, so the layer's transpose + split into q / k / v
+    # (dfs_tree_forward.py:403-410) are views with no transposing copy
+    outs = []
+    for i in range(x.shape[0]):
+        xi = x[i].contiguous()
+        tm = (x.shape[0] == 1 and xi.shape[0] % 8 == 0 and xi.shape[1] % 4 == 0
+              and xi.data_ptr() % 16 == 0)
+        outs.append(_conv_fwd_op(xi, w, b, has_b, plan.pred, plan.succ_ptr, plan.succ_tok,
+                                 plan.succ_lag, tm))
     return outs[0].unsqueeze(0) if len(outs) == 1 else torch.stack(outs, 0)
 
 
