@@ -71,6 +71,9 @@ def parse():
                     help="gdn: exact-inverse correction T = (I - A)^-1 instead of the "
                          "reference's I + A + A^2")
     ap.add_argument("--layers", type=int, default=36, help="e2e5: decoder layers (36 = Qwen3-4B)")
+    ap.add_argument("--other-configs", type=int, default=1,
+                    help="attn at N=1: also measure config 3 (attn3) and config 4 (gdn) in the "
+                         "same process and report them under other_configs (0 = skip)")
     ap.add_argument("--ckpt-mlp", type=int, default=1,
                     help="e2e5: recompute decoder MLPs in backward (1) or save them (0)")
     return ap.parse_args()
@@ -763,6 +766,8 @@ def run_ours(args):
             line["e2e"]["reference_packer"] = reference_packer_sample(roots, V)
         if world == 1 and not args.no_reference_gpu:
             line["reference_gpu"] = reference_gpu_sample(meta, dev, V)
+        if world == 1 and args.other_configs:
+            line["other_configs"] = other_configs(args)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -824,7 +829,7 @@ def gdn_cpu_baseline(info, min_tokens: int = 4096):
                       f"{torch.get_num_threads()} threads"}
 
 
-def run_gdn(args):
+def run_gdn(args, emit: bool = True):
     import tree_training_b200 as tt
     from tree_training_b200 import _lib
     from tree_training_b200.gdn import torch_chunk_gated_delta_rule_tree_varlen, tree_conv
@@ -963,6 +968,8 @@ def run_gdn(args):
                         "schedule": "one stream: upload, conv + GDN fwd + bwd, download"}}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = gdn_cpu_baseline(info)
+        if not emit:
+            return line
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -975,7 +982,7 @@ HQ3 = 40      # config 3 heads (Hkv = 8, D = 128)
 CFG3_TOKENS = 65536
 
 
-def run_attn3(args):
+def run_attn3(args, emit: bool = True):
     """Config 3: 8 agentic trees of 65,536 tokens (root prefix 8,192, 32 leaves,
     node lengths log-uniform [32, 4096], depth <= 10), 40 q / 8 kv heads, tree
     attention fwd+bwd.  The job's trees are fixed and dealt round robin to the
@@ -1122,6 +1129,8 @@ def run_attn3(args):
                                 "peak": float(pk["bf16_tflops"]), "unit": "TFLOP/s",
                                 "frac": ach / float(pk["bf16_tflops"]), "traffic": None,
                                 "peak_source": f"{pk_src} bf16 dense (burst)"}
+        if not emit:
+            return line
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -1150,7 +1159,7 @@ def run_e2e5(args):
     import tree_training_b200 as tt
     from tree_training_b200 import _lib
     from tree_training_b200.dist import GradAverager, RankWatch
-    from tree_training_b200.hybrid import make_tree_loss_fn, tree_grad_hybrid
+    from tree_training_b200.hybrid import make_tree_loss_fn, partition_tree, tree_grad_hybrid
     from tree_training_b200.synthetic import random_branching_tree
     world, rank, local = dist_env()
     dev = torch.device("cuda", local)
@@ -1186,13 +1195,15 @@ def run_e2e5(args):
         import torch.distributed as dist
         watch = RankWatch(dist.distributed_c10d._get_default_store(), rank, world, timeout_s=120)
     step_no = [0]
-    ar_ms, ar_issued = [], []
+    ar_ms, ar_issued, comp_ms = [], [], []
 
     def step():
         # heartbeat first: the all-reduce starts inside the last partition's backward
         if watch is not None:
             watch.beat(step_no[0])
         step_no[0] += 1
+        c0 = torch.cuda.Event(enable_timing=True)
+        c0.record()
         opt.zero_grad(set_to_none=True)
         loss = tree_grad_hybrid(model, roots, loss_fn, max_tokens=8192,
                                 fused_ce=bool(args.fused_ce), before_last_backward=avg.arm)
@@ -1204,6 +1215,7 @@ def run_e2e5(args):
         opt.step()
         out = float(loss.item())             # the step's d2h result
         ar_ms.append(e0.elapsed_time(e1))
+        comp_ms.append(c0.elapsed_time(e0))  # this rank's forward + backward
         return out
 
     clocks = ClockSampler(dev)
@@ -1219,6 +1231,7 @@ def run_e2e5(args):
     ts, losses = [], []
     ar_ms.clear()
     ar_issued.clear()
+    comp_ms.clear()
     for _ in range(args.steps):
         torch.cuda.synchronize()
         a = torch.cuda.Event(enable_timing=True)
@@ -1232,6 +1245,23 @@ def run_e2e5(args):
     clk = clocks.stop()
     tt.check_device_status(dev)
     exposed_ms = max_over_ranks(statistics.mean(ar_ms), world, dev)
+    # every rank's own forward + backward time (its tree's partitions differ):
+    # a step cannot end before the slowest rank's backward
+    my_comp = torch.tensor([statistics.mean(comp_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        comp_all = [torch.zeros_like(my_comp) for _ in range(world)]
+        dist.all_gather(comp_all, my_comp)
+        rank_comp_ms = [float(t.item()) for t in comp_all]
+    else:
+        rank_comp_ms = [float(my_comp.item())]
+    n_parts = len(partition_tree(roots, 8192))
+    parts_all = [n_parts]
+    if world > 1:
+        pt = torch.tensor([n_parts], dtype=torch.int64, device=dev)
+        pt_all = [torch.zeros_like(pt) for _ in range(world)]
+        dist.all_gather(pt_all, pt)
+        parts_all = [int(t.item()) for t in pt_all]
     # the same all-reduce issued as one block after the step, for comparison
     standalone_ms = 0.0
     if world > 1:
@@ -1285,6 +1315,12 @@ def run_e2e5(args):
                                   "time average() still takes after the backward (max over "
                                   "ranks); standalone = the same buckets all-reduced after "
                                   "the step with nothing to overlap"},
+            "ranks": {"compute_ms_per_step": rank_comp_ms, "partitions": parts_all,
+                      "slowest_compute_ms": max(rank_comp_ms),
+                      "note": "each rank's forward + backward of its own tree (before the "
+                              "all-reduce wait); the trees differ per rank (seed + rank), so "
+                              "their partition counts and times differ and the step waits for "
+                              "the slowest"},
             "gpu_launches": int(launches),
             "clocks": clk,
             "cpu_baseline": None,
@@ -1298,6 +1334,32 @@ def run_e2e5(args):
 
 
 DEFAULT_STEPS = {"attn": 200, "attn3": 5, "gdn": 20, "e2e5": 3}
+
+_OTHER_KEYS = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "tokens_per_s",
+               "dtype", "e2e", "roofline", "roofline_tensor", "cpu_baseline",
+               "cpu_baseline_note", "gpu_launches", "clocks", "kernel_ms_per_step")
+
+
+def other_configs(args):
+    """Config 3 (attn3) and config 4 (gdn) measured in the same process after
+    the config-2 line, each with its own workload's default step count, 3
+    warm-up steps and its own timing, L2 and clock rules; their lines trimmed
+    to the figures (the full lines come from --workload attn3 / gdn)."""
+    import copy
+    out = {}
+    for name, fn in (("config3", run_attn3), ("config4", run_gdn)):
+        a = copy.copy(args)
+        a.workload = "attn3" if fn is run_attn3 else "gdn"
+        a.steps, a.warmup = DEFAULT_STEPS[a.workload], 3
+        a.tokens = 16384
+        try:
+            line = fn(a, emit=False)
+            out[name] = {k: line[k] for k in _OTHER_KEYS if k in line}
+            out[name]["workload"] = line["config"]["workload"]
+        except Exception as e:      # reported, never hides the config-2 line
+            out[name] = {"error": f"{type(e).__name__}: {e}"}
+        torch.cuda.empty_cache()
+    return out
 
 
 def main():

@@ -154,7 +154,7 @@ def test_library_exports_every_header_symbol():
     for n in names:
         assert hasattr(L, n), n
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
-    assert L.tt_abi_version() == 2
+    assert L.tt_abi_version() == 3
     assert _lib.status_string(_lib.TT_ERR_NOT_INTERVAL).startswith("mask is not")
 
 

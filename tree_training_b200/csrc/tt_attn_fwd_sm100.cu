@@ -313,21 +313,6 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
           m_run = m_new;
           need = true;
         }
-        if (__any_sync(0xffffffffu, need)) {
-          // PV_g(it-1) has completed: the commit that signalled S_g(it) was
-          // issued after it, and a commit tracks every earlier MMA.
-          // (16 columns at a time: the score row stays live across this)
-#pragma unroll 1
-          for (int c = 0; c < kD / 16; ++c) {
-            float o[16];
-            uint32_t w[16];
-            tmem_ld16(lane_addr + col_o + c * 16, o);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(o[i] * alpha);
-            tmem_st16(lane_addr + col_o + c * 16, w);
-          }
-          tmem_st_wait();
-        }
         l_run *= alpha;
         const float mb = (m_run == -INFINITY) ? 0.f : m_run;
         const float2 sc2 = make_float2(scale_log2, scale_log2), nmb2 = make_float2(-mb, -mb);
@@ -359,6 +344,23 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CU
         const float2 a01 = fadd2(acc[0], acc[1]), a23 = fadd2(acc[2], acc[3]);
         l_run += (a01.x + a23.x) + (a01.y + a23.y);
         tmem_st_wait();
+        if (__any_sync(0xffffffffu, need)) {
+          // O_g *= alpha before PV_g(it) adds to it (the MMA warp issues that
+          // only after p_full).  PV_g(it-1) has completed: the commit that
+          // signalled S_g(it) was issued after it, and a commit tracks every
+          // earlier MMA.  Done after the P stores, when the score row is no
+          // longer live (fewer registers at the peak).
+#pragma unroll 1
+          for (int c = 0; c < kD / 16; ++c) {
+            float o[16];
+            uint32_t w[16];
+            tmem_ld16(lane_addr + col_o + c * 16, o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(o[i] * alpha);
+            tmem_st16(lane_addr + col_o + c * 16, w);
+          }
+          tmem_st_wait();
+        }
         tc_fence_before();
         mbar_arrive(&sh->p_full[g]);
       }

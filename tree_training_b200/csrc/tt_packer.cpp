@@ -28,7 +28,7 @@ extern "C" const char* tt_status_string(int s) {
   }
 }
 
-extern "C" int tt_abi_version(void) { return 2; }
+extern "C" int tt_abi_version(void) { return 3; }
 
 extern "C" int tt_pack_forest(int32_t n_nodes, const int32_t* node_len,
                               const int32_t* node_parent, int32_t pos_offset, int32_t* pos_ids,
