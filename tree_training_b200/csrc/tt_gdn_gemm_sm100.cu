@@ -55,7 +55,7 @@ constexpr int kMaxStages = 6;
 template <int kSplit>
 struct Ring {
   static constexpr int kStageBytes = (kSplit == 3 ? 4 : 2) * kOpBytes;   // A, B (+ lo copies)
-  static constexpr int kStages = kSplit == 3 ? 3 : 6;
+  static constexpr int kStages = kSplit == 3 ? 2 : 4;
   static constexpr int kLag = kStages - 1;   // slices in flight per producer thread
 };
 
@@ -74,11 +74,15 @@ struct Bars {
 // padded to 33 columns (conflict-free row writes and column reads).
 constexpr int kStgPitch = 33;
 constexpr int kStgBytes = kEpilogueWarps * 32 * kStgPitch * 4;
+// C_in of the tile, prefetched by the epilogue warps (each its 32 rows x 128
+// columns) before they wait for the accumulator, so the reads of C_in overlap
+// the tile's main loop instead of stalling the epilogue row by row.
+constexpr int kCinBytes = kEpilogueWarps * 32 * kTN * 4;
 
 template <int kSplit>
 constexpr size_t smem_bytes() {
   return 1024 + (size_t)Ring<kSplit>::kStages * Ring<kSplit>::kStageBytes + kStgBytes +
-         sizeof(Bars);
+         kCinBytes + sizeof(Bars);
 }
 
 __device__ int32_t g_status;   // first error of any launch since the last take
@@ -282,13 +286,14 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
                                           const float* __restrict__ B, long long b_hs, float* C,
                                           long long c_hs, float alpha, float beta,
                                           const float* Cin, const CUtensorMap* maps,
-                                          int seg_first) {
+                                          int seg_first, bool cin_async) {
   using R = Ring<kSplit>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   float* stg_all = reinterpret_cast<float*>(ring + (size_t)R::kStages * R::kStageBytes);
-  Bars* sh = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(stg_all) + kStgBytes);
+  float* cin_all = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(stg_all) + kStgBytes);
+  Bars* sh = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(cin_all) + kCinBytes);
   const volatile int32_t* abort_flag = &sh->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_items = n_tiles * H;
@@ -517,21 +522,45 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
       const int h = item % H;
       const int i0 = (tl.y >> 16) * kTM, j0 = (tl.y & 0xFFFF) * kTN;
       const int buf = acc_i & 1;
+      const float* cin = Cin ? Cin : C;
+      const long long hoff = h * c_hs + sd.c_off;
+      const int rows = sd.M - (i0 + quad * 32);      // rows of this warp's block in C
+      // C_in prefetch: lane l copies columns [4l, 4l + 4) of each of the warp's
+      // 32 rows (one 512-byte row segment per instruction), zero-filled past
+      // the segment; it lands while the tile's MMAs run
+      float* cinb = cin_all + quad * 32 * kTN;
+      const bool pre = cin_async && beta != 0.f;
+      if (pre) {
+        const int col = j0 + 4 * lane;
+        const int ncol = min(max(sd.N - col, 0), 4);
+        const float* base = cin + hoff + (long long)(i0 + quad * 32) * sd.c_rs + col;
+        const uint32_t dst0 = smem_u32(cinb) + lane * 16;
+#pragma unroll 4
+        for (int r = 0; r < 32; ++r) {
+          const int n_el = r < rows ? ncol : 0;
+          cp_async16(dst0 + r * kTN * 4, n_el > 0 ? base + (long long)r * sd.c_rs : cin,
+                     (uint32_t)n_el * 4u);
+        }
+        cp_async_commit();
+      }
       bool ok = mbar_wait(&sh->acc_full[buf], (acc_i >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
+        if (pre) cp_async_wait<0>();          // the copies land before the CTA exits
         record_error(sh, TT_ERR_DEVICE_TIMEOUT);
         break;
       }
       tc_fence_after();
+      if (pre) {
+        cp_async_wait<0>();
+        __syncwarp();
+      }
       int kb, nk;
       k_range(sd, i0, j0, kb, nk);
       const bool empty_k = nk == 0;            // no MMA wrote this accumulator
       // each 32 x 32 block goes through shared memory so that the warp
       // stores (and reads C_in) one 128-byte row segment per instruction
       float* stg = stg_all + quad * 32 * kStgPitch;
-      const float* cin = Cin ? Cin : C;
-      const long long hoff = h * c_hs + sd.c_off;
 #pragma unroll 1
       for (int cc = 0; cc < kTN / 32; ++cc) {
         float v[32];
@@ -540,13 +569,15 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
         for (int i = 0; i < 32; ++i) stg[lane * kStgPitch + i] = empty_k ? 0.f : alpha * v[i];
         __syncwarp();
         const int gj = j0 + cc * 32 + lane;
-        const int rows = sd.M - (i0 + quad * 32);      // rows of this warp's block in C
         if (gj < sd.N && rows > 0) {
           const long long o0 = hoff + (long long)(i0 + quad * 32) * sd.c_rs + gj;
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             float cv[16];
-            if (beta != 0.f) {
+            if (pre) {
+#pragma unroll
+              for (int rr = 0; rr < 16; ++rr) cv[rr] = cinb[(half * 16 + rr) * kTN + cc * 32 + lane];
+            } else if (beta != 0.f) {
               // 16 rows' C_in loads in flight before the first store
 #pragma unroll
               for (int rr = 0; rr < 16; ++rr) {
@@ -588,7 +619,7 @@ seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, in
             const float* __restrict__ A, long long a_hs, const float* __restrict__ B,
             long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin) {
   gemm_body<kSplit, false>(segs, tiles, n_tiles, H, A, a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
-                           nullptr, 0);
+                           nullptr, 0, false);
 }
 
 // Operands staged with TMA tile copies through per-segment tensor maps.
@@ -597,9 +628,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 seg_gemm_tma(const __grid_constant__ MapPack mp, int seg_first,
              const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, int n_tiles, int H,
              const float* __restrict__ A, long long a_hs, const float* __restrict__ B,
-             long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin) {
+             long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin,
+             bool cin_async) {
   gemm_body<kSplit, true>(segs, tiles, n_tiles, H, A, a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
-                          mp.m, seg_first);
+                          mp.m, seg_first, cin_async);
 }
 
 constexpr int kMaxDevices = 64;
@@ -748,14 +780,21 @@ int tt_gdn_seg_gemm_tma(const SegDesc* h_segs, int seg_first, int seg_count,
       g_attr_set[dev][si] = true;
     }
   }
+  // the epilogue's 16-byte C_in prefetch needs every row of C_in 16-byte aligned
+  const float* cin = Cin ? Cin : C;
+  bool cin_async = beta != 0.f && (reinterpret_cast<uintptr_t>(cin) & 15u) == 0 && (c_hs & 3) == 0;
+  for (int i = 0; i < seg_count && cin_async; ++i)
+    cin_async = (h_segs[i].c_off & 3) == 0 && (h_segs[i].c_rs & 3) == 0;
   const long long items = (long long)n_tiles * H;
   const int grid = (int)std::min<long long>(items, g_sms[dev]);
   if (split == 3)
     seg_gemm_tma<3><<<grid, kThreads, smem, st>>>(mp, seg_first, d_desc, d_tiles, n_tiles, H, A,
-                                                   a_hs, B, b_hs, C, c_hs, alpha, beta, Cin);
+                                                   a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
+                                                   cin_async);
   else
     seg_gemm_tma<1><<<grid, kThreads, smem, st>>>(mp, seg_first, d_desc, d_tiles, n_tiles, H, A,
-                                                   a_hs, B, b_hs, C, c_hs, alpha, beta, Cin);
+                                                   a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
+                                                   cin_async);
   return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
 }
 
