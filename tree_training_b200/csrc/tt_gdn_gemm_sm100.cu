@@ -78,6 +78,9 @@ constexpr int kStgBytes = kEpilogueWarps * 32 * kStgPitch * 4;
 // columns) before they wait for the accumulator, so the reads of C_in overlap
 // the tile's main loop instead of stalling the epilogue row by row.
 constexpr int kCinBytes = kEpilogueWarps * 32 * kTN * 4;
+// epilogue options a launch can use (host-checked alignment)
+constexpr int kEpiCinAsync = 1;   // C_in rows 16-byte aligned: prefetch them by cp.async
+constexpr int kEpiVecC = 2;       // C rows 16-byte aligned: 16-byte stores
 
 template <int kSplit>
 constexpr size_t smem_bytes() {
@@ -286,7 +289,7 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
                                           const float* __restrict__ B, long long b_hs, float* C,
                                           long long c_hs, float alpha, float beta,
                                           const float* Cin, const CUtensorMap* maps,
-                                          int seg_first, bool cin_async) {
+                                          int seg_first, int epi_flags) {
   using R = Ring<kSplit>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>(
@@ -529,7 +532,10 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
       // 32 rows (one 512-byte row segment per instruction), zero-filled past
       // the segment; it lands while the tile's MMAs run
       float* cinb = cin_all + quad * 32 * kTN;
-      const bool pre = cin_async && beta != 0.f;
+      const bool pre = (epi_flags & kEpiCinAsync) && beta != 0.f;
+      // 16-byte stores need 16-byte aligned rows of C, and C_in (if any)
+      // already in shared memory
+      const bool vec = (epi_flags & kEpiVecC) && (beta == 0.f || pre);
       if (pre) {
         const int col = j0 + 4 * lane;
         const int ncol = min(max(sd.N - col, 0), 4);
@@ -568,30 +574,64 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
 #pragma unroll
         for (int i = 0; i < 32; ++i) stg[lane * kStgPitch + i] = empty_k ? 0.f : alpha * v[i];
         __syncwarp();
-        const int gj = j0 + cc * 32 + lane;
-        if (gj < sd.N && rows > 0) {
-          const long long o0 = hoff + (long long)(i0 + quad * 32) * sd.c_rs + gj;
+        if (vec) {
+          // 16-byte stores, 4 rows per instruction: lane l takes row
+          // (l >> 3) + 4 k and columns [4 (l & 7), 4 (l & 7) + 4) of the block
+          // (the reads of the padded block hit 32 distinct banks)
+          const int q4 = (lane & 7) * 4, rsub = lane >> 3;
+          const int gq = j0 + cc * 32 + q4;
+          const int ncol = min(max(sd.N - gq, 0), 4);
+          const long long o0 = hoff + (long long)(i0 + quad * 32) * sd.c_rs + gq;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            float cv[16];
-            if (pre) {
+          for (int k = 0; k < 8; ++k) {
+            const int r = rsub + 4 * k;
+            if (r < rows && ncol > 0) {
+              const float* sr = stg + r * kStgPitch + q4;
+              float4 x = make_float4(sr[0], sr[1], sr[2], sr[3]);
+              if (pre) {
+                const float4 c = *reinterpret_cast<const float4*>(cinb + r * kTN + cc * 32 + q4);
+                x.x += beta * c.x;
+                x.y += beta * c.y;
+                x.z += beta * c.z;
+                x.w += beta * c.w;
+              }
+              float* dst = C + o0 + (long long)r * sd.c_rs;
+              if (ncol == 4) {
+                *reinterpret_cast<float4*>(dst) = x;
+              } else {
+                dst[0] = x.x;
+                if (ncol > 1) dst[1] = x.y;
+                if (ncol > 2) dst[2] = x.z;
+              }
+            }
+          }
+        } else {
+          const int gj = j0 + cc * 32 + lane;
+          if (gj < sd.N && rows > 0) {
+            const long long o0 = hoff + (long long)(i0 + quad * 32) * sd.c_rs + gj;
 #pragma unroll
-              for (int rr = 0; rr < 16; ++rr) cv[rr] = cinb[(half * 16 + rr) * kTN + cc * 32 + lane];
-            } else if (beta != 0.f) {
-              // 16 rows' C_in loads in flight before the first store
+            for (int half = 0; half < 2; ++half) {
+              float cv[16];
+              if (pre) {
+#pragma unroll
+                for (int rr = 0; rr < 16; ++rr)
+                  cv[rr] = cinb[(half * 16 + rr) * kTN + cc * 32 + lane];
+              } else if (beta != 0.f) {
+                // 16 rows' C_in loads in flight before the first store
+#pragma unroll
+                for (int rr = 0; rr < 16; ++rr) {
+                  const int r = half * 16 + rr;
+                  cv[rr] = r < rows ? cin[o0 + (long long)r * sd.c_rs] : 0.f;
+                }
+              }
 #pragma unroll
               for (int rr = 0; rr < 16; ++rr) {
                 const int r = half * 16 + rr;
-                cv[rr] = r < rows ? cin[o0 + (long long)r * sd.c_rs] : 0.f;
-              }
-            }
-#pragma unroll
-            for (int rr = 0; rr < 16; ++rr) {
-              const int r = half * 16 + rr;
-              if (r < rows) {
-                float x = stg[r * kStgPitch + lane];
-                if (beta != 0.f) x += beta * cv[rr];
-                C[o0 + (long long)r * sd.c_rs] = x;
+                if (r < rows) {
+                  float x = stg[r * kStgPitch + lane];
+                  if (beta != 0.f) x += beta * cv[rr];
+                  C[o0 + (long long)r * sd.c_rs] = x;
+                }
               }
             }
           }
@@ -619,7 +659,7 @@ seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, in
             const float* __restrict__ A, long long a_hs, const float* __restrict__ B,
             long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin) {
   gemm_body<kSplit, false>(segs, tiles, n_tiles, H, A, a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
-                           nullptr, 0, false);
+                           nullptr, 0, 0);
 }
 
 // Operands staged with TMA tile copies through per-segment tensor maps.
@@ -629,9 +669,9 @@ seg_gemm_tma(const __grid_constant__ MapPack mp, int seg_first,
              const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, int n_tiles, int H,
              const float* __restrict__ A, long long a_hs, const float* __restrict__ B,
              long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin,
-             bool cin_async) {
+             int epi_flags) {
   gemm_body<kSplit, true>(segs, tiles, n_tiles, H, A, a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
-                          mp.m, seg_first, cin_async);
+                          mp.m, seg_first, epi_flags);
 }
 
 constexpr int kMaxDevices = 64;
@@ -780,21 +820,25 @@ int tt_gdn_seg_gemm_tma(const SegDesc* h_segs, int seg_first, int seg_count,
       g_attr_set[dev][si] = true;
     }
   }
-  // the epilogue's 16-byte C_in prefetch needs every row of C_in 16-byte aligned
+  // the epilogue's 16-byte C_in prefetch and C stores need every row of C_in
+  // and C 16-byte aligned
   const float* cin = Cin ? Cin : C;
-  bool cin_async = beta != 0.f && (reinterpret_cast<uintptr_t>(cin) & 15u) == 0 && (c_hs & 3) == 0;
-  for (int i = 0; i < seg_count && cin_async; ++i)
-    cin_async = (h_segs[i].c_off & 3) == 0 && (h_segs[i].c_rs & 3) == 0;
+  bool rows16 = (c_hs & 3) == 0;
+  for (int i = 0; i < seg_count && rows16; ++i)
+    rows16 = (h_segs[i].c_off & 3) == 0 && (h_segs[i].c_rs & 3) == 0;
+  const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const int epi_flags = (rows16 && beta != 0.f && al16(cin) ? kEpiCinAsync : 0) |
+                        (rows16 && al16(C) ? kEpiVecC : 0);
   const long long items = (long long)n_tiles * H;
   const int grid = (int)std::min<long long>(items, g_sms[dev]);
   if (split == 3)
     seg_gemm_tma<3><<<grid, kThreads, smem, st>>>(mp, seg_first, d_desc, d_tiles, n_tiles, H, A,
                                                    a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
-                                                   cin_async);
+                                                   epi_flags);
   else
     seg_gemm_tma<1><<<grid, kThreads, smem, st>>>(mp, seg_first, d_desc, d_tiles, n_tiles, H, A,
                                                    a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
-                                                   cin_async);
+                                                   epi_flags);
   return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
 }
 
