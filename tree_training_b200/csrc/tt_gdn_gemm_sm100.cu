@@ -530,7 +530,9 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
       const int rows = sd.M - (i0 + quad * 32);      // rows of this warp's block in C
       // C_in prefetch: lane l copies columns [4l, 4l + 4) of each of the warp's
       // 32 rows (one 512-byte row segment per instruction), zero-filled past
-      // the segment; it lands while the tile's MMAs run
+      // the segment; it lands while the tile's MMAs run.  Row r's 16-byte
+      // chunk c sits at slot c ^ r of the row, so a warp reading one chunk of
+      // each of its 32 rows spreads over every bank.
       float* cinb = cin_all + quad * 32 * kTN;
       const bool pre = (epi_flags & kEpiCinAsync) && beta != 0.f;
       // 16-byte stores need 16-byte aligned rows of C, and C_in (if any)
@@ -540,12 +542,12 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
         const int col = j0 + 4 * lane;
         const int ncol = min(max(sd.N - col, 0), 4);
         const float* base = cin + hoff + (long long)(i0 + quad * 32) * sd.c_rs + col;
-        const uint32_t dst0 = smem_u32(cinb) + lane * 16;
+        const uint32_t dst0 = smem_u32(cinb);
 #pragma unroll 4
         for (int r = 0; r < 32; ++r) {
           const int n_el = r < rows ? ncol : 0;
-          cp_async16(dst0 + r * kTN * 4, n_el > 0 ? base + (long long)r * sd.c_rs : cin,
-                     (uint32_t)n_el * 4u);
+          cp_async16(dst0 + r * kTN * 4 + ((lane ^ r) << 4),
+                     n_el > 0 ? base + (long long)r * sd.c_rs : cin, (uint32_t)n_el * 4u);
         }
         cp_async_commit();
       }
@@ -564,38 +566,35 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
       int kb, nk;
       k_range(sd, i0, j0, kb, nk);
       const bool empty_k = nk == 0;            // no MMA wrote this accumulator
-      // each 32 x 32 block goes through shared memory so that the warp
-      // stores (and reads C_in) one 128-byte row segment per instruction
+      // without 16-byte aligned rows of C, each 32 x 32 block goes through
+      // shared memory so that the warp stores (and reads C_in) one 128-byte
+      // row segment per instruction
       float* stg = stg_all + quad * 32 * kStgPitch;
 #pragma unroll 1
       for (int cc = 0; cc < kTN / 32; ++cc) {
         float v[32];
         tmem_ld32(lane_addr + buf * kTN + cc * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) stg[lane * kStgPitch + i] = empty_k ? 0.f : alpha * v[i];
-        __syncwarp();
         if (vec) {
-          // 16-byte stores, 4 rows per instruction: lane l takes row
-          // (l >> 3) + 4 k and columns [4 (l & 7), 4 (l & 7) + 4) of the block
-          // (the reads of the padded block hit 32 distinct banks)
-          const int q4 = (lane & 7) * 4, rsub = lane >> 3;
-          const int gq = j0 + cc * 32 + q4;
-          const int ncol = min(max(sd.N - gq, 0), 4);
-          const long long o0 = hoff + (long long)(i0 + quad * 32) * sd.c_rs + gq;
+          // straight from the accumulator rows: lane = row, eight 16-byte
+          // stores of its 32 columns (no staging through shared memory)
+          const long long orow = hoff + (long long)(i0 + quad * 32 + lane) * sd.c_rs;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            const int r = rsub + 4 * k;
-            if (r < rows && ncol > 0) {
-              const float* sr = stg + r * kStgPitch + q4;
-              float4 x = make_float4(sr[0], sr[1], sr[2], sr[3]);
-              if (pre) {
-                const float4 c = *reinterpret_cast<const float4*>(cinb + r * kTN + cc * 32 + q4);
-                x.x += beta * c.x;
-                x.y += beta * c.y;
-                x.z += beta * c.z;
-                x.w += beta * c.w;
-              }
-              float* dst = C + o0 + (long long)r * sd.c_rs;
+            const int c = cc * 8 + k;                 // 16-byte chunk of the tile row
+            const int ncol = min(max(sd.N - (j0 + 4 * c), 0), 4);
+            float4 x = empty_k ? make_float4(0.f, 0.f, 0.f, 0.f)
+                               : make_float4(alpha * v[4 * k], alpha * v[4 * k + 1],
+                                             alpha * v[4 * k + 2], alpha * v[4 * k + 3]);
+            if (pre) {
+              const float4 cv =
+                  *reinterpret_cast<const float4*>(cinb + lane * kTN + ((c ^ lane) << 2));
+              x.x += beta * cv.x;
+              x.y += beta * cv.y;
+              x.z += beta * cv.z;
+              x.w += beta * cv.w;
+            }
+            if (lane < rows && ncol > 0) {
+              float* dst = C + orow + j0 + 4 * c;
               if (ncol == 4) {
                 *reinterpret_cast<float4*>(dst) = x;
               } else {
@@ -606,6 +605,9 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
             }
           }
         } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) stg[lane * kStgPitch + i] = empty_k ? 0.f : alpha * v[i];
+          __syncwarp();
           const int gj = j0 + cc * 32 + lane;
           if (gj < sd.N && rows > 0) {
             const long long o0 = hoff + (long long)(i0 + quad * 32) * sd.c_rs + gj;
@@ -614,8 +616,10 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
               float cv[16];
               if (pre) {
 #pragma unroll
-                for (int rr = 0; rr < 16; ++rr)
-                  cv[rr] = cinb[(half * 16 + rr) * kTN + cc * 32 + lane];
+                for (int rr = 0; rr < 16; ++rr) {
+                  const int r = half * 16 + rr;
+                  cv[rr] = cinb[r * kTN + (((cc * 8 + (lane >> 2)) ^ r) << 2) + (lane & 3)];
+                }
               } else if (beta != 0.f) {
                 // 16 rows' C_in loads in flight before the first store
 #pragma unroll
@@ -635,8 +639,8 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
               }
             }
           }
+          __syncwarp();
         }
-        __syncwarp();
       }
       tc_fence_before();
       mbar_arrive(&sh->acc_empty[buf]);
