@@ -303,8 +303,10 @@ def _gemm_mode(mode):
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 2e-5), (torch.bfloat16, 1e-2)])
 def test_gdn_tensor_core_gemm_matches_cuda_core_gemm(dtype, tol):
     """The same forward and backward with the segmented GEMMs on the tensor
-    cores (default: 3xTF32 products for fp32 inputs, TF32 for bf16) and on
-    the CUDA cores (fp32 FMA).  The tree has an empty node, one-token nodes,
+    cores (default: 3xTF32 products for fp32 inputs, TF32 for bf16, operands
+    staged by TMA, decay masks applied in the K K^T / Q K^T epilogues), on the
+    tensor cores with cp.async staging (masks applied by their own kernel) and
+    on the CUDA cores (fp32 FMA).  The tree has an empty node, one-token nodes,
     and nodes past one 128-row tile (up to 300 tokens), D = 128 and GQA 2:4."""
     lens = [300, 0, 1, 129, 7, 128, 64, 1, 250, 33]
     parents = [-1, 0, 0, 2, 3, 3, 1, 6, 0, 8]
@@ -323,7 +325,7 @@ def test_gdn_tensor_core_gemm_matches_cuda_core_gemm(dtype, tol):
     do = g_.standard_normal((1, S, H, D))
     dl = g_.standard_normal((1, H, D, D))
     res = []
-    for mode in (0, 2):
+    for mode in (0, 2, 4):
         prev = _gemm_mode(mode)
         try:
             res.append(run_gdn(q, k, v, gg, bt, bounds, parents, s0_, True, do, dl, dtype))
@@ -332,7 +334,8 @@ def test_gdn_tensor_core_gemm_matches_cuda_core_gemm(dtype, tol):
     tt.check_device_status(DEV)
     for key in ("out", "last", "dq", "dk", "dv", "dg", "dbeta", "dinit"):
         assert np.isfinite(res[0][key]).all(), key
-        assert rel(res[0][key], res[1][key]) < tol, (key, rel(res[0][key], res[1][key]))
+        for other in res[1:]:
+            assert rel(res[0][key], other[key]) < tol, (key, rel(res[0][key], other[key]))
     # and the tensor-core result against the float64 oracle at the GDN bar, on
     # the same tree without its empty node (which the reference's algorithm,
     # like the oracle, cannot take: it reads the node's last cumulative gate)

@@ -385,11 +385,15 @@ __global__ void dstate_decay(int H, int DkDv, int n_nodes, const int* __restrict
 //   G   = -dA * D (-> dKb += G K, dK += G^T Kb)
 //   F   = dAqk * D (lower incl.; -> dQ += F K, dK += F^T Q)
 //   dDD = (-dA * KK + dAqk * QK) * D, whose row/col sums give dgam.
+// KK / QK: the raw products (premasked = 0) or the masked A and Aqk
+// (premasked = 1, A = -KK D below the diagonal, Aqk = QK D on and below it):
+// either way dDD = (-dA KK + dAqk QK) D = dA A + dAqk Aqk.
 __global__ void grad_masks(int S, const int* __restrict__ nstart, const int* __restrict__ nlen,
                            const int* __restrict__ tok_node,
                            const long long* __restrict__ loff, long long l_hs,
                            const float* __restrict__ gam, const float* __restrict__ KK,
-                           const float* __restrict__ QK, float* dA, float* dAqk, float* dDD) {
+                           const float* __restrict__ QK, int premasked, float* dA, float* dAqk,
+                           float* dDD) {
   const int t = blockIdx.x, h = blockIdx.y, c = tok_node[t], j = t - nstart[c];
   const int L = nlen[c];
   const long long base = h * l_hs + loff[c] + (long long)j * row_stride(L);
@@ -398,7 +402,8 @@ __global__ void grad_masks(int S, const int* __restrict__ nstart, const int* __r
     const float d = m <= j ? expf(gj - gam[(long long)h * S + nstart[c] + m]) : 0.f;
     const float da = m < j ? dA[base + m] : 0.f;
     const float dq = m <= j ? dAqk[base + m] : 0.f;
-    dDD[base + m] = (-da * KK[base + m] + dq * QK[base + m]) * d;
+    dDD[base + m] = premasked ? da * KK[base + m] + dq * QK[base + m]
+                              : (-da * KK[base + m] + dq * QK[base + m]) * d;
     dA[base + m] = -da * d;      // G
     dAqk[base + m] = dq * d;     // F
   }
@@ -703,7 +708,7 @@ SegDesc desc(int M, int N, int K, long long ao, long long ars, long long acs, lo
              long long brs, long long bcs, long long co, long long crs, long long ccs,
              int kmode = kKFull) {
   SegDesc d;
-  d.M = M; d.N = N; d.K = K; d.kmode = kmode;
+  d.M = M; d.N = N; d.K = K; d.kmode = kmode; d.tok0 = 0;
   d.a_off = ao; d.a_rs = ars; d.a_cs = acs;
   d.b_off = bo; d.b_rs = brs; d.b_cs = bcs;
   d.c_off = co; d.c_rs = crs; d.c_cs = ccs;
@@ -749,10 +754,15 @@ struct GemmCtx {
 // C = alpha A B + beta Cin (Cin defaults to C; it has C's offsets and strides)
 void launch_gemm(GemmCtx& g, DescSet ds, int H, const float* A, long long a_hs, const float* B,
                  long long b_hs, float* C, long long c_hs, float alpha, float beta,
-                 cudaStream_t st, const float* Cin = nullptr) {
+                 cudaStream_t st, const float* Cin = nullptr, EpiMask mask = {}) {
   if (ds.tcount == 0) return;
-  if (g.split != 0 && tt_gdn_tc_gemm_supported(g.h_desc->data(), ds.first, ds.count, A, a_hs, B,
-                                               b_hs, C, c_hs)) {
+  const bool tc = g.split != 0 && tt_gdn_tc_gemm_supported(g.h_desc->data(), ds.first, ds.count,
+                                                           A, a_hs, B, b_hs, C, c_hs);
+  if (mask.mode != kMaskNone && !tc) {   // only the tensor-core epilogue applies masks
+    g.rc = TT_ERR_UNSUPPORTED;
+    return;
+  }
+  if (tc) {
     int launches = 0;
     if (g.tma) {
       // chunks of at most kTmaMaxSegs segments (their tensor maps travel as
@@ -766,17 +776,18 @@ void launch_gemm(GemmCtx& g, DescSet ds, int H, const float* A, long long a_hs, 
         while (t1 < t_end && (*g.h_tiles_tc)[t1].x < seg_end) ++t1;
         int rc = tt_gdn_seg_gemm_tma(g.h_desc->data() + ds.first + c0, ds.first + c0, c1 - c0,
                                      g.d_desc, g.d_tiles_tc + t, t1 - t, H, A, a_hs, B, b_hs, C,
-                                     c_hs, alpha, beta, Cin, g.split, st);
+                                     c_hs, alpha, beta, Cin, g.split, st, mask);
         if (rc == TT_ERR_UNSUPPORTED)
           rc = tt_gdn_seg_gemm_tc(g.d_desc, g.d_tiles_tc + t, t1 - t, H, A, a_hs, B, b_hs, C,
-                                  c_hs, alpha, beta, Cin, g.split, st);
+                                  c_hs, alpha, beta, Cin, g.split, st, mask);
         if (rc != TT_OK) g.rc = rc;
         if (t1 > t) ++launches;
         t = t1;
       }
     } else {
       const int rc = tt_gdn_seg_gemm_tc(g.d_desc, g.d_tiles_tc + ds.tc_first, ds.tc_count, H, A,
-                                        a_hs, B, b_hs, C, c_hs, alpha, beta, Cin, g.split, st);
+                                        a_hs, B, b_hs, C, c_hs, alpha, beta, Cin, g.split, st,
+                                        mask);
       if (rc != TT_OK) g.rc = rc;
       launches = 1;
     }
@@ -843,16 +854,16 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   }
   // metadata + descriptors
   Builder bd(p);
-  std::vector<SegDesc> v_kk, v_qk, v_av, v_ak, v_ws, v_qs, v_aqv, v_kdv;
-  std::vector<std::vector<SegDesc>> lv_ws(p.levels.size()), lv_qs(p.levels.size()),
-      lv_aqv(p.levels.size()), lv_kdv(p.levels.size());
+  std::vector<SegDesc> v_kk, v_av, v_ak, v_qs, v_aqv;
+  std::vector<std::vector<SegDesc>> lv_ws(p.levels.size()), lv_kdv(p.levels.size());
   for (int c = 0; c < n; ++c) {
     const int L = p.len[c];
     const long long tk = (long long)p.start[c] * Dk, tv = (long long)p.start[c] * Dv;
     const long long lo = p.loff[c];
     const int Lp = row_stride(L);
-    // KK = Kb K^T, QK = Q K^T : [L x L], K = Dk
+    // KK = Kb K^T, QK = Q K^T : [L x L], K = Dk (tok0: the decay-mask epilogue)
     v_kk.push_back(desc(L, L, Dk, tk, Dk, 1, tk, 1, Dk, lo, Lp, 1));
+    v_kk.back().tok0 = p.start[c];
     // A * X for X = [L x Dv] (U) / [L x Dk] (W)
     v_av.push_back(desc(L, Dv, L, lo, Lp, 1, tv, Dv, 1, tv, Dv, 1, kKToRow));
     v_ak.push_back(desc(L, Dk, L, lo, Lp, 1, tk, Dk, 1, tk, Dk, 1, kKToRow));
@@ -866,11 +877,12 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
       const long long sout = (long long)(c + 1) * st_off;
       // Vn -= W S_in : [L x Dv] = [L x Dk][Dk x Dv]
       lv_ws[d].push_back(desc(L, Dv, Dk, tk, Dk, 1, sin, Dv, 1, tv, Dv, 1));
-      // O = Qg S_in
-      lv_qs[d].push_back(desc(L, Dv, Dk, tk, Dk, 1, sin, Dv, 1, tv, Dv, 1));
-      // O += Aqk Vn
-      lv_aqv[d].push_back(desc(L, Dv, L, p.loff[c], row_stride(L), 1, tv, Dv, 1, tv, Dv, 1,
-                               kKToRow));
+      // O = Qg S_in, then O += Aqk Vn: they read the recurrence's results
+      // but feed nothing back into it, so each runs once over every node
+      // after the level sweep
+      v_qs.push_back(desc(L, Dv, Dk, tk, Dk, 1, sin, Dv, 1, tv, Dv, 1));
+      v_aqv.push_back(desc(L, Dv, L, p.loff[c], row_stride(L), 1, tv, Dv, 1, tv, Dv, 1,
+                           kKToRow));
       // S_out = Kd^T Vn : [Dk x Dv] = [Dk x L][L x Dv]
       lv_kdv[d].push_back(desc(Dk, Dv, L, tk, 1, Dk, tv, Dv, 1, sout, Dv, 1));
     }
@@ -901,16 +913,15 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     ds_inv_x.push_back(bd.add(li_x[i]));
     ds_inv_t.push_back(bd.add(li_t[i]));
   }
-  std::vector<DescSet> ds_ws, ds_qs, ds_aqv, ds_kdv;
+  std::vector<DescSet> ds_ws, ds_kdv;
   for (size_t d = 0; d < p.levels.size(); ++d) {
     ds_ws.push_back(bd.add(lv_ws[d]));
-    ds_qs.push_back(bd.add(lv_qs[d]));
-    ds_aqv.push_back(bd.add(lv_aqv[d]));
     ds_kdv.push_back(bd.add(lv_kdv[d]));
   }
+  const DescSet ds_qs = bd.add(v_qs), ds_aqv = bd.add(v_aqv);
   // backward descriptors
-  std::vector<std::vector<SegDesc>> lb_dvn1(p.levels.size()), lb_dvn2(p.levels.size()),
-      lb_dsi1(p.levels.size()), lb_dsi2(p.levels.size());
+  std::vector<std::vector<SegDesc>> lb_dvn2(p.levels.size()), lb_dsi2(p.levels.size());
+  std::vector<SegDesc> b_dvn1, b_dsi1;
   std::vector<SegDesc> b_dqg, b_dkd, b_dw, b_daqk, b_dt1, b_dt2, b_x1, b_x2, b_tvt, b_tvt2,
       b_tkt, b_tkt2, b_gk, b_gtk, b_fk, b_ftq;
   if (backward) {
@@ -920,13 +931,13 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
         const long long tk = (long long)p.start[c] * Dk, tv = (long long)p.start[c] * Dv;
         const long long lo = p.loff[c];
         const long long so = (long long)c * st_off;
-        // dVn = Aqk^T dO : [L x Dv] = [L x L]^T [L x Dv]
-        lb_dvn1[d].push_back(desc(L, Dv, L, lo, 1, row_stride(L), tv, Dv, 1, tv, Dv, 1,
-                                  kKFromRow));
+        // dVn = Aqk^T dO : [L x Dv] = [L x L]^T [L x Dv] (independent of the
+        // reverse sweep: once over every node before it)
+        b_dvn1.push_back(desc(L, Dv, L, lo, 1, row_stride(L), tv, Dv, 1, tv, Dv, 1, kKFromRow));
         // dVn += Kd dSo : [L x Dv] = [L x Dk][Dk x Dv]
         lb_dvn2[d].push_back(desc(L, Dv, Dk, tk, Dk, 1, so, Dv, 1, tv, Dv, 1));
-        // dSi = Qg^T dO : [Dk x Dv] = [Dk x L][L x Dv]
-        lb_dsi1[d].push_back(desc(Dk, Dv, L, tk, 1, Dk, tv, Dv, 1, so, Dv, 1));
+        // dSi = Qg^T dO : [Dk x Dv] = [Dk x L][L x Dv] (likewise before the sweep)
+        b_dsi1.push_back(desc(Dk, Dv, L, tk, 1, Dk, tv, Dv, 1, so, Dv, 1));
         // dSi -= W^T dVn
         lb_dsi2[d].push_back(desc(Dk, Dv, L, tk, 1, Dk, tv, Dv, 1, so, Dv, 1));
       }
@@ -964,13 +975,12 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
           ds_daqk = bd.add(b_daqk), ds_dt1 = bd.add(b_dt1), ds_dt2 = bd.add(b_dt2),
           ds_x1 = bd.add(b_x1), ds_x2 = bd.add(b_x2), ds_tvt = bd.add(b_tvt),
           ds_tkt = bd.add(b_tkt), ds_gk = bd.add(b_gk), ds_gtk = bd.add(b_gtk);
-  std::vector<DescSet> ds_dvn1, ds_dvn2, ds_dsi1, ds_dsi2;
+  std::vector<DescSet> ds_dvn2, ds_dsi2;
   for (size_t d = 0; d < p.levels.size(); ++d) {
-    ds_dvn1.push_back(bd.add(lb_dvn1[d]));
     ds_dvn2.push_back(bd.add(lb_dvn2[d]));
-    ds_dsi1.push_back(bd.add(lb_dsi1[d]));
     ds_dsi2.push_back(bd.add(lb_dsi2[d]));
   }
+  const DescSet ds_dvn1 = bd.add(b_dvn1), ds_dsi1 = bd.add(b_dsi1);
   // int metadata
   std::vector<int> level_nodes, level_first;
   for (auto& l : p.levels) {
@@ -1019,6 +1029,10 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   GemmCtx gc{b.d_desc, b.d_tiles, b.d_tiles_tc, &bd.all, &bd.tiles_tc,
              (mode & 3) == 2 ? 0 : ((mode & 3) == 1 || std::is_same<T, float>::value) ? 3 : 1,
              (mode & 4) == 0};
+  // the decay masks ride on the K K^T / Q K^T epilogues when the TMA-staged
+  // tensor-core GEMM runs them and A is kept (the exact-inverse mode
+  // overwrites it with T)
+  const bool fuse_mask = gc.split != 0 && gc.tma && !exact;
   auto blocks = [](long long nel) { return (unsigned)((nel + 255) / 256); };
   int launches = 0;
   // ---------------------------------------------------------------- forward
@@ -1031,11 +1045,20 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
         b.K, b.Vb, b.Kb,
         b.Kbg, b.Qg, b.Kd);
     launches += 2;
-    launch_gemm(gc, ds_kk, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
-    launch_gemm(gc, ds_kk, H, b.Q, vk, b.K, vk, b.QK, llh, 1.f, 0.f, st);
-    decay_masks<<<dim3(S, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_tok_node, b.d_loff, llh,
-                                             b.gam, b.KK, b.QK, b.Am, b.Aqk);
-    ++launches;
+    if (fuse_mask) {
+      // A = -(Kb K^T) * D (strictly lower), Aqk = (Q K^T) * D (lower) straight
+      // from the GEMM epilogue
+      launch_gemm(gc, ds_kk, H, b.Kb, vk, b.K, vk, b.Am, llh, 1.f, 0.f, st, nullptr,
+                  EpiMask{kMaskA, b.gam, (long long)S});
+      launch_gemm(gc, ds_kk, H, b.Q, vk, b.K, vk, b.Aqk, llh, 1.f, 0.f, st, nullptr,
+                  EpiMask{kMaskAqk, b.gam, (long long)S});
+    } else {
+      launch_gemm(gc, ds_kk, H, b.Kb, vk, b.K, vk, b.KK, llh, 1.f, 0.f, st);
+      launch_gemm(gc, ds_kk, H, b.Q, vk, b.K, vk, b.QK, llh, 1.f, 0.f, st);
+      decay_masks<<<dim3(S, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_tok_node, b.d_loff, llh,
+                                               b.gam, b.KK, b.QK, b.Am, b.Aqk);
+      ++launches;
+    }
     if (exact) {
       // Am <- T = (I - A)^-1 in place: diagonal blocks, then block rows in order
       tri_inv_diag<<<dim3((unsigned)inv_blocks.size(), H), kInvB, 0, st>>>(
@@ -1066,16 +1089,14 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
       // states are [n+1][H][Dk][Dv]: per-head stride DkDv, segment offsets cover (c+1)*H*DkDv
       // Vn = U - W S_in (every node's rows are written by its own level)
       launch_gemm(gc, ds_ws[d], H, b.W, vk, b.states, DkDv, b.Vn, vv, -1.f, 1.f, st, b.U);
-      if (!backward) {   // the output; the backward (which recomputes this pass) never reads it
-        launch_gemm(gc, ds_qs[d], H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f,
-                    st);
-        launch_gemm(gc, ds_aqv[d], H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f,
-                    st);
-      }
       launch_gemm(gc, ds_kdv[d], H, b.Kd, vk, b.Vn, vv, b.states, DkDv, 1.f, 0.f, st);
       state_decay_add<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
           H, DkDv, n, b.d_level_nodes + level_first[d], b.d_parent, b.gl, b.states);
       ++launches;
+    }
+    if (!backward) {   // the output; the backward (which recomputes this pass) never reads it
+      launch_gemm(gc, ds_qs, H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f, st);
+      launch_gemm(gc, ds_aqv, H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f, st);
     }
   }
   if (!backward) {
@@ -1096,14 +1117,14 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   // ---------------------------------------------------------------- backward
   load_dout<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(S, H, Dv, (const T*)dout_, b.dO);
   ++launches;
+  launch_gemm(gc, ds_dvn1, H, b.Aqk, llh, b.dO, vv, b.dVn, vv, 1.f, 0.f, st);
+  launch_gemm(gc, ds_dsi1, H, b.Qg, vk, b.dO, vv, b.dSi, DkDv, 1.f, 0.f, st);
   for (int d = (int)p.levels.size() - 1; d >= 0; --d) {
     const int cnt = (int)p.levels[d].size();
     gather_dstate<<<dim3(std::max(1, DkDv / 1024), cnt, H), 256, 0, st>>>(
         H, DkDv, n, b.d_level_nodes + level_first[d], b.d_child_ptr, b.d_child_idx, b.dSi, dlast,
         b.d_cap_slot, dcaptured, b.dSo);
-    launch_gemm(gc, ds_dvn1[d], H, b.Aqk, llh, b.dO, vv, b.dVn, vv, 1.f, 0.f, st);
     launch_gemm(gc, ds_dvn2[d], H, b.Kd, vk, b.dSo, DkDv, b.dVn, vv, 1.f, 1.f, st);
-    launch_gemm(gc, ds_dsi1[d], H, b.Qg, vk, b.dO, vv, b.dSi, DkDv, 1.f, 0.f, st);
     launch_gemm(gc, ds_dsi2[d], H, b.W, vk, b.dVn, vv, b.dSi, DkDv, -1.f, 1.f, st);
     dstate_decay<<<dim3(cnt, H), 256, 0, st>>>(H, DkDv, n, b.d_level_nodes + level_first[d],
                                                b.d_parent, b.gl, b.states, b.dSo, b.dSi, b.dgl);
@@ -1136,7 +1157,9 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   // masks: dA -> G = -dA*D, dAqk -> F = dAqk*D, dDD
   TT_CUDA_OK(cudaMemsetAsync(b.dgam, 0, (size_t)H * S * 4, st));
   grad_masks<<<dim3(S, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_tok_node, b.d_loff, llh,
-                                            b.gam, b.KK, b.QK, b.dA, b.dAqk, b.dDD);
+                                            b.gam, fuse_mask ? b.Am : b.KK,
+                                            fuse_mask ? b.Aqk : b.QK, fuse_mask ? 1 : 0, b.dA,
+                                            b.dAqk, b.dDD);
   ddd_rowcol<<<dim3(n, H), kRowColThreads, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh,
                                                      b.dDD, b.rowsum, b.dgam);
   launches += 2;

@@ -14,6 +14,7 @@ namespace gdn {
 struct SegDesc {
   int M, N, K;
   int kmode;   // which part of the K range can hold nonzero products (kKFull, ...)
+  int tok0;    // first token of the segment's node (the decay-mask epilogue)
   long long a_off, a_rs, a_cs;
   long long b_off, b_rs, b_cs;
   long long c_off, c_rs, c_cs;
@@ -27,6 +28,18 @@ struct SegDesc {
 //   kKToCol  B upper triangular (B[k][n] = 0 for k > n): k < col + 1;
 //   kKFromCol B lower triangular: k >= col.
 enum { kKFull = 0, kKToRow = 1, kKFromRow = 2, kKToCol = 3, kKFromCol = 4 };
+
+// Decay mask applied by the tensor-core GEMM's epilogue to an L x L product
+// of one node (row i, column m, gam the per-token cumulative log decay of
+// the node's tokens, head stride gam_hs):
+//   kMaskA    C = -P * exp(gam_i - gam_m) for m < i, 0 elsewhere (A of the chunk)
+//   kMaskAqk  C =  P * exp(gam_i - gam_m) for m <= i, 0 elsewhere (the q-k weights)
+enum { kMaskNone = 0, kMaskA = 1, kMaskAqk = 2 };
+struct EpiMask {
+  int mode = kMaskNone;
+  const float* gam = nullptr;
+  long long gam_hs = 0;
+};
 
 // Output tile edge of the tensor-core GEMM (tiles of the tile list are
 // kTcTile x kTcTile; the CUDA-core GEMM uses 64 x 64).
@@ -48,7 +61,7 @@ constexpr int kTcTile = 128;
 int tt_gdn_seg_gemm_tc(const tt::gdn::SegDesc* d_desc, const int2* d_tiles, int n_tiles, int H,
                        const float* A, long long a_hs, const float* B, long long b_hs, float* C,
                        long long c_hs, float alpha, float beta, const float* Cin, int split,
-                       cudaStream_t st);
+                       cudaStream_t st, tt::gdn::EpiMask mask = {});
 // The same GEMM with the operand slices staged by TMA tile copies through
 // tensor maps encoded here for each segment (the faster staging): segments
 // seg_first .. seg_first + seg_count - 1 (at most 120; h_segs their host
@@ -59,7 +72,7 @@ int tt_gdn_seg_gemm_tma(const tt::gdn::SegDesc* h_segs, int seg_first, int seg_c
                         const tt::gdn::SegDesc* d_desc, const int2* d_tiles, int n_tiles, int H,
                         const float* A, long long a_hs, const float* B, long long b_hs, float* C,
                         long long c_hs, float alpha, float beta, const float* Cin, int split,
-                        cudaStream_t st);
+                        cudaStream_t st, tt::gdn::EpiMask mask = {});
 constexpr int kTmaMaxSegs = 120;
 bool tt_gdn_tc_gemm_supported(const tt::gdn::SegDesc* h_desc, int first, int count,
                               const float* A, long long a_hs, const float* B, long long b_hs,

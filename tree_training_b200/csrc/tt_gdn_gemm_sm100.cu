@@ -78,6 +78,8 @@ constexpr int kStgBytes = kEpilogueWarps * 32 * kStgPitch * 4;
 // columns) before they wait for the accumulator, so the reads of C_in overlap
 // the tile's main loop instead of stalling the epilogue row by row.
 constexpr int kCinBytes = kEpilogueWarps * 32 * kTN * 4;
+// per epilogue warp the tile's 128 column gammas of a decay-masked product
+constexpr int kGcolBytes = kEpilogueWarps * kTN * 4;
 // epilogue options a launch can use (host-checked alignment)
 constexpr int kEpiCinAsync = 1;   // C_in rows 16-byte aligned: prefetch them by cp.async
 constexpr int kEpiVecC = 2;       // C rows 16-byte aligned: 16-byte stores
@@ -85,7 +87,7 @@ constexpr int kEpiVecC = 2;       // C rows 16-byte aligned: 16-byte stores
 template <int kSplit>
 constexpr size_t smem_bytes() {
   return 1024 + (size_t)Ring<kSplit>::kStages * Ring<kSplit>::kStageBytes + kStgBytes +
-         kCinBytes + sizeof(Bars);
+         kCinBytes + kGcolBytes + sizeof(Bars);
 }
 
 __device__ int32_t g_status;   // first error of any launch since the last take
@@ -99,6 +101,11 @@ __device__ __forceinline__ void record_error(Bars* sh, int32_t code) {
 // the rest of the 16 destination bytes is zero-filled.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes)
+               : "memory");
+}
+// 4-byte global -> shared copy (`bytes` 0 or 4; 0 zero-fills)
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(bytes)
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() {
@@ -282,6 +289,8 @@ __device__ __forceinline__ void tma_slice(uint8_t* dst, const CUtensorMap* map, 
   }
 }
 
+constexpr float kLog2e = 1.4426950408889634f;
+
 template <int kSplit, bool kTma>
 __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
                                           const int2* __restrict__ tiles, int n_tiles, int H,
@@ -289,14 +298,15 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
                                           const float* __restrict__ B, long long b_hs, float* C,
                                           long long c_hs, float alpha, float beta,
                                           const float* Cin, const CUtensorMap* maps,
-                                          int seg_first, int epi_flags) {
+                                          int seg_first, int epi_flags, EpiMask mask) {
   using R = Ring<kSplit>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   float* stg_all = reinterpret_cast<float*>(ring + (size_t)R::kStages * R::kStageBytes);
   float* cin_all = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(stg_all) + kStgBytes);
-  Bars* sh = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(cin_all) + kCinBytes);
+  float* gcol_all = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(cin_all) + kCinBytes);
+  Bars* sh = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(gcol_all) + kGcolBytes);
   const volatile int32_t* abort_flag = &sh->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_items = n_tiles * H;
@@ -551,15 +561,37 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
         }
         cp_async_commit();
       }
+      // decay mask: this lane's row gamma (vec path, log2 units) and the
+      // tile's 128 column gammas, copied into this warp's shared-memory row
+      // before the accumulator wait (they land while the MMAs run)
+      const int row_t = i0 + quad * 32 + lane;
+      const float* gam_h =
+          mask.mode != kMaskNone ? mask.gam + h * mask.gam_hs + sd.tok0 : nullptr;
+      float g_row = 0.f;
+      float* gcb = gcol_all + quad * kTN;
+      if (kTma && mask.mode != kMaskNone) {
+        if (row_t < sd.M) g_row = gam_h[row_t] * kLog2e;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int m = j0 + 4 * lane + e;
+          cp_async4(smem_u32(gcb + 4 * lane + e), m < sd.N ? gam_h + m : gam_h,
+                    m < sd.N ? 4u : 0u);
+        }
+        cp_async_commit();
+      }
       bool ok = mbar_wait(&sh->acc_full[buf], (acc_i >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
-        if (pre) cp_async_wait<0>();          // the copies land before the CTA exits
+        cp_async_wait<0>();                    // the copies land before the CTA exits
         record_error(sh, TT_ERR_DEVICE_TIMEOUT);
         break;
       }
       tc_fence_after();
       if (pre) {
+        cp_async_wait<0>();
+        __syncwarp();
+      }
+      if (kTma && mask.mode != kMaskNone) {
         cp_async_wait<0>();
         __syncwarp();
       }
@@ -574,6 +606,20 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
       for (int cc = 0; cc < kTN / 32; ++cc) {
         float v[32];
         tmem_ld32(lane_addr + buf * kTN + cc * 32, v);
+        // (the TMA-staged kernel only: the cp.async one takes no mask).  The
+        // decay is exp(gam_i - gam_m) = 2^(log2e gam_i - log2e gam_m), on the
+        // SFU (about 2 ulp); masked columns select 0.
+        if (kTma && mask.mode != kMaskNone && !empty_k) {   // lane = row of the block
+          const int c0 = j0 + cc * 32;
+          const bool strict = mask.mode == kMaskA;
+          const float sgn = strict ? -1.f : 1.f;
+          const int lim = strict ? row_t : row_t + 1;   // kept columns: m < lim
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float d = fast_exp2(fmaf(-gcb[cc * 32 + i], kLog2e, g_row));
+            v[i] = c0 + i < lim ? sgn * v[i] * d : 0.f;
+          }
+        }
         if (vec) {
           // straight from the accumulator rows: lane = row, eight 16-byte
           // stores of its 32 columns (no staging through shared memory)
@@ -642,6 +688,7 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
           __syncwarp();
         }
       }
+      __syncwarp();   // every lane is done with this tile's C_in and gamma rows
       tc_fence_before();
       mbar_arrive(&sh->acc_empty[buf]);
       f.fetch_seg();
@@ -661,9 +708,10 @@ template <int kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
 seg_gemm_tc(const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, int n_tiles, int H,
             const float* __restrict__ A, long long a_hs, const float* __restrict__ B,
-            long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin) {
+            long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin,
+            EpiMask mask) {
   gemm_body<kSplit, false>(segs, tiles, n_tiles, H, A, a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
-                           nullptr, 0, 0);
+                           nullptr, 0, 0, mask);
 }
 
 // Operands staged with TMA tile copies through per-segment tensor maps.
@@ -673,9 +721,9 @@ seg_gemm_tma(const __grid_constant__ MapPack mp, int seg_first,
              const SegDesc* __restrict__ segs, const int2* __restrict__ tiles, int n_tiles, int H,
              const float* __restrict__ A, long long a_hs, const float* __restrict__ B,
              long long b_hs, float* C, long long c_hs, float alpha, float beta, const float* Cin,
-             int epi_flags) {
+             int epi_flags, EpiMask mask) {
   gemm_body<kSplit, true>(segs, tiles, n_tiles, H, A, a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
-                          mp.m, seg_first, epi_flags);
+                          mp.m, seg_first, epi_flags, mask);
 }
 
 constexpr int kMaxDevices = 64;
@@ -750,8 +798,9 @@ bool tt_gdn_tc_gemm_supported(const SegDesc* d, int first, int count, const floa
 int tt_gdn_seg_gemm_tc(const SegDesc* d_desc, const int2* d_tiles, int n_tiles, int H,
                        const float* A, long long a_hs, const float* B, long long b_hs, float* C,
                        long long c_hs, float alpha, float beta, const float* Cin, int split,
-                       cudaStream_t st) {
+                       cudaStream_t st, tt::gdn::EpiMask mask) {
   using namespace tt::gdn;
+  if (mask.mode != kMaskNone) return TT_ERR_UNSUPPORTED;   // masks: TMA-staged kernel only
   if (n_tiles <= 0 || H <= 0) return TT_OK;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TT_ERR_CUDA;
@@ -776,10 +825,10 @@ int tt_gdn_seg_gemm_tc(const SegDesc* d_desc, const int2* d_tiles, int n_tiles, 
   const int grid = (int)std::min<long long>(items, g_sms[dev]);
   if (split == 3)
     seg_gemm_tc<3><<<grid, kThreads, smem, st>>>(d_desc, d_tiles, n_tiles, H, A, a_hs, B, b_hs,
-                                                  C, c_hs, alpha, beta, Cin);
+                                                  C, c_hs, alpha, beta, Cin, mask);
   else
     seg_gemm_tc<1><<<grid, kThreads, smem, st>>>(d_desc, d_tiles, n_tiles, H, A, a_hs, B, b_hs,
-                                                  C, c_hs, alpha, beta, Cin);
+                                                  C, c_hs, alpha, beta, Cin, mask);
   return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
 }
 
@@ -787,7 +836,7 @@ int tt_gdn_seg_gemm_tma(const SegDesc* h_segs, int seg_first, int seg_count,
                         const SegDesc* d_desc, const int2* d_tiles, int n_tiles, int H,
                         const float* A, long long a_hs, const float* B, long long b_hs, float* C,
                         long long c_hs, float alpha, float beta, const float* Cin, int split,
-                        cudaStream_t st) {
+                        cudaStream_t st, tt::gdn::EpiMask mask) {
   using namespace tt::gdn;
   if (n_tiles <= 0 || H <= 0) return TT_OK;
   if (seg_count > kMaxSegsPerLaunch) return TT_ERR_INVALID_ARG;
@@ -838,11 +887,11 @@ int tt_gdn_seg_gemm_tma(const SegDesc* h_segs, int seg_first, int seg_count,
   if (split == 3)
     seg_gemm_tma<3><<<grid, kThreads, smem, st>>>(mp, seg_first, d_desc, d_tiles, n_tiles, H, A,
                                                    a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
-                                                   epi_flags);
+                                                   epi_flags, mask);
   else
     seg_gemm_tma<1><<<grid, kThreads, smem, st>>>(mp, seg_first, d_desc, d_tiles, n_tiles, H, A,
                                                    a_hs, B, b_hs, C, c_hs, alpha, beta, Cin,
-                                                   epi_flags);
+                                                   epi_flags, mask);
   return cudaGetLastError() == cudaSuccess ? TT_OK : TT_ERR_CUDA;
 }
 
