@@ -424,8 +424,7 @@ def test_token_major_conv_and_in_place_gdn_rows_match_packed(dtype):
     C = 2 * Hk * D + H * D
     info = tt.build_dfs_tree_info(random_branching_tree(23, 1200, 16, 120))
     S = info.N
-    if S % 4:
-        pytest.skip("tree size not a multiple of 4")
+    assert S % 8 == 0 and S % 128      # whole 16-byte token chunks; a partial last tile
     bounds, parents = _tree_arrays(info.chunk_boundaries, info.chunk_parent_map)
     plan = _conv_plan(bounds, parents, K, DEV)
     gen = torch.Generator(device=DEV).manual_seed(5)
@@ -460,3 +459,50 @@ def test_token_major_conv_and_in_place_gdn_rows_match_packed(dtype):
         assert torch.equal(a, b)
     assert torch.equal(tm[4], pk[4]) and torch.equal(tm[5], pk[5])   # dg, dbeta
     assert rel(tm[3].cpu().numpy(), pk[3].cpu().numpy()) < 1e-5       # dw
+
+
+@pytest.mark.parametrize("K,dtype", [(2, torch.bfloat16), (4, torch.float32), (7, torch.bfloat16),
+                                     (7, torch.float32)])
+def test_tree_conv_token_major_kernels_match_channel_major(K, dtype):
+    """The shared-memory-tiled token-major conv kernels (output / output
+    gradient as [S, C] rows) against the channel-major ones on a tree of
+    many short nodes (windows that leave a 128-token tile at node starts) with
+    a partial last tile and a partial last 64-channel tile: out and dx bit for
+    bit, dw and db (summed over other token blocks) to 1e-5."""
+    from tree_training_b200 import _lib
+    from tree_training_b200.gdn import TreeConvPlan, _tree_arrays
+    info = tt.build_dfs_tree_info(random_branching_tree(41, 3000, 2, 40))
+    S, C = info.N, 200
+    assert S % 8 == 0 and S % 128 and C % 64
+    bounds, parents = _tree_arrays(info.chunk_boundaries, info.chunk_parent_map)
+    plan = TreeConvPlan(bounds, parents, K, DEV)
+    g = torch.Generator(device=DEV).manual_seed(K + 100)
+    x = torch.randn(C, S, generator=g, device=DEV).to(dtype)
+    dy = torch.randn(C, S, generator=g, device=DEV).to(dtype)
+    w = torch.randn(C, K, generator=g, device=DEV) * 0.5
+    b = torch.randn(C, generator=g, device=DEV) * 0.1
+    dt = {torch.float32: _lib.TT_F32, torch.bfloat16: _lib.TT_BF16}[dtype]
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+    ws_bytes = int(_lib.lib().tt_tree_conv_bwd_workspace_size(C, S, K))
+
+    def run(tm):
+        out = torch.empty((S, C) if tm else (C, S), dtype=dtype, device=DEV)
+        _lib.call("tt_tree_conv_fwd_ex", dt, C, S, K, x.data_ptr(), w.data_ptr(), b.data_ptr(),
+                  plan.pred.data_ptr(), out.data_ptr(), int(tm), stream)
+        dyl = dy.t().contiguous() if tm else dy
+        dx = torch.empty_like(x)
+        dw = torch.zeros(C, K, device=DEV)
+        db = torch.zeros(C, device=DEV)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=DEV)
+        _lib.call("tt_tree_conv_bwd_ex", dt, C, S, K, x.data_ptr(), w.data_ptr(), b.data_ptr(),
+                  plan.pred.data_ptr(), plan.succ_ptr.data_ptr(), plan.succ_tok.data_ptr(),
+                  plan.succ_lag.data_ptr(), dyl.data_ptr(), int(tm), dx.data_ptr(),
+                  dw.data_ptr(), db.data_ptr(), ws.data_ptr(), ws_bytes, stream)
+        torch.cuda.synchronize()
+        return (out.t() if tm else out), dx, dw, db
+
+    tm, cm = run(True), run(False)
+    assert torch.equal(tm[0], cm[0])
+    assert torch.equal(tm[1], cm[1])
+    for a, r in zip(tm[2:], cm[2:]):
+        assert rel(a.cpu().numpy(), r.cpu().numpy()) < 1e-5

@@ -459,45 +459,82 @@ conv_bwd_dx4(int C, int S, const float* __restrict__ w, const float* __restrict_
 // ---- token-major side ----------------------------------------------------------
 // The conv output and its gradient in token-major memory ([S, C], channel rows
 // contiguous: what the layer's transpose + split into q / k / v reads without a
-// transposing copy).  One block per 64 channels x 128 tokens: warp w computes
-// channels 8w .. 8w+7 of the tile, lane l tokens 4l .. 4l+3 (the loads of x
-// along tokens as in the 4-token kernels), and the tile is transposed through
-// shared memory (channel rows padded by 4 bytes: the column reads of the other
-// side fall in distinct banks), so the token-major side moves whole 128-byte
-// (16-bit) or 256-byte (fp32) channel segments per token.  Needs S % 4 == 0,
-// C % 8 == 0 and 16-byte aligned bases.
-constexpr int kTmCh = 64;                    // channels per tile (8 warps x kConvCh)
-constexpr int kTmTok = 128;                  // tokens per tile (32 lanes x 4)
+// transposing copy).  One block per 64 channels x 128 tokens, 256 threads:
+//   1. 16-byte cp.async copies stage the tile's x rows (channel-major, tokens
+//      [t0 - 8, t0 + 128): the window's predecessors inside the tile) and, in
+//      the backward, the dy rows (token-major, 64 channels) in shared memory;
+//   2. thread (token tt = tid % 128, channel half tid / 128) computes its 32
+//      channels of token t0 + tt from shared memory (a window that leaves the
+//      tile, at a node's first tokens, is read from global memory), with the
+//      same arithmetic per output as the channel-major kernels;
+//   3. the forward writes the token-major tile back as whole 16-byte row
+//      chunks; the backward writes dpre channel-major (consecutive tokens per
+//      warp) and reduces the dw / db partials of each channel over the tile.
+// Needs S * sizeof(T) % 16 == 0, C % 8 == 0 and 16-byte aligned bases.
+constexpr int kTmCh = 64;                    // channels per tile
+constexpr int kTmTok = 128;                  // tokens per tile
 constexpr int kTmThreads = 256;
+constexpr int kTmHalo = 8;                   // staged tokens before the tile (K - 1 <= 7)
 
 template <typename T>
 struct TmTile {
-  static constexpr int kLd = kTmTok + 4 / static_cast<int>(sizeof(T));   // padded row (elements)
-  T v[kTmCh][kLd];
+  static constexpr int kEl = 16 / static_cast<int>(sizeof(T));   // elements per 16 bytes
+  static constexpr int kXW = kTmHalo + kTmTok;                     // staged tokens per x row
+  static constexpr int kTW = kTmCh + kEl;                          // token row (+ one chunk pad)
+  T x[kTmCh][kXW];                       // x[c0 + r][t0 - 8 + i]
+  T tm[kTmTok][kTW];                     // token-major rows: out (fwd) or dy (bwd)
+  float red[kTmThreads / 32][kTmCh / 2][kPartW];   // bwd: per-warp channel partials
 };
 
-// Channels [c0, c0 + 64) x tokens [t0, t0 + 128) of tile `sm` <-> token-major
-// rows: warp w takes tokens t0 + w, t0 + w + 8, ...; lane l channels 2l, 2l+1.
-template <typename T, bool kToGlobal>
-__device__ __forceinline__ void tm_tile_rows(TmTile<T>& sm, T* tm, int C, int S, int c0, int t0) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = c0 + 2 * lane;
-  if (c >= C) return;                        // C % 8 == 0: channel pairs are whole
-  struct alignas(2 * sizeof(T)) Pair {
-    T a, b;
-  };
-  for (int r = warp; r < kTmTok; r += kTmThreads / 32) {
-    const int t = t0 + r;
-    if (t >= S) break;
-    Pair* g = reinterpret_cast<Pair*>(tm + (int64_t)t * C + c);
-    if (kToGlobal) {
-      *g = Pair{sm.v[2 * lane][r], sm.v[2 * lane + 1][r]};
+__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool ok) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src), "r"(ok ? 16u : 0u)
+               : "memory");
+}
+
+// Stage x[c0 .. c0 + 63][t0 - 8 .. t0 + 127] (zero outside [0, S) and past C).
+template <typename T>
+__device__ __forceinline__ void stage_x(TmTile<T>& sm, const T* x, int C, int S, int c0, int t0) {
+  constexpr int kEl = TmTile<T>::kEl, kXC = TmTile<T>::kXW / kEl;
+  for (int q = threadIdx.x; q < kTmCh * kXC; q += kTmThreads) {
+    const int r = q / kXC, k = q % kXC;
+    const int c = c0 + r, t = t0 - kTmHalo + k * kEl;   // chunks are whole: S % kEl == 0
+    const bool ok = c < C && t >= 0 && t < S;
+    cp_async16_zfill(&sm.x[r][k * kEl], ok ? x + (int64_t)c * S + t : x, ok);
+  }
+}
+
+// The window of token t (tile token tt) in tile channel r: xs[m] = x[c][pred_m(t)].
+template <typename T, int K>
+__device__ __forceinline__ void tile_window(const TmTile<T>& sm, const T* x, int S, int c, int r,
+                                            int t0, int tt, bool plain,
+                                            const int (&pr)[K > 1 ? K - 1 : 1], float (&xs)[K]) {
+  xs[0] = to_f32(sm.x[r][kTmHalo + tt]);
+#pragma unroll
+  for (int m = 1; m < K; ++m) {
+    if (plain) {
+      xs[m] = to_f32(sm.x[r][kTmHalo + tt - m]);
     } else {
-      const Pair p = *g;
-      sm.v[2 * lane][r] = p.a;
-      sm.v[2 * lane + 1][r] = p.b;
+      const int p = pr[m - 1];
+      xs[m] = p < 0 ? 0.f
+              : (p >= t0 - kTmHalo && p < t0 + kTmTok) ? to_f32(sm.x[r][p - t0 + kTmHalo])
+                                                       : to_f32(x[(int64_t)c * S + p]);
     }
   }
+}
+
+template <int K>
+__device__ __forceinline__ bool tile_pred(const int32_t* __restrict__ pred, int t, bool live,
+                                          int (&pr)[K > 1 ? K - 1 : 1]) {
+  pr[0] = -1;
+  bool plain = true;
+#pragma unroll
+  for (int m = 0; m < K - 1; ++m) {
+    pr[m] = live ? pred[(int64_t)t * (K - 1) + m] : -1;
+    plain &= pr[m] == t - 1 - m;
+  }
+  return plain;
 }
 
 template <typename T, int K>
@@ -505,90 +542,113 @@ __global__ void __launch_bounds__(kTmThreads)
 conv_fwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
             const float* __restrict__ bias, const int32_t* __restrict__ pred,
             T* __restrict__ out_tm) {
-  __shared__ TmTile<T> sm;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cb = blockIdx.y * kTmCh, tb = blockIdx.x * kTmTok;
-  const int c0 = cb + warp * kConvCh, t0 = tb + lane * 4;
-  if (t0 < S && c0 < C) {
-    int pr[4][K > 1 ? K - 1 : 1];
-    const bool plain = load_pred4<K>(pred, t0, pr);
+  extern __shared__ __align__(16) uint8_t tm_smem[];
+  TmTile<T>& sm = *reinterpret_cast<TmTile<T>*>(tm_smem);
+  constexpr int kEl = TmTile<T>::kEl;
+  const int c0 = blockIdx.y * kTmCh, t0 = blockIdx.x * kTmTok;
+  stage_x<T>(sm, x, C, S, c0, t0);
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  const int tt = threadIdx.x & (kTmTok - 1), half = threadIdx.x / kTmTok;
+  const int t = t0 + tt;
+  const bool live = t < S;
+  int pr[K > 1 ? K - 1 : 1];
+  const bool plain = tile_pred<K>(pred, t, live, pr);
+  struct alignas(2 * sizeof(T)) Pair {
+    T a, b;
+  };
 #pragma unroll 1
-    for (int hc = 0; hc < kConvCh; hc += kHalfCh) {
-      float xs[kHalfCh][4][K];
-      load_windows4<T, K>(x, C, S, c0 + hc, t0, plain, pr, xs);
+  for (int cp = 0; cp < kTmCh / 2; cp += 2) {
+    const int r = half * (kTmCh / 2) + cp;
+    float o[2] = {0.f, 0.f};
 #pragma unroll
-      for (int cc = 0; cc < kHalfCh; ++cc) {
-        const int c = min(c0 + hc + cc, C - 1);
-        const float* wc = w + (int64_t)c * K;
+    for (int e = 0; e < 2; ++e) {
+      const int c = min(c0 + r + e, C - 1);
+      float xs[K];
+      tile_window<T, K>(sm, x, S, c, r + e, t0, tt, plain, pr, xs);
+      const float* wc = w + (int64_t)c * K;
+      float pre = bias ? bias[c] : 0.f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float pre = bias ? bias[c] : 0.f;
-#pragma unroll
-          for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[cc][i][m], pre);
-          sm.v[warp * kConvCh + hc + cc][lane * 4 + i] = from_f32<T>(silu(pre));
-        }
-      }
+      for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[m], pre);
+      o[e] = silu(pre);
     }
+    *reinterpret_cast<Pair*>(&sm.tm[tt][r]) = Pair{from_f32<T>(o[0]), from_f32<T>(o[1])};
   }
   __syncthreads();
-  tm_tile_rows<T, true>(sm, out_tm, C, S, cb, tb);
+  constexpr int kTC = kTmCh / kEl;               // 16-byte chunks per token row
+  for (int q = threadIdx.x; q < kTmTok * kTC; q += kTmThreads) {
+    const int rr = q / kTC, k = q % kTC;
+    const int tq = t0 + rr, c = c0 + k * kEl;
+    if (tq < S && c < C)
+      *reinterpret_cast<uint4*>(out_tm + (int64_t)tq * C + c) =
+          *reinterpret_cast<const uint4*>(&sm.tm[rr][k * kEl]);
+  }
 }
 
 // dpre (channel-major fp32) from x (channel-major) and dy (token-major), and
-// per (channel, 128-token block) the dw / db partials.  Each warp owns its 8
-// channels, so a partial is one warp sum, written by lane 0.
+// per (channel, 128-token block) the dw / db partials (each warp sums its 32
+// tokens by shuffles, then the 4 warps of a channel half add up in a fixed
+// order).
 template <typename T, int K>
 __global__ void __launch_bounds__(kTmThreads)
 conv_bwd_dpre_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
                  const float* __restrict__ bias, const int32_t* __restrict__ pred,
                  const T* __restrict__ dy_tm, float* __restrict__ dpre, float* __restrict__ part,
                  int nb) {
-  __shared__ TmTile<T> sm;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cb = blockIdx.y * kTmCh, tb = blockIdx.x * kTmTok;
-  const int c0 = cb + warp * kConvCh, t0 = tb + lane * 4;
-  tm_tile_rows<T, false>(sm, const_cast<T*>(dy_tm), C, S, cb, tb);
+  extern __shared__ __align__(16) uint8_t tm_smem[];
+  TmTile<T>& sm = *reinterpret_cast<TmTile<T>*>(tm_smem);
+  constexpr int kEl = TmTile<T>::kEl, kTC = kTmCh / kEl;
+  const int c0 = blockIdx.y * kTmCh, t0 = blockIdx.x * kTmTok;
+  stage_x<T>(sm, x, C, S, c0, t0);
+  for (int q = threadIdx.x; q < kTmTok * kTC; q += kTmThreads) {
+    const int rr = q / kTC, k = q % kTC;
+    const int tq = t0 + rr, c = c0 + k * kEl;
+    const bool ok = tq < S && c < C;
+    cp_async16_zfill(&sm.tm[rr][k * kEl], ok ? dy_tm + (int64_t)tq * C + c : dy_tm, ok);
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  if (c0 >= C) return;                       // whole warps: no block-wide syncs below
-  const bool live = t0 < S;                  // S % 4 == 0: a live group is whole
-  const int tl = live ? t0 : 0;
-  int pr[4][K > 1 ? K - 1 : 1];
-  const bool plain = load_pred4<K>(pred, tl, pr);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tt = threadIdx.x & (kTmTok - 1), half = threadIdx.x / kTmTok;
+  const int t = t0 + tt;
+  const bool live = t < S;
+  int pr[K > 1 ? K - 1 : 1];
+  const bool plain = tile_pred<K>(pred, t, live, pr);
 #pragma unroll 1
-  for (int hc = 0; hc < kConvCh; hc += kHalfCh) {
-    float xs[kHalfCh][4][K];
-    load_windows4<T, K>(x, C, S, c0 + hc, tl, plain, pr, xs);
+  for (int cl = 0; cl < kTmCh / 2; ++cl) {
+    const int r = half * (kTmCh / 2) + cl;
+    const int c = min(c0 + r, C - 1);
+    float xs[K];
+    tile_window<T, K>(sm, x, S, c, r, t0, tt, plain, pr, xs);
+    const float* wc = w + (int64_t)c * K;
+    float pre = bias ? bias[c] : 0.f;
 #pragma unroll
-    for (int cc = 0; cc < kHalfCh; ++cc) {
-      const int c = c0 + hc + cc;
-      if (c >= C) break;                     // the same for the whole warp
-      const float* wc = w + (int64_t)c * K;
-      float d[4];
+    for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[m], pre);
+    const float sg = 1.f / (1.f + __expf(-pre));
+    const float g = to_f32(sm.tm[tt][r]);
+    const float d = live ? g * sg * (1.f + pre * (1.f - sg)) : 0.f;
+    if (live && c0 + r < C) dpre[(int64_t)(c0 + r) * S + t] = d;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float pre = bias ? bias[c] : 0.f;
+    for (int j = 0; j < kPartW; ++j) {
+      float v = 0.f;
+      if (j < K || j == 8) {
+        v = j == 8 ? d : d * xs[j < K ? K - 1 - j : 0];
 #pragma unroll
-        for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[cc][i][m], pre);
-        const float sg = 1.f / (1.f + __expf(-pre));
-        const float g = live ? to_f32(sm.v[warp * kConvCh + hc + cc][lane * 4 + i]) : 0.f;
-        d[i] = live ? g * sg * (1.f + pre * (1.f - sg)) : 0.f;
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       }
-      if (live)
-        *reinterpret_cast<float4*>(dpre + (int64_t)c * S + t0) =
-            make_float4(d[0], d[1], d[2], d[3]);
-#pragma unroll
-      for (int j = 0; j < kPartW; ++j) {
-        float v = 0.f;
-        if (j < K || j == 8) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            v += j == 8 ? d[i] : d[i] * xs[cc][i][j < K ? K - 1 - j : 0];
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        }
-        if (lane == 0) part[((int64_t)c * nb + blockIdx.x) * kPartW + j] = v;
-      }
+      if (lane == 0) sm.red[warp][cl][j] = v;
     }
+  }
+  __syncthreads();
+  constexpr int kWarpsPerHalf = kTmTok / 32;
+  for (int i = threadIdx.x; i < kTmCh * kPartW; i += kTmThreads) {
+    const int r = i / kPartW, j = i % kPartW;
+    if (c0 + r >= C) continue;
+    const int hf = r / (kTmCh / 2), cl = r % (kTmCh / 2);
+    float v = 0.f;
+#pragma unroll
+    for (int q = 0; q < kWarpsPerHalf; ++q) v += sm.red[hf * kWarpsPerHalf + q][cl][j];
+    part[((int64_t)(c0 + r) * nb + blockIdx.x) * kPartW + j] = v;
   }
 }
 
@@ -627,8 +687,20 @@ int by_dtype(int dtype, Fn fn) {
 }  // namespace tt
 
 namespace {
-bool tm_ok(int C, int S, const void* a, const void* b, const void* c) {
-  return C % 8 == 0 && tt::quad_ok(S, a, b, c);
+bool tm_ok(int dtype, int C, int S, const void* a, const void* b, const void* c) {
+  const int el = dtype == TT_F32 ? 4 : 8;   // elements per 16 bytes
+  return C % 8 == 0 && S % el == 0 && tt::quad_ok(S, a, b, c);
+}
+
+// Launch a token-major tile kernel with its dynamic shared memory.
+template <typename T, typename Kern, typename... Args>
+int launch_tm(Kern kern, dim3 grid, cudaStream_t st, Args... args) {
+  const int bytes = (int)sizeof(tt::TmTile<T>);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess)
+    return TT_ERR_CUDA;
+  kern<<<grid, tt::kTmThreads, bytes, st>>>(args...);
+  return cudaGetLastError() == cudaSuccess ? (int)TT_OK : (int)TT_ERR_CUDA;
 }
 }  // namespace
 
@@ -638,17 +710,16 @@ extern "C" int tt_tree_conv_fwd_ex(int dtype, int32_t C, int32_t S, int32_t K, c
   if (C < 0 || S < 0 || K < 1 || K > 8) return TT_ERR_INVALID_ARG;
   if (C == 0 || S == 0) return TT_OK;
   if (!x || !weight || !out || (K > 1 && !pred)) return TT_ERR_INVALID_ARG;
-  if (out_token_major && !tm_ok(C, S, x, out, out)) return TT_ERR_UNSUPPORTED;
+  if (out_token_major && !tm_ok(dtype, C, S, x, out, out)) return TT_ERR_UNSUPPORTED;
   return tt::by_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     return tt::by_k(K, [&](auto kc) {
       constexpr int KK = decltype(kc)::value;
       if (out_token_major) {
         dim3 g((S + tt::kTmTok - 1) / tt::kTmTok, (C + tt::kTmCh - 1) / tt::kTmCh);
-        tt::conv_fwd_tm<T, KK><<<g, tt::kTmThreads, 0, (cudaStream_t)stream>>>(
-            C, S, (const T*)x, weight, bias, pred, (T*)out);
         tt_count_launches(1);
-        return cudaGetLastError() == cudaSuccess ? (int)TT_OK : (int)TT_ERR_CUDA;
+        return launch_tm<T>(tt::conv_fwd_tm<T, KK>, g, (cudaStream_t)stream, C, S, (const T*)x,
+                            weight, bias, pred, (T*)out);
       }
       dim3 g((S + tt::kConvTok - 1) / tt::kConvTok, (C + tt::kConvCh - 1) / tt::kConvCh);
       tt::conv_fwd<T, KK><<<g, tt::kConvTok, 0, (cudaStream_t)stream>>>(
@@ -686,7 +757,7 @@ extern "C" int tt_tree_conv_bwd_ex(int dtype, int32_t C, int32_t S, int32_t K, c
     return TT_ERR_INVALID_ARG;
   if (!workspace || workspace_bytes < tt_tree_conv_bwd_workspace_size(C, S, K))
     return TT_ERR_WORKSPACE;
-  if (dout_token_major && !(tm_ok(C, S, x, dout, dx) &&
+  if (dout_token_major && !(tm_ok(dtype, C, S, x, dout, dx) &&
                             (reinterpret_cast<uintptr_t>(workspace) & 15) == 0))
     return TT_ERR_UNSUPPORTED;
   return tt::by_dtype(dtype, [&](auto tag) {
@@ -702,11 +773,13 @@ extern "C" int tt_tree_conv_bwd_ex(int dtype, int32_t C, int32_t S, int32_t K, c
       // the 4-token kernels also move dpre by 16 bytes
       const bool q4 = tt::quad_ok(S, x, dout, dx) &&
                       (reinterpret_cast<uintptr_t>(workspace) & 15) == 0;
-      if (dout_token_major)
-        tt::conv_bwd_dpre_tm<T, KK><<<dim3(nb, (C + tt::kTmCh - 1) / tt::kTmCh), tt::kTmThreads,
-                                      0, st>>>(C, S, (const T*)x, weight, bias, pred,
-                                               (const T*)dout, dpre, part, nb);
-      else if (q4)
+      if (dout_token_major) {
+        const int rc = launch_tm<T>(tt::conv_bwd_dpre_tm<T, KK>,
+                                    dim3(nb, (C + tt::kTmCh - 1) / tt::kTmCh), st, C, S,
+                                    (const T*)x, weight, bias, pred, (const T*)dout, dpre, part,
+                                    nb);
+        if (rc != TT_OK) return rc;
+      } else if (q4)
         tt::conv_bwd_dpre4<T, KK><<<g, tt::kConvThr4, 0, st>>>(
             C, S, (const T*)x, weight, bias, pred, (const T*)dout, dpre, part, nb);
       else

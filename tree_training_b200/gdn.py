@@ -301,11 +301,18 @@ def _conv_plan(bounds: torch.Tensor, parents: torch.Tensor, K: int, device) -> T
     return plan
 
 
+def _tm_sizes_ok(C: int, S: int, dtype: torch.dtype) -> bool:
+    """Sizes the token-major conv kernels take: C % 8 == 0 and whole 16-byte
+    chunks of tokens per channel row (S * element size % 16 == 0)."""
+    el = torch.empty((), dtype=dtype).element_size()
+    return C % 8 == 0 and (S * el) % 16 == 0
+
+
 def _token_major_ok(t: torch.Tensor) -> bool:
-    """t [C, S] held token-major (strides (1, C)) with the alignment the
-    token-major conv kernels need (S % 4 == 0, C % 8 == 0, 16-byte base)."""
+    """t [C, S] held token-major (strides (1, C)) with the sizes and 16-byte
+    base the token-major conv kernels need."""
     C, S = t.shape
-    return (t.stride() == (1, C) and C % 8 == 0 and S % 4 == 0 and t.data_ptr() % 16 == 0)
+    return t.stride() == (1, C) and _tm_sizes_ok(C, S, t.dtype) and t.data_ptr() % 16 == 0
 
 
 def _conv_out(x: torch.Tensor, token_major: bool) -> torch.Tensor:
@@ -395,7 +402,7 @@ def tree_conv(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor
     outs = []
     for i in range(x.shape[0]):
         xi = x[i].contiguous()
-        tm = (x.shape[0] == 1 and xi.shape[0] % 8 == 0 and xi.shape[1] % 4 == 0
+        tm = (x.shape[0] == 1 and _tm_sizes_ok(xi.shape[0], xi.shape[1], xi.dtype)
               and xi.data_ptr() % 16 == 0)
         outs.append(_conv_fwd_op(xi, w, b, has_b, plan.pred, plan.succ_ptr, plan.succ_tok,
                                  plan.succ_lag, tm))
