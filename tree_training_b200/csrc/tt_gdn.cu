@@ -25,6 +25,7 @@
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <type_traits>
 #include <vector>
 
@@ -585,6 +586,74 @@ __global__ void dinit_kernel(int H, int DkDv, int n_roots, const int* __restrict
 // host orchestration
 // =============================================================================
 
+// A call's metadata (plan arrays, GEMM descriptors and tile lists: one
+// contiguous span of the workspace) travels host -> device through a pinned
+// staging buffer that a copy kernel reads in stream order.  No pageable copy
+// (which can make the host wait for the stream) and no copy-engine queue (in
+// which it would wait behind a large upload the caller has in flight on
+// another stream).  Two buffers per device alternate; one is refilled only
+// after the copy kernel that read it has run.
+struct MetaStage {
+  char* host = nullptr;
+  size_t cap = 0;
+  cudaEvent_t read = nullptr;   // recorded after the copy kernel that read `host`
+  bool pending = false;
+};
+constexpr int kStageDevs = 64;
+MetaStage g_stage[kStageDevs][2];
+int g_stage_next[kStageDevs];
+std::mutex g_stage_mu;
+
+__global__ void copy_from_host(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                               long long n16) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n16;
+       i += (long long)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
+struct MetaPiece {
+  void* dst;
+  const void* src;
+  size_t bytes;
+};
+
+// Copies every piece (device destinations inside [span, span + span_bytes),
+// span and span_bytes multiples of 16) through a staging buffer.
+int upload_meta(char* span, size_t span_bytes, const std::vector<MetaPiece>& pieces,
+                cudaStream_t st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kStageDevs) return TT_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_stage_mu);
+  MetaStage& m = g_stage[dev][g_stage_next[dev]];
+  g_stage_next[dev] ^= 1;
+  if (m.pending && cudaEventSynchronize(m.read) != cudaSuccess) return TT_ERR_CUDA;
+  m.pending = false;
+  if (m.cap < span_bytes) {
+    if (m.host) cudaFreeHost(m.host);
+    m.host = nullptr;
+    m.cap = 0;
+    const size_t cap = span_bytes + span_bytes / 2 + 4096;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&m.host), cap,
+                      cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess)
+      return TT_ERR_CUDA;
+    m.cap = cap;
+  }
+  if (!m.read && cudaEventCreateWithFlags(&m.read, cudaEventDisableTiming) != cudaSuccess)
+    return TT_ERR_CUDA;
+  for (const MetaPiece& pc : pieces)
+    if (pc.bytes) std::memcpy(m.host + (static_cast<char*>(pc.dst) - span), pc.src, pc.bytes);
+  void* src_dev = nullptr;
+  if (cudaHostGetDevicePointer(&src_dev, m.host, 0) != cudaSuccess) return TT_ERR_CUDA;
+  const long long n16 = (long long)(span_bytes / 16);
+  const int blocks = (int)std::min<long long>((n16 + 255) / 256, 512);
+  copy_from_host<<<std::max(blocks, 1), 256, 0, st>>>(static_cast<const uint4*>(src_dev),
+                                                      reinterpret_cast<uint4*>(span), n16);
+  if (cudaGetLastError() != cudaSuccess || cudaEventRecord(m.read, st) != cudaSuccess)
+    return TT_ERR_CUDA;
+  m.pending = true;
+  return TT_OK;
+}
+
 struct Plan {
   int S, H, Hk, Dk, Dv, n;
   // elements from one token's q / k / v row to the next (0: packed rows of
@@ -1000,29 +1069,32 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   b.d_cap_slot = ar.get<int>(n);
   if (ar.sizing) return TT_OK;
   if (ar.used > ar.cap) return TT_ERR_WORKSPACE;
-  auto h2d = [&](void* dst, const void* src, size_t bytes) -> int {
-    if (bytes == 0) return TT_OK;
-    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, st) == cudaSuccess ? TT_OK
-                                                                                        : TT_ERR_CUDA;
-  };
-  int rc = TT_OK;
-  rc |= h2d(b.d_tok_node, p.tok_node.data(), (size_t)S * 4);
-  rc |= h2d(b.d_start, p.start.data(), n * 4);
-  rc |= h2d(b.d_len, p.len.data(), n * 4);
-  rc |= h2d(b.d_parent, p.parent.data(), n * 4);
-  rc |= h2d(b.d_child_ptr, p.child_ptr.data(), (n + 1) * 4);
-  rc |= h2d(b.d_child_idx, p.child_idx.data(), p.child_idx.size() * 4);
-  rc |= h2d(b.d_roots, p.roots.data(), p.roots.size() * 4);
-  rc |= h2d(b.d_level_nodes, level_nodes.data(), level_nodes.size() * 4);
-  rc |= h2d(b.d_loff, p.loff.data(), n * 8);
-  rc |= h2d(b.d_desc, bd.all.data(), bd.all.size() * sizeof(SegDesc));
-  rc |= h2d(b.d_tiles, bd.tiles.data(), bd.tiles.size() * sizeof(int2));
-  rc |= h2d(b.d_tiles_tc, bd.tiles_tc.data(), bd.tiles_tc.size() * sizeof(int2));
-  if (exact) rc |= h2d(b.d_inv_blocks, inv_blocks.data(), inv_blocks.size() * sizeof(int2));
   std::vector<int> cap_slot(n, -1);
   for (int i = 0; i < n_cap; ++i) cap_slot[cap_nodes[i]] = i;
-  if (backward && dcaptured) rc |= h2d(b.d_cap_slot, cap_slot.data(), n * 4);
-  if (rc != TT_OK) return TT_ERR_CUDA;
+  {
+    // the metadata pieces are consecutive arena allocations: one span
+    char* span = reinterpret_cast<char*>(b.d_tok_node);
+    const size_t span_bytes =
+        (size_t)(reinterpret_cast<char*>(b.d_cap_slot) + (((size_t)n * 4 + 255) / 256) * 256 -
+                 span);
+    const std::vector<MetaPiece> pieces = {
+        {b.d_tok_node, p.tok_node.data(), (size_t)S * 4},
+        {b.d_start, p.start.data(), (size_t)n * 4},
+        {b.d_len, p.len.data(), (size_t)n * 4},
+        {b.d_parent, p.parent.data(), (size_t)n * 4},
+        {b.d_child_ptr, p.child_ptr.data(), (size_t)(n + 1) * 4},
+        {b.d_child_idx, p.child_idx.data(), p.child_idx.size() * 4},
+        {b.d_roots, p.roots.data(), p.roots.size() * 4},
+        {b.d_level_nodes, level_nodes.data(), level_nodes.size() * 4},
+        {b.d_loff, p.loff.data(), (size_t)n * 8},
+        {b.d_desc, bd.all.data(), bd.all.size() * sizeof(SegDesc)},
+        {b.d_tiles, bd.tiles.data(), bd.tiles.size() * sizeof(int2)},
+        {b.d_tiles_tc, bd.tiles_tc.data(), bd.tiles_tc.size() * sizeof(int2)},
+        {b.d_inv_blocks, inv_blocks.data(), inv_blocks.size() * sizeof(int2)},
+        {b.d_cap_slot, cap_slot.data(), (size_t)n * 4}};
+    const int rc = upload_meta(span, span_bytes, pieces, st);
+    if (rc != TT_OK) return rc;
+  }
 
   const float q_scale = 1.f / sqrtf((float)Dk);
   const int mode = gemm_mode();
@@ -1034,7 +1106,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   // overwrites it with T)
   const bool fuse_mask = gc.split != 0 && gc.tma && !exact;
   auto blocks = [](long long nel) { return (unsigned)((nel + 255) / 256); };
-  int launches = 0;
+  int launches = 1;   // the metadata copy
   // ---------------------------------------------------------------- forward
   // (skipped when the workspace still holds this pass from tt_gdn_tree_fwd)
   if (!reuse) {
