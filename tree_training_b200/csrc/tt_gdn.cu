@@ -416,6 +416,61 @@ __global__ void grad_masks(int S, const int* __restrict__ nstart, const int* __r
 // so every read of the node's matrix is a coalesced row segment.  The two
 // sums cancel to a small difference: both accumulate in fp64.
 constexpr int kRowColThreads = 256;
+// grad_masks and ddd_rowcol in one pass per (node, head), without writing
+// dDD: warp w takes rows j = w, w + 8, ...; for each element of its row it
+// forms G, F (written back over dA, dAqk, the whole row as grad_masks does)
+// and dDD[j, m] in registers, sums the row (fp64, lanes then shuffles, as
+// ddd_rowcol) and adds the value to its own fp64 column partial in shared
+// memory.  After all rows the 8 warps' partials of each column are added in
+// warp order and dgam_m += rowsum_m - colsum_m.  Shared memory: 9 x L doubles
+// (the launch takes nodes up to kFusedMaskMaxL tokens).
+constexpr int kFusedMaskMaxL = 2048;
+__global__ void __launch_bounds__(kRowColThreads)
+grad_masks_rowcol(int S, const int* __restrict__ nstart, const int* __restrict__ nlen,
+                  const long long* __restrict__ loff, long long l_hs,
+                  const float* __restrict__ gam, const float* __restrict__ KK,
+                  const float* __restrict__ QK, int premasked, float* dA, float* dAqk,
+                  float* dgam) {
+  extern __shared__ double gm_smem[];
+  constexpr int kW = kRowColThreads / 32;
+  const int c = blockIdx.x, h = blockIdx.y;
+  const int L = nlen[c], Lp = row_stride(L), s0 = nstart[c];
+  double* colp = gm_smem;               // [kW][L]
+  double* rs = gm_smem + kW * L;        // [L]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kW * L; i += kRowColThreads) colp[i] = 0.0;
+  __syncthreads();
+  const float* g = gam + (long long)h * S + s0;
+  const long long nb = h * l_hs + loff[c];
+  for (int j = warp; j < L; j += kW) {
+    const long long base = nb + (long long)j * Lp;
+    const float gj = g[j];
+    double a = 0.0;
+    for (int m = lane; m < L; m += 32) {
+      const float d = m <= j ? expf(gj - g[m]) : 0.f;
+      const float da = m < j ? dA[base + m] : 0.f;
+      const float dq = m <= j ? dAqk[base + m] : 0.f;
+      const float v = premasked ? da * KK[base + m] + dq * QK[base + m]
+                                : (-da * KK[base + m] + dq * QK[base + m]) * d;
+      dA[base + m] = -da * d;      // G
+      dAqk[base + m] = dq * d;     // F
+      if (m <= j) {
+        a += (double)v;
+        colp[warp * L + m] += (double)v;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) rs[j] = a;
+  }
+  __syncthreads();
+  for (int m = threadIdx.x; m < L; m += kRowColThreads) {
+    double col = 0.0;
+#pragma unroll
+    for (int w = 0; w < kW; ++w) col += colp[w * L + m];
+    dgam[(long long)h * S + s0 + m] += (float)(rs[m] - col);
+  }
+}
+
 __global__ void __launch_bounds__(kRowColThreads)
 ddd_rowcol(int S, const int* __restrict__ nstart, const int* __restrict__ nlen,
            const long long* __restrict__ loff, long long l_hs, const float* __restrict__ dDD,
@@ -1228,13 +1283,25 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   }
   // masks: dA -> G = -dA*D, dAqk -> F = dAqk*D, dDD
   TT_CUDA_OK(cudaMemsetAsync(b.dgam, 0, (size_t)H * S * 4, st));
-  grad_masks<<<dim3(S, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_tok_node, b.d_loff, llh,
-                                            b.gam, fuse_mask ? b.Am : b.KK,
-                                            fuse_mask ? b.Aqk : b.QK, fuse_mask ? 1 : 0, b.dA,
-                                            b.dAqk, b.dDD);
-  ddd_rowcol<<<dim3(n, H), kRowColThreads, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh,
-                                                     b.dDD, b.rowsum, b.dgam);
-  launches += 2;
+  if (p.max_len <= kFusedMaskMaxL) {
+    // one pass: G, F and the row / column sums of dDD without storing it
+    const size_t smem = (size_t)(kRowColThreads / 32 + 1) * std::max(p.max_len, 1) * 8;
+    if (smem > 48 * 1024)
+      TT_CUDA_OK(cudaFuncSetAttribute(grad_masks_rowcol,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    grad_masks_rowcol<<<dim3(n, H), kRowColThreads, smem, st>>>(
+        S, b.d_start, b.d_len, b.d_loff, llh, b.gam, fuse_mask ? b.Am : b.KK,
+        fuse_mask ? b.Aqk : b.QK, fuse_mask ? 1 : 0, b.dA, b.dAqk, b.dgam);
+    launches += 1;
+  } else {
+    grad_masks<<<dim3(S, H), 128, 0, st>>>(S, b.d_start, b.d_len, b.d_tok_node, b.d_loff, llh,
+                                              b.gam, fuse_mask ? b.Am : b.KK,
+                                              fuse_mask ? b.Aqk : b.QK, fuse_mask ? 1 : 0, b.dA,
+                                              b.dAqk, b.dDD);
+    ddd_rowcol<<<dim3(n, H), kRowColThreads, 0, st>>>(S, b.d_start, b.d_len, b.d_loff, llh,
+                                                       b.dDD, b.rowsum, b.dgam);
+    launches += 2;
+  }
   // dKb = G K ; dK = G^T Kb + F^T Q ; dQ = F K
   launch_gemm(gc, ds_gk, H, b.dA, llh, b.K, vk, b.dKb, vk, 1.f, 0.f, st);
   launch_gemm(gc, ds_gtk, H, b.dA, llh, b.Kb, vk, b.dK, vk, 1.f, 0.f, st);
