@@ -463,10 +463,12 @@ conv_bwd_dx4(int C, int S, const float* __restrict__ w, const float* __restrict_
 //   1. 16-byte cp.async copies stage the tile's x rows (channel-major, tokens
 //      [t0 - 8, t0 + 128): the window's predecessors inside the tile) and, in
 //      the backward, the dy rows (token-major, 64 channels) in shared memory;
-//   2. thread (token tt = tid % 128, channel half tid / 128) computes its 32
-//      channels of token t0 + tt from shared memory (a window that leaves the
-//      tile, at a node's first tokens, is read from global memory), with the
-//      same arithmetic per output as the channel-major kernels;
+//   2. the forward's thread (token tt = tid % 128, channel half tid / 128)
+//      computes its 32 channels of token t0 + tt, the backward's warp w
+//      channels 8w .. 8w + 7 of tokens t0 + lane + 32 i, from shared memory
+//      (a window that leaves the tile, at a node's first tokens, is read from
+//      global memory), with the same arithmetic per output as the
+//      channel-major kernels;
 //   3. the forward writes the token-major tile back as whole 16-byte row
 //      chunks; the backward writes dpre channel-major (consecutive tokens per
 //      warp) and reduces the dw / db partials of each channel over the tile.
@@ -483,7 +485,6 @@ struct TmTile {
   static constexpr int kTW = kTmCh + kEl;                          // token row (+ one chunk pad)
   T x[kTmCh][kXW];                       // x[c0 + r][t0 - 8 + i]
   T tm[kTmTok][kTW];                     // token-major rows: out (fwd) or dy (bwd)
-  float red[kTmThreads / 32][kTmCh / 2][kPartW];   // bwd: per-warp channel partials
 };
 
 __device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool ok) {
@@ -586,11 +587,11 @@ conv_fwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
 }
 
 // dpre (channel-major fp32) from x (channel-major) and dy (token-major), and
-// per (channel, 128-token block) the dw / db partials (each warp sums its 32
-// tokens by shuffles, then the 4 warps of a channel half add up in a fixed
-// order).
+// per (channel, 128-token block) the dw / db partials: a channel's 128 tokens
+// are in one warp, each thread adds its 4 tokens' terms and one shuffle
+// reduction per term finishes the partial.
 template <typename T, int K>
-__global__ void __launch_bounds__(kTmThreads)
+__global__ void __launch_bounds__(kTmThreads, 3)
 conv_bwd_dpre_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
                  const float* __restrict__ bias, const int32_t* __restrict__ pred,
                  const T* __restrict__ dy_tm, float* __restrict__ dpre, float* __restrict__ part,
@@ -608,47 +609,55 @@ conv_bwd_dpre_tm(int C, int S, const T* __restrict__ x, const float* __restrict_
   }
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
   __syncthreads();
+  // warp w: channels 8w .. 8w + 7; lane l: tokens t0 + l + 32 i (i < 4), so a
+  // channel's 128 tokens sit in one warp: each thread adds its 4 tokens'
+  // terms, one shuffle reduction per (channel, term), lane 0 writes the partial
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tt = threadIdx.x & (kTmTok - 1), half = threadIdx.x / kTmTok;
-  const int t = t0 + tt;
-  const bool live = t < S;
-  int pr[K > 1 ? K - 1 : 1];
-  const bool plain = tile_pred<K>(pred, t, live, pr);
-#pragma unroll 1
-  for (int cl = 0; cl < kTmCh / 2; ++cl) {
-    const int r = half * (kTmCh / 2) + cl;
-    const int c = min(c0 + r, C - 1);
-    float xs[K];
-    tile_window<T, K>(sm, x, S, c, r, t0, tt, plain, pr, xs);
-    const float* wc = w + (int64_t)c * K;
-    float pre = bias ? bias[c] : 0.f;
+  constexpr int kTokPerLane = kTmTok / 32, kChPerWarp = kTmCh / (kTmThreads / 32);
+  int pr[kTokPerLane][K > 1 ? K - 1 : 1];
+  bool plain[kTokPerLane], live[kTokPerLane];
 #pragma unroll
-    for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[m], pre);
-    const float sg = 1.f / (1.f + __expf(-pre));
-    const float g = to_f32(sm.tm[tt][r]);
-    const float d = live ? g * sg * (1.f + pre * (1.f - sg)) : 0.f;
-    if (live && c0 + r < C) dpre[(int64_t)(c0 + r) * S + t] = d;
+  for (int i = 0; i < kTokPerLane; ++i) {
+    const int t = t0 + lane + 32 * i;
+    live[i] = t < S;
+    plain[i] = tile_pred<K>(pred, t, live[i], pr[i]);
+  }
+#pragma unroll 1
+  for (int cl = 0; cl < kChPerWarp; ++cl) {
+    const int r = warp * kChPerWarp + cl;
+    if (c0 + r >= C) break;                          // the same for the whole warp
+    const int c = c0 + r;
+    const float* wc = w + (int64_t)c * K;
+    const float b0 = bias ? bias[c] : 0.f;
+    float acc[kPartW];
+#pragma unroll
+    for (int j = 0; j < kPartW; ++j) acc[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kTokPerLane; ++i) {
+      const int tt = lane + 32 * i, t = t0 + tt;
+      float xs[K];
+      tile_window<T, K>(sm, x, S, c, r, t0, tt, plain[i], pr[i], xs);
+      float pre = b0;
+#pragma unroll
+      for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[m], pre);
+      const float sg = 1.f / (1.f + __expf(-pre));
+      const float g = to_f32(sm.tm[tt][r]);
+      const float d = live[i] ? g * sg * (1.f + pre * (1.f - sg)) : 0.f;
+      if (live[i]) dpre[(int64_t)c * S + t] = d;
+#pragma unroll
+      for (int j = 0; j < K; ++j) acc[j] += d * xs[K - 1 - j];
+      acc[8] += d;
+    }
 #pragma unroll
     for (int j = 0; j < kPartW; ++j) {
       float v = 0.f;
       if (j < K || j == 8) {
-        v = j == 8 ? d : d * xs[j < K ? K - 1 - j : 0];
+        v = acc[j];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       }
-      if (lane == 0) sm.red[warp][cl][j] = v;
+      if (lane == 0) part[((int64_t)c * nb + blockIdx.x) * kPartW + j] = v;
     }
-  }
-  __syncthreads();
-  constexpr int kWarpsPerHalf = kTmTok / 32;
-  for (int i = threadIdx.x; i < kTmCh * kPartW; i += kTmThreads) {
-    const int r = i / kPartW, j = i % kPartW;
-    if (c0 + r >= C) continue;
-    const int hf = r / (kTmCh / 2), cl = r % (kTmCh / 2);
-    float v = 0.f;
-#pragma unroll
-    for (int q = 0; q < kWarpsPerHalf; ++q) v += sm.red[hf * kWarpsPerHalf + q][cl][j];
-    part[((int64_t)(c0 + r) * nb + blockIdx.x) * kPartW + j] = v;
   }
 }
 

@@ -1253,7 +1253,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
         b.d_cap_slot, dcaptured, b.dSo);
     launch_gemm(gc, ds_dvn2[d], H, b.Kd, vk, b.dSo, DkDv, b.dVn, vv, 1.f, 1.f, st);
     launch_gemm(gc, ds_dsi2[d], H, b.W, vk, b.dVn, vv, b.dSi, DkDv, -1.f, 1.f, st);
-    dstate_decay<<<dim3(cnt, H), 256, 0, st>>>(H, DkDv, n, b.d_level_nodes + level_first[d],
+    dstate_decay<<<dim3(cnt, H), 1024, 0, st>>>(H, DkDv, n, b.d_level_nodes + level_first[d],
                                                b.d_parent, b.gl, b.states, b.dSo, b.dSi, b.dgl);
     launches += 2;
   }
