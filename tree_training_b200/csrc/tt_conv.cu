@@ -70,7 +70,11 @@ extern "C" int tt_conv_successors(int32_t S, int32_t K, const int32_t* pred, int
 namespace tt {
 namespace {
 
-__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+// SiLU and the logistic sigmoid with the fast exponential and divide (a few
+// ulp; the conv's outputs carry them into 16-bit or fp32 values checked at
+// 1e-5 against the float64 oracle)
+__device__ __forceinline__ float sigm(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
 constexpr int kConvTok = 256;   // tokens per block (one per thread)
 constexpr int kConvCh = 8;      // channels per thread: the token's predecessor and
@@ -156,7 +160,7 @@ conv_bwd_dpre(int C, int S, const T* __restrict__ x, const float* __restrict__ w
     float pre = bias ? bias[c] : 0.f;
 #pragma unroll
     for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[cc][m], pre);
-    const float sg = 1.f / (1.f + __expf(-pre));
+    const float sg = sigm(pre);
     const float d = live ? g[cc] * sg * (1.f + pre * (1.f - sg)) : 0.f;
     if (live) dpre[(int64_t)c * S + t] = d;
 #pragma unroll
@@ -363,7 +367,7 @@ conv_bwd_dpre4(int C, int S, const T* __restrict__ x, const float* __restrict__ 
         float pre = bias ? bias[c] : 0.f;
 #pragma unroll
         for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[cc][i][m], pre);
-        const float sg = 1.f / (1.f + __expf(-pre));
+        const float sg = sigm(pre);
         d[i] = live ? g[cc][i] * sg * (1.f + pre * (1.f - sg)) : 0.f;
       }
       if (live)
@@ -485,7 +489,21 @@ struct TmTile {
   static constexpr int kTW = kTmCh + kEl;                          // token row (+ one chunk pad)
   T x[kTmCh][kXW];                       // x[c0 + r][t0 - 8 + i]
   T tm[kTmTok][kTW];                     // token-major rows: out (fwd) or dy (bwd)
+  float w[kTmCh * 8];                    // the tile's weights, [r][K]
+  float b[kTmCh];                        // and biases (0 without)
 };
+
+// Stage the tile's weights and biases (read by every thread of a channel).
+template <typename T, int K>
+__device__ __forceinline__ void stage_w(TmTile<T>& sm, const float* w, const float* bias, int C,
+                                        int c0) {
+  for (int i = threadIdx.x; i < kTmCh * K; i += kTmThreads) {
+    const int c = c0 + i / K;
+    sm.w[i] = c < C ? w[(int64_t)c0 * K + i] : 0.f;
+  }
+  for (int i = threadIdx.x; i < kTmCh; i += kTmThreads)
+    sm.b[i] = (bias && c0 + i < C) ? bias[c0 + i] : 0.f;
+}
 
 __device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool ok) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
@@ -548,6 +566,7 @@ conv_fwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
   constexpr int kEl = TmTile<T>::kEl;
   const int c0 = blockIdx.y * kTmCh, t0 = blockIdx.x * kTmTok;
   stage_x<T>(sm, x, C, S, c0, t0);
+  stage_w<T, K>(sm, w, bias, C, c0);
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   const int tt = threadIdx.x & (kTmTok - 1), half = threadIdx.x / kTmTok;
@@ -567,8 +586,8 @@ conv_fwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
       const int c = min(c0 + r + e, C - 1);
       float xs[K];
       tile_window<T, K>(sm, x, S, c, r + e, t0, tt, plain, pr, xs);
-      const float* wc = w + (int64_t)c * K;
-      float pre = bias ? bias[c] : 0.f;
+      const float* wc = sm.w + (r + e) * K;
+      float pre = sm.b[r + e];
 #pragma unroll
       for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[m], pre);
       o[e] = silu(pre);
@@ -601,6 +620,7 @@ conv_bwd_dpre_tm(int C, int S, const T* __restrict__ x, const float* __restrict_
   constexpr int kEl = TmTile<T>::kEl, kTC = kTmCh / kEl;
   const int c0 = blockIdx.y * kTmCh, t0 = blockIdx.x * kTmTok;
   stage_x<T>(sm, x, C, S, c0, t0);
+  stage_w<T, K>(sm, w, bias, C, c0);
   for (int q = threadIdx.x; q < kTmTok * kTC; q += kTmThreads) {
     const int rr = q / kTC, k = q % kTC;
     const int tq = t0 + rr, c = c0 + k * kEl;
@@ -627,8 +647,8 @@ conv_bwd_dpre_tm(int C, int S, const T* __restrict__ x, const float* __restrict_
     const int r = warp * kChPerWarp + cl;
     if (c0 + r >= C) break;                          // the same for the whole warp
     const int c = c0 + r;
-    const float* wc = w + (int64_t)c * K;
-    const float b0 = bias ? bias[c] : 0.f;
+    const float* wc = sm.w + r * K;
+    const float b0 = sm.b[r];
     float acc[kPartW];
 #pragma unroll
     for (int j = 0; j < kPartW; ++j) acc[j] = 0.f;
@@ -640,7 +660,7 @@ conv_bwd_dpre_tm(int C, int S, const T* __restrict__ x, const float* __restrict_
       float pre = b0;
 #pragma unroll
       for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[m], pre);
-      const float sg = 1.f / (1.f + __expf(-pre));
+      const float sg = sigm(pre);
       const float g = to_f32(sm.tm[tt][r]);
       const float d = live[i] ? g * sg * (1.f + pre * (1.f - sg)) : 0.f;
       if (live[i]) dpre[(int64_t)c * S + t] = d;
