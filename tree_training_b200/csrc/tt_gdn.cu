@@ -826,13 +826,34 @@ struct Builder {
     all.insert(all.end(), v.begin(), v.end());
     return d;
   }
+  // Dual pairs (v1[i] then v2[i], the first flagged `dual`) adding both
+  // products into v1[i]'s output tiles: tensor-core tiles for the first of
+  // each pair only, none for the CUDA-core GEMM (which runs the two single
+  // sets instead).
+  DescSet add_dual(const std::vector<SegDesc>& v1, const std::vector<SegDesc>& v2) {
+    DescSet d{(int)all.size(), 2 * (int)v1.size(), (int)tiles.size(), 0,
+              (int)tiles_tc.size(), 0, 0.0};
+    for (size_t i = 0; i < v1.size(); ++i) {
+      d.flops += 2.0 * v1[i].M * v1[i].N * v1[i].K + 2.0 * v2[i].M * v2[i].N * v2[i].K;
+      const int seg = (int)all.size();
+      SegDesc first = v1[i];
+      first.dual = 1;
+      all.push_back(first);
+      all.push_back(v2[i]);
+      const int ums = (first.M + kTcTile - 1) / kTcTile, uns = (first.N + kTcTile - 1) / kTcTile;
+      for (int tm = 0; tm < ums; ++tm)
+        for (int tn = 0; tn < uns; ++tn) tiles_tc.push_back(make_int2(seg, (tm << 16) | tn));
+    }
+    d.tc_count = (int)tiles_tc.size() - d.tc_first;
+    return d;
+  }
 };
 
 SegDesc desc(int M, int N, int K, long long ao, long long ars, long long acs, long long bo,
              long long brs, long long bcs, long long co, long long crs, long long ccs,
              int kmode = kKFull) {
   SegDesc d;
-  d.M = M; d.N = N; d.K = K; d.kmode = kmode; d.tok0 = 0;
+  d.M = M; d.N = N; d.K = K; d.kmode = kmode; d.tok0 = 0; d.dual = 0;
   d.a_off = ao; d.a_rs = ars; d.a_cs = acs;
   d.b_off = bo; d.b_rs = brs; d.b_cs = bcs;
   d.c_off = co; d.c_rs = crs; d.c_cs = ccs;
@@ -925,6 +946,49 @@ void launch_gemm(GemmCtx& g, DescSet ds, int H, const float* A, long long a_hs, 
                                           c_hs, alpha, beta, Cin);
   tt_count_launches(1);
   g_gemm_flops.fetch_add(static_cast<int64_t>(ds.flops * H), std::memory_order_relaxed);
+}
+
+// C = A1 B1 + A2 B2 + beta C_in over the dual set `dual_ds` (pairs of ds1's
+// and ds2's segments) in one TMA-staged tensor-core launch per chunk, the
+// two products accumulating in the same TMEM tile; the CUDA-core GEMM and
+// the cp.async staging run the two single sets one after the other instead.
+void launch_gemm_dual(GemmCtx& g, DescSet dual_ds, DescSet ds1, DescSet ds2, int H,
+                      const float* A1, long long a1_hs, const float* B1, long long b1_hs,
+                      const float* A2, long long a2_hs, const float* B2, long long b2_hs,
+                      float* C, long long c_hs, float beta, cudaStream_t st,
+                      const float* Cin = nullptr) {
+  const bool fused = g.split != 0 && g.tma && dual_ds.tc_count > 0 &&
+                     tt_gdn_tc_gemm_supported(g.h_desc->data(), ds1.first, ds1.count, A1, a1_hs,
+                                              B1, b1_hs, C, c_hs) &&
+                     tt_gdn_tc_gemm_supported(g.h_desc->data(), ds2.first, ds2.count, A2, a2_hs,
+                                              B2, b2_hs, C, c_hs);
+  if (!fused) {
+    launch_gemm(g, ds1, H, A1, a1_hs, B1, b1_hs, C, c_hs, 1.f, beta, st, Cin);
+    launch_gemm(g, ds2, H, A2, a2_hs, B2, b2_hs, C, c_hs, 1.f, 1.f, st);
+    return;
+  }
+  int launches = 0;
+  int t = dual_ds.tc_first;
+  const int t_end = dual_ds.tc_first + dual_ds.tc_count;
+  // kTmaMaxSegs is even, so no pair straddles two chunks
+  static_assert(kTmaMaxSegs % 2 == 0, "dual pairs per launch");
+  for (int c0 = 0; c0 < dual_ds.count; c0 += kTmaMaxSegs) {
+    const int c1 = std::min(dual_ds.count, c0 + kTmaMaxSegs);
+    const int seg_end = dual_ds.first + c1;
+    int t1 = t;
+    while (t1 < t_end && (*g.h_tiles_tc)[t1].x < seg_end) ++t1;
+    const int rc = tt_gdn_seg_gemm_tma(g.h_desc->data() + dual_ds.first + c0,
+                                       dual_ds.first + c0, c1 - c0, g.d_desc, g.d_tiles_tc + t,
+                                       t1 - t, H, A1, a1_hs, B1, b1_hs, C, c_hs, 1.f, beta, Cin,
+                                       g.split, st, EpiMask{},
+                                       DualOperands{A2, a2_hs, B2, b2_hs});
+    if (rc != TT_OK) g.rc = rc;
+    if (t1 > t) ++launches;
+    t = t1;
+  }
+  tt_count_launches(launches);
+  g_gemm_flops.fetch_add(static_cast<int64_t>(dual_ds.flops * H), std::memory_order_relaxed);
+  g_gemm_tc_flops.fetch_add(static_cast<int64_t>(dual_ds.flops * H), std::memory_order_relaxed);
 }
 
 template <typename T>
@@ -1099,6 +1163,10 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
           ds_daqk = bd.add(b_daqk), ds_dt1 = bd.add(b_dt1), ds_dt2 = bd.add(b_dt2),
           ds_x1 = bd.add(b_x1), ds_x2 = bd.add(b_x2), ds_tvt = bd.add(b_tvt),
           ds_tkt = bd.add(b_tkt), ds_gk = bd.add(b_gk), ds_gtk = bd.add(b_gtk);
+  // products that add into the same output, as dual pairs: dT = dVn Vb^T +
+  // dW Kbg^T; dA = dT A^T + A^T dT (+ dT); dK = G^T Kb + F^T Q
+  const DescSet dd_dt = bd.add_dual(b_dt1, b_dt2), dd_x = bd.add_dual(b_x1, b_x2),
+                dd_gtk = bd.add_dual(b_gtk, b_gtk);
   std::vector<DescSet> ds_dvn2, ds_dsi2;
   for (size_t d = 0; d < p.levels.size(); ++d) {
     ds_dvn2.push_back(bd.add(lb_dvn2[d]));
@@ -1262,8 +1330,8 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   launch_gemm(gc, ds_dkd, H, b.Vn, vv, b.dSo, DkDv, b.dKd, vk, 1.f, 0.f, st);
   launch_gemm(gc, ds_dw, H, b.dVn, vv, b.states, DkDv, b.dW, vk, -1.f, 0.f, st);
   launch_gemm(gc, ds_daqk, H, b.dO, vv, b.Vn, vv, b.dAqk, llh, 1.f, 0.f, st);
-  launch_gemm(gc, ds_dt1, H, b.dVn, vv, b.Vb, vv, b.dT, llh, 1.f, 0.f, st);
-  launch_gemm(gc, ds_dt2, H, b.dW, vk, b.Kbg, vk, b.dT, llh, 1.f, 1.f, st);
+  launch_gemm_dual(gc, dd_dt, ds_dt1, ds_dt2, H, b.dVn, vv, b.Vb, vv, b.dW, vk, b.Kbg, vk, b.dT,
+                   llh, 0.f, st);
   if (exact) {
     // Am holds T = (I - A)^-1:  dA = T^T dT T^T (masked in grad_masks);
     // dVb = T^T dVn;  dKbg = T^T dW
@@ -1273,8 +1341,8 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     launch_gemm(gc, ds_tkt, H, b.Am, llh, b.dW, vk, b.dKbg, vk, 1.f, 0.f, st);
   } else {
     // dA = dT + dT A^T + A^T dT  (masked in grad_masks)
-    launch_gemm(gc, ds_x1, H, b.dT, llh, b.Am, llh, b.dA, llh, 1.f, 1.f, st, b.dT);
-    launch_gemm(gc, ds_x2, H, b.Am, llh, b.dT, llh, b.dA, llh, 1.f, 1.f, st);
+    launch_gemm_dual(gc, dd_x, ds_x1, ds_x2, H, b.dT, llh, b.Am, llh, b.Am, llh, b.dT, llh,
+                     b.dA, llh, 1.f, st, b.dT);
     // dVb = T^T dVn = dVn + A^T (dVn + A^T dVn);  dKbg = T^T dW likewise
     launch_gemm(gc, ds_tvt, H, b.Am, llh, b.dVn, vv, b.T1, vv, 1.f, 1.f, st, b.dVn);
     launch_gemm(gc, ds_tvt, H, b.Am, llh, b.T1, vv, b.dVb, vv, 1.f, 1.f, st, b.dVn);
@@ -1304,8 +1372,8 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
   }
   // dKb = G K ; dK = G^T Kb + F^T Q ; dQ = F K
   launch_gemm(gc, ds_gk, H, b.dA, llh, b.K, vk, b.dKb, vk, 1.f, 0.f, st);
-  launch_gemm(gc, ds_gtk, H, b.dA, llh, b.Kb, vk, b.dK, vk, 1.f, 0.f, st);
-  launch_gemm(gc, ds_gtk, H, b.dAqk, llh, b.Q, vk, b.dK, vk, 1.f, 1.f, st);
+  launch_gemm_dual(gc, dd_gtk, ds_gtk, ds_gtk, H, b.dA, llh, b.Kb, vk, b.dAqk, llh, b.Q, vk,
+                   b.dK, vk, 0.f, st);
   launch_gemm(gc, ds_gk, H, b.dAqk, llh, b.K, vk, b.dQ, vk, 1.f, 0.f, st);
   kd_dot_kernel<<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(S, Dk, b.Kd, b.dKd, b.kd_dot);
   assemble_token_grads<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(

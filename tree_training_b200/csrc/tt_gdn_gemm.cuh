@@ -15,6 +15,8 @@ struct SegDesc {
   int M, N, K;
   int kmode;   // which part of the K range can hold nonzero products (kKFull, ...)
   int tok0;    // first token of the segment's node (the decay-mask epilogue)
+  int dual;    // 1: the next segment is a second product added into this one's
+               // output tile (its own A, B, K range; C fields unused), 0: none
   long long a_off, a_rs, a_cs;
   long long b_off, b_rs, b_cs;
   long long c_off, c_rs, c_cs;
@@ -39,6 +41,15 @@ struct EpiMask {
   int mode = kMaskNone;
   const float* gam = nullptr;
   long long gam_hs = 0;
+};
+
+// Second operand pair of a launch whose segments come in dual pairs (see
+// SegDesc::dual): the second segment of each pair reads A2 / B2.
+struct DualOperands {
+  const float* A2 = nullptr;
+  long long a2_hs = 0;
+  const float* B2 = nullptr;
+  long long b2_hs = 0;
 };
 
 // Output tile edge of the tensor-core GEMM (tiles of the tile list are
@@ -72,7 +83,8 @@ int tt_gdn_seg_gemm_tma(const tt::gdn::SegDesc* h_segs, int seg_first, int seg_c
                         const tt::gdn::SegDesc* d_desc, const int2* d_tiles, int n_tiles, int H,
                         const float* A, long long a_hs, const float* B, long long b_hs, float* C,
                         long long c_hs, float alpha, float beta, const float* Cin, int split,
-                        cudaStream_t st, tt::gdn::EpiMask mask = {});
+                        cudaStream_t st, tt::gdn::EpiMask mask = {},
+                        tt::gdn::DualOperands dual = {});
 constexpr int kTmaMaxSegs = 120;
 bool tt_gdn_tc_gemm_supported(const tt::gdn::SegDesc* h_desc, int first, int count,
                               const float* A, long long a_hs, const float* B, long long b_hs,

@@ -268,6 +268,39 @@ struct ItemFetch {
   }
 };
 
+// The K slices of an item: those of its segment, then (dual pair) those of
+// the second product, read from the following segment and its tensor maps.
+struct ItemSlices {
+  int kb1, n1, kb2, n2;
+  bool kc1a, kc1b, kc2a, kc2b;
+  __device__ __forceinline__ ItemSlices(const SegDesc* segs, int seg, const SegDesc& sd, int i0,
+                                        int j0) {
+    k_range(sd, i0, j0, kb1, n1);
+    kc1a = sd.a_cs == 1;
+    kc1b = sd.b_rs == 1;
+    kb2 = 0;
+    n2 = 0;
+    kc2a = kc2b = true;
+    if (sd.dual) {   // only the second product's K range and layouts are needed
+      const SegDesc* p2 = segs + seg + 1;
+      SegDesc sd2;
+      sd2.K = p2->K;
+      sd2.kmode = p2->kmode;
+      k_range(sd2, i0, j0, kb2, n2);
+      kc2a = p2->a_cs == 1;
+      kc2b = p2->b_rs == 1;
+    }
+  }
+  __device__ __forceinline__ int count() const { return n1 + n2; }
+  // slice t: which product, its K origin and operand layouts
+  __device__ __forceinline__ void at(int t, int& prod, int& k0, bool& a_kc, bool& b_kc) const {
+    prod = t < n1 ? 0 : 1;
+    k0 = prod == 0 ? kb1 + t * kTK : kb2 + (t - n1) * kTK;
+    a_kc = prod == 0 ? kc1a : kc2a;
+    b_kc = prod == 0 ? kc1b : kc2b;
+  }
+};
+
 // Tensor maps of one launch's segments (kernel parameter space): map 2 i is
 // operand A of segment seg_first + i, map 2 i + 1 its operand B.
 constexpr int kMaxSegsPerLaunch = 120;
@@ -351,10 +384,9 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
       f.advance(tl, sd);
       const int h = item % H;
       const int i0 = (tl.y >> 16) * kTM, j0 = (tl.y & 0xFFFF) * kTN;
-      const bool a_kc = sd.a_cs == 1, b_kc = sd.b_rs == 1;
       const CUtensorMap* ma = maps + 2 * (tl.x - seg_first);
-      int kb, nk;
-      k_range(sd, i0, j0, kb, nk);
+      const ItemSlices sl(segs, tl.x, sd, i0, j0);
+      const int nk = sl.count();
       for (int t = 0; t < nk; ++t, ++slot) {
         const int s = slot % R::kStages;
         const uint32_t use = slot / R::kStages;
@@ -364,10 +396,14 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
               !mbar_wait(&sh->empty[s], (use - 1) & 1, abort_flag)) {
             ok = false;
           } else {
+            int prod, k0;
+            bool a_kc, b_kc;
+            sl.at(t, prod, k0, a_kc, b_kc);
+            const CUtensorMap* mp_ = ma + 2 * prod;   // the pair's second segment: next maps
             uint64_t* bar = kSplit == 3 ? &sh->landed[s] : &sh->full[s];
             mbar_arrive_expect_tx(bar, 2 * kOpBytes);
-            tma_slice(st, ma, bar, a_kc, kb + t * kTK, i0, h);
-            tma_slice(st + kOpBytes, ma + 1, bar, b_kc, kb + t * kTK, j0, h);
+            tma_slice(st, mp_, bar, a_kc, k0, i0, h);
+            tma_slice(st + kOpBytes, mp_ + 1, bar, b_kc, k0, j0, h);
             issued |= 1u << s;
             parity = (parity & ~(1u << s)) | ((use & 1u) << s);
           }
@@ -477,9 +513,8 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
         int2 tl;
         SegDesc sd;
         f.advance(tl, sd);
-        const bool a_kc = sd.a_cs == 1, b_kc = sd.b_rs == 1;
-        int kb, nk;
-        k_range(sd, (tl.y >> 16) * kTM, (tl.y & 0xFFFF) * kTN, kb, nk);
+        const ItemSlices sl(segs, tl.x, sd, (tl.y >> 16) * kTM, (tl.y & 0xFFFF) * kTN);
+        const int nk = sl.count();
         const int buf = acc_i & 1;
         if (acc_i >= 2 && !mbar_wait(&sh->acc_empty[buf], ((acc_i >> 1) - 1) & 1, abort_flag)) {
           ok = false;
@@ -487,9 +522,12 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
         }
         tc_fence_after();
         const uint32_t d = tmem + buf * kTN;
-        const uint32_t idesc = idesc_tf32(!a_kc, !b_kc);
         for (int t = 0; t < nk; ++t, ++slot) {
           const int s = slot % R::kStages;
+          int prod, k0;
+          bool a_kc, b_kc;
+          sl.at(t, prod, k0, a_kc, b_kc);
+          const uint32_t idesc = idesc_tf32(!a_kc, !b_kc);
           if (!mbar_wait(&sh->full[s], (slot / R::kStages) & 1, abort_flag)) {
             ok = false;
             break;
@@ -595,9 +633,18 @@ __device__ __forceinline__ void gemm_body(const SegDesc* __restrict__ segs,
         cp_async_wait<0>();
         __syncwarp();
       }
-      int kb, nk;
-      k_range(sd, i0, j0, kb, nk);
-      const bool empty_k = nk == 0;            // no MMA wrote this accumulator
+      bool empty_k;                            // no MMA wrote this accumulator
+      {
+        int kb, nk;
+        k_range(sd, i0, j0, kb, nk);
+        if (nk == 0 && sd.dual) {
+          SegDesc sd2;
+          sd2.K = segs[tl.x + 1].K;
+          sd2.kmode = segs[tl.x + 1].kmode;
+          k_range(sd2, i0, j0, kb, nk);
+        }
+        empty_k = nk == 0;
+      }
       // without 16-byte aligned rows of C, each 32 x 32 block goes through
       // shared memory so that the warp stores (and reads C_in) one 128-byte
       // row segment per instruction
@@ -836,10 +883,12 @@ int tt_gdn_seg_gemm_tma(const SegDesc* h_segs, int seg_first, int seg_count,
                         const SegDesc* d_desc, const int2* d_tiles, int n_tiles, int H,
                         const float* A, long long a_hs, const float* B, long long b_hs, float* C,
                         long long c_hs, float alpha, float beta, const float* Cin, int split,
-                        cudaStream_t st, tt::gdn::EpiMask mask) {
+                        cudaStream_t st, tt::gdn::EpiMask mask, tt::gdn::DualOperands dual) {
   using namespace tt::gdn;
   if (n_tiles <= 0 || H <= 0) return TT_OK;
   if (seg_count > kMaxSegsPerLaunch) return TT_ERR_INVALID_ARG;
+  // a dual pair never straddles two launches
+  if (seg_count > 0 && h_segs[seg_count - 1].dual) return TT_ERR_INVALID_ARG;
   const EncodeTiledFn fn = encoder();
   if (!fn) return TT_ERR_UNSUPPORTED;
   MapPack mp;
@@ -847,11 +896,16 @@ int tt_gdn_seg_gemm_tma(const SegDesc* h_segs, int seg_first, int seg_count,
   for (int i = 0; i < seg_count; ++i) {
     const SegDesc& d = h_segs[i];
     if (d.M <= 0 || d.N <= 0 || d.K <= 0) continue;   // no tiles, or no slices to load
+    const bool second = i > 0 && h_segs[i - 1].dual;  // the second product of a pair
+    if (second && (!dual.A2 || !dual.B2)) return TT_ERR_INVALID_ARG;
+    const float* Ab = second ? dual.A2 : A;
+    const float* Bb = second ? dual.B2 : B;
+    const long long ahs = second ? dual.a2_hs : a_hs, bhs = second ? dual.b2_hs : b_hs;
     const bool a_kc = d.a_cs == 1, b_kc = d.b_rs == 1;
-    if (!encode_operand(fn, &mp.m[2 * i], A + d.a_off, a_kc, d.M, d.K, a_kc ? d.a_rs : d.a_cs,
-                        a_hs, H) ||
-        !encode_operand(fn, &mp.m[2 * i + 1], B + d.b_off, b_kc, d.N, d.K, b_kc ? d.b_cs : d.b_rs,
-                        b_hs, H))
+    if (!encode_operand(fn, &mp.m[2 * i], Ab + d.a_off, a_kc, d.M, d.K, a_kc ? d.a_rs : d.a_cs,
+                        ahs, H) ||
+        !encode_operand(fn, &mp.m[2 * i + 1], Bb + d.b_off, b_kc, d.N, d.K,
+                        b_kc ? d.b_cs : d.b_rs, bhs, H))
       return TT_ERR_UNSUPPORTED;
   }
   int dev = 0;
