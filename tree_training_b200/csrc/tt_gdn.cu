@@ -1107,6 +1107,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     ds_kdv.push_back(bd.add(lv_kdv[d]));
   }
   const DescSet ds_qs = bd.add(v_qs), ds_aqv = bd.add(v_aqv);
+  const DescSet dd_o = bd.add_dual(v_qs, v_aqv);   // O = Qg S_in + Aqk Vn in one launch
   // backward descriptors
   std::vector<std::vector<SegDesc>> lb_dvn2(p.levels.size()), lb_dsi2(p.levels.size());
   std::vector<SegDesc> b_dvn1, b_dsi1;
@@ -1290,8 +1291,8 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
       ++launches;
     }
     if (!backward) {   // the output; the backward (which recomputes this pass) never reads it
-      launch_gemm(gc, ds_qs, H, b.Qg, vk, b.states, DkDv, b.O, vv, 1.f, 0.f, st);
-      launch_gemm(gc, ds_aqv, H, b.Aqk, llh, b.Vn, vv, b.O, vv, 1.f, 1.f, st);
+      launch_gemm_dual(gc, dd_o, ds_qs, ds_aqv, H, b.Qg, vk, b.states, DkDv, b.Aqk, llh, b.Vn,
+                       vv, b.O, vv, 0.f, st);
     }
   }
   if (!backward) {
