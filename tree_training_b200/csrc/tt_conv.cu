@@ -75,6 +75,12 @@ namespace {
 // 1e-5 against the float64 oracle)
 __device__ __forceinline__ float sigm(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 __device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.f + __expf(-x)); }
+// d silu(pre) / d pre times the output gradient g (every backward kernel
+// computes dpre through this one expression, so their dpre agree bit for bit)
+__device__ __forceinline__ float silu_grad(float g, float pre) {
+  const float sg = sigm(pre);
+  return g * sg * (1.f + pre * (1.f - sg));
+}
 
 constexpr int kConvTok = 256;   // tokens per block (one per thread)
 constexpr int kConvCh = 8;      // channels per thread: the token's predecessor and
@@ -160,8 +166,7 @@ conv_bwd_dpre(int C, int S, const T* __restrict__ x, const float* __restrict__ w
     float pre = bias ? bias[c] : 0.f;
 #pragma unroll
     for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[cc][m], pre);
-    const float sg = sigm(pre);
-    const float d = live ? g[cc] * sg * (1.f + pre * (1.f - sg)) : 0.f;
+    const float d = live ? silu_grad(g[cc], pre) : 0.f;
     if (live) dpre[(int64_t)c * S + t] = d;
 #pragma unroll
     for (int j = 0; j < kPartW; ++j) {
@@ -367,8 +372,7 @@ conv_bwd_dpre4(int C, int S, const T* __restrict__ x, const float* __restrict__ 
         float pre = bias ? bias[c] : 0.f;
 #pragma unroll
         for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[cc][i][m], pre);
-        const float sg = sigm(pre);
-        d[i] = live ? g[cc][i] * sg * (1.f + pre * (1.f - sg)) : 0.f;
+        d[i] = live ? silu_grad(g[cc][i], pre) : 0.f;
       }
       if (live)
         *reinterpret_cast<float4*>(dpre + (int64_t)c * S + t0) = make_float4(d[0], d[1], d[2], d[3]);
@@ -465,37 +469,59 @@ conv_bwd_dx4(int C, int S, const float* __restrict__ w, const float* __restrict_
 // contiguous: what the layer's transpose + split into q / k / v reads without a
 // transposing copy).  One block per 64 channels x 128 tokens, 256 threads:
 //   1. 16-byte cp.async copies stage the tile's x rows (channel-major, tokens
-//      [t0 - 8, t0 + 128): the window's predecessors inside the tile) and, in
-//      the backward, the dy rows (token-major, 64 channels) in shared memory;
-//   2. the forward's thread (token tt = tid % 128, channel half tid / 128)
-//      computes its 32 channels of token t0 + tt, the backward's warp w
-//      channels 8w .. 8w + 7 of tokens t0 + lane + 32 i, from shared memory
-//      (a window that leaves the tile, at a node's first tokens, is read from
-//      global memory), with the same arithmetic per output as the
-//      channel-major kernels;
-//   3. the forward writes the token-major tile back as whole 16-byte row
-//      chunks; the backward writes dpre channel-major (consecutive tokens per
-//      warp) and reduces the dw / db partials of each channel over the tile.
+//      [t0 - 8, t0 + 128), the backward 8 more) in shared memory, the
+//      backward also the dy rows (token-major, 64 channels); one ballot per
+//      32 tokens marks the tokens whose window is t, t - 1, .., t - K + 1
+//      (the inside of a node);
+//   2. thread (r, q) = (lane + 32 (warp % 2), warp / 2) owns tile channel r
+//      over tokens 32 q .. 32 q + 31: it holds the channel's weights in
+//      registers and slides along the row, reading each x value once from
+//      shared memory (16 bytes at a time) into a register window; a token
+//      whose window leaves the node gathers its window from the predecessor
+//      table instead (shared memory inside the staged range, global memory
+//      outside).  The arithmetic per output is that of the channel-major
+//      kernels, in the same order, so the results match them bit for bit;
+//   3. the forward writes its output tile into shared memory (one 64-byte
+//      token row per warp store) and then to global memory as whole 16-byte
+//      row chunks; the backward keeps dpre in registers (see conv_bwd_tm).
 // Needs S * sizeof(T) % 16 == 0, C % 8 == 0 and 16-byte aligned bases.
 constexpr int kTmCh = 64;                    // channels per tile
 constexpr int kTmTok = 128;                  // tokens per tile
 constexpr int kTmThreads = 256;
 constexpr int kTmHalo = 8;                   // staged tokens before the tile (K - 1 <= 7)
+constexpr int kTmRun = 32;                   // tokens per thread
 
+// x row stride (elements) for n staged tokens (a multiple of 16 bytes): the
+// smallest with 4 words mod 8 per row, so the 8 lanes of a quarter warp reading
+// 16 bytes each from 8 consecutive rows hit disjoint banks
 template <typename T>
-struct TmTile {
+constexpr int x_row_stride(int n) {
+  const int per_word = 4 / static_cast<int>(sizeof(T));
+  const int words = n / per_word;
+  return (words + (12 - words % 8) % 8) * per_word;
+}
+
+// kRight: tokens staged past the tile's end (x and the token-major rows)
+template <typename T, int kRight>
+struct TmTileR {
   static constexpr int kEl = 16 / static_cast<int>(sizeof(T));   // elements per 16 bytes
-  static constexpr int kXW = kTmHalo + kTmTok;                     // staged tokens per x row
+  static constexpr int kXS = kTmHalo + kTmTok + kRight;            // staged tokens per x row
+  static constexpr int kXW = x_row_stride<T>(kXS);                 // x row stride
+  static constexpr int kRows = kTmTok + kRight;                    // token-major rows
   static constexpr int kTW = kTmCh + kEl;                          // token row (+ one chunk pad)
+  static constexpr int kBits = (kRows + 31) / 32;                  // plain-window words
   T x[kTmCh][kXW];                       // x[c0 + r][t0 - 8 + i]
-  T tm[kTmTok][kTW];                     // token-major rows: out (fwd) or dy (bwd)
+  T tm[kRows][kTW];                      // token-major rows: out (fwd) or dy (bwd)
   float w[kTmCh * 8];                    // the tile's weights, [r][K]
   float b[kTmCh];                        // and biases (0 without)
+  uint32_t plain[kBits];                 // bit j of word i: token t0 + 32 i + j
 };
+template <typename T>
+using TmTile = TmTileR<T, 0>;
 
-// Stage the tile's weights and biases (read by every thread of a channel).
-template <typename T, int K>
-__device__ __forceinline__ void stage_w(TmTile<T>& sm, const float* w, const float* bias, int C,
+// Stage the tile's weights and biases.
+template <int K, typename Tile>
+__device__ __forceinline__ void stage_w(Tile& sm, const float* w, const float* bias, int C,
                                         int c0) {
   for (int i = threadIdx.x; i < kTmCh * K; i += kTmThreads) {
     const int c = c0 + i / K;
@@ -512,10 +538,11 @@ __device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, boo
                : "memory");
 }
 
-// Stage x[c0 .. c0 + 63][t0 - 8 .. t0 + 127] (zero outside [0, S) and past C).
-template <typename T>
-__device__ __forceinline__ void stage_x(TmTile<T>& sm, const T* x, int C, int S, int c0, int t0) {
-  constexpr int kEl = TmTile<T>::kEl, kXC = TmTile<T>::kXW / kEl;
+// Stage x[c0 .. c0 + 63][t0 - 8 .. t0 + kXS - 9] (zero outside [0, S) and
+// past C).
+template <typename Tile, typename T>
+__device__ __forceinline__ void stage_x(Tile& sm, const T* x, int C, int S, int c0, int t0) {
+  constexpr int kEl = Tile::kEl, kXC = Tile::kXS / kEl;
   for (int q = threadIdx.x; q < kTmCh * kXC; q += kTmThreads) {
     const int r = q / kXC, k = q % kXC;
     const int c = c0 + r, t = t0 - kTmHalo + k * kEl;   // chunks are whole: S % kEl == 0
@@ -524,160 +551,334 @@ __device__ __forceinline__ void stage_x(TmTile<T>& sm, const T* x, int C, int S,
   }
 }
 
-// The window of token t (tile token tt) in tile channel r: xs[m] = x[c][pred_m(t)].
-template <typename T, int K>
-__device__ __forceinline__ void tile_window(const TmTile<T>& sm, const T* x, int S, int c, int r,
-                                            int t0, int tt, bool plain,
-                                            const int (&pr)[K > 1 ? K - 1 : 1], float (&xs)[K]) {
-  xs[0] = to_f32(sm.x[r][kTmHalo + tt]);
+// The plain-window bits of tile tokens 0 .. 32 kBits - 1 (whole warps per word).
+template <int K, typename Tile>
+__device__ __forceinline__ void stage_plain(Tile& sm, const int32_t* __restrict__ pred, int S,
+                                            int t0) {
+  for (int base = (threadIdx.x >> 5) * 32; base < Tile::kBits * 32; base += kTmThreads) {
+    const int t = t0 + base + (threadIdx.x & 31);
+    bool pl = t < S;
+    if (pl) {
+      int pv[K > 1 ? K - 1 : 1];             // independent loads, then the compares
 #pragma unroll
-  for (int m = 1; m < K; ++m) {
-    if (plain) {
-      xs[m] = to_f32(sm.x[r][kTmHalo + tt - m]);
-    } else {
-      const int p = pr[m - 1];
-      xs[m] = p < 0 ? 0.f
-              : (p >= t0 - kTmHalo && p < t0 + kTmTok) ? to_f32(sm.x[r][p - t0 + kTmHalo])
-                                                       : to_f32(x[(int64_t)c * S + p]);
+      for (int m = 0; m < K - 1; ++m) pv[m] = pred[(int64_t)t * (K - 1) + m];
+#pragma unroll
+      for (int m = 0; m < K - 1; ++m) pl = pl && pv[m] == t - 1 - m;
     }
+    const uint32_t bits = __ballot_sync(0xffffffffu, pl);
+    if ((threadIdx.x & 31) == 0) sm.plain[base >> 5] = bits;
   }
 }
 
-template <int K>
-__device__ __forceinline__ bool tile_pred(const int32_t* __restrict__ pred, int t, bool live,
-                                          int (&pr)[K > 1 ? K - 1 : 1]) {
-  pr[0] = -1;
-  bool plain = true;
-#pragma unroll
-  for (int m = 0; m < K - 1; ++m) {
-    pr[m] = live ? pred[(int64_t)t * (K - 1) + m] : -1;
-    plain &= pr[m] == t - 1 - m;
+// The window of token t = t0 + tt in tile channel r (c = c0 + r) through the
+// predecessor table: xs[m] = x[c][pred_m(t)], from shared memory inside the
+// staged range, else from global memory (0 for t >= S or where the path is
+// shorter).
+template <int K, typename Tile, typename T>
+__device__ __forceinline__ void window_gather(const Tile& sm, const T* __restrict__ x,
+                                           const int32_t* __restrict__ pred, int S, int c, int r,
+                                           int t0, int tt, float* xs) {
+  const int t = t0 + tt;
+  if (t >= S) {
+    for (int m = 0; m < K; ++m) xs[m] = 0.f;
+    return;
   }
-  return plain;
+  auto at = [&](int p) {
+    return p < 0 ? 0.f
+           : (p >= t0 - kTmHalo && p < t0 - kTmHalo + Tile::kXS)
+               ? to_f32(sm.x[r][p - t0 + kTmHalo])
+               : to_f32(x[(int64_t)c * S + p]);
+  };
+  xs[0] = at(t);
+  for (int m = 1; m < K; ++m) xs[m] = at(pred[(int64_t)t * (K - 1) + m - 1]);
+}
+
+// n consecutive x values of tile row r starting at staged index i0 (a
+// multiple of kEl) into xr[0 .. n)
+template <typename Tile, typename T>
+__device__ __forceinline__ void ld_chunk(const Tile& sm, int r, int i0, float* xr) {
+  const uint4 v = *reinterpret_cast<const uint4*>(&sm.x[r][i0]);
+  const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < Tile::kEl; ++i) xr[i] = to_f32(e[i]);
 }
 
 template <typename T, int K>
-__global__ void __launch_bounds__(kTmThreads)
+__global__ void __launch_bounds__(kTmThreads, 4)
 conv_fwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
             const float* __restrict__ bias, const int32_t* __restrict__ pred,
             T* __restrict__ out_tm) {
   extern __shared__ __align__(16) uint8_t tm_smem[];
-  TmTile<T>& sm = *reinterpret_cast<TmTile<T>*>(tm_smem);
-  constexpr int kEl = TmTile<T>::kEl;
+  using Tile = TmTile<T>;
+  Tile& sm = *reinterpret_cast<Tile*>(tm_smem);
+  constexpr int kEl = Tile::kEl;
   const int c0 = blockIdx.y * kTmCh, t0 = blockIdx.x * kTmTok;
-  stage_x<T>(sm, x, C, S, c0, t0);
-  stage_w<T, K>(sm, w, bias, C, c0);
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  stage_x(sm, x, C, S, c0, t0);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  stage_w<K>(sm, w, bias, C, c0);
+  stage_plain<K>(sm, pred, S, t0);
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  const int tt = threadIdx.x & (kTmTok - 1), half = threadIdx.x / kTmTok;
-  const int t = t0 + tt;
-  const bool live = t < S;
-  int pr[K > 1 ? K - 1 : 1];
-  const bool plain = tile_pred<K>(pred, t, live, pr);
-  struct alignas(2 * sizeof(T)) Pair {
-    T a, b;
-  };
-#pragma unroll 1
-  for (int cp = 0; cp < kTmCh / 2; cp += 2) {
-    const int r = half * (kTmCh / 2) + cp;
-    float o[2] = {0.f, 0.f};
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = (warp & 1) * 32 + lane, tq = (warp >> 1) * kTmRun;
+  const uint32_t bits = sm.plain[warp >> 1];
+  float wr[K];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int c = min(c0 + r + e, C - 1);
+  for (int m = 0; m < K; ++m) wr[m] = sm.w[r * K + m];
+  const float b0 = sm.b[r];
+  // clean: every window of the run is plain (a run inside one node), no
+  // per-token branch
+  auto run = [&](auto clean) {
+    constexpr bool kClean = decltype(clean)::value;
+    // xr[kTmHalo + j] = x at tile token tq + j
+    float xr[kTmHalo + kTmRun];
+    ld_chunk<Tile, T>(sm, r, tq, xr);
+    if (kEl == 4) ld_chunk<Tile, T>(sm, r, tq + 4, xr + 4);
+#pragma unroll
+    for (int j = 0; j < kTmRun; ++j) {
+      if (j % kEl == 0) ld_chunk<Tile, T>(sm, r, kTmHalo + tq + j, xr + kTmHalo + j);
       float xs[K];
-      tile_window<T, K>(sm, x, S, c, r + e, t0, tt, plain, pr, xs);
-      const float* wc = sm.w + (r + e) * K;
-      float pre = sm.b[r + e];
+      if (kClean || (bits >> j & 1)) {
 #pragma unroll
-      for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[m], pre);
-      o[e] = silu(pre);
+        for (int m = 0; m < K; ++m) xs[m] = xr[kTmHalo + j - m];
+      } else {
+        window_gather<K>(sm, x, pred, S, min(c0 + r, C - 1), r, t0, tq + j, xs);
+      }
+      float pre = b0;
+#pragma unroll
+      for (int m = 0; m < K; ++m) pre = fmaf(wr[K - 1 - m], xs[m], pre);
+      sm.tm[tq + j][r] = from_f32<T>(silu(pre));
     }
-    *reinterpret_cast<Pair*>(&sm.tm[tt][r]) = Pair{from_f32<T>(o[0]), from_f32<T>(o[1])};
-  }
+  };
+  if (bits == 0xffffffffu)
+    run(std::true_type());
+  else
+    run(std::false_type());
   __syncthreads();
   constexpr int kTC = kTmCh / kEl;               // 16-byte chunks per token row
   for (int q = threadIdx.x; q < kTmTok * kTC; q += kTmThreads) {
     const int rr = q / kTC, k = q % kTC;
-    const int tq = t0 + rr, c = c0 + k * kEl;
-    if (tq < S && c < C)
-      *reinterpret_cast<uint4*>(out_tm + (int64_t)tq * C + c) =
+    const int t = t0 + rr, c = c0 + k * kEl;
+    if (t < S && c < C)
+      *reinterpret_cast<uint4*>(out_tm + (int64_t)t * C + c) =
           *reinterpret_cast<const uint4*>(&sm.tm[rr][k * kEl]);
   }
 }
 
-// dpre (channel-major fp32) from x (channel-major) and dy (token-major), and
-// per (channel, 128-token block) the dw / db partials: a channel's 128 tokens
-// are in one warp, each thread adds its 4 tokens' terms and one shuffle
-// reduction per term finishes the partial.
+// The backward from token-major dy in one pass: dx (channel-major) and the
+// dw / db partials per (channel, 128-token block), without dpre in global
+// memory.  The tile stages x over [t0 - 8, t0 + 136) and dy rows t0 .. t0 +
+// 135, and marks the tokens whose successor list is exactly t + 1 .. t + K - 1
+// with lags 1 .. K - 1 in CSR order (the inside of a node).  Thread (r, q)
+// then slides over tokens 32 q .. 32 q + 31 + K - 1 of channel r: dpre of
+// each (the K - 1 past its run are the next run's first tokens, computed
+// again here) into a register window, its tokens' dw / db terms, and
+// dx[t] = w[K-1] dpre[t] + sum_l w[K-1-l] dpre[t + l] once dpre[t + K - 1] is
+// known.  A token with another successor list walks the successor CSR,
+// recomputing each successor's dpre from x and dy (a node's last tokens feed
+// its later children, far away in DFS order).  Per output the arithmetic and
+// its order are those of conv_bwd_dpre4 + conv_bwd_dx4, so dx matches the
+// channel-major kernels bit for bit; the four runs' dw / db terms are added in
+// run order.
+template <typename T>
+struct TmBwdTile {
+  TmTileR<T, kTmHalo> s;                 // x [t0 - 8, t0 + 136), dy rows t0 .. t0 + 135
+  float red[kTmTok / kTmRun][kTmCh][kPartW];   // per run: dw / db terms
+  uint32_t succ_plain[kTmTok / 32];      // bit j of word i: token t0 + 32 i + j
+};
+
+// dpre of token u in tile channel r (c = c0 + r): the window through the
+// predecessor table, dy from the staged rows or global memory.
+template <int K, typename Tile, typename T>
+__device__ __forceinline__ float dpre_any(const Tile& sm, const T* __restrict__ x,
+                                          const T* __restrict__ dy_tm,
+                                          const int32_t* __restrict__ pred, int C, int S, int c,
+                                          int r, int t0, int u) {
+  float xs[K];
+  window_gather<K>(sm, x, pred, S, c, r, t0, u - t0, xs);
+  float pre = sm.b[r];
+#pragma unroll
+  for (int m = 0; m < K; ++m) pre = fmaf(sm.w[r * K + K - 1 - m], xs[m], pre);
+  const float g = u - t0 < Tile::kRows ? to_f32(sm.tm[u - t0][r])
+                                       : to_f32(dy_tm[(int64_t)u * C + c]);
+  return silu_grad(g, pre);
+}
+
+// dx of token t with an irregular successor list (dpre_t: its own dpre)
+template <int K, typename Tile, typename T>
+__device__ __forceinline__ float dx_walk(const Tile& sm, const T* __restrict__ x,
+                                      const T* __restrict__ dy_tm,
+                                      const int32_t* __restrict__ pred,
+                                      const int32_t* __restrict__ sp,
+                                      const int32_t* __restrict__ stok,
+                                      const int32_t* __restrict__ slag, int C, int S, int c, int r,
+                                      int t0, int t, float dpre_t) {
+  const float* wc = sm.w + r * K;
+  float s = wc[K - 1] * dpre_t;
+  const int e1 = sp[t + 1];
+  for (int e = sp[t]; e < e1; ++e) {
+    const int u = stok[e], l = slag[e];
+    s = fmaf(wc[K - 1 - l], dpre_any<K>(sm, x, dy_tm, pred, C, S, c, r, t0, u), s);
+  }
+  return s;
+}
+
 template <typename T, int K>
-__global__ void __launch_bounds__(kTmThreads, 3)
-conv_bwd_dpre_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
-                 const float* __restrict__ bias, const int32_t* __restrict__ pred,
-                 const T* __restrict__ dy_tm, float* __restrict__ dpre, float* __restrict__ part,
-                 int nb) {
+__global__ void __launch_bounds__(kTmThreads)
+conv_bwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
+            const float* __restrict__ bias, const int32_t* __restrict__ pred,
+            const int32_t* __restrict__ sp, const int32_t* __restrict__ stok,
+            const int32_t* __restrict__ slag, const T* __restrict__ dy_tm, T* __restrict__ dx,
+            float* __restrict__ part, int nb) {
   extern __shared__ __align__(16) uint8_t tm_smem[];
-  TmTile<T>& sm = *reinterpret_cast<TmTile<T>*>(tm_smem);
-  constexpr int kEl = TmTile<T>::kEl, kTC = kTmCh / kEl;
+  using Tile = TmTileR<T, kTmHalo>;
+  TmBwdTile<T>& bt = *reinterpret_cast<TmBwdTile<T>*>(tm_smem);
+  Tile& sm = bt.s;
+  constexpr int kEl = Tile::kEl, kTC = kTmCh / kEl;
   const int c0 = blockIdx.y * kTmCh, t0 = blockIdx.x * kTmTok;
-  stage_x<T>(sm, x, C, S, c0, t0);
-  stage_w<T, K>(sm, w, bias, C, c0);
-  for (int q = threadIdx.x; q < kTmTok * kTC; q += kTmThreads) {
+  stage_x(sm, x, C, S, c0, t0);
+  for (int q = threadIdx.x; q < Tile::kRows * kTC; q += kTmThreads) {
     const int rr = q / kTC, k = q % kTC;
-    const int tq = t0 + rr, c = c0 + k * kEl;
-    const bool ok = tq < S && c < C;
-    cp_async16_zfill(&sm.tm[rr][k * kEl], ok ? dy_tm + (int64_t)tq * C + c : dy_tm, ok);
+    const int t = t0 + rr, c = c0 + k * kEl;
+    const bool ok = t < S && c < C;
+    cp_async16_zfill(&sm.tm[rr][k * kEl], ok ? dy_tm + (int64_t)t * C + c : dy_tm, ok);
   }
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-  __syncthreads();
-  // warp w: channels 8w .. 8w + 7; lane l: tokens t0 + l + 32 i (i < 4), so a
-  // channel's 128 tokens sit in one warp: each thread adds its 4 tokens'
-  // terms, one shuffle reduction per (channel, term), lane 0 writes the partial
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int kTokPerLane = kTmTok / 32, kChPerWarp = kTmCh / (kTmThreads / 32);
-  int pr[kTokPerLane][K > 1 ? K - 1 : 1];
-  bool plain[kTokPerLane], live[kTokPerLane];
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  stage_w<K>(sm, w, bias, C, c0);
+  stage_plain<K>(sm, pred, S, t0);
+  if (threadIdx.x < kTmTok) {                // successor lists
+    const int t = t0 + threadIdx.x;
+    bool pl = t < S;
+    if (pl) {
+      const int e0 = sp[t], e1 = sp[t + 1];
+      int su[K > 1 ? K - 1 : 1], sl[K > 1 ? K - 1 : 1];   // independent loads
 #pragma unroll
-  for (int i = 0; i < kTokPerLane; ++i) {
-    const int t = t0 + lane + 32 * i;
-    live[i] = t < S;
-    plain[i] = tile_pred<K>(pred, t, live[i], pr[i]);
-  }
-#pragma unroll 1
-  for (int cl = 0; cl < kChPerWarp; ++cl) {
-    const int r = warp * kChPerWarp + cl;
-    if (c0 + r >= C) break;                          // the same for the whole warp
-    const int c = c0 + r;
-    const float* wc = sm.w + r * K;
-    const float b0 = sm.b[r];
-    float acc[kPartW];
-#pragma unroll
-    for (int j = 0; j < kPartW; ++j) acc[j] = 0.f;
-#pragma unroll
-    for (int i = 0; i < kTokPerLane; ++i) {
-      const int tt = lane + 32 * i, t = t0 + tt;
-      float xs[K];
-      tile_window<T, K>(sm, x, S, c, r, t0, tt, plain[i], pr[i], xs);
-      float pre = b0;
-#pragma unroll
-      for (int m = 0; m < K; ++m) pre = fmaf(wc[K - 1 - m], xs[m], pre);
-      const float sg = sigm(pre);
-      const float g = to_f32(sm.tm[tt][r]);
-      const float d = live[i] ? g * sg * (1.f + pre * (1.f - sg)) : 0.f;
-      if (live[i]) dpre[(int64_t)c * S + t] = d;
-#pragma unroll
-      for (int j = 0; j < K; ++j) acc[j] += d * xs[K - 1 - j];
-      acc[8] += d;
-    }
-#pragma unroll
-    for (int j = 0; j < kPartW; ++j) {
-      float v = 0.f;
-      if (j < K || j == 8) {
-        v = acc[j];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      for (int m = 0; m < K - 1; ++m) {
+        const bool in = e0 + m < e1;
+        su[m] = in ? stok[e0 + m] : -1;
+        sl[m] = in ? slag[e0 + m] : 0;
       }
-      if (lane == 0) part[((int64_t)c * nb + blockIdx.x) * kPartW + j] = v;
+      pl = e1 - e0 == K - 1;
+#pragma unroll
+      for (int m = 0; m < K - 1; ++m) pl = pl && su[m] == t + 1 + m && sl[m] == m + 1;
     }
+    const uint32_t bits = __ballot_sync(0xffffffffu, pl);
+    if ((threadIdx.x & 31) == 0) bt.succ_plain[threadIdx.x >> 5] = bits;
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int run = warp >> 1, r = (warp & 1) * 32 + lane, tq = run * kTmRun;
+  const int c = min(c0 + r, C - 1);          // rows past C compute on row C - 1, never stored
+  const uint32_t pb0 = sm.plain[run], pb1 = sm.plain[run + 1], sb = bt.succ_plain[run];
+  float wr[K];
+#pragma unroll
+  for (int m = 0; m < K; ++m) wr[m] = sm.w[r * K + m];
+  const float b0 = sm.b[r];
+  float acc[kPartW];
+#pragma unroll
+  for (int j = 0; j < kPartW; ++j) acc[j] = 0.f;
+  T* dxr = dx + (int64_t)(c0 + r) * S + t0 + tq;
+  const bool row_live = c0 + r < C;
+  const uint64_t pbits = pb0 | (uint64_t)pb1 << 32;
+  // The run in chunks of 8 tokens (a loop that is not unrolled, so the state
+  // carried across chunks bounds the registers): chunk ci computes dpre of
+  // run tokens 8 ci .. 8 ci + 7 (chunk 4: only the K - 1 tokens past the
+  // run), then dx of chunk ci - 1, whose successors' dpre are now known.
+  // clean: every window and successor list of the run is plain (a run inside
+  // one node, all tokens < S), no per-token branch.
+  auto body = [&](auto clean) {
+    constexpr bool kClean = decltype(clean)::value;
+    float xp[8], dp[8];                      // the previous chunk's x and dpre
+    ld_chunk<Tile, T>(sm, r, tq, xp);
+    if (kEl == 4) ld_chunk<Tile, T>(sm, r, tq + 4, xp + 4);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dp[i] = 0.f;
+#pragma unroll 1
+    for (int ci = 0; ci <= kTmRun / 8; ++ci) {
+      const int base = 8 * ci;
+      float xc[8], dc[8];
+      ld_chunk<Tile, T>(sm, r, kTmHalo + tq + base, xc);
+      if (kEl == 4) ld_chunk<Tile, T>(sm, r, kTmHalo + tq + base + 4, xc + 4);
+      const uint32_t cb = (uint32_t)(pbits >> base) & 0xffu;
+      const bool last = ci == kTmRun / 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int tt = tq + base + i;
+        if (last && i >= K - 1) {
+          dc[i] = 0.f;
+          continue;
+        }
+        float xs[K];
+        if (kClean || (cb >> i & 1)) {
+#pragma unroll
+          for (int m = 0; m < K; ++m) xs[m] = i >= m ? xc[i - m] : xp[8 + i - m];
+        } else {
+          window_gather<K>(sm, x, pred, S, c, r, t0, tt, xs);
+        }
+        float pre = b0;
+#pragma unroll
+        for (int m = 0; m < K; ++m) pre = fmaf(wr[K - 1 - m], xs[m], pre);
+        dc[i] = (kClean || t0 + tt < S) ? silu_grad(to_f32(sm.tm[tt][r]), pre) : 0.f;
+        if (!last) {
+#pragma unroll
+          for (int jj = 0; jj < K; ++jj) acc[jj] += dc[i] * xs[K - 1 - jj];
+          acc[8] += dc[i];
+        }
+      }
+      if (ci > 0) {                          // dx of chunk ci - 1
+        const int pbase = base - 8;
+        const uint32_t sc = (sb >> pbase) & 0xffu;
+        float dxv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (kClean || (sc >> i & 1)) {
+            float sacc = wr[K - 1] * dp[i];
+#pragma unroll
+            for (int l = 1; l < K; ++l) sacc = fmaf(wr[K - 1 - l], i + l < 8 ? dp[i + l] : dc[i + l - 8], sacc);
+            dxv[i] = sacc;
+          } else if (t0 + tq + pbase + i < S) {
+            dxv[i] = dx_walk<K>(sm, x, dy_tm, pred, sp, stok, slag, C, S, c, r, t0,
+                                t0 + tq + pbase + i, dp[i]);
+          }
+        }
+        // whole 16-byte chunks (S % kEl == 0: live or dead as a whole)
+#pragma unroll
+        for (int h = 0; h < 8 / kEl; ++h) {
+          if (row_live && (kClean || t0 + tq + pbase + h * kEl < S)) {
+            uint4 v;
+            T* e = reinterpret_cast<T*>(&v);
+#pragma unroll
+            for (int i = 0; i < kEl; ++i) e[i] = from_f32<T>(dxv[h * kEl + i]);
+            *reinterpret_cast<uint4*>(dxr + pbase + h * kEl) = v;
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        xp[i] = xc[i];
+        dp[i] = dc[i];
+      }
+    }
+  };
+  constexpr uint32_t kTail = (1u << (K - 1)) - 1u;
+  if (pb0 == 0xffffffffu && (pb1 & kTail) == kTail && sb == 0xffffffffu)
+    body(std::true_type());
+  else
+    body(std::false_type());
+  // the run's dw / db terms, added over the four runs in order
+#pragma unroll
+  for (int j = 0; j < kPartW; ++j) bt.red[run][r][j] = acc[j];
+  __syncthreads();
+  for (int i = threadIdx.x; i < kTmCh * kPartW; i += kTmThreads) {
+    const int rr = i / kPartW, j = i % kPartW;
+    if (c0 + rr >= C) continue;
+    float v = 0.f;
+    if (j < K || j == 8) {
+#pragma unroll
+      for (int q = 0; q < kTmTok / kTmRun; ++q) v += bt.red[q][rr][j];
+    }
+    part[((int64_t)(c0 + rr) * nb + blockIdx.x) * kPartW + j] = v;
   }
 }
 
@@ -721,10 +922,10 @@ bool tm_ok(int dtype, int C, int S, const void* a, const void* b, const void* c)
   return C % 8 == 0 && S % el == 0 && tt::quad_ok(S, a, b, c);
 }
 
-// Launch a token-major tile kernel with its dynamic shared memory.
-template <typename T, typename Kern, typename... Args>
+// Launch a token-major tile kernel with its dynamic shared memory (Tile).
+template <typename Tile, typename Kern, typename... Args>
 int launch_tm(Kern kern, dim3 grid, cudaStream_t st, Args... args) {
-  const int bytes = (int)sizeof(tt::TmTile<T>);
+  const int bytes = (int)sizeof(Tile);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
       cudaSuccess)
     return TT_ERR_CUDA;
@@ -747,7 +948,7 @@ extern "C" int tt_tree_conv_fwd_ex(int dtype, int32_t C, int32_t S, int32_t K, c
       if (out_token_major) {
         dim3 g((S + tt::kTmTok - 1) / tt::kTmTok, (C + tt::kTmCh - 1) / tt::kTmCh);
         tt_count_launches(1);
-        return launch_tm<T>(tt::conv_fwd_tm<T, KK>, g, (cudaStream_t)stream, C, S, (const T*)x,
+        return launch_tm<tt::TmTile<T>>(tt::conv_fwd_tm<T, KK>, g, (cudaStream_t)stream, C, S, (const T*)x,
                             weight, bias, pred, (T*)out);
       }
       dim3 g((S + tt::kConvTok - 1) / tt::kConvTok, (C + tt::kConvCh - 1) / tt::kConvCh);
@@ -803,12 +1004,18 @@ extern "C" int tt_tree_conv_bwd_ex(int dtype, int32_t C, int32_t S, int32_t K, c
       const bool q4 = tt::quad_ok(S, x, dout, dx) &&
                       (reinterpret_cast<uintptr_t>(workspace) & 15) == 0;
       if (dout_token_major) {
-        const int rc = launch_tm<T>(tt::conv_bwd_dpre_tm<T, KK>,
-                                    dim3(nb, (C + tt::kTmCh - 1) / tt::kTmCh), st, C, S,
-                                    (const T*)x, weight, bias, pred, (const T*)dout, dpre, part,
-                                    nb);
+        // dpre stays in shared memory: one pass to dx and the partials
+        const int rc = launch_tm<tt::TmBwdTile<T>>(
+            tt::conv_bwd_tm<T, KK>, dim3(nb, (C + tt::kTmCh - 1) / tt::kTmCh), st, C, S,
+            (const T*)x, weight, bias, pred, succ_ptr, succ_tok, succ_lag, (const T*)dout, (T*)dx,
+            part, nb);
         if (rc != TT_OK) return rc;
-      } else if (q4)
+        tt::conv_bwd_dw_reduce<<<(C * tt::kPartW + 255) / 256, 256, 0, st>>>(C, K, nb, part,
+                                                                           dweight, dbias);
+        tt_count_launches(2);
+        return cudaGetLastError() == cudaSuccess ? (int)TT_OK : (int)TT_ERR_CUDA;
+      }
+      if (q4)
         tt::conv_bwd_dpre4<T, KK><<<g, tt::kConvThr4, 0, st>>>(
             C, S, (const T*)x, weight, bias, pred, (const T*)dout, dpre, part, nb);
       else

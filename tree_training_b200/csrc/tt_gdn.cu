@@ -501,7 +501,11 @@ ddd_rowcol(int S, const int* __restrict__ nstart, const int* __restrict__ nlen,
 // dQs (grad of the scaled q, incl. the e^gam part via dQg), dKt (grad of k
 // from all k-terms except the beta-scaled ones), dKb (grad of k*beta incl.
 // dKbg*e^gam), dVb; plus gam, gl, and the Qg/Kbg/Kd-dependent dgam parts.
-template <typename T>
+// kIt > 0: Dk == 32 kIt, every lane's q / k values and gradients held in
+// registers (all loads issued up front, dq / dk written once); kIt == 0: any
+// Dk, the gradients stored and finished in a second pass.  Same arithmetic
+// and order either way.
+template <typename T, int kIt>
 __global__ void __launch_bounds__(32 * kTokWarps)
 assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__ q,
                                      const T* __restrict__ k, const T* __restrict__ v,
@@ -523,12 +527,24 @@ assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__
   const float bt = beta[(long long)t * H + h];
   const float gm = gam[ht];
   const float eg = expf(gm), ed = expf(gl_tok[ht] - gm);
+  constexpr int kR = kIt > 0 ? kIt : 1;
+  float qv[kR], kv[kR], gq[kR], gkk[kR];
   // norms again (cheap) for the normalised q/k and the l2norm backward
   float sq = 0.f, sk = 0.f;
-  for (int d = lane; d < Dk; d += 32) {
-    const float a = to_f32(qr[d]), b = to_f32(kr[d]);
-    sq += a * a;
-    sk += b * b;
+  if (kIt > 0) {
+#pragma unroll
+    for (int i = 0; i < kR; ++i) {
+      qv[i] = to_f32(qr[lane + 32 * i]);
+      kv[i] = to_f32(kr[lane + 32 * i]);
+      sq += qv[i] * qv[i];
+      sk += kv[i] * kv[i];
+    }
+  } else {
+    for (int d = lane; d < Dk; d += 32) {
+      const float a = to_f32(qr[d]), b = to_f32(kr[d]);
+      sq += a * a;
+      sk += b * b;
+    }
   }
   sq = warp_sum(sq);
   sk = warp_sum(sk);
@@ -536,8 +552,8 @@ assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__
   const float rk = l2norm ? rsqrtf(sk + 1e-6f) : 1.f;
   // d(scaled q) = dQ + dQg e^gam ; d(k) = dK + dKd e^{gl-gam} + beta (dKb + dKbg e^gam)
   float p_qg = 0.f, p_kbg = 0.f, p_kd = 0.f, p_kb = 0.f, xdq = 0.f, xdk = 0.f;
-  for (int d = lane; d < Dk; d += 32) {
-    const float qn = to_f32(qr[d]) * rq, kn = to_f32(kr[d]) * rk;
+  auto term = [&](int d, float qx, float kx, float& gqn_out, float& gk_out) {
+    const float qn = qx * rq, kn = kx * rk;
     const float qs = qn * q_scale;
     const float gqs = dQ[ht * Dk + d] + dQg[ht * Dk + d] * eg;
     const float gkb = dKb[ht * Dk + d] + dKbg[ht * Dk + d] * eg;
@@ -549,8 +565,19 @@ assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__
     const float gqn = gqs * q_scale;          // grad wrt normalised q
     xdq += qn * gqn;
     xdk += kn * gk;
-    dq_h[ht * Dk + d] = gqn;                  // finished below with the l2norm backward
-    dk_h[ht * Dk + d] = gk;
+    gqn_out = gqn;
+    gk_out = gk;
+  };
+  if (kIt > 0) {
+#pragma unroll
+    for (int i = 0; i < kR; ++i) term(lane + 32 * i, qv[i], kv[i], gq[i], gkk[i]);
+  } else {
+    for (int d = lane; d < Dk; d += 32) {
+      float gqn, gk;
+      term(d, to_f32(qr[d]), to_f32(kr[d]), gqn, gk);
+      dq_h[ht * Dk + d] = gqn;                // finished below with the l2norm backward
+      dk_h[ht * Dk + d] = gk;
+    }
   }
   p_qg = warp_sum(p_qg);
   p_kbg = warp_sum(p_kbg);
@@ -559,15 +586,30 @@ assemble_token_grads(int S, int Hk, int H, int Dk, int Dv, const T* __restrict__
   xdq = warp_sum(xdq);
   xdk = warp_sum(xdk);
   // y = x r (r = (|x|^2+eps)^-1/2): dx = r dy - r^3 (x.dy) x = r (dy - (y.dy) y)
-  for (int d = lane; d < Dk; d += 32) {
-    if (l2norm) {
-      const float qn = to_f32(qr[d]) * rq, kn = to_f32(kr[d]) * rk;
-      dq_h[ht * Dk + d] = rq * (dq_h[ht * Dk + d] - xdq * qn);
-      dk_h[ht * Dk + d] = rk * (dk_h[ht * Dk + d] - xdk * kn);
+  if (kIt > 0) {
+#pragma unroll
+    for (int i = 0; i < kR; ++i) {
+      const int d = lane + 32 * i;
+      if (l2norm) {
+        dq_h[ht * Dk + d] = rq * (gq[i] - xdq * (qv[i] * rq));
+        dk_h[ht * Dk + d] = rk * (gkk[i] - xdk * (kv[i] * rk));
+      } else {
+        dq_h[ht * Dk + d] = gq[i];
+        dk_h[ht * Dk + d] = gkk[i];
+      }
+    }
+  } else {
+    for (int d = lane; d < Dk; d += 32) {
+      if (l2norm) {
+        const float qn = to_f32(qr[d]) * rq, kn = to_f32(kr[d]) * rk;
+        dq_h[ht * Dk + d] = rq * (dq_h[ht * Dk + d] - xdq * qn);
+        dk_h[ht * Dk + d] = rk * (dk_h[ht * Dk + d] - xdk * kn);
+      }
     }
   }
   float p_vb = 0.f;
   const T* vr = v + (long long)t * v_ts + (long long)h * Dv;
+#pragma unroll 4
   for (int d = lane; d < Dv; d += 32) {
     const float g = dVb[ht * Dv + d];
     p_vb += to_f32(vr[d]) * g;
@@ -625,6 +667,39 @@ reduce_gqa(int S, int Hk, int H, int Dk, const float* __restrict__ src, T* dst) 
     for (int r = 0; r < rep; ++r) a += src[(((long long)(hk * rep + r)) * S + t) * Dk + d];
     dst[((long long)t * Hk + hk) * Dk + d] = from_f32<T>(a);
   }
+}
+
+// The same for dq and dk in one launch (blockIdx.y: 0 = q, 1 = k), one thread
+// per 4 consecutive elements of a (token, k-head) row: 16-byte loads of each
+// group head, added in head order as above.  Needs Dk % 4 == 0, 16-byte aligned
+// sources and destinations aligned to 4 elements.
+template <typename T>
+__global__ void __launch_bounds__(256)
+reduce_gqa4(int S, int Hk, int H, int Dk, const float* __restrict__ src_q, T* dst_q,
+            const float* __restrict__ src_k, T* dst_k) {
+  const float* src = blockIdx.y ? src_k : src_q;
+  T* dst = blockIdx.y ? dst_k : dst_q;
+  const int nq = Dk / 4, rep = H / Hk;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)S * Hk * nq) return;
+  const int e = (int)(i % nq) * 4;
+  const long long th = i / nq;
+  const int hk = (int)(th % Hk), t = (int)(th / Hk);
+  float a[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int r = 0; r < rep; ++r) {
+    const float4 v =
+        *reinterpret_cast<const float4*>(src + (((long long)(hk * rep + r)) * S + t) * Dk + e);
+    a[0] += v.x;
+    a[1] += v.y;
+    a[2] += v.z;
+    a[3] += v.w;
+  }
+  struct alignas(4 * sizeof(T)) Q4 {
+    T v[4];
+  } o;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o.v[j] = from_f32<T>(a[j]);
+  *reinterpret_cast<Q4*>(dst + ((long long)t * Hk + hk) * Dk + e) = o;
 }
 
 __global__ void dinit_kernel(int H, int DkDv, int n_roots, const int* __restrict__ roots,
@@ -1377,15 +1452,28 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
                    b.dK, vk, 0.f, st);
   launch_gemm(gc, ds_gk, H, b.dAqk, llh, b.K, vk, b.dQ, vk, 1.f, 0.f, st);
   kd_dot_kernel<<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(S, Dk, b.Kd, b.dKd, b.kd_dot);
-  assemble_token_grads<T><<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(
-      S, Hk, H, Dk, Dv, q, k, v, q_ts, k_ts, v_ts, beta, b.gam, b.gl_tok, l2norm, q_scale, b.dQ,
-      b.dQg, b.dK,
-      b.dKd, b.dKb, b.dKbg, b.dVb, b.dgam, b.dq_h, b.dk_h, dbeta, (T*)dv_);
+  {
+    auto asm_kernel = Dk == 128 ? assemble_token_grads<T, 4> : assemble_token_grads<T, 0>;
+    asm_kernel<<<dim3((S + kTokWarps - 1) / kTokWarps, H), 32 * kTokWarps, 0, st>>>(
+        S, Hk, H, Dk, Dv, q, k, v, q_ts, k_ts, v_ts, beta, b.gam, b.gl_tok, l2norm, q_scale, b.dQ,
+        b.dQg, b.dK, b.dKd, b.dKb, b.dKbg, b.dVb, b.dgam, b.dq_h, b.dk_h, dbeta, (T*)dv_);
+  }
   node_dg<<<dim3((n + 127) / 128, H), 128, 0, st>>>(S, H, n, b.d_start, b.d_len, b.kd_dot, b.dgl,
                                                     b.dgam, dg);
-  reduce_gqa<T><<<dim3((S + kTokWarps - 1) / kTokWarps, Hk), 32 * kTokWarps, 0, st>>>(S, Hk, H, Dk, b.dq_h, (T*)dq_);
-  reduce_gqa<T><<<dim3((S + kTokWarps - 1) / kTokWarps, Hk), 32 * kTokWarps, 0, st>>>(S, Hk, H, Dk, b.dk_h, (T*)dk_);
-  launches += 5;
+  const auto al = [](const void* ptr, int a) { return reinterpret_cast<uintptr_t>(ptr) % a == 0; };
+  if (Dk % 4 == 0 && al(b.dq_h, 16) && al(b.dk_h, 16) && al(dq_, 4 * sizeof(T)) &&
+      al(dk_, 4 * sizeof(T))) {
+    const long long n4 = (long long)S * Hk * (Dk / 4);
+    reduce_gqa4<T><<<dim3((unsigned)((n4 + 255) / 256), 2), 256, 0, st>>>(
+        S, Hk, H, Dk, b.dq_h, (T*)dq_, b.dk_h, (T*)dk_);
+    launches += 4;
+  } else {
+    reduce_gqa<T><<<dim3((S + kTokWarps - 1) / kTokWarps, Hk), 32 * kTokWarps, 0, st>>>(
+        S, Hk, H, Dk, b.dq_h, (T*)dq_);
+    reduce_gqa<T><<<dim3((S + kTokWarps - 1) / kTokWarps, Hk), 32 * kTokWarps, 0, st>>>(
+        S, Hk, H, Dk, b.dk_h, (T*)dk_);
+    launches += 5;
+  }
   if (dinit) {
     dinit_kernel<<<blocks(sh), 256, 0, st>>>(H, DkDv, (int)p.roots.size(), b.d_roots, b.dSi, dinit);
     ++launches;
