@@ -1125,7 +1125,7 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
     const long long lo = p.loff[c];
     const int Lp = row_stride(L);
     // KK = Kb K^T, QK = Q K^T : [L x L], K = Dk (tok0: the decay-mask epilogue)
-    v_kk.push_back(desc(L, L, Dk, tk, Dk, 1, tk, 1, Dk, lo, Lp, 1));
+    v_kk.push_back(desc(L, L, Dk, tk, Dk, 1, tk, 1, Dk, lo, Lp, 1, kKLowerC));
     v_kk.back().tok0 = p.start[c];
     // A * X for X = [L x Dv] (U) / [L x Dk] (W)
     v_av.push_back(desc(L, Dv, L, lo, Lp, 1, tv, Dv, 1, tv, Dv, 1, kKToRow));
@@ -1220,10 +1220,10 @@ int run(const Plan& p, bool backward, Arena& ar, const void* q_, const void* k_,
       // dW = -dVn S_in^T
       b_dw.push_back(desc(L, Dk, Dv, tv, Dv, 1, sin, 1, Dv, tk, Dk, 1));
       // dAqk = dO Vn^T : [L x L]
-      b_daqk.push_back(desc(L, L, Dv, tv, Dv, 1, tv, 1, Dv, lo, Lp, 1));
+      b_daqk.push_back(desc(L, L, Dv, tv, Dv, 1, tv, 1, Dv, lo, Lp, 1, kKLowerC));
       // dT = dVn Vb^T + dW Kbg^T
-      b_dt1.push_back(desc(L, L, Dv, tv, Dv, 1, tv, 1, Dv, lo, Lp, 1));
-      b_dt2.push_back(desc(L, L, Dk, tk, Dk, 1, tk, 1, Dk, lo, Lp, 1));
+      b_dt1.push_back(desc(L, L, Dv, tv, Dv, 1, tv, 1, Dv, lo, Lp, 1, kKLowerC));
+      b_dt2.push_back(desc(L, L, Dk, tk, Dk, 1, tk, 1, Dk, lo, Lp, 1, kKLowerC));
       // X = dT A^T : [L x L] = [L x L][L x L]^T ; X += A^T dT
       b_x1.push_back(desc(L, L, L, lo, Lp, 1, lo, 1, Lp, lo, Lp, 1, kKToCol));
       b_x2.push_back(desc(L, L, L, lo, 1, Lp, lo, Lp, 1, lo, Lp, 1, kKFromRow));

@@ -28,8 +28,11 @@ struct SegDesc {
 //   kKToRow  A lower triangular (A[r][k] = 0 for k > r): k < row + 1;
 //   kKFromRow A upper triangular (the transpose of a lower one): k >= row;
 //   kKToCol  B upper triangular (B[k][n] = 0 for k > n): k < col + 1;
-//   kKFromCol B lower triangular: k >= col.
-enum { kKFull = 0, kKToRow = 1, kKFromRow = 2, kKToCol = 3, kKFromCol = 4 };
+//   kKFromCol B lower triangular: k >= col;
+//   kKLowerC every k, but only C's lower triangle is wanted (the decay-masked
+//            K K^T / Q K^T): a tile entirely above the diagonal gets no K
+//            slice, and the tensor-core GEMM's epilogue writes it as zeros.
+enum { kKFull = 0, kKToRow = 1, kKFromRow = 2, kKToCol = 3, kKFromCol = 4, kKLowerC = 5 };
 
 // Decay mask applied by the tensor-core GEMM's epilogue to an L x L product
 // of one node (row i, column m, gam the per-token cumulative log decay of

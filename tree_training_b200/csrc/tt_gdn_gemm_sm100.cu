@@ -126,6 +126,7 @@ __device__ __forceinline__ void k_range(const SegDesc& sd, int i0, int j0, int& 
     case kKFromRow: kb = i0; break;
     case kKToCol: ke = min(ke, j0 + kTN); break;
     case kKFromCol: kb = j0; break;
+    case kKLowerC: ke = j0 >= i0 + kTM ? 0 : ke; break;
     default: break;
   }
   n = ke > kb ? (ke - kb + kTK - 1) / kTK : 0;
