@@ -515,6 +515,7 @@ struct TmTileR {
   float w[kTmCh * 8];                    // the tile's weights, [r][K]
   float b[kTmCh];                        // and biases (0 without)
   uint32_t plain[kBits];                 // bit j of word i: token t0 + 32 i + j
+  alignas(16) int32_t pred[kRows * 7];   // the rows' predecessor table, [t][K - 1]
 };
 template <typename T>
 using TmTile = TmTileR<T, 0>;
@@ -548,6 +549,20 @@ __device__ __forceinline__ void stage_x(Tile& sm, const T* x, int C, int S, int 
     const int c = c0 + r, t = t0 - kTmHalo + k * kEl;   // chunks are whole: S % kEl == 0
     const bool ok = c < C && t >= 0 && t < S;
     cp_async16_zfill(&sm.x[r][k * kEl], ok ? x + (int64_t)c * S + t : x, ok);
+  }
+}
+
+// Stage the predecessor rows of tile tokens 0 .. kRows - 1 (16-byte chunks:
+// t0 (K - 1) and S (K - 1) are multiples of 4; rows past S read as 0 and are
+// never used).
+template <int K, typename Tile>
+__device__ __forceinline__ void stage_pred(Tile& sm, const int32_t* pred, int S, int t0) {
+  if (K == 1) return;
+  constexpr int kChunks = Tile::kRows * (K - 1) / 4;
+  const int64_t end = (int64_t)S * (K - 1), base = (int64_t)t0 * (K - 1);
+  for (int q = threadIdx.x; q < kChunks; q += kTmThreads) {
+    const bool ok = base + 4 * q < end;
+    cp_async16_zfill(&sm.pred[4 * q], ok ? pred + base + 4 * q : pred, ok);
   }
 }
 
@@ -590,7 +605,9 @@ __device__ __forceinline__ void window_gather(const Tile& sm, const T* __restric
                : to_f32(x[(int64_t)c * S + p]);
   };
   xs[0] = at(t);
-  for (int m = 1; m < K; ++m) xs[m] = at(pred[(int64_t)t * (K - 1) + m - 1]);
+  const bool staged = tt < Tile::kRows;      // (tt >= 0: t >= t0 always)
+  for (int m = 1; m < K; ++m)
+    xs[m] = at(staged ? sm.pred[tt * (K - 1) + m - 1] : pred[(int64_t)t * (K - 1) + m - 1]);
 }
 
 // n consecutive x values of tile row r starting at staged index i0 (a
@@ -614,6 +631,7 @@ conv_fwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
   constexpr int kEl = Tile::kEl;
   const int c0 = blockIdx.y * kTmCh, t0 = blockIdx.x * kTmTok;
   stage_x(sm, x, C, S, c0, t0);
+  stage_pred<K>(sm, pred, S, t0);
   asm volatile("cp.async.commit_group;" ::: "memory");
   stage_w<K>(sm, w, bias, C, c0);
   stage_plain<K>(sm, pred, S, t0);
@@ -674,9 +692,11 @@ conv_fwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
 // each (the K - 1 past its run are the next run's first tokens, computed
 // again here) into a register window, its tokens' dw / db terms, and
 // dx[t] = w[K-1] dpre[t] + sum_l w[K-1-l] dpre[t + l] once dpre[t + K - 1] is
-// known.  A token with another successor list walks the successor CSR,
-// recomputing each successor's dpre from x and dy (a node's last tokens feed
-// its later children, far away in DFS order).  Per output the arithmetic and
+// known.  A token with another successor list (a node's last tokens) adds
+// the successors of its near chain (t + 1 .. t + near, inside its path) from
+// the same registers, then walks the rest of its CSR list, recomputing each
+// far successor's dpre from x and dy (a node's later children, far away in
+// DFS order).  Per output the arithmetic and
 // its order are those of conv_bwd_dpre4 + conv_bwd_dx4, so dx matches the
 // channel-major kernels bit for bit; the four runs' dw / db terms are added in
 // run order.
@@ -685,6 +705,7 @@ struct TmBwdTile {
   TmTileR<T, kTmHalo> s;                 // x [t0 - 8, t0 + 136), dy rows t0 .. t0 + 135
   float red[kTmTok / kTmRun][kTmCh][kPartW];   // per run: dw / db terms
   uint32_t succ_plain[kTmTok / 32];      // bit j of word i: token t0 + 32 i + j
+  uint8_t succ_info[kTmTok];             // per token: near chain length | 8 if far successors
 };
 
 // dpre of token u in tile channel r (c = c0 + r): the window through the
@@ -704,19 +725,20 @@ __device__ __forceinline__ float dpre_any(const Tile& sm, const T* __restrict__ 
   return silu_grad(g, pre);
 }
 
-// dx of token t with an irregular successor list (dpre_t: its own dpre)
+// The far part of dx[t]: the successor CSR entries after the first `near`
+// (its near chain t + 1 .. t + near, whose terms the caller has added),
+// each successor's dpre recomputed from x and dy.
 template <int K, typename Tile, typename T>
-__device__ __forceinline__ float dx_walk(const Tile& sm, const T* __restrict__ x,
-                                      const T* __restrict__ dy_tm,
-                                      const int32_t* __restrict__ pred,
-                                      const int32_t* __restrict__ sp,
-                                      const int32_t* __restrict__ stok,
-                                      const int32_t* __restrict__ slag, int C, int S, int c, int r,
-                                      int t0, int t, float dpre_t) {
+__device__ __forceinline__ float dx_far(const Tile& sm, const T* __restrict__ x,
+                                        const T* __restrict__ dy_tm,
+                                        const int32_t* __restrict__ pred,
+                                        const int32_t* __restrict__ sp,
+                                        const int32_t* __restrict__ stok,
+                                        const int32_t* __restrict__ slag, int C, int S, int c,
+                                        int r, int t0, int t, int near, float s) {
   const float* wc = sm.w + r * K;
-  float s = wc[K - 1] * dpre_t;
   const int e1 = sp[t + 1];
-  for (int e = sp[t]; e < e1; ++e) {
+  for (int e = sp[t] + near; e < e1; ++e) {
     const int u = stok[e], l = slag[e];
     s = fmaf(wc[K - 1 - l], dpre_any<K>(sm, x, dy_tm, pred, C, S, c, r, t0, u), s);
   }
@@ -743,13 +765,20 @@ conv_bwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
     const bool ok = t < S && c < C;
     cp_async16_zfill(&sm.tm[rr][k * kEl], ok ? dy_tm + (int64_t)t * C + c : dy_tm, ok);
   }
+  stage_pred<K>(sm, pred, S, t0);
   asm volatile("cp.async.commit_group;" ::: "memory");
   stage_w<K>(sm, w, bias, C, c0);
   stage_plain<K>(sm, pred, S, t0);
-  if (threadIdx.x < kTmTok) {                // successor lists
+  if (threadIdx.x < kTmTok) {
+    // successor lists: the near chain (the leading entries (t + 1 + m, m + 1),
+    // the tokens that follow t inside its path) and whether others follow.
+    // A successor u of lag l is at least l tokens after t in DFS order, and
+    // u = t + l only on the chain, so the chain's entries come first in the
+    // CSR's token order.
     const int t = t0 + threadIdx.x;
-    bool pl = t < S;
-    if (pl) {
+    int near = 0;
+    bool far = false;
+    if (t < S) {
       const int e0 = sp[t], e1 = sp[t + 1];
       int su[K > 1 ? K - 1 : 1], sl[K > 1 ? K - 1 : 1];   // independent loads
 #pragma unroll
@@ -758,10 +787,16 @@ conv_bwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
         su[m] = in ? stok[e0 + m] : -1;
         sl[m] = in ? slag[e0 + m] : 0;
       }
-      pl = e1 - e0 == K - 1;
+      bool chain = true;
 #pragma unroll
-      for (int m = 0; m < K - 1; ++m) pl = pl && su[m] == t + 1 + m && sl[m] == m + 1;
+      for (int m = 0; m < K - 1; ++m) {
+        chain = chain && su[m] == t + 1 + m && sl[m] == m + 1;
+        near += chain;
+      }
+      far = e1 - e0 > near;
     }
+    bt.succ_info[threadIdx.x] = (uint8_t)(near | (far ? 8 : 0));
+    const bool pl = t < S && near == K - 1 && !far;
     const uint32_t bits = __ballot_sync(0xffffffffu, pl);
     if ((threadIdx.x & 31) == 0) bt.succ_plain[threadIdx.x >> 5] = bits;
   }
@@ -838,8 +873,16 @@ conv_bwd_tm(int C, int S, const T* __restrict__ x, const float* __restrict__ w,
             for (int l = 1; l < K; ++l) sacc = fmaf(wr[K - 1 - l], i + l < 8 ? dp[i + l] : dc[i + l - 8], sacc);
             dxv[i] = sacc;
           } else if (t0 + tq + pbase + i < S) {
-            dxv[i] = dx_walk<K>(sm, x, dy_tm, pred, sp, stok, slag, C, S, c, r, t0,
-                                t0 + tq + pbase + i, dp[i]);
+            // the near chain from registers, then the far successors
+            const int info = bt.succ_info[tq + pbase + i], near = info & 7;
+            float sacc = wr[K - 1] * dp[i];
+#pragma unroll
+            for (int l = 1; l < K; ++l)
+              if (l <= near) sacc = fmaf(wr[K - 1 - l], i + l < 8 ? dp[i + l] : dc[i + l - 8], sacc);
+            if (info & 8)
+              sacc = dx_far<K>(sm, x, dy_tm, pred, sp, stok, slag, C, S, c, r, t0,
+                               t0 + tq + pbase + i, near, sacc);
+            dxv[i] = sacc;
           }
         }
         // whole 16-byte chunks (S % kEl == 0: live or dead as a whole)
