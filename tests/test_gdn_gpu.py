@@ -461,8 +461,9 @@ def test_token_major_conv_and_in_place_gdn_rows_match_packed(dtype):
     assert rel(tm[3].cpu().numpy(), pk[3].cpu().numpy()) < 1e-5       # dw
 
 
-@pytest.mark.parametrize("K,dtype", [(2, torch.bfloat16), (4, torch.float32), (7, torch.bfloat16),
-                                     (7, torch.float32)])
+@pytest.mark.parametrize("K,dtype", [(1, torch.bfloat16), (2, torch.bfloat16), (4, torch.float32),
+                                     (4, torch.bfloat16), (7, torch.bfloat16), (7, torch.float32),
+                                     (8, torch.bfloat16)])
 def test_tree_conv_token_major_kernels_match_channel_major(K, dtype):
     """The shared-memory-tiled token-major conv kernels (output / output
     gradient as [S, C] rows) against the channel-major ones on a tree of
